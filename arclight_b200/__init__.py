@@ -1,0 +1,79 @@
+"""arclight_b200 -- B200-native (sm_100a) ArcLight Qwen3 Q4_0 decode/prefill hot path.
+
+The product is ``libalb_cuda.so`` (CUDA kernels + the C ABI declared in
+``include/alb_cuda.h``).  This module only loads it with ctypes and declares
+argument types; there is no Python or CPU fallback: if the library is missing
+or fails to load, every call raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(PKG)
+LIB_PATH = os.path.join(PKG, "libalb_cuda.so")
+HEADER = os.path.join(ROOT, "include", "alb_cuda.h")
+
+ALB_OK = 0
+_lib = None
+
+
+class AlbError(RuntimeError):
+    pass
+
+
+def header_symbols(path: str = HEADER) -> list[str]:
+    """Every function the C ABI header declares."""
+    src = open(path).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(alb_[a-z0-9_]+)\s*\(", src)))
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise AlbError(f"{LIB_PATH} is not built (run `python -m arclight_b200.build`); "
+                           "there is no fallback path")
+        _lib = C.CDLL(LIB_PATH)
+        _declare(_lib)
+    return _lib
+
+
+def check(rc: int, what: str = "") -> None:
+    if rc != ALB_OK:
+        msg = lib().alb_last_error().decode(errors="replace")
+        raise AlbError(f"{what or 'alb call'} failed with status {rc}: {msg}")
+
+
+def _declare(L: C.CDLL) -> None:
+    vp, i64, i32, f32, sz = C.c_void_p, C.c_int64, C.c_int32, C.c_float, C.c_size_t
+    ci = C.c_int
+    sigs = {
+        "alb_version": (ci, []),
+        "alb_last_error": (C.c_char_p, []),
+        "alb_device_check": (ci, [ci]),
+        "alb_device_error": (ci, [ci]),
+        "alb_q4_0_gpu_bytes": (sz, [i64, i64]),
+        "alb_q4_0_scale_offset": (sz, [i64, i64]),
+        "alb_repack_q4_0": (ci, [vp, vp, i64, i64, vp]),
+        "alb_unpack_q4_0": (ci, [vp, vp, i64, i64, vp]),
+        "alb_quantize_q8_0": (ci, [vp, vp, i64, i64, vp]),
+        "alb_gemv_q4_0_q8_0": (ci, [vp, vp, vp, i64, i64, vp, vp]),
+        "alb_gemv_q4_0_q8_0_block_dots": (ci, [vp, vp, vp, i64, i64, vp]),
+        "alb_rms_norm": (ci, [vp, vp, vp, i64, i64, f32, vp]),
+        "alb_swiglu": (ci, [vp, vp, vp, i64, vp]),
+        "alb_get_rows_q4_0": (ci, [vp, i64, i64, vp, i64, vp, vp]),
+        "alb_rope_table": (ci, [vp, i32, i32, f32]),
+        "alb_qk_norm_rope_kv": (ci, [vp, i64, i32, i32, vp, vp, f32, vp, i32, vp, vp, vp, vp]),
+        "alb_flash_attn_workspace_bytes": (sz, [i32, i32, i64, i32]),
+        "alb_flash_attn": (ci, [vp, vp, vp, i64, i32, i32, i32, f32, i32, vp, vp, vp]),
+        "alb_argmax": (ci, [vp, i64, vp, vp, vp]),
+    }
+    for name, (res, args) in sigs.items():
+        if hasattr(L, name):
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args

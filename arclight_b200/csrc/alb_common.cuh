@@ -1,0 +1,128 @@
+// Shared device helpers for the ArcLight B200 hot path (sm_100a only).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "alb_cuda.h"
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
+#error "arclight_b200 kernels are written for sm_100a only"
+#endif
+
+#define ALB_QK 32
+
+// Return a status from a CUDA runtime call (host side).
+#define ALB_CUDA_TRY(expr)                                                        \
+    do {                                                                          \
+        cudaError_t e__ = (expr);                                                 \
+        if (e__ != cudaSuccess) { alb_set_last_cuda_error(e__, #expr); return ALB_ERR_CUDA; } \
+    } while (0)
+
+#define ALB_CHECK_ARG(cond)                                                       \
+    do { if (!(cond)) { alb_set_last_error_msg("invalid argument: " #cond); return ALB_ERR_INVALID; } } while (0)
+
+void alb_set_last_cuda_error(cudaError_t e, const char * what);
+void alb_set_last_error_msg(const char * msg);
+int  alb_sm_count();
+
+// Programmatic dependent launch: the kernels below call these so that a
+// dependent kernel (launched with cudaLaunchAttributeProgrammaticStreamSerialization)
+// can start its prologue -- e.g. stream its weights -- while this grid drains.
+__device__ __forceinline__ void alb_pdl_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void alb_pdl_trigger() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// 16-byte read-only streaming load that does not allocate in L1.
+__device__ __forceinline__ uint4 alb_ld_stream(const void * p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ float alb_h2f(uint16_t h) {
+    return __half2float(__ushort_as_half(h));
+}
+__device__ __forceinline__ uint16_t alb_f2h(float f) {
+    return __half_as_ushort(__float2half_rn(f));
+}
+
+template <int W = 32>
+__device__ __forceinline__ float alb_warp_sum(float v) {
+#pragma unroll
+    for (int o = W / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float alb_warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Launch helper: optionally marks the launch as a programmatic dependent of the
+// previous kernel in the stream.
+template <typename... KArgs, typename... Args>
+static inline cudaError_t alb_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                     cudaStream_t stream, bool pdl, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+// ---------------------------------------------------------------- mbarrier / bulk copy
+__device__ __forceinline__ uint32_t alb_smem_addr(const void * p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void alb_mbar_init(uint64_t * bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(alb_smem_addr(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void alb_mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void alb_mbar_expect_tx(uint64_t * bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(alb_smem_addr(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void alb_mbar_arrive(uint64_t * bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(alb_smem_addr(bar)) : "memory");
+}
+__device__ __forceinline__ bool alb_mbar_try_wait(uint64_t * bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(ok) : "r"(alb_smem_addr(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ uint64_t alb_globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Bounded wait on an mbarrier phase: gives up after `ns` nanoseconds of
+// %globaltimer (default 2 s) and returns false, so no wait can hang the GPU.
+__device__ __forceinline__ bool alb_mbar_wait(uint64_t * bar, uint32_t parity, uint64_t ns = 2000000000ull) {
+    if (alb_mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = alb_globaltimer();
+    for (uint32_t i = 1;; ++i) {
+        if (alb_mbar_try_wait(bar, parity)) return true;
+        if ((i & 255) == 0 && alb_globaltimer() - t0 > ns) return false;
+    }
+}
+// 1-D bulk copy global -> shared, completion counted on `bar` (16-byte aligned, size % 16 == 0).
+__device__ __forceinline__ void alb_bulk_g2s(void * dst_smem, const void * src, uint32_t bytes, uint64_t * bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 :: "r"(alb_smem_addr(dst_smem)), "l"(src), "r"(bytes), "r"(alb_smem_addr(bar)) : "memory");
+}

@@ -1,0 +1,106 @@
+// Internal (C++) interface between the C ABI, the kernels and the Qwen3 engine.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "alb_cuda.h"
+
+namespace alb {
+
+// How a GEMV obtains its Q8_0 activation vector.
+enum GemvIn : int {
+    GEMV_IN_Q8 = 0,       // block_q8_0 [K/32] in global memory (reference layout)
+    GEMV_IN_F32 = 1,      // fp32 [K]: quantized to Q8_0 in the prologue (arm.cpp:1886-1897)
+    GEMV_IN_F32_RMS = 2,  // fp32 [K]: RMSNorm (ops.cpp:680-724) * w, then quantized
+};
+
+// What a GEMV writes.
+enum GemvOut : int {
+    GEMV_OUT_PLAIN = 0,   // y[n] = acc (+ residual[n])
+    GEMV_OUT_SWIGLU = 1,  // rows interleaved (gate n, up n): y[n] = silu(gate)*up (ops.cpp:1038-1092)
+    GEMV_OUT_DOTS = 2,    // y[n] = acc and I[n][b] = int32 block dots (parity check)
+};
+
+struct GemvArgs {
+    const uint8_t * W = nullptr;   // nibble plane of the alb Q4_0 GPU layout (row 0 of this view)
+    const uint8_t * S = nullptr;   // fp16 scale plane (row 0 of this view)
+    int64_t N = 0, K = 0;          // physical rows, columns
+    int in_mode = GEMV_IN_Q8;
+    const void * x = nullptr;      // block_q8_0 or fp32 per in_mode
+    const float * norm_w = nullptr;
+    float eps = 1e-6f;
+    int out_mode = GEMV_OUT_PLAIN;
+    float * y = nullptr;
+    const float * residual = nullptr;
+    int32_t * dots = nullptr;
+    bool pdl = false;              // launch as a programmatic dependent
+    int ctas_per_sm = 0;           // 0 = default
+    int variant = 0;               // 0/1 = direct loads + L2 prefetch (default), 2 = bulk-copy pipeline
+    int stage_budget = 0;          // bytes of shared-memory stages (0 = default)
+    int * err = nullptr;           // device error word (filled by launch_gemv)
+};
+
+struct FlashArgs {
+    const float * q = nullptr;          // [T][Hq][128] fp32
+    const uint16_t * kc = nullptr;      // [cells][Hkv][128] fp16
+    const uint16_t * vc = nullptr;
+    int Hq = 0, Hkv = 0, T = 1;
+    int32_t pos0 = 0;                   // position of token 0 (ignored when pos_dev)
+    const int32_t * pos_dev = nullptr;  // device-resident pos0 (CUDA-graph replay)
+    float scale = 0.0f;
+    int S = 1;                          // splits along the cells
+    float * ws = nullptr;               // flash_attn_ws_bytes(); tickets must start at 0
+    float * out = nullptr;              // [T][Hq][128] fp32
+    bool pdl = false;
+};
+size_t flash_attn_ws_bytes(int Hq, int Hkv, int T, int S);
+cudaError_t launch_flash_attn(const FlashArgs & f, cudaStream_t st);
+
+struct QkvArgs {
+    const float * qkv = nullptr;        // [T][qkv_stride]: q (Hq*128) | k (Hkv*128) | v (Hkv*128)
+    int64_t qkv_stride = 0;
+    int Hq = 0, Hkv = 0, T = 1;
+    const float * q_norm = nullptr, * k_norm = nullptr;
+    float eps = 1e-6f;
+    const float2 * rope = nullptr;      // [max_pos][64] (cos, sin)
+    int32_t pos0 = 0;
+    const int32_t * pos_dev = nullptr;
+    float * q_out = nullptr;            // [T][Hq][128]
+    uint16_t * kc = nullptr, * vc = nullptr;  // cache base of this layer [cells][Hkv][128]
+    bool pdl = false;
+};
+cudaError_t launch_qk_norm_rope_kv(const QkvArgs & a, cudaStream_t st);
+cudaError_t launch_embed(const uint8_t * Wn, const uint8_t * Ws, int64_t vocab, int64_t E, const int32_t * tokens,
+                         int T, float * x, bool pdl, cudaStream_t st);
+// argmax over x[0..n): scratch >= 64*8 + 16 bytes with its ticket word zero at first use
+cudaError_t launch_argmax(const float * x, int64_t n, int64_t idx_base, void * scratch,
+                          unsigned long long * key_out, int32_t * idx_out, bool pdl, cudaStream_t st);
+cudaError_t launch_key_to_index(const unsigned long long * key, int32_t * idx, bool pdl, cudaStream_t st);
+cudaError_t launch_rms_norm(const float * x, const float * w, float * y, int64_t rows, int64_t n, float eps, bool pdl,
+                            cudaStream_t st);
+cudaError_t launch_swiglu(const float * g, const float * u, float * y, int64_t n, bool pdl, cudaStream_t st);
+
+// Device-side error word (bounded waits that expire set it; see alb_device_error).
+enum : int { ALB_DEVERR_NONE = 0, ALB_DEVERR_MBAR_TIMEOUT = 1, ALB_DEVERR_FLAG_TIMEOUT = 2 };
+// Host: the current device's error word (allocated once per device, zeroed).
+int * device_error_ptr();
+
+cudaError_t launch_gemv(const GemvArgs & a, cudaStream_t stream);
+
+// alb Q4_0 GPU layout: nibble plane [N][K/2] bytes, then (256-aligned) the fp16
+// scale plane [N][q4_scale_pitch(K)] (row pitch padded to 16 bytes so that every
+// row range is a legal bulk-copy source).
+__host__ __device__ inline int64_t q4_scale_pitch(int64_t K) {   // in fp16 elements
+    return ((K / 32) + 7) & ~(int64_t)7;
+}
+__host__ __device__ inline size_t q4_scale_offset(int64_t N, int64_t K) {
+    const size_t nib = (size_t)N * (size_t)(K / 2);
+    return (nib + 255) & ~(size_t)255;
+}
+__host__ __device__ inline size_t q4_gpu_bytes(int64_t N, int64_t K) {
+    const size_t sc = (size_t)N * (size_t)q4_scale_pitch(K) * 2;
+    return (q4_scale_offset(N, K) + sc + 255) & ~(size_t)255;
+}
+
+}  // namespace alb

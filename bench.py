@@ -1,0 +1,236 @@
+#!/usr/bin/env python3
+"""ArcLight B200 hot-path benchmark (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode|gemv] [--impl ours|reference]
+
+Workloads:
+  gemv    config 1: one Q4_0 x Q8_0 mat-vec, W [9728 x 2560]; a step is one
+          launch over one of 24 distinct weight copies (336 MB > 126 MB L2).
+Metric / value / roofline conventions: see DESIGN.md "Measurement".
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
+
+
+# ----------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples nvidia-smi SM clocks and throttle reasons during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.samples = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                self.samples.append(parts)
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if s[5 + i].lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+# ----------------------------------------------------------------- GEMV (config 1)
+GEMV_N, GEMV_K = 9728, 2560
+GEMV_BYTES = GEMV_N * (GEMV_K // 32) * 18 + (GEMV_K // 32) * 34 + GEMV_N * 4  # 14 049 952
+
+
+def cpu_gemv_baseline(seconds: float = 12.0):
+    """The oracle mat-vec (reference semantics, all host threads) on a bounded sample."""
+    from oracle import lib as O
+    rng = np.random.default_rng(1)
+    wq = O.quantize_q4_0((rng.standard_normal((GEMV_N, GEMV_K)) * 0.02).astype(np.float32))
+    xq = O.quantize_q8_0(rng.standard_normal(GEMV_K).astype(np.float32))
+    threads = os.cpu_count() or 1
+    O.gemv(wq, xq, threads)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        O.gemv(wq, xq, threads)
+        n += 1
+    dt = (time.perf_counter() - t0) / n
+    return {"value": GEMV_BYTES / dt / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{n} mat-vecs of config 1 ({GEMV_N}x{GEMV_K}) in {seconds:.0f} s"}
+
+
+def run_gemv(args, rank, world):
+    import torch
+    import arclight_b200 as A
+    from arclight_b200 import bench_util as BU
+
+    L = A.lib()
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    A.check(L.alb_device_check(dev.index), "device check")
+    s = torch.cuda.current_stream()
+    n_copies = 24
+    Ws, xqs = BU.make_gemv_weights(n_copies, GEMV_N, GEMV_K, seed=1234)
+    y = torch.empty(GEMV_N, dtype=torch.float32, device=dev)
+
+    # one CUDA graph = one pass over the 24 weight copies (24 launches, PDL edges)
+    g = torch.cuda.CUDAGraph()
+    cap = torch.cuda.Stream()
+    with torch.cuda.stream(cap):
+        for i in range(n_copies):   # untimed eager pass (also sets kernel attributes)
+            A.check(L.alb_gemv_q4_0_q8_0(Ws[i].data_ptr(), xqs.data_ptr(), y.data_ptr(), GEMV_N, GEMV_K, None,
+                                         cap.cuda_stream))
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g, stream=cap):
+            for i in range(n_copies):
+                A.check(L.alb_gemv_q4_0_q8_0(Ws[i].data_ptr(), xqs.data_ptr(), y.data_ptr(), GEMV_N, GEMV_K,
+                                             None, cap.cuda_stream))
+    reps = max(1, args.steps // n_copies)
+    steps = reps * n_copies
+    with ClockSampler(dev.index) as clk:
+        t_end = time.time() + 0.6          # warm-up: >= W graph replays and >= 0.6 s under load
+        w = 0
+        while w < args.warmup or time.time() < t_end:
+            g.replay()
+            w += 1
+        torch.cuda.synchronize()
+        BU.barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(reps):
+            g.replay()
+        e1.record(s)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    ms = BU.max_over_ranks(ms, world)
+    launch_us = ms * 1e3
+    args.steps = steps
+
+    # e2e through the C ABI with host buffers: H2D x, quantize, gemv, D2H y
+    xh = torch.randn(GEMV_K, dtype=torch.float32).pin_memory()
+    yh = torch.empty(GEMV_N, dtype=torch.float32).pin_memory()
+    xd = torch.empty(GEMV_K, dtype=torch.float32, device=dev)
+    xqd = torch.empty((GEMV_K // 32) * 34, dtype=torch.uint8, device=dev)
+
+    def e2e_step(i):
+        xd.copy_(xh, non_blocking=True)
+        A.check(L.alb_quantize_q8_0(xd.data_ptr(), xqd.data_ptr(), GEMV_K, 1, s.cuda_stream))
+        A.check(L.alb_gemv_q4_0_q8_0(Ws[i % n_copies].data_ptr(), xqd.data_ptr(), y.data_ptr(),
+                                     GEMV_N, GEMV_K, None, s.cuda_stream))
+        yh.copy_(y, non_blocking=True)
+
+    for i in range(args.warmup):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    e0.record(s)
+    for i in range(args.steps):
+        e2e_step(i)
+    e1.record(s)
+    torch.cuda.synchronize()
+    e2e_ms = BU.max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+
+    peaks = load_peaks()
+    achieved = GEMV_BYTES / (launch_us * 1e-6) / 1e9
+    out = {
+        "metric": "Q4_0xQ8_0 GEMV HBM GB/s (config 1, W 9728x2560)",
+        "value": achieved * world, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "q4_0 x q8_0 -> int32 dots, fp32 accumulate", "data": "synthetic",
+        "config": {"workload": "config1_gemv", "N": GEMV_N, "K": GEMV_K, "weight_copies": n_copies,
+                   "l2": "inputs larger than L2: 24 rotating weight copies (336 MB)"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / peaks["hbm_gbs"], "traffic": None,
+                     "peak_src": peaks["src"], "algorithmic_bytes_per_launch": GEMV_BYTES},
+        "e2e": {"value": GEMV_BYTES / (e2e_ms * 1e-3) / 1e9 * world, "unit": "GB/s",
+                "h2d_bytes_per_step": GEMV_K * 4, "d2h_bytes_per_step": GEMV_N * 4},
+        "gpu_launches": args.steps,
+        "clocks": clk.summary(),
+    }
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2400)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="gemv", choices=["gemv"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    if world > 1:
+        import torch.distributed as dist
+        import datetime
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
+
+    if args.impl == "reference":
+        if rank == 0:
+            cb = cpu_gemv_baseline(seconds=min(20.0, 2.0 + 0.05 * args.steps))
+            line = {"impl": "reference", "metric": "Q4_0xQ8_0 GEMV HBM GB/s (config 1, W 9728x2560)",
+                    "value": cb["value"], "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+                    "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                    "dtype": "q4_0 x q8_0", "data": "synthetic", "config": {"workload": "config1_gemv"},
+                    "cpu_baseline": cb,
+                    "e2e": {"value": cb["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            print(json.dumps(line), flush=True)
+        return
+
+    out = run_gemv(args, rank, world)
+    if rank == 0:
+        if not args.no_cpu_baseline:
+            out["cpu_baseline"] = cpu_gemv_baseline(seconds=10.0)
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

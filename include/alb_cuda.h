@@ -1,0 +1,122 @@
+/*
+ * alb_cuda.h -- C ABI of the ArcLight B200 hot path (libalb_cuda.so).
+ *
+ * Drop-in boundary for the nnml operators of OpenBMB/ArcLight's Qwen3 Q4_0
+ * decode/prefill path.  Every entry point takes caller-owned device pointers,
+ * plain sizes and a cudaStream_t (passed as void *), is stream ordered, never
+ * allocates on the hot path and returns an int status (ALB_OK = 0, < 0 error;
+ * alb_last_error() gives the message).  The reference's ops return void and
+ * abort (nnml.h:97-111); callers that want that behaviour abort on status < 0.
+ *
+ * Each declaration cites the reference interface it replaces (file:line in the
+ * ArcLight tree).  Layouts:
+ *   block_q4_0  : {fp16 d; uint8 qs[16]}  18 B per 32 values (nnml.h:646-651)
+ *   block_q8_0  : {fp16 d; int8  qs[32]}  34 B per 32 values (nnml.h:695-700)
+ *   alb Q4_0 GPU layout (what alb_repack_q4_0 writes; replaces block_q4_0x4):
+ *       nibble plane  [N][K/2] bytes, block b of row n at n*K/2 + 16*b, the 16
+ *                     bytes of block_q4_0.qs unchanged;
+ *       scale plane   [N][K/32] fp16 at byte offset alb_q4_0_scale_offset(N, K).
+ *   activations fp32 row-major; KV cache fp16 [cells][n_head_kv][head_dim].
+ */
+#ifndef ALB_CUDA_H
+#define ALB_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ALB_API __attribute__((visibility("default")))
+#else
+#define ALB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    ALB_OK = 0,
+    ALB_ERR_INVALID = -1,     /* bad argument (null pointer, unsupported shape) */
+    ALB_ERR_CUDA = -2,        /* CUDA runtime error (message in alb_last_error) */
+    ALB_ERR_NCCL = -3,        /* collective error or abort */
+    ALB_ERR_TIMEOUT = -4,     /* a bounded device/host wait expired */
+    ALB_ERR_UNSUPPORTED = -5, /* no sm_100a device / feature not built */
+    ALB_ERR_OOM = -6,
+};
+
+/* ---------------------------------------------------------------- runtime */
+ALB_API int          alb_version(void);
+ALB_API const char * alb_last_error(void);
+/* 0 when device `dev` is an sm_100 part this library can run on. */
+ALB_API int          alb_device_check(int dev);
+/* Device-side error word of the current device: 0, or the code of a bounded
+ * in-kernel wait that expired (1 = mbarrier, 2 = cross-rank flag).  Kernels
+ * never trap; they record the error and return.  clear != 0 resets it. */
+ALB_API int          alb_device_error(int clear);
+
+/* ---------------------------------------------------------------- formats */
+/* Bytes of the alb Q4_0 GPU layout of an [N x K] weight (K % 32 == 0). */
+ALB_API size_t alb_q4_0_gpu_bytes(int64_t N, int64_t K);
+ALB_API size_t alb_q4_0_scale_offset(int64_t N, int64_t K);
+/* format_repack / repack<block_q4_0,4,4> (types.cpp:199-240): block_q4_0 rows
+ * [N][K/32] (device) -> alb GPU layout (device). */
+ALB_API int alb_repack_q4_0(void * dst, const void * src_blocks, int64_t N, int64_t K, void * stream);
+/* inverse of alb_repack_q4_0 (tests / export) */
+ALB_API int alb_unpack_q4_0(void * dst_blocks, const void * src, int64_t N, int64_t K, void * stream);
+
+/* ----------------------------------------------------------- quantization */
+/* quantize_row_q8_0 (arm.cpp:1819-1853) / nnml_quantize_mat_q8_0_4x4
+ * (gemm.cpp:1943-2009): fp32 [rows][K] -> block_q8_0 [rows][K/32], RNE. */
+ALB_API int alb_quantize_q8_0(const float * x, void * xq, int64_t K, int64_t rows, void * stream);
+
+/* ------------------------------------------------------------------- GEMV */
+/* nnml_gemv_q4_0_4x4_q8_0 (gemm.cpp:127-190) driven by forward_mul_mat
+ * (arm.cpp:1855-1925), ne11 = 1: y[n] = sum_b I(n,b) * f32(dw) * f32(dx)
+ * (+ residual[n] when non-null: the ADD of qwen3.cpp:239/270 fused).
+ * W in the alb GPU layout, xq block_q8_0 [K/32]. */
+ALB_API int alb_gemv_q4_0_q8_0(const void * W, const void * xq, float * y, int64_t N, int64_t K,
+                       const float * residual, void * stream);
+/* Debug twin of alb_gemv_q4_0_q8_0 writing the int32 block dots I[N][K/32]. */
+ALB_API int alb_gemv_q4_0_q8_0_block_dots(const void * W, const void * xq, int32_t * I, int64_t N, int64_t K,
+                                  void * stream);
+
+/* ----------------------------------------------------------- elementwise */
+/* RMS_NORM (ops.cpp:680-724; double sum of squares) followed by the graph's
+ * MUL by w (binary.cpp:15-23, cgraph.cpp:115-120); w may be NULL.  x, y [rows][n]. */
+ALB_API int alb_rms_norm(const float * x, const float * w, float * y, int64_t rows, int64_t n, float eps, void * stream);
+/* swiglu_split (ops.cpp:1038-1092, arm.cpp:1789-1809): y = silu(g) * u. */
+ALB_API int alb_swiglu(const float * g, const float * u, float * y, int64_t n, void * stream);
+/* GET_ROWS of a Q4_0 table in the alb GPU layout (ops.cpp:12-52): out [n_ids][K]. */
+ALB_API int alb_get_rows_q4_0(const void * W, int64_t n_rows, int64_t K, const int32_t * ids, int64_t n_ids,
+                              float * out, void * stream);
+/* RoPE cos/sin table of nnml_rope_cache_init (ops.cpp:759-771; NEOX, ext_factor 0,
+ * freq_scale 1): host-computed, copied to table_dev [max_pos][head_dim/2] (cos, sin). */
+ALB_API int alb_rope_table(float * table_dev, int32_t max_pos, int32_t head_dim, float freq_base);
+/* Per-head QK-RMSNorm * w + NEOX RoPE of Q and K and the fp16 KV store of K and V
+ * (qwen3.cpp:215-224, ops.cpp:830-938, set_rows ops.cpp:135-181).  qkv [T][(Hq+2Hkv)*128]
+ * fp32 (the fused QKV projection), q_out [T][Hq][128], caches [cells][Hkv][128] fp16;
+ * token t is at position pos0+t.  head_dim is 128. */
+ALB_API int alb_qk_norm_rope_kv(const float * qkv, int64_t T, int32_t n_head, int32_t n_head_kv,
+                                const float * q_norm, const float * k_norm, float eps, const float * rope_table,
+                                int32_t pos0, float * q_out, uint16_t * k_cache, uint16_t * v_cache, void * stream);
+
+/* ------------------------------------------------------------- attention */
+/* nnml_compute_forward_flash_attn_ext_f16 (arm.cpp:2196-2433), one sequence,
+ * causal: token t (position pos0+t) attends cells [0, pos0+t] of the fp16
+ * caches [cells][Hkv][128]; GQA ratio n_head/n_head_kv in {1,2,4,8}; split-K
+ * over `splits` ranges merged in-kernel.  The workspace must be zeroed once
+ * before first use (its tickets are re-armed by every call).  q/out [T][Hq][128]. */
+ALB_API size_t alb_flash_attn_workspace_bytes(int32_t n_head, int32_t n_head_kv, int64_t T, int32_t splits);
+ALB_API int alb_flash_attn(const float * q, const uint16_t * k_cache, const uint16_t * v_cache, int64_t T,
+                           int32_t n_head, int32_t n_head_kv, int32_t pos0, float scale, int32_t splits,
+                           void * workspace, float * out, void * stream);
+
+/* -------------------------------------------------------------- sampling */
+/* sample_none (sampler.cpp:34-36): first index of the maximum of x[0..n).
+ * scratch >= 1024 bytes, zeroed once before first use. */
+ALB_API int alb_argmax(const float * x, int64_t n, void * scratch, int32_t * idx_out, void * stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ALB_CUDA_H */

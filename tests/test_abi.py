@@ -1,0 +1,48 @@
+"""CPU checks of the C-ABI library: it loads, and exports every symbol that
+include/alb_cuda.h declares.  No compute call is made (no GPU here)."""
+import ctypes as C
+import subprocess
+
+import pytest
+
+import arclight_b200 as A
+
+
+def test_library_is_built_and_loads():
+    L = A.lib()
+    assert L.alb_version() >= 100
+
+
+def test_every_header_symbol_is_exported():
+    syms = A.header_symbols()
+    assert len(syms) >= 8
+    out = subprocess.run(["nm", "-D", "--defined-only", A.LIB_PATH], capture_output=True, text=True, check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if line.strip()}
+    missing = [s for s in syms if s not in exported]
+    assert not missing, f"declared in alb_cuda.h but not exported: {missing}"
+
+
+def test_only_c_abi_symbols_are_exported():
+    out = subprocess.run(["nm", "-D", "--defined-only", A.LIB_PATH], capture_output=True, text=True, check=True).stdout
+    ours = [l.split()[-1] for l in out.splitlines() if " T " in l]
+    leaked = [s for s in ours if not s.startswith("alb_") and not s.startswith("_init") and not s.startswith("_fini")]
+    assert not leaked, f"non-ABI symbols exported: {leaked[:10]}"
+
+
+def test_q4_gpu_layout_sizes():
+    L = A.lib()
+    # nibble plane N*K/2 (256-aligned) + scale plane N*K/16
+    assert L.alb_q4_0_scale_offset(9728, 2560) == 9728 * 1280
+    assert L.alb_q4_0_gpu_bytes(9728, 2560) == 9728 * 1280 + 9728 * 160
+    assert L.alb_q4_0_scale_offset(3, 32) == 256
+    # every plane start is 16-byte aligned for the vector loads
+    for n, k in [(1, 32), (7, 96), (151936, 2560), (1216, 2560)]:
+        assert L.alb_q4_0_scale_offset(n, k) % 256 == 0
+
+
+def test_invalid_arguments_are_rejected_without_a_gpu():
+    L = A.lib()
+    # null pointers / bad K are caught on the host before any CUDA call
+    assert L.alb_gemv_q4_0_q8_0(None, None, None, 16, 2560, None, None) == -1
+    assert L.alb_quantize_q8_0(None, None, 33, 1, None) == -1
+    assert b"invalid argument" in L.alb_last_error()

@@ -1,0 +1,138 @@
+"""GPU parity of the elementwise, attention and sampling kernels (C ABI) vs the oracle."""
+import math
+
+import numpy as np
+import pytest
+
+import arclight_b200 as A
+from oracle import lib as O
+from tests.util import assert_rel
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+L = None
+
+
+def setup_module():
+    global L
+    L = A.lib()
+
+
+def st():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def cu(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+@pytest.mark.parametrize("rows,n", [(1, 2560), (3, 4096), (40, 128), (2, 1024)])
+def test_rms_norm(rows, n):
+    rng = np.random.default_rng(n + rows)
+    x = (rng.standard_normal((rows, n)) * 3).astype(np.float32)
+    w = (1 + 0.01 * rng.standard_normal(n)).astype(np.float32)
+    X, W = cu(x), cu(w)
+    Y = torch.empty_like(X)
+    A.check(L.alb_rms_norm(X.data_ptr(), W.data_ptr(), Y.data_ptr(), rows, n, 1e-6, st()))
+    torch.cuda.synchronize()
+    # double-precision sum in a different order: identical in practice; 1e-6 bound
+    assert_rel(Y.cpu().numpy(), O.rms_norm(x, w), rtol=1e-6, what="rms_norm")
+
+
+def test_swiglu():
+    rng = np.random.default_rng(1)
+    g = (rng.standard_normal(9728) * 4).astype(np.float32)
+    u = rng.standard_normal(9728).astype(np.float32)
+    Y = torch.empty(9728, dtype=torch.float32, device="cuda")
+    A.check(L.alb_swiglu(cu(g).data_ptr(), cu(u).data_ptr(), Y.data_ptr(), 9728, st()))
+    torch.cuda.synchronize()
+    assert_rel(Y.cpu().numpy(), O.swiglu(g, u), what="swiglu")
+
+
+def test_get_rows_bit_exact():
+    rng = np.random.default_rng(2)
+    tab = O.quantize_q4_0((rng.standard_normal((1000, 256)) * 0.02).astype(np.float32))
+    src = cu(tab.view(np.uint8).reshape(-1))
+    W = torch.empty(L.alb_q4_0_gpu_bytes(1000, 256), dtype=torch.uint8, device="cuda")
+    A.check(L.alb_repack_q4_0(W.data_ptr(), src.data_ptr(), 1000, 256, st()))
+    ids = np.array([0, 999, 17, 17, 500], np.int32)
+    out = torch.empty((5, 256), dtype=torch.float32, device="cuda")
+    A.check(L.alb_get_rows_q4_0(W.data_ptr(), 1000, 256, cu(ids).data_ptr(), 5, out.data_ptr(), st()))
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out.cpu().numpy(), np.stack([O.dequantize_q4_0(tab[i]) for i in ids]))
+
+
+def rope_table(max_pos):
+    t = torch.empty(max_pos * 64 * 2, dtype=torch.float32, device="cuda")
+    A.check(L.alb_rope_table(t.data_ptr(), max_pos, 128, 1e6))
+    return t
+
+
+@pytest.mark.parametrize("Hq,Hkv,T,pos0", [(32, 8, 1, 0), (32, 8, 1, 4095), (16, 8, 5, 100), (4, 1, 3, 32760)])
+def test_qk_norm_rope_kv(Hq, Hkv, T, pos0):
+    rng = np.random.default_rng(Hq * 7 + T)
+    qkv = (rng.standard_normal((T, (Hq + 2 * Hkv) * 128)) * 2).astype(np.float32)
+    qn = (1 + 0.01 * rng.standard_normal(128)).astype(np.float32)
+    kn = (1 + 0.01 * rng.standard_normal(128)).astype(np.float32)
+    cells = pos0 + T + 1
+    rt = rope_table(cells)
+    Q = torch.empty((T, Hq, 128), dtype=torch.float32, device="cuda")
+    KC = torch.zeros((cells, Hkv, 128), dtype=torch.int16, device="cuda")
+    VC = torch.zeros((cells, Hkv, 128), dtype=torch.int16, device="cuda")
+    A.check(L.alb_qk_norm_rope_kv(cu(qkv).data_ptr(), T, Hq, Hkv, cu(qn).data_ptr(), cu(kn).data_ptr(), 1e-6,
+                                  rt.data_ptr(), pos0, Q.data_ptr(), KC.data_ptr(), VC.data_ptr(), st()))
+    torch.cuda.synchronize()
+    q = qkv[:, :Hq * 128].reshape(T, Hq, 128)
+    k = qkv[:, Hq * 128:(Hq + Hkv) * 128].reshape(T, Hkv, 128)
+    v = qkv[:, (Hq + Hkv) * 128:].reshape(T, Hkv, 128)
+    for t in range(T):
+        qr = O.rope_neox(O.rms_norm(q[t], qn), pos0 + t)
+        kr = O.rope_neox(O.rms_norm(k[t], kn), pos0 + t)
+        assert_rel(Q.cpu().numpy()[t], qr, rtol=1e-6, what="q")
+        kg = KC.cpu().numpy()[pos0 + t].view(np.float16).astype(np.float32)
+        assert_rel(kg, O.fp32_to_fp16(kr).view(np.float16).astype(np.float32), rtol=1e-3, what="k cache")
+        np.testing.assert_array_equal(VC.cpu().numpy()[pos0 + t].view(np.uint16), O.fp32_to_fp16(v[t]))
+
+
+@pytest.mark.parametrize("Hq,Hkv,T,pos0,S", [
+    (32, 8, 1, 639, 74),     # 4B decode at the config-3 mean position
+    (32, 8, 1, 0, 74),       # first token: one cell, most splits empty
+    (16, 8, 1, 200, 16),     # 0.6B GQA 2:1
+    (4, 1, 1, 4095, 296),    # TP=8 shard of the 8B (1 kv head), long
+    (32, 8, 7, 100, 1),      # small prefill ubatch, causal within the ubatch
+    (32, 8, 64, 0, 1),       # prefill from an empty cache
+])
+def test_flash_attn(Hq, Hkv, T, pos0, S):
+    rng = np.random.default_rng(Hq + T + pos0)
+    cells = pos0 + T
+    k = O.fp32_to_fp16(rng.standard_normal((cells, Hkv, 128)).astype(np.float32))
+    v = O.fp32_to_fp16(rng.standard_normal((cells, Hkv, 128)).astype(np.float32))
+    q = (rng.standard_normal((T, Hq, 128)) * 0.5).astype(np.float32)
+    kv_len = (pos0 + np.arange(T) + 1).astype(np.int32)
+    scale = 1.0 / math.sqrt(128.0)
+    ws = torch.zeros(max(1, L.alb_flash_attn_workspace_bytes(Hq, Hkv, T, S)), dtype=torch.uint8, device="cuda")
+    out = torch.empty((T, Hq, 128), dtype=torch.float32, device="cuda")
+    Kd, Vd, Qd = cu(k.view(np.int16)), cu(v.view(np.int16)), cu(q)
+    for rep in range(2):  # second call checks the re-armed tickets
+        A.check(L.alb_flash_attn(Qd.data_ptr(), Kd.data_ptr(), Vd.data_ptr(), T, Hq, Hkv, pos0, scale, S,
+                                 ws.data_ptr(), out.data_ptr(), st()))
+        torch.cuda.synchronize()
+        ref = O.flash_attn(q, k, v, kv_len, scale, mode=0)
+        assert_rel(out.cpu().numpy(), ref, what=f"flash_attn rep {rep}")
+    # the reference's own fp16-accumulating path differs from fp32 by its fp16 rounding
+    ref16 = O.flash_attn(q, k, v, kv_len, scale, mode=1)
+    assert_rel(out.cpu().numpy(), ref16, rtol=2e-2, what="flash_attn vs arm-faithful fp16")
+
+
+@pytest.mark.parametrize("n", [151936, 18992, 1, 1000])
+def test_argmax_first_max(n):
+    rng = np.random.default_rng(n)
+    x = rng.standard_normal(n).astype(np.float32)
+    if n > 10:
+        x[n // 3] = x[n - 2] = 50.0   # tie: first index wins (std::max_element)
+    scratch = torch.zeros(1024, dtype=torch.uint8, device="cuda")
+    idx = torch.empty(1, dtype=torch.int32, device="cuda")
+    for _ in range(2):
+        A.check(L.alb_argmax(cu(x).data_ptr(), n, scratch.data_ptr(), idx.data_ptr(), st()))
+        torch.cuda.synchronize()
+        assert int(idx.item()) == O.argmax(x)
