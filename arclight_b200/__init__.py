@@ -68,9 +68,23 @@ def _declare(L: C.CDLL) -> None:
         "alb_get_rows_q4_0": (ci, [vp, i64, i64, vp, i64, vp, vp]),
         "alb_rope_table": (ci, [vp, i32, i32, f32]),
         "alb_qk_norm_rope_kv": (ci, [vp, i64, i32, i32, vp, vp, f32, vp, i32, vp, vp, vp, vp]),
-        "alb_flash_attn_workspace_bytes": (sz, [i32, i32, i64, i32]),
+        "alb_flash_attn_workspace_bytes": (sz, [i32, i32, i64, i32, i32]),
         "alb_flash_attn": (ci, [vp, vp, vp, i64, i32, i32, i32, f32, i32, vp, vp, vp]),
         "alb_argmax": (ci, [vp, i64, vp, vp, vp]),
+        "alb_nccl_unique_id": (ci, [vp]),
+        "alb_engine_create": (ci, [vp, C.c_uint64, i32, i32, i32, i32, vp, i32, vp]),
+        "alb_engine_destroy": (ci, [vp]),
+        "alb_engine_device_bytes": (sz, [vp]),
+        "alb_engine_reset": (ci, [vp]),
+        "alb_engine_prefill": (ci, [vp, vp, i32, i32, vp]),
+        "alb_engine_decode": (ci, [vp, i32, i32, vp]),
+        "alb_engine_decode_loop": (ci, [vp, i32, i32, i32, vp, i32]),
+        "alb_engine_logits": (ci, [vp, vp, i64]),
+        "alb_engine_info": (ci, [vp, vp, i32]),
+        "alb_engine_stream": (vp, [vp]),
+        "alb_engine_weight_blocks": (ci, [vp, i32, i32, vp, vp, vp]),
+        "alb_engine_norm_weights": (ci, [vp, i32, i32, vp, i64]),
+        "alb_engine_fill_kv": (ci, [vp, i32, C.c_uint64]),
     }
     for name, (res, args) in sigs.items():
         if hasattr(L, name):

@@ -72,9 +72,10 @@ extern "C" int alb_qk_norm_rope_kv(const float * qkv, int64_t T, int32_t n_head,
     return ALB_OK;
 }
 
-extern "C" size_t alb_flash_attn_workspace_bytes(int32_t n_head, int32_t n_head_kv, int64_t T, int32_t splits) {
-    if (n_head <= 0 || n_head_kv <= 0 || T <= 0 || splits <= 0) return 0;
-    return flash_attn_ws_bytes(n_head, n_head_kv, (int)T, splits);
+extern "C" size_t alb_flash_attn_workspace_bytes(int32_t n_head, int32_t n_head_kv, int64_t T, int32_t splits,
+                                                 int32_t n_cells) {
+    if (n_head <= 0 || n_head_kv <= 0 || T <= 0 || splits <= 0 || n_cells <= 0) return 0;
+    return flash_attn_ws_bytes(n_head, n_head_kv, (int)T, splits, n_cells);
 }
 
 extern "C" int alb_flash_attn(const float * q, const uint16_t * k_cache, const uint16_t * v_cache, int64_t T,
@@ -84,8 +85,9 @@ extern "C" int alb_flash_attn(const float * q, const uint16_t * k_cache, const u
     ALB_CHECK_ARG(n_head > 0 && n_head_kv > 0 && n_head % n_head_kv == 0);
     const int G = n_head / n_head_kv;
     ALB_CHECK_ARG(G == 1 || G == 2 || G == 4 || G == 8);
-    ALB_CHECK_ARG(splits >= 1 && splits <= 65535 && (splits == 1 || workspace));
+    ALB_CHECK_ARG(splits >= 1 && splits <= 65535 && (int64_t)pos0 + T < (int64_t)1 << 30);
     FlashArgs f;
+    f.ncap = (int)(pos0 + T);
     f.q = q; f.kc = k_cache; f.vc = v_cache; f.Hq = n_head; f.Hkv = n_head_kv; f.T = (int)T;
     f.pos0 = pos0; f.scale = scale; f.S = splits; f.ws = (float *)workspace; f.out = out; f.pdl = true;
     ALB_CUDA_TRY(launch_flash_attn(f, (cudaStream_t)stream));

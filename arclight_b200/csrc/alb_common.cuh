@@ -58,6 +58,11 @@ __device__ __forceinline__ float alb_warp_sum(float v) {
     for (int o = W / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     return v;
 }
+__device__ __forceinline__ double alb_warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
 __device__ __forceinline__ float alb_warp_max(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -125,4 +130,33 @@ __device__ __forceinline__ bool alb_mbar_wait(uint64_t * bar, uint32_t parity, u
 __device__ __forceinline__ void alb_bulk_g2s(void * dst_smem, const void * src, uint32_t bytes, uint64_t * bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                  :: "r"(alb_smem_addr(dst_smem)), "l"(src), "r"(bytes), "r"(alb_smem_addr(bar)) : "memory");
+}
+
+// ---------------------------------------------------------------- reference expf / silu
+// nnml_v_expf (arm.cpp:1757-1787) per lane, so SwiGLU matches the reference's
+// NEON path bit for bit: exp(x) = 2^n (1 + p(b)), n from the 1.5*2^23 shift,
+// b = x - n ln2 (two-part ln2), degree-5 polynomial; |n| > 126 / > 192 use the
+// scaled / saturated forms.  Same algorithm, restated with explicit roundings.
+__device__ __forceinline__ float alb_ref_expf(float x) {
+    const float r = 0x1.8p23f;
+    const float z = __fmaf_rn(x, 0x1.715476p+0f, r);
+    const float n = __fsub_rn(z, r);
+    const float b = __fmaf_rn(-n, 0x1.7f7d1cp-20f, __fmaf_rn(-n, 0x1.62e4p-1f, x));
+    const uint32_t e = __float_as_uint(z) << 23;
+    const float k = __uint_as_float(e + 0x3f800000u);
+    const float u = __fmul_rn(b, b);
+    const float j = __fmaf_rn(__fmaf_rn(__fmaf_rn(0x1.0e4020p-7f, b, 0x1.573e2ep-5f), u,
+                                        __fmaf_rn(0x1.555e66p-3f, b, 0x1.fffdb6p-2f)),
+                              u, __fmul_rn(0x1.ffffecp-1f, b));
+    const float an = fabsf(n);
+    if (!(an > 126.0f)) return __fmaf_rn(j, k, k);
+    const uint32_t d = (n <= 0.0f) ? 0x82000000u : 0u;
+    const float s1 = __uint_as_float(d + 0x7f000000u);
+    const float s2 = __uint_as_float(e - d);
+    if (an > 192.0f) return __fmul_rn(s1, s1);
+    return __fmul_rn(__fmaf_rn(s2, j, s2), s1);
+}
+// nnml_vec_swiglu_f32 NEON path (arm.cpp:1789-1809): (x / (1 + exp(0 - x))) * g
+__device__ __forceinline__ float alb_swiglu1(float x, float g) {
+    return __fmul_rn(__fdiv_rn(x, __fadd_rn(1.0f, alb_ref_expf(__fsub_rn(0.0f, x)))), g);
 }

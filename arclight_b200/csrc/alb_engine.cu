@@ -1,0 +1,511 @@
+// Qwen3 Q4_0 decode/prefill engine: the B200 counterpart of the reference's
+// llm_model + nnml_cgraph + llm_kv_cache + decoding_context for one sequence.
+//
+// One engine per GPU (one process or thread per GPU).  With tp_size > 1 the
+// weights are sharded exactly as the reference's NUMA tensor parallelism
+// (model.cpp:21-130): Q/K/V and gate/up by output rows (whole heads / 32-row
+// units), O and down by input columns, norms replicated, KV cache by KV head
+// (cgraph.cpp:962-973); the reference's GATHER (ops.cpp:1465-1511) becomes an
+// NCCL sum all-reduce of the residual stream after O and after down.  The lm
+// head is sharded by vocabulary rows and the greedy argmax is an all-reduce
+// MAX over (value, index) keys.
+//
+// A decode step is one CUDA graph (captured once): every kernel is launched as
+// a programmatic dependent of the previous one, reads the token and position
+// from device memory and writes the next token back, so a greedy loop needs
+// no host round trip.  Prefill runs the same ops over a ubatch of T tokens.
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <vector>
+
+#include "alb_common.cuh"
+#include "alb_internal.h"
+#include "alb_nccl.h"
+
+namespace alb {
+void normal_table_host(std::vector<float> & t);
+uint64_t tensor_seed(uint64_t model_seed, int layer, int kind);
+void rope_table_host(std::vector<float> & t, int32_t max_pos, int32_t head_dim, float freq_base);
+cudaError_t gen_q4(uint8_t * W, int64_t N_total, int64_t K, int64_t dst_row0, int64_t dst_row_stride, int64_t n_rows,
+                   uint64_t seed, int64_t src_row0, int64_t K_full, int64_t c0, const float * table, cudaStream_t st);
+cudaError_t gen_norm(float * w, int64_t n, uint64_t seed, const float * table, cudaStream_t st);
+cudaError_t gen_f16(uint16_t * dst, int64_t cells, int64_t row, int64_t full_row, int64_t col0, uint64_t seed,
+                    const float * table, cudaStream_t st);
+
+enum Kind { T_TOK_EMBD = 0, T_OUTPUT = 1, T_OUTPUT_NORM = 2, T_ATTN_NORM = 3, T_WQ = 4, T_WK = 5, T_WV = 6, T_WO = 7,
+            T_Q_NORM = 8, T_K_NORM = 9, T_FFN_NORM = 10, T_GATE = 11, T_UP = 12, T_DOWN = 13 };
+
+__global__ void k_advance(int32_t * tok, int32_t * pos, const int32_t * next, int32_t * out, int32_t * step, int32_t cap) {
+    alb_pdl_wait();
+    const int32_t n = *next;
+    const int32_t s = *step;
+    if (s < cap) out[s] = n;
+    *step = s + 1;
+    *tok = n;
+    *pos = *pos + 1;
+}
+}  // namespace alb
+
+using namespace alb;
+
+struct alb_engine {
+    alb_qwen3_config c;
+    uint64_t seed = 0;
+    int32_t max_ctx = 0, max_ub = 0, rank = 0, tp = 1;
+    int E = 0, Hq = 0, Hkv = 0, F = 0, V = 0, Dq = 0, Dkv = 0, Nqkv = 0, v0 = 0;
+    int dev = 0;
+    cudaStream_t st = nullptr;
+    void * comm = nullptr;
+    struct Layer {
+        uint8_t * qkv = nullptr, * o = nullptr, * gu = nullptr, * down = nullptr;
+        float * an = nullptr, * fn = nullptr, * qn = nullptr, * kn = nullptr;
+        uint16_t * kc = nullptr, * vc = nullptr;
+    };
+    std::vector<Layer> layers;
+    uint8_t * tok = nullptr, * out_w = nullptr;
+    const uint8_t * lm_W = nullptr, * lm_S = nullptr;
+    float * out_norm = nullptr, * table = nullptr, * rope = nullptr;
+    float * x = nullptr, * qkv = nullptr, * q = nullptr, * att = nullptr, * h = nullptr, * logits = nullptr;
+    int32_t * tok_dev = nullptr, * pos_dev = nullptr, * next_dev = nullptr, * step_dev = nullptr, * gen_out = nullptr;
+    int32_t gen_cap = 0;
+    unsigned long long * key = nullptr;
+    void * am_scratch = nullptr;
+    float * fa_ws = nullptr;
+    int fa_S_decode = 1;
+    size_t fa_ws_bytes = 0;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t gexec = nullptr;
+    bool graph_loop = false;        // graph also advances token/pos (greedy loop)
+    std::vector<void *> allocs;
+    size_t bytes = 0;
+    int32_t * pinned = nullptr;     // host staging for the e2e path
+    int launches_per_step = 0;
+
+    template <typename T> int alloc(T ** p, size_t n) {
+        void * v = nullptr;
+        const size_t b = (n * sizeof(T) + 255) & ~(size_t)255;
+        if (cudaMalloc(&v, b) != cudaSuccess) { alb_set_last_error_msg("cudaMalloc failed (engine)"); return ALB_ERR_OOM; }
+        allocs.push_back(v);
+        bytes += b;
+        *p = static_cast<T *>(v);
+        return ALB_OK;
+    }
+};
+
+#define ALB_TRY(expr) do { int r__ = (expr); if (r__ != ALB_OK) return r__; } while (0)
+
+static int engine_allreduce_x(alb_engine * e, int64_t T) {
+    if (e->tp <= 1) return ALB_OK;
+    return nccl_allreduce(e->comm, e->x, e->x, (size_t)T * e->E, 0, 0, e->st);
+}
+
+// One ubatch of T tokens (token ids in tok_dev[0..T), first position in pos_dev)
+// through the whole model, ending with the greedy next token in next_dev.
+static int engine_forward(alb_engine * e, int64_t T, bool pdl, int ncap_prefill = 0) {
+    const alb_qwen3_config & c = e->c;
+    cudaStream_t st = e->st;
+    int launches = 0;
+    ALB_CUDA_TRY(launch_embed(e->tok, e->tok + q4_scale_offset(c.n_vocab, e->E), c.n_vocab, e->E, e->tok_dev,
+                              (int)T, e->x, pdl, st));
+    ++launches;
+    auto gemv = [&](const uint8_t * W, int64_t N, int64_t K, int in, const void * x, const float * nw, int out,
+                    float * y, const float * res) -> cudaError_t {
+        GemvArgs a;
+        a.W = W; a.S = W + q4_scale_offset(N, K); a.N = N; a.K = K;
+        a.in_mode = in; a.x = x; a.norm_w = nw; a.eps = c.eps;
+        a.out_mode = out; a.y = y; a.residual = res; a.pdl = pdl;
+        ++launches;
+        if (T == 1) return launch_gemv(a, st);
+        a.x_stride = K; a.y_stride = out == GEMV_OUT_SWIGLU ? N / 2 : N;
+        launches += (int)((T + 7) / 8) - 1;
+        return launch_gemv_tokens(a, T, st);
+    };
+    const int S = T == 1 ? e->fa_S_decode : 1;
+    for (int l = 0; l < c.n_layer; ++l) {
+        alb_engine::Layer & L = e->layers[l];
+        ALB_CUDA_TRY(gemv(L.qkv, e->Nqkv, e->E, GEMV_IN_F32_RMS, e->x, L.an, GEMV_OUT_PLAIN, e->qkv, nullptr));
+        QkvArgs qa;
+        qa.qkv = e->qkv; qa.qkv_stride = e->Nqkv; qa.Hq = e->Hq; qa.Hkv = e->Hkv; qa.T = (int)T;
+        qa.q_norm = L.qn; qa.k_norm = L.kn; qa.eps = c.eps; qa.rope = reinterpret_cast<const float2 *>(e->rope);
+        qa.pos_dev = e->pos_dev; qa.q_out = e->q; qa.kc = L.kc; qa.vc = L.vc; qa.pdl = pdl;
+        ALB_CUDA_TRY(launch_qk_norm_rope_kv(qa, st));
+        FlashArgs fa;
+        fa.q = e->q; fa.kc = L.kc; fa.vc = L.vc; fa.Hq = e->Hq; fa.Hkv = e->Hkv; fa.T = (int)T;
+        fa.pos_dev = e->pos_dev; fa.scale = 1.0f / sqrtf((float)c.head_dim); fa.S = S; fa.ws = e->fa_ws;
+        fa.ncap = T == 1 ? e->max_ctx : ncap_prefill;
+        fa.out = e->att; fa.pdl = pdl;
+        ALB_CUDA_TRY(launch_flash_attn(fa, st));
+        launches += 2;
+        ALB_CUDA_TRY(gemv(L.o, e->E, e->Dq, GEMV_IN_F32, e->att, nullptr, GEMV_OUT_PLAIN, e->x,
+                          e->rank == 0 ? e->x : nullptr));
+        ALB_TRY(engine_allreduce_x(e, T));
+        ALB_CUDA_TRY(gemv(L.gu, 2 * (int64_t)e->F, e->E, GEMV_IN_F32_RMS, e->x, L.fn, GEMV_OUT_SWIGLU, e->h, nullptr));
+        ALB_CUDA_TRY(gemv(L.down, e->E, e->F, GEMV_IN_F32, e->h, nullptr, GEMV_OUT_PLAIN, e->x,
+                          e->rank == 0 ? e->x : nullptr));
+        ALB_TRY(engine_allreduce_x(e, T));
+        if (e->tp > 1) launches += 2;
+    }
+    // final norm + lm_head on the last token (qwen3.cpp:235-238, 266-274)
+    {
+        GemvArgs a;
+        a.W = e->lm_W; a.S = e->lm_S; a.N = e->V; a.K = e->E;
+        a.in_mode = GEMV_IN_F32_RMS; a.x = e->x + (size_t)(T - 1) * e->E; a.norm_w = e->out_norm; a.eps = c.eps;
+        a.out_mode = GEMV_OUT_PLAIN; a.y = e->logits; a.pdl = pdl;
+        ALB_CUDA_TRY(launch_gemv(a, st));
+        ++launches;
+    }
+    if (e->tp == 1) {
+        ALB_CUDA_TRY(launch_argmax(e->logits, e->V, 0, e->am_scratch, e->key, e->next_dev, pdl, st));
+        ++launches;
+    } else {
+        ALB_CUDA_TRY(launch_argmax(e->logits, e->V, e->v0, e->am_scratch, e->key, nullptr, pdl, st));
+        ALB_TRY(nccl_allreduce(e->comm, e->key, e->key, 1, 1, 1, st));
+        ALB_CUDA_TRY(launch_key_to_index(e->key, e->next_dev, false, st));
+        launches += 3;
+    }
+    e->launches_per_step = launches;
+    return ALB_OK;
+}
+
+static int engine_build_graph(alb_engine * e) {
+    if (e->gexec) return ALB_OK;
+    ALB_CUDA_TRY(cudaStreamBeginCapture(e->st, cudaStreamCaptureModeThreadLocal));
+    int rc = engine_forward(e, 1, true);
+    if (rc == ALB_OK) {
+        const cudaError_t le = alb_launch(k_advance, dim3(1), dim3(1), 0, e->st, true, e->tok_dev, e->pos_dev,
+                                          (const int32_t *)e->next_dev, e->gen_out, e->step_dev, e->gen_cap);
+        if (le != cudaSuccess) { alb_set_last_cuda_error(le, "k_advance"); rc = ALB_ERR_CUDA; }
+    }
+    cudaGraph_t g = nullptr;
+    const cudaError_t ce = cudaStreamEndCapture(e->st, &g);
+    if (rc != ALB_OK) { if (g) cudaGraphDestroy(g); return rc; }
+    ALB_CUDA_TRY(ce);
+    e->graph = g;
+    ALB_CUDA_TRY(cudaGraphInstantiate(&e->gexec, g, 0));
+    e->launches_per_step += 1;
+    return ALB_OK;
+}
+
+static int engine_init_weights(alb_engine * e) {
+    const alb_qwen3_config & c = e->c;
+    cudaStream_t st = e->st;
+    std::vector<float> tab;
+    normal_table_host(tab);
+    ALB_TRY(e->alloc(&e->table, tab.size()));
+    ALB_CUDA_TRY(cudaMemcpyAsync(e->table, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice, st));
+    const int64_t E = e->E, HD = c.head_dim;
+    const int64_t Dq_full = (int64_t)c.n_head * HD, Dkv_full = (int64_t)c.n_head_kv * HD;
+    auto seed = [&](int layer, int kind) { return tensor_seed(e->seed, layer, kind); };
+    // token table: full on every rank (embedding lookup; tied lm_head shard is a view)
+    ALB_TRY(e->alloc(&e->tok, q4_gpu_bytes(c.n_vocab, E)));
+    ALB_CUDA_TRY(gen_q4(e->tok, c.n_vocab, E, 0, 1, c.n_vocab, seed(-1, T_TOK_EMBD), 0, E, 0, e->table, st));
+    if (c.tied) {
+        e->lm_W = e->tok + (size_t)e->v0 * (E / 2);
+        e->lm_S = e->tok + q4_scale_offset(c.n_vocab, E) + (size_t)e->v0 * q4_scale_pitch(E) * 2;
+    } else {
+        ALB_TRY(e->alloc(&e->out_w, q4_gpu_bytes(e->V, E)));
+        ALB_CUDA_TRY(gen_q4(e->out_w, e->V, E, 0, 1, e->V, seed(-1, T_OUTPUT), e->v0, E, 0, e->table, st));
+        e->lm_W = e->out_w;
+        e->lm_S = e->out_w + q4_scale_offset(e->V, E);
+    }
+    ALB_TRY(e->alloc(&e->out_norm, E));
+    ALB_CUDA_TRY(gen_norm(e->out_norm, E, seed(-1, T_OUTPUT_NORM), e->table, st));
+    e->layers.resize(c.n_layer);
+    const int64_t cells = e->max_ctx;
+    for (int l = 0; l < c.n_layer; ++l) {
+        alb_engine::Layer & L = e->layers[l];
+        ALB_TRY(e->alloc(&L.qkv, q4_gpu_bytes(e->Nqkv, E)));
+        ALB_CUDA_TRY(gen_q4(L.qkv, e->Nqkv, E, 0, 1, e->Dq, seed(l, T_WQ), (int64_t)e->rank * e->Dq, E, 0, e->table, st));
+        ALB_CUDA_TRY(gen_q4(L.qkv, e->Nqkv, E, e->Dq, 1, e->Dkv, seed(l, T_WK), (int64_t)e->rank * e->Dkv, E, 0, e->table, st));
+        ALB_CUDA_TRY(gen_q4(L.qkv, e->Nqkv, E, e->Dq + e->Dkv, 1, e->Dkv, seed(l, T_WV), (int64_t)e->rank * e->Dkv, E, 0,
+                            e->table, st));
+        ALB_TRY(e->alloc(&L.o, q4_gpu_bytes(E, e->Dq)));
+        ALB_CUDA_TRY(gen_q4(L.o, E, e->Dq, 0, 1, E, seed(l, T_WO), 0, Dq_full, (int64_t)e->rank * e->Dq, e->table, st));
+        ALB_TRY(e->alloc(&L.gu, q4_gpu_bytes(2 * (int64_t)e->F, E)));
+        ALB_CUDA_TRY(gen_q4(L.gu, 2 * (int64_t)e->F, E, 0, 2, e->F, seed(l, T_GATE), (int64_t)e->rank * e->F, E, 0, e->table, st));
+        ALB_CUDA_TRY(gen_q4(L.gu, 2 * (int64_t)e->F, E, 1, 2, e->F, seed(l, T_UP), (int64_t)e->rank * e->F, E, 0, e->table, st));
+        ALB_TRY(e->alloc(&L.down, q4_gpu_bytes(E, e->F)));
+        ALB_CUDA_TRY(gen_q4(L.down, E, e->F, 0, 1, E, seed(l, T_DOWN), 0, c.n_ff, (int64_t)e->rank * e->F, e->table, st));
+        ALB_TRY(e->alloc(&L.an, E));
+        ALB_TRY(e->alloc(&L.fn, E));
+        ALB_TRY(e->alloc(&L.qn, HD));
+        ALB_TRY(e->alloc(&L.kn, HD));
+        ALB_CUDA_TRY(gen_norm(L.an, E, seed(l, T_ATTN_NORM), e->table, st));
+        ALB_CUDA_TRY(gen_norm(L.fn, E, seed(l, T_FFN_NORM), e->table, st));
+        ALB_CUDA_TRY(gen_norm(L.qn, HD, seed(l, T_Q_NORM), e->table, st));
+        ALB_CUDA_TRY(gen_norm(L.kn, HD, seed(l, T_K_NORM), e->table, st));
+        ALB_TRY(e->alloc(&L.kc, (size_t)cells * e->Dkv));
+        ALB_TRY(e->alloc(&L.vc, (size_t)cells * e->Dkv));
+        ALB_CUDA_TRY(cudaMemsetAsync(L.kc, 0, (size_t)cells * e->Dkv * 2, st));
+        ALB_CUDA_TRY(cudaMemsetAsync(L.vc, 0, (size_t)cells * e->Dkv * 2, st));
+        (void)Dkv_full;
+    }
+    std::vector<float> rt;
+    rope_table_host(rt, e->max_ctx, (int)HD, c.freq_base);
+    ALB_TRY(e->alloc(&e->rope, rt.size()));
+    ALB_CUDA_TRY(cudaMemcpyAsync(e->rope, rt.data(), rt.size() * 4, cudaMemcpyHostToDevice, st));
+    ALB_CUDA_TRY(cudaStreamSynchronize(st));
+    return ALB_OK;
+}
+
+static int engine_init_acts(alb_engine * e) {
+    const int64_t U = e->max_ub;
+    ALB_TRY(e->alloc(&e->x, U * e->E));
+    ALB_TRY(e->alloc(&e->qkv, U * e->Nqkv));
+    ALB_TRY(e->alloc(&e->q, U * e->Dq));
+    ALB_TRY(e->alloc(&e->att, U * e->Dq));
+    ALB_TRY(e->alloc(&e->h, U * e->F));
+    ALB_TRY(e->alloc(&e->logits, (size_t)e->V));
+    ALB_TRY(e->alloc(&e->tok_dev, (size_t)U));
+    ALB_TRY(e->alloc(&e->pos_dev, 1));
+    ALB_TRY(e->alloc(&e->next_dev, 1));
+    ALB_TRY(e->alloc(&e->step_dev, 1));
+    e->gen_cap = 1 << 16;
+    ALB_TRY(e->alloc(&e->gen_out, (size_t)e->gen_cap));
+    ALB_TRY(e->alloc(&e->key, 1));
+    uint8_t * scr = nullptr;
+    ALB_TRY(e->alloc(&scr, 1024));
+    e->am_scratch = scr;
+    // decode split-K: ~4 CTAs per SM over the local KV heads
+    int S = (4 * alb_sm_count() + e->Hkv - 1) / e->Hkv;
+    if (S > 1024) S = 1024;
+    e->fa_S_decode = S;
+    e->fa_ws_bytes = flash_attn_ws_bytes(e->Hq, e->Hkv, 1, S, e->max_ctx);
+    const size_t pre = flash_attn_ws_bytes(e->Hq, e->Hkv, e->max_ub, 1, e->max_ctx);   // prefill beyond fused smem
+    if (pre > e->fa_ws_bytes) e->fa_ws_bytes = pre;
+    uint8_t * ws = nullptr;
+    ALB_TRY(e->alloc(&ws, e->fa_ws_bytes));
+    e->fa_ws = reinterpret_cast<float *>(ws);
+    ALB_CUDA_TRY(cudaMemsetAsync(ws, 0, e->fa_ws_bytes, e->st));
+    ALB_CUDA_TRY(cudaMemsetAsync(scr, 0, 1024, e->st));
+    ALB_CUDA_TRY(cudaMemsetAsync(e->step_dev, 0, 4, e->st));
+    ALB_CUDA_TRY(cudaMallocHost(&e->pinned, 64));
+    ALB_CUDA_TRY(cudaStreamSynchronize(e->st));
+    return ALB_OK;
+}
+
+static void engine_free(alb_engine * e) {
+    if (!e) return;
+    cudaSetDevice(e->dev);
+    if (e->st) cudaStreamSynchronize(e->st);
+    if (e->gexec) cudaGraphExecDestroy(e->gexec);
+    if (e->graph) cudaGraphDestroy(e->graph);
+    for (void * p : e->allocs) cudaFree(p);
+    if (e->pinned) cudaFreeHost(e->pinned);
+    if (e->comm) nccl_destroy(e->comm, false);
+    if (e->st) cudaStreamDestroy(e->st);
+    delete e;
+}
+
+extern "C" int alb_nccl_unique_id(void * out128) {
+    ALB_CHECK_ARG(out128);
+    return nccl_unique_id(out128);
+}
+
+extern "C" int alb_engine_create(const alb_qwen3_config * cfg, uint64_t seed, int32_t max_ctx, int32_t max_ubatch,
+                                 int32_t tp_rank, int32_t tp_size, const void * nccl_id, int32_t device,
+                                 alb_engine ** out) {
+    ALB_CHECK_ARG(cfg && out && max_ctx > 0 && max_ubatch > 0 && tp_size >= 1 && tp_rank >= 0 && tp_rank < tp_size);
+    ALB_CHECK_ARG(cfg->head_dim == 128 && cfg->n_layer > 0 && cfg->n_embd % 32 == 0 && cfg->n_embd <= 12288);
+    ALB_CHECK_ARG(cfg->n_head % tp_size == 0 && cfg->n_head_kv % tp_size == 0 && cfg->n_head % cfg->n_head_kv == 0);
+    ALB_CHECK_ARG(cfg->n_ff % (32 * tp_size) == 0 && cfg->n_vocab % tp_size == 0);
+    ALB_CHECK_ARG(tp_size == 1 || nccl_id);
+    *out = nullptr;
+    const int rc0 = alb_device_check(device);
+    if (rc0 != ALB_OK) return rc0;
+    ALB_CUDA_TRY(cudaSetDevice(device));
+    alb_engine * e = new alb_engine();
+    e->c = *cfg; e->seed = seed; e->max_ctx = max_ctx; e->max_ub = max_ubatch;
+    e->rank = tp_rank; e->tp = tp_size; e->dev = device;
+    e->E = cfg->n_embd;
+    e->Hq = cfg->n_head / tp_size; e->Hkv = cfg->n_head_kv / tp_size;
+    e->F = cfg->n_ff / tp_size; e->V = cfg->n_vocab / tp_size; e->v0 = e->V * tp_rank;
+    e->Dq = e->Hq * cfg->head_dim; e->Dkv = e->Hkv * cfg->head_dim;
+    e->Nqkv = e->Dq + 2 * e->Dkv;
+    int rc = ALB_OK;
+    if (cudaStreamCreateWithFlags(&e->st, cudaStreamNonBlocking) != cudaSuccess) rc = ALB_ERR_CUDA;
+    if (rc == ALB_OK && tp_size > 1) rc = nccl_init(&e->comm, tp_rank, tp_size, nccl_id);
+    if (rc == ALB_OK) rc = engine_init_weights(e);
+    if (rc == ALB_OK) rc = engine_init_acts(e);
+    if (rc != ALB_OK) { engine_free(e); return rc; }
+    *out = e;
+    return ALB_OK;
+}
+
+extern "C" int alb_engine_destroy(alb_engine * e) {
+    engine_free(e);
+    return ALB_OK;
+}
+
+extern "C" size_t alb_engine_device_bytes(const alb_engine * e) { return e ? e->bytes : 0; }
+
+extern "C" int alb_engine_reset(alb_engine * e) {
+    ALB_CHECK_ARG(e);
+    ALB_CUDA_TRY(cudaSetDevice(e->dev));
+    for (auto & L : e->layers) {
+        ALB_CUDA_TRY(cudaMemsetAsync(L.kc, 0, (size_t)e->max_ctx * e->Dkv * 2, e->st));
+        ALB_CUDA_TRY(cudaMemsetAsync(L.vc, 0, (size_t)e->max_ctx * e->Dkv * 2, e->st));
+    }
+    ALB_CUDA_TRY(cudaStreamSynchronize(e->st));
+    return ALB_OK;
+}
+
+// decoding_context::decode / process_ubatch (context.cpp:74-205) for a prompt
+// chunk: tokens at positions [pos0, pos0 + n), split into ubatches of max_ubatch.
+extern "C" int alb_engine_prefill(alb_engine * e, const int32_t * tokens, int32_t n, int32_t pos0,
+                                  int32_t * next_token) {
+    ALB_CHECK_ARG(e && tokens && n > 0 && pos0 >= 0 && (int64_t)pos0 + n <= e->max_ctx);
+    for (int32_t i = 0; i < n; ++i) ALB_CHECK_ARG(tokens[i] >= 0 && tokens[i] < e->c.n_vocab);
+    ALB_CUDA_TRY(cudaSetDevice(e->dev));
+    for (int32_t off = 0; off < n; off += e->max_ub) {
+        const int32_t T = (n - off) < e->max_ub ? (n - off) : e->max_ub;
+        const int32_t p = pos0 + off;
+        ALB_CUDA_TRY(cudaMemcpyAsync(e->tok_dev, tokens + off, (size_t)T * 4, cudaMemcpyHostToDevice, e->st));
+        ALB_CUDA_TRY(cudaMemcpyAsync(e->pos_dev, &p, 4, cudaMemcpyHostToDevice, e->st));
+        ALB_CUDA_TRY(cudaStreamSynchronize(e->st));   // pageable sources: keep them alive
+        ALB_TRY(engine_forward(e, T, false, p + T));
+    }
+    ALB_CUDA_TRY(cudaMemcpyAsync(e->pinned, e->next_dev, 4, cudaMemcpyDeviceToHost, e->st));
+    ALB_CUDA_TRY(cudaStreamSynchronize(e->st));
+    ALB_TRY(nccl_async_error(e->comm));
+    if (next_token) *next_token = e->pinned[0];
+    return ALB_OK;
+}
+
+// One greedy decode step (context.cpp:51-67): token at position pos.  Host
+// buffers in and out: 8 bytes H2D (token, pos), 4 bytes D2H (next token).
+extern "C" int alb_engine_decode(alb_engine * e, int32_t token, int32_t pos, int32_t * next_token) {
+    ALB_CHECK_ARG(e && token >= 0 && token < e->c.n_vocab && pos >= 0 && pos < e->max_ctx);
+    ALB_CUDA_TRY(cudaSetDevice(e->dev));
+    ALB_TRY(engine_build_graph(e));
+    e->pinned[0] = token;
+    e->pinned[1] = pos;
+    ALB_CUDA_TRY(cudaMemcpyAsync(e->tok_dev, &e->pinned[0], 4, cudaMemcpyHostToDevice, e->st));
+    ALB_CUDA_TRY(cudaMemcpyAsync(e->pos_dev, &e->pinned[1], 4, cudaMemcpyHostToDevice, e->st));
+    ALB_CUDA_TRY(cudaGraphLaunch(e->gexec, e->st));
+    ALB_CUDA_TRY(cudaMemcpyAsync(&e->pinned[2], e->next_dev, 4, cudaMemcpyDeviceToHost, e->st));
+    ALB_CUDA_TRY(cudaStreamSynchronize(e->st));
+    ALB_TRY(nccl_async_error(e->comm));
+    if (next_token) *next_token = e->pinned[2];
+    return ALB_OK;
+}
+
+// Device-resident greedy loop: n_steps graph replays starting from (token, pos);
+// every step's next token is appended on the device.  If tokens_out is non-null
+// the generated tokens are copied back at the end.  Stream ordered, no host
+// round trip between steps.
+extern "C" int alb_engine_decode_loop(alb_engine * e, int32_t token, int32_t pos, int32_t n_steps,
+                                      int32_t * tokens_out, int32_t sync) {
+    ALB_CHECK_ARG(e && token >= 0 && token < e->c.n_vocab && pos >= 0 && n_steps > 0 && n_steps <= e->gen_cap);
+    ALB_CHECK_ARG((int64_t)pos + n_steps <= e->max_ctx);
+    ALB_CUDA_TRY(cudaSetDevice(e->dev));
+    ALB_TRY(engine_build_graph(e));
+    e->pinned[0] = token;
+    e->pinned[1] = pos;
+    e->pinned[2] = 0;
+    ALB_CUDA_TRY(cudaMemcpyAsync(e->tok_dev, &e->pinned[0], 4, cudaMemcpyHostToDevice, e->st));
+    ALB_CUDA_TRY(cudaMemcpyAsync(e->pos_dev, &e->pinned[1], 4, cudaMemcpyHostToDevice, e->st));
+    ALB_CUDA_TRY(cudaMemcpyAsync(e->step_dev, &e->pinned[2], 4, cudaMemcpyHostToDevice, e->st));
+    for (int32_t i = 0; i < n_steps; ++i) ALB_CUDA_TRY(cudaGraphLaunch(e->gexec, e->st));
+    if (tokens_out) {
+        ALB_CUDA_TRY(cudaMemcpyAsync(tokens_out, e->gen_out, (size_t)n_steps * 4, cudaMemcpyDeviceToHost, e->st));
+    }
+    if (sync || tokens_out) {
+        ALB_CUDA_TRY(cudaStreamSynchronize(e->st));
+        ALB_TRY(nccl_async_error(e->comm));
+    }
+    return ALB_OK;
+}
+
+extern "C" int alb_engine_logits(alb_engine * e, float * host, int64_t n) {
+    ALB_CHECK_ARG(e && host && n == e->V);
+    ALB_CUDA_TRY(cudaSetDevice(e->dev));
+    ALB_CUDA_TRY(cudaMemcpyAsync(host, e->logits, (size_t)n * 4, cudaMemcpyDeviceToHost, e->st));
+    ALB_CUDA_TRY(cudaStreamSynchronize(e->st));
+    return ALB_OK;
+}
+
+extern "C" int alb_engine_info(const alb_engine * e, int64_t * info, int32_t n) {
+    ALB_CHECK_ARG(e && info && n >= 8);
+    info[0] = e->V; info[1] = e->v0; info[2] = e->Hq; info[3] = e->Hkv; info[4] = e->F;
+    info[5] = e->launches_per_step; info[6] = (int64_t)e->bytes; info[7] = e->fa_S_decode;
+    return ALB_OK;
+}
+
+extern "C" void * alb_engine_stream(alb_engine * e) { return e ? (void *)e->st : nullptr; }
+
+// Weight shard of (layer, kind) back in the reference's block_q4_0 layout
+// [rows][K/32] (host buffer of rows*(K/32)*18 bytes) for parity checks of the
+// generator; rows/cols describe this rank's shard.
+extern "C" int alb_engine_weight_blocks(alb_engine * e, int32_t layer, int32_t kind, void * host, int64_t * rows,
+                                        int64_t * cols) {
+    ALB_CHECK_ARG(e && rows && cols && layer >= -1 && layer < e->c.n_layer);
+    ALB_CUDA_TRY(cudaSetDevice(e->dev));
+    const uint8_t * W = nullptr;
+    int64_t N = 0, K = 0, r0 = 0, nr = 0, stride = 1;
+    if (layer < 0) {
+        if (kind == T_TOK_EMBD) { W = e->tok; N = e->c.n_vocab; K = e->E; nr = N; }
+        else return ALB_ERR_INVALID;
+    } else {
+        alb_engine::Layer & L = e->layers[layer];
+        switch (kind) {
+            case T_WQ: W = L.qkv; N = e->Nqkv; K = e->E; r0 = 0; nr = e->Dq; break;
+            case T_WK: W = L.qkv; N = e->Nqkv; K = e->E; r0 = e->Dq; nr = e->Dkv; break;
+            case T_WV: W = L.qkv; N = e->Nqkv; K = e->E; r0 = e->Dq + e->Dkv; nr = e->Dkv; break;
+            case T_WO: W = L.o; N = e->E; K = e->Dq; nr = N; break;
+            case T_GATE: W = L.gu; N = 2 * (int64_t)e->F; K = e->E; r0 = 0; nr = e->F; stride = 2; break;
+            case T_UP: W = L.gu; N = 2 * (int64_t)e->F; K = e->E; r0 = 1; nr = e->F; stride = 2; break;
+            case T_DOWN: W = L.down; N = e->E; K = e->F; nr = N; break;
+            default: return ALB_ERR_INVALID;
+        }
+    }
+    *rows = nr; *cols = K;
+    if (!host) return ALB_OK;
+    uint8_t * tmp = nullptr;
+    ALB_CUDA_TRY(cudaMalloc(&tmp, (size_t)N * (K / 32) * 18));
+    int rc = alb_unpack_q4_0(tmp, W, N, K, e->st);
+    if (rc == ALB_OK) {
+        std::vector<uint8_t> all((size_t)N * (K / 32) * 18);
+        if (cudaMemcpyAsync(all.data(), tmp, all.size(), cudaMemcpyDeviceToHost, e->st) != cudaSuccess ||
+            cudaStreamSynchronize(e->st) != cudaSuccess) rc = ALB_ERR_CUDA;
+        const size_t rb = (size_t)(K / 32) * 18;
+        for (int64_t i = 0; rc == ALB_OK && i < nr; ++i)
+            memcpy(static_cast<uint8_t *>(host) + i * rb, all.data() + (size_t)(r0 + i * stride) * rb, rb);
+    }
+    cudaFree(tmp);
+    return rc;
+}
+
+extern "C" int alb_engine_norm_weights(alb_engine * e, int32_t layer, int32_t kind, float * host, int64_t n) {
+    ALB_CHECK_ARG(e && host && layer >= -1 && layer < e->c.n_layer);
+    const float * src = nullptr;
+    int64_t len = 0;
+    if (layer < 0 && kind == T_OUTPUT_NORM) { src = e->out_norm; len = e->E; }
+    else if (layer >= 0) {
+        alb_engine::Layer & L = e->layers[layer];
+        if (kind == T_ATTN_NORM) { src = L.an; len = e->E; }
+        if (kind == T_FFN_NORM) { src = L.fn; len = e->E; }
+        if (kind == T_Q_NORM) { src = L.qn; len = 128; }
+        if (kind == T_K_NORM) { src = L.kn; len = 128; }
+    }
+    ALB_CHECK_ARG(src && n == len);
+    ALB_CUDA_TRY(cudaMemcpy(host, src, (size_t)n * 4, cudaMemcpyDeviceToHost));
+    return ALB_OK;
+}
+
+// Config 5: fill the KV cache of every layer for positions [0, n_pos) with
+// N(0,1) fp16 values (seeded per layer and K/V, indexed on the full KV row).
+extern "C" int alb_engine_fill_kv(alb_engine * e, int32_t n_pos, uint64_t seed) {
+    ALB_CHECK_ARG(e && n_pos > 0 && n_pos <= e->max_ctx);
+    ALB_CUDA_TRY(cudaSetDevice(e->dev));
+    const int64_t full = (int64_t)e->c.n_head_kv * e->c.head_dim;
+    for (int l = 0; l < e->c.n_layer; ++l) {
+        ALB_CUDA_TRY(gen_f16(e->layers[l].kc, n_pos, e->Dkv, full, (int64_t)e->rank * e->Dkv, tensor_seed(seed, l, 62),
+                             e->table, e->st));
+        ALB_CUDA_TRY(gen_f16(e->layers[l].vc, n_pos, e->Dkv, full, (int64_t)e->rank * e->Dkv, tensor_seed(seed, l, 63),
+                             e->table, e->st));
+    }
+    ALB_CUDA_TRY(cudaStreamSynchronize(e->st));
+    return ALB_OK;
+}

@@ -39,6 +39,8 @@ struct GemvArgs {
     int variant = 0;               // 0/1 = direct loads + L2 prefetch (default), 2 = bulk-copy pipeline
     int stage_budget = 0;          // bytes of shared-memory stages (0 = default)
     int * err = nullptr;           // device error word (filled by launch_gemv)
+    int64_t x_stride = 0;          // token-batched form: floats between token rows of x
+    int64_t y_stride = 0;          //                     floats between token rows of y / residual
 };
 
 struct FlashArgs {
@@ -50,11 +52,12 @@ struct FlashArgs {
     const int32_t * pos_dev = nullptr;  // device-resident pos0 (CUDA-graph replay)
     float scale = 0.0f;
     int S = 1;                          // splits along the cells
+    int ncap = 0;                       // upper bound of cells attended (>= pos0 + T)
     float * ws = nullptr;               // flash_attn_ws_bytes(); tickets must start at 0
     float * out = nullptr;              // [T][Hq][128] fp32
     bool pdl = false;
 };
-size_t flash_attn_ws_bytes(int Hq, int Hkv, int T, int S);
+size_t flash_attn_ws_bytes(int Hq, int Hkv, int T, int S, int ncap);
 cudaError_t launch_flash_attn(const FlashArgs & f, cudaStream_t st);
 
 struct QkvArgs {
@@ -87,6 +90,8 @@ enum : int { ALB_DEVERR_NONE = 0, ALB_DEVERR_MBAR_TIMEOUT = 1, ALB_DEVERR_FLAG_T
 int * device_error_ptr();
 
 cudaError_t launch_gemv(const GemvArgs & a, cudaStream_t stream);
+// prefill ubatch of T tokens (fp32 inputs only), launched in chunks of 8 tokens
+cudaError_t launch_gemv_tokens(const GemvArgs & a, int64_t T, cudaStream_t stream);
 
 // alb Q4_0 GPU layout: nibble plane [N][K/2] bytes, then (256-aligned) the fp16
 // scale plane [N][q4_scale_pitch(K)] (row pitch padded to 16 bytes so that every

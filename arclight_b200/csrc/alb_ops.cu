@@ -88,132 +88,178 @@ k_qk_norm_rope_kv(const float * __restrict__ qkv, int64_t qkv_stride, int Hq, in
 }
 
 // ------------------------------------------------------------ flash attention
-// nnml_compute_forward_flash_attn_ext_f16 (arm.cpp:2196-2433) for F16 K/V,
-// one sequence, causal: token t (position p0 + t) attends cells [0, p0+t+1).
-// Q is rounded to fp16 first as the reference does (arm.cpp:2307); scores,
-// softmax and the V accumulation are fp32 (the reference accumulates V in
-// fp16; fp32 is the more accurate choice and stays well inside 1e-3).
-// Split-K over the cells: CTA (kv head h, token t, split s) runs an online
-// softmax over its cell range for the G = Hq/Hkv query heads of h and writes
-// (m, l, acc) to the workspace; the last CTA of (h, t) (atomic ticket, no
-// spin) merges the splits with the usual log-sum-exp rescale.
+// nnml_compute_forward_flash_attn_ext_f16 (arm.cpp:2196-2433) for F16 K/V, one
+// sequence, causal: token t (position p0 + t) attends cells [0, p0+t+1).
+// Semantics (identical to the oracle's fp32 mode, independent of how the cells
+// are split across CTAs): Q rounded to fp16 as the reference does
+// (arm.cpp:2307); score s_c = sequential fp32 fma chain over d of K.Q, times
+// scale; M = max_c s_c; p_c = v_expf(s_c - M) (the reference's NEON exp,
+// arm.cpp:1757-1787); L = sum p_c and O_d = sum p_c V_cd in double; out = O/L.
+// Softmax is shift invariant, so this is the reference's online softmax with
+// different (and fewer) roundings.
+//
+// Decode / small ubatches split the cells over S CTAs in two kernels:
+// k_fa_scores writes the scores and per-split maxima, k_fa_pv applies the
+// global max, accumulates its split in double and the last CTA of (h, t)
+// (atomic ticket, no spin) adds the S partials in split order.  Large prefill
+// ubatches use k_fa_fused (one CTA per (h, t), scores in shared memory).
+static constexpr int FA_TICKETS = 8192;
+
+__device__ __forceinline__ float fa_score(const uint16_t * __restrict__ krow, const float * __restrict__ qg) {
+    const uint4 * kr = reinterpret_cast<const uint4 *>(krow);
+    float a = 0.0f;
+#pragma unroll 4
+    for (int j = 0; j < 16; ++j) {
+        const uint4 kv = kr[j];
+        const uint32_t wd[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float2 kf = __half22float2(*reinterpret_cast<const __half2 *>(&wd[e]));
+            const int d = 8 * j + 2 * e;
+            a = __fmaf_rn(kf.x, qg[d], a);
+            a = __fmaf_rn(kf.y, qg[d + 1], a);
+        }
+    }
+    return a;
+}
+
+template <int G>
+__device__ __forceinline__ void fa_load_q(const float * __restrict__ q, int Hq, int h, int t, float (*qs)[128]) {
+    for (int i = threadIdx.x; i < G * 128; i += blockDim.x) {
+        const int g = i / 128, d = i - g * 128;
+        qs[g][d] = __half2float(__float2half_rn(q[((size_t)t * Hq + h * G + g) * 128 + d]));
+    }
+}
+
+__device__ __forceinline__ void fa_split(int n, int S, int s, int & c0, int & c1) {
+    int sz = (n + S - 1) / S;
+    c0 = s * sz;
+    c1 = min(n, c0 + sz);
+    if (c0 > n) c0 = n;
+}
+
 template <int G>
 __global__ void __launch_bounds__(128)
-k_flash_attn(const float * __restrict__ q, const uint16_t * __restrict__ kc, const uint16_t * __restrict__ vc,
-             int Hq, int Hkv, int T, int32_t pos0, const int32_t * __restrict__ pos_dev, float scale,
-             int S, float * __restrict__ ws, int * __restrict__ tickets, float * __restrict__ out) {
+k_fa_scores(const float * __restrict__ q, const uint16_t * __restrict__ kc, int Hq, int Hkv, int T, int32_t pos0,
+            const int32_t * __restrict__ pos_dev, float scale, int S, int ncap, float * __restrict__ scores,
+            float * __restrict__ smax) {
     const int h = blockIdx.x, t = blockIdx.y, s = blockIdx.z;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    constexpr int D = 128;
-    __shared__ float qs[G][D];
-    __shared__ float wm[4][G], wl[4][G];
-    __shared__ float wacc[4][G][D];
-    __shared__ int last;
+    __shared__ float qs[G][128];
+    __shared__ float red[4][G];
     alb_pdl_wait();
-    const int32_t p0 = pos_dev ? pos_dev[0] : pos0;
-    const int n = p0 + t + 1;
-    const int64_t row = (int64_t)Hkv * D;
-    for (int i = tid; i < G * D; i += 128) {
-        const int g = i / D, d = i - g * D;
-        qs[g][d] = __half2float(__float2half_rn(q[((size_t)t * Hq + h * G + g) * D + d]));
-    }
+    const int n = (pos_dev ? pos_dev[0] : pos0) + t + 1;
+    fa_load_q<G>(q, Hq, h, t, qs);
     __syncthreads();
-    int sz = (n + S - 1) / S;
-    sz = (sz + 31) & ~31;
-    const int c0 = s * sz, c1 = min(n, c0 + sz);
-
-    float m[G], l[G], acc[G][4];
+    int c0, c1;
+    fa_split(n, S, s, c0, c1);
+    const int64_t row = (int64_t)Hkv * 128;
+    float mx[G];
 #pragma unroll
-    for (int g = 0; g < G; ++g) { m[g] = -INFINITY; l[g] = 0.0f; acc[g][0] = acc[g][1] = acc[g][2] = acc[g][3] = 0.0f; }
-
-    for (int base = c0 + warp * 32; base < c1; base += 128) {
-        const int c = base + lane;
-        float sc[G];
-#pragma unroll
-        for (int g = 0; g < G; ++g) sc[g] = -INFINITY;
-        if (c < c1) {
-            const uint4 * kr = reinterpret_cast<const uint4 *>(kc + (size_t)c * row + (size_t)h * D);
-            float a[G];
-#pragma unroll
-            for (int g = 0; g < G; ++g) a[g] = 0.0f;
-#pragma unroll 4
-            for (int j = 0; j < 16; ++j) {
-                const uint4 kv = kr[j];
-                const uint32_t wd[4] = {kv.x, kv.y, kv.z, kv.w};
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float2 kf = __half22float2(*reinterpret_cast<const __half2 *>(&wd[e]));
-                    const int d = 8 * j + 2 * e;
-#pragma unroll
-                    for (int g = 0; g < G; ++g) a[g] = fmaf(kf.y, qs[g][d + 1], fmaf(kf.x, qs[g][d], a[g]));
-                }
-            }
-#pragma unroll
-            for (int g = 0; g < G; ++g) sc[g] = a[g] * scale;
-        }
-        float p[G];
+    for (int g = 0; g < G; ++g) mx[g] = -INFINITY;
+    float * sc = scores + ((size_t)h * T + t) * G * ncap;
+    for (int c = c0 + (int)threadIdx.x; c < c1; c += 128) {
+        const uint16_t * krow = kc + (size_t)c * row + (size_t)h * 128;
 #pragma unroll
         for (int g = 0; g < G; ++g) {
-            const float cm = alb_warp_max(sc[g]);
-            const float mn = fmaxf(m[g], cm);
-            const float r = (m[g] == -INFINITY) ? 0.0f : expf(m[g] - mn);
-            p[g] = (c < c1) ? expf(sc[g] - mn) : 0.0f;
-            l[g] = l[g] * r + alb_warp_sum(p[g]);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) acc[g][e] *= r;
-            m[g] = mn;
+            const float v = __fmul_rn(fa_score(krow, qs[g]), scale);
+            sc[(size_t)g * ncap + c] = v;
+            mx[g] = fmaxf(mx[g], v);
         }
-        const int nc = min(32, c1 - base);
-        for (int j = 0; j < nc; ++j) {
-            const uint2 vv = *reinterpret_cast<const uint2 *>(vc + (size_t)(base + j) * row + (size_t)h * D + 4 * lane);
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const float m = alb_warp_max(mx[g]);
+        if (lane == 0) red[warp][g] = m;
+    }
+    __syncthreads();
+    if (threadIdx.x < G) {
+        const int g = threadIdx.x;
+        smax[(((size_t)h * T + t) * S + s) * G + g] = fmaxf(fmaxf(red[0][g], red[1][g]), fmaxf(red[2][g], red[3][g]));
+    }
+    alb_pdl_trigger();
+}
+
+template <int G>
+__global__ void __launch_bounds__(128)
+k_fa_pv(const uint16_t * __restrict__ vc, int Hq, int Hkv, int T, int32_t pos0, const int32_t * __restrict__ pos_dev,
+        int S, int ncap, const float * __restrict__ scores, const float * __restrict__ smax, double * __restrict__ part,
+        int * __restrict__ tickets, float * __restrict__ out) {
+    const int h = blockIdx.x, t = blockIdx.y, s = blockIdx.z;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int FA_CHUNK = (2048 / G) < 512 ? (2048 / G) : 512;   // cells per shared-memory chunk
+    __shared__ float M[G];
+    __shared__ float ps[G][FA_CHUNK];
+    __shared__ double Lred[4][G];
+    __shared__ double ored[4][G][128];
+    __shared__ int last;
+    alb_pdl_wait();
+    const int n = (pos_dev ? pos_dev[0] : pos0) + t + 1;
+    if (tid < G) {
+        float m = -INFINITY;
+        for (int k = 0; k < S; ++k) m = fmaxf(m, smax[(((size_t)h * T + t) * S + k) * G + tid]);
+        M[tid] = m;
+    }
+    __syncthreads();
+    int c0, c1;
+    fa_split(n, S, s, c0, c1);
+    const int64_t row = (int64_t)Hkv * 128;
+    const float * sc = scores + ((size_t)h * T + t) * G * ncap;
+    double L[G], O[G][4];
+#pragma unroll
+    for (int g = 0; g < G; ++g) { L[g] = 0.0; O[g][0] = O[g][1] = O[g][2] = O[g][3] = 0.0; }
+    for (int cb = c0; cb < c1; cb += FA_CHUNK) {
+        const int ce = min(c1, cb + FA_CHUNK);
+        __syncthreads();
+        for (int c = cb + tid; c < ce; c += 128)
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                const float p = alb_ref_expf(__fsub_rn(sc[(size_t)g * ncap + c], M[g]));
+                ps[g][c - cb] = p;
+                L[g] += (double)p;
+            }
+        __syncthreads();
+        for (int c = cb + warp; c < ce; c += 4) {
+            const uint2 vv = *reinterpret_cast<const uint2 *>(vc + (size_t)c * row + (size_t)h * 128 + 4 * lane);
             const float2 v01 = __half22float2(*reinterpret_cast<const __half2 *>(&vv.x));
             const float2 v23 = __half22float2(*reinterpret_cast<const __half2 *>(&vv.y));
 #pragma unroll
             for (int g = 0; g < G; ++g) {
-                const float pj = __shfl_sync(0xffffffffu, p[g], j);
-                acc[g][0] = fmaf(v01.x, pj, acc[g][0]);
-                acc[g][1] = fmaf(v01.y, pj, acc[g][1]);
-                acc[g][2] = fmaf(v23.x, pj, acc[g][2]);
-                acc[g][3] = fmaf(v23.y, pj, acc[g][3]);
+                const double p = (double)ps[g][c - cb];
+                O[g][0] = fma(p, (double)v01.x, O[g][0]);
+                O[g][1] = fma(p, (double)v01.y, O[g][1]);
+                O[g][2] = fma(p, (double)v23.x, O[g][2]);
+                O[g][3] = fma(p, (double)v23.y, O[g][3]);
             }
         }
     }
-    // merge the 4 warps of this CTA
-    if (lane == 0)
-#pragma unroll
-        for (int g = 0; g < G; ++g) { wm[warp][g] = m[g]; wl[warp][g] = l[g]; }
-#pragma unroll
-    for (int g = 0; g < G; ++g)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) wacc[warp][g][4 * lane + e] = acc[g][e];
-    __syncthreads();
-    // thread tid owns dimension tid for every head
-    float M[G], Lsum[G], O[G];
+    // CTA reduction: L over threads, O over the 4 warps (thread tid owns dim tid afterwards)
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-        float mx = -INFINITY;
-        for (int w = 0; w < 4; ++w) mx = fmaxf(mx, wm[w][g]);
-        float L = 0.0f, o = 0.0f;
-        for (int w = 0; w < 4; ++w) {
-            const float f = (wm[w][g] == -INFINITY) ? 0.0f : expf(wm[w][g] - mx);
-            L += wl[w][g] * f;
-            o += wacc[w][g][tid] * f;
-        }
-        M[g] = mx; Lsum[g] = L; O[g] = o;
+        const double l = alb_warp_sum_d(L[g]);
+        if (lane == 0) Lred[warp][g] = l;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) ored[warp][g][4 * lane + e] = O[g][e];
+    }
+    __syncthreads();
+    double Ls[G], Os[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        Ls[g] = ((Lred[0][g] + Lred[1][g]) + Lred[2][g]) + Lred[3][g];
+        Os[g] = ((ored[0][g][tid] + ored[1][g][tid]) + ored[2][g][tid]) + ored[3][g][tid];
     }
     if (S == 1) {
 #pragma unroll
         for (int g = 0; g < G; ++g)
-            out[((size_t)t * Hq + h * G + g) * D + tid] = Lsum[g] > 0.0f ? O[g] / Lsum[g] : 0.0f;
+            out[((size_t)t * Hq + h * G + g) * 128 + tid] = Ls[g] > 0.0 ? __double2float_rn(Os[g] / Ls[g]) : 0.0f;
         alb_pdl_trigger();
         return;
     }
-    // write the split partial: [h][t][s][G][D + 2]
-    float * part = ws + (((size_t)h * T + t) * S + s) * G * (D + 2);
+    double * pp = part + (((size_t)h * T + t) * S + s) * G * 129;
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-        part[g * (D + 2) + tid] = O[g];
-        if (tid == 0) { part[g * (D + 2) + D] = M[g]; part[g * (D + 2) + D + 1] = Lsum[g]; }
+        pp[g * 129 + tid] = Os[g];
+        if (tid == 0) pp[g * 129 + 128] = Ls[g];
     }
     __threadfence();
     __syncthreads();
@@ -221,41 +267,159 @@ k_flash_attn(const float * __restrict__ q, const uint16_t * __restrict__ kc, con
     __syncthreads();
     if (!last) { alb_pdl_trigger(); return; }
     __threadfence();
-    const float * base = ws + ((size_t)h * T + t) * S * G * (D + 2);
+    const double * base = part + ((size_t)h * T + t) * S * G * 129;
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-        float mx = -INFINITY;
-        for (int k = 0; k < S; ++k) mx = fmaxf(mx, __ldcg(base + ((size_t)k * G + g) * (D + 2) + D));
-        float L = 0.0f, o = 0.0f;
+        double Lt = 0.0, Ot = 0.0;
         for (int k = 0; k < S; ++k) {
-            const float * pk = base + ((size_t)k * G + g) * (D + 2);
-            const float mk = __ldcg(pk + D);
-            const float f = (mk == -INFINITY) ? 0.0f : expf(mk - mx);
-            L += __ldcg(pk + D + 1) * f;
-            o += __ldcg(pk + tid) * f;
+            const double * pk = base + ((size_t)k * G + g) * 129;
+            Lt += __ldcg(pk + 128);
+            Ot += __ldcg(pk + tid);
         }
-        out[((size_t)t * Hq + h * G + g) * D + tid] = L > 0.0f ? o / L : 0.0f;
+        out[((size_t)t * Hq + h * G + g) * 128 + tid] = Lt > 0.0 ? __double2float_rn(Ot / Lt) : 0.0f;
     }
     if (tid == 0) tickets[h * T + t] = 0;   // re-arm for the next launch / graph replay
     alb_pdl_trigger();
 }
 
-size_t flash_attn_ws_bytes(int Hq, int Hkv, int T, int S) {
+// One CTA per (h, t): scores of all cells in shared memory, then the same
+// global-max softmax and double sums.
+template <int G>
+__global__ void __launch_bounds__(128)
+k_fa_fused(const float * __restrict__ q, const uint16_t * __restrict__ kc, const uint16_t * __restrict__ vc, int Hq,
+           int Hkv, int T, int32_t pos0, const int32_t * __restrict__ pos_dev, float scale, float * __restrict__ out) {
+    extern __shared__ float fsm[];   // [G][n] scores -> probabilities
+    const int h = blockIdx.x, t = blockIdx.y;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    __shared__ float qs[G][128];
+    __shared__ float red[4][G];
+    __shared__ double Lred[4][G];
+    __shared__ double ored[4][G][128];
+    alb_pdl_wait();
+    const int n = (pos_dev ? pos_dev[0] : pos0) + t + 1;
+    fa_load_q<G>(q, Hq, h, t, qs);
+    __syncthreads();
+    const int64_t row = (int64_t)Hkv * 128;
+    float mx[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) mx[g] = -INFINITY;
+    for (int c = tid; c < n; c += 128) {
+        const uint16_t * krow = kc + (size_t)c * row + (size_t)h * 128;
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const float v = __fmul_rn(fa_score(krow, qs[g]), scale);
+            fsm[(size_t)g * n + c] = v;
+            mx[g] = fmaxf(mx[g], v);
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const float m = alb_warp_max(mx[g]);
+        if (lane == 0) red[warp][g] = m;
+    }
+    __syncthreads();
+    float M[G];
+    double L[G], O[G][4];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        M[g] = fmaxf(fmaxf(red[0][g], red[1][g]), fmaxf(red[2][g], red[3][g]));
+        L[g] = 0.0; O[g][0] = O[g][1] = O[g][2] = O[g][3] = 0.0;
+    }
+    for (int c = tid; c < n; c += 128)
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const float p = alb_ref_expf(__fsub_rn(fsm[(size_t)g * n + c], M[g]));
+            fsm[(size_t)g * n + c] = p;
+            L[g] += (double)p;
+        }
+    __syncthreads();
+    for (int c = warp; c < n; c += 4) {
+        const uint2 vv = *reinterpret_cast<const uint2 *>(vc + (size_t)c * row + (size_t)h * 128 + 4 * lane);
+        const float2 v01 = __half22float2(*reinterpret_cast<const __half2 *>(&vv.x));
+        const float2 v23 = __half22float2(*reinterpret_cast<const __half2 *>(&vv.y));
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const double p = (double)fsm[(size_t)g * n + c];
+            O[g][0] = fma(p, (double)v01.x, O[g][0]);
+            O[g][1] = fma(p, (double)v01.y, O[g][1]);
+            O[g][2] = fma(p, (double)v23.x, O[g][2]);
+            O[g][3] = fma(p, (double)v23.y, O[g][3]);
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const double l = alb_warp_sum_d(L[g]);
+        if (lane == 0) Lred[warp][g] = l;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) ored[warp][g][4 * lane + e] = O[g][e];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const double Ls = ((Lred[0][g] + Lred[1][g]) + Lred[2][g]) + Lred[3][g];
+        const double Os = ((ored[0][g][tid] + ored[1][g][tid]) + ored[2][g][tid]) + ored[3][g][tid];
+        out[((size_t)t * Hq + h * G + g) * 128 + tid] = Ls > 0.0 ? __double2float_rn(Os / Ls) : 0.0f;
+    }
+    alb_pdl_trigger();
+}
+
+// Workspace: [tickets FA_TICKETS ints | split maxima | scores | split partials (double)].
+// Tickets must be zero at first use; every launch re-arms them.
+struct FaLayout { size_t smax_off, scores_off, part_off, bytes; };
+static FaLayout fa_layout(int Hq, int Hkv, int T, int S, int ncap) {
     const int G = Hq / Hkv;
-    return (size_t)Hkv * T * S * G * (128 + 2) * 4 + (size_t)Hkv * T * 4 + 256;
+    FaLayout l;
+    l.smax_off = (size_t)FA_TICKETS * 4;
+    l.scores_off = (l.smax_off + (size_t)Hkv * T * S * G * 4 + 255) & ~(size_t)255;
+    l.part_off = (l.scores_off + (size_t)Hkv * T * G * ncap * 4 + 255) & ~(size_t)255;
+    l.bytes = l.part_off + (size_t)Hkv * T * S * G * 129 * 8;
+    return l;
+}
+
+size_t flash_attn_ws_bytes(int Hq, int Hkv, int T, int S, int ncap) {
+    return fa_layout(Hq, Hkv, T, S, ncap).bytes;
+}
+
+// shared memory available for the fused kernel's score array
+static constexpr size_t FA_FUSED_SMEM = 160 * 1024;
+
+template <int G>
+static cudaError_t launch_fa_t(const FlashArgs & f, cudaStream_t st) {
+    const int n_max = f.ncap;   // cells attended by the last token at most
+    if (f.S == 1 && (size_t)G * n_max * 4 <= FA_FUSED_SMEM) {
+        const size_t smem = (size_t)G * n_max * 4;
+        static size_t attr = 0;
+        if (smem > 48 * 1024 && smem > attr) {
+            cudaError_t e = cudaFuncSetAttribute(k_fa_fused<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return e;
+            attr = smem;
+        }
+        return alb_launch(k_fa_fused<G>, dim3((unsigned)f.Hkv, (unsigned)f.T), dim3(128), smem, st, f.pdl, f.q, f.kc,
+                          f.vc, f.Hq, f.Hkv, f.T, f.pos0, f.pos_dev, f.scale, f.out);
+    }
+    if (!f.ws) return cudaErrorInvalidValue;
+    if ((int64_t)f.Hkv * f.T > FA_TICKETS) return cudaErrorInvalidValue;
+    const FaLayout l = fa_layout(f.Hq, f.Hkv, f.T, f.S, f.ncap);
+    uint8_t * ws = reinterpret_cast<uint8_t *>(f.ws);
+    int * tickets = reinterpret_cast<int *>(ws);
+    float * smax = reinterpret_cast<float *>(ws + l.smax_off);
+    float * scores = reinterpret_cast<float *>(ws + l.scores_off);
+    double * part = reinterpret_cast<double *>(ws + l.part_off);
+    dim3 grid((unsigned)f.Hkv, (unsigned)f.T, (unsigned)f.S);
+    cudaError_t e = alb_launch(k_fa_scores<G>, grid, dim3(128), 0, st, f.pdl, f.q, f.kc, f.Hq, f.Hkv, f.T, f.pos0,
+                               f.pos_dev, f.scale, f.S, f.ncap, scores, smax);
+    if (e != cudaSuccess) return e;
+    return alb_launch(k_fa_pv<G>, grid, dim3(128), 0, st, f.pdl, f.vc, f.Hq, f.Hkv, f.T, f.pos0, f.pos_dev, f.S,
+                      f.ncap, (const float *)scores, (const float *)smax, part, tickets, f.out);
 }
 
 cudaError_t launch_flash_attn(const FlashArgs & f, cudaStream_t st) {
-    const int G = f.Hq / f.Hkv;
-    dim3 grid((unsigned)f.Hkv, (unsigned)f.T, (unsigned)f.S);
-    float * ws = f.ws;
-    int * tickets = reinterpret_cast<int *>(reinterpret_cast<uint8_t *>(f.ws) +
-                                            (size_t)f.Hkv * f.T * f.S * G * (128 + 2) * 4);
-    switch (G) {
-        case 1: return alb_launch(k_flash_attn<1>, grid, dim3(128), 0, st, f.pdl, f.q, f.kc, f.vc, f.Hq, f.Hkv, f.T, f.pos0, f.pos_dev, f.scale, f.S, ws, tickets, f.out);
-        case 2: return alb_launch(k_flash_attn<2>, grid, dim3(128), 0, st, f.pdl, f.q, f.kc, f.vc, f.Hq, f.Hkv, f.T, f.pos0, f.pos_dev, f.scale, f.S, ws, tickets, f.out);
-        case 4: return alb_launch(k_flash_attn<4>, grid, dim3(128), 0, st, f.pdl, f.q, f.kc, f.vc, f.Hq, f.Hkv, f.T, f.pos0, f.pos_dev, f.scale, f.S, ws, tickets, f.out);
-        case 8: return alb_launch(k_flash_attn<8>, grid, dim3(128), 0, st, f.pdl, f.q, f.kc, f.vc, f.Hq, f.Hkv, f.T, f.pos0, f.pos_dev, f.scale, f.S, ws, tickets, f.out);
+    if (f.ncap <= 0 || f.Hkv <= 0 || f.Hq % f.Hkv != 0) return cudaErrorInvalidValue;
+    switch (f.Hq / f.Hkv) {
+        case 1: return launch_fa_t<1>(f, st);
+        case 2: return launch_fa_t<2>(f, st);
+        case 4: return launch_fa_t<4>(f, st);
+        case 8: return launch_fa_t<8>(f, st);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -357,7 +521,7 @@ k_rms_norm(const float * __restrict__ x, const float * __restrict__ w, float * _
 __global__ void k_swiglu(const float * __restrict__ g, const float * __restrict__ u, float * __restrict__ y, int64_t n) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     alb_pdl_wait();
-    if (i < n) { const float gv = g[i]; y[i] = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), u[i]); }
+    if (i < n) y[i] = alb_swiglu1(g[i], u[i]);
     alb_pdl_trigger();
 }
 

@@ -17,13 +17,10 @@
 #include <cstdio>
 #include <cstdlib>
 
-#include "alb_common.cuh"
-#include "alb_internal.h"
+#include "alb_q4_dev.cuh"
 
 namespace alb {
 
-static constexpr int GEMV_WARPS = 8;            // 256 threads per CTA
-static constexpr int XREC_INTS = 12;            // 48-byte activation record per block
 
 
 // ---------------------------------------------------------------- repack
@@ -62,18 +59,6 @@ __global__ void k_unpack_q4_0(uint8_t * __restrict__ dst, const uint8_t * __rest
     for (int j = 0; j < 4; ++j) { d[1 + 2 * j] = (uint16_t)(w[j] & 0xFFFF); d[2 + 2 * j] = (uint16_t)(w[j] >> 16); }
 }
 
-// ------------------------------------------------------------ quantizer
-// One warp per 32-value block; lane j owns element j.  amax is an exact max
-// (order-free), d = amax/127 and id = 1/d are IEEE divisions, q = RNE(x*id)
-// (vcvtnq_s32_f32), d stored as fp16 (arm.cpp:1834-1851).
-__device__ __forceinline__ void q8_block_lane(float v, int8_t & q, uint16_t & dh) {
-    const float amax = alb_warp_max(fabsf(v));
-    const float d = amax / 127.0f;
-    const float id = d != 0.0f ? 1.0f / d : 0.0f;
-    q = (int8_t)__float2int_rn(__fmul_rn(v, id));
-    dh = alb_f2h(d);
-}
-
 __global__ void k_quantize_q8_0(const float * __restrict__ x, uint8_t * __restrict__ y, int64_t n_blocks) {
     const int64_t b = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
@@ -83,39 +68,6 @@ __global__ void k_quantize_q8_0(const float * __restrict__ x, uint8_t * __restri
     uint8_t * blk = y + b * 34;
     if (lane == 0) *reinterpret_cast<uint16_t *>(blk) = dh;
     blk[2 + lane] = (uint8_t)q;
-}
-
-// ------------------------------------------------------------ GEMV core
-// Exact int32 dot of one Q4_0 block (16 nibble bytes, offset 8) with one Q8_0
-// block held as 8 packed ints (elements 4k..4k+3 in qs[k]) and its sum.
-__device__ __forceinline__ int q4q8_dot(uint4 w, const int4 a_lo, const int4 a_hi, int asum) {
-    int s = 0;
-    s = __dp4a((int)(w.x & 0x0F0F0F0Fu), a_lo.x, s);
-    s = __dp4a((int)(w.y & 0x0F0F0F0Fu), a_lo.y, s);
-    s = __dp4a((int)(w.z & 0x0F0F0F0Fu), a_lo.z, s);
-    s = __dp4a((int)(w.w & 0x0F0F0F0Fu), a_lo.w, s);
-    s = __dp4a((int)((w.x >> 4) & 0x0F0F0F0Fu), a_hi.x, s);
-    s = __dp4a((int)((w.y >> 4) & 0x0F0F0F0Fu), a_hi.y, s);
-    s = __dp4a((int)((w.z >> 4) & 0x0F0F0F0Fu), a_hi.z, s);
-    s = __dp4a((int)((w.w >> 4) & 0x0F0F0F0Fu), a_hi.w, s);
-    return s - 8 * asum;
-}
-
-// Writes the Q8_0 record of block b from one warp's 32 lane values.
-__device__ __forceinline__ void store_xrec(int * xs, int b, int lane, int8_t q, uint16_t dh) {
-    const int qi = (int)(uint8_t)q;
-    const int b1 = __shfl_down_sync(0xffffffffu, qi, 1);
-    const int b2 = __shfl_down_sync(0xffffffffu, qi, 2);
-    const int b3 = __shfl_down_sync(0xffffffffu, qi, 3);
-    int s = (int)q;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    int * rec = xs + b * XREC_INTS;
-    if ((lane & 3) == 0) rec[lane >> 2] = qi | (b1 << 8) | (b2 << 16) | (b3 << 24);
-    if (lane == 0) {
-        rec[8] = __float_as_int(alb_h2f(dh));
-        rec[9] = s;
-    }
 }
 
 // CONSUMERS_ONLY: synchronise the GEMV_WARPS consumer warps with named barrier 1
@@ -258,9 +210,9 @@ k_gemv_direct(const GemvArgs a) {
 
     for (; item < it1; item += GEMV_WARPS) {
         if (warp == 0 && lane == 0) prefetch_upto(item + pf_items);
-        float acc[RPW];
+        double acc[RPW];
 #pragma unroll
-        for (int r = 0; r < RPW; ++r) acc[r] = 0.0f;
+        for (int r = 0; r < RPW; ++r) acc[r] = 0.0;
 #pragma unroll
         for (int i = 0; i < ITERS; ++i) {
             const int b = lane + 32 * i;
@@ -273,23 +225,24 @@ k_gemv_direct(const GemvArgs a) {
                 for (int r = 0; r < RPW; ++r) {
                     const int I = q4q8_dot(w[r][i], a_lo, a_hi, ds.y);
                     if constexpr (OUT == GEMV_OUT_DOTS) a.dots[(item * RPW + r) * nb + b] = I;
-                    acc[r] = fmaf(__int2float_rn(I), __fmul_rn(dx, alb_h2f(dw[r][i])), acc[r]);
+                    acc[r] = fma((double)I, (double)__fmul_rn(dx, alb_h2f(dw[r][i])), acc[r]);
                 }
             }
         }
         const int64_t cur = item;
         if (item + GEMV_WARPS < it1) load(item + GEMV_WARPS);  // next item's weights in flight
 #pragma unroll
-        for (int r = 0; r < RPW; ++r) acc[r] = alb_warp_sum(acc[r]);
+        for (int r = 0; r < RPW; ++r) acc[r] = alb_warp_sum_d(acc[r]);
         if (lane == 0 && a.y) {
             if constexpr (OUT == GEMV_OUT_SWIGLU) {
-                const float g = acc[0], u = acc[1];
-                a.y[cur] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+                const float g = __double2float_rn(acc[0]), u = __double2float_rn(acc[1]);
+                a.y[cur] = alb_swiglu1(g, u);
             } else {
 #pragma unroll
                 for (int r = 0; r < RPW; ++r) {
                     const int64_t row = cur * RPW + r;
-                    a.y[row] = a.residual ? __fadd_rn(acc[r], a.residual[row]) : acc[r];
+                    const float yv = __double2float_rn(acc[r]);
+                    a.y[row] = a.residual ? __fadd_rn(yv, a.residual[row]) : yv;
                 }
             }
         }
@@ -394,9 +347,9 @@ k_gemv_tma(const GemvArgs a, const TmaPlan plan) {
         if (item < it1) {
             const uint8_t * nib = stages + (size_t)st * plan.stage_bytes + (size_t)warp * RPW * row_bytes;
             const uint16_t * sc = reinterpret_cast<const uint16_t *>(stages + (size_t)st * plan.stage_bytes + plan.nib_bytes) + (size_t)warp * RPW * sp;
-            float acc[RPW];
+            double acc[RPW];
 #pragma unroll
-            for (int r = 0; r < RPW; ++r) acc[r] = 0.0f;
+            for (int r = 0; r < RPW; ++r) acc[r] = 0.0;
 #pragma unroll
             for (int i = 0; i < ITERS; ++i) {
                 const int b = lane + 32 * i;
@@ -409,21 +362,22 @@ k_gemv_tma(const GemvArgs a, const TmaPlan plan) {
                     for (int r = 0; r < RPW; ++r) {
                         const uint4 w = *reinterpret_cast<const uint4 *>(nib + r * row_bytes + 16 * b);
                         const int I = q4q8_dot(w, a_lo, a_hi, ds.y);
-                        acc[r] = fmaf(__int2float_rn(I), __fmul_rn(dx, alb_h2f(sc[r * sp + b])), acc[r]);
+                        acc[r] = fma((double)I, (double)__fmul_rn(dx, alb_h2f(sc[r * sp + b])), acc[r]);
                     }
                 }
             }
 #pragma unroll
-            for (int r = 0; r < RPW; ++r) acc[r] = alb_warp_sum(acc[r]);
+            for (int r = 0; r < RPW; ++r) acc[r] = alb_warp_sum_d(acc[r]);
             if (lane == 0) {
                 if constexpr (OUT == GEMV_OUT_SWIGLU) {
-                    const float gt = acc[0], u = acc[1];
-                    a.y[item] = __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, expf(-gt))), u);
+                    const float gt = __double2float_rn(acc[0]), u = __double2float_rn(acc[1]);
+                    a.y[item] = alb_swiglu1(gt, u);
                 } else {
 #pragma unroll
                     for (int r = 0; r < RPW; ++r) {
                         const int64_t row = item * RPW + r;
-                        a.y[row] = a.residual ? __fadd_rn(acc[r], a.residual[row]) : acc[r];
+                        const float yv = __double2float_rn(acc[r]);
+                    a.y[row] = a.residual ? __fadd_rn(yv, a.residual[row]) : yv;
                     }
                 }
             }

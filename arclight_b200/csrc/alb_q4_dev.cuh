@@ -1,0 +1,58 @@
+// Device helpers shared by the Q4_0 x Q8_0 kernels (mat-vec, token-batched mat-vec).
+#pragma once
+
+#include "alb_common.cuh"
+#include "alb_internal.h"
+
+namespace alb {
+
+static constexpr int GEMV_WARPS = 8;            // consumer warps per CTA
+static constexpr int XREC_INTS = 12;            // 48-byte activation record per block
+
+// ------------------------------------------------------------ quantizer
+// One warp per 32-value block; lane j owns element j.  amax is an exact max
+// (order-free), d = amax/127 and id = 1/d are IEEE divisions, q = RNE(x*id)
+// (vcvtnq_s32_f32), d stored as fp16 (arm.cpp:1834-1851).
+__device__ __forceinline__ void q8_block_lane(float v, int8_t & q, uint16_t & dh) {
+    const float amax = alb_warp_max(fabsf(v));
+    const float d = amax / 127.0f;
+    const float id = d != 0.0f ? 1.0f / d : 0.0f;
+    q = (int8_t)__float2int_rn(__fmul_rn(v, id));
+    dh = alb_f2h(d);
+}
+
+// ------------------------------------------------------------ GEMV core
+// Exact int32 dot of one Q4_0 block (16 nibble bytes, offset 8) with one Q8_0
+// block held as 8 packed ints (elements 4k..4k+3 in qs[k]) and its sum.
+__device__ __forceinline__ int q4q8_dot(uint4 w, const int4 a_lo, const int4 a_hi, int asum) {
+    int s = 0;
+    s = __dp4a((int)(w.x & 0x0F0F0F0Fu), a_lo.x, s);
+    s = __dp4a((int)(w.y & 0x0F0F0F0Fu), a_lo.y, s);
+    s = __dp4a((int)(w.z & 0x0F0F0F0Fu), a_lo.z, s);
+    s = __dp4a((int)(w.w & 0x0F0F0F0Fu), a_lo.w, s);
+    s = __dp4a((int)((w.x >> 4) & 0x0F0F0F0Fu), a_hi.x, s);
+    s = __dp4a((int)((w.y >> 4) & 0x0F0F0F0Fu), a_hi.y, s);
+    s = __dp4a((int)((w.z >> 4) & 0x0F0F0F0Fu), a_hi.z, s);
+    s = __dp4a((int)((w.w >> 4) & 0x0F0F0F0Fu), a_hi.w, s);
+    return s - 8 * asum;
+}
+
+// Writes the Q8_0 record of block b from one warp's 32 lane values.
+__device__ __forceinline__ void store_xrec(int * xs, int b, int lane, int8_t q, uint16_t dh) {
+    const int qi = (int)(uint8_t)q;
+    const int b1 = __shfl_down_sync(0xffffffffu, qi, 1);
+    const int b2 = __shfl_down_sync(0xffffffffu, qi, 2);
+    const int b3 = __shfl_down_sync(0xffffffffu, qi, 3);
+    int s = (int)q;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    int * rec = xs + b * XREC_INTS;
+    if ((lane & 3) == 0) rec[lane >> 2] = qi | (b1 << 8) | (b2 << 16) | (b3 << 24);
+    if (lane == 0) {
+        rec[8] = __float_as_int(alb_h2f(dh));
+        rec[9] = s;
+    }
+}
+
+
+}  // namespace alb

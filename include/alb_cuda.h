@@ -103,10 +103,15 @@ ALB_API int alb_qk_norm_rope_kv(const float * qkv, int64_t T, int32_t n_head, in
 /* ------------------------------------------------------------- attention */
 /* nnml_compute_forward_flash_attn_ext_f16 (arm.cpp:2196-2433), one sequence,
  * causal: token t (position pos0+t) attends cells [0, pos0+t] of the fp16
- * caches [cells][Hkv][128]; GQA ratio n_head/n_head_kv in {1,2,4,8}; split-K
- * over `splits` ranges merged in-kernel.  The workspace must be zeroed once
- * before first use (its tickets are re-armed by every call).  q/out [T][Hq][128]. */
-ALB_API size_t alb_flash_attn_workspace_bytes(int32_t n_head, int32_t n_head_kv, int64_t T, int32_t splits);
+ * caches [cells][Hkv][128]; GQA ratio n_head/n_head_kv in {1,2,4,8}.  Scores
+ * are fp32 (Q rounded to fp16 as the reference), the softmax uses the global
+ * max and the reference's NEON exp, sums are double: the result does not depend
+ * on `splits` (the cells are split over that many CTAs and merged in-kernel).
+ * Workspace: alb_flash_attn_workspace_bytes(.., n_cells = pos0 + T); zeroed
+ * once before first use (its tickets are re-armed by every call); may be NULL
+ * when splits == 1 and 4 * (n_head/n_head_kv) * (pos0+T) <= 160 KiB.  q/out [T][Hq][128]. */
+ALB_API size_t alb_flash_attn_workspace_bytes(int32_t n_head, int32_t n_head_kv, int64_t T, int32_t splits,
+                                             int32_t n_cells);
 ALB_API int alb_flash_attn(const float * q, const uint16_t * k_cache, const uint16_t * v_cache, int64_t T,
                            int32_t n_head, int32_t n_head_kv, int32_t pos0, float scale, int32_t splits,
                            void * workspace, float * out, void * stream);
@@ -115,6 +120,56 @@ ALB_API int alb_flash_attn(const float * q, const uint16_t * k_cache, const uint
 /* sample_none (sampler.cpp:34-36): first index of the maximum of x[0..n).
  * scratch >= 1024 bytes, zeroed once before first use. */
 ALB_API int alb_argmax(const float * x, int64_t n, void * scratch, int32_t * idx_out, void * stream);
+
+/* ------------------------------------------------------- Qwen3 engine
+ * llm_model + nnml_cgraph (build_qwen3_forward_tp, qwen3.cpp:174-275) +
+ * llm_kv_cache + decoding_context (context.cpp:21-205) for one sequence, on
+ * one GPU or as one tensor-parallel rank (one process/thread per GPU).  The
+ * model is the seeded synthetic Qwen3 of the benchmark configs (weights
+ * generated on the device; the same stream as oracle/oracle.c).  KV cache fp16,
+ * greedy sampling. */
+typedef struct alb_engine alb_engine;
+typedef struct {
+    int32_t n_layer, n_embd, n_head, n_head_kv, head_dim, n_ff, n_vocab, tied;
+    float   eps, freq_base;
+} alb_qwen3_config;   /* llm_hparams subset (model.h), head_dim = key_length */
+
+/* ncclGetUniqueId for tensor-parallel engines (128 bytes). */
+ALB_API int alb_nccl_unique_id(void * out128);
+/* al-gen.cpp:60-141 setup: weights, KV cache [max_ctx] and buffers for ubatches
+ * of up to max_ubatch tokens on CUDA device `device`; tp_size > 1 joins the
+ * NCCL clique `nccl_id` as tp_rank (n_head, n_head_kv, n_vocab divisible by
+ * tp_size; n_ff by 32*tp_size). */
+ALB_API int alb_engine_create(const alb_qwen3_config * cfg, uint64_t seed, int32_t max_ctx, int32_t max_ubatch,
+                              int32_t tp_rank, int32_t tp_size, const void * nccl_id, int32_t device,
+                              alb_engine ** out);
+ALB_API int alb_engine_destroy(alb_engine * e);
+ALB_API size_t alb_engine_device_bytes(const alb_engine * e);
+/* llm_kv_cache::clear (cgraph.cpp:988-993): zero the KV cache. */
+ALB_API int alb_engine_reset(alb_engine * e);
+/* decode() over a prompt chunk at positions [pos0, pos0+n) in ubatches of
+ * max_ubatch; returns the greedy next token. */
+ALB_API int alb_engine_prefill(alb_engine * e, const int32_t * tokens, int32_t n, int32_t pos0, int32_t * next_token);
+/* One greedy decode step of `token` at position `pos` (one CUDA-graph replay). */
+ALB_API int alb_engine_decode(alb_engine * e, int32_t token, int32_t pos, int32_t * next_token);
+/* n_steps greedy steps without host round trips; tokens_out (nullable) gets the
+ * generated tokens; sync != 0 waits for completion. */
+ALB_API int alb_engine_decode_loop(alb_engine * e, int32_t token, int32_t pos, int32_t n_steps, int32_t * tokens_out,
+                                   int32_t sync);
+/* Last logits of this rank's vocabulary shard [n_vocab / tp_size]. */
+ALB_API int alb_engine_logits(alb_engine * e, float * host, int64_t n);
+/* info[0..7] = local vocab, vocab offset, local q heads, local kv heads, local
+ * ffn, kernel launches per decode step, device bytes, decode attention splits */
+ALB_API int alb_engine_info(const alb_engine * e, int64_t * info, int32_t n);
+ALB_API void * alb_engine_stream(alb_engine * e);
+/* This rank's shard of weight (layer, kind) in block_q4_0 rows (host), kinds as
+ * oracle.h (4 WQ, 5 WK, 6 WV, 7 WO, 11 GATE, 12 UP, 13 DOWN; layer -1 kind 0 =
+ * token table).  host = NULL only reports the shard shape. */
+ALB_API int alb_engine_weight_blocks(alb_engine * e, int32_t layer, int32_t kind, void * host, int64_t * rows,
+                                     int64_t * cols);
+ALB_API int alb_engine_norm_weights(alb_engine * e, int32_t layer, int32_t kind, float * host, int64_t n);
+/* Fill every layer's KV cache for positions [0, n_pos) with seeded N(0,1) fp16. */
+ALB_API int alb_engine_fill_kv(alb_engine * e, int32_t n_pos, uint64_t seed);
 
 #ifdef __cplusplus
 }

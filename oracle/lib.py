@@ -72,6 +72,9 @@ def lib() -> C.CDLL:
             "orc_dequantize_row_q8_0": (None, [vp, vp, i64]),
             "orc_repack_q4_0_4x4": (C.c_int, [vp, vp, i64, i64]),
             "orc_gemv_q4_0_q8_0": (None, [vp, vp, vp, i64, i64, vp, C.c_int]),
+            "orc_gemv_q4_0_q8_0_exact": (None, [vp, vp, vp, i64, i64, C.c_int]),
+            "orc_neon_expf": (f32, [f32]),
+            "orc_model_set_exact": (None, [vp, C.c_int]),
             "orc_vec_dot_q4_0_q8_0": (f32, [vp, vp, i64]),
             "orc_mul_mat_generic": (None, [vp, vp, vp, i64, i64, C.c_int]),
             "orc_rms_norm": (None, [vp, vp, vp, i64, i64, f32]),
@@ -155,6 +158,16 @@ def gemv(w: np.ndarray, xq: np.ndarray, threads: int = 8):
     dots = np.empty((n, nb), np.int32)
     lib().orc_gemv_q4_0_q8_0(_ptr(w), _ptr(xq), _ptr(y), n, nb * 32, _ptr(dots), threads)
     return y, dots
+
+
+def gemv_exact(w: np.ndarray, xq: np.ndarray, threads: int = 8) -> np.ndarray:
+    """Exactly rounded mat-vec (block terms summed exactly in double)."""
+    w = np.ascontiguousarray(w)
+    xq = np.ascontiguousarray(xq)
+    n, nb = w.shape
+    y = np.empty(n, np.float32)
+    lib().orc_gemv_q4_0_q8_0_exact(_ptr(w), _ptr(xq), _ptr(y), n, nb * 32, threads)
+    return y
 
 
 def mul_mat_generic(w: np.ndarray, xq: np.ndarray, threads: int = 8) -> np.ndarray:
@@ -248,6 +261,10 @@ class Model:
 
     def reset(self):
         lib().orc_model_reset(self.h)
+
+    def set_exact(self, exact: bool):
+        """True (default): exactly rounded mat-vecs; False: the reference's NEON fp32 chains."""
+        lib().orc_model_set_exact(self.h, 1 if exact else 0)
 
 
 def argmax(x: np.ndarray) -> int:

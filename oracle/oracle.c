@@ -41,6 +41,8 @@ static inline uint16_t h_add(uint16_t a, uint16_t b) { return h_from_d(d_from_h(
 static inline uint16_t h_mul(uint16_t a, uint16_t b) { return h_from_d(d_from_h(a) * d_from_h(b)); }
 static inline uint16_t h_fma(uint16_t a, uint16_t b, uint16_t c) { return h_from_d(d_from_h(a) * d_from_h(b) + d_from_h(c)); }
 
+float orc_neon_expf(float x);
+
 /* ------------------------------------------------------- synthetic inputs */
 uint64_t orc_splitmix64(uint64_t x) {
     uint64_t z = x + 0x9E3779B97F4A7C15ULL;
@@ -229,7 +231,7 @@ static inline int32_t block_dot_q4_0_q8_0(const orc_block_q4_0 * w, const orc_bl
 }
 
 typedef struct {
-    const orc_block_q4_0 * W; const orc_block_q8_0 * xq; float * y; int32_t * dots; int64_t nb;
+    const orc_block_q4_0 * W; const orc_block_q8_0 * xq; float * y; int32_t * dots; int64_t nb; int exact;
 } gemv_ctx;
 
 /* gemm.cpp:127-190: acc = vfmaq_f32(acc, vcvtq_n_f32_s32(16*I, 4), vmulq_f32(f32(ad), f32(bd)));
@@ -239,19 +241,32 @@ static void gemv_range(void * p, int64_t r0, int64_t r1) {
     for (int64_t n = r0; n < r1; ++n) {
         const orc_block_q4_0 * w = c->W + n * c->nb;
         float acc = 0.0f;
+        double accd = 0.0;
         for (int64_t b = 0; b < c->nb; ++b) {
             const int32_t I = block_dot_q4_0_q8_0(&w[b], &c->xq[b]);
             if (c->dots) c->dots[n * c->nb + b] = I;
-            const float s = orc_fp16_to_fp32(c->xq[b].d) * orc_fp16_to_fp32(w[b].d);
-            acc = fmaf((float)I, s, acc);
+            const float s = orc_fp16_to_fp32(c->xq[b].d) * orc_fp16_to_fp32(w[b].d);  /* exact: 11x11 bits */
+            if (c->exact) accd += (double)I * (double)s;                               /* exact product */
+            else acc = fmaf((float)I, s, acc);
         }
-        c->y[n] = acc;
+        c->y[n] = c->exact ? (float)accd : acc;
     }
 }
 
 void orc_gemv_q4_0_q8_0(const orc_block_q4_0 * W, const orc_block_q8_0 * xq, float * y,
                         int64_t N, int64_t K, int32_t * block_dots, int n_threads) {
-    gemv_ctx c = { W, xq, y, block_dots, K / ORC_QK };
+    gemv_ctx c = { W, xq, y, block_dots, K / ORC_QK, 0 };
+    orc_parallel_for(n_threads, N, gemv_range, &c);
+}
+
+/* The exactly rounded value of the same mat-vec: every block term I*dx*dw is
+ * exact in double (38 significant bits); their double sum is exact whenever the
+ * block scales of a row span < 2^7 (always, for these models), so the result
+ * does not depend on the summation order.  It differs from the NEON fp32 chain
+ * above by a few fp32 ulps. */
+void orc_gemv_q4_0_q8_0_exact(const orc_block_q4_0 * W, const orc_block_q8_0 * xq, float * y,
+                              int64_t N, int64_t K, int n_threads) {
+    gemv_ctx c = { W, xq, y, NULL, K / ORC_QK, 1 };
     orc_parallel_for(n_threads, N, gemv_range, &c);
 }
 
@@ -348,10 +363,40 @@ void orc_rope_neox(const float * x, float * y, int64_t n_heads, int64_t head_dim
     }
 }
 
-/* nnml_vec_swiglu_f32 (arm.cpp:1789-1809): silu(x) * g with x = gate, g = up
- * (nnml_swiglu_split(cur=gate, tmp=up), cgraph.cpp:610-614). */
+static inline uint32_t f_bits(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
+static inline float bits_f(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+
+/* nnml_v_expf (arm.cpp:1757-1787), per lane: exp(x) = 2^n * (1 + poly(b)),
+ * n = round(x/ln2) by the 1.5*2^23 shift, b = x - n*ln2 (two-part ln2), a
+ * degree-5 polynomial; |n| > 126 / > 192 take the scaled and saturated paths.
+ * vfmaq_f32(a, b, c) = a + b*c fused; vfmsq_f32(a, b, c) = a - b*c fused. */
+float orc_neon_expf(float x) {
+    const float r = 0x1.8p23f;
+    const float z = fmaf(x, 0x1.715476p+0f, r);
+    const float n = z - r;
+    const float b = fmaf(-n, 0x1.7f7d1cp-20f, fmaf(-n, 0x1.62e4p-1f, x));
+    const uint32_t e = f_bits(z) << 23;
+    const float k = bits_f(e + f_bits(1.0f));
+    const float u = b * b;
+    const float j = fmaf(fmaf(fmaf(0x1.0e4020p-7f, b, 0x1.573e2ep-5f), u, fmaf(0x1.555e66p-3f, b, 0x1.fffdb6p-2f)), u,
+                         0x1.ffffecp-1f * b);
+    const float an = fabsf(n);
+    if (!(an > 126.0f)) return fmaf(j, k, k);
+    const uint32_t d = (n <= 0.0f) ? 0x82000000u : 0u;
+    const float s1 = bits_f(d + 0x7f000000u);
+    const float s2 = bits_f(e - d);
+    if (an > 192.0f) return s1 * s1;
+    return fmaf(s2, j, s2) * s1;
+}
+
+/* nnml_vec_swiglu_f32 NEON path (arm.cpp:1789-1809): silu(x) * g with x = gate,
+ * g = up (nnml_swiglu_split(cur=gate, tmp=up), cgraph.cpp:610-614);
+ * nnml_v_silu = x / (1 + v_expf(0 - x)). */
 void orc_swiglu(const float * g, const float * u, float * y, int64_t n) {
-    for (int64_t i = 0; i < n; ++i) y[i] = (g[i] / (1.0f + expf(-g[i]))) * u[i];
+    for (int64_t i = 0; i < n; ++i) {
+        const float x = g[i];
+        y[i] = (x / (1.0f + orc_neon_expf(0.0f - x))) * u[i];
+    }
 }
 
 /* nnml_vec_add_f32 (arm.cpp:2435-2451): acc = src0; acc += src_j in order. */
@@ -383,35 +428,63 @@ static float vec_dot_f16_arm(int64_t n, const uint16_t * x, const uint16_t * y) 
 }
 
 /* nnml_compute_forward_flash_attn_ext_f16 (arm.cpp:2196-2433) for F16 K/V,
- * max_bias = 0, softcap = 0, no sinks; the mask admits cells [0, kv_len). */
+ * max_bias = 0, softcap = 0, no sinks; the mask admits cells [0, kv_len).
+ *
+ * mode 1 restates the reference's NEON loop: Q rounded to fp16, K.Q with
+ * vec_dot_f16's fp16 FMA lanes, online softmax with libm expf, V accumulated
+ * in fp16 (VKQ16), out = VKQ/S.
+ * mode 0 is the fp32 semantics the CUDA kernels implement, defined so that it
+ * does not depend on how the cells are split: Q rounded to fp16 (as the
+ * reference), score s_c = (sequential fp32 fma chain over d of K.Q) * scale,
+ * M = max_c s_c, p_c = v_expf(s_c - M) (nnml_v_expf, arm.cpp:1757-1787),
+ * L = sum_c p_c and O_d = sum_c p_c V_cd summed in double, out_d = O_d / L.
+ * Softmax is shift invariant, so this is the same function as the
+ * reference's online form; only roundings differ. */
 void orc_flash_attn(const float * q, const uint16_t * k, const uint16_t * v, const int32_t * kv_len,
                     int64_t T, int64_t n_head, int64_t n_head_kv, int64_t D, float scale,
                     int mode, float * out) {
     const int64_t rk2 = n_head / n_head_kv;
     const int64_t row = n_head_kv * D;
+    int64_t nmax = 1;
+    for (int64_t t = 0; t < T; ++t) nmax = kv_len[t] > nmax ? kv_len[t] : nmax;
     uint16_t * Qh = (uint16_t *)malloc(D * 2);
     uint16_t * VKQ16 = (uint16_t *)malloc(D * 2);
     float * VKQ32 = (float *)malloc(D * 4);
     float * Qf = (float *)malloc(D * 4);
+    float * sc = (float *)malloc(nmax * 4);
+    double * Od = (double *)malloc(D * sizeof(double));
     for (int64_t t = 0; t < T; ++t) {
         for (int64_t h = 0; h < n_head; ++h) {
             const int64_t hk = h / rk2;
             const float * pq = q + (t * n_head + h) * D;
+            float * po = out + (t * n_head + h) * D;
             for (int64_t d = 0; d < D; ++d) { Qh[d] = orc_fp32_to_fp16(pq[d]); Qf[d] = orc_fp16_to_fp32(Qh[d]); }
+            if (mode == 0) {
+                float M = -INFINITY;
+                for (int64_t c = 0; c < kv_len[t]; ++c) {
+                    const uint16_t * kc = k + c * row + hk * D;
+                    float a = 0.0f;
+                    for (int64_t d = 0; d < D; ++d) a = fmaf(orc_fp16_to_fp32(kc[d]), Qf[d], a);
+                    sc[c] = a * scale;
+                    M = sc[c] > M ? sc[c] : M;
+                }
+                double L = 0.0;
+                for (int64_t d = 0; d < D; ++d) Od[d] = 0.0;
+                for (int64_t c = 0; c < kv_len[t]; ++c) {
+                    const float p = orc_neon_expf(sc[c] - M);
+                    const uint16_t * vc = v + c * row + hk * D;
+                    L += (double)p;
+                    for (int64_t d = 0; d < D; ++d) Od[d] += (double)p * (double)orc_fp16_to_fp32(vc[d]);
+                }
+                for (int64_t d = 0; d < D; ++d) po[d] = L > 0.0 ? (float)(Od[d] / L) : 0.0f;
+                continue;
+            }
             float S = 0.0f, M = -INFINITY;
             memset(VKQ16, 0, D * 2);
-            memset(VKQ32, 0, D * 4);
             for (int64_t c = 0; c < kv_len[t]; ++c) {
                 const uint16_t * kc = k + c * row + hk * D;
                 const uint16_t * vc = v + c * row + hk * D;
-                float s;
-                if (mode == 1) {
-                    s = vec_dot_f16_arm(D, kc, Qh);
-                } else {
-                    float a = 0.0f;
-                    for (int64_t d = 0; d < D; ++d) a = fmaf(orc_fp16_to_fp32(kc[d]), Qf[d], a);
-                    s = a;
-                }
+                float s = vec_dot_f16_arm(D, kc, Qh);
                 s = s * scale;
                 s += 0.0f; /* mask value of an admitted cell */
                 const float Mold = M;
@@ -419,22 +492,21 @@ void orc_flash_attn(const float * q, const uint16_t * k, const uint16_t * v, con
                 if (s > M) {
                     M = s;
                     ms = expf(Mold - M);
-                    if (mode == 1) { const uint16_t hm = orc_fp32_to_fp16(ms); for (int64_t d = 0; d < D; ++d) VKQ16[d] = h_mul(VKQ16[d], hm); }
-                    else           { for (int64_t d = 0; d < D; ++d) VKQ32[d] *= ms; }
+                    const uint16_t hm = orc_fp32_to_fp16(ms);
+                    for (int64_t d = 0; d < D; ++d) VKQ16[d] = h_mul(VKQ16[d], hm);
                 } else {
                     vs = expf(s - M);
                 }
-                if (mode == 1) { const uint16_t hv = orc_fp32_to_fp16(vs); for (int64_t d = 0; d < D; ++d) VKQ16[d] = h_fma(vc[d], hv, VKQ16[d]); }
-                else           { for (int64_t d = 0; d < D; ++d) VKQ32[d] = fmaf(orc_fp16_to_fp32(vc[d]), vs, VKQ32[d]); }
+                const uint16_t hv = orc_fp32_to_fp16(vs);
+                for (int64_t d = 0; d < D; ++d) VKQ16[d] = h_fma(vc[d], hv, VKQ16[d]);
                 S = S * ms + vs;
             }
-            if (mode == 1) for (int64_t d = 0; d < D; ++d) VKQ32[d] = orc_fp16_to_fp32(VKQ16[d]);
+            for (int64_t d = 0; d < D; ++d) VKQ32[d] = orc_fp16_to_fp32(VKQ16[d]);
             const float S_inv = S > 0.0f ? 1.0f / S : 0.0f;
-            float * po = out + (t * n_head + h) * D;
             for (int64_t d = 0; d < D; ++d) po[d] = VKQ32[d] * S_inv;
         }
     }
-    free(Qh); free(VKQ16); free(VKQ32); free(Qf);
+    free(Qh); free(VKQ16); free(VKQ32); free(Qf); free(sc); free(Od);
 }
 
 /* ------------------------------------------------------------ Qwen3 model */
@@ -452,6 +524,7 @@ struct orc_model {
     orc_layer * layers;
     float * table;
     uint64_t seed;
+    int exact;   /* 1: exactly rounded mat-vecs (default); 0: NEON fp32 chains */
 };
 
 typedef struct { const float * table; uint64_t seed; int64_t K; orc_block_q4_0 * dst; } gen_ctx;
@@ -485,6 +558,7 @@ orc_model * orc_model_create(const orc_qwen3_config * cfg, uint64_t seed, int32_
     m->max_ctx = max_ctx;
     m->n_threads = n_threads > 0 ? n_threads : 1;
     m->seed = seed;
+    m->exact = 1;
     m->table = (float *)malloc(65537 * sizeof(float));
     orc_normal_table(m->table);
     const orc_qwen3_config * c = &m->c;
@@ -577,9 +651,12 @@ static void matmul_rows(orc_model * m, const orc_block_q4_0 * W, const float * x
                         int64_t T, int64_t N, int64_t K, orc_block_q8_0 * qbuf) {
     for (int64_t t = 0; t < T; ++t) {
         orc_quantize_row_q8_0(x + t * K, qbuf, K);
-        orc_gemv_q4_0_q8_0(W, qbuf, y + t * N, N, K, NULL, m->n_threads);
+        if (m->exact) orc_gemv_q4_0_q8_0_exact(W, qbuf, y + t * N, N, K, m->n_threads);
+        else orc_gemv_q4_0_q8_0(W, qbuf, y + t * N, N, K, NULL, m->n_threads);
     }
 }
+
+void orc_model_set_exact(orc_model * m, int exact) { m->exact = exact; }
 
 int orc_model_forward(orc_model * m, const int32_t * tokens, int32_t T, int32_t pos0,
                       int fa_mode, float * logits, float * hidden) {
@@ -644,7 +721,8 @@ int orc_model_forward(orc_model * m, const int32_t * tokens, int32_t T, int32_t 
         orc_rms_norm(xl, m->output_norm, h, 1, E, c->eps);
         if (hidden) memcpy(hidden, h, E * 4);
         orc_quantize_row_q8_0(h, qb, E);
-        orc_mul_mat_generic(m->output, qb, logits, c->n_vocab, E, m->n_threads);
+        if (m->exact) orc_gemv_q4_0_q8_0_exact(m->output, qb, logits, c->n_vocab, E, m->n_threads);
+        else orc_mul_mat_generic(m->output, qb, logits, c->n_vocab, E, m->n_threads);
     }
     free(x); free(h); free(q); free(k); free(v); free(att); free(g); free(u); free(o); free(kv_len); free(qb);
     return rc;

@@ -60,6 +60,10 @@ int  orc_repack_q4_0_4x4(const orc_block_q4_0 * src, orc_block_q4_0x4 * dst, int
  * (the 4x4 interleave only reorders bytes).  block_dots (nullable) [N][K/32]. */
 void orc_gemv_q4_0_q8_0(const orc_block_q4_0 * W, const orc_block_q8_0 * xq, float * y,
                         int64_t N, int64_t K, int32_t * block_dots, int n_threads);
+/* Exactly rounded twin: block terms summed exactly in double, rounded once
+ * (order independent; within a few fp32 ulps of the NEON chain). */
+void orc_gemv_q4_0_q8_0_exact(const orc_block_q4_0 * W, const orc_block_q8_0 * xq, float * y,
+                              int64_t N, int64_t K, int n_threads);
 /* nnml_vec_dot_q4_0_q8_0 NEON path (arm.cpp:633-692): generic mul_mat (lm_head). */
 float orc_vec_dot_q4_0_q8_0(const orc_block_q4_0 * x, const orc_block_q8_0 * y, int64_t k);
 void  orc_mul_mat_generic(const orc_block_q4_0 * W, const orc_block_q8_0 * xq, float * y,
@@ -71,6 +75,8 @@ void orc_rms_norm(const float * x, const float * w, float * y, int64_t rows, int
 /* rope NEOX, ext_factor 0, freq_scale 1, attn_factor 1 (ops.cpp:747-961) */
 void orc_rope_cache(int32_t pos, int64_t n_dims, float theta_scale, float * cache /* [n_dims] cos,sin */);
 void orc_rope_neox(const float * x, float * y, int64_t n_heads, int64_t head_dim, int32_t pos, float freq_base);
+/* nnml_v_expf restated per lane (arm.cpp:1757-1787) */
+float orc_neon_expf(float x);
 /* swiglu: silu(g)*u (ops.cpp:1038-1092, arm.cpp:1789-1809) */
 void orc_swiglu(const float * g, const float * u, float * y, int64_t n);
 /* GATHER sum (ops.cpp:1465-1511, arm.cpp:2435-2451): dst = src0 + src1 + ... */
@@ -83,7 +89,9 @@ void orc_gather_sum(const float * const * srcs, int n_srcs, float * dst, int64_t
  * kv_len[t]: token t attends cells [0, kv_len[t]) (the causal mask of
  *        cgraph.cpp:1224-1261 for one sequence filled in order)
  * out  : [T][n_head][D] fp32
- * mode 0: fp32 accumulation; mode 1: ARM-faithful fp16 VKQ/KQ accumulation. */
+ * mode 0: fp32 scores, global-max softmax with nnml_v_expf, double sums (the
+ *         split-independent semantics of the CUDA kernels);
+ * mode 1: ARM-faithful fp16 VKQ/KQ accumulation with online softmax. */
 void orc_flash_attn(const float * q, const uint16_t * k, const uint16_t * v, const int32_t * kv_len,
                     int64_t T, int64_t n_head, int64_t n_head_kv, int64_t D, float scale,
                     int mode, float * out);
@@ -113,6 +121,10 @@ const float *          orc_model_f32_tensor(orc_model * m, int layer, int kind, 
 int  orc_model_forward(orc_model * m, const int32_t * tokens, int32_t T, int32_t pos0,
                        int fa_mode, float * logits, float * hidden);
 void orc_model_reset(orc_model * m);
+/* exact != 0 (default): mat-vecs use orc_gemv_q4_0_q8_0_exact (also for the lm
+ * head); 0: the reference's NEON fp32 chains (gemv for projections,
+ * nnml_vec_dot_q4_0_q8_0 lanes for the lm head). */
+void orc_model_set_exact(orc_model * m, int exact);
 /* greedy argmax (sampler.cpp:34-36: std::max_element => first maximum) */
 int32_t orc_argmax(const float * x, int64_t n);
 

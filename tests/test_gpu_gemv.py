@@ -1,7 +1,9 @@
 """GPU parity of the Q4_0 x Q8_0 mat-vec path against the oracle, through the C ABI.
 
 Bar (north_star): int32 block dots bit-exact; y within 1e-3 relative
-(tests/util.py); Q8_0 quantization and the GPU repack bit-exact.
+(tests/util.py) of the reference's NEON fp32 chain; Q8_0 quantization and the
+GPU repack bit-exact.  The kernel sums the exact block terms in double and
+rounds once, so y is also bit-identical to the oracle's exactly rounded mat-vec.
 """
 import numpy as np
 import pytest
@@ -68,6 +70,7 @@ def test_gemv_block_dots_bit_exact_and_y_within_tol(N, K):
     torch.cuda.synchronize()
     np.testing.assert_array_equal(I.cpu().numpy(), dots_ref)
     assert_rel(y.cpu().numpy(), y_ref, what=f"gemv {N}x{K}")
+    np.testing.assert_array_equal(y.cpu().numpy(), O.gemv_exact(wq, xq))
 
 
 def test_gemv_residual_add():

@@ -6,7 +6,7 @@ import pytest
 
 import arclight_b200 as A
 from oracle import lib as O
-from tests.util import assert_rel
+from tests.util import assert_rel, max_rel_err
 
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
@@ -44,9 +44,11 @@ def test_swiglu():
     g = (rng.standard_normal(9728) * 4).astype(np.float32)
     u = rng.standard_normal(9728).astype(np.float32)
     Y = torch.empty(9728, dtype=torch.float32, device="cuda")
-    A.check(L.alb_swiglu(cu(g).data_ptr(), cu(u).data_ptr(), Y.data_ptr(), 9728, st()))
+    G, U = cu(g), cu(u)   # keep the device tensors alive across the call
+    A.check(L.alb_swiglu(G.data_ptr(), U.data_ptr(), Y.data_ptr(), 9728, st()))
     torch.cuda.synchronize()
-    assert_rel(Y.cpu().numpy(), O.swiglu(g, u), what="swiglu")
+    # same restated nnml_v_expf polynomial on both sides: bit-exact
+    np.testing.assert_array_equal(Y.cpu().numpy(), O.swiglu(g, u))
 
 
 def test_get_rows_bit_exact():
@@ -57,7 +59,8 @@ def test_get_rows_bit_exact():
     A.check(L.alb_repack_q4_0(W.data_ptr(), src.data_ptr(), 1000, 256, st()))
     ids = np.array([0, 999, 17, 17, 500], np.int32)
     out = torch.empty((5, 256), dtype=torch.float32, device="cuda")
-    A.check(L.alb_get_rows_q4_0(W.data_ptr(), 1000, 256, cu(ids).data_ptr(), 5, out.data_ptr(), st()))
+    I = cu(ids)
+    A.check(L.alb_get_rows_q4_0(W.data_ptr(), 1000, 256, I.data_ptr(), 5, out.data_ptr(), st()))
     torch.cuda.synchronize()
     np.testing.assert_array_equal(out.cpu().numpy(), np.stack([O.dequantize_q4_0(tab[i]) for i in ids]))
 
@@ -79,7 +82,8 @@ def test_qk_norm_rope_kv(Hq, Hkv, T, pos0):
     Q = torch.empty((T, Hq, 128), dtype=torch.float32, device="cuda")
     KC = torch.zeros((cells, Hkv, 128), dtype=torch.int16, device="cuda")
     VC = torch.zeros((cells, Hkv, 128), dtype=torch.int16, device="cuda")
-    A.check(L.alb_qk_norm_rope_kv(cu(qkv).data_ptr(), T, Hq, Hkv, cu(qn).data_ptr(), cu(kn).data_ptr(), 1e-6,
+    QKV, QN, KN = cu(qkv), cu(qn), cu(kn)
+    A.check(L.alb_qk_norm_rope_kv(QKV.data_ptr(), T, Hq, Hkv, QN.data_ptr(), KN.data_ptr(), 1e-6,
                                   rt.data_ptr(), pos0, Q.data_ptr(), KC.data_ptr(), VC.data_ptr(), st()))
     torch.cuda.synchronize()
     q = qkv[:, :Hq * 128].reshape(T, Hq, 128)
@@ -101,6 +105,8 @@ def test_qk_norm_rope_kv(Hq, Hkv, T, pos0):
     (4, 1, 1, 4095, 296),    # TP=8 shard of the 8B (1 kv head), long
     (32, 8, 7, 100, 1),      # small prefill ubatch, causal within the ubatch
     (32, 8, 64, 0, 1),       # prefill from an empty cache
+    (32, 8, 3, 5000, 1),     # splits == 1 but too many cells for the fused kernel
+    (32, 8, 2, 300, 8),      # two tokens, split
 ])
 def test_flash_attn(Hq, Hkv, T, pos0, S):
     rng = np.random.default_rng(Hq + T + pos0)
@@ -110,7 +116,8 @@ def test_flash_attn(Hq, Hkv, T, pos0, S):
     q = (rng.standard_normal((T, Hq, 128)) * 0.5).astype(np.float32)
     kv_len = (pos0 + np.arange(T) + 1).astype(np.int32)
     scale = 1.0 / math.sqrt(128.0)
-    ws = torch.zeros(max(1, L.alb_flash_attn_workspace_bytes(Hq, Hkv, T, S)), dtype=torch.uint8, device="cuda")
+    ws = torch.zeros(max(1, L.alb_flash_attn_workspace_bytes(Hq, Hkv, T, S, pos0 + T)), dtype=torch.uint8,
+                     device="cuda")
     out = torch.empty((T, Hq, 128), dtype=torch.float32, device="cuda")
     Kd, Vd, Qd = cu(k.view(np.int16)), cu(v.view(np.int16)), cu(q)
     for rep in range(2):  # second call checks the re-armed tickets
@@ -119,9 +126,14 @@ def test_flash_attn(Hq, Hkv, T, pos0, S):
         torch.cuda.synchronize()
         ref = O.flash_attn(q, k, v, kv_len, scale, mode=0)
         assert_rel(out.cpu().numpy(), ref, what=f"flash_attn rep {rep}")
-    # the reference's own fp16-accumulating path differs from fp32 by its fp16 rounding
+        # split-independent semantics: identical to the oracle bit for bit
+        np.testing.assert_array_equal(out.cpu().numpy(), ref)
+    # The reference's own NEON path accumulates K.Q and V in fp16 (arm.cpp:2299-2368);
+    # against that arm-faithful restatement the fp32 kernel differs by the
+    # reference's fp16 rounding, which grows with the number of cells (2.2e-2
+    # normwise at 5000 cells); bounded normwise here.
     ref16 = O.flash_attn(q, k, v, kv_len, scale, mode=1)
-    assert_rel(out.cpu().numpy(), ref16, rtol=2e-2, what="flash_attn vs arm-faithful fp16")
+    assert max_rel_err(out.cpu().numpy(), ref16) < 5e-2
 
 
 @pytest.mark.parametrize("n", [151936, 18992, 1, 1000])
@@ -132,7 +144,8 @@ def test_argmax_first_max(n):
         x[n // 3] = x[n - 2] = 50.0   # tie: first index wins (std::max_element)
     scratch = torch.zeros(1024, dtype=torch.uint8, device="cuda")
     idx = torch.empty(1, dtype=torch.int32, device="cuda")
+    X = cu(x)
     for _ in range(2):
-        A.check(L.alb_argmax(cu(x).data_ptr(), n, scratch.data_ptr(), idx.data_ptr(), st()))
+        A.check(L.alb_argmax(X.data_ptr(), n, scratch.data_ptr(), idx.data_ptr(), st()))
         torch.cuda.synchronize()
         assert int(idx.item()) == O.argmax(x)
