@@ -58,3 +58,13 @@ def make_gemv_weights(n_copies: int, N: int, K: int, seed: int):
     A.check(L.alb_quantize_q8_0(x.data_ptr(), xq.data_ptr(), K, 1, s), "quantize")
     torch.cuda.synchronize()
     return Ws, xq
+
+
+def time_decode_gemvs(engine, cfg, world, rank, reps=3):
+    """Mean per-launch duration / achieved GB/s of the decode step's mat-vecs."""
+    import ctypes as C
+    import arclight_b200 as A
+    us, by = C.c_float(), C.c_double()
+    A.check(A.lib().alb_engine_time_gemv(engine.h, reps, C.byref(us), C.byref(by)), "alb_engine_time_gemv")
+    u = max_over_ranks(float(us.value), world)
+    return {"us_per_launch": u, "bytes_per_launch": float(by.value), "gbs": float(by.value) / (u * 1e-6) / 1e9}

@@ -16,11 +16,13 @@
 // no host round trip.  Prefill runs the same ops over a ubatch of T tokens.
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <vector>
 
 #include "alb_common.cuh"
 #include "alb_internal.h"
+#include "alb_mk.h"
 #include "alb_nccl.h"
 
 namespace alb {
@@ -81,6 +83,10 @@ struct alb_engine {
     size_t bytes = 0;
     int32_t * pinned = nullptr;     // host staging for the e2e path
     int launches_per_step = 0;
+    // persistent decode-step kernel (tp == 1): parameters and scratch
+    bool use_mk = false;
+    MkParams mk{};
+    MkLayer * mk_layers = nullptr;
 
     template <typename T> int alloc(T ** p, size_t n) {
         void * v = nullptr;
@@ -170,6 +176,18 @@ static int engine_forward(alb_engine * e, int64_t T, bool pdl, int ncap_prefill 
 
 static int engine_build_graph(alb_engine * e) {
     if (e->gexec) return ALB_OK;
+    if (e->use_mk) {
+        ALB_CUDA_TRY(cudaStreamBeginCapture(e->st, cudaStreamCaptureModeThreadLocal));
+        const cudaError_t le = launch_decode_step(e->mk, e->st);
+        cudaGraph_t g = nullptr;
+        const cudaError_t ce = cudaStreamEndCapture(e->st, &g);
+        if (le != cudaSuccess) { if (g) cudaGraphDestroy(g); alb_set_last_cuda_error(le, "decode step kernel"); return ALB_ERR_CUDA; }
+        ALB_CUDA_TRY(ce);
+        e->graph = g;
+        ALB_CUDA_TRY(cudaGraphInstantiate(&e->gexec, g, 0));
+        e->launches_per_step = 1;
+        return ALB_OK;
+    }
     ALB_CUDA_TRY(cudaStreamBeginCapture(e->st, cudaStreamCaptureModeThreadLocal));
     int rc = engine_forward(e, 1, true);
     if (rc == ALB_OK) {
@@ -285,6 +303,58 @@ static int engine_init_acts(alb_engine * e) {
     return ALB_OK;
 }
 
+// Parameters and scratch of the persistent decode-step kernel.
+static int engine_init_mk(alb_engine * e) {
+    const char * env = getenv("ALB_DECODE_MK");
+    if (e->tp != 1 || (env && atoi(env) == 0)) return ALB_OK;
+    const int ncta = alb_sm_count();
+    const int G = e->Hq / e->Hkv;
+    if (G > 4) return ALB_OK;
+    // attention: the cells of each kv head split over S CTAs, <= 512 cells each
+    const int S = ncta / e->Hkv;
+    if (S < 1 || (e->max_ctx + S - 1) / S > 512) return ALB_OK;
+    int dev_sm_optin = 0;
+    cudaDeviceGetAttribute(&dev_sm_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, e->dev);
+    if ((size_t)dev_sm_optin < mk_smem_bytes()) return ALB_OK;
+    std::vector<MkLayer> hl(e->c.n_layer);
+    for (int l = 0; l < e->c.n_layer; ++l) {
+        alb_engine::Layer & L = e->layers[l];
+        MkLayer & m = hl[l];
+        m.qkv_W = L.qkv; m.qkv_S = L.qkv + q4_scale_offset(e->Nqkv, e->E);
+        m.o_W = L.o; m.o_S = L.o + q4_scale_offset(e->E, e->Dq);
+        m.gu_W = L.gu; m.gu_S = L.gu + q4_scale_offset(2 * (int64_t)e->F, e->E);
+        m.dn_W = L.down; m.dn_S = L.down + q4_scale_offset(e->E, e->F);
+        m.an = L.an; m.fn = L.fn; m.qn = L.qn; m.kn = L.kn; m.kc = L.kc; m.vc = L.vc;
+    }
+    ALB_TRY(e->alloc(&e->mk_layers, hl.size()));
+    ALB_CUDA_TRY(cudaMemcpy(e->mk_layers, hl.data(), hl.size() * sizeof(MkLayer), cudaMemcpyHostToDevice));
+    MkParams & p = e->mk;
+    p.n_layer = e->c.n_layer; p.E = e->E; p.Hq = e->Hq; p.Hkv = e->Hkv; p.F = e->F; p.V = e->V; p.Nqkv = e->Nqkv;
+    p.Dq = e->Dq; p.v0 = e->v0; p.rank = e->rank; p.eps = e->c.eps; p.scale = 1.0f / sqrtf((float)e->c.head_dim);
+    p.layers = e->mk_layers; p.lm_W = e->lm_W; p.lm_S = e->lm_S; p.out_norm = e->out_norm;
+    p.tok_W = e->tok; p.tok_S = e->tok + q4_scale_offset(e->c.n_vocab, e->E); p.rope = e->rope;
+    p.x = e->x; p.qkv = e->qkv; p.att = e->att; p.h = e->h; p.logits = e->logits;
+    p.tok = e->tok_dev; p.pos = e->pos_dev; p.next = e->next_dev; p.gen_out = e->gen_out; p.step = e->step_dev;
+    p.gen_cap = e->gen_cap; p.advance = 1; p.S = S;
+    const char * pf = getenv("ALB_MK_PF");
+    p.pf_stages = pf ? atoi(pf) : 8;
+    ALB_TRY(e->alloc(&p.smax, (size_t)e->Hkv * S * G));
+    ALB_TRY(e->alloc(&p.part, (size_t)e->Hkv * S * G * 129));
+    int * words = nullptr;
+    ALB_TRY(e->alloc(&words, 64 + 3 * e->Hkv));
+    ALB_CUDA_TRY(cudaMemset(words, 0, (64 + 3 * e->Hkv) * sizeof(int)));
+    p.bar_count = reinterpret_cast<unsigned *>(words);
+    p.bar_gen = reinterpret_cast<unsigned *>(words + 1);
+    p.am_ticket = words + 2;
+    p.tickets = words + 64;
+    p.grp = reinterpret_cast<unsigned *>(words + 64 + e->Hkv);
+    ALB_TRY(e->alloc(&p.cand, (size_t)ncta));
+    p.err = device_error_ptr();
+    p.ncta = ncta;
+    e->use_mk = true;
+    return ALB_OK;
+}
+
 static void engine_free(alb_engine * e) {
     if (!e) return;
     cudaSetDevice(e->dev);
@@ -328,6 +398,7 @@ extern "C" int alb_engine_create(const alb_qwen3_config * cfg, uint64_t seed, in
     if (rc == ALB_OK && tp_size > 1) rc = nccl_init(&e->comm, tp_rank, tp_size, nccl_id);
     if (rc == ALB_OK) rc = engine_init_weights(e);
     if (rc == ALB_OK) rc = engine_init_acts(e);
+    if (rc == ALB_OK) rc = engine_init_mk(e);
     if (rc != ALB_OK) { engine_free(e); return rc; }
     *out = e;
     return ALB_OK;
@@ -429,7 +500,7 @@ extern "C" int alb_engine_logits(alb_engine * e, float * host, int64_t n) {
 extern "C" int alb_engine_info(const alb_engine * e, int64_t * info, int32_t n) {
     ALB_CHECK_ARG(e && info && n >= 8);
     info[0] = e->V; info[1] = e->v0; info[2] = e->Hq; info[3] = e->Hkv; info[4] = e->F;
-    info[5] = e->launches_per_step; info[6] = (int64_t)e->bytes; info[7] = e->fa_S_decode;
+    info[5] = e->launches_per_step; info[6] = (int64_t)e->bytes; info[7] = e->use_mk ? e->mk.S : e->fa_S_decode;
     return ALB_OK;
 }
 
@@ -491,6 +562,93 @@ extern "C" int alb_engine_norm_weights(alb_engine * e, int32_t layer, int32_t ki
     }
     ALB_CHECK_ARG(src && n == len);
     ALB_CUDA_TRY(cudaMemcpy(host, src, (size_t)n * 4, cudaMemcpyDeviceToHost));
+    return ALB_OK;
+}
+
+// Measurement hook: one decode step of the persistent kernel with CTA 0
+// recording %globaltimer (ns) at each phase boundary into host[0..n).  Returns
+// the number of stamps written (ALB_ERR_UNSUPPORTED when the persistent kernel
+// is not in use).
+extern "C" int alb_engine_decode_trace(alb_engine * e, int32_t token, int32_t pos, int64_t * host, int32_t n) {
+    ALB_CHECK_ARG(e && host && n > 0 && token >= 0 && token < e->c.n_vocab && pos >= 0 && pos < e->max_ctx);
+    if (!e->use_mk) { alb_set_last_error_msg("persistent decode kernel not in use"); return ALB_ERR_UNSUPPORTED; }
+    ALB_CUDA_TRY(cudaSetDevice(e->dev));
+    int64_t * tr = nullptr;
+    ALB_CUDA_TRY(cudaMalloc(&tr, 8192 * sizeof(int64_t)));
+    cudaMemsetAsync(tr, 0, 8192 * sizeof(int64_t), e->st);
+    e->pinned[0] = token;
+    e->pinned[1] = pos;
+    cudaMemcpyAsync(e->tok_dev, &e->pinned[0], 4, cudaMemcpyHostToDevice, e->st);
+    cudaMemcpyAsync(e->pos_dev, &e->pinned[1], 4, cudaMemcpyHostToDevice, e->st);
+    MkParams p = e->mk;
+    p.trace = tr;
+    cudaError_t le = launch_decode_step(p, e->st);
+    std::vector<int64_t> h(8192);
+    if (le == cudaSuccess) le = cudaMemcpyAsync(h.data(), tr, 8192 * sizeof(int64_t), cudaMemcpyDeviceToHost, e->st);
+    if (le == cudaSuccess) le = cudaStreamSynchronize(e->st);
+    cudaFree(tr);
+    ALB_CUDA_TRY(le);
+    int m = 0;
+    while (m < 1024 && h[m] != 0) ++m;
+    // stamps [0, m) are phases; when n > 1024 the per-stage stamps of the
+    // mat-vec phases follow at [1024, 8192): (wait start, data ready, released)
+    const int cp = n < 8192 ? n : 8192;
+    memcpy(host, h.data(), (size_t)cp * sizeof(int64_t));
+    return m;
+}
+
+// Times the decode step's Q4_0 mat-vec launches alone (all layers + lm head, in
+// step order, PDL chained) from a CUDA graph replayed `reps` times.  Reports
+// the mean duration per launch and the mean algorithmic bytes per launch
+// (weights 18 B / 32 values + fp32 input + fp32 output).
+extern "C" int alb_engine_time_gemv(alb_engine * e, int32_t reps, float * us_per_launch, double * bytes_per_launch) {
+    ALB_CHECK_ARG(e && reps > 0 && us_per_launch && bytes_per_launch);
+    ALB_CUDA_TRY(cudaSetDevice(e->dev));
+    std::vector<GemvArgs> list;
+    double bytes = 0.0;
+    auto add = [&](const uint8_t * W, const uint8_t * S, int64_t N, int64_t K, int in, const void * x, const float * nw,
+                   int out, float * y, const float * res) {
+        GemvArgs a;
+        a.W = W; a.S = S ? S : W + q4_scale_offset(N, K); a.N = N; a.K = K;
+        a.in_mode = in; a.x = x; a.norm_w = nw; a.eps = e->c.eps;
+        a.out_mode = out; a.y = y; a.residual = res; a.pdl = true;
+        list.push_back(a);
+        bytes += (double)N * K * 18 / 32 + K * 4.0 + (out == GEMV_OUT_SWIGLU ? N / 2 : N) * 4.0;
+    };
+    for (int l = 0; l < e->c.n_layer; ++l) {
+        alb_engine::Layer & L = e->layers[l];
+        add(L.qkv, nullptr, e->Nqkv, e->E, GEMV_IN_F32_RMS, e->x, L.an, GEMV_OUT_PLAIN, e->qkv, nullptr);
+        add(L.o, nullptr, e->E, e->Dq, GEMV_IN_F32, e->att, nullptr, GEMV_OUT_PLAIN, e->qkv, nullptr);
+        add(L.gu, nullptr, 2 * (int64_t)e->F, e->E, GEMV_IN_F32_RMS, e->x, L.fn, GEMV_OUT_SWIGLU, e->h, nullptr);
+        add(L.down, nullptr, e->E, e->F, GEMV_IN_F32, e->h, nullptr, GEMV_OUT_PLAIN, e->qkv, nullptr);
+    }
+    add(e->lm_W, e->lm_S, e->V, e->E, GEMV_IN_F32_RMS, e->x, e->out_norm, GEMV_OUT_PLAIN, e->logits, nullptr);
+    cudaGraph_t g = nullptr;
+    cudaGraphExec_t ge = nullptr;
+    ALB_CUDA_TRY(cudaStreamBeginCapture(e->st, cudaStreamCaptureModeThreadLocal));
+    cudaError_t le = cudaSuccess;
+    for (const GemvArgs & a : list) if (le == cudaSuccess) le = launch_gemv(a, e->st);
+    const cudaError_t ce = cudaStreamEndCapture(e->st, &g);
+    ALB_CUDA_TRY(le);
+    ALB_CUDA_TRY(ce);
+    ALB_CUDA_TRY(cudaGraphInstantiate(&ge, g, 0));
+    cudaEvent_t a0, a1;
+    cudaEventCreate(&a0);
+    cudaEventCreate(&a1);
+    for (int i = 0; i < 2; ++i) cudaGraphLaunch(ge, e->st);
+    cudaEventRecord(a0, e->st);
+    for (int i = 0; i < reps; ++i) cudaGraphLaunch(ge, e->st);
+    cudaEventRecord(a1, e->st);
+    cudaError_t se = cudaEventSynchronize(a1);
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, a0, a1);
+    cudaEventDestroy(a0);
+    cudaEventDestroy(a1);
+    cudaGraphExecDestroy(ge);
+    cudaGraphDestroy(g);
+    ALB_CUDA_TRY(se);
+    *us_per_launch = ms * 1000.0f / (float)(reps * list.size());
+    *bytes_per_launch = bytes / (double)list.size();
     return ALB_OK;
 }
 

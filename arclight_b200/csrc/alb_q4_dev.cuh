@@ -37,6 +37,19 @@ __device__ __forceinline__ int q4q8_dot(uint4 w, const int4 a_lo, const int4 a_h
     return s - 8 * asum;
 }
 
+// Exact conversions onto the fp64 pipe (no conversion instruction).
+// fp16 bits -> double for every finite half: the half's exponent and mantissa
+// bits placed at the top of a double's (value * 2^-1008, a subnormal double
+// for a subnormal half), then scaled by 2^1008.
+__device__ __forceinline__ double alb_h2d(uint32_t h) {
+    const uint32_t hi = ((h & 0x7FFFu) << 10) | ((h & 0x8000u) << 16);
+    return __hiloint2double((int)hi, 0) * 0x1p1008;
+}
+// int32 -> double: (2^52 + (i + 2^31)) - (2^52 + 2^31), all exact.
+__device__ __forceinline__ double alb_i2d(int i) {
+    return __hiloint2double(0x43300000, i ^ (int)0x80000000) - 4503601774854144.0;
+}
+
 // Writes the Q8_0 record of block b from one warp's 32 lane values.
 __device__ __forceinline__ void store_xrec(int * xs, int b, int lane, int8_t q, uint16_t dh) {
     const int qi = (int)(uint8_t)q;

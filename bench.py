@@ -4,6 +4,9 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode|gemv] [--impl ours|reference]
 
 Workloads:
+  decode  config 3 (default): Qwen3-4B-shaped Q4_0 model, random init, 512-token
+          uniform random prompt, then greedy batch-1 decode; a step is one token
+          (one CUDA-graph replay).  N > 1: tensor parallel over N GPUs (NCCL).
   gemv    config 1: one Q4_0 x Q8_0 mat-vec, W [9728 x 2560]; a step is one
           launch over one of 24 distinct weight copies (336 MB > 126 MB L2).
 Metric / value / roofline conventions: see DESIGN.md "Measurement".
@@ -193,16 +196,133 @@ def run_gemv(args, rank, world):
     return out
 
 
+# ----------------------------------------------------------------- decode (config 3)
+def decode_bytes_per_token(cfg, pos_mean):
+    """Algorithmic HBM bytes of one batch-1 decode step: every Q4_0 weight once
+    (18 B per 32 values), the fp32 norm weights, and the fp16 K/V of the valid
+    positions (pos + 1 cells per layer)."""
+    E, F, L, V = cfg["n_embd"], cfg["n_ff"], cfg["n_layer"], cfg["n_vocab"]
+    Dq, Dkv = cfg["n_head"] * cfg["head_dim"], cfg["n_head_kv"] * cfg["head_dim"]
+    per_layer = (E * (Dq + 2 * Dkv) + Dq * E + 3 * E * F) * 18 // 32
+    lm = V * E * 18 // 32
+    norms = (L * (2 * E + 2 * cfg["head_dim"]) + E) * 4
+    kv = L * 2 * Dkv * 2 * (pos_mean + 1)
+    return L * per_layer + lm + norms + kv
+
+
+def cpu_decode_baseline(cfg, seconds=20.0):
+    """The oracle (reference semantics, all host threads) decoding the same model
+    from an empty cache: a bounded sample of tokens."""
+    from oracle import lib as O
+    threads = os.cpu_count() or 1
+    t0 = time.perf_counter()
+    m = O.Model(cfg, 1234, 64, threads)
+    build_s = time.perf_counter() - t0
+    n, tok, t0 = 0, 1, time.perf_counter()
+    while n < 3 or (time.perf_counter() - t0 < seconds and n < 60):
+        lg, _ = m.forward([tok], n, 0)
+        tok = O.argmax(lg)
+        n += 1
+    dt = (time.perf_counter() - t0) / n
+    m.close()
+    return {"value": 1.0 / dt, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"{n} greedy decode steps of the same model at positions 0..{n - 1} "
+                      f"(oracle/oracle.c, {threads} threads; weights generated in {build_s:.0f} s); "
+                      f"decode is weight-bound, the 4B KV traffic at the bench positions is 4% of the bytes"}
+
+
+def run_decode(args, rank, world):
+    import torch
+    import arclight_b200 as A
+    from arclight_b200 import bench_util as BU
+    from arclight_b200.configs import QWEN3_4B
+    from arclight_b200.engine import Engine, nccl_unique_id
+
+    cfg = QWEN3_4B
+    L = A.lib()
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    torch.cuda.set_device(local)
+    A.check(L.alb_device_check(local), "device check")
+    nid = None
+    if world > 1:
+        import torch.distributed as dist
+        obj = [nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        nid = obj[0]
+    n_prompt, n_gen = 512, args.steps
+    max_ctx = n_prompt + max(n_gen, args.warmup) + 16
+    e = Engine(cfg, 1234, max_ctx, 256, rank, world, nid, local)
+    prompt = np.random.default_rng(1234).integers(0, cfg["n_vocab"], n_prompt).astype(np.int32)
+    tok0 = e.prefill(prompt, 0)
+    st = torch.cuda.ExternalStream(e.stream())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        # warm-up: W greedy steps from the prompt end (re-run below from the same position)
+        e.decode_loop(tok0, n_prompt, max(args.warmup, 3), want_tokens=False, sync=True)
+        BU.barrier(world)
+        torch.cuda.synchronize()
+        e0.record(st)
+        e.decode_loop(tok0, n_prompt, n_gen, want_tokens=False, sync=False)
+        e1.record(st)
+        e1.synchronize()
+    ms = BU.max_over_ranks(e0.elapsed_time(e1) / n_gen, world)
+    tok_s = 1000.0 / ms
+    info = e.info()   # launches per decode step (the captured graph)
+
+    # e2e through the public C ABI with host buffers: token and position in
+    # (8 B H2D), next token out (4 B D2H), one call per step
+    BU.barrier(world)
+    tok = tok0
+    t_e2e = time.perf_counter()
+    for i in range(n_gen):
+        tok = e.decode(tok, n_prompt + i)
+    e2e_ms = BU.max_over_ranks((time.perf_counter() - t_e2e) * 1000.0 / n_gen, world)
+
+    # dominant kernel (the Q4_0 mat-vec family) timed live: the step's mat-vec
+    # launches replayed from a CUDA graph on the same weights
+    gemv = BU.time_decode_gemvs(e, cfg, world, rank, reps=3)
+
+    peaks = load_peaks()
+    pos_mean = n_prompt + (n_gen - 1) / 2.0
+    bpt = decode_bytes_per_token(cfg, pos_mean)
+    step_gbs = bpt * tok_s / 1e9
+    out = {
+        "metric": "Qwen3-4B Q4_0 decode tok/s bs=1",
+        "value": tok_s, "unit": "tok/s", "n_gpus": world, "steps": n_gen, "warmup": max(args.warmup, 3),
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "q4_0 weights x q8_0 activations (int32 block dots), fp32/fp64 accumulate, fp16 KV",
+        "data": "synthetic: seeded random-init Qwen3-4B-shaped weights (device-generated), uniform random prompt",
+        "config": {"workload": "config3_decode_qwen3_4b", "prompt": n_prompt, "decode_steps": n_gen,
+                   "parallelism": f"tp{world}", "global_batch": 1,
+                   "l2": "inputs larger than L2 (2.26 GB of weights per token)",
+                   "launches_per_token": info["launches_per_step"], "attn_splits": info["attn_splits"]},
+        "roofline": {"bound": "hbm", "achieved": gemv["gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": gemv["gbs"] / peaks["hbm_gbs"], "traffic": None, "peak_src": peaks["src"],
+                     "kernel": "q4_0 x q8_0 mat-vec (all decode-step launches)",
+                     "algorithmic_bytes_per_launch": gemv["bytes_per_launch"], "avg_launch_us": gemv["us_per_launch"]},
+        "step_roofline": {"bytes_per_token": bpt, "achieved_gbs": step_gbs, "peak_gbs": peaks["hbm_gbs"] * world,
+                          "frac": step_gbs / (peaks["hbm_gbs"] * world),
+                          "roofline_tok_s": peaks["hbm_gbs"] * world * 1e9 / bpt},
+        "e2e": {"value": 1000.0 / e2e_ms, "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4},
+        "gpu_launches": info["launches_per_step"] * n_gen,
+        "clocks": clk.summary(),
+    }
+    e.close()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2400)
+    ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="gemv", choices=["gemv"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "gemv"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.steps is None:
+        args.steps = 256 if args.workload == "decode" else 2400
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     if world > 1:
@@ -212,20 +332,36 @@ def main():
 
     if args.impl == "reference":
         if rank == 0:
-            cb = cpu_gemv_baseline(seconds=min(20.0, 2.0 + 0.05 * args.steps))
-            line = {"impl": "reference", "metric": "Q4_0xQ8_0 GEMV HBM GB/s (config 1, W 9728x2560)",
-                    "value": cb["value"], "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-                    "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-                    "dtype": "q4_0 x q8_0", "data": "synthetic", "config": {"workload": "config1_gemv"},
+            if args.workload == "decode":
+                from arclight_b200.configs import QWEN3_4B
+                cb = cpu_decode_baseline(QWEN3_4B, seconds=min(60.0, 5.0 + 0.2 * args.steps))
+                metric, unit, cfgname = "Qwen3-4B Q4_0 decode tok/s bs=1", "tok/s", "config3_decode_qwen3_4b"
+            else:
+                cb = cpu_gemv_baseline(seconds=min(20.0, 2.0 + 0.005 * args.steps))
+                metric, unit, cfgname = "Q4_0xQ8_0 GEMV HBM GB/s (config 1, W 9728x2560)", "GB/s", "config1_gemv"
+            line = {"impl": "reference", "metric": metric, "value": cb["value"], "unit": unit, "n_gpus": world,
+                    "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+                    "scaling": "strong" if args.workload == "decode" else "weak", "vs_baseline": None,
+                    "dtype": "q4_0 x q8_0", "data": "synthetic", "config": {"workload": cfgname},
                     "cpu_baseline": cb,
-                    "e2e": {"value": cb["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+                    "e2e": {"value": cb["value"], "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
             print(json.dumps(line), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
         return
 
-    out = run_gemv(args, rank, world)
+    if args.workload == "decode":
+        out = run_decode(args, rank, world)
+    else:
+        out = run_gemv(args, rank, world)
     if rank == 0:
         if not args.no_cpu_baseline:
-            out["cpu_baseline"] = cpu_gemv_baseline(seconds=10.0)
+            if args.workload == "decode":
+                from arclight_b200.configs import QWEN3_4B
+                out["cpu_baseline"] = cpu_decode_baseline(QWEN3_4B, seconds=20.0)
+            else:
+                out["cpu_baseline"] = cpu_gemv_baseline(seconds=10.0)
         print(json.dumps(out), flush=True)
     if world > 1:
         import torch.distributed as dist

@@ -168,6 +168,12 @@ ALB_API void * alb_engine_stream(alb_engine * e);
 ALB_API int alb_engine_weight_blocks(alb_engine * e, int32_t layer, int32_t kind, void * host, int64_t * rows,
                                      int64_t * cols);
 ALB_API int alb_engine_norm_weights(alb_engine * e, int32_t layer, int32_t kind, float * host, int64_t n);
+/* Measurement hook: one decode step with the persistent kernel's CTA 0
+ * stamping %globaltimer (ns) at each phase boundary; returns the stamp count. */
+ALB_API int alb_engine_decode_trace(alb_engine * e, int32_t token, int32_t pos, int64_t * host, int32_t n);
+/* Measurement hook: mean duration and algorithmic bytes per launch of the
+ * decode step's Q4_0 mat-vecs replayed alone from a CUDA graph. */
+ALB_API int alb_engine_time_gemv(alb_engine * e, int32_t reps, float * us_per_launch, double * bytes_per_launch);
 /* Fill every layer's KV cache for positions [0, n_pos) with seeded N(0,1) fp16. */
 ALB_API int alb_engine_fill_kv(alb_engine * e, int32_t n_pos, uint64_t seed);
 

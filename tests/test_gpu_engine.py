@@ -93,3 +93,27 @@ def test_engine_qwen3_0_6b_config2_greedy_32():
     """Config 2 shape (Qwen3-0.6B, random init): 128-token prompt, 32 greedy steps."""
     err = run_parity(QWEN3_0_6B, seed=1234, n_prompt=128, n_gen=32, max_ub=128)
     assert err < LOGIT_ATOL
+
+
+def test_persistent_decode_kernel_matches_multi_kernel_path(monkeypatch):
+    """The persistent decode-step kernel and the one-kernel-per-op graph give the
+    same greedy tokens and bit-identical logits."""
+    from arclight_b200.engine import Engine
+    cfg = TINY_GQA
+    rng = np.random.default_rng(9)
+    prompt = rng.integers(0, cfg["n_vocab"], 24).astype(np.int32)
+    res = {}
+    for mk in ("1", "0"):
+        monkeypatch.setenv("ALB_DECODE_MK", mk)
+        e = Engine(cfg, 9, 64, 16)
+        assert (e.info()["launches_per_step"] == 0) or True
+        tok = e.prefill(prompt, 0)
+        toks, lgs = [tok], []
+        for i in range(12):
+            toks.append(e.decode(toks[-1], 24 + i))
+            lgs.append(e.logits())
+        res[mk] = (toks, np.stack(lgs), e.info()["launches_per_step"])
+        e.close()
+    assert res["1"][2] == 1 and res["0"][2] > 1
+    assert res["1"][0] == res["0"][0]
+    np.testing.assert_array_equal(res["1"][1], res["0"][1])
