@@ -111,6 +111,16 @@ __device__ __forceinline__ bool alb_mbar_try_wait(uint64_t * bar, uint32_t parit
                  : "=r"(ok) : "r"(alb_smem_addr(bar)), "r"(parity) : "memory");
     return ok != 0;
 }
+// Same, but the thread may be suspended (issuing nothing) until the phase
+// completes or `hint_ns` elapses.
+__device__ __forceinline__ bool alb_mbar_try_wait_sleep(uint64_t * bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(ok) : "r"(alb_smem_addr(bar)), "r"(parity), "r"(hint_ns) : "memory");
+    return ok != 0;
+}
 __device__ __forceinline__ uint64_t alb_globaltimer() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -118,12 +128,14 @@ __device__ __forceinline__ uint64_t alb_globaltimer() {
 }
 // Bounded wait on an mbarrier phase: gives up after `ns` nanoseconds of
 // %globaltimer (default 2 s) and returns false, so no wait can hang the GPU.
+// Waiting threads sleep in the try_wait (at most 20 us per try) instead of
+// spinning, so they take no issue slots from the warps that work.
 __device__ __forceinline__ bool alb_mbar_wait(uint64_t * bar, uint32_t parity, uint64_t ns = 2000000000ull) {
     if (alb_mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = alb_globaltimer();
     for (uint32_t i = 1;; ++i) {
-        if (alb_mbar_try_wait(bar, parity)) return true;
-        if ((i & 255) == 0 && alb_globaltimer() - t0 > ns) return false;
+        if (alb_mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+        if ((i & 15) == 0 && alb_globaltimer() - t0 > ns) return false;
     }
 }
 // 1-D bulk copy global -> shared, completion counted on `bar` (16-byte aligned, size % 16 == 0).

@@ -24,6 +24,7 @@
 // All waits (mbarriers, grid barrier) are bounded by %globaltimer; on timeout
 // the kernel records ALB_DEVERR_* in the error word and returns.
 #include <cfloat>
+#include <cstddef>
 
 #include "alb_q4_dev.cuh"
 #include "alb_mk.h"
@@ -33,30 +34,54 @@ namespace alb {
 static constexpr int MK_CONSUMERS = 15;                 // consumer warps (+1 producer = 16 warps, 128 registers)
 static constexpr int MK_THREADS = (MK_CONSUMERS + 1) * 32;
 static constexpr int MK_NSLOT = 4;
-static constexpr uint32_t MK_SLOT = 45 * 1024;
+static constexpr uint32_t MK_SLOT = 44 * 1024;          // 30 rows of K = 2560
 static constexpr int MK_MAX_NB = 384;                   // K <= 12288
-static constexpr int MK_UNION_FLOATS = 8192;            // xs records | attention scores
 static constexpr int MK_MAX_G = 4;
+static constexpr int MK_SC_PITCH = MK_ATT_MAX_CELLS + 4;
+static constexpr int MK_KV_TILE = 64;                   // cells staged in shared memory per split
+static constexpr int MK_KROW = 136;                     // K tile row pitch (halves): rows on distinct banks
+static constexpr int MK_QROW = 132;                     // q row pitch (floats)
+
+// Attention scratch of one (kv head, split) item: K/V cells [c0, c0 + 64), the
+// layer's QK-norm weights and the RoPE row are bulk-copied in during the QKV
+// phase; scores / probabilities per q head.
+struct MkAttSmem {
+    // scores (fp32, pitch MK_SC_PITCH, in the first half), then the numerators
+    // times 2^1008 (double; see the P.V loop) in place
+    double pd[MK_MAX_G][MK_ATT_MAX_CELLS];
+    alignas(16) uint16_t kt[MK_KV_TILE][MK_KROW];
+    alignas(16) uint16_t vt[MK_KV_TILE][128];
+    alignas(16) float qn[128];
+    alignas(16) float kn[128];
+    alignas(16) float2 rope[64];
+};
 
 struct MkShared {
     alignas(128) uint8_t ring[MK_NSLOT][MK_SLOT];
-    // GEMV phases use xs (Q8_0 activation records); attention phases use sc
-    // (scores / probabilities of this CTA's (kv head, split) item, G x cells)
+    // GEMV phases use xs (Q8_0 activation records, read into registers at the
+    // start of each mat-vec); the attention phase uses a
     union alignas(16) {
         int xs[MK_MAX_NB * XREC_INTS];
-        float sc[MK_UNION_FLOATS];
+        MkAttSmem a;
     } u;
-    float qs[MK_MAX_G][128];                             // fp16-rounded q of this item
+    alignas(16) float qs[MK_MAX_G][MK_QROW];             // fp16-rounded q of this item
     float ktmp[128];                                     // normed + roped k of the new cell
     double red_d[MK_CONSUMERS];
     double part[MK_CONSUMERS][2];
     float red_f[MK_CONSUMERS][MK_MAX_G];
     uint64_t full[MK_NSLOT], empty[MK_NSLOT];
+    uint64_t kvbar;                                      // attention staging copies landed
+    uint64_t stage_ok;                                   // consumers: the staging region is free
     int abort_flag;
     int last;
     unsigned long long am;
 };
-static_assert(MK_MAX_NB * XREC_INTS * 4 <= MK_UNION_FLOATS * 4, "union too small for xs");
+
+// The CTA's shared state, addressed from the extern __shared__ symbol inside
+// every function (so the compiler emits shared-space loads and stores, also in
+// the non-inlined phase functions, instead of generic ones).
+extern __shared__ __align__(128) uint8_t mk_smem[];
+__device__ __forceinline__ MkShared & mk_sh() { return *reinterpret_cast<MkShared *>(mk_smem); }
 
 __device__ __forceinline__ void mk_bar() {   // the 8 consumer warps only
     asm volatile("bar.sync 1, %0;" :: "n"(MK_CONSUMERS * 32) : "memory");
@@ -82,7 +107,9 @@ __device__ __forceinline__ unsigned atom_add_release(unsigned * p, unsigned v) {
 // writes part of the release), the last arrival resets the count and
 // publishes the next generation with a release store, the others poll the
 // generation with acquire loads.
-__device__ bool mk_grid_sync(const MkParams & p, MkShared & sh) {
+__device__ bool mk_grid_sync(const MkParams & p, MkShared & sh_arg) {
+    MkShared & sh = mk_sh();
+    (void)sh_arg;
     mk_bar();
     if (threadIdx.x == 0) {
         const unsigned g = ld_acquire(p.bar_gen);
@@ -123,17 +150,21 @@ struct MkStream {
 // busy as possible) and combined through shared memory.
 struct MkPlan { int R, units, P; };
 
+static constexpr int MK_RECS = 4;                       // activation records per lane (128 blocks per warp)
+
 __device__ __forceinline__ MkPlan mk_plan(int64_t K, int unit) {
     const int64_t rb = K / 2 + q4_scale_pitch(K) * 2;
+    const int nb = (int)(K / 32);
+    const int pmin = (nb + 32 * MK_RECS - 1) / (32 * MK_RECS);
     int fit = (int)((int64_t)MK_SLOT / rb) / unit;      // units that fit a slot
     if (fit > 4 * MK_CONSUMERS) fit = 4 * MK_CONSUMERS;
     MkPlan pl;
-    if (fit >= MK_CONSUMERS) {
+    if (fit >= MK_CONSUMERS && pmin == 1) {
         pl.units = fit / MK_CONSUMERS * MK_CONSUMERS;
         pl.P = 1;
     } else {
-        int best_u = 1, best_w = 1;
-        for (int u = 1; u <= fit; ++u) {
+        int best_u = 1, best_w = 0;
+        for (int u = 1; u <= fit && u * pmin <= MK_CONSUMERS; ++u) {
             const int w = u * (MK_CONSUMERS / u);
             if (w > best_w || (w == best_w && u > best_u)) { best_w = w; best_u = u; }
         }
@@ -203,7 +234,9 @@ __device__ __forceinline__ void mk_prefetch_stage(const MkCursor & c) {
 // One elected thread: bulk copies of every stage into the ring, and L2
 // prefetches of the stages pf_stages ahead, so that HBM keeps streaming
 // through the consumers' prologues, barriers and attention.
-__device__ void mk_producer(const MkParams & p, MkShared & sh) {
+__device__ void mk_producer(const MkParams & p, MkShared & sh_arg) {
+    MkShared & sh = mk_sh();
+    (void)sh_arg;
     const int n_streams = 4 * p.n_layer + 1;
     MkCursor cur, ahead;
     for (int k = 0; k < p.pf_stages && mk_cursor_next(p, ahead, n_streams); ++k) mk_prefetch_stage(ahead);
@@ -231,18 +264,13 @@ __device__ void mk_producer(const MkParams & p, MkShared & sh) {
 // ------------------------------------------------------------ prologues
 // RMSNorm (ops.cpp:680-724) * w then Q8_0 (arm.cpp:1819-1853) of an fp32 vector
 // into the activation records; w == nullptr: quantize only.  Same arithmetic as
-// gemv_prologue_impl (alb_q4.cu).  EMB: the vector is row `token` of the Q4_0
-// token table (GET_ROWS, ops.cpp:12-52), dequantized on the fly.
-template <bool EMB>
-__device__ __forceinline__ float mk_src(const MkParams & p, const float * x, int token, int i) {
-    if constexpr (EMB) {
-        const int b = i >> 5, j = i & 31;
-        const uint8_t byte = p.tok_W[(size_t)token * (p.E / 2) + 16 * b + (j & 15)];
-        const float d = alb_h2f(reinterpret_cast<const uint16_t *>(p.tok_S)[(size_t)token * q4_scale_pitch(p.E) + b]);
-        return (float)((j < 16 ? (byte & 0x0F) : (byte >> 4)) - 8) * d;
-    } else {
-        return x[i];
-    }
+// gemv_prologue_impl (alb_q4.cu).  The embedding (GET_ROWS, ops.cpp:12-52) is
+// row `token` of the Q4_0 token table, dequantized on the fly.
+__device__ __forceinline__ float mk_embed(const MkParams & p, int token, int i) {
+    const int b = i >> 5, j = i & 31;
+    const uint8_t byte = p.tok_W[(size_t)token * (p.E / 2) + 16 * b + (j & 15)];
+    const float d = alb_h2f(reinterpret_cast<const uint16_t *>(p.tok_S)[(size_t)token * q4_scale_pitch(p.E) + b]);
+    return (float)((j < 16 ? (byte & 0x0F) : (byte >> 4)) - 8) * d;
 }
 
 // Four consumer threads per 32-value block (a lane quad; thread part k owns
@@ -252,9 +280,8 @@ __device__ __forceinline__ float mk_src(const MkParams & p, const float * x, int
 // fp16-rounded d as float, sum of the q, d as double).
 static constexpr int MK_QROUNDS = (MK_MAX_NB * 4 + MK_CONSUMERS * 32 - 1) / (MK_CONSUMERS * 32);
 
-template <bool EMB>
 __device__ __forceinline__ void mk_load_quarter(const MkParams & p, const float * x, int token, int q, float * v) {
-    if constexpr (EMB) {
+    if (x == nullptr) {   // row `token` of the Q4_0 token table
         const int b = q >> 2, part = q & 3;
         const uint2 u = *reinterpret_cast<const uint2 *>(p.tok_W + (size_t)token * (p.E / 2) + 16 * b + 8 * (part & 1));
         const float d = alb_h2f(reinterpret_cast<const uint16_t *>(p.tok_S)[(size_t)token * q4_scale_pitch(p.E) + b]);
@@ -272,8 +299,10 @@ __device__ __forceinline__ void mk_load_quarter(const MkParams & p, const float 
     }
 }
 
-template <bool EMB>
-__device__ void mk_quantize(const MkParams & p, const float * x, int token, const float * w, int K, MkShared & sh) {
+// x == nullptr: the vector is row `token` of the token table (the embedding).
+__device__ __noinline__ void mk_quantize(const MkParams & p, const float * x, int token, const float * w, int K, MkShared & sh_arg) {
+    MkShared & sh = mk_sh();
+    (void)sh_arg;
     constexpr int T = MK_CONSUMERS * 32;
     static_assert(T % 32 == 0, "quads stay inside warps");
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -283,7 +312,7 @@ __device__ void mk_quantize(const MkParams & p, const float * x, int token, cons
         double s = 0.0;
         for (int q = tid; q < nq; q += T) {
             float v[8];
-            mk_load_quarter<EMB>(p, x, token, q, v);
+            mk_load_quarter(p, x, token, q, v);
 #pragma unroll
             for (int j = 0; j < 8; ++j) s += (double)__fmul_rn(v[j], v[j]);
         }
@@ -303,7 +332,7 @@ __device__ void mk_quantize(const MkParams & p, const float * x, int token, cons
         float amax = 0.0f;
         float v[8];
         if (mine) {
-            mk_load_quarter<EMB>(p, x, token, q, v);
+            mk_load_quarter(p, x, token, q, v);
             if (w) {
                 const float4 * w4 = reinterpret_cast<const float4 *>(w + (size_t)q * 8);
                 const float4 f0 = w4[0], f1 = w4[1];
@@ -347,20 +376,19 @@ __device__ void mk_quantize(const MkParams & p, const float * x, int token, cons
 // ------------------------------------------------------------ mat-vec phase
 // Consumes this CTA's stages of stream `s`.  OUT: 0 plain y[row], 1 y[row] +=
 // (residual when add_res), 2 SwiGLU pairs y[row/2], 3 logits + argmax key.
-template <int OUT>
-__device__ __forceinline__ void mk_emit(const MkParams & p, float * y, int row, double a0, double a1, bool add_res,
+__device__ __forceinline__ void mk_emit(int OUT, const MkParams & p, float * y, int row, double a0, double a1, bool add_res,
                                         unsigned long long * best) {
-    if constexpr (OUT == 2) {
+    if (OUT == 2) {
         y[row / 2] = alb_swiglu1(__double2float_rn(a0), __double2float_rn(a1));
     } else {
         const float yv = __double2float_rn(a0);
-        if constexpr (OUT == 3) {
+        if (OUT == 3) {
             y[row] = yv;
             uint32_t uu = __float_as_uint(yv);
             uu = (uu & 0x80000000u) ? ~uu : (uu | 0x80000000u);
             const unsigned long long key = ((unsigned long long)uu << 32) | (uint32_t)(0x7FFFFFFF - (row + p.v0));
             *best = key > *best ? key : *best;
-        } else if constexpr (OUT == 1) {
+        } else if (OUT == 1) {
             y[row] = add_res ? __fadd_rn(yv, y[row]) : yv;
         } else {
             y[row] = yv;
@@ -368,16 +396,43 @@ __device__ __forceinline__ void mk_emit(const MkParams & p, float * y, int row, 
     }
 }
 
-// Dot of one row's blocks [b0, b1) (lane-strided) against the activation
-// records; two rows at a time share the record loads.
-template <int OUT>
-__device__ bool mk_gemv(const MkParams & p, MkShared & sh, const MkStream & s, uint32_t & g, float * y,
-                        bool add_res, unsigned long long * best) {
+// Each lane holds the activation records of its blocks in registers for the
+// whole stream (P == 1: blocks lane + 32k; P > 1: the warp's K part
+// [b0, b1), lane-strided).  A pass reduces two rows at once.
+__device__ __forceinline__ void mk_dot(double & a, const uint8_t * nrow, const uint16_t * srow, int b, int4 lo, int4 hi,
+                                       int asum, double dx) {
+    const uint4 w4 = *reinterpret_cast<const uint4 *>(nrow + 16 * b);
+    a = fma(alb_i2d(q4q8_dot(w4, lo, hi, asum)), dx * alb_h2d(srow[b]), a);
+}
+
+// Returns the stage counter after the stream, or -1 on a timeout.  OUT == 3
+// leaves the CTA's best (logit, index) key in sh.am.
+__device__ __noinline__ int64_t mk_gemv(int OUT, const MkParams & p, MkShared & sh_arg, const MkStream s, uint32_t g, float * y,
+                                        bool add_res) {
+    MkShared & sh = mk_sh();
+    (void)sh_arg;
+    unsigned long long best_key = 0ull;
+    unsigned long long * best = &best_key;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const MkPlan pl = mk_plan(s.K, s.unit);
     const int R = pl.R, P = pl.P;
     const int nb = (int)(s.K / 32);
     const int64_t rb = s.K / 2, sp = q4_scale_pitch(s.K);
+    const int part = warp % P, uw = warp / P;
+    const int b0 = nb * part / P, b1 = nb * (part + 1) / P;
+    int4 rlo[MK_RECS], rhi[MK_RECS];
+    int rsum[MK_RECS];
+    double rdx[MK_RECS];
+#pragma unroll
+    for (int k = 0; k < MK_RECS; ++k) {
+        const int b = b0 + lane + 32 * k;
+        const int4 * rec = reinterpret_cast<const int4 *>(sh.u.xs + (b < b1 ? b : b0) * XREC_INTS);
+        rlo[k] = rec[0];
+        rhi[k] = rec[1];
+        const int4 r2 = rec[2];
+        rsum[k] = r2.y;
+        rdx[k] = __hiloint2double(r2.w, r2.z);
+    }
     int r0, r1;
     mk_range(s, r0, r1);
     int64_t * st_tr = (p.trace && blockIdx.x == 0 && threadIdx.x == 0) ? p.trace + 1024 : nullptr;
@@ -387,67 +442,57 @@ __device__ bool mk_gemv(const MkParams & p, MkShared & sh, const MkStream & s, u
         if (!alb_mbar_wait(&sh.full[slot], (g / MK_NSLOT) & 1)) {
             if (lane == 0) atomicExch(p.err, ALB_DEVERR_MBAR_TIMEOUT);
             sh.abort_flag = 1;
-            return false;
+            return -1;
         }
         if (st_tr && 3 * g + 2 < 7168) st_tr[3 * g + 1] = (int64_t)alb_globaltimer();
-        const int n_units = ((r1 - r) < R ? (r1 - r) : R) / s.unit;
+        const int rows = (r1 - r) < R ? (r1 - r) : R;
         const uint8_t * nib = sh.ring[slot];
         const uint16_t * scl = reinterpret_cast<const uint16_t *>(sh.ring[slot] + (size_t)R * rb);
         if (P == 1) {
-            // warp w owns units w, w + W, w + 2W, ...; two per pass
-            for (int u0 = warp; u0 < n_units; u0 += 2 * MK_CONSUMERS) {
-                const int u1 = u0 + MK_CONSUMERS;
-                const bool two = u1 < n_units;
-                double a00 = 0.0, a01 = 0.0, a10 = 0.0, a11 = 0.0;
-                const int ra = u0 * s.unit, rbw = u1 * s.unit;
-                for (int b = lane; b < nb; b += 32) {
-                    const int4 * rec = reinterpret_cast<const int4 *>(sh.u.xs + b * XREC_INTS);
-                    const int4 a_lo = rec[0], a_hi = rec[1], r2 = rec[2];
-                    const double dx = __hiloint2double(r2.w, r2.z);
-                    {
-                        const uint4 w4 = *reinterpret_cast<const uint4 *>(nib + (size_t)ra * rb + 16 * b);
-                        a00 = fma(alb_i2d(q4q8_dot(w4, a_lo, a_hi, r2.y)), dx * alb_h2d(scl[(size_t)ra * sp + b]), a00);
-                    }
-                    if (s.unit == 2) {
-                        const uint4 w4 = *reinterpret_cast<const uint4 *>(nib + (size_t)(ra + 1) * rb + 16 * b);
-                        a01 = fma(alb_i2d(q4q8_dot(w4, a_lo, a_hi, r2.y)), dx * alb_h2d(scl[(size_t)(ra + 1) * sp + b]), a01);
-                    }
-                    if (two) {
-                        const uint4 w4 = *reinterpret_cast<const uint4 *>(nib + (size_t)rbw * rb + 16 * b);
-                        a10 = fma(alb_i2d(q4q8_dot(w4, a_lo, a_hi, r2.y)), dx * alb_h2d(scl[(size_t)rbw * sp + b]), a10);
-                        if (s.unit == 2) {
-                            const uint4 w5 = *reinterpret_cast<const uint4 *>(nib + (size_t)(rbw + 1) * rb + 16 * b);
-                            a11 = fma(alb_i2d(q4q8_dot(w5, a_lo, a_hi, r2.y)), dx * alb_h2d(scl[(size_t)(rbw + 1) * sp + b]), a11);
-                        }
+            // passes over row pairs: (2u, 2u + 1) for the gate/up units u = warp + 15 i,
+            // else rows (warp + 30 i, warp + 30 i + 15)
+            for (int i = 0;; ++i) {
+                int ra, rc;
+                if (s.unit == 2) { ra = 2 * (warp + MK_CONSUMERS * i); rc = ra + 1; }
+                else { ra = warp + 2 * MK_CONSUMERS * i; rc = ra + MK_CONSUMERS; }
+                if (ra >= rows) break;
+                const bool has_c = rc < rows;
+                const uint8_t * na = nib + (size_t)ra * rb, * nc = nib + (size_t)(has_c ? rc : ra) * rb;
+                const uint16_t * sa = scl + (size_t)ra * sp, * sc = scl + (size_t)(has_c ? rc : ra) * sp;
+                double aa = 0.0, ac = 0.0;
+#pragma unroll
+                for (int k = 0; k < MK_RECS; ++k) {
+                    const int b = lane + 32 * k;
+                    if (b < nb) {
+                        mk_dot(aa, na, sa, b, rlo[k], rhi[k], rsum[k], rdx[k]);
+                        if (has_c) mk_dot(ac, nc, sc, b, rlo[k], rhi[k], rsum[k], rdx[k]);
                     }
                 }
-                a00 = alb_warp_sum_d(a00);
-                if (s.unit == 2) a01 = alb_warp_sum_d(a01);
-                if (two) {
-                    a10 = alb_warp_sum_d(a10);
-                    if (s.unit == 2) a11 = alb_warp_sum_d(a11);
-                }
+                aa = alb_warp_sum_d(aa);
+                if (has_c) ac = alb_warp_sum_d(ac);
                 if (lane == 0) {
-                    mk_emit<OUT>(p, y, r + ra, a00, a01, add_res, best);
-                    if (two) mk_emit<OUT>(p, y, r + rbw, a10, a11, add_res, best);
+                    if (s.unit == 2) {
+                        mk_emit(OUT, p, y, r + ra, aa, ac, add_res, best);
+                    } else {
+                        mk_emit(OUT, p, y, r + ra, aa, 0.0, add_res, best);
+                        if (has_c) mk_emit(OUT, p, y, r + rc, ac, 0.0, add_res, best);
+                    }
                 }
             }
         } else {
-            // unit warp / P, block part warp % P
-            const int u = warp / P, part = warp % P;
-            if (u < n_units) {
-                const int b0 = nb * part / P, b1 = nb * (part + 1) / P;
-                const int rl = u * s.unit;
+            // unit uw, K part `part` of the warp; partials combined in shared memory
+            const int n_units = rows / s.unit;
+            if (uw < n_units) {
+                const int rl = uw * s.unit;
+                const uint8_t * na = nib + (size_t)rl * rb;
+                const uint16_t * sa = scl + (size_t)rl * sp;
                 double acc0 = 0.0, acc1 = 0.0;
-                for (int b = b0 + lane; b < b1; b += 32) {
-                    const int4 * rec = reinterpret_cast<const int4 *>(sh.u.xs + b * XREC_INTS);
-                    const int4 a_lo = rec[0], a_hi = rec[1], r2 = rec[2];
-                    const double dx = __hiloint2double(r2.w, r2.z);
-                    const uint4 w4 = *reinterpret_cast<const uint4 *>(nib + (size_t)rl * rb + 16 * b);
-                    acc0 = fma(alb_i2d(q4q8_dot(w4, a_lo, a_hi, r2.y)), dx * alb_h2d(scl[(size_t)rl * sp + b]), acc0);
-                    if (s.unit == 2) {
-                        const uint4 w5 = *reinterpret_cast<const uint4 *>(nib + (size_t)(rl + 1) * rb + 16 * b);
-                        acc1 = fma(alb_i2d(q4q8_dot(w5, a_lo, a_hi, r2.y)), dx * alb_h2d(scl[(size_t)(rl + 1) * sp + b]), acc1);
+#pragma unroll
+                for (int k = 0; k < MK_RECS; ++k) {
+                    const int b = b0 + lane + 32 * k;
+                    if (b < b1) {
+                        mk_dot(acc0, na, sa, b, rlo[k], rhi[k], rsum[k], rdx[k]);
+                        if (s.unit == 2) mk_dot(acc1, na + rb, sa + sp, b, rlo[k], rhi[k], rsum[k], rdx[k]);
                     }
                 }
                 acc0 = alb_warp_sum_d(acc0);
@@ -458,7 +503,7 @@ __device__ bool mk_gemv(const MkParams & p, MkShared & sh, const MkStream & s, u
             if (warp < n_units && lane == 0) {
                 double a0 = 0.0, a1 = 0.0;
                 for (int k = 0; k < P; ++k) { a0 += sh.part[warp * P + k][0]; a1 += sh.part[warp * P + k][1]; }
-                mk_emit<OUT>(p, y, r + warp * s.unit, a0, a1, add_res, best);
+                mk_emit(OUT, p, y, r + warp * s.unit, a0, a1, add_res, best);
             }
             mk_bar();
         }
@@ -466,7 +511,15 @@ __device__ bool mk_gemv(const MkParams & p, MkShared & sh, const MkStream & s, u
         if (lane == 0) alb_mbar_arrive(&sh.empty[slot]);
         if (st_tr && 3 * g + 2 < 7168) st_tr[3 * g + 2] = (int64_t)alb_globaltimer();
     }
-    return true;
+    if (OUT == 3) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long kk = __shfl_xor_sync(0xffffffffu, best_key, o);
+            best_key = kk > best_key ? kk : best_key;
+        }
+        if ((threadIdx.x & 31) == 0) atomicMax(&sh.am, best_key);
+    }
+    return (int64_t)g;
 }
 
 // ------------------------------------------------------------ attention
@@ -502,6 +555,25 @@ __device__ void mk_norm_rope(const float * src, const float * w, float eps, cons
     (void)sh; (void)warp_slot;
 }
 
+
+// Attention of the new token, one (kv head h, cell split s) item per CTA
+// (Hkv * S <= gridDim.x).  Same arithmetic as k_fa_scores / k_fa_pv:
+//   QK-norm + RoPE of the G q heads (and of k, stored with v into the cache by
+//   the split holding the new cell); scores s_c = fp32 fma chain over d in
+//   order, times scale; split max -> the S CTAs of head h wait for one another
+//   (bounded; all CTAs are co-resident under the cooperative launch) -> global
+//   max M; p_c = v_expf(s_c - M); L and O = sum_c p_c V_c in double; the last
+//   split (ticket) adds the S split records in split order and writes att.
+// Cells [c0, c0 + 64) of the split come from shared memory (staged by
+// mk_kv_stage during the QKV phase), the rest of a long split from L2/HBM.
+static_assert(MK_MAX_G * 128 <= 2 * MK_CONSUMERS * 32, "two (g, d) outputs per thread");
+static_assert(offsetof(MkAttSmem, kt) >= MK_STAGE_OFFSET, "staged inputs above the QKV records");
+static_assert(MK_MAX_G * MK_ATT_MAX_CELLS <= 4 * MK_CONSUMERS * 32, "four numerators per thread");
+static_assert(MK_MAX_G * MK_SC_PITCH * 4 <= sizeof(double) * MK_MAX_G * MK_ATT_MAX_CELLS, "scores fit the numerator array");
+// merge scratch of one split: at most G*128/S + 1 outputs and 2 heads' L, each
+// S doubles, i.e. <= (G*128 + 3 S) doubles, inside the numerator array (S <= 160)
+static_assert((MK_MAX_G * 128 + 3 * 160) * 8 <= sizeof(double) * MK_MAX_G * MK_ATT_MAX_CELLS, "merge scratch fits");
+
 __device__ __forceinline__ void mk_split(int n, int S, int s, int & c0, int & c1) {
     const int sz = (n + S - 1) / S;
     c0 = s * sz;
@@ -509,23 +581,56 @@ __device__ __forceinline__ void mk_split(int n, int S, int s, int & c0, int & c1
     if (c0 > n) c0 = n;
 }
 
-// Attention of the new token, one (kv head h, cell split s) item per CTA
-// (Hkv * S <= gridDim.x).  Same arithmetic as k_fa_scores / k_fa_pv:
-//   QK-norm + RoPE of the G q heads (and of k, stored with v into the cache by
-//   the split holding the new cell); scores s_c = fp32 fma chain * scale;
-//   split max -> the S CTAs of head h wait for one another (bounded; all CTAs
-//   are co-resident under the cooperative launch) -> global max M;
-//   p_c = v_expf(s_c - M); L and O = sum_c p_c V_c in double, V staged in
-//   shared memory; the last split (ticket) adds the S split records in split
-//   order and writes att.
-static constexpr int MK_ATT_MAX_CELLS = 512;            // cells per split
-static constexpr int MK_VTILE = 64;                     // V rows per shared tile
-static_assert(MK_MAX_G * MK_ATT_MAX_CELLS + MK_VTILE * 64 <= MK_UNION_FLOATS, "attention scratch too large");
-static_assert(MK_MAX_G * 128 <= 2 * MK_CONSUMERS * 32, "two (g, d) outputs per thread");
+// Lanes 1..31 of the producer warp, attention CTAs only: for every layer, once
+// the consumers signal sh.stage_ok (the union's attention region is free: the
+// previous layer's attention is over), copy the inputs of this CTA's
+// attention that do not depend on the current token -- the cached K/V cells
+// below pos (at most MK_KV_TILE), the layer's q/k norm weights and the RoPE row
+// of pos -- into the union with 16-byte cp.async; each lane's completion
+// arrives on sh.kvbar (expected count 31).  The region lies above the Q8_0
+// records of the QKV phase, which the consumers write meanwhile.
+__device__ void mk_stager(const MkParams & p, MkShared & sh_arg, int pos) {
+    MkShared & sh = mk_sh();
+    (void)sh_arg;
+    const int lane = threadIdx.x & 31;
+    const int h = blockIdx.x / p.S, s = blockIdx.x % p.S;
+    int c0, c1;
+    mk_split(pos + 1, p.S, s, c0, c1);
+    int ce = min(c1, pos);
+    ce = min(ce, c0 + MK_KV_TILE);
+    const int ncp = ce > c0 ? ce - c0 : 0;
+    MkAttSmem & A = sh.u.a;
+    const int64_t row = (int64_t)p.Hkv * 128;
+    const int total = ncp * 32 + 96;                    // 16-byte chunks
+    for (int l = 0; l < p.n_layer; ++l) {
+        if (!alb_mbar_wait(&sh.stage_ok, l & 1) || sh.abort_flag) break;
+        const MkLayer & L = p.layers[l];
+        for (int i = lane - 1; i < total; i += 31) {
+            const void * src;
+            void * dst;
+            if (i < ncp * 32) {
+                const int c = i >> 5, j = i & 15;
+                const bool v = (i >> 4) & 1;
+                src = (v ? L.vc : L.kc) + (size_t)(c0 + c) * row + (size_t)h * 128 + 8 * j;
+                dst = v ? (void *)&A.vt[c][8 * j] : (void *)&A.kt[c][8 * j];
+            } else {
+                const int k = i - ncp * 32, j = k & 31;
+                if (k < 32) { src = L.qn + 4 * j; dst = &A.qn[4 * j]; }
+                else if (k < 64) { src = L.kn + 4 * j; dst = &A.kn[4 * j]; }
+                else { src = reinterpret_cast<const float2 *>(p.rope) + (size_t)pos * 64 + 2 * j; dst = &A.rope[2 * j]; }
+            }
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(alb_smem_addr(dst)), "l"(src) : "memory");
+        }
+        asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" :: "r"(alb_smem_addr(&sh.kvbar)) : "memory");
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");   // no copy in flight when the lane exits
+}
 
 // Barrier of the S CTAs of one kv head (same protocol as mk_grid_sync on the
 // head's own count / generation words).
-__device__ bool mk_group_sync(const MkParams & p, MkShared & sh, unsigned * count, unsigned * gen, unsigned S) {
+__device__ bool mk_group_sync(const MkParams & p, MkShared & sh_arg, unsigned * count, unsigned * gen, unsigned S) {
+    MkShared & sh = mk_sh();
+    (void)sh_arg;
     mk_bar();
     if (threadIdx.x == 0) {
         const unsigned g = ld_acquire(gen);
@@ -548,79 +653,85 @@ __device__ bool mk_group_sync(const MkParams & p, MkShared & sh, unsigned * coun
     return sh.abort_flag == 0;
 }
 
+// fp16 bits -> double bits of (value * 2^-1008) (see alb_h2d)
+__device__ __forceinline__ double mk_vbits(uint32_t v) {
+    return __hiloint2double((int)(((v & 0x7FFFu) << 10) | ((v & 0x8000u) << 16)), 0);
+}
+
+// Called after sh.kvbar completed for this layer.
 template <int G>
-__device__ bool mk_attention(const MkParams & p, MkShared & sh, const MkLayer & L, int pos, int layer) {
+__device__ __noinline__ bool mk_attention(const MkParams & p, MkShared & sh_arg, const MkLayer & L, int pos, int layer) {
+    MkShared & sh = mk_sh();
+    (void)sh_arg;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int item = blockIdx.x;
+    int64_t * ct = (p.trace && tid == 0 && layer < 36 && gridDim.x <= 160)
+                    ? p.trace + 8192 + (size_t)layer * 2 * gridDim.x + 2 * blockIdx.x : nullptr;
+    if (ct) ct[0] = (int64_t)alb_globaltimer();
     if (item >= p.Hkv * p.S) return true;
-    int64_t * ft = (p.trace && item == 0 && tid == 0 && layer < 36) ? p.trace + 640 + 8 * layer : nullptr;
-#define MK_FT(k) do { if (ft) ft[k] = (int64_t)alb_globaltimer(); } while (0)
+    int64_t * ft = (p.trace && tid == 0 && layer < 36 && gridDim.x <= 160)
+                    ? p.trace + 24576 + ((size_t)layer * gridDim.x + blockIdx.x) * 8 : nullptr;
+    int64_t * fc = (p.trace && tid == 0 && item == 0 && layer < 36) ? p.trace + 20000 + layer * 16 : nullptr;
+#define MK_FT(k) do { if (ft) ft[k] = (int64_t)alb_globaltimer(); if (fc) fc[k] = (int64_t)clock64(); } while (0)
+#define MK_FC(k) do { if (fc) fc[k] = (int64_t)clock64(); } while (0)
     MK_FT(0);
+    MkAttSmem & A = sh.u.a;
     const int n = pos + 1;
     const int64_t row = (int64_t)p.Hkv * 128;
     const int h = item / p.S, s = item % p.S;
     int c0, c1;
     mk_split(n, p.S, s, c0, c1);
     const int nc = c1 - c0;
-    const float2 * rp = reinterpret_cast<const float2 *>(p.rope) + (size_t)pos * 64;
-    float * sc = sh.u.sc;                                                            // [G][MK_ATT_MAX_CELLS]
-    uint16_t * vt = reinterpret_cast<uint16_t *>(sh.u.sc + MK_MAX_G * MK_ATT_MAX_CELLS);  // [MK_VTILE][128]
     for (int g = warp; g < G; g += MK_CONSUMERS) {
-        mk_norm_rope(p.qkv + (size_t)(h * G + g) * 128, L.qn, p.eps, rp, sh.qs[g], sh, g);
+        mk_norm_rope(p.qkv + (size_t)(h * G + g) * 128, A.qn, p.eps, A.rope, sh.qs[g], sh, g);
 #pragma unroll
         for (int e = 0; e < 4; ++e) sh.qs[g][4 * lane + e] = __half2float(__float2half_rn(sh.qs[g][4 * lane + e]));
     }
     if (c0 < n && c1 == n && warp == MK_CONSUMERS - 1) {
-        mk_norm_rope(p.qkv + (size_t)(p.Hq + h) * 128, L.kn, p.eps, rp, sh.ktmp, sh, 0);
+        mk_norm_rope(p.qkv + (size_t)(p.Hq + h) * 128, A.kn, p.eps, A.rope, sh.ktmp, sh, 0);
+        const bool in_tile = pos - c0 < MK_KV_TILE;
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             const int d = 4 * lane + e;
-            L.kc[(size_t)pos * row + h * 128 + d] = alb_f2h(sh.ktmp[d]);
-            L.vc[(size_t)pos * row + h * 128 + d] = alb_f2h(p.qkv[(size_t)(p.Hq + p.Hkv + h) * 128 + d]);
+            const uint16_t kh = alb_f2h(sh.ktmp[d]);
+            const uint16_t vh = alb_f2h(p.qkv[(size_t)(p.Hq + p.Hkv + h) * 128 + d]);
+            L.kc[(size_t)pos * row + h * 128 + d] = kh;
+            L.vc[(size_t)pos * row + h * 128 + d] = vh;
+            if (in_tile) { A.kt[pos - c0][d] = kh; A.vt[pos - c0][d] = vh; }
         }
     }
     mk_bar();   // q in smem; the new K/V cell is stored (visible to this CTA)
-    // scores: one thread per cell, K row read as 16 x 16 B
-    float mx[G];
-#pragma unroll
-    for (int g = 0; g < G; ++g) mx[g] = -INFINITY;
-    for (int c = c0 + tid; c < c1; c += MK_CONSUMERS * 32) {
-        const uint4 * kr = reinterpret_cast<const uint4 *>(L.kc + (size_t)c * row + (size_t)h * 128);
-        float a[G];
-#pragma unroll
-        for (int g = 0; g < G; ++g) a[g] = 0.0f;
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-            uint4 kv[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) kv[j] = __ldcg(kr + 8 * half + j);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const uint32_t wd[4] = {kv[j].x, kv[j].y, kv[j].z, kv[j].w};
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float2 kf = __half22float2(*reinterpret_cast<const __half2 *>(&wd[e]));
-                    const int d = 64 * half + 8 * j + 2 * e;
-#pragma unroll
-                    for (int g = 0; g < G; ++g) {
-                        a[g] = __fmaf_rn(kf.x, sh.qs[g][d], a[g]);
-                        a[g] = __fmaf_rn(kf.y, sh.qs[g][d + 1], a[g]);
-                    }
-                }
-            }
+    MK_FT(6);
+    // scores: thread (cell c, head g); fp32 fma chain over d = 0..127 in order
+    float mx = -INFINITY;
+    const int gl = tid % G;                           // G divides 32: fixed per lane
+    for (int i = tid; i < nc * G; i += MK_CONSUMERS * 32) {
+        const int c = c0 + i / G;
+        const uint4 * kr = c - c0 < MK_KV_TILE ? reinterpret_cast<const uint4 *>(A.kt[c - c0])
+                                               : reinterpret_cast<const uint4 *>(L.kc + (size_t)c * row + (size_t)h * 128);
+        const float4 * q4 = reinterpret_cast<const float4 *>(sh.qs[gl]);
+        float a = 0.0f;
+#pragma unroll 4
+        for (int j = 0; j < 16; ++j) {
+            const uint4 kv = kr[j];
+            const float4 qa = q4[2 * j], qb = q4[2 * j + 1];
+            const float2 k0 = __half22float2(*reinterpret_cast<const __half2 *>(&kv.x));
+            const float2 k1 = __half22float2(*reinterpret_cast<const __half2 *>(&kv.y));
+            const float2 k2 = __half22float2(*reinterpret_cast<const __half2 *>(&kv.z));
+            const float2 k3 = __half22float2(*reinterpret_cast<const __half2 *>(&kv.w));
+            a = __fmaf_rn(k0.x, qa.x, a); a = __fmaf_rn(k0.y, qa.y, a);
+            a = __fmaf_rn(k1.x, qa.z, a); a = __fmaf_rn(k1.y, qa.w, a);
+            a = __fmaf_rn(k2.x, qb.x, a); a = __fmaf_rn(k2.y, qb.y, a);
+            a = __fmaf_rn(k3.x, qb.z, a); a = __fmaf_rn(k3.y, qb.w, a);
         }
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-            const float v = __fmul_rn(a[g], p.scale);
-            sc[g * MK_ATT_MAX_CELLS + (c - c0)] = v;
-            mx[g] = fmaxf(mx[g], v);
-        }
+        const float v = __fmul_rn(a, p.scale);
+        reinterpret_cast<float *>(A.pd)[gl * MK_SC_PITCH + (c - c0)] = v;
+        mx = fmaxf(mx, v);
     }
+    // max per head: lanes with equal lane % G hold the same head
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-        const float m = alb_warp_max(mx[g]);
-        if (lane == 0) sh.red_f[warp][g] = m;
-    }
+    for (int o = 16; o >= G; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane < G) sh.red_f[warp][lane] = mx;
     mk_bar();
     if (tid < G) {
         float m = -INFINITY;
@@ -630,90 +741,132 @@ __device__ bool mk_attention(const MkParams & p, MkShared & sh, const MkLayer & 
     MK_FT(1);
     if (!mk_group_sync(p, sh, p.grp + 2 * h, p.grp + 2 * h + 1, (unsigned)p.S)) return false;
     MK_FT(2);
-    if (tid < G) {
+    if (warp == 0) {   // the S*G split maxima, loaded at once; lanes with equal lane % G hold one head
         float m = -INFINITY;
-        for (int k = 0; k < p.S; ++k) m = fmaxf(m, __ldcg(p.smax + ((size_t)h * p.S + k) * G + tid));
-        sh.red_f[0][tid] = m;
+        for (int i = lane; i < p.S * G; i += 32) m = fmaxf(m, __ldcg(p.smax + (size_t)h * p.S * G + i));
+#pragma unroll
+        for (int o = 16; o >= G; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (lane < G) sh.red_f[0][lane] = m;
     }
     mk_bar();
-    for (int i = tid; i < G * nc; i += MK_CONSUMERS * 32) {
-        const int g = i / nc, c = i - g * nc;
-        float & sref = sc[g * MK_ATT_MAX_CELLS + c];
-        sref = alb_ref_expf(__fsub_rn(sref, sh.red_f[0][g]));
-    }
-    MK_FT(3);
-    // P.V: thread (g, d) owns output d of q head g; cells summed in order in double
-    double O[2] = {0.0, 0.0};
-    for (int t0 = 0; t0 < nc; t0 += MK_VTILE) {
-        const int tn = min(MK_VTILE, nc - t0);
-        mk_bar();   // numerators written / previous tile consumed
-        for (int i = tid; i < tn * 16; i += MK_CONSUMERS * 32) {
-            const int c = i >> 4, j = i & 15;
-            reinterpret_cast<uint4 *>(vt)[i] =
-                __ldcg(reinterpret_cast<const uint4 *>(L.vc + (size_t)(c0 + t0 + c) * row + (size_t)h * 128) + j);
-        }
-        mk_bar();
+    MK_FT(7);
+    {
+        float sv[4];
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {
-            const int i = tid + q * MK_CONSUMERS * 32;
-            if (i < G * 128) {
-                const int g = i >> 7, d = i & 127;
-                const float * pg = sc + g * MK_ATT_MAX_CELLS + t0;
-                double o = O[q];
-                for (int c = 0; c < tn; ++c) o = fma((double)pg[c], (double)alb_h2f(vt[c * 128 + d]), o);
-                O[q] = o;
+        for (int k = 0; k < 4; ++k) {
+            const int i = tid + k * MK_CONSUMERS * 32;
+            if (i < G * nc) sv[k] = reinterpret_cast<const float *>(A.pd)[(i / nc) * MK_SC_PITCH + i % nc];
+        }
+        mk_bar();   // every score read before the numerators overwrite them
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int i = tid + k * MK_CONSUMERS * 32;
+            if (i < G * nc) {
+                const int g = i / nc, c = i - g * nc;
+                // p_c * 2^1008: exact, and p * (bits of v as a double) = p * v (alb_h2d)
+                A.pd[g][c] = (double)alb_ref_expf(__fsub_rn(sv[k], sh.red_f[0][g])) * 0x1p1008;
             }
+        }
+    }
+    mk_bar();
+    MK_FT(3);
+    // P.V: thread (g, d) owns output d of q head g (threads below G*128 - 480
+    // own a second one); cells summed in double, four cells' loads at a time
+    {
+        double * rec = p.part + ((size_t)h * p.S + s) * G * 129;
+        const int i0 = tid, i1 = tid + MK_CONSUMERS * 32;
+        const bool two = i1 < G * 128;
+        const int ga = i0 >> 7, da = i0 & 127;
+        const int gb = two ? i1 >> 7 : ga, db = two ? i1 & 127 : da;
+        const double * pa = A.pd[ga], * pb = A.pd[gb];
+        double oa = 0.0, ob = 0.0;
+        const int nt = min(nc, MK_KV_TILE);
+        if (i0 < G * 128) {
+            int c = 0;
+            for (; c + 4 <= nt; c += 4) {
+                uint32_t va[4], vb[4];
+                double wa[4], wb[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    va[k] = A.vt[c + k][da]; wa[k] = pa[c + k];
+                    vb[k] = A.vt[c + k][db]; wb[k] = pb[c + k];
+                }
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    oa = fma(wa[k], mk_vbits(va[k]), oa);
+                    if (two) ob = fma(wb[k], mk_vbits(vb[k]), ob);
+                }
+            }
+            for (; c < nt; ++c) {
+                oa = fma(pa[c], mk_vbits(A.vt[c][da]), oa);
+                if (two) ob = fma(pb[c], mk_vbits(A.vt[c][db]), ob);
+            }
+            for (; c < nc; ++c) {
+                const uint16_t * vr = L.vc + (size_t)(c0 + c) * row + (size_t)h * 128;
+                oa = fma(pa[c], mk_vbits(__ldcg(vr + da)), oa);
+                if (two) ob = fma(pb[c], mk_vbits(__ldcg(vr + db)), ob);
+            }
+            MK_FC(8);
+            __stcg(rec + ga * 129 + da, oa);
+            if (two) __stcg(rec + gb * 129 + db, ob);
+            MK_FC(9);
+        }
+        if (tid >= 32 && tid < 32 + G) {
+            // L of head tid - 32 (these threads own a single output), four partial chains
+            const int g = tid - 32;
+            double l0 = 0.0, l1 = 0.0, l2 = 0.0, l3 = 0.0;
+            int c = 0;
+            for (; c + 4 <= nc; c += 4) { l0 += A.pd[g][c]; l1 += A.pd[g][c + 1]; l2 += A.pd[g][c + 2]; l3 += A.pd[g][c + 3]; }
+            for (; c < nc; ++c) l0 += A.pd[g][c];
+            __stcg(rec + g * 129 + 128, ((l0 + l1) + (l2 + l3)) * 0x1p-1008);
         }
     }
     MK_FT(4);
-    // split record [h][s][G][129] doubles: O[0..127], L
-    double * rec = p.part + ((size_t)h * p.S + s) * G * 129;
-#pragma unroll
-    for (int q = 0; q < 2; ++q) {
-        const int i = tid + q * MK_CONSUMERS * 32;
-        if (i < G * 128) {
-            const int g = i >> 7, d = i & 127;
-            __stcg(rec + g * 129 + d, O[q]);
-            if (d == 0) {
-                double l = 0.0;
-                for (int c = 0; c < nc; ++c) l += (double)sc[g * MK_ATT_MAX_CELLS + c];
-                __stcg(rec + g * 129 + 128, l);
-            }
+    // all S records of head h written -> split s merges outputs [o0, o1) of the
+    // head's G*128, adding the split records in split order (all loads at once)
+    if (!mk_group_sync(p, sh, p.grp + 2 * h, p.grp + 2 * h + 1, (unsigned)p.S)) return false;
+    MK_FC(10);
+    {
+        const int S = p.S;
+        const int o0 = G * 128 * s / S, o1 = G * 128 * (s + 1) / S, no = o1 - o0;
+        const int g0 = o0 >> 7, ng = ((o1 - 1) >> 7) - g0 + 1;
+        double * ov = A.pd[0];                          // [no][S] then [ng][S]
+        double * lv = ov + no * S;
+        const double * hb = p.part + (size_t)h * S * G * 129;
+        for (int i = tid; i < (no + ng) * S; i += MK_CONSUMERS * 32) {
+            const int r = i / S, k = i - r * S;
+            double v;
+            if (r < no) { const int o = o0 + r; v = __ldcg(hb + ((size_t)k * G + (o >> 7)) * 129 + (o & 127)); }
+            else v = __ldcg(hb + ((size_t)k * G + g0 + (r - no)) * 129 + 128);
+            (r < no ? ov[r * S + k] : lv[(r - no) * S + k]) = v;
         }
-    }
-    __threadfence();
-    mk_bar();
-    if (tid == 0) sh.last = (atomicAdd(&p.tickets[h], 1) == p.S - 1);
-    mk_bar();
-    if (sh.last) {
-        __threadfence();
-        const double * hb = p.part + (size_t)h * p.S * G * 129;
-        for (int i = tid; i < G * 128; i += MK_CONSUMERS * 32) {
-            const int g = i >> 7, d = i & 127;
+        mk_bar();
+        MK_FC(11);
+        for (int r = tid; r < no; r += MK_CONSUMERS * 32) {
+            const int o = o0 + r, g = o >> 7;
             double Lt = 0.0, Ot = 0.0;
-            for (int k = 0; k < p.S; ++k) {
-                const double * pk = hb + ((size_t)k * G + g) * 129;
-                Lt += __ldcg(pk + 128);
-                Ot += __ldcg(pk + d);
-            }
-            p.att[(size_t)(h * G + g) * 128 + d] = Lt > 0.0 ? __double2float_rn(Ot / Lt) : 0.0f;
+#pragma unroll 6
+            for (int k = 0; k < S; ++k) { Lt += lv[(g - g0) * S + k]; Ot += ov[r * S + k]; }
+            p.att[(size_t)(h * G + g) * 128 + (o & 127)] = Lt > 0.0 ? __double2float_rn(Ot / Lt) : 0.0f;
         }
-        if (tid == 0) p.tickets[h] = 0;
     }
     MK_FT(5);
 #undef MK_FT
+#undef MK_FC
+    if (ct) ct[1] = (int64_t)alb_globaltimer();
     return true;
 }
 
 // ------------------------------------------------------------ the kernel
 template <int G>
 __global__ void __launch_bounds__(MK_THREADS, 1)
-k_decode_step(const MkParams p) {
-    extern __shared__ __align__(128) uint8_t mk_smem[];
-    MkShared & sh = *reinterpret_cast<MkShared *>(mk_smem);
+k_decode_step(const __grid_constant__ MkParams p) {
+    MkShared & sh = mk_sh();
     const int tid = threadIdx.x, warp = tid >> 5;
     if (tid == 0) {
         for (int i = 0; i < MK_NSLOT; ++i) { alb_mbar_init(&sh.full[i], 1); alb_mbar_init(&sh.empty[i], MK_CONSUMERS); }
+        alb_mbar_init(&sh.kvbar, 31);
+        alb_mbar_init(&sh.stage_ok, 1);
         sh.abort_flag = 0;
         sh.am = 0ull;
         alb_mbar_fence_init();
@@ -721,6 +874,7 @@ k_decode_step(const MkParams p) {
     __syncthreads();
     if (warp == MK_CONSUMERS) {
         if ((tid & 31) == 0) mk_producer(p, sh);
+        else if ((int)blockIdx.x < p.Hkv * p.S) mk_stager(p, sh, p.pos[0]);
         return;
     }
     const int pos = p.pos[0];
@@ -731,23 +885,34 @@ k_decode_step(const MkParams p) {
         const MkStream so = mk_stream(p, 1);
         int r0, r1;
         mk_range(so, r0, r1);
-        for (int i = r0 + tid; i < r1; i += MK_CONSUMERS * 32) p.x[i] = mk_src<true>(p, nullptr, token, i);
+        for (int i = r0 + tid; i < r1; i += MK_CONSUMERS * 32) p.x[i] = mk_embed(p, token, i);
     }
     int64_t * tr = (p.trace && blockIdx.x == 0 && tid == 0) ? p.trace : nullptr;
     int tn = 0;
 #define MK_TRACE() do { if (tr && tn < 1024) tr[tn++] = (int64_t)alb_globaltimer(); } while (0)
     MK_TRACE();
+    const bool att_cta = (int)blockIdx.x < p.Hkv * p.S;
     for (int l = 0; l < p.n_layer && ok; ++l) {
         const MkLayer & L = p.layers[l];
+        // the previous layer's attention is over: its staging region may be refilled
+        if (att_cta && tid == 0) alb_mbar_arrive(&sh.stage_ok);
         // P1: attn norm + QKV
-        if (l == 0) mk_quantize<true>(p, nullptr, token, L.an, p.E, sh);
-        else mk_quantize<false>(p, p.x, 0, L.an, p.E, sh);
+        if (l == 0) mk_quantize(p, nullptr, token, L.an, p.E, sh);
+        else mk_quantize(p, p.x, 0, L.an, p.E, sh);
         MK_TRACE();
-        ok = mk_gemv<0>(p, sh, mk_stream(p, 4 * l + 0), g, p.qkv, false, nullptr);
+        { const int64_t gn = mk_gemv(0, p, sh, mk_stream(p, 4 * l + 0), g, p.qkv, false); ok = gn >= 0; g = (uint32_t)gn; }
         MK_TRACE();
         if (!ok || !mk_grid_sync(p, sh)) { ok = false; break; }
         MK_TRACE();
         // P2+P3: attention of the new token
+        if (att_cta) {
+            if (!alb_mbar_wait(&sh.kvbar, (uint32_t)(l & 1))) {
+                if (tid == 0) atomicExch(p.err, ALB_DEVERR_MBAR_TIMEOUT);
+                sh.abort_flag = 1;
+                ok = false;
+                break;
+            }
+        }
         if (!mk_attention<G>(p, sh, L, pos, l)) { ok = false; break; }
         MK_TRACE();
         MK_TRACE();
@@ -755,42 +920,37 @@ k_decode_step(const MkParams p) {
         if (!mk_grid_sync(p, sh)) { ok = false; break; }
         MK_TRACE();
         // P4: O projection + residual
-        mk_quantize<false>(p, p.att, 0, nullptr, p.Dq, sh);
+        mk_quantize(p, p.att, 0, nullptr, p.Dq, sh);
         MK_TRACE();
-        ok = mk_gemv<1>(p, sh, mk_stream(p, 4 * l + 1), g, p.x, p.rank == 0, nullptr);
+        { const int64_t gn = mk_gemv(1, p, sh, mk_stream(p, 4 * l + 1), g, p.x, p.rank == 0); ok = gn >= 0; g = (uint32_t)gn; }
         MK_TRACE();
         if (!ok || !mk_grid_sync(p, sh)) { ok = false; break; }
         MK_TRACE();
         // P5: ffn norm + gate/up + SwiGLU
-        mk_quantize<false>(p, p.x, 0, L.fn, p.E, sh);
+        mk_quantize(p, p.x, 0, L.fn, p.E, sh);
         MK_TRACE();
-        ok = mk_gemv<2>(p, sh, mk_stream(p, 4 * l + 2), g, p.h, false, nullptr);
+        { const int64_t gn = mk_gemv(2, p, sh, mk_stream(p, 4 * l + 2), g, p.h, false); ok = gn >= 0; g = (uint32_t)gn; }
         MK_TRACE();
         if (!ok || !mk_grid_sync(p, sh)) { ok = false; break; }
         MK_TRACE();
         // P6: down projection + residual
-        mk_quantize<false>(p, p.h, 0, nullptr, p.F, sh);
+        mk_quantize(p, p.h, 0, nullptr, p.F, sh);
         MK_TRACE();
-        ok = mk_gemv<1>(p, sh, mk_stream(p, 4 * l + 3), g, p.x, p.rank == 0, nullptr);
+        { const int64_t gn = mk_gemv(1, p, sh, mk_stream(p, 4 * l + 3), g, p.x, p.rank == 0); ok = gn >= 0; g = (uint32_t)gn; }
         MK_TRACE();
         if (!ok || !mk_grid_sync(p, sh)) { ok = false; break; }
         MK_TRACE();
     }
-    if (!ok) return;
+    if (!ok) {
+        sh.abort_flag = 1;   // the stager lanes stop at their next wait
+        return;
+    }
     // P7: output norm + lm head + argmax
-    mk_quantize<false>(p, p.x, 0, p.out_norm, p.E, sh);
+    mk_quantize(p, p.x, 0, p.out_norm, p.E, sh);
     MK_TRACE();
-    unsigned long long best = 0ull;
-    if (!mk_gemv<3>(p, sh, mk_stream(p, 4 * p.n_layer), g, p.logits, false, &best)) return;
+    if (mk_gemv(3, p, sh, mk_stream(p, 4 * p.n_layer), g, p.logits, false) < 0) return;
     MK_TRACE();
 #undef MK_TRACE
-    // CTA argmax over the warps' candidates
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const unsigned long long k = __shfl_xor_sync(0xffffffffu, best, o);
-        best = k > best ? k : best;
-    }
-    if ((tid & 31) == 0) atomicMax(&sh.am, best);
     mk_bar();
     if (tid == 0) {
         p.cand[blockIdx.x] = sh.am;
@@ -802,7 +962,11 @@ k_decode_step(const MkParams p) {
         __threadfence();
         unsigned long long b = 0ull;
         for (unsigned i = 0; i < gridDim.x; ++i) { const unsigned long long k = __ldcg(p.cand + i); b = k > b ? k : b; }
-        const int32_t nxt = 0x7FFFFFFF - (int32_t)(b & 0xFFFFFFFFu);
+        int32_t nxt = 0x7FFFFFFF - (int32_t)(b & 0xFFFFFFFFu);
+        if (b == 0ull || nxt < 0 || nxt >= p.v0 + p.V) {   // no logit was emitted: never feed an invalid row back
+            atomicExch(p.err, ALB_DEVERR_BAD_TOKEN);
+            nxt = 0;
+        }
         *p.next = nxt;
         if (p.advance) {
             const int32_t st = *p.step;

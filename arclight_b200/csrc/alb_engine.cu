@@ -310,9 +310,12 @@ static int engine_init_mk(alb_engine * e) {
     const int ncta = alb_sm_count();
     const int G = e->Hq / e->Hkv;
     if (G > 4) return ALB_OK;
-    // attention: the cells of each kv head split over S CTAs, <= 512 cells each
-    const int S = ncta / e->Hkv;
-    if (S < 1 || (e->max_ctx + S - 1) / S > 512) return ALB_OK;
+    // attention: the cells of each kv head split over S CTAs, <= MK_ATT_MAX_CELLS each
+    // (ALB_MK_SPLITS lowers S for tuning)
+    int S = ncta / e->Hkv;
+    if (const char * sv = getenv("ALB_MK_SPLITS")) { const int v = atoi(sv); if (v >= 1 && v < S) S = v; }
+    if (S < 1 || (e->max_ctx + S - 1) / S > MK_ATT_MAX_CELLS) return ALB_OK;
+    if ((int64_t)(e->E / 32) * 48 > MK_STAGE_OFFSET) return ALB_OK;
     int dev_sm_optin = 0;
     cudaDeviceGetAttribute(&dev_sm_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, e->dev);
     if ((size_t)dev_sm_optin < mk_smem_bytes()) return ALB_OK;
@@ -574,8 +577,9 @@ extern "C" int alb_engine_decode_trace(alb_engine * e, int32_t token, int32_t po
     if (!e->use_mk) { alb_set_last_error_msg("persistent decode kernel not in use"); return ALB_ERR_UNSUPPORTED; }
     ALB_CUDA_TRY(cudaSetDevice(e->dev));
     int64_t * tr = nullptr;
-    ALB_CUDA_TRY(cudaMalloc(&tr, 8192 * sizeof(int64_t)));
-    cudaMemsetAsync(tr, 0, 8192 * sizeof(int64_t), e->st);
+    constexpr int TN = 24576 + 36 * 8 * 160;   // covers every stamp index below (<= 160 CTAs)
+    ALB_CUDA_TRY(cudaMalloc(&tr, TN * sizeof(int64_t)));
+    cudaMemsetAsync(tr, 0, TN * sizeof(int64_t), e->st);
     e->pinned[0] = token;
     e->pinned[1] = pos;
     cudaMemcpyAsync(e->tok_dev, &e->pinned[0], 4, cudaMemcpyHostToDevice, e->st);
@@ -583,16 +587,18 @@ extern "C" int alb_engine_decode_trace(alb_engine * e, int32_t token, int32_t po
     MkParams p = e->mk;
     p.trace = tr;
     cudaError_t le = launch_decode_step(p, e->st);
-    std::vector<int64_t> h(8192);
-    if (le == cudaSuccess) le = cudaMemcpyAsync(h.data(), tr, 8192 * sizeof(int64_t), cudaMemcpyDeviceToHost, e->st);
+    std::vector<int64_t> h(TN);
+    if (le == cudaSuccess) le = cudaMemcpyAsync(h.data(), tr, TN * sizeof(int64_t), cudaMemcpyDeviceToHost, e->st);
     if (le == cudaSuccess) le = cudaStreamSynchronize(e->st);
     cudaFree(tr);
     ALB_CUDA_TRY(le);
     int m = 0;
     while (m < 1024 && h[m] != 0) ++m;
     // stamps [0, m) are phases; when n > 1024 the per-stage stamps of the
-    // mat-vec phases follow at [1024, 8192): (wait start, data ready, released)
-    const int cp = n < 8192 ? n : 8192;
+    // mat-vec phases follow at [1024, 8192): (wait start, data ready, released),
+    // then per layer and CTA the attention (start, end) at [8192, 8192 + 36 * 2 * ncta),
+    // and per layer and CTA 8 attention sub-phase stamps at [24576, 24576 + 36 * 8 * ncta)
+    const int cp = n < TN ? n : TN;
     memcpy(host, h.data(), (size_t)cp * sizeof(int64_t));
     return m;
 }

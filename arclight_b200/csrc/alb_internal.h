@@ -85,7 +85,7 @@ cudaError_t launch_rms_norm(const float * x, const float * w, float * y, int64_t
 cudaError_t launch_swiglu(const float * g, const float * u, float * y, int64_t n, bool pdl, cudaStream_t st);
 
 // Device-side error word (bounded waits that expire set it; see alb_device_error).
-enum : int { ALB_DEVERR_NONE = 0, ALB_DEVERR_MBAR_TIMEOUT = 1, ALB_DEVERR_FLAG_TIMEOUT = 2 };
+enum : int { ALB_DEVERR_NONE = 0, ALB_DEVERR_MBAR_TIMEOUT = 1, ALB_DEVERR_FLAG_TIMEOUT = 2, ALB_DEVERR_BAD_TOKEN = 3 };
 // Host: the current device's error word (allocated once per device, zeroed).
 int * device_error_ptr();
 

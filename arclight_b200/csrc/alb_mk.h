@@ -11,6 +11,14 @@ struct MkLayer {
     uint16_t * kc, * vc;                                                             // [cells][Hkv][128] fp16
 };
 
+// Most cells one attention split of the persistent kernel handles (its scores
+// live in shared memory); the engine uses the kernel only below this bound.
+constexpr int MK_ATT_MAX_CELLS = 384;
+// Byte offset in the shared union above which the attention inputs are staged
+// while the QKV phase's Q8_0 records (48 bytes per 32 values of n_embd) sit
+// below it: the kernel needs n_embd / 32 * 48 <= MK_STAGE_OFFSET.
+constexpr int MK_STAGE_OFFSET = 4 * MK_ATT_MAX_CELLS * 8;
+
 struct MkParams {
     int n_layer, E, Hq, Hkv, F, V, Nqkv, Dq, v0, rank;
     float eps, scale;

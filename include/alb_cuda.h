@@ -15,7 +15,8 @@
  *   alb Q4_0 GPU layout (what alb_repack_q4_0 writes; replaces block_q4_0x4):
  *       nibble plane  [N][K/2] bytes, block b of row n at n*K/2 + 16*b, the 16
  *                     bytes of block_q4_0.qs unchanged;
- *       scale plane   [N][K/32] fp16 at byte offset alb_q4_0_scale_offset(N, K).
+ *       scale plane   [N][pitch] fp16 at byte offset alb_q4_0_scale_offset(N, K),
+ *                     pitch = K/32 rounded up to a multiple of 8 (16-byte rows).
  *   activations fp32 row-major; KV cache fp16 [cells][n_head_kv][head_dim].
  */
 #ifndef ALB_CUDA_H
@@ -50,8 +51,9 @@ ALB_API const char * alb_last_error(void);
 /* 0 when device `dev` is an sm_100 part this library can run on. */
 ALB_API int          alb_device_check(int dev);
 /* Device-side error word of the current device: 0, or the code of a bounded
- * in-kernel wait that expired (1 = mbarrier, 2 = cross-rank flag).  Kernels
- * never trap; they record the error and return.  clear != 0 resets it. */
+ * in-kernel wait that expired (1 = mbarrier, 2 = cross-CTA / cross-rank flag),
+ * or 3 = a decode step produced no valid next token (token 0 was fed back).
+ * Kernels never trap; they record the error and return.  clear != 0 resets it. */
 ALB_API int          alb_device_error(int clear);
 
 /* ---------------------------------------------------------------- formats */
