@@ -138,6 +138,20 @@ __device__ __forceinline__ bool alb_mbar_wait(uint64_t * bar, uint32_t parity, u
         if ((i & 15) == 0 && alb_globaltimer() - t0 > ns) return false;
     }
 }
+// Bounded wait for a thread with nothing else to do (a producer ahead of its
+// consumers): polls with exponential __nanosleep backoff (32 ns .. 512 ns), so
+// the waiting warp takes almost no issue slots from the warps that compute.
+__device__ __forceinline__ bool alb_mbar_wait_backoff(uint64_t * bar, uint32_t parity, uint64_t ns = 2000000000ull) {
+    if (alb_mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = alb_globaltimer();
+    uint32_t nap = 32;
+    for (;;) {
+        __nanosleep(nap);
+        if (alb_mbar_try_wait(bar, parity)) return true;
+        if (nap < 512) nap <<= 1;
+        if (alb_globaltimer() - t0 > ns) return false;
+    }
+}
 // 1-D bulk copy global -> shared, completion counted on `bar` (16-byte aligned, size % 16 == 0).
 __device__ __forceinline__ void alb_bulk_g2s(void * dst_smem, const void * src, uint32_t bytes, uint64_t * bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"

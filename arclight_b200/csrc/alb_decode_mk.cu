@@ -245,7 +245,7 @@ __device__ void mk_producer(const MkParams & p, MkShared & sh_arg) {
     while (ok && mk_cursor_next(p, cur, n_streams)) {
         const int slot = g % MK_NSLOT;
         if (g >= MK_NSLOT) {
-            if (!alb_mbar_wait(&sh.empty[slot], ((g / MK_NSLOT) - 1) & 1) || sh.abort_flag) { ok = false; break; }
+            if (!alb_mbar_wait_backoff(&sh.empty[slot], ((g / MK_NSLOT) - 1) & 1) || sh.abort_flag) { ok = false; break; }
         }
         const int rows = (cur.r1 - cur.r) < cur.R ? (cur.r1 - cur.r) : cur.R;
         const uint32_t nb = (uint32_t)(rows * cur.rb), sb = (uint32_t)(rows * cur.sp2);
@@ -405,16 +405,98 @@ __device__ __forceinline__ void mk_dot(double & a, const uint8_t * nrow, const u
     a = fma(alb_i2d(q4q8_dot(w4, lo, hi, asum)), dx * alb_h2d(srow[b]), a);
 }
 
+// Half-warp form for K <= 2560 (nb <= 80, no K split): each half-warp takes
+// one row of a pair (gate/up unit, or rows u and u + 15), 16 lanes x 5 blocks
+// of records in registers, a 4-level shuffle reduction per half.
+static constexpr int MK_RECS_H = 5;
+
+__device__ __noinline__ int64_t mk_gemv_h(int OUT, const MkParams & p, const MkStream s, uint32_t g, float * y,
+                                          bool add_res) {
+    MkShared & sh = mk_sh();
+    unsigned long long best_key = 0ull;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, half = lane >> 4, hl = lane & 15;
+    const int R = mk_plan(s.K, s.unit).R;
+    const int nb = (int)(s.K / 32);
+    const int64_t rb = s.K / 2, sp = q4_scale_pitch(s.K);
+    int4 rlo[MK_RECS_H], rhi[MK_RECS_H];
+    int rsum[MK_RECS_H];
+    double rdx[MK_RECS_H];
+#pragma unroll
+    for (int k = 0; k < MK_RECS_H; ++k) {
+        const int b = hl + 16 * k;
+        const int4 * rec = reinterpret_cast<const int4 *>(sh.u.xs + (b < nb ? b : 0) * XREC_INTS);
+        rlo[k] = rec[0];
+        rhi[k] = rec[1];
+        const int4 r2 = rec[2];
+        rsum[k] = r2.y;
+        rdx[k] = __hiloint2double(r2.w, r2.z);
+    }
+    int r0, r1;
+    mk_range(s, r0, r1);
+    int64_t * st_tr = (p.trace && blockIdx.x == 0 && threadIdx.x == 0) ? p.trace + 1024 : nullptr;
+    for (int r = r0; r < r1; r += R, ++g) {
+        const int slot = g % MK_NSLOT;
+        if (st_tr && 3 * g + 2 < 7168) st_tr[3 * g] = (int64_t)alb_globaltimer();
+        if (!alb_mbar_wait(&sh.full[slot], (g / MK_NSLOT) & 1)) {
+            if (lane == 0) atomicExch(p.err, ALB_DEVERR_MBAR_TIMEOUT);
+            sh.abort_flag = 1;
+            return -1;
+        }
+        if (st_tr && 3 * g + 2 < 7168) st_tr[3 * g + 1] = (int64_t)alb_globaltimer();
+        const int rows = (r1 - r) < R ? (r1 - r) : R;
+        const uint8_t * nib = sh.ring[slot];
+        const uint16_t * scl = reinterpret_cast<const uint16_t *>(sh.ring[slot] + (size_t)R * rb);
+        for (int i = 0;; ++i) {
+            int ra, rc;
+            if (s.unit == 2) { ra = 2 * (warp + MK_CONSUMERS * i); rc = ra + 1; }
+            else { ra = warp + 2 * MK_CONSUMERS * i; rc = ra + MK_CONSUMERS; }
+            if (ra >= rows) break;
+            const int row = half ? rc : ra;
+            const bool live = row < rows;
+            const int rr = live ? row : ra;
+            const uint8_t * nr = nib + (size_t)rr * rb;
+            const uint16_t * sr = scl + (size_t)rr * sp;
+            double a = 0.0;
+#pragma unroll
+            for (int k = 0; k < MK_RECS_H; ++k) {
+                const int b = hl + 16 * k;
+                if (b < nb) mk_dot(a, nr, sr, b, rlo[k], rhi[k], rsum[k], rdx[k]);
+            }
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+            if (s.unit == 2) {
+                const double up = __shfl_sync(0xffffffffu, a, 16);
+                if (lane == 0) mk_emit(OUT, p, y, r + ra, a, up, add_res, &best_key);
+            } else if (hl == 0 && live) {
+                mk_emit(OUT, p, y, r + row, a, 0.0, add_res, &best_key);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) alb_mbar_arrive(&sh.empty[slot]);
+        if (st_tr && 3 * g + 2 < 7168) st_tr[3 * g + 2] = (int64_t)alb_globaltimer();
+    }
+    if (OUT == 3) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long kk = __shfl_xor_sync(0xffffffffu, best_key, o);
+            best_key = kk > best_key ? kk : best_key;
+        }
+        if (lane == 0) atomicMax(&sh.am, best_key);
+    }
+    return (int64_t)g;
+}
+
 // Returns the stage counter after the stream, or -1 on a timeout.  OUT == 3
 // leaves the CTA's best (logit, index) key in sh.am.
 __device__ __noinline__ int64_t mk_gemv(int OUT, const MkParams & p, MkShared & sh_arg, const MkStream s, uint32_t g, float * y,
                                         bool add_res) {
     MkShared & sh = mk_sh();
     (void)sh_arg;
+    const MkPlan pl = mk_plan(s.K, s.unit);
+    if (pl.P == 1 && s.K <= 32 * 16 * MK_RECS_H) return mk_gemv_h(OUT, p, s, g, y, add_res);
     unsigned long long best_key = 0ull;
     unsigned long long * best = &best_key;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const MkPlan pl = mk_plan(s.K, s.unit);
     const int R = pl.R, P = pl.P;
     const int nb = (int)(s.K / 32);
     const int64_t rb = s.K / 2, sp = q4_scale_pitch(s.K);
@@ -603,7 +685,7 @@ __device__ void mk_stager(const MkParams & p, MkShared & sh_arg, int pos) {
     const int64_t row = (int64_t)p.Hkv * 128;
     const int total = ncp * 32 + 96;                    // 16-byte chunks
     for (int l = 0; l < p.n_layer; ++l) {
-        if (!alb_mbar_wait(&sh.stage_ok, l & 1) || sh.abort_flag) break;
+        if (!alb_mbar_wait_backoff(&sh.stage_ok, l & 1) || sh.abort_flag) break;
         const MkLayer & L = p.layers[l];
         for (int i = lane - 1; i < total; i += 31) {
             const void * src;

@@ -47,6 +47,17 @@ __global__ void k_advance(int32_t * tok, int32_t * pos, const int32_t * next, in
     *tok = n;
     *pos = *pos + 1;
 }
+// GATHER (ops.cpp:1465-1511, nnml_vec_add_f32 arm.cpp:2435-2451) then ADD of
+// the residual (qwen3.cpp:241,270): x[i] = (((p_0 + p_1) + ...) + p_{n-1}) + x[i],
+// the rank partials added in rank order in fp32, as the reference's nodes.
+__global__ void k_gather_add(float * x, const float * parts, int n_parts, int64_t count) {
+    alb_pdl_wait();
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x) {
+        float acc = parts[i];
+        for (int j = 1; j < n_parts; ++j) acc = __fadd_rn(acc, parts[(int64_t)j * count + i]);
+        x[i] = __fadd_rn(acc, x[i]);
+    }
+}
 }  // namespace alb
 
 using namespace alb;
@@ -69,6 +80,7 @@ struct alb_engine {
     const uint8_t * lm_W = nullptr, * lm_S = nullptr;
     float * out_norm = nullptr, * table = nullptr, * rope = nullptr;
     float * x = nullptr, * qkv = nullptr, * q = nullptr, * att = nullptr, * h = nullptr, * logits = nullptr;
+    float * part = nullptr, * part_all = nullptr;   // TP: this rank's O / down partial, all ranks' partials
     int32_t * tok_dev = nullptr, * pos_dev = nullptr, * next_dev = nullptr, * step_dev = nullptr, * gen_out = nullptr;
     int32_t gen_cap = 0;
     unsigned long long * key = nullptr;
@@ -101,9 +113,16 @@ struct alb_engine {
 
 #define ALB_TRY(expr) do { int r__ = (expr); if (r__ != ALB_OK) return r__; } while (0)
 
-static int engine_allreduce_x(alb_engine * e, int64_t T) {
-    if (e->tp <= 1) return ALB_OK;
-    return nccl_allreduce(e->comm, e->x, e->x, (size_t)T * e->E, 0, 0, e->st);
+// TP: the reference's GATHER of the rank partials (e->part) then the residual
+// ADD, as an all-gather plus an ordered sum (same fp32 additions in the same
+// order on every rank, for any number of ranks).
+static int engine_gather_add_x(alb_engine * e, int64_t T, bool pdl) {
+    const size_t n = (size_t)T * e->E;
+    ALB_TRY(nccl_allgather_f32(e->comm, e->part, e->part_all, n, e->st));
+    const int blocks = (int)((n + 255) / 256 < 1024 ? (n + 255) / 256 : 1024);
+    ALB_CUDA_TRY(alb_launch(k_gather_add, dim3(blocks), dim3(256), 0, e->st, pdl, e->x, (const float *)e->part_all,
+                            e->tp, (int64_t)n));
+    return ALB_OK;
 }
 
 // One ubatch of T tokens (token ids in tok_dev[0..T), first position in pos_dev)
@@ -143,14 +162,20 @@ static int engine_forward(alb_engine * e, int64_t T, bool pdl, int ncap_prefill 
         fa.out = e->att; fa.pdl = pdl;
         ALB_CUDA_TRY(launch_flash_attn(fa, st));
         launches += 2;
-        ALB_CUDA_TRY(gemv(L.o, e->E, e->Dq, GEMV_IN_F32, e->att, nullptr, GEMV_OUT_PLAIN, e->x,
-                          e->rank == 0 ? e->x : nullptr));
-        ALB_TRY(engine_allreduce_x(e, T));
+        if (e->tp == 1) {
+            ALB_CUDA_TRY(gemv(L.o, e->E, e->Dq, GEMV_IN_F32, e->att, nullptr, GEMV_OUT_PLAIN, e->x, e->x));
+        } else {
+            ALB_CUDA_TRY(gemv(L.o, e->E, e->Dq, GEMV_IN_F32, e->att, nullptr, GEMV_OUT_PLAIN, e->part, nullptr));
+            ALB_TRY(engine_gather_add_x(e, T, pdl));
+        }
         ALB_CUDA_TRY(gemv(L.gu, 2 * (int64_t)e->F, e->E, GEMV_IN_F32_RMS, e->x, L.fn, GEMV_OUT_SWIGLU, e->h, nullptr));
-        ALB_CUDA_TRY(gemv(L.down, e->E, e->F, GEMV_IN_F32, e->h, nullptr, GEMV_OUT_PLAIN, e->x,
-                          e->rank == 0 ? e->x : nullptr));
-        ALB_TRY(engine_allreduce_x(e, T));
-        if (e->tp > 1) launches += 2;
+        if (e->tp == 1) {
+            ALB_CUDA_TRY(gemv(L.down, e->E, e->F, GEMV_IN_F32, e->h, nullptr, GEMV_OUT_PLAIN, e->x, e->x));
+        } else {
+            ALB_CUDA_TRY(gemv(L.down, e->E, e->F, GEMV_IN_F32, e->h, nullptr, GEMV_OUT_PLAIN, e->part, nullptr));
+            ALB_TRY(engine_gather_add_x(e, T, pdl));
+            launches += 4;
+        }
     }
     // final norm + lm_head on the last token (qwen3.cpp:235-238, 266-274)
     {
@@ -274,6 +299,10 @@ static int engine_init_acts(alb_engine * e) {
     ALB_TRY(e->alloc(&e->q, U * e->Dq));
     ALB_TRY(e->alloc(&e->att, U * e->Dq));
     ALB_TRY(e->alloc(&e->h, U * e->F));
+    if (e->tp > 1) {
+        ALB_TRY(e->alloc(&e->part, U * e->E));
+        ALB_TRY(e->alloc(&e->part_all, (int64_t)e->tp * U * e->E));
+    }
     ALB_TRY(e->alloc(&e->logits, (size_t)e->V));
     ALB_TRY(e->alloc(&e->tok_dev, (size_t)U));
     ALB_TRY(e->alloc(&e->pos_dev, 1));

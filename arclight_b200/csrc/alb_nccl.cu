@@ -16,6 +16,7 @@ struct NcclApi {
     ncclResult_t (*GetUniqueId)(ncclUniqueId *) = nullptr;
     ncclResult_t (*CommInitRank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
     ncclResult_t (*AllReduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*AllGather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
     ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
     ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
     ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t *) = nullptr;
@@ -34,12 +35,13 @@ static NcclApi & api() {
         ALB_SYM(GetUniqueId, "ncclGetUniqueId");
         ALB_SYM(CommInitRank, "ncclCommInitRank");
         ALB_SYM(AllReduce, "ncclAllReduce");
+        ALB_SYM(AllGather, "ncclAllGather");
         ALB_SYM(CommDestroy, "ncclCommDestroy");
         ALB_SYM(CommAbort, "ncclCommAbort");
         ALB_SYM(CommGetAsyncError, "ncclCommGetAsyncError");
         ALB_SYM(GetErrorString, "ncclGetErrorString");
 #undef ALB_SYM
-        a.ok = a.GetUniqueId && a.CommInitRank && a.AllReduce && a.CommDestroy && a.CommAbort && a.GetErrorString;
+        a.ok = a.GetUniqueId && a.CommInitRank && a.AllReduce && a.AllGather && a.CommDestroy && a.CommAbort && a.GetErrorString;
     });
     return a;
 }
@@ -69,6 +71,12 @@ int nccl_init(void ** comm, int rank, int size, const void * id128) {
     const ncclResult_t r = api().CommInitRank(&c, size, id, rank);
     if (r != ncclSuccess) return nccl_fail(r, "ncclCommInitRank");
     *comm = c;
+    return ALB_OK;
+}
+
+int nccl_allgather_f32(void * comm, const float * src, float * dst, size_t count, cudaStream_t st) {
+    const ncclResult_t r = api().AllGather(src, dst, count, ncclFloat32, static_cast<ncclComm_t>(comm), st);
+    if (r != ncclSuccess) return nccl_fail(r, "ncclAllGather");
     return ALB_OK;
 }
 

@@ -143,10 +143,12 @@ def run_gemv(args, rank, world):
         torch.cuda.synchronize()
         BU.barrier(world)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.nvtx.range_push("timed")   # lets ncu --nvtx-include timed/ list exactly these launches
         e0.record(s)
         for _ in range(reps):
             g.replay()
         e1.record(s)
+        torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / steps
     ms = BU.max_over_ranks(ms, world)
@@ -261,9 +263,11 @@ def run_decode(args, rank, world):
         e.decode_loop(tok0, n_prompt, max(args.warmup, 3), want_tokens=False, sync=True)
         BU.barrier(world)
         torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("timed")   # lets ncu --nvtx-include timed/ list exactly these launches
         e0.record(st)
         e.decode_loop(tok0, n_prompt, n_gen, want_tokens=False, sync=False)
         e1.record(st)
+        torch.cuda.nvtx.range_pop()
         e1.synchronize()
     ms = BU.max_over_ranks(e0.elapsed_time(e1) / n_gen, world)
     tok_s = 1000.0 / ms

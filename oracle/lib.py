@@ -75,6 +75,8 @@ def lib() -> C.CDLL:
             "orc_gemv_q4_0_q8_0_exact": (None, [vp, vp, vp, i64, i64, C.c_int]),
             "orc_neon_expf": (f32, [f32]),
             "orc_model_set_exact": (None, [vp, C.c_int]),
+            "orc_model_set_tp": (None, [vp, C.c_int]),
+            "orc_gemv_q4_0_q8_0_exact_tp": (None, [vp, vp, vp, C.c_int64, C.c_int64, C.c_int, C.c_int]),
             "orc_vec_dot_q4_0_q8_0": (f32, [vp, vp, i64]),
             "orc_mul_mat_generic": (None, [vp, vp, vp, i64, i64, C.c_int]),
             "orc_rms_norm": (None, [vp, vp, vp, i64, i64, f32]),
@@ -265,6 +267,11 @@ class Model:
     def set_exact(self, exact: bool):
         """True (default): exactly rounded mat-vecs; False: the reference's NEON fp32 chains."""
         lib().orc_model_set_exact(self.h, 1 if exact else 0)
+
+    def set_tp(self, tp: int):
+        """tp > 1: O and down projections as tp node partials added in node order
+        (the reference's tensor-parallel GATHER), exact mat-vecs."""
+        lib().orc_model_set_tp(self.h, int(tp))
 
 
 def argmax(x: np.ndarray) -> int:

@@ -270,6 +270,37 @@ void orc_gemv_q4_0_q8_0_exact(const orc_block_q4_0 * W, const orc_block_q8_0 * x
     orc_parallel_for(n_threads, N, gemv_range, &c);
 }
 
+/* Tensor-parallel form of the exact mat-vec for the O / down projections
+ * (model.cpp:21-54 split their input columns over the nodes): node j's partial
+ * is the exactly rounded sum over its column slice of K/tp (32-aligned) and the
+ * partials are added in node order in fp32, as GATHER does
+ * (ops.cpp:1465-1511, nnml_vec_add_f32 arm.cpp:2435-2451). */
+typedef struct { const orc_block_q4_0 * W; const orc_block_q8_0 * xq; float * y; int64_t nb; int tp; } gemv_tp_ctx;
+static void gemv_tp_range(void * p, int64_t n0, int64_t n1) {
+    const gemv_tp_ctx * c = (const gemv_tp_ctx *)p;
+    const int64_t nbs = c->nb / c->tp;
+    for (int64_t n = n0; n < n1; ++n) {
+        const orc_block_q4_0 * w = c->W + n * c->nb;
+        float acc = 0.0f;
+        for (int j = 0; j < c->tp; ++j) {
+            double accd = 0.0;
+            for (int64_t b = j * nbs; b < (j + 1) * nbs; ++b) {
+                const int32_t I = block_dot_q4_0_q8_0(&w[b], &c->xq[b]);
+                const float s = orc_fp16_to_fp32(c->xq[b].d) * orc_fp16_to_fp32(w[b].d);
+                accd += (double)I * (double)s;
+            }
+            acc = j == 0 ? (float)accd : acc + (float)accd;
+        }
+        c->y[n] = acc;
+    }
+}
+
+void orc_gemv_q4_0_q8_0_exact_tp(const orc_block_q4_0 * W, const orc_block_q8_0 * xq, float * y,
+                                 int64_t N, int64_t K, int tp, int n_threads) {
+    gemv_tp_ctx c = { W, xq, y, K / ORC_QK, tp > 0 ? tp : 1 };
+    orc_parallel_for(n_threads, N, gemv_tp_range, &c);
+}
+
 /* nnml_vec_dot_q4_0_q8_0 NEON path (arm.cpp:633-692): blocks in pairs, two
  * float32x4 accumulators; lane i of vdotq_s32 sums elements 4i..4i+3 of the
  * low half and of the high half; vmlaq_n_f32 is contracted to fmla under
@@ -525,6 +556,7 @@ struct orc_model {
     float * table;
     uint64_t seed;
     int exact;   /* 1: exactly rounded mat-vecs (default); 0: NEON fp32 chains */
+    int tp;      /* > 1: O / down as tp column-slice partials added in node order */
 };
 
 typedef struct { const float * table; uint64_t seed; int64_t K; orc_block_q4_0 * dst; } gen_ctx;
@@ -559,6 +591,7 @@ orc_model * orc_model_create(const orc_qwen3_config * cfg, uint64_t seed, int32_
     m->n_threads = n_threads > 0 ? n_threads : 1;
     m->seed = seed;
     m->exact = 1;
+    m->tp = 1;
     m->table = (float *)malloc(65537 * sizeof(float));
     orc_normal_table(m->table);
     const orc_qwen3_config * c = &m->c;
@@ -657,6 +690,17 @@ static void matmul_rows(orc_model * m, const orc_block_q4_0 * W, const float * x
 }
 
 void orc_model_set_exact(orc_model * m, int exact) { m->exact = exact; }
+void orc_model_set_tp(orc_model * m, int tp) { m->tp = tp > 0 ? tp : 1; }
+
+/* O / down projections: tp > 1 forms the node partials (exact mode only). */
+static void matmul_rows_cols_split(orc_model * m, const orc_block_q4_0 * W, const float * x, float * y,
+                                   int64_t T, int64_t N, int64_t K, orc_block_q8_0 * qbuf) {
+    if (m->tp <= 1 || !m->exact) { matmul_rows(m, W, x, y, T, N, K, qbuf); return; }
+    for (int64_t t = 0; t < T; ++t) {
+        orc_quantize_row_q8_0(x + t * K, qbuf, K);
+        orc_gemv_q4_0_q8_0_exact_tp(W, qbuf, y + t * N, N, K, m->tp, m->n_threads);
+    }
+}
 
 int orc_model_forward(orc_model * m, const int32_t * tokens, int32_t T, int32_t pos0,
                       int fa_mode, float * logits, float * hidden) {
@@ -702,7 +746,7 @@ int orc_model_forward(orc_model * m, const int32_t * tokens, int32_t T, int32_t 
             }
         }
         orc_flash_attn(q, L->kc, L->vc, kv_len, Tcur, c->n_head, c->n_head_kv, HD, 1.0f / sqrtf((float)HD), fa_mode, att);
-        matmul_rows(m, L->wo, att, o, Tcur, E, Dq, qb);
+        matmul_rows_cols_split(m, L->wo, att, o, Tcur, E, Dq, qb);
         if (l == c->n_layer - 1 && Tcur > 1) { /* keep the last row only (qwen3.cpp:235-238) */
             memmove(o, o + (Tcur - 1) * E, E * 4);
             memmove(x, x + (Tcur - 1) * E, E * 4);
@@ -713,7 +757,7 @@ int orc_model_forward(orc_model * m, const int32_t * tokens, int32_t T, int32_t 
         matmul_rows(m, L->wgate, h, g, Tcur, c->n_ff, E, qb);
         matmul_rows(m, L->wup, h, u, Tcur, c->n_ff, E, qb);
         orc_swiglu(g, u, g, Tcur * c->n_ff);
-        matmul_rows(m, L->wdown, g, o, Tcur, E, c->n_ff, qb);
+        matmul_rows_cols_split(m, L->wdown, g, o, Tcur, E, c->n_ff, qb);
         for (int64_t i = 0; i < Tcur * E; ++i) x[i] = o[i] + x[i];
     }
     if (rc == 0) {

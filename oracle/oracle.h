@@ -64,6 +64,11 @@ void orc_gemv_q4_0_q8_0(const orc_block_q4_0 * W, const orc_block_q8_0 * xq, flo
  * (order independent; within a few fp32 ulps of the NEON chain). */
 void orc_gemv_q4_0_q8_0_exact(const orc_block_q4_0 * W, const orc_block_q8_0 * xq, float * y,
                               int64_t N, int64_t K, int n_threads);
+/* Tensor-parallel twin for column-split matrices (O, down; model.cpp:21-54): node
+ * j's exactly rounded partial over its K/tp column slice, partials added in node
+ * order in fp32 (GATHER, ops.cpp:1465-1511). */
+void orc_gemv_q4_0_q8_0_exact_tp(const orc_block_q4_0 * W, const orc_block_q8_0 * xq, float * y,
+                                 int64_t N, int64_t K, int tp, int n_threads);
 /* nnml_vec_dot_q4_0_q8_0 NEON path (arm.cpp:633-692): generic mul_mat (lm_head). */
 float orc_vec_dot_q4_0_q8_0(const orc_block_q4_0 * x, const orc_block_q8_0 * y, int64_t k);
 void  orc_mul_mat_generic(const orc_block_q4_0 * W, const orc_block_q8_0 * xq, float * y,
@@ -125,6 +130,9 @@ void orc_model_reset(orc_model * m);
  * head); 0: the reference's NEON fp32 chains (gemv for projections,
  * nnml_vec_dot_q4_0_q8_0 lanes for the lm head). */
 void orc_model_set_exact(orc_model * m, int exact);
+/* tp > 1: the O and down projections as tp node partials added in node order,
+ * then the residual (qwen3.cpp:232-241,262-270 with is_tp); exact mode only. */
+void orc_model_set_tp(orc_model * m, int tp);
 /* greedy argmax (sampler.cpp:34-36: std::max_element => first maximum) */
 int32_t orc_argmax(const float * x, int64_t n);
 
