@@ -17,6 +17,8 @@ LIB_PATH = os.path.join(PKG, "libalb_cuda.so")
 HEADER = os.path.join(ROOT, "include", "alb_cuda.h")
 
 ALB_OK = 0
+ALB_ERR_INVALID = -1
+ALB_FLASH_ATTN_STATIC_BYTES = 4 << 20   # include/alb_cuda.h
 _lib = None
 
 
@@ -70,6 +72,7 @@ def _declare(L: C.CDLL) -> None:
         "alb_qk_norm_rope_kv": (ci, [vp, i64, i32, i32, vp, vp, f32, vp, i32, vp, vp, vp, vp]),
         "alb_flash_attn_workspace_bytes": (sz, [i32, i32, i64, i32, i32]),
         "alb_flash_attn": (ci, [vp, vp, vp, i64, i32, i32, i32, f32, i32, vp, vp, vp]),
+        "alb_flash_attn_static": (ci, [vp, vp, vp, i64, i32, i32, i32, f32, i32, vp, vp]),
         "alb_argmax": (ci, [vp, i64, vp, vp, vp]),
         "alb_nccl_unique_id": (ci, [vp]),
         "alb_engine_create": (ci, [vp, C.c_uint64, i32, i32, i32, i32, vp, i32, vp]),

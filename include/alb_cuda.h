@@ -118,6 +118,20 @@ ALB_API int alb_flash_attn(const float * q, const uint16_t * k_cache, const uint
                            int32_t n_head, int32_t n_head_kv, int32_t pos0, float scale, int32_t splits,
                            void * workspace, float * out, void * stream);
 
+/* Size of the fixed device workspace of alb_flash_attn_static (one per device). */
+#define ALB_FLASH_ATTN_STATIC_BYTES (4u << 20)
+/* alb_flash_attn without a caller workspace and without allocating: the
+ * workspace is a file-scope device array of ALB_FLASH_ATTN_STATIC_BYTES per
+ * device (calls whose alb_flash_attn_workspace_bytes exceeds it return
+ * ALB_ERR_INVALID).  Calls on one device share that array and must not
+ * overlap in time.  The first call on a device looks the array up and clears
+ * it (cudaGetSymbolAddress, cudaMemsetAsync on `stream`); make it outside any
+ * stream capture.  Same results as alb_flash_attn.  No counterpart in the
+ * reference (its ops take scratch from params->work_data, thread.h:166-167). */
+ALB_API int alb_flash_attn_static(const float * q, const uint16_t * k_cache, const uint16_t * v_cache, int64_t T,
+                                  int32_t n_head, int32_t n_head_kv, int32_t pos0, float scale, int32_t splits,
+                                  float * out, void * stream);
+
 /* -------------------------------------------------------------- sampling */
 /* sample_none (sampler.cpp:34-36): first index of the maximum of x[0..n).
  * scratch >= 1024 bytes, zeroed once before first use. */
