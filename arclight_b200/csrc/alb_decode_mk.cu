@@ -410,6 +410,86 @@ __device__ __forceinline__ void mk_dot(double & a, const uint8_t * nrow, const u
 // of records in registers, a 4-level shuffle reduction per half.
 static constexpr int MK_RECS_H = 5;
 
+// KB = blocks per lane = nb / 16 exactly (no per-block predicates); the record
+// scale is held pre-multiplied by 2^1008 so the weight scale enters as bits.
+template <int KB>
+__device__ __noinline__ int64_t mk_gemv_hk(int OUT, const MkParams & p, const MkStream s, uint32_t g, float * y,
+                                           bool add_res) {
+    MkShared & sh = mk_sh();
+    unsigned long long best_key = 0ull;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, half = lane >> 4, hl = lane & 15;
+    const int R = mk_plan(s.K, s.unit).R;
+    constexpr int nb = 16 * KB;
+    const int64_t rb = s.K / 2, sp = q4_scale_pitch(s.K);
+    int4 rlo[KB], rhi[KB];
+    int rsum[KB];
+    double rdx[KB];
+#pragma unroll
+    for (int k = 0; k < KB; ++k) {
+        const int4 * rec = reinterpret_cast<const int4 *>(sh.u.xs + (hl + 16 * k) * XREC_INTS);
+        rlo[k] = rec[0];
+        rhi[k] = rec[1];
+        const int4 r2 = rec[2];
+        rsum[k] = r2.y;
+        rdx[k] = __hiloint2double(r2.w, r2.z) * 0x1p1008;   // finite: d <= 65504 < 2^16
+    }
+    int r0, r1;
+    mk_range(s, r0, r1);
+    int64_t * st_tr = (p.trace && blockIdx.x == 0 && threadIdx.x == 0) ? p.trace + 1024 : nullptr;
+    for (int r = r0; r < r1; r += R, ++g) {
+        const int slot = g % MK_NSLOT;
+        if (st_tr && 3 * g + 2 < 7168) st_tr[3 * g] = (int64_t)alb_globaltimer();
+        if (!alb_mbar_wait(&sh.full[slot], (g / MK_NSLOT) & 1)) {
+            if (lane == 0) atomicExch(p.err, ALB_DEVERR_MBAR_TIMEOUT);
+            sh.abort_flag = 1;
+            return -1;
+        }
+        if (st_tr && 3 * g + 2 < 7168) st_tr[3 * g + 1] = (int64_t)alb_globaltimer();
+        const int rows = (r1 - r) < R ? (r1 - r) : R;
+        const uint8_t * nib = sh.ring[slot];
+        const uint16_t * scl = reinterpret_cast<const uint16_t *>(sh.ring[slot] + (size_t)R * rb);
+        for (int i = 0;; ++i) {
+            int ra, rc;
+            if (s.unit == 2) { ra = 2 * (warp + MK_CONSUMERS * i); rc = ra + 1; }
+            else { ra = warp + 2 * MK_CONSUMERS * i; rc = ra + MK_CONSUMERS; }
+            if (ra >= rows) break;
+            const int row = half ? rc : ra;
+            const bool live = row < rows;
+            const int rr = live ? row : ra;
+            const uint4 * nr = reinterpret_cast<const uint4 *>(nib + (size_t)rr * rb) + hl;
+            const uint16_t * sr = scl + (size_t)rr * sp + hl;
+            uint4 w[KB];
+            uint32_t hs[KB];
+#pragma unroll
+            for (int k = 0; k < KB; ++k) { w[k] = nr[16 * k]; hs[k] = sr[16 * k]; }
+            double a = 0.0;
+#pragma unroll
+            for (int k = 0; k < KB; ++k)
+                a = fma(alb_i2d(q4q8_dot_fast(w[k], rlo[k], rhi[k], rsum[k])), rdx[k] * alb_h2d_bits(hs[k]), a);
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+            if (s.unit == 2) {
+                const double up = __shfl_sync(0xffffffffu, a, 16);
+                if (lane == 0) mk_emit(OUT, p, y, r + ra, a, up, add_res, &best_key);
+            } else if (hl == 0 && live) {
+                mk_emit(OUT, p, y, r + row, a, 0.0, add_res, &best_key);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) alb_mbar_arrive(&sh.empty[slot]);
+        if (st_tr && 3 * g + 2 < 7168) st_tr[3 * g + 2] = (int64_t)alb_globaltimer();
+    }
+    if (OUT == 3) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long kk = __shfl_xor_sync(0xffffffffu, best_key, o);
+            best_key = kk > best_key ? kk : best_key;
+        }
+        if (lane == 0) atomicMax(&sh.am, best_key);
+    }
+    return (int64_t)g;
+}
+
 __device__ __noinline__ int64_t mk_gemv_h(int OUT, const MkParams & p, const MkStream s, uint32_t g, float * y,
                                           bool add_res) {
     MkShared & sh = mk_sh();
@@ -493,7 +573,15 @@ __device__ __noinline__ int64_t mk_gemv(int OUT, const MkParams & p, MkShared & 
     MkShared & sh = mk_sh();
     (void)sh_arg;
     const MkPlan pl = mk_plan(s.K, s.unit);
-    if (pl.P == 1 && s.K <= 32 * 16 * MK_RECS_H) return mk_gemv_h(OUT, p, s, g, y, add_res);
+    if (pl.P == 1) {
+        switch (s.K) {
+            case 32 * 16 * 5: return mk_gemv_hk<5>(OUT, p, s, g, y, add_res);
+            case 32 * 16 * 4: return mk_gemv_hk<4>(OUT, p, s, g, y, add_res);
+            case 32 * 16 * 2: return mk_gemv_hk<2>(OUT, p, s, g, y, add_res);
+            default: break;
+        }
+        if (s.K <= 32 * 16 * MK_RECS_H) return mk_gemv_h(OUT, p, s, g, y, add_res);
+    }
     unsigned long long best_key = 0ull;
     unsigned long long * best = &best_key;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;

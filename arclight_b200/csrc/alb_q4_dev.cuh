@@ -37,6 +37,26 @@ __device__ __forceinline__ int q4q8_dot(uint4 w, const int4 a_lo, const int4 a_h
     return s - 8 * asum;
 }
 
+// Same dot with fewer integer operations: the high nibbles enter dp4a in place
+// (bytes 16*hi, as unsigned) and the sum is divided by 16 once; exact.
+__device__ __forceinline__ int q4q8_dot_fast(uint4 w, const int4 a_lo, const int4 a_hi, int asum) {
+    int s = 0, t = 0;
+    asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(s) : "r"(w.x & 0x0F0F0F0Fu), "r"(a_lo.x));
+    asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(s) : "r"(w.y & 0x0F0F0F0Fu), "r"(a_lo.y));
+    asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(s) : "r"(w.z & 0x0F0F0F0Fu), "r"(a_lo.z));
+    asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(s) : "r"(w.w & 0x0F0F0F0Fu), "r"(a_lo.w));
+    asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(t) : "r"(w.x & 0xF0F0F0F0u), "r"(a_hi.x));
+    asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(t) : "r"(w.y & 0xF0F0F0F0u), "r"(a_hi.y));
+    asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(t) : "r"(w.z & 0xF0F0F0F0u), "r"(a_hi.z));
+    asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(t) : "r"(w.w & 0xF0F0F0F0u), "r"(a_hi.w));
+    return s + (t >> 4) - 8 * asum;   // t is 16 * (sum of hi * a): exact division
+}
+// fp16 bits -> the bits of (value * 2^-1008) as a double (see alb_h2d), without
+// the final scaling; pairs with an operand pre-scaled by 2^1008.
+__device__ __forceinline__ double alb_h2d_bits(uint32_t h) {
+    return __hiloint2double((int)(((h & 0x7FFFu) << 10) | ((h & 0x8000u) << 16)), 0);
+}
+
 // Exact conversions onto the fp64 pipe (no conversion instruction).
 // fp16 bits -> double for every finite half: the half's exponent and mantissa
 // bits placed at the top of a double's (value * 2^-1008, a subnormal double
