@@ -72,6 +72,9 @@ def _declare(L: C.CDLL) -> None:
         "alb_qk_norm_rope_kv": (ci, [vp, i64, i32, i32, vp, vp, f32, vp, i32, vp, vp, vp, vp]),
         "alb_flash_attn_workspace_bytes": (sz, [i32, i32, i64, i32, i32]),
         "alb_flash_attn": (ci, [vp, vp, vp, i64, i32, i32, i32, f32, i32, vp, vp, vp]),
+        "alb_gemm_workspace_bytes": (C.c_size_t, [i64, i64]),
+        "alb_gemm_q4_0_q8_0": (ci, [vp, vp, vp, i64, i64, i64, vp, vp, vp]),
+        "alb_engine_time_prefill_gemm": (ci, [vp, i32, C.POINTER(C.c_float), C.POINTER(C.c_double)]),
         "alb_flash_attn_static": (ci, [vp, vp, vp, i64, i32, i32, i32, f32, i32, vp, vp]),
         "alb_argmax": (ci, [vp, i64, vp, vp, vp]),
         "alb_nccl_unique_id": (ci, [vp]),

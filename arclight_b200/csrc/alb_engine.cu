@@ -81,6 +81,8 @@ struct alb_engine {
     float * out_norm = nullptr, * table = nullptr, * rope = nullptr;
     float * x = nullptr, * qkv = nullptr, * q = nullptr, * att = nullptr, * h = nullptr, * logits = nullptr;
     float * part = nullptr, * part_all = nullptr;   // TP: this rank's O / down partial, all ranks' partials
+    float * xn = nullptr;                           // prefill: RMS-normalized rows
+    void * pg_ws = nullptr;                         // prefill: quantized activations of the mat-mul
     int32_t * tok_dev = nullptr, * pos_dev = nullptr, * next_dev = nullptr, * step_dev = nullptr, * gen_out = nullptr;
     int32_t gen_cap = 0;
     unsigned long long * key = nullptr;
@@ -142,9 +144,17 @@ static int engine_forward(alb_engine * e, int64_t T, bool pdl, int ncap_prefill 
         a.out_mode = out; a.y = y; a.residual = res; a.pdl = pdl;
         ++launches;
         if (T == 1) return launch_gemv(a, st);
-        a.x_stride = K; a.y_stride = out == GEMV_OUT_SWIGLU ? N / 2 : N;
-        launches += (int)((T + 7) / 8) - 1;
-        return launch_gemv_tokens(a, T, st);
+        // prefill: RMSNorm rows (when asked), then the tensor-core mat-mul
+        const float * xin = static_cast<const float *>(x);
+        if (in == GEMV_IN_F32_RMS) {
+            const cudaError_t re = launch_rms_norm(xin, nw, e->xn, T, K, c.eps, pdl, st);
+            if (re != cudaSuccess) return re;
+            xin = e->xn;
+            ++launches;
+        }
+        ++launches;   // activation quantizer
+        return launch_prefill_gemm(W, N, K, xin, nullptr, T, y, out == GEMV_OUT_SWIGLU ? N / 2 : N, res,
+                                   out == GEMV_OUT_SWIGLU, e->pg_ws, device_error_ptr(), pdl, st);
     };
     const int S = T == 1 ? e->fa_S_decode : 1;
     for (int l = 0; l < c.n_layer; ++l) {
@@ -299,6 +309,14 @@ static int engine_init_acts(alb_engine * e) {
     ALB_TRY(e->alloc(&e->q, U * e->Dq));
     ALB_TRY(e->alloc(&e->att, U * e->Dq));
     ALB_TRY(e->alloc(&e->h, U * e->F));
+    if (U > 1) {
+        ALB_TRY(e->alloc(&e->xn, U * e->E));
+        int64_t kmax = e->E > e->Dq ? e->E : e->Dq;
+        if (e->F > kmax) kmax = e->F;
+        uint8_t * w = nullptr;
+        ALB_TRY(e->alloc(&w, prefill_ws_bytes(U, kmax)));
+        e->pg_ws = w;
+    }
     if (e->tp > 1) {
         ALB_TRY(e->alloc(&e->part, U * e->E));
         ALB_TRY(e->alloc(&e->part_all, (int64_t)e->tp * U * e->E));
@@ -636,6 +654,60 @@ extern "C" int alb_engine_decode_trace(alb_engine * e, int32_t token, int32_t po
 // step order, PDL chained) from a CUDA graph replayed `reps` times.  Reports
 // the mean duration per launch and the mean algorithmic bytes per launch
 // (weights 18 B / 32 values + fp32 input + fp32 output).
+// Times the prefill mat-muls of one ubatch of T = max_ubatch tokens alone (every
+// layer's QKV, O, gate/up, down on the tensor cores, each with its activation
+// quantizer), replayed `reps` times from a CUDA graph; reports the mean time per
+// mat-mul launch and its int8 operations (2 * T * N * K).
+extern "C" int alb_engine_time_prefill_gemm(alb_engine * e, int32_t reps, float * us_per_launch, double * ops_per_launch) {
+    ALB_CHECK_ARG(e && reps > 0 && us_per_launch && ops_per_launch && e->max_ub > 1 && e->pg_ws);
+    ALB_CUDA_TRY(cudaSetDevice(e->dev));
+    const int64_t T = e->max_ub;
+    struct G { const uint8_t * W; int64_t N, K; const float * x; float * y; bool swiglu; };
+    std::vector<G> list;
+    double ops = 0.0;
+    for (int l = 0; l < e->c.n_layer; ++l) {
+        alb_engine::Layer & L = e->layers[l];
+        list.push_back({L.qkv, e->Nqkv, e->E, e->xn, e->qkv, false});
+        list.push_back({L.o, e->E, e->Dq, e->att, e->qkv, false});
+        list.push_back({L.gu, 2 * (int64_t)e->F, e->E, e->xn, e->h, true});
+        list.push_back({L.down, e->E, e->F, e->h, e->qkv, false});
+    }
+    for (const G & g : list) ops += 2.0 * (double)T * (double)g.N * (double)g.K;
+    ALB_CUDA_TRY(cudaMemsetAsync(e->xn, 0, (size_t)T * e->E * 4, e->st));
+    ALB_CUDA_TRY(cudaMemsetAsync(e->att, 0, (size_t)T * e->Dq * 4, e->st));
+    ALB_CUDA_TRY(cudaMemsetAsync(e->h, 0, (size_t)T * e->F * 4, e->st));
+    cudaGraph_t g = nullptr;
+    cudaGraphExec_t ge = nullptr;
+    ALB_CUDA_TRY(cudaStreamBeginCapture(e->st, cudaStreamCaptureModeThreadLocal));
+    cudaError_t le = cudaSuccess;
+    for (const G & a : list)
+        if (le == cudaSuccess)
+            le = launch_prefill_gemm(a.W, a.N, a.K, a.x, nullptr, T, a.y, a.swiglu ? a.N / 2 : a.N, nullptr, a.swiglu,
+                                     e->pg_ws, device_error_ptr(), true, e->st);
+    const cudaError_t ce = cudaStreamEndCapture(e->st, &g);
+    ALB_CUDA_TRY(le);
+    ALB_CUDA_TRY(ce);
+    ALB_CUDA_TRY(cudaGraphInstantiate(&ge, g, 0));
+    cudaEvent_t a0, a1;
+    cudaEventCreate(&a0);
+    cudaEventCreate(&a1);
+    cudaGraphLaunch(ge, e->st);
+    cudaEventRecord(a0, e->st);
+    for (int i = 0; i < reps; ++i) cudaGraphLaunch(ge, e->st);
+    cudaEventRecord(a1, e->st);
+    cudaError_t se = cudaEventSynchronize(a1);
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, a0, a1);
+    cudaEventDestroy(a0);
+    cudaEventDestroy(a1);
+    cudaGraphExecDestroy(ge);
+    cudaGraphDestroy(g);
+    ALB_CUDA_TRY(se);
+    *us_per_launch = ms * 1000.0f / (float)(reps * list.size());
+    *ops_per_launch = ops / (double)list.size();
+    return ALB_OK;
+}
+
 extern "C" int alb_engine_time_gemv(alb_engine * e, int32_t reps, float * us_per_launch, double * bytes_per_launch) {
     ALB_CHECK_ARG(e && reps > 0 && us_per_launch && bytes_per_launch);
     ALB_CUDA_TRY(cudaSetDevice(e->dev));

@@ -39,8 +39,6 @@ struct GemvArgs {
     int variant = 0;               // 0/1 = direct loads + L2 prefetch (default), 2 = bulk-copy pipeline
     int stage_budget = 0;          // bytes of shared-memory stages (0 = default)
     int * err = nullptr;           // device error word (filled by launch_gemv)
-    int64_t x_stride = 0;          // token-batched form: floats between token rows of x
-    int64_t y_stride = 0;          //                     floats between token rows of y / residual
 };
 
 struct FlashArgs {
@@ -90,8 +88,13 @@ enum : int { ALB_DEVERR_NONE = 0, ALB_DEVERR_MBAR_TIMEOUT = 1, ALB_DEVERR_FLAG_T
 int * device_error_ptr();
 
 cudaError_t launch_gemv(const GemvArgs & a, cudaStream_t stream);
-// prefill ubatch of T tokens (fp32 inputs only), launched in chunks of 8 tokens
-cudaError_t launch_gemv_tokens(const GemvArgs & a, int64_t T, cudaStream_t stream);
+// prefill mat-mul on the tensor cores: x fp32 [M][K] (or, x == nullptr, block_q8_0
+// rows xq_blocks) times W [N][K] -> y [M][y_stride] (SwiGLU: y [M][N/2]);
+// workspace prefill_ws_bytes(M, K)
+size_t prefill_ws_bytes(int64_t M, int64_t K);
+cudaError_t launch_prefill_gemm(const uint8_t * W, int64_t N, int64_t K, const float * x, const void * xq_blocks,
+                                int64_t M, float * y, int64_t y_stride, const float * residual, bool swiglu, void * ws,
+                                int * err, bool pdl, cudaStream_t st);
 
 // alb Q4_0 GPU layout: nibble plane [N][K/2] bytes, then (256-aligned) the fp16
 // scale plane [N][q4_scale_pitch(K)] (row pitch padded to 16 bytes so that every

@@ -388,11 +388,12 @@ static cudaError_t launch_fa_t(const FlashArgs & f, cudaStream_t st) {
     const int n_max = f.ncap;   // cells attended by the last token at most
     if (f.S == 1 && (size_t)G * n_max * 4 <= FA_FUSED_SMEM) {
         const size_t smem = (size_t)G * n_max * 4;
-        static size_t attr = 0;
-        if (smem > 48 * 1024 && smem > attr) {
-            cudaError_t e = cudaFuncSetAttribute(k_fa_fused<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        static bool attr = false;   // the kernel's static shared memory counts against the 48 KiB default too
+        if (!attr) {
+            cudaError_t e = cudaFuncSetAttribute(k_fa_fused<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)FA_FUSED_SMEM);
             if (e != cudaSuccess) return e;
-            attr = smem;
+            attr = true;
         }
         return alb_launch(k_fa_fused<G>, dim3((unsigned)f.Hkv, (unsigned)f.T), dim3(128), smem, st, f.pdl, f.q, f.kc,
                           f.vc, f.Hq, f.Hkv, f.T, f.pos0, f.pos_dev, f.scale, f.out);

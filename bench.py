@@ -1,7 +1,7 @@
 #!/usr/bin/env python3
 """ArcLight B200 hot-path benchmark (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode|gemv] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode|gemv|prefill] [--impl ours|reference]
 
 Workloads:
   decode  config 3 (default): Qwen3-4B-shaped Q4_0 model, random init, 512-token
@@ -9,6 +9,9 @@ Workloads:
           (one CUDA-graph replay).  N > 1: tensor parallel over N GPUs (NCCL).
   gemv    config 1: one Q4_0 x Q8_0 mat-vec, W [9728 x 2560]; a step is one
           launch over one of 24 distinct weight copies (336 MB > 126 MB L2).
+  prefill config 4: the same model prefilling a 2048-token prompt from an empty
+          cache; a step is one prompt (time to first token); the mat-muls run on
+          the int8 tensor cores.
 Metric / value / roofline: value is whole-job tok/s with inputs resident; e2e goes through the C ABI with host buffers; roofline.achieved = algorithmic bytes per launch / CUDA-event launch time.
 """
 from __future__ import annotations
@@ -233,6 +236,22 @@ def cpu_decode_baseline(cfg, seconds=20.0):
                       f"decode is weight-bound, the 4B KV traffic at the bench positions is 4% of the bytes"}
 
 
+def cpu_prefill_baseline(cfg, n_tokens=48):
+    """The oracle (reference semantics, all host threads) prefilling a bounded
+    prompt of the same model from an empty cache: prompt tokens per second."""
+    from oracle import lib as O
+    threads = os.cpu_count() or 1
+    m = O.Model(cfg, 1234, n_tokens + 8, threads)
+    prompt = np.random.default_rng(4).integers(0, cfg["n_vocab"], n_tokens).astype(np.int32)
+    t0 = time.perf_counter()
+    m.forward(prompt, 0)
+    dt = time.perf_counter() - t0
+    m.close()
+    return {"value": n_tokens / dt, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"one {n_tokens}-token prompt prefilled from an empty cache (oracle/oracle.c, {threads} threads; "
+                      f"its mat-muls run row by row, as the reference's gemv path)"}
+
+
 def run_decode(args, rank, world):
     import torch
     import arclight_b200 as A
@@ -327,18 +346,95 @@ def run_decode(args, rank, world):
     return out
 
 
+# ----------------------------------------------------------------- prefill (config 4)
+PREFILL_T = 2048
+INT8_PEAK_TOPS = 4500.0   # nominal dense int8 (no measured int8 peak in MEASURED_PEAKS.json)
+
+
+def run_prefill(args, rank, world):
+    import torch
+    import arclight_b200 as A
+    from arclight_b200 import bench_util as BU
+    from arclight_b200.configs import QWEN3_4B
+    from arclight_b200.engine import Engine, nccl_unique_id
+    import ctypes as C
+
+    cfg = QWEN3_4B
+    L = A.lib()
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    torch.cuda.set_device(local)
+    A.check(L.alb_device_check(local), "device check")
+    nid = None
+    if world > 1:
+        import torch.distributed as dist
+        obj = [nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        nid = obj[0]
+    T = PREFILL_T
+    e = Engine(cfg, 1234, T + 16, T, rank, world, nid, local)
+    prompt = np.random.default_rng(4).integers(0, cfg["n_vocab"], T).astype(np.int32)
+    st = torch.cuda.ExternalStream(e.stream())
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(local) as clk:
+        for _ in range(args.warmup):
+            A.check(L.alb_engine_reset(e.h))
+            e.prefill(prompt, 0)
+        info = e.info()                      # launches of one prefill ubatch
+        BU.barrier(world)
+        torch.cuda.synchronize()
+        walls = []
+        torch.cuda.nvtx.range_push("timed")
+        for k in range(args.steps):
+            A.check(L.alb_engine_reset(e.h))  # empty cache before every prompt (not timed)
+            t0 = time.perf_counter()
+            ev[k][0].record(st)
+            e.prefill(prompt, 0)                # host tokens in, greedy next token out
+            ev[k][1].record(st)
+            walls.append(time.perf_counter() - t0)
+        torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize()
+    ms = BU.max_over_ranks(sum(a.elapsed_time(b) for a, b in ev) / args.steps, world)
+    wall_ms = BU.max_over_ranks(1000.0 * sum(walls) / len(walls), world)
+    us = C.c_float()
+    ops = C.c_double()
+    A.check(L.alb_engine_time_prefill_gemm(e.h, 3, C.byref(us), C.byref(ops)), "time_prefill_gemm")
+    tops = ops.value / (us.value * 1e-6) / 1e12
+    total_ops = 2.0 * T * (cfg["n_layer"] * ((cfg["n_head"] + 2 * cfg["n_head_kv"]) * 128 * cfg["n_embd"]
+                                             + cfg["n_head"] * 128 * cfg["n_embd"] + 3 * cfg["n_embd"] * cfg["n_ff"]))
+    out = {
+        "metric": "Qwen3-4B Q4_0 prefill tok/s (2048-token prompt, 1/TTFT)",
+        "value": T * 1000.0 / ms, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "ttft_ms": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "q4_0 x q8_0 int8 tensor cores (tcgen05 kind::i8), exact fp64 block sums, fp16 KV",
+        "data": "synthetic: seeded random-init Qwen3-4B-shaped weights, uniform random prompt",
+        "config": {"workload": "config4_prefill_qwen3_4b", "prompt": T, "parallelism": f"tp{world}",
+                   "global_batch": 1, "l2": "inputs larger than L2 (2.26 GB of weights per prefill)",
+                   "launches_per_prefill": info["launches_per_step"]},
+        "roofline": {"bound": "tensor", "achieved": tops, "peak": INT8_PEAK_TOPS, "unit": "TOP/s",
+                     "frac": tops / INT8_PEAK_TOPS, "traffic": None, "peak_src": "nominal dense int8 (B200)",
+                     "kernel": "k_prefill_gemm (tcgen05 kind::i8, TMEM accumulators; + its activation quantizer)",
+                     "algorithmic_ops_per_launch": ops.value, "avg_launch_us": us.value},
+        "prefill_int8_ops": total_ops,
+        "e2e": {"value": T * 1000.0 / wall_ms, "unit": "tok/s", "h2d_bytes_per_step": 4 * T, "d2h_bytes_per_step": 4},
+        "gpu_launches": info["launches_per_step"] * args.steps,
+        "clocks": clk.summary(),
+    }
+    e.close()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "gemv"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "gemv", "prefill"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.steps is None:
-        args.steps = 256 if args.workload == "decode" else 2400
+        args.steps = {"decode": 256, "gemv": 2400, "prefill": 5}[args.workload]
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     if world > 1:
@@ -352,12 +448,17 @@ def main():
                 from arclight_b200.configs import QWEN3_4B
                 cb = cpu_decode_baseline(QWEN3_4B, seconds=min(60.0, 5.0 + 0.2 * args.steps))
                 metric, unit, cfgname = "Qwen3-4B Q4_0 decode tok/s bs=1", "tok/s", "config3_decode_qwen3_4b"
+            elif args.workload == "prefill":
+                from arclight_b200.configs import QWEN3_4B
+                cb = cpu_prefill_baseline(QWEN3_4B)
+                metric, unit = "Qwen3-4B Q4_0 prefill tok/s (2048-token prompt, 1/TTFT)", "tok/s"
+                cfgname = "config4_prefill_qwen3_4b"
             else:
                 cb = cpu_gemv_baseline(seconds=min(20.0, 2.0 + 0.005 * args.steps))
                 metric, unit, cfgname = "Q4_0xQ8_0 GEMV HBM GB/s (config 1, W 9728x2560)", "GB/s", "config1_gemv"
             line = {"impl": "reference", "metric": metric, "value": cb["value"], "unit": unit, "n_gpus": world,
                     "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
-                    "scaling": "strong" if args.workload == "decode" else "weak", "vs_baseline": None,
+                    "scaling": "weak" if args.workload == "gemv" else "strong", "vs_baseline": None,
                     "dtype": "q4_0 x q8_0", "data": "synthetic", "config": {"workload": cfgname},
                     "cpu_baseline": cb,
                     "e2e": {"value": cb["value"], "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -369,6 +470,8 @@ def main():
 
     if args.workload == "decode":
         out = run_decode(args, rank, world)
+    elif args.workload == "prefill":
+        out = run_prefill(args, rank, world)
     else:
         out = run_gemv(args, rank, world)
     if rank == 0:
@@ -376,6 +479,9 @@ def main():
             if args.workload == "decode":
                 from arclight_b200.configs import QWEN3_4B
                 out["cpu_baseline"] = cpu_decode_baseline(QWEN3_4B, seconds=20.0)
+            elif args.workload == "prefill":
+                from arclight_b200.configs import QWEN3_4B
+                out["cpu_baseline"] = cpu_prefill_baseline(QWEN3_4B)
             else:
                 out["cpu_baseline"] = cpu_gemv_baseline(seconds=10.0)
         print(json.dumps(out), flush=True)

@@ -78,6 +78,15 @@ ALB_API int alb_quantize_q8_0(const float * x, void * xq, int64_t K, int64_t row
  * W in the alb GPU layout, xq block_q8_0 [K/32]. */
 ALB_API int alb_gemv_q4_0_q8_0(const void * W, const void * xq, float * y, int64_t N, int64_t K,
                        const float * residual, void * stream);
+/* ------------------------------------------------------------------- GEMM */
+/* nnml_gemm_q4_0_4x4_q8_0 (gemm.cpp:495-974) driven by forward_mul_mat
+ * (arm.cpp:1855-1925), ne11 = M > 1 (prefill): y[m][n] = sum_b I(m,n,b) * f32(dw) *
+ * f32(dx) (+ residual[m][n] when non-null), exact block terms summed in double;
+ * on tcgen05 int8 tensor cores.  W in the alb GPU layout [N][K], xq block_q8_0
+ * [M][K/32], y / residual [M][N].  workspace: alb_gemm_workspace_bytes(M, K). */
+ALB_API size_t alb_gemm_workspace_bytes(int64_t M, int64_t K);
+ALB_API int alb_gemm_q4_0_q8_0(const void * W, const void * xq, float * y, int64_t M, int64_t N, int64_t K,
+                               const float * residual, void * workspace, void * stream);
 /* Debug twin of alb_gemv_q4_0_q8_0 writing the int32 block dots I[N][K/32]. */
 ALB_API int alb_gemv_q4_0_q8_0_block_dots(const void * W, const void * xq, int32_t * I, int64_t N, int64_t K,
                                   void * stream);
@@ -190,6 +199,9 @@ ALB_API int alb_engine_decode_trace(alb_engine * e, int32_t token, int32_t pos, 
 /* Measurement hook: mean duration and algorithmic bytes per launch of the
  * decode step's Q4_0 mat-vecs replayed alone from a CUDA graph. */
 ALB_API int alb_engine_time_gemv(alb_engine * e, int32_t reps, float * us_per_launch, double * bytes_per_launch);
+/* Measurement hook: mean duration and int8 operations per launch of the prefill
+ * mat-muls of one max_ubatch-token ubatch (all layers) replayed alone from a CUDA graph. */
+ALB_API int alb_engine_time_prefill_gemm(alb_engine * e, int32_t reps, float * us_per_launch, double * ops_per_launch);
 /* Fill every layer's KV cache for positions [0, n_pos) with seeded N(0,1) fp16. */
 ALB_API int alb_engine_fill_kv(alb_engine * e, int32_t n_pos, uint64_t seed);
 
