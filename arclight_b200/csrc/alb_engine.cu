@@ -332,8 +332,8 @@ static int engine_init_acts(alb_engine * e) {
     uint8_t * scr = nullptr;
     ALB_TRY(e->alloc(&scr, 1024));
     e->am_scratch = scr;
-    // decode split-K: ~4 CTAs per SM over the local KV heads
-    int S = (4 * alb_sm_count() + e->Hkv - 1) / e->Hkv;
+    // decode split-K: 2 CTAs per SM (the split kernels' staging ring allows two) over the local KV heads
+    int S = (2 * alb_sm_count() + e->Hkv - 1) / e->Hkv;
     if (S > 1024) S = 1024;
     e->fa_S_decode = S;
     e->fa_ws_bytes = flash_attn_ws_bytes(e->Hq, e->Hkv, 1, S, e->max_ctx);
@@ -435,6 +435,9 @@ extern "C" int alb_engine_create(const alb_qwen3_config * cfg, uint64_t seed, in
     const int rc0 = alb_device_check(device);
     if (rc0 != ALB_OK) return rc0;
     ALB_CUDA_TRY(cudaSetDevice(device));
+    // The per-device error word is created by a synchronous allocation on first
+    // use; that first use must not fall inside the decode-graph capture.
+    if (!device_error_ptr()) { alb_set_last_error_msg("device error word: allocation failed"); return ALB_ERR_CUDA; }
     alb_engine * e = new alb_engine();
     e->c = *cfg; e->seed = seed; e->max_ctx = max_ctx; e->max_ub = max_ubatch;
     e->rank = tp_rank; e->tp = tp_size; e->dev = device;

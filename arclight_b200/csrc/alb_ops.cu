@@ -5,6 +5,7 @@
 
 #include "alb_common.cuh"
 #include "alb_internal.h"
+#include "alb_q4_dev.cuh"
 
 namespace alb {
 
@@ -138,102 +139,234 @@ __device__ __forceinline__ void fa_split(int n, int S, int s, int & c0, int & c1
     if (c0 > n) c0 = n;
 }
 
+// Split kernels stream K and V through a shared-memory ring filled by
+// cp.async (FA_NST stages of FA_CH cells, FA_NST - 1 stages in flight), so each
+// CTA keeps tens of KB of HBM reads outstanding while it computes; one cell per
+// thread per stage.  K rows are padded to 272 B in shared memory so the 16-byte
+// row reads of a quarter-warp fall in distinct banks.
+static constexpr int FA_CH = 128;                          // cells per stage (one per thread)
+static constexpr int FA_NST = 3;                           // ring stages
+static constexpr int FA_KPITCH = 272;                      // bytes per staged K row
+static constexpr int FA_KSTAGE = FA_CH * FA_KPITCH;        // 34,816 B
+static constexpr int FA_VSTAGE = FA_CH * 256;              // 32,768 B
+static constexpr size_t FA_SCORES_SMEM = (size_t)FA_NST * FA_KSTAGE;
+template <int G>
+constexpr size_t fa_pv_smem() { return (size_t)FA_NST * (FA_VSTAGE + G * FA_CH * 4); }
+
+__device__ __forceinline__ void fa_cp16(void * dst, const void * src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(alb_smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void fa_cp4(void * dst, const void * src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" :: "r"(alb_smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void fa_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void fa_wait_ring() {   // all but the newest FA_NST - 2 groups have landed
+    asm volatile("cp.async.wait_group %0;" :: "n"(FA_NST - 2) : "memory");
+}
+__device__ __forceinline__ void fa_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 template <int G>
 __global__ void __launch_bounds__(128)
 k_fa_scores(const float * __restrict__ q, const uint16_t * __restrict__ kc, int Hq, int Hkv, int T, int32_t pos0,
             const int32_t * __restrict__ pos_dev, float scale, int S, int ncap, float * __restrict__ scores,
             float * __restrict__ smax) {
-    const int h = blockIdx.x, t = blockIdx.y, s = blockIdx.z;
-    __shared__ float qs[G][128];
+    extern __shared__ __align__(16) uint8_t fa_ring[];   // FA_NST x FA_CH x FA_KPITCH
+    __shared__ __align__(16) float qs[G][128];
     __shared__ float red[4][G];
+    const int h = blockIdx.x, t = blockIdx.y, s = blockIdx.z, tid = threadIdx.x;
     alb_pdl_wait();
     const int n = (pos_dev ? pos_dev[0] : pos0) + t + 1;
-    fa_load_q<G>(q, Hq, h, t, qs);
-    __syncthreads();
     int c0, c1;
     fa_split(n, S, s, c0, c1);
     const int64_t row = (int64_t)Hkv * 128;
+    const uint16_t * kb = kc + (size_t)h * 128;
+    const int nst = (c1 - c0 + FA_CH - 1) / FA_CH;
+    auto issue = [&](int i) {
+        if (i < nst) {
+            const int cb = c0 + i * FA_CH, rows = min(FA_CH, c1 - cb);
+            uint8_t * dst = fa_ring + (i % FA_NST) * FA_KSTAGE;
+            for (int p = tid; p < rows * 16; p += 128) {
+                const int r = p >> 4, j = p & 15;
+                fa_cp16(dst + r * FA_KPITCH + j * 16, kb + (size_t)(cb + r) * row + j * 8);
+            }
+        }
+        fa_commit();   // one group per stage, empty past the end
+    };
+#pragma unroll
+    for (int i = 0; i < FA_NST - 1; ++i) issue(i);
+    fa_load_q<G>(q, Hq, h, t, qs);
     float mx[G];
 #pragma unroll
     for (int g = 0; g < G; ++g) mx[g] = -INFINITY;
     float * sc = scores + ((size_t)h * T + t) * G * ncap;
-    for (int c = c0 + (int)threadIdx.x; c < c1; c += 128) {
-        const uint16_t * krow = kc + (size_t)c * row + (size_t)h * 128;
+    for (int i = 0; i < nst; ++i) {
+        fa_wait_ring();
+        __syncthreads();   // stage i visible to all; stage i-1 consumed by all
+        issue(i + FA_NST - 1);
+        const int c = c0 + i * FA_CH + tid;
+        if (c < c1) {
+            const uint8_t * kr = fa_ring + (i % FA_NST) * FA_KSTAGE + tid * FA_KPITCH;
+            float a[G];
 #pragma unroll
-        for (int g = 0; g < G; ++g) {
-            const float v = __fmul_rn(fa_score(krow, qs[g]), scale);
-            sc[(size_t)g * ncap + c] = v;
-            mx[g] = fmaxf(mx[g], v);
+            for (int g = 0; g < G; ++g) a[g] = 0.0f;
+#pragma unroll 4
+            for (int j = 0; j < 16; ++j) {   // dims 8j .. 8j+7, in order (the reference's sequential chain)
+                const uint4 kv = *reinterpret_cast<const uint4 *>(kr + j * 16);
+                const uint32_t wd[4] = {kv.x, kv.y, kv.z, kv.w};
+                float kf[8];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&wd[e]));
+                    kf[2 * e] = f.x;
+                    kf[2 * e + 1] = f.y;
+                }
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    const float4 qa = *reinterpret_cast<const float4 *>(&qs[g][8 * j]);
+                    const float4 qb = *reinterpret_cast<const float4 *>(&qs[g][8 * j + 4]);
+                    a[g] = __fmaf_rn(kf[0], qa.x, a[g]);
+                    a[g] = __fmaf_rn(kf[1], qa.y, a[g]);
+                    a[g] = __fmaf_rn(kf[2], qa.z, a[g]);
+                    a[g] = __fmaf_rn(kf[3], qa.w, a[g]);
+                    a[g] = __fmaf_rn(kf[4], qb.x, a[g]);
+                    a[g] = __fmaf_rn(kf[5], qb.y, a[g]);
+                    a[g] = __fmaf_rn(kf[6], qb.z, a[g]);
+                    a[g] = __fmaf_rn(kf[7], qb.w, a[g]);
+                }
+            }
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                const float v = __fmul_rn(a[g], scale);
+                sc[(size_t)g * ncap + c] = v;
+                mx[g] = fmaxf(mx[g], v);
+            }
         }
     }
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    fa_wait_all();
+    const int lane = tid & 31, warp = tid >> 5;
 #pragma unroll
     for (int g = 0; g < G; ++g) {
         const float m = alb_warp_max(mx[g]);
         if (lane == 0) red[warp][g] = m;
     }
     __syncthreads();
-    if (threadIdx.x < G) {
-        const int g = threadIdx.x;
+    if (tid < G) {
+        const int g = tid;
         smax[(((size_t)h * T + t) * S + s) * G + g] = fmaxf(fmaxf(red[0][g], red[1][g]), fmaxf(red[2][g], red[3][g]));
     }
     alb_pdl_trigger();
 }
 
+// V rows and the split's scores stream through the ring; each stage: every
+// thread turns its cell's G scores into p = v_expf(s - M) (L in double) and
+// p * 2^1008 as a double, then warp w accumulates cells w, w+4, .. with lane
+// owning dims 4*lane .. 4*lane+3: O += (p * 2^1008) * (v * 2^-1008), the V
+// element's bits placed in a double with no conversion instruction (the
+// product is p * v exactly, as fma(p, v, O) in double).
 template <int G>
 __global__ void __launch_bounds__(128)
 k_fa_pv(const uint16_t * __restrict__ vc, int Hq, int Hkv, int T, int32_t pos0, const int32_t * __restrict__ pos_dev,
         int S, int ncap, const float * __restrict__ scores, const float * __restrict__ smax, double * __restrict__ part,
         int * __restrict__ tickets, float * __restrict__ out) {
+    extern __shared__ __align__(16) uint8_t fa_ring[];   // FA_NST x (V rows [FA_CH][256 B] + scores [G][FA_CH])
+    __shared__ __align__(16) double pd[FA_CH][G];
+    __shared__ float M[G];
+    __shared__ double Lred[4][G];
+    __shared__ int last;
     const int h = blockIdx.x, t = blockIdx.y, s = blockIdx.z;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    constexpr int FA_CHUNK = (2048 / G) < 512 ? (2048 / G) : 512;   // cells per shared-memory chunk
-    __shared__ float M[G];
-    __shared__ float ps[G][FA_CHUNK];
-    __shared__ double Lred[4][G];
-    __shared__ double ored[4][G][128];
-    __shared__ int last;
+    constexpr int STAGE = FA_VSTAGE + G * FA_CH * 4;
     alb_pdl_wait();
     const int n = (pos_dev ? pos_dev[0] : pos0) + t + 1;
+    int c0, c1;
+    fa_split(n, S, s, c0, c1);
+    const int64_t row = (int64_t)Hkv * 128;
+    const uint16_t * vb = vc + (size_t)h * 128;
+    const float * sc = scores + ((size_t)h * T + t) * G * ncap;
+    const int nst = (c1 - c0 + FA_CH - 1) / FA_CH;
+    auto issue = [&](int i) {
+        if (i < nst) {
+            const int cb = c0 + i * FA_CH, rows = min(FA_CH, c1 - cb);
+            uint8_t * dst = fa_ring + (i % FA_NST) * STAGE;
+            for (int p = tid; p < rows * 16; p += 128) {
+                const int r = p >> 4, j = p & 15;
+                fa_cp16(dst + r * 256 + j * 16, vb + (size_t)(cb + r) * row + j * 8);
+            }
+            if (tid < rows) {
+                float * sdst = reinterpret_cast<float *>(dst + FA_VSTAGE);
+#pragma unroll
+                for (int g = 0; g < G; ++g) fa_cp4(sdst + g * FA_CH + tid, sc + (size_t)g * ncap + cb + tid);
+            }
+        }
+        fa_commit();
+    };
+#pragma unroll
+    for (int i = 0; i < FA_NST - 1; ++i) issue(i);
     if (tid < G) {
         float m = -INFINITY;
         for (int k = 0; k < S; ++k) m = fmaxf(m, smax[(((size_t)h * T + t) * S + k) * G + tid]);
         M[tid] = m;
     }
-    __syncthreads();
-    int c0, c1;
-    fa_split(n, S, s, c0, c1);
-    const int64_t row = (int64_t)Hkv * 128;
-    const float * sc = scores + ((size_t)h * T + t) * G * ncap;
     double L[G], O[G][4];
 #pragma unroll
     for (int g = 0; g < G; ++g) { L[g] = 0.0; O[g][0] = O[g][1] = O[g][2] = O[g][3] = 0.0; }
-    for (int cb = c0; cb < c1; cb += FA_CHUNK) {
-        const int ce = min(c1, cb + FA_CHUNK);
-        __syncthreads();
-        for (int c = cb + tid; c < ce; c += 128)
+    for (int i = 0; i < nst; ++i) {
+        fa_wait_ring();
+        __syncthreads();   // stage i visible; stage i-1 and pd consumed by all; M visible
+        issue(i + FA_NST - 1);
+        const uint8_t * stg = fa_ring + (i % FA_NST) * STAGE;
+        const int rows = min(FA_CH, c1 - (c0 + i * FA_CH));
+        {
+            const float * ss = reinterpret_cast<const float *>(stg + FA_VSTAGE);
 #pragma unroll
             for (int g = 0; g < G; ++g) {
-                const float p = alb_ref_expf(__fsub_rn(sc[(size_t)g * ncap + c], M[g]));
-                ps[g][c - cb] = p;
-                L[g] += (double)p;
+                double v = 0.0;
+                if (tid < rows) {
+                    const float p = alb_ref_expf(__fsub_rn(ss[g * FA_CH + tid], M[g]));
+                    L[g] += (double)p;
+                    v = (double)p * 0x1p1008;
+                }
+                pd[tid][g] = v;
             }
+        }
         __syncthreads();
-        for (int c = cb + warp; c < ce; c += 4) {
-            const uint2 vv = *reinterpret_cast<const uint2 *>(vc + (size_t)c * row + (size_t)h * 128 + 4 * lane);
-            const float2 v01 = __half22float2(*reinterpret_cast<const __half2 *>(&vv.x));
-            const float2 v23 = __half22float2(*reinterpret_cast<const __half2 *>(&vv.y));
+        // 16 rows per pass (4 per warp, loads first); rows past the stage's end
+        // have p = 0 and finite (possibly stale) V bits, so they add exact zeros.
+        for (int r0 = 0; r0 < rows; r0 += 16) {
+            uint2 vv[4];
 #pragma unroll
-            for (int g = 0; g < G; ++g) {
-                const double p = (double)ps[g][c - cb];
-                O[g][0] = fma(p, (double)v01.x, O[g][0]);
-                O[g][1] = fma(p, (double)v01.y, O[g][1]);
-                O[g][2] = fma(p, (double)v23.x, O[g][2]);
-                O[g][3] = fma(p, (double)v23.y, O[g][3]);
+            for (int u = 0; u < 4; ++u)
+                vv[u] = *reinterpret_cast<const uint2 *>(stg + (r0 + warp + 4 * u) * 256 + lane * 8);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int r = r0 + warp + 4 * u;
+                const double v0 = alb_h2d_bits(vv[u].x & 0xFFFFu), v1 = alb_h2d_bits(vv[u].x >> 16);
+                const double v2 = alb_h2d_bits(vv[u].y & 0xFFFFu), v3 = alb_h2d_bits(vv[u].y >> 16);
+                double p[G];
+                if constexpr (G % 2 == 0) {
+#pragma unroll
+                    for (int g = 0; g < G; g += 2) {
+                        const double2 pp = *reinterpret_cast<const double2 *>(&pd[r][g]);
+                        p[g] = pp.x;
+                        p[g + 1] = pp.y;
+                    }
+                } else {
+#pragma unroll
+                    for (int g = 0; g < G; ++g) p[g] = pd[r][g];
+                }
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    O[g][0] = fma(p[g], v0, O[g][0]);
+                    O[g][1] = fma(p[g], v1, O[g][1]);
+                    O[g][2] = fma(p[g], v2, O[g][2]);
+                    O[g][3] = fma(p[g], v3, O[g][3]);
+                }
             }
         }
     }
-    // CTA reduction: L over threads, O over the 4 warps (thread tid owns dim tid afterwards)
+    fa_wait_all();
+    __syncthreads();   // the ring is free: it holds the per-warp O partials now
+    double (*ored)[G][128] = reinterpret_cast<double (*)[G][128]>(fa_ring);   // [4][G][128]
 #pragma unroll
     for (int g = 0; g < G; ++g) {
         const double l = alb_warp_sum_d(L[g]);
@@ -406,12 +539,21 @@ static cudaError_t launch_fa_t(const FlashArgs & f, cudaStream_t st) {
     float * smax = reinterpret_cast<float *>(ws + l.smax_off);
     float * scores = reinterpret_cast<float *>(ws + l.scores_off);
     double * part = reinterpret_cast<double *>(ws + l.part_off);
+    static bool split_attr = false;   // per instantiation; legal inside stream capture
+    if (!split_attr) {
+        cudaError_t e = cudaFuncSetAttribute(k_fa_scores<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)FA_SCORES_SMEM);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(k_fa_pv<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fa_pv_smem<G>());
+        if (e != cudaSuccess) return e;
+        split_attr = true;
+    }
     dim3 grid((unsigned)f.Hkv, (unsigned)f.T, (unsigned)f.S);
-    cudaError_t e = alb_launch(k_fa_scores<G>, grid, dim3(128), 0, st, f.pdl, f.q, f.kc, f.Hq, f.Hkv, f.T, f.pos0,
-                               f.pos_dev, f.scale, f.S, f.ncap, scores, smax);
+    cudaError_t e = alb_launch(k_fa_scores<G>, grid, dim3(128), FA_SCORES_SMEM, st, f.pdl, f.q, f.kc, f.Hq, f.Hkv, f.T,
+                               f.pos0, f.pos_dev, f.scale, f.S, f.ncap, scores, smax);
     if (e != cudaSuccess) return e;
-    return alb_launch(k_fa_pv<G>, grid, dim3(128), 0, st, f.pdl, f.vc, f.Hq, f.Hkv, f.T, f.pos0, f.pos_dev, f.S,
-                      f.ncap, (const float *)scores, (const float *)smax, part, tickets, f.out);
+    return alb_launch(k_fa_pv<G>, grid, dim3(128), fa_pv_smem<G>(), st, f.pdl, f.vc, f.Hq, f.Hkv, f.T, f.pos0,
+                      f.pos_dev, f.S, f.ncap, (const float *)scores, (const float *)smax, part, tickets, f.out);
 }
 
 cudaError_t launch_flash_attn(const FlashArgs & f, cudaStream_t st) {

@@ -1,7 +1,7 @@
 #!/usr/bin/env python3
 """ArcLight B200 hot-path benchmark (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode|gemv|prefill] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode|gemv|prefill|long|attn] [--impl ours|reference]
 
 Workloads:
   decode  config 3 (default): Qwen3-4B-shaped Q4_0 model, random init, 512-token
@@ -12,6 +12,10 @@ Workloads:
   prefill config 4: the same model prefilling a 2048-token prompt from an empty
           cache; a step is one prompt (time to first token); the mat-muls run on
           the int8 tensor cores.
+  long    config 5: Qwen3-8B shape, KV cache filled to 32768 positions, then
+          batch-1 decode; a step is one token; N > 1: tensor parallel.
+  attn    config 5's attention alone: split-K flash decode of one token over
+          32768 fp16 cells (32 query / 8 KV heads); a step is one call.
 Metric / value / roofline: value is whole-job tok/s with inputs resident; e2e goes through the C ABI with host buffers; roofline.achieved = algorithmic bytes per launch / CUDA-event launch time.
 """
 from __future__ import annotations
@@ -346,6 +350,202 @@ def run_decode(args, rank, world):
     return out
 
 
+# ----------------------------------------------------------------- long context (config 5)
+LONG_CTX = 32768
+
+
+# ----------------------------------------------------------------- attention alone (config 5 shape)
+ATT_HQ, ATT_HKV, ATT_CELLS, ATT_COPIES = 32, 8, 32768, 4
+ATT_BYTES = 2 * ATT_CELLS * ATT_HKV * 128 * 2 + 2 * ATT_HQ * 128 * 4   # K + V + q + out per call
+
+
+def cpu_attn_baseline(seconds: float = 10.0):
+    """The oracle's attention (mode 0, one thread) at the same shape, bounded sample."""
+    from oracle import lib as O
+    rng = np.random.default_rng(2)
+    k = rng.standard_normal((ATT_CELLS, ATT_HKV, 128)).astype(np.float16).view(np.uint16)
+    v = rng.standard_normal((ATT_CELLS, ATT_HKV, 128)).astype(np.float16).view(np.uint16)
+    q = rng.standard_normal((1, ATT_HQ, 128)).astype(np.float32)
+    kv_len = np.array([ATT_CELLS], np.int32)
+    n, t0 = 0, time.perf_counter()
+    while n == 0 or time.perf_counter() - t0 < seconds:
+        O.flash_attn(q, k, v, kv_len, 1.0 / np.sqrt(128.0), 0)
+        n += 1
+    dt = (time.perf_counter() - t0) / n
+    return {"value": ATT_BYTES / dt / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"{n} attention calls ({ATT_HQ}/{ATT_HKV} heads over {ATT_CELLS} cells) in {seconds:.0f} s"}
+
+
+def run_attn(args, rank, world):
+    """Config 5's attention alone: split-K flash decode of one token over a
+    32768-cell fp16 KV cache (Qwen3-8B heads: 32 query / 8 KV), one call per
+    step through the C ABI, rotating over 4 cache copies (512 MB > L2)."""
+    import torch
+    import arclight_b200 as A
+    from arclight_b200 import bench_util as BU
+
+    L = A.lib()
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    A.check(L.alb_device_check(local), "device check")
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    S = (2 * sms + ATT_HKV - 1) // ATT_HKV          # the engine's decode split count
+    gen = torch.Generator(device=dev).manual_seed(7)
+    kc = torch.randn((ATT_COPIES, ATT_CELLS, ATT_HKV, 128), generator=gen, device=dev).half()
+    vc = torch.randn((ATT_COPIES, ATT_CELLS, ATT_HKV, 128), generator=gen, device=dev).half()
+    q = torch.randn((1, ATT_HQ, 128), generator=gen, device=dev)
+    out = torch.empty_like(q)
+    ws = torch.zeros(L.alb_flash_attn_workspace_bytes(ATT_HQ, ATT_HKV, 1, S, ATT_CELLS), dtype=torch.uint8,
+                     device=dev)
+    scale = 1.0 / float(np.sqrt(128.0))
+    s = torch.cuda.Stream()
+
+    def call(i, qp=None, op=None):
+        qp = q if qp is None else qp
+        op = out if op is None else op
+        A.check(L.alb_flash_attn(qp.data_ptr(), kc[i % ATT_COPIES].data_ptr(), vc[i % ATT_COPIES].data_ptr(),
+                                 1, ATT_HQ, ATT_HKV, ATT_CELLS - 1, scale, S, ws.data_ptr(), op.data_ptr(),
+                                 s.cuda_stream), "alb_flash_attn")
+
+    with torch.cuda.stream(s):
+        for i in range(ATT_COPIES):
+            call(i)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for i in range(ATT_COPIES):
+                call(i)
+    reps = max(1, args.steps // ATT_COPIES)
+    steps = reps * ATT_COPIES
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        for _ in range(max(args.warmup, 3)):
+            g.replay()
+        torch.cuda.synchronize()
+        BU.barrier(world)
+        torch.cuda.nvtx.range_push("timed")
+        e0.record(s)
+        for _ in range(reps):
+            g.replay()
+        e1.record(s)
+        torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize()
+    ms = BU.max_over_ranks(e0.elapsed_time(e1) / steps, world)
+
+    # e2e through the C ABI with host buffers: H2D q, attention, D2H out
+    qh = torch.randn((1, ATT_HQ, 128)).pin_memory()
+    oh = torch.empty((1, ATT_HQ, 128)).pin_memory()
+    qd, od = torch.empty_like(q), torch.empty_like(q)
+    with torch.cuda.stream(s):
+        for i in range(3):
+            qd.copy_(qh, non_blocking=True)
+            call(i, qd, od)
+            oh.copy_(od, non_blocking=True)
+        torch.cuda.synchronize()
+        e0.record(s)
+        for i in range(steps):
+            qd.copy_(qh, non_blocking=True)
+            call(i, qd, od)
+            oh.copy_(od, non_blocking=True)
+        e1.record(s)
+        torch.cuda.synchronize()
+    e2e_ms = BU.max_over_ranks(e0.elapsed_time(e1) / steps, world)
+    peaks = load_peaks()
+    achieved = ATT_BYTES / (ms * 1e-3) / 1e9
+    return {
+        "metric": "split-K flash decode GB/s (config 5 attention: 32/8 heads, 32768 fp16 cells)",
+        "value": achieved * world, "unit": "GB/s", "n_gpus": world, "steps": steps, "warmup": max(args.warmup, 3),
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp16 KV, fp32 scores (sequential fma), fp64 softmax sums", "data": "synthetic: N(0,1) q/K/V",
+        "config": {"workload": "config5_attention", "n_head": ATT_HQ, "n_head_kv": ATT_HKV, "cells": ATT_CELLS,
+                   "splits": S, "kv_copies": ATT_COPIES, "l2": "inputs larger than L2: 4 rotating caches (512 MB)"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / peaks["hbm_gbs"], "traffic": None, "peak_src": peaks["src"],
+                     "kernel": "k_fa_scores + k_fa_pv (one call)", "algorithmic_bytes_per_launch": ATT_BYTES},
+        "e2e": {"value": ATT_BYTES / (e2e_ms * 1e-3) / 1e9 * world, "unit": "GB/s",
+                "h2d_bytes_per_step": ATT_HQ * 128 * 4, "d2h_bytes_per_step": ATT_HQ * 128 * 4},
+        "gpu_launches": 2 * steps,
+        "clocks": clk.summary(),
+    }
+
+
+def run_long(args, rank, world):
+    """Config 5: Qwen3-8B shape, KV cache pre-filled to 32768 positions with
+    N(0,1) fp16, then greedy batch-1 decode (split-K attention over the cache)."""
+    import torch
+    import arclight_b200 as A
+    from arclight_b200 import bench_util as BU
+    from arclight_b200.configs import QWEN3_8B
+    from arclight_b200.engine import Engine, nccl_unique_id
+
+    cfg = QWEN3_8B
+    L = A.lib()
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    torch.cuda.set_device(local)
+    A.check(L.alb_device_check(local), "device check")
+    nid = None
+    if world > 1:
+        import torch.distributed as dist
+        obj = [nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        nid = obj[0]
+    n_gen = args.steps
+    max_ctx = LONG_CTX + max(n_gen, args.warmup) + 16
+    e = Engine(cfg, 1234, max_ctx, 16, rank, world, nid, local)
+    e.fill_kv(LONG_CTX, 99)
+    tok0 = 1
+    st = torch.cuda.ExternalStream(e.stream())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e.decode_loop(tok0, LONG_CTX, max(args.warmup, 3), want_tokens=False, sync=True)
+        BU.barrier(world)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("timed")
+        e0.record(st)
+        e.decode_loop(tok0, LONG_CTX, n_gen, want_tokens=False, sync=False)
+        e1.record(st)
+        torch.cuda.nvtx.range_pop()
+        e1.synchronize()
+    ms = BU.max_over_ranks(e0.elapsed_time(e1) / n_gen, world)
+    info = e.info()
+    BU.barrier(world)
+    tok = tok0
+    t_e2e = time.perf_counter()
+    for i in range(min(n_gen, 32)):
+        tok = e.decode(tok, LONG_CTX + i)
+    e2e_ms = BU.max_over_ranks((time.perf_counter() - t_e2e) * 1000.0 / min(n_gen, 32), world)
+    peaks = load_peaks()
+    E, F, Lr, V = cfg["n_embd"], cfg["n_ff"], cfg["n_layer"], cfg["n_vocab"]
+    Dq, Dkv = cfg["n_head"] * 128, cfg["n_head_kv"] * 128
+    weights = (Lr * (E * (Dq + 2 * Dkv) + Dq * E + 3 * E * F) + V * E) * 18 // 32
+    kv = Lr * 2 * Dkv * 2 * (LONG_CTX + (n_gen - 1) / 2.0 + 1)
+    bpt = weights + kv + (Lr * (2 * E + 256) + E) * 4
+    gbs_total = bpt * 1000.0 / ms / 1e9
+    gbs_gpu = gbs_total / world
+    out = {
+        "metric": "Qwen3-8B Q4_0 decode tok/s bs=1 at 32768-token context",
+        "value": 1000.0 / ms, "unit": "tok/s", "n_gpus": world, "steps": n_gen, "warmup": max(args.warmup, 3),
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "q4_0 weights x q8_0 activations (int32 block dots), fp32/fp64 accumulate, fp16 KV",
+        "data": "synthetic: seeded random-init Qwen3-8B-shaped weights; KV cache filled with seeded N(0,1) fp16",
+        "config": {"workload": "config5_long_qwen3_8b", "context": LONG_CTX, "decode_steps": n_gen,
+                   "parallelism": f"tp{world}", "global_batch": 1,
+                   "l2": "inputs larger than L2 (4.26 GB of weights + 4.83 GB of KV per token)",
+                   "launches_per_token": info["launches_per_step"], "attn_splits": info["attn_splits"]},
+        "roofline": {"bound": "hbm", "achieved": gbs_gpu, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": gbs_gpu / peaks["hbm_gbs"], "traffic": None, "peak_src": peaks["src"],
+                     "kernel": "decode step (multi-kernel CUDA graph: mat-vecs + split-K flash decode), per GPU",
+                     "algorithmic_bytes_per_launch": bpt / world, "avg_launch_us": ms * 1000.0},
+        "gbs_per_gpu": gbs_gpu,
+        "e2e": {"value": 1000.0 / e2e_ms, "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4},
+        "gpu_launches": info["launches_per_step"] * n_gen,
+        "clocks": clk.summary(),
+    }
+    e.close()
+    return out
+
+
 # ----------------------------------------------------------------- prefill (config 4)
 PREFILL_T = 2048
 INT8_PEAK_TOPS = 4500.0   # nominal dense int8 (no measured int8 peak in MEASURED_PEAKS.json)
@@ -429,12 +629,12 @@ def main():
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "gemv", "prefill"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "gemv", "prefill", "long", "attn"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.steps is None:
-        args.steps = {"decode": 256, "gemv": 2400, "prefill": 5}[args.workload]
+        args.steps = {"decode": 256, "gemv": 2400, "prefill": 5, "long": 128, "attn": 400}[args.workload]
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     if world > 1:
@@ -453,12 +653,22 @@ def main():
                 cb = cpu_prefill_baseline(QWEN3_4B)
                 metric, unit = "Qwen3-4B Q4_0 prefill tok/s (2048-token prompt, 1/TTFT)", "tok/s"
                 cfgname = "config4_prefill_qwen3_4b"
+            elif args.workload == "long":
+                from arclight_b200.configs import QWEN3_8B
+                cb = cpu_decode_baseline(QWEN3_8B, seconds=min(60.0, 5.0 + 0.2 * args.steps))
+                cb["sample"] += "; 8B weights but a short cache: a lower bound of the CPU time at 32768 positions"
+                metric, unit = "Qwen3-8B Q4_0 decode tok/s bs=1 at 32768-token context", "tok/s"
+                cfgname = "config5_long_qwen3_8b"
+            elif args.workload == "attn":
+                cb = cpu_attn_baseline(seconds=10.0)
+                metric, unit = "split-K flash decode GB/s (config 5 attention: 32/8 heads, 32768 fp16 cells)", "GB/s"
+                cfgname = "config5_attention"
             else:
                 cb = cpu_gemv_baseline(seconds=min(20.0, 2.0 + 0.005 * args.steps))
                 metric, unit, cfgname = "Q4_0xQ8_0 GEMV HBM GB/s (config 1, W 9728x2560)", "GB/s", "config1_gemv"
             line = {"impl": "reference", "metric": metric, "value": cb["value"], "unit": unit, "n_gpus": world,
                     "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
-                    "scaling": "weak" if args.workload == "gemv" else "strong", "vs_baseline": None,
+                    "scaling": "weak" if args.workload in ("gemv", "attn") else "strong", "vs_baseline": None,
                     "dtype": "q4_0 x q8_0", "data": "synthetic", "config": {"workload": cfgname},
                     "cpu_baseline": cb,
                     "e2e": {"value": cb["value"], "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -472,6 +682,10 @@ def main():
         out = run_decode(args, rank, world)
     elif args.workload == "prefill":
         out = run_prefill(args, rank, world)
+    elif args.workload == "long":
+        out = run_long(args, rank, world)
+    elif args.workload == "attn":
+        out = run_attn(args, rank, world)
     else:
         out = run_gemv(args, rank, world)
     if rank == 0:
@@ -482,6 +696,13 @@ def main():
             elif args.workload == "prefill":
                 from arclight_b200.configs import QWEN3_4B
                 out["cpu_baseline"] = cpu_prefill_baseline(QWEN3_4B)
+            elif args.workload == "long":
+                from arclight_b200.configs import QWEN3_8B
+                cb = cpu_decode_baseline(QWEN3_8B, seconds=20.0)
+                cb["sample"] += "; 8B weights but a short cache: a lower bound of the CPU time at 32768 positions"
+                out["cpu_baseline"] = cb
+            elif args.workload == "attn":
+                out["cpu_baseline"] = cpu_attn_baseline(seconds=10.0)
             else:
                 out["cpu_baseline"] = cpu_gemv_baseline(seconds=10.0)
         print(json.dumps(out), flush=True)

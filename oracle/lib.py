@@ -91,6 +91,7 @@ def lib() -> C.CDLL:
             "orc_model_f32_tensor": (vp, [vp, C.c_int, C.c_int, vp]),
             "orc_model_forward": (C.c_int, [vp, vp, i32, i32, C.c_int, vp, vp]),
             "orc_model_reset": (None, [vp]),
+            "orc_model_fill_kv": (None, [vp, i32, C.c_uint64]),
             "orc_argmax": (i32, [vp, i64]),
         }
         for name, (res, args) in sig.items():
@@ -263,6 +264,10 @@ class Model:
 
     def reset(self):
         lib().orc_model_reset(self.h)
+
+    def fill_kv(self, n_pos: int, seed: int):
+        """K/V of positions [0, n_pos) := fp16 N(0,1), the long-context benchmark's pre-fill."""
+        lib().orc_model_fill_kv(self.h, int(n_pos), int(seed))
 
     def set_exact(self, exact: bool):
         """True (default): exactly rounded mat-vecs; False: the reference's NEON fp32 chains."""

@@ -642,6 +642,18 @@ void orc_model_reset(orc_model * m) {
     }
 }
 
+void orc_model_fill_kv(orc_model * m, int32_t n_pos, uint64_t seed) {
+    const int64_t Dkv = (int64_t)m->c.n_head_kv * m->c.head_dim;
+    if (n_pos > m->max_ctx) n_pos = m->max_ctx;
+    for (int l = 0; l < m->c.n_layer; ++l) {
+        const uint64_t sk = orc_tensor_seed(seed, l, 62), sv = orc_tensor_seed(seed, l, 63);
+        for (int64_t i = 0; i < (int64_t)n_pos * Dkv; ++i) {
+            m->layers[l].kc[i] = orc_fp32_to_fp16(orc_normal(m->table, sk, (uint64_t)i));
+            m->layers[l].vc[i] = orc_fp32_to_fp16(orc_normal(m->table, sv, (uint64_t)i));
+        }
+    }
+}
+
 const orc_block_q4_0 * orc_model_q4_tensor(orc_model * m, int layer, int kind, int64_t * rows, int64_t * cols) {
     const orc_qwen3_config * c = &m->c;
     const int64_t E = c->n_embd, Dq = (int64_t)c->n_head * c->head_dim, Dkv = (int64_t)c->n_head_kv * c->head_dim;

@@ -126,6 +126,10 @@ const float *          orc_model_f32_tensor(orc_model * m, int layer, int kind, 
 int  orc_model_forward(orc_model * m, const int32_t * tokens, int32_t T, int32_t pos0,
                        int fa_mode, float * logits, float * hidden);
 void orc_model_reset(orc_model * m);
+/* Long-context benchmark pre-fill: K and V of positions [0, n_pos) of every
+ * layer set to fp16(N(0,1)) from the seeded generator, element (cell, e) of
+ * layer l drawn at index cell * Dkv + e under orc_tensor_seed(seed, l, 62 | 63). */
+void orc_model_fill_kv(orc_model * m, int32_t n_pos, uint64_t seed);
 /* exact != 0 (default): mat-vecs use orc_gemv_q4_0_q8_0_exact (also for the lm
  * head); 0: the reference's NEON fp32 chains (gemv for projections,
  * nnml_vec_dot_q4_0_q8_0 lanes for the lm head). */

@@ -118,3 +118,53 @@ def test_persistent_decode_kernel_matches_multi_kernel_path(monkeypatch):
     assert res["1"][2] == 1 and res["0"][2] > 1
     assert res["1"][0] == res["0"][0]
     np.testing.assert_array_equal(res["1"][1], res["0"][1])
+
+
+@pytest.mark.parametrize("mk", ["1", "0"], ids=["persistent", "multi_kernel"])
+def test_prefilled_kv_long_context_decode(mk, monkeypatch):
+    """Config-5 path at a small shape: the KV cache of 1000 positions pre-filled
+    with fp16 N(0,1) on both sides (no prompt), then greedy decode from position
+    1000; logits within the north_star bar and identical greedy tokens."""
+    from arclight_b200.engine import Engine
+    monkeypatch.setenv("ALB_DECODE_MK", mk)
+    cfg, n_fill, n_gen = TINY_GQA, 1000, 8
+    e = Engine(cfg, 21, n_fill + n_gen + 8, 16)
+    m = O.Model(cfg, 21, n_fill + n_gen + 8)
+    try:
+        e.fill_kv(n_fill, 99)
+        m.fill_kv(n_fill, 99)
+        gpu_toks, ref_toks, errs = [1], [1], []
+        for i in range(n_gen):
+            gpu_toks.append(e.decode(gpu_toks[-1], n_fill + i))
+            lg_ref, _ = m.forward([ref_toks[-1]], n_fill + i, 0)
+            errs.append(float(np.max(np.abs(e.logits() - lg_ref))))
+            ref_toks.append(O.argmax(lg_ref))
+        assert gpu_toks == ref_toks, f"greedy tokens diverge: {gpu_toks} vs {ref_toks}"
+        assert max(errs) < LOGIT_ATOL, f"decode logits max-abs {max(errs)}"
+        assert list(e.decode_loop(1, n_fill, n_gen)) == gpu_toks[1:]
+    finally:
+        e.close()
+        m.close()
+
+
+def test_decode_graph_built_before_any_prefill_in_fresh_process():
+    """A process whose first GPU work is fill_kv + the device decode loop (the
+    long-context benchmark) captures the decode graph before any eager launch."""
+    import os
+    import subprocess
+    import sys
+    code = ("from arclight_b200.engine import Engine\n"
+            "from arclight_b200.configs import TINY_GQA\n"
+            "e = Engine(TINY_GQA, 3, 600, 16)\n"
+            "e.fill_kv(512, 7)\n"
+            "a = list(e.decode_loop(1, 512, 4))\n"
+            "b = [e.decode(1, 512)]\n"
+            "for i in range(3): b.append(e.decode(b[-1], 513 + i))\n"
+            "assert a == b, (a, b)\n"
+            "e.close()\n")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    for mk in ("0", "1"):
+        env = dict(os.environ, ALB_DECODE_MK=mk)
+        r = subprocess.run([sys.executable, "-c", code], cwd=root, env=env, capture_output=True, text=True,
+                           timeout=600)
+        assert r.returncode == 0, f"ALB_DECODE_MK={mk}: {r.stderr[-2000:]}"
