@@ -67,6 +67,12 @@ def _declare(L: C.CDLL) -> None:
         "alb_gemv_q4_0_q8_0_block_dots": (ci, [vp, vp, vp, i64, i64, vp]),
         "alb_rms_norm": (ci, [vp, vp, vp, i64, i64, f32, vp]),
         "alb_swiglu": (ci, [vp, vp, vp, i64, vp]),
+        "alb_rms_norm_q8": (ci, [vp, vp, vp, vp, i64, i64, f32, vp]),
+        "alb_swiglu_q8": (ci, [vp, vp, vp, vp, i64, vp]),
+        "alb_comm_create": (ci, [vp, C.c_int32, C.c_int32, C.c_int32, vp]),
+        "alb_comm_destroy": (ci, [vp]),
+        "alb_allreduce_sum_f32": (ci, [vp, vp, vp, i64, vp]),
+        "alb_allgather_f32": (ci, [vp, vp, vp, i64, vp]),
         "alb_get_rows_q4_0": (ci, [vp, i64, i64, vp, i64, vp, vp]),
         "alb_rope_table": (ci, [vp, i32, i32, f32]),
         "alb_qk_norm_rope_kv": (ci, [vp, i64, i32, i32, vp, vp, f32, vp, i32, vp, vp, vp, vp]),

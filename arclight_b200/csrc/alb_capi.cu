@@ -20,6 +20,19 @@ extern "C" int alb_swiglu(const float * g, const float * u, float * y, int64_t n
     return ALB_OK;
 }
 
+extern "C" int alb_rms_norm_q8(const float * x, const float * w, float * y, void * yq, int64_t rows, int64_t n,
+                               float eps, void * stream) {
+    ALB_CHECK_ARG(x && yq && rows > 0 && rows < (1LL << 31) && n > 0 && n % 32 == 0 && n / 256 < 65535 && eps >= 0.0f);
+    ALB_CUDA_TRY(launch_rms_norm_q8(x, w, y, yq, rows, n, eps, true, (cudaStream_t)stream));
+    return ALB_OK;
+}
+
+extern "C" int alb_swiglu_q8(const float * g, const float * u, float * y, void * yq, int64_t n, void * stream) {
+    ALB_CHECK_ARG(g && u && yq && n > 0 && n % 32 == 0 && n / 32 < (1LL << 34));
+    ALB_CUDA_TRY(launch_swiglu_q8(g, u, y, yq, n, true, (cudaStream_t)stream));
+    return ALB_OK;
+}
+
 extern "C" int alb_get_rows_q4_0(const void * W, int64_t n_rows, int64_t K, const int32_t * ids, int64_t n_ids,
                                  float * out, void * stream) {
     ALB_CHECK_ARG(W && ids && out && n_rows > 0 && K > 0 && K % 32 == 0 && n_ids > 0 && n_ids < (1 << 30));

@@ -82,6 +82,7 @@ struct alb_engine {
     float * x = nullptr, * qkv = nullptr, * q = nullptr, * att = nullptr, * h = nullptr, * logits = nullptr;
     float * part = nullptr, * part_all = nullptr;   // TP: this rank's O / down partial, all ranks' partials
     float * xn = nullptr;                           // prefill: RMS-normalized rows
+    void * xq = nullptr;                            // decode: block_q8_0 input of the next mat-vec
     void * pg_ws = nullptr;                         // prefill: quantized activations of the mat-mul
     int32_t * tok_dev = nullptr, * pos_dev = nullptr, * next_dev = nullptr, * step_dev = nullptr, * gen_out = nullptr;
     int32_t gen_cap = 0;
@@ -143,7 +144,19 @@ static int engine_forward(alb_engine * e, int64_t T, bool pdl, int ncap_prefill 
         a.in_mode = in; a.x = x; a.norm_w = nw; a.eps = c.eps;
         a.out_mode = out; a.y = y; a.residual = res; a.pdl = pdl;
         ++launches;
-        if (T == 1) return launch_gemv(a, st);
+        if (T == 1 && in == GEMV_IN_Q8) return launch_gemv(a, st);   // records already in x
+        if (T == 1) {
+            // the input quantized once (RMSNorm fused), so every CTA of the mat-vec
+            // stages the block_q8_0 records instead of re-quantizing the vector
+            const cudaError_t qe = in == GEMV_IN_F32_RMS
+                ? launch_rms_norm_q8(static_cast<const float *>(x), nw, nullptr, e->xq, 1, K, c.eps, pdl, st)
+                : launch_quantize_q8_0(static_cast<const float *>(x), e->xq, K, pdl, st);
+            if (qe != cudaSuccess) return qe;
+            ++launches;
+            a.in_mode = GEMV_IN_Q8;
+            a.x = e->xq;
+            return launch_gemv(a, st);
+        }
         // prefill: RMSNorm rows (when asked), then the tensor-core mat-mul
         const float * xin = static_cast<const float *>(x);
         if (in == GEMV_IN_F32_RMS) {
@@ -170,12 +183,15 @@ static int engine_forward(alb_engine * e, int64_t T, bool pdl, int ncap_prefill 
         fa.pos_dev = e->pos_dev; fa.scale = 1.0f / sqrtf((float)c.head_dim); fa.S = S; fa.ws = e->fa_ws;
         fa.ncap = T == 1 ? e->max_ctx : ncap_prefill;
         fa.out = e->att; fa.pdl = pdl;
+        fa.xq = T == 1 ? e->xq : nullptr;   // decode: the merge writes the o_proj input records
         ALB_CUDA_TRY(launch_flash_attn(fa, st));
-        launches += 2;
+        launches += S > 1 ? 3 : 2;
+        const int o_in = T == 1 ? GEMV_IN_Q8 : GEMV_IN_F32;
+        const void * o_x = T == 1 ? e->xq : static_cast<const void *>(e->att);
         if (e->tp == 1) {
-            ALB_CUDA_TRY(gemv(L.o, e->E, e->Dq, GEMV_IN_F32, e->att, nullptr, GEMV_OUT_PLAIN, e->x, e->x));
+            ALB_CUDA_TRY(gemv(L.o, e->E, e->Dq, o_in, o_x, nullptr, GEMV_OUT_PLAIN, e->x, e->x));
         } else {
-            ALB_CUDA_TRY(gemv(L.o, e->E, e->Dq, GEMV_IN_F32, e->att, nullptr, GEMV_OUT_PLAIN, e->part, nullptr));
+            ALB_CUDA_TRY(gemv(L.o, e->E, e->Dq, o_in, o_x, nullptr, GEMV_OUT_PLAIN, e->part, nullptr));
             ALB_TRY(engine_gather_add_x(e, T, pdl));
         }
         ALB_CUDA_TRY(gemv(L.gu, 2 * (int64_t)e->F, e->E, GEMV_IN_F32_RMS, e->x, L.fn, GEMV_OUT_SWIGLU, e->h, nullptr));
@@ -189,12 +205,14 @@ static int engine_forward(alb_engine * e, int64_t T, bool pdl, int ncap_prefill 
     }
     // final norm + lm_head on the last token (qwen3.cpp:235-238, 266-274)
     {
+        ALB_CUDA_TRY(launch_rms_norm_q8(e->x + (size_t)(T - 1) * e->E, e->out_norm, nullptr, e->xq, 1, e->E, c.eps,
+                                        pdl, st));
         GemvArgs a;
         a.W = e->lm_W; a.S = e->lm_S; a.N = e->V; a.K = e->E;
-        a.in_mode = GEMV_IN_F32_RMS; a.x = e->x + (size_t)(T - 1) * e->E; a.norm_w = e->out_norm; a.eps = c.eps;
+        a.in_mode = GEMV_IN_Q8; a.x = e->xq; a.eps = c.eps;
         a.out_mode = GEMV_OUT_PLAIN; a.y = e->logits; a.pdl = pdl;
         ALB_CUDA_TRY(launch_gemv(a, st));
-        ++launches;
+        launches += 2;
     }
     if (e->tp == 1) {
         ALB_CUDA_TRY(launch_argmax(e->logits, e->V, 0, e->am_scratch, e->key, e->next_dev, pdl, st));
@@ -309,6 +327,13 @@ static int engine_init_acts(alb_engine * e) {
     ALB_TRY(e->alloc(&e->q, U * e->Dq));
     ALB_TRY(e->alloc(&e->att, U * e->Dq));
     ALB_TRY(e->alloc(&e->h, U * e->F));
+    {
+        int64_t kmax = e->E > e->Dq ? e->E : e->Dq;
+        if (e->F > kmax) kmax = e->F;
+        uint8_t * q8 = nullptr;
+        ALB_TRY(e->alloc(&q8, (size_t)(kmax / 32) * 34));
+        e->xq = q8;
+    }
     if (U > 1) {
         ALB_TRY(e->alloc(&e->xn, U * e->E));
         int64_t kmax = e->E > e->Dq ? e->E : e->Dq;
@@ -332,8 +357,8 @@ static int engine_init_acts(alb_engine * e) {
     uint8_t * scr = nullptr;
     ALB_TRY(e->alloc(&scr, 1024));
     e->am_scratch = scr;
-    // decode split-K: 2 CTAs per SM (the split kernels' staging ring allows two) over the local KV heads
-    int S = (2 * alb_sm_count() + e->Hkv - 1) / e->Hkv;
+    // decode split-K: 4 CTAs per SM (the split kernels' staging ring allows four) over the local KV heads
+    int S = (4 * alb_sm_count() + e->Hkv - 1) / e->Hkv;
     if (S > 1024) S = 1024;
     e->fa_S_decode = S;
     e->fa_ws_bytes = flash_attn_ws_bytes(e->Hq, e->Hkv, 1, S, e->max_ctx);
@@ -421,6 +446,44 @@ static void engine_free(alb_engine * e) {
 extern "C" int alb_nccl_unique_id(void * out128) {
     ALB_CHECK_ARG(out128);
     return nccl_unique_id(out128);
+}
+
+// Communicator of the tensor-parallel clique for callers that run the op-level
+// ABI themselves (the reference's GATHER, ops.cpp:1465-1511, becomes a sum
+// all-reduce or an all-gather followed by an ordered sum).
+struct alb_comm {
+    void * nccl = nullptr;
+    int dev = 0;
+};
+
+extern "C" int alb_comm_create(const void * nccl_id, int32_t rank, int32_t size, int32_t device, alb_comm ** out) {
+    ALB_CHECK_ARG(nccl_id && out && size >= 1 && rank >= 0 && rank < size && device >= 0);
+    *out = nullptr;
+    ALB_CUDA_TRY(cudaSetDevice(device));
+    alb_comm * c = new alb_comm();
+    c->dev = device;
+    const int rc = nccl_init(&c->nccl, rank, size, nccl_id);
+    if (rc != ALB_OK) { delete c; return rc; }
+    *out = c;
+    return ALB_OK;
+}
+
+extern "C" int alb_comm_destroy(alb_comm * c) {
+    if (!c) return ALB_OK;
+    cudaSetDevice(c->dev);
+    nccl_destroy(c->nccl, false);
+    delete c;
+    return ALB_OK;
+}
+
+extern "C" int alb_allreduce_sum_f32(alb_comm * c, const float * src, float * dst, int64_t n, void * stream) {
+    ALB_CHECK_ARG(c && src && dst && n > 0);
+    return nccl_allreduce(c->nccl, src, dst, (size_t)n, 0, 0, (cudaStream_t)stream);
+}
+
+extern "C" int alb_allgather_f32(alb_comm * c, const float * src, float * dst, int64_t n, void * stream) {
+    ALB_CHECK_ARG(c && src && dst && n > 0);
+    return nccl_allgather_f32(c->nccl, src, dst, (size_t)n, (cudaStream_t)stream);
 }
 
 extern "C" int alb_engine_create(const alb_qwen3_config * cfg, uint64_t seed, int32_t max_ctx, int32_t max_ubatch,

@@ -51,8 +51,9 @@ struct FlashArgs {
     float scale = 0.0f;
     int S = 1;                          // splits along the cells
     int ncap = 0;                       // upper bound of cells attended (>= pos0 + T)
-    float * ws = nullptr;               // flash_attn_ws_bytes(); tickets must start at 0
+    float * ws = nullptr;               // flash_attn_ws_bytes()
     float * out = nullptr;              // [T][Hq][128] fp32
+    void * xq = nullptr;                // optional: block_q8_0 records of out, [T][Hq*4]
     bool pdl = false;
 };
 size_t flash_attn_ws_bytes(int Hq, int Hkv, int T, int S, int ncap);
@@ -80,6 +81,14 @@ cudaError_t launch_argmax(const float * x, int64_t n, int64_t idx_base, void * s
 cudaError_t launch_key_to_index(const unsigned long long * key, int32_t * idx, bool pdl, cudaStream_t st);
 cudaError_t launch_rms_norm(const float * x, const float * w, float * y, int64_t rows, int64_t n, float eps, bool pdl,
                             cudaStream_t st);
+// RMSNorm (+ MUL by w) / swiglu followed by quantize_row_q8_0 of the result;
+// y (fp32 copy of the result) may be null; n % 32 == 0.
+cudaError_t launch_rms_norm_q8(const float * x, const float * w, float * y, void * yq, int64_t rows, int64_t n,
+                               float eps, bool pdl, cudaStream_t st);
+// quantize_row_q8_0 of n fp32 values (n % 32 == 0) -> block_q8_0 [n/32]
+cudaError_t launch_quantize_q8_0(const float * x, void * xq, int64_t n, bool pdl, cudaStream_t st);
+cudaError_t launch_swiglu_q8(const float * g, const float * u, float * y, void * yq, int64_t n, bool pdl,
+                             cudaStream_t st);
 cudaError_t launch_swiglu(const float * g, const float * u, float * y, int64_t n, bool pdl, cudaStream_t st);
 
 // Device-side error word (bounded waits that expire set it; see alb_device_error).

@@ -10,10 +10,9 @@
 //     device: calls that overlap in time (other streams, other host threads)
 //     race on it and must not be issued;
 //   * the first call on a device looks the array up with cudaGetSymbolAddress
-//     (that device current) and clears it with cudaMemsetAsync on the call's
-//     stream (the split-merge tickets at its start must be zero at first use;
-//     every launch re-arms them); make that first call outside any stream
-//     capture.
+//     (that device current) and clears it once with cudaMemsetAsync on the
+//     call's stream (the kernels keep no state in it between calls); make that
+//     first call outside any stream capture.
 #include <mutex>
 
 #include "alb_common.cuh"

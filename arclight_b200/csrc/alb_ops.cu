@@ -99,11 +99,11 @@ k_qk_norm_rope_kv(const float * __restrict__ qkv, int64_t qkv_stride, int Hq, in
 // Softmax is shift invariant, so this is the reference's online softmax with
 // different (and fewer) roundings.
 //
-// Decode / small ubatches split the cells over S CTAs in two kernels:
-// k_fa_scores writes the scores and per-split maxima, k_fa_pv applies the
-// global max, accumulates its split in double and the last CTA of (h, t)
-// (atomic ticket, no spin) adds the S partials in split order.  Large prefill
-// ubatches use k_fa_fused (one CTA per (h, t), scores in shared memory).
+// Decode / small ubatches split the cells over S CTAs: k_fa_scores writes the
+// scores and per-split maxima, k_fa_pv applies the global max and accumulates
+// its split in double, k_fa_merge adds the S partials of each query head in
+// split order (and can emit the block_q8_0 records of the result).  Large
+// prefill ubatches use k_fa_fused (one CTA per (h, t), scores in shared memory).
 static constexpr int FA_TICKETS = 8192;
 
 __device__ __forceinline__ float fa_score(const uint16_t * __restrict__ krow, const float * __restrict__ qg) {
@@ -141,14 +141,16 @@ __device__ __forceinline__ void fa_split(int n, int S, int s, int & c0, int & c1
 
 // Split kernels stream K and V through a shared-memory ring filled by
 // cp.async (FA_NST stages of FA_CH cells, FA_NST - 1 stages in flight), so each
-// CTA keeps tens of KB of HBM reads outstanding while it computes; one cell per
-// thread per stage.  K rows are padded to 272 B in shared memory so the 16-byte
-// row reads of a quarter-warp fall in distinct banks.
-static constexpr int FA_CH = 128;                          // cells per stage (one per thread)
+// CTA keeps tens of KB of HBM reads outstanding while it computes, with ~52 KB
+// of shared memory: four CTAs (16 warps) per SM.  Two threads per cell, each
+// with half of the G query heads.  K rows are padded to 272 B in shared memory
+// so the 16-byte row reads of a quarter-warp fall in distinct banks.
+static constexpr int FA_CH = 64;                           // cells per stage (two threads per cell)
 static constexpr int FA_NST = 3;                           // ring stages
 static constexpr int FA_KPITCH = 272;                      // bytes per staged K row
-static constexpr int FA_KSTAGE = FA_CH * FA_KPITCH;        // 34,816 B
-static constexpr int FA_VSTAGE = FA_CH * 256;              // 32,768 B
+static constexpr int FA_KSTAGE = FA_CH * FA_KPITCH;        // 17,408 B
+static constexpr int FA_VSTAGE = FA_CH * 256;              // 16,384 B
+template <int G> __host__ __device__ constexpr int fa_gh() { return G >= 2 ? 2 : 1; }   // head halves (threads per cell)
 static constexpr size_t FA_SCORES_SMEM = (size_t)FA_NST * FA_KSTAGE;
 template <int G>
 constexpr size_t fa_pv_smem() { return (size_t)FA_NST * (FA_VSTAGE + G * FA_CH * 4); }
@@ -195,23 +197,28 @@ k_fa_scores(const float * __restrict__ q, const uint16_t * __restrict__ kc, int 
 #pragma unroll
     for (int i = 0; i < FA_NST - 1; ++i) issue(i);
     fa_load_q<G>(q, Hq, h, t, qs);
-    float mx[G];
+    constexpr int GH = fa_gh<G>(), GPT = G / GH;
+    const int cl = tid & (FA_CH - 1), gh = tid / FA_CH;   // cell of the stage, head half
+    float mx[GPT];
 #pragma unroll
-    for (int g = 0; g < G; ++g) mx[g] = -INFINITY;
+    for (int k = 0; k < GPT; ++k) mx[k] = -INFINITY;
     float * sc = scores + ((size_t)h * T + t) * G * ncap;
     for (int i = 0; i < nst; ++i) {
         fa_wait_ring();
         __syncthreads();   // stage i visible to all; stage i-1 consumed by all
         issue(i + FA_NST - 1);
-        const int c = c0 + i * FA_CH + tid;
-        if (c < c1) {
-            const uint8_t * kr = fa_ring + (i % FA_NST) * FA_KSTAGE + tid * FA_KPITCH;
-            float a[G];
+        const int c = c0 + i * FA_CH + cl;
+        if (gh < GH && c < c1) {
+            const uint8_t * kr = fa_ring + (i % FA_NST) * FA_KSTAGE + cl * FA_KPITCH;
+            float a[GPT];
 #pragma unroll
-            for (int g = 0; g < G; ++g) a[g] = 0.0f;
-#pragma unroll 4
+            for (int k = 0; k < GPT; ++k) a[k] = 0.0f;
+            uint4 krow[16];   // the whole K row in registers first: 16 independent shared loads
+#pragma unroll
+            for (int j = 0; j < 16; ++j) krow[j] = *reinterpret_cast<const uint4 *>(kr + j * 16);
+#pragma unroll
             for (int j = 0; j < 16; ++j) {   // dims 8j .. 8j+7, in order (the reference's sequential chain)
-                const uint4 kv = *reinterpret_cast<const uint4 *>(kr + j * 16);
+                const uint4 kv = krow[j];
                 const uint32_t wd[4] = {kv.x, kv.y, kv.z, kv.w};
                 float kf[8];
 #pragma unroll
@@ -221,24 +228,25 @@ k_fa_scores(const float * __restrict__ q, const uint16_t * __restrict__ kc, int 
                     kf[2 * e + 1] = f.y;
                 }
 #pragma unroll
-                for (int g = 0; g < G; ++g) {
-                    const float4 qa = *reinterpret_cast<const float4 *>(&qs[g][8 * j]);
-                    const float4 qb = *reinterpret_cast<const float4 *>(&qs[g][8 * j + 4]);
-                    a[g] = __fmaf_rn(kf[0], qa.x, a[g]);
-                    a[g] = __fmaf_rn(kf[1], qa.y, a[g]);
-                    a[g] = __fmaf_rn(kf[2], qa.z, a[g]);
-                    a[g] = __fmaf_rn(kf[3], qa.w, a[g]);
-                    a[g] = __fmaf_rn(kf[4], qb.x, a[g]);
-                    a[g] = __fmaf_rn(kf[5], qb.y, a[g]);
-                    a[g] = __fmaf_rn(kf[6], qb.z, a[g]);
-                    a[g] = __fmaf_rn(kf[7], qb.w, a[g]);
+                for (int k = 0; k < GPT; ++k) {
+                    const float * qg = qs[gh * GPT + k];
+                    const float4 qa = *reinterpret_cast<const float4 *>(qg + 8 * j);
+                    const float4 qb = *reinterpret_cast<const float4 *>(qg + 8 * j + 4);
+                    a[k] = __fmaf_rn(kf[0], qa.x, a[k]);
+                    a[k] = __fmaf_rn(kf[1], qa.y, a[k]);
+                    a[k] = __fmaf_rn(kf[2], qa.z, a[k]);
+                    a[k] = __fmaf_rn(kf[3], qa.w, a[k]);
+                    a[k] = __fmaf_rn(kf[4], qb.x, a[k]);
+                    a[k] = __fmaf_rn(kf[5], qb.y, a[k]);
+                    a[k] = __fmaf_rn(kf[6], qb.z, a[k]);
+                    a[k] = __fmaf_rn(kf[7], qb.w, a[k]);
                 }
             }
 #pragma unroll
-            for (int g = 0; g < G; ++g) {
-                const float v = __fmul_rn(a[g], scale);
-                sc[(size_t)g * ncap + c] = v;
-                mx[g] = fmaxf(mx[g], v);
+            for (int k = 0; k < GPT; ++k) {
+                const float v = __fmul_rn(a[k], scale);
+                sc[(size_t)(gh * GPT + k) * ncap + c] = v;
+                mx[k] = fmaxf(mx[k], v);
             }
         }
     }
@@ -246,7 +254,7 @@ k_fa_scores(const float * __restrict__ q, const uint16_t * __restrict__ kc, int 
     const int lane = tid & 31, warp = tid >> 5;
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-        const float m = alb_warp_max(mx[g]);
+        const float m = alb_warp_max(g / GPT == gh ? mx[g % GPT] : -INFINITY);
         if (lane == 0) red[warp][g] = m;
     }
     __syncthreads();
@@ -257,22 +265,22 @@ k_fa_scores(const float * __restrict__ q, const uint16_t * __restrict__ kc, int 
     alb_pdl_trigger();
 }
 
-// V rows and the split's scores stream through the ring; each stage: every
-// thread turns its cell's G scores into p = v_expf(s - M) (L in double) and
-// p * 2^1008 as a double, then warp w accumulates cells w, w+4, .. with lane
-// owning dims 4*lane .. 4*lane+3: O += (p * 2^1008) * (v * 2^-1008), the V
-// element's bits placed in a double with no conversion instruction (the
-// product is p * v exactly, as fma(p, v, O) in double).
+// V rows and the split's scores stream through the ring; each stage, warp w
+// owns cells w, w+4, .. of the stage: its lanes turn those cells' scores into
+// p = v_expf(s - M) (L in double) and p * 2^1008 as a double, then the warp
+// accumulates the cells with lane owning dims 4*lane .. 4*lane+3:
+// O += (p * 2^1008) * (v * 2^-1008), the V element's bits placed in a double
+// with no conversion instruction (the product is p * v exactly, as fma(p, v, O)
+// in double).  One CTA barrier per stage (the ring), none between the phases.
 template <int G>
 __global__ void __launch_bounds__(128)
 k_fa_pv(const uint16_t * __restrict__ vc, int Hq, int Hkv, int T, int32_t pos0, const int32_t * __restrict__ pos_dev,
         int S, int ncap, const float * __restrict__ scores, const float * __restrict__ smax, double * __restrict__ part,
-        int * __restrict__ tickets, float * __restrict__ out) {
+        float * __restrict__ out) {
     extern __shared__ __align__(16) uint8_t fa_ring[];   // FA_NST x (V rows [FA_CH][256 B] + scores [G][FA_CH])
     __shared__ __align__(16) double pd[FA_CH][G];
     __shared__ float M[G];
     __shared__ double Lred[4][G];
-    __shared__ int last;
     const int h = blockIdx.x, t = blockIdx.y, s = blockIdx.z;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int STAGE = FA_VSTAGE + G * FA_CH * 4;
@@ -307,29 +315,36 @@ k_fa_pv(const uint16_t * __restrict__ vc, int Hq, int Hkv, int T, int32_t pos0, 
         for (int k = 0; k < S; ++k) m = fmaxf(m, smax[(((size_t)h * T + t) * S + k) * G + tid]);
         M[tid] = m;
     }
-    double L[G], O[G][4];
+    constexpr int GL = G >= 2 ? G / 2 : 1;   // heads per lane in the softmax phase
+    double L[GL], O[G][4];
 #pragma unroll
-    for (int g = 0; g < G; ++g) { L[g] = 0.0; O[g][0] = O[g][1] = O[g][2] = O[g][3] = 0.0; }
+    for (int k = 0; k < GL; ++k) L[k] = 0.0;
+#pragma unroll
+    for (int g = 0; g < G; ++g) O[g][0] = O[g][1] = O[g][2] = O[g][3] = 0.0;
     for (int i = 0; i < nst; ++i) {
         fa_wait_ring();
-        __syncthreads();   // stage i visible; stage i-1 and pd consumed by all; M visible
+        __syncthreads();   // stage i visible; stage i-1 consumed by all; M visible
         issue(i + FA_NST - 1);
         const uint8_t * stg = fa_ring + (i % FA_NST) * STAGE;
         const int rows = min(FA_CH, c1 - (c0 + i * FA_CH));
-        {
+        {   // softmax numerators of the rows this warp accumulates (lane: row, head half)
             const float * ss = reinterpret_cast<const float *>(stg + FA_VSTAGE);
+            const int r = warp + 4 * (lane & 15), lh = lane >> 4;
 #pragma unroll
-            for (int g = 0; g < G; ++g) {
-                double v = 0.0;
-                if (tid < rows) {
-                    const float p = alb_ref_expf(__fsub_rn(ss[g * FA_CH + tid], M[g]));
-                    L[g] += (double)p;
-                    v = (double)p * 0x1p1008;
+            for (int k = 0; k < GL; ++k) {
+                const int g = lh * GL + k;
+                if (g < G) {
+                    double v = 0.0;
+                    if (r < rows) {
+                        const float p = alb_ref_expf(__fsub_rn(ss[g * FA_CH + r], M[g]));
+                        L[k] += (double)p;
+                        v = (double)p * 0x1p1008;
+                    }
+                    pd[r][g] = v;
                 }
-                pd[tid][g] = v;
             }
         }
-        __syncthreads();
+        __syncwarp();
         // 16 rows per pass (4 per warp, loads first); rows past the stage's end
         // have p = 0 and finite (possibly stale) V bits, so they add exact zeros.
         for (int r0 = 0; r0 < rows; r0 += 16) {
@@ -369,7 +384,7 @@ k_fa_pv(const uint16_t * __restrict__ vc, int Hq, int Hkv, int T, int32_t pos0, 
     double (*ored)[G][128] = reinterpret_cast<double (*)[G][128]>(fa_ring);   // [4][G][128]
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-        const double l = alb_warp_sum_d(L[g]);
+        const double l = alb_warp_sum_d(g / GL == (lane >> 4) ? L[g % GL] : 0.0);
         if (lane == 0) Lred[warp][g] = l;
 #pragma unroll
         for (int e = 0; e < 4; ++e) ored[warp][g][4 * lane + e] = O[g][e];
@@ -394,24 +409,49 @@ k_fa_pv(const uint16_t * __restrict__ vc, int Hq, int Hkv, int T, int32_t pos0, 
         pp[g * 129 + tid] = Os[g];
         if (tid == 0) pp[g * 129 + 128] = Ls[g];
     }
-    __threadfence();
+    alb_pdl_trigger();
+}
+
+// The S split partials of query head hq = h*G + g, out = O / L.  One CTA of
+// 1024 threads per (hq, t): group j (threads 128j .. 128j+127, thread = dim)
+// adds splits [S*j/8, S*(j+1)/8) in split order, then the 8 group sums are
+// added in group order (a fixed association, the same on every call).  Warp w
+// of group 0 owns dims 32w .. 32w+31 (one Q8_0 block of the output row, lane =
+// dim) and, when xq is given, writes that block's block_q8_0 record
+// (quantize_row_q8_0 of the fp32 result: the o_proj input).
+template <int G>
+__global__ void __launch_bounds__(1024)
+k_fa_merge(const double * __restrict__ part, int Hq, int T, int S, float * __restrict__ out,
+           uint8_t * __restrict__ xq) {
+    constexpr int NG = 8;
+    __shared__ double so[NG][128];
+    __shared__ double sl[NG];
+    const int hq = blockIdx.x, t = blockIdx.y, d = threadIdx.x & 127, j = threadIdx.x >> 7;
+    const int h = hq / G, g = hq - h * G;
+    alb_pdl_wait();
+    const double * base = part + (((size_t)h * T + t) * S * G + g) * 129;   // split k at base + k*G*129
+    constexpr size_t KS = (size_t)G * 129;
+    const int k0 = (int)((int64_t)S * j / NG), k1 = (int)((int64_t)S * (j + 1) / NG);
+    double L = 0.0, O = 0.0;
+    for (int k = k0; k < k1; ++k) { L += base[k * KS + 128]; O += base[k * KS + d]; }
+    so[j][d] = O;
+    if (d == 0) sl[j] = L;
     __syncthreads();
-    if (tid == 0) last = (atomicAdd(&tickets[h * T + t], 1) == S - 1);
-    __syncthreads();
-    if (!last) { alb_pdl_trigger(); return; }
-    __threadfence();
-    const double * base = part + ((size_t)h * T + t) * S * G * 129;
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
+    if (j == 0) {
         double Lt = 0.0, Ot = 0.0;
-        for (int k = 0; k < S; ++k) {
-            const double * pk = base + ((size_t)k * G + g) * 129;
-            Lt += __ldcg(pk + 128);
-            Ot += __ldcg(pk + tid);
+#pragma unroll
+        for (int i = 0; i < NG; ++i) { Lt += sl[i]; Ot += so[i][d]; }
+        const float v = Lt > 0.0 ? __double2float_rn(Ot / Lt) : 0.0f;
+        out[((size_t)t * Hq + hq) * 128 + d] = v;
+        if (xq) {
+            const int lane = d & 31, warp = d >> 5;
+            int8_t q; uint16_t dh;
+            q8_block_lane(v, q, dh);
+            uint8_t * blk = xq + (((size_t)t * Hq + hq) * 4 + warp) * 34;
+            if (lane == 0) *reinterpret_cast<uint16_t *>(blk) = dh;
+            blk[2 + lane] = (uint8_t)q;
         }
-        out[((size_t)t * Hq + h * G + g) * 128 + tid] = Lt > 0.0 ? __double2float_rn(Ot / Lt) : 0.0f;
     }
-    if (tid == 0) tickets[h * T + t] = 0;   // re-arm for the next launch / graph replay
     alb_pdl_trigger();
 }
 
@@ -496,8 +536,8 @@ k_fa_fused(const float * __restrict__ q, const uint16_t * __restrict__ kc, const
     alb_pdl_trigger();
 }
 
-// Workspace: [tickets FA_TICKETS ints | split maxima | scores | split partials (double)].
-// Tickets must be zero at first use; every launch re-arms them.
+// Workspace: [reserved FA_TICKETS ints | split maxima | scores | split partials (double)].
+// Every region is written before it is read within a call (no state between calls).
 struct FaLayout { size_t smax_off, scores_off, part_off, bytes; };
 static FaLayout fa_layout(int Hq, int Hkv, int T, int S, int ncap) {
     const int G = Hq / Hkv;
@@ -517,7 +557,7 @@ size_t flash_attn_ws_bytes(int Hq, int Hkv, int T, int S, int ncap) {
 static constexpr size_t FA_FUSED_SMEM = 160 * 1024;
 
 template <int G>
-static cudaError_t launch_fa_t(const FlashArgs & f, cudaStream_t st) {
+static cudaError_t launch_fa_core(const FlashArgs & f, cudaStream_t st) {
     const int n_max = f.ncap;   // cells attended by the last token at most
     if (f.S == 1 && (size_t)G * n_max * 4 <= FA_FUSED_SMEM) {
         const size_t smem = (size_t)G * n_max * 4;
@@ -532,10 +572,9 @@ static cudaError_t launch_fa_t(const FlashArgs & f, cudaStream_t st) {
                           f.vc, f.Hq, f.Hkv, f.T, f.pos0, f.pos_dev, f.scale, f.out);
     }
     if (!f.ws) return cudaErrorInvalidValue;
-    if ((int64_t)f.Hkv * f.T > FA_TICKETS) return cudaErrorInvalidValue;
+    if (f.T > 65535 || f.S > 65535) return cudaErrorInvalidValue;
     const FaLayout l = fa_layout(f.Hq, f.Hkv, f.T, f.S, f.ncap);
     uint8_t * ws = reinterpret_cast<uint8_t *>(f.ws);
-    int * tickets = reinterpret_cast<int *>(ws);
     float * smax = reinterpret_cast<float *>(ws + l.smax_off);
     float * scores = reinterpret_cast<float *>(ws + l.scores_off);
     double * part = reinterpret_cast<double *>(ws + l.part_off);
@@ -552,8 +591,19 @@ static cudaError_t launch_fa_t(const FlashArgs & f, cudaStream_t st) {
     cudaError_t e = alb_launch(k_fa_scores<G>, grid, dim3(128), FA_SCORES_SMEM, st, f.pdl, f.q, f.kc, f.Hq, f.Hkv, f.T,
                                f.pos0, f.pos_dev, f.scale, f.S, f.ncap, scores, smax);
     if (e != cudaSuccess) return e;
-    return alb_launch(k_fa_pv<G>, grid, dim3(128), fa_pv_smem<G>(), st, f.pdl, f.vc, f.Hq, f.Hkv, f.T, f.pos0,
-                      f.pos_dev, f.S, f.ncap, (const float *)scores, (const float *)smax, part, tickets, f.out);
+    e = alb_launch(k_fa_pv<G>, grid, dim3(128), fa_pv_smem<G>(), st, f.pdl, f.vc, f.Hq, f.Hkv, f.T, f.pos0,
+                   f.pos_dev, f.S, f.ncap, (const float *)scores, (const float *)smax, part, f.out);
+    if (e != cudaSuccess || f.S == 1) return e;
+    return alb_launch(k_fa_merge<G>, dim3((unsigned)f.Hq, (unsigned)f.T), dim3(1024), 0, st, f.pdl,
+                      (const double *)part, f.Hq, f.T, f.S, f.out, static_cast<uint8_t *>(f.xq));
+}
+
+// The split path's merge writes f.xq itself; the one-CTA paths quantize out after.
+template <int G>
+static cudaError_t launch_fa_t(const FlashArgs & f, cudaStream_t st) {
+    const cudaError_t e = launch_fa_core<G>(f, st);
+    if (e != cudaSuccess || !f.xq || f.S > 1) return e;
+    return launch_quantize_q8_0(f.out, f.xq, (int64_t)f.T * f.Hq * 128, f.pdl, st);
 }
 
 cudaError_t launch_flash_attn(const FlashArgs & f, cudaStream_t st) {
@@ -666,6 +716,76 @@ __global__ void k_swiglu(const float * __restrict__ g, const float * __restrict_
     alb_pdl_wait();
     if (i < n) y[i] = alb_swiglu1(g[i], u[i]);
     alb_pdl_trigger();
+}
+
+// RMSNorm (+ MUL by w) then quantize_row_q8_0 of the result (arm.cpp:1819-1853):
+// CTA (row, j) forms the row's sum of squares (every CTA of the row in the same
+// order) and warp w quantizes block 8j + w of the normalized row (lane =
+// element), so the Q8_0 records are those of the fp32 values y.
+__global__ void __launch_bounds__(256)
+k_rms_norm_q8(const float * __restrict__ x, const float * __restrict__ w, float * __restrict__ y,
+              uint8_t * __restrict__ yq, int64_t n, float eps) {
+    const float * xr = x + (size_t)blockIdx.x * n;
+    __shared__ double red[8];
+    alb_pdl_wait();
+    double s = 0.0;
+    for (int64_t i = threadIdx.x; i < n; i += 256) { const float v = xr[i]; s += (double)__fmul_rn(v, v); }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    double t = 0.0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t += red[i];
+    const float mean = (float)(t / (double)n);
+    const float scale = 1.0f / sqrtf(__fadd_rn(mean, eps));
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t nb = n / 32;
+    uint8_t * qr = yq + (size_t)blockIdx.x * nb * 34;
+    const int64_t b = (int64_t)blockIdx.y * 8 + warp;
+    if (b < nb) {
+        const int64_t i = b * 32 + lane;
+        float v = __fmul_rn(xr[i], scale);
+        if (w) v = __fmul_rn(v, w[i]);
+        if (y) y[(size_t)blockIdx.x * n + i] = v;
+        int8_t q; uint16_t dh;
+        q8_block_lane(v, q, dh);
+        if (lane == 0) *reinterpret_cast<uint16_t *>(qr + b * 34) = dh;
+        qr[b * 34 + 2 + lane] = (uint8_t)q;
+    }
+    alb_pdl_trigger();
+}
+
+// swiglu (ops.cpp:1038-1092) then quantize_row_q8_0 of the product: one warp per block.
+__global__ void __launch_bounds__(256)
+k_swiglu_q8(const float * __restrict__ g, const float * __restrict__ u, float * __restrict__ y,
+            uint8_t * __restrict__ yq, int64_t n_blocks) {
+    const int64_t b = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    alb_pdl_wait();
+    if (b < n_blocks) {
+        const int64_t i = b * 32 + lane;
+        const float v = alb_swiglu1(g[i], u[i]);
+        if (y) y[i] = v;
+        int8_t q; uint16_t dh;
+        q8_block_lane(v, q, dh);
+        if (lane == 0) *reinterpret_cast<uint16_t *>(yq + b * 34) = dh;
+        yq[b * 34 + 2 + lane] = (uint8_t)q;
+    }
+    alb_pdl_trigger();
+}
+
+cudaError_t launch_rms_norm_q8(const float * x, const float * w, float * y, void * yq, int64_t rows, int64_t n,
+                               float eps, bool pdl, cudaStream_t st) {
+    return alb_launch(k_rms_norm_q8, dim3((unsigned)rows, (unsigned)((n / 32 + 7) / 8)), dim3(256), 0, st, pdl, x,
+                      w, y, static_cast<uint8_t *>(yq), n, eps);
+}
+
+cudaError_t launch_swiglu_q8(const float * g, const float * u, float * y, void * yq, int64_t n, bool pdl,
+                             cudaStream_t st) {
+    const int64_t nb = n / 32;
+    return alb_launch(k_swiglu_q8, dim3((unsigned)((nb + 7) / 8)), dim3(256), 0, st, pdl, g, u, y,
+                      static_cast<uint8_t *>(yq), nb);
 }
 
 cudaError_t launch_embed(const uint8_t * Wn, const uint8_t * Ws, int64_t vocab, int64_t E, const int32_t * tokens,

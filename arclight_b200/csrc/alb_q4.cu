@@ -62,12 +62,21 @@ __global__ void k_unpack_q4_0(uint8_t * __restrict__ dst, const uint8_t * __rest
 __global__ void k_quantize_q8_0(const float * __restrict__ x, uint8_t * __restrict__ y, int64_t n_blocks) {
     const int64_t b = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
-    if (b >= n_blocks) return;
-    int8_t q; uint16_t dh;
-    q8_block_lane(x[b * 32 + lane], q, dh);
-    uint8_t * blk = y + b * 34;
-    if (lane == 0) *reinterpret_cast<uint16_t *>(blk) = dh;
-    blk[2 + lane] = (uint8_t)q;
+    alb_pdl_wait();
+    if (b < n_blocks) {
+        int8_t q; uint16_t dh;
+        q8_block_lane(x[b * 32 + lane], q, dh);
+        uint8_t * blk = y + b * 34;
+        if (lane == 0) *reinterpret_cast<uint16_t *>(blk) = dh;
+        blk[2 + lane] = (uint8_t)q;
+    }
+    alb_pdl_trigger();
+}
+
+cudaError_t launch_quantize_q8_0(const float * x, void * xq, int64_t n, bool pdl, cudaStream_t st) {
+    const int64_t nb = n / 32;
+    return alb_launch(k_quantize_q8_0, dim3((unsigned)((nb + 7) / 8)), dim3(256), 0, st, pdl, x,
+                      static_cast<uint8_t *>(xq), nb);
 }
 
 // CONSUMERS_ONLY: synchronise the GEMV_WARPS consumer warps with named barrier 1

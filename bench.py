@@ -390,7 +390,7 @@ def run_attn(args, rank, world):
     torch.cuda.set_device(dev)
     A.check(L.alb_device_check(local), "device check")
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    S = (2 * sms + ATT_HKV - 1) // ATT_HKV          # the engine's decode split count
+    S = (4 * sms + ATT_HKV - 1) // ATT_HKV          # the engine's decode split count
     gen = torch.Generator(device=dev).manual_seed(7)
     kc = torch.randn((ATT_COPIES, ATT_CELLS, ATT_HKV, 128), generator=gen, device=dev).half()
     vc = torch.randn((ATT_COPIES, ATT_CELLS, ATT_HKV, 128), generator=gen, device=dev).half()
@@ -419,7 +419,7 @@ def run_attn(args, rank, world):
     reps = max(1, args.steps // ATT_COPIES)
     steps = reps * ATT_COPIES
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    with ClockSampler(local) as clk, torch.cuda.stream(s):   # replays and events on the same stream
         for _ in range(max(args.warmup, 3)):
             g.replay()
         torch.cuda.synchronize()

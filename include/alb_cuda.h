@@ -97,6 +97,14 @@ ALB_API int alb_gemv_q4_0_q8_0_block_dots(const void * W, const void * xq, int32
 ALB_API int alb_rms_norm(const float * x, const float * w, float * y, int64_t rows, int64_t n, float eps, void * stream);
 /* swiglu_split (ops.cpp:1038-1092, arm.cpp:1789-1809): y = silu(g) * u. */
 ALB_API int alb_swiglu(const float * g, const float * u, float * y, int64_t n, void * stream);
+/* rms_norm_f32 + MUL (as alb_rms_norm) fused with quantize_row_q8_0
+ * (arm.cpp:1819-1853) of the result: yq [rows][n/32] block_q8_0, the input of
+ * the next mat-vec / mat-mul; y (fp32 result) may be NULL; n % 32 == 0. */
+ALB_API int alb_rms_norm_q8(const float * x, const float * w, float * y, void * yq, int64_t rows, int64_t n,
+                            float eps, void * stream);
+/* alb_swiglu fused with quantize_row_q8_0 of the product (the down
+ * projection's input); y may be NULL; n % 32 == 0. */
+ALB_API int alb_swiglu_q8(const float * g, const float * u, float * y, void * yq, int64_t n, void * stream);
 /* GET_ROWS of a Q4_0 table in the alb GPU layout (ops.cpp:12-52): out [n_ids][K]. */
 ALB_API int alb_get_rows_q4_0(const void * W, int64_t n_rows, int64_t K, const int32_t * ids, int64_t n_ids,
                               float * out, void * stream);
@@ -118,9 +126,9 @@ ALB_API int alb_qk_norm_rope_kv(const float * qkv, int64_t T, int32_t n_head, in
  * are fp32 (Q rounded to fp16 as the reference), the softmax uses the global
  * max and the reference's NEON exp, sums are double: the result does not depend
  * on `splits` (the cells are split over that many CTAs and merged in-kernel).
- * Workspace: alb_flash_attn_workspace_bytes(.., n_cells = pos0 + T); zeroed
- * once before first use (its tickets are re-armed by every call); may be NULL
- * when splits == 1 and 4 * (n_head/n_head_kv) * (pos0+T) <= 160 KiB.  q/out [T][Hq][128]. */
+ * Workspace: alb_flash_attn_workspace_bytes(.., n_cells = pos0 + T) (no
+ * state kept between calls); may be NULL when splits == 1 and
+ * 4 * (n_head/n_head_kv) * (pos0+T) <= 160 KiB.  q/out [T][Hq][128]. */
 ALB_API size_t alb_flash_attn_workspace_bytes(int32_t n_head, int32_t n_head_kv, int64_t T, int32_t splits,
                                              int32_t n_cells);
 ALB_API int alb_flash_attn(const float * q, const uint16_t * k_cache, const uint16_t * v_cache, int64_t T,
@@ -161,6 +169,16 @@ typedef struct {
 
 /* ncclGetUniqueId for tensor-parallel engines (128 bytes). */
 ALB_API int alb_nccl_unique_id(void * out128);
+/* Tensor-parallel communicator for the op-level ABI (NCCL, one per rank and
+ * device).  The reference's GATHER of node partials (ops.cpp:1465-1511):
+ * alb_allreduce_sum_f32 (dst = sum over ranks, NCCL's order) or
+ * alb_allgather_f32 (dst [size][n], rank r's src at dst + r*n, for an ordered
+ * sum on the device).  Stream-ordered; every rank makes the same calls. */
+typedef struct alb_comm alb_comm;
+ALB_API int alb_comm_create(const void * nccl_id, int32_t rank, int32_t size, int32_t device, alb_comm ** out);
+ALB_API int alb_comm_destroy(alb_comm * comm);
+ALB_API int alb_allreduce_sum_f32(alb_comm * comm, const float * src, float * dst, int64_t n, void * stream);
+ALB_API int alb_allgather_f32(alb_comm * comm, const float * src, float * dst, int64_t n, void * stream);
 /* al-gen.cpp:60-141 setup: weights, KV cache [max_ctx] and buffers for ubatches
  * of up to max_ubatch tokens on CUDA device `device`; tp_size > 1 joins the
  * NCCL clique `nccl_id` as tp_rank (n_head, n_head_kv, n_vocab divisible by

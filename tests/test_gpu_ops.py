@@ -51,6 +51,47 @@ def test_swiglu():
     np.testing.assert_array_equal(Y.cpu().numpy(), O.swiglu(g, u))
 
 
+@pytest.mark.parametrize("rows,n", [(1, 2560), (3, 4096), (2, 12288), (5, 64)])
+def test_rms_norm_q8(rows, n):
+    """Fused RMSNorm -> Q8_0: the fp32 rows equal alb_rms_norm's, the records
+    equal the oracle's quantize_row_q8_0 of those rows byte for byte."""
+    rng = np.random.default_rng(3 * n + rows)
+    x = (rng.standard_normal((rows, n)) * 3).astype(np.float32)
+    x[0, :32] = 0.0                                   # an all-zero block
+    w = (1 + 0.01 * rng.standard_normal(n)).astype(np.float32)
+    X, W = cu(x), cu(w)
+    Y, Y0 = torch.empty_like(X), torch.empty_like(X)
+    Q = torch.empty(rows * (n // 32) * 34, dtype=torch.uint8, device="cuda")
+    A.check(L.alb_rms_norm_q8(X.data_ptr(), W.data_ptr(), Y.data_ptr(), Q.data_ptr(), rows, n, 1e-6, st()))
+    A.check(L.alb_rms_norm(X.data_ptr(), W.data_ptr(), Y0.data_ptr(), rows, n, 1e-6, st()))
+    torch.cuda.synchronize()
+    y = Y.cpu().numpy()
+    np.testing.assert_array_equal(y, Y0.cpu().numpy())
+    assert_rel(y, O.rms_norm(x, w), rtol=1e-6, what="rms_norm_q8 rows")
+    ref = O.quantize_q8_0(y).view(np.uint8).reshape(-1)
+    np.testing.assert_array_equal(Q.cpu().numpy(), ref)
+    # the fp32 copy is optional
+    Q2 = torch.empty_like(Q)
+    A.check(L.alb_rms_norm_q8(X.data_ptr(), W.data_ptr(), None, Q2.data_ptr(), rows, n, 1e-6, st()))
+    torch.cuda.synchronize()
+    assert torch.equal(Q, Q2)
+
+
+def test_swiglu_q8():
+    rng = np.random.default_rng(8)
+    n = 12288
+    g = (rng.standard_normal(n) * 4).astype(np.float32)
+    u = rng.standard_normal(n).astype(np.float32)
+    G, U = cu(g), cu(u)
+    Y = torch.empty(n, dtype=torch.float32, device="cuda")
+    Q = torch.empty((n // 32) * 34, dtype=torch.uint8, device="cuda")
+    A.check(L.alb_swiglu_q8(G.data_ptr(), U.data_ptr(), Y.data_ptr(), Q.data_ptr(), n, st()))
+    torch.cuda.synchronize()
+    y = O.swiglu(g, u)
+    np.testing.assert_array_equal(Y.cpu().numpy(), y)
+    np.testing.assert_array_equal(Q.cpu().numpy(), O.quantize_q8_0(y).view(np.uint8).reshape(-1))
+
+
 def test_get_rows_bit_exact():
     rng = np.random.default_rng(2)
     tab = O.quantize_q4_0((rng.standard_normal((1000, 256)) * 0.02).astype(np.float32))

@@ -84,3 +84,56 @@ def test_tp_matches_oracle_tp(cfg, tp):
     logits = np.concatenate([res[r][1] for r in range(tp)])   # vocabulary shards in rank order
     assert logits.shape == lg.shape
     np.testing.assert_array_equal(logits, lg)
+
+
+def _comm_rank_main(rank, size, nid, q):
+    try:
+        import ctypes as C
+        import torch as T
+        import arclight_b200 as A
+        L = A.lib()
+        T.cuda.set_device(rank)
+        comm = C.c_void_p()
+        A.check(L.alb_comm_create(nid, rank, size, rank, C.byref(comm)), "alb_comm_create")
+        n = 10240
+        x = T.arange(n, dtype=T.float32, device="cuda") * (rank + 1) + 0.25
+        red = T.empty_like(x)
+        gat = T.empty(size * n, dtype=T.float32, device="cuda")
+        s = T.cuda.current_stream().cuda_stream
+        A.check(L.alb_allreduce_sum_f32(comm, x.data_ptr(), red.data_ptr(), n, s), "allreduce")
+        A.check(L.alb_allgather_f32(comm, x.data_ptr(), gat.data_ptr(), n, s), "allgather")
+        T.cuda.synchronize()
+        q.put((rank, red.cpu().numpy(), gat.cpu().numpy()))
+        A.check(L.alb_comm_destroy(comm), "alb_comm_destroy")
+    except Exception as ex:
+        q.put((rank, None, repr(ex)))
+
+
+def test_comm_allreduce_and_allgather():
+    """The op-level communicator ABI: sum all-reduce and rank-ordered all-gather."""
+    size = 2
+    if torch.cuda.device_count() < size:
+        pytest.skip(f"needs {size} GPUs")
+    from arclight_b200.engine import nccl_unique_id
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    nid = nccl_unique_id()
+    procs = [ctx.Process(target=_comm_rank_main, args=(r, size, nid, q)) for r in range(size)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in range(size):
+            r, red, gat = q.get(timeout=300)
+            assert red is not None, f"rank {r}: {gat}"
+            res[r] = (red, gat)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    n = 10240
+    parts = [np.arange(n, dtype=np.float32) * (r + 1) + np.float32(0.25) for r in range(size)]
+    for r in range(size):
+        np.testing.assert_array_equal(res[r][0], parts[0] + parts[1])
+        np.testing.assert_array_equal(res[r][1], np.concatenate(parts))
