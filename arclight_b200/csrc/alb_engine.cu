@@ -144,10 +144,13 @@ static int engine_forward(alb_engine * e, int64_t T, bool pdl, int ncap_prefill 
         a.in_mode = in; a.x = x; a.norm_w = nw; a.eps = c.eps;
         a.out_mode = out; a.y = y; a.residual = res; a.pdl = pdl;
         ++launches;
-        if (T == 1 && in == GEMV_IN_Q8) return launch_gemv(a, st);   // records already in x
+        // decode: records already in x (attention merge), or, for K <= 2560, RMSNorm
+        // + quantization in the mat-vec's prologue (overlapping its first weight
+        // loads; measured the cheaper of the two there, not at K = 4096)
+        if (T == 1 && (in == GEMV_IN_Q8 || (in == GEMV_IN_F32_RMS && K <= 2560))) return launch_gemv(a, st);
         if (T == 1) {
-            // the input quantized once (RMSNorm fused), so every CTA of the mat-vec
-            // stages the block_q8_0 records instead of re-quantizing the vector
+            // otherwise the input is quantized once (RMSNorm fused) and the CTAs of
+            // the mat-vec stage its block_q8_0 records
             const cudaError_t qe = in == GEMV_IN_F32_RMS
                 ? launch_rms_norm_q8(static_cast<const float *>(x), nw, nullptr, e->xq, 1, K, c.eps, pdl, st)
                 : launch_quantize_q8_0(static_cast<const float *>(x), e->xq, K, pdl, st);
@@ -205,14 +208,12 @@ static int engine_forward(alb_engine * e, int64_t T, bool pdl, int ncap_prefill 
     }
     // final norm + lm_head on the last token (qwen3.cpp:235-238, 266-274)
     {
-        ALB_CUDA_TRY(launch_rms_norm_q8(e->x + (size_t)(T - 1) * e->E, e->out_norm, nullptr, e->xq, 1, e->E, c.eps,
-                                        pdl, st));
         GemvArgs a;
         a.W = e->lm_W; a.S = e->lm_S; a.N = e->V; a.K = e->E;
-        a.in_mode = GEMV_IN_Q8; a.x = e->xq; a.eps = c.eps;
+        a.in_mode = GEMV_IN_F32_RMS; a.x = e->x + (size_t)(T - 1) * e->E; a.norm_w = e->out_norm; a.eps = c.eps;
         a.out_mode = GEMV_OUT_PLAIN; a.y = e->logits; a.pdl = pdl;
         ALB_CUDA_TRY(launch_gemv(a, st));
-        launches += 2;
+        ++launches;
     }
     if (e->tp == 1) {
         ALB_CUDA_TRY(launch_argmax(e->logits, e->V, 0, e->am_scratch, e->key, e->next_dev, pdl, st));
@@ -377,8 +378,9 @@ static int engine_init_acts(alb_engine * e) {
 
 // Parameters and scratch of the persistent decode-step kernel.
 static int engine_init_mk(alb_engine * e) {
+    // opt-in (ALB_DECODE_MK=1): the one-graph multi-kernel step is the faster decode path
     const char * env = getenv("ALB_DECODE_MK");
-    if (e->tp != 1 || (env && atoi(env) == 0)) return ALB_OK;
+    if (e->tp != 1 || !env || atoi(env) == 0) return ALB_OK;
     const int ncta = alb_sm_count();
     const int G = e->Hq / e->Hkv;
     if (G > 4) return ALB_OK;

@@ -132,6 +132,15 @@ __device__ __forceinline__ void fa_load_q(const float * __restrict__ q, int Hq, 
     }
 }
 
+// Splits in use for n cells: at most S, at least FA_MIN_SPLIT cells each (short
+// contexts use fewer CTAs and the merge adds fewer partials).  Computed on the
+// device from the position, so a captured graph serves every context length.
+static constexpr int FA_MIN_SPLIT = 128;
+__device__ __forceinline__ int fa_splits_used(int n, int S) {
+    const int m = (n + FA_MIN_SPLIT - 1) / FA_MIN_SPLIT;
+    return m < 1 ? 1 : (m < S ? m : S);
+}
+
 __device__ __forceinline__ void fa_split(int n, int S, int s, int & c0, int & c1) {
     int sz = (n + S - 1) / S;
     c0 = s * sz;
@@ -178,8 +187,10 @@ k_fa_scores(const float * __restrict__ q, const uint16_t * __restrict__ kc, int 
     const int h = blockIdx.x, t = blockIdx.y, s = blockIdx.z, tid = threadIdx.x;
     alb_pdl_wait();
     const int n = (pos_dev ? pos_dev[0] : pos0) + t + 1;
+    const int Su = fa_splits_used(n, S);
+    if (s >= Su) return;
     int c0, c1;
-    fa_split(n, S, s, c0, c1);
+    fa_split(n, Su, s, c0, c1);
     const int64_t row = (int64_t)Hkv * 128;
     const uint16_t * kb = kc + (size_t)h * 128;
     const int nst = (c1 - c0 + FA_CH - 1) / FA_CH;
@@ -286,8 +297,10 @@ k_fa_pv(const uint16_t * __restrict__ vc, int Hq, int Hkv, int T, int32_t pos0, 
     constexpr int STAGE = FA_VSTAGE + G * FA_CH * 4;
     alb_pdl_wait();
     const int n = (pos_dev ? pos_dev[0] : pos0) + t + 1;
+    const int Su = fa_splits_used(n, S);
+    if (s >= Su) return;
     int c0, c1;
-    fa_split(n, S, s, c0, c1);
+    fa_split(n, Su, s, c0, c1);
     const int64_t row = (int64_t)Hkv * 128;
     const uint16_t * vb = vc + (size_t)h * 128;
     const float * sc = scores + ((size_t)h * T + t) * G * ncap;
@@ -312,7 +325,7 @@ k_fa_pv(const uint16_t * __restrict__ vc, int Hq, int Hkv, int T, int32_t pos0, 
     for (int i = 0; i < FA_NST - 1; ++i) issue(i);
     if (tid < G) {
         float m = -INFINITY;
-        for (int k = 0; k < S; ++k) m = fmaxf(m, smax[(((size_t)h * T + t) * S + k) * G + tid]);
+        for (int k = 0; k < Su; ++k) m = fmaxf(m, smax[(((size_t)h * T + t) * S + k) * G + tid]);
         M[tid] = m;
     }
     constexpr int GL = G >= 2 ? G / 2 : 1;   // heads per lane in the softmax phase
@@ -414,15 +427,15 @@ k_fa_pv(const uint16_t * __restrict__ vc, int Hq, int Hkv, int T, int32_t pos0, 
 
 // The S split partials of query head hq = h*G + g, out = O / L.  One CTA of
 // 1024 threads per (hq, t): group j (threads 128j .. 128j+127, thread = dim)
-// adds splits [S*j/8, S*(j+1)/8) in split order, then the 8 group sums are
+// adds splits [Su*j/8, Su*(j+1)/8) of the Su in use in split order, then the 8 group sums are
 // added in group order (a fixed association, the same on every call).  Warp w
 // of group 0 owns dims 32w .. 32w+31 (one Q8_0 block of the output row, lane =
 // dim) and, when xq is given, writes that block's block_q8_0 record
 // (quantize_row_q8_0 of the fp32 result: the o_proj input).
 template <int G>
 __global__ void __launch_bounds__(1024)
-k_fa_merge(const double * __restrict__ part, int Hq, int T, int S, float * __restrict__ out,
-           uint8_t * __restrict__ xq) {
+k_fa_merge(const double * __restrict__ part, int Hq, int T, int S, int32_t pos0, const int32_t * __restrict__ pos_dev,
+           float * __restrict__ out, uint8_t * __restrict__ xq) {
     constexpr int NG = 8;
     __shared__ double so[NG][128];
     __shared__ double sl[NG];
@@ -431,7 +444,8 @@ k_fa_merge(const double * __restrict__ part, int Hq, int T, int S, float * __res
     alb_pdl_wait();
     const double * base = part + (((size_t)h * T + t) * S * G + g) * 129;   // split k at base + k*G*129
     constexpr size_t KS = (size_t)G * 129;
-    const int k0 = (int)((int64_t)S * j / NG), k1 = (int)((int64_t)S * (j + 1) / NG);
+    const int Su = fa_splits_used((pos_dev ? pos_dev[0] : pos0) + t + 1, S);
+    const int k0 = (int)((int64_t)Su * j / NG), k1 = (int)((int64_t)Su * (j + 1) / NG);
     double L = 0.0, O = 0.0;
     for (int k = k0; k < k1; ++k) { L += base[k * KS + 128]; O += base[k * KS + d]; }
     so[j][d] = O;
@@ -595,7 +609,7 @@ static cudaError_t launch_fa_core(const FlashArgs & f, cudaStream_t st) {
                    f.pos_dev, f.S, f.ncap, (const float *)scores, (const float *)smax, part, f.out);
     if (e != cudaSuccess || f.S == 1) return e;
     return alb_launch(k_fa_merge<G>, dim3((unsigned)f.Hq, (unsigned)f.T), dim3(1024), 0, st, f.pdl,
-                      (const double *)part, f.Hq, f.T, f.S, f.out, static_cast<uint8_t *>(f.xq));
+                      (const double *)part, f.Hq, f.T, f.S, f.pos0, f.pos_dev, f.out, static_cast<uint8_t *>(f.xq));
 }
 
 // The split path's merge writes f.xq itself; the one-CTA paths quantize out after.

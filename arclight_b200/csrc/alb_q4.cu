@@ -115,13 +115,36 @@ __device__ __forceinline__ void gemv_prologue_impl(const GemvArgs & a, int * xs,
             rec[9] = sum;
         }
     } else {
+        // x (and the norm weights) staged in shared memory with 16-byte copies,
+        // then the sum of squares in a 256-thread strided order and the blocks
+        // quantized from shared memory (no dependent global loads per block)
         const float * x = static_cast<const float *>(a.x);
+        float * xf = reinterpret_cast<float *>(stage);
+        float * wf = xf + a.K;   // RMS only
+        const int K = (int)a.K;
+        const bool vec = (K & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+                         (IN != GEMV_IN_F32_RMS || (reinterpret_cast<uintptr_t>(a.norm_w) & 15) == 0);
+        if (vec) {
+            const float4 * x4 = reinterpret_cast<const float4 *>(x);
+            const float4 * w4 = reinterpret_cast<const float4 *>(a.norm_w);
+            for (int i = tid; i < K / 4; i += GEMV_WARPS * 32) {
+                reinterpret_cast<float4 *>(xf)[i] = x4[i];
+                if constexpr (IN == GEMV_IN_F32_RMS) reinterpret_cast<float4 *>(wf)[i] = w4[i];
+            }
+        } else {
+            for (int i = tid; i < K; i += GEMV_WARPS * 32) {
+                xf[i] = x[i];
+                if constexpr (IN == GEMV_IN_F32_RMS) wf[i] = a.norm_w[i];
+            }
+        }
+        if constexpr (CONSUMERS_ONLY) asm volatile("bar.sync 1, %0;" :: "n"(GEMV_WARPS * 32) : "memory");
+        else __syncthreads();
         float scale = 1.0f;
         if constexpr (IN == GEMV_IN_F32_RMS) {
             // sum of float squares accumulated in double (ops.cpp:703-710)
             __shared__ double red[GEMV_WARPS];
             double s = 0.0;
-            for (int i = tid; i < a.K; i += GEMV_WARPS * 32) { const float v = x[i]; s += (double)__fmul_rn(v, v); }
+            for (int i = tid; i < K; i += GEMV_WARPS * 32) { const float v = xf[i]; s += (double)__fmul_rn(v, v); }
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
             if (lane == 0) red[warp] = s;
@@ -134,13 +157,21 @@ __device__ __forceinline__ void gemv_prologue_impl(const GemvArgs & a, int * xs,
             scale = 1.0f / sqrtf(__fadd_rn(mean, a.eps));
         }
         for (int b = warp; b < nb; b += GEMV_WARPS) {
-            float v = x[b * 32 + lane];
-            if constexpr (IN == GEMV_IN_F32_RMS) v = __fmul_rn(__fmul_rn(v, scale), a.norm_w[b * 32 + lane]);
+            float v = xf[b * 32 + lane];
+            if constexpr (IN == GEMV_IN_F32_RMS) v = __fmul_rn(__fmul_rn(v, scale), wf[b * 32 + lane]);
             int8_t q; uint16_t dh;
             q8_block_lane(v, q, dh);
             store_xrec(xs, b, lane, q, dh);
         }
     }
+}
+
+// Shared memory after the activation records: the raw block_q8_0 vector
+// (IN_Q8) or the fp32 input (and norm weights) of the prologue.
+__host__ __device__ inline size_t gemv_stage_bytes(int64_t K, int in_mode) {
+    const size_t q8 = ((size_t)(K / 32) * 34 + 15) / 16 * 16;
+    const size_t f32 = in_mode == GEMV_IN_F32 ? (size_t)K * 4 : in_mode == GEMV_IN_F32_RMS ? (size_t)K * 8 : 0;
+    return q8 > f32 ? q8 : f32;
 }
 
 template <int IN>
@@ -273,7 +304,7 @@ struct TmaPlan {
     size_t smem;
 };
 
-__host__ __device__ inline TmaPlan tma_plan(int64_t K, int rpw, int max_stage_budget) {
+__host__ __device__ inline TmaPlan tma_plan(int64_t K, int rpw, int max_stage_budget, int in_mode) {
     TmaPlan p;
     const int64_t nb = K / 32;
     p.rs = GEMV_WARPS * rpw;
@@ -283,7 +314,7 @@ __host__ __device__ inline TmaPlan tma_plan(int64_t K, int rpw, int max_stage_bu
     p.ns = (int)(max_stage_budget / p.stage_bytes);
     if (p.ns < 2) p.ns = 2;
     if (p.ns > 8) p.ns = 8;
-    p.xs_bytes = (uint32_t)(nb * XREC_INTS * 4 + ((nb * 34 + 15) / 16) * 16);
+    p.xs_bytes = (uint32_t)(nb * XREC_INTS * 4 + gemv_stage_bytes(K, in_mode));
     p.smem = (size_t)p.ns * p.stage_bytes + p.xs_bytes + 2 * 8 * p.ns;
     return p;
 }
@@ -403,7 +434,7 @@ static cudaError_t launch_gemv_t(const GemvArgs & a, cudaStream_t stream) {
     const bool direct = (OUT == GEMV_OUT_DOTS) || a.variant != 2;
     if (direct) {
         auto kern = k_gemv_direct<ITERS, RPW, IN, OUT>;
-        const size_t smem = (size_t)nb * XREC_INTS * 4 + ((size_t)nb * 34 + 15) / 16 * 16;
+        const size_t smem = (size_t)nb * XREC_INTS * 4 + gemv_stage_bytes(a.K, IN);
         static size_t attr_smem = 0;   // per instantiation
         if (smem > 48 * 1024 && smem > attr_smem) {
             cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -417,7 +448,7 @@ static cudaError_t launch_gemv_t(const GemvArgs & a, cudaStream_t stream) {
         return alb_launch(kern, dim3((unsigned)grid), dim3(GEMV_WARPS * 32), smem, stream, a.pdl, a);
     }
     auto kern = k_gemv_tma<ITERS, RPW, IN, OUT>;
-    const TmaPlan plan = tma_plan(a.K, RPW, a.stage_budget > 0 ? a.stage_budget : 88 * 1024);
+    const TmaPlan plan = tma_plan(a.K, RPW, a.stage_budget > 0 ? a.stage_budget : 88 * 1024, IN);
     static size_t attr_smem = 0;
     if (plan.smem > attr_smem) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan.smem);
