@@ -357,6 +357,9 @@ LONG_CTX = 32768
 # ----------------------------------------------------------------- attention alone (config 5 shape)
 ATT_HQ, ATT_HKV, ATT_CELLS, ATT_COPIES = 32, 8, 32768, 4
 ATT_BYTES = 2 * ATT_CELLS * ATT_HKV * 128 * 2 + 2 * ATT_HQ * 128 * 4   # K + V + q + out per call
+# DRAM bytes per call from one ncu capture of the three kernels (scores 68.21 MB,
+# PV 72.78 MB, merge 2.46 MB; caches flushed between kernels by ncu)
+ATT_TRAFFIC = 143.45e6
 
 
 def cpu_attn_baseline(seconds: float = 10.0):
@@ -461,11 +464,13 @@ def run_attn(args, rank, world):
         "config": {"workload": "config5_attention", "n_head": ATT_HQ, "n_head_kv": ATT_HKV, "cells": ATT_CELLS,
                    "splits": S, "kv_copies": ATT_COPIES, "l2": "inputs larger than L2: 4 rotating caches (512 MB)"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": achieved / peaks["hbm_gbs"], "traffic": None, "peak_src": peaks["src"],
-                     "kernel": "k_fa_scores + k_fa_pv (one call)", "algorithmic_bytes_per_launch": ATT_BYTES},
+                     "frac": achieved / peaks["hbm_gbs"], "traffic": ATT_TRAFFIC, "peak_src": peaks["src"],
+                     "traffic_src": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the three kernels of one call",
+                     "kernel": "k_fa_scores + k_fa_pv + k_fa_merge (one call)",
+                     "algorithmic_bytes_per_launch": ATT_BYTES},
         "e2e": {"value": ATT_BYTES / (e2e_ms * 1e-3) / 1e9 * world, "unit": "GB/s",
                 "h2d_bytes_per_step": ATT_HQ * 128 * 4, "d2h_bytes_per_step": ATT_HQ * 128 * 4},
-        "gpu_launches": 2 * steps,
+        "gpu_launches": 3 * steps,
         "clocks": clk.summary(),
     }
 
