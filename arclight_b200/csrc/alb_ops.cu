@@ -99,11 +99,12 @@ k_qk_norm_rope_kv(const float * __restrict__ qkv, int64_t qkv_stride, int Hq, in
 // Softmax is shift invariant, so this is the reference's online softmax with
 // different (and fewer) roundings.
 //
-// Decode / small ubatches split the cells over S CTAs: k_fa_scores writes the
-// scores and per-split maxima, k_fa_pv applies the global max and accumulates
-// its split in double, k_fa_merge adds the S partials of each query head in
-// split order (and can emit the block_q8_0 records of the result).  Large
-// prefill ubatches use k_fa_fused (one CTA per (h, t), scores in shared memory).
+// Decode splits the cells over S CTAs: k_fa_scores writes the scores and
+// per-split maxima, k_fa_pv applies the global max and accumulates its split in
+// double, k_fa_merge adds the S partials of each query head in split order (and
+// can emit the block_q8_0 records of the result).  Prefill ubatches (T > 1, one
+// split) use k_fa_prefill (token tiles over staged cells); k_fa_fused (one CTA
+// per (h, t), scores in shared memory) serves single-split single-token calls.
 static constexpr int FA_TICKETS = 8192;
 
 __device__ __forceinline__ float fa_score(const uint16_t * __restrict__ krow, const float * __restrict__ qg) {
@@ -469,6 +470,193 @@ k_fa_merge(const double * __restrict__ part, int Hq, int T, int S, int32_t pos0,
     alb_pdl_trigger();
 }
 
+// Prefill attention (ubatches of T > 1 tokens): one CTA per (KV head h, tile of
+// TQ = 64/G tokens) computes the 64 rows (row r: token t0 + r/G, query head
+// h*G + r%G) over K/V stages of 64 cells brought by cp.async (double-buffered),
+// so each staged cell serves 64 rows instead of one.  Same arithmetic as the
+// decode kernels: every score is the sequential fp32 fma chain over d of the
+// fp16-rounded q (16 chains per thread: one cell, 16 rows); pass 1 takes the
+// row maxima over each row's causal cells, pass 2 recomputes the same scores,
+// forms p = v_expf(s - M) (L in double) and accumulates O += p * v in double as
+// a register tile of 4 rows x 8 dims per thread, cell by cell in order (p kept
+// as p * 2^1008 so the V bits enter the fma with no conversion instruction).
+static constexpr int FP_R = 64;                 // rows per CTA
+static constexpr int FP_CH = 64;                // cells per stage
+static constexpr int FP_KPITCH = 272;           // padded K row in shared memory
+static constexpr size_t FP_SMEM = (size_t)128 * FP_R * 4 + 2 * FP_CH * FP_KPITCH + 2 * FP_CH * 256 +
+                                  (size_t)FP_R * FP_CH * 8;   // q^T, K x2, V x2, p: 133,120 B
+
+// the 16 score chains of one cell (K row in shared memory) against rows
+// 16*rg .. 16*rg+15 of q^T [128][FP_R]
+__device__ __forceinline__ void fp_scores16(const uint8_t * __restrict__ kr, const float * __restrict__ qT, int rg,
+                                            float (&a)[16]) {
+#pragma unroll
+    for (int k = 0; k < 16; ++k) a[k] = 0.0f;
+#pragma unroll 2
+    for (int j = 0; j < 16; ++j) {
+        const uint4 kv = *reinterpret_cast<const uint4 *>(kr + j * 16);
+        const uint32_t wd[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float2 kf = __half22float2(*reinterpret_cast<const __half2 *>(&wd[e]));
+#pragma unroll
+            for (int hlf = 0; hlf < 2; ++hlf) {
+                const float kd = hlf ? kf.y : kf.x;
+                const float * qd = qT + (8 * j + 2 * e + hlf) * FP_R + 16 * rg;
+#pragma unroll
+                for (int k4 = 0; k4 < 4; ++k4) {
+                    const float4 q4 = *reinterpret_cast<const float4 *>(qd + 4 * k4);
+                    a[4 * k4 + 0] = __fmaf_rn(kd, q4.x, a[4 * k4 + 0]);
+                    a[4 * k4 + 1] = __fmaf_rn(kd, q4.y, a[4 * k4 + 1]);
+                    a[4 * k4 + 2] = __fmaf_rn(kd, q4.z, a[4 * k4 + 2]);
+                    a[4 * k4 + 3] = __fmaf_rn(kd, q4.w, a[4 * k4 + 3]);
+                }
+            }
+        }
+    }
+}
+
+template <int G>
+__global__ void __launch_bounds__(256, 1)
+k_fa_prefill(const float * __restrict__ q, const uint16_t * __restrict__ kc, const uint16_t * __restrict__ vc, int Hq,
+             int Hkv, int T, int32_t pos0, const int32_t * __restrict__ pos_dev, float scale, float * __restrict__ out) {
+    constexpr int TQ = FP_R / G;
+    extern __shared__ __align__(16) uint8_t fp_sm[];
+    float * qT = reinterpret_cast<float *>(fp_sm);                            // [128][FP_R]
+    uint8_t * kst = fp_sm + (size_t)128 * FP_R * 4;                           // 2 x [FP_CH][FP_KPITCH]
+    uint8_t * vst = kst + 2 * FP_CH * FP_KPITCH;                              // 2 x [FP_CH][256]
+    double * pd = reinterpret_cast<double *>(vst + 2 * FP_CH * 256);          // [FP_R][FP_CH]
+    __shared__ float Mrow[FP_R];
+    __shared__ float red_m[2][FP_R];
+    __shared__ double red_l[2][FP_R];
+    const int h = blockIdx.x, t0 = blockIdx.y * TQ, tid = threadIdx.x;
+    const int lane = tid & 31, warp = tid >> 5;
+    alb_pdl_wait();
+    const int p0 = pos_dev ? pos_dev[0] : pos0;
+    const int tn = min(TQ, T - t0);                  // tokens of this tile
+    const int n = p0 + t0 + tn;                      // cells seen by the tile's last token
+    // q tile, transposed, rounded to fp16 (arm.cpp:2307); rows past the tile are 0
+    for (int i = tid; i < FP_R * 128; i += 256) {
+        const int r = i % FP_R, d = i / FP_R;
+        const int tt = r / G, g = r % G;
+        float v = 0.0f;
+        if (tt < tn) v = __half2float(__float2half_rn(q[((size_t)(t0 + tt) * Hq + h * G + g) * 128 + d]));
+        qT[d * FP_R + r] = v;
+    }
+    const int64_t row = (int64_t)Hkv * 128;
+    const int nst = (n + FP_CH - 1) / FP_CH;
+    auto issue = [&](int i, bool with_v) {
+        if (i < nst) {
+            const int cb = i * FP_CH, rows = min(FP_CH, n - cb);
+            uint8_t * kd = kst + (i & 1) * FP_CH * FP_KPITCH;
+            uint8_t * vd = vst + (i & 1) * FP_CH * 256;
+            for (int p = tid; p < rows * 16; p += 256) {
+                const int r = p >> 4, j = p & 15;
+                const size_t src = (size_t)(cb + r) * row + (size_t)h * 128 + j * 8;
+                fa_cp16(kd + r * FP_KPITCH + j * 16, kc + src);
+                if (with_v) fa_cp16(vd + r * 256 + j * 16, vc + src);
+            }
+        }
+        fa_commit();
+    };
+    const int cl = tid & (FP_CH - 1), rg = tid >> 6;   // score phase: cell of the stage, rows 16*rg ..
+    // ---- pass 1: row maxima over the causal cells
+    float mx[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) mx[k] = -INFINITY;
+    issue(0, false);
+    for (int i = 0; i < nst; ++i) {
+        issue(i + 1, false);
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+        __syncthreads();   // stage i (and q^T) visible
+        const int c = i * FP_CH + cl;
+        if (c < n) {
+            float a[16];
+            fp_scores16(kst + (i & 1) * FP_CH * FP_KPITCH + cl * FP_KPITCH, qT, rg, a);
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+                const int tt = (16 * rg + k) / G;
+                if (tt < tn && c <= p0 + t0 + tt) mx[k] = fmaxf(mx[k], __fmul_rn(a[k], scale));
+            }
+        }
+        __syncthreads();   // buffer i & 1 consumed before stage i + 2 refills it
+    }
+    fa_wait_all();
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+        const float m = alb_warp_max(mx[k]);
+        if (lane == 0) red_m[warp & 1][16 * rg + k] = m;
+    }
+    __syncthreads();
+    if (tid < FP_R) Mrow[tid] = fmaxf(red_m[0][tid], red_m[1][tid]);
+    // ---- pass 2: p, L and O
+    const int r4 = (tid >> 4) * 4, d8 = (tid & 15) * 8;   // P.V tile of this thread
+    double L[16], O[4][8];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) L[k] = 0.0;
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) O[u][e] = 0.0;
+    issue(0, true);
+    for (int i = 0; i < nst; ++i) {
+        issue(i + 1, true);
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+        __syncthreads();   // stage i visible; Mrow visible; pd free
+        const int c = i * FP_CH + cl;
+        float a[16];
+        if (c < n) fp_scores16(kst + (i & 1) * FP_CH * FP_KPITCH + cl * FP_KPITCH, qT, rg, a);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            const int r = 16 * rg + k, tt = r / G;
+            double v = 0.0;
+            if (c < n && tt < tn && c <= p0 + t0 + tt) {
+                const float p = alb_ref_expf(__fsub_rn(__fmul_rn(a[k], scale), Mrow[r]));
+                L[k] += (double)p;
+                v = (double)p * 0x1p1008;
+            }
+            pd[r * FP_CH + cl] = v;
+        }
+        __syncthreads();
+        const int rows = min(FP_CH, n - i * FP_CH);
+        const uint8_t * vs = vst + (i & 1) * FP_CH * 256 + d8 * 2;
+        for (int cc = 0; cc < rows; ++cc) {
+            const uint4 vv = *reinterpret_cast<const uint4 *>(vs + cc * 256);
+            const uint32_t wd[4] = {vv.x, vv.y, vv.z, vv.w};
+            double vd[8];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                vd[2 * e] = alb_h2d_bits(wd[e] & 0xFFFFu);
+                vd[2 * e + 1] = alb_h2d_bits(wd[e] >> 16);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const double p = pd[(r4 + u) * FP_CH + cc];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) O[u][e] = fma(p, vd[e], O[u][e]);
+            }
+        }
+        __syncthreads();   // pd and buffer i & 1 consumed
+    }
+    fa_wait_all();
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+        const double l = alb_warp_sum_d(L[k]);
+        if (lane == 0) red_l[warp & 1][16 * rg + k] = l;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        const int r = r4 + u, tt = r / G, g = r % G;
+        if (tt >= tn) continue;
+        const double Ls = red_l[0][r] + red_l[1][r];
+        float * o = out + ((size_t)(t0 + tt) * Hq + h * G + g) * 128 + d8;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = Ls > 0.0 ? __double2float_rn(O[u][e] / Ls) : 0.0f;
+    }
+    alb_pdl_trigger();
+}
+
 // One CTA per (h, t): scores of all cells in shared memory, then the same
 // global-max softmax and double sums.
 template <int G>
@@ -572,6 +760,19 @@ static constexpr size_t FA_FUSED_SMEM = 160 * 1024;
 
 template <int G>
 static cudaError_t launch_fa_core(const FlashArgs & f, cudaStream_t st) {
+    if (f.T > 1 && f.S == 1) {   // prefill ubatch: token tiles share the staged cells
+        static bool pattr = false;
+        if (!pattr) {
+            cudaError_t e = cudaFuncSetAttribute(k_fa_prefill<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)FP_SMEM);
+            if (e != cudaSuccess) return e;
+            pattr = true;
+        }
+        constexpr int TQ = FP_R / G;
+        const dim3 grid((unsigned)f.Hkv, (unsigned)((f.T + TQ - 1) / TQ));
+        return alb_launch(k_fa_prefill<G>, grid, dim3(256), FP_SMEM, st, f.pdl, f.q, f.kc, f.vc, f.Hq, f.Hkv, f.T,
+                          f.pos0, f.pos_dev, f.scale, f.out);
+    }
     const int n_max = f.ncap;   // cells attended by the last token at most
     if (f.S == 1 && (size_t)G * n_max * 4 <= FA_FUSED_SMEM) {
         const size_t smem = (size_t)G * n_max * 4;

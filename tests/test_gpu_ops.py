@@ -148,6 +148,10 @@ def test_qk_norm_rope_kv(Hq, Hkv, T, pos0):
     (32, 8, 64, 0, 1),       # prefill from an empty cache
     (32, 8, 3, 5000, 1),     # splits == 1 but too many cells for the fused kernel
     (32, 8, 2, 300, 8),      # two tokens, split
+    (32, 8, 300, 0, 1),      # prefill tiles of 16 tokens (G = 4), partial last tile
+    (16, 8, 100, 37, 1),     # G = 2 tiles of 32 tokens after a cached prefix
+    (8, 8, 70, 10, 1),       # G = 1 tiles of 64 tokens
+    (64, 8, 20, 3, 1),       # G = 8 tiles of 8 tokens
 ])
 def test_flash_attn(Hq, Hkv, T, pos0, S):
     rng = np.random.default_rng(Hq + T + pos0)
