@@ -83,6 +83,8 @@ struct alb_engine {
     float * part = nullptr, * part_all = nullptr;   // TP: this rank's O / down partial, all ranks' partials
     float * xn = nullptr;                           // prefill: RMS-normalized rows
     void * xq = nullptr;                            // decode: block_q8_0 input of the next mat-vec
+    uint8_t * hq = nullptr;                         // decode: block_q8_0 of the SwiGLU output (down's input)
+    int * hcnt = nullptr;                           // its per-block arrival counters (self re-arming)
     void * pg_ws = nullptr;                         // prefill: quantized activations of the mat-mul
     int32_t * tok_dev = nullptr, * pos_dev = nullptr, * next_dev = nullptr, * step_dev = nullptr, * gen_out = nullptr;
     int32_t gen_cap = 0;
@@ -143,6 +145,7 @@ static int engine_forward(alb_engine * e, int64_t T, bool pdl, int ncap_prefill 
         a.W = W; a.S = W + q4_scale_offset(N, K); a.N = N; a.K = K;
         a.in_mode = in; a.x = x; a.norm_w = nw; a.eps = c.eps;
         a.out_mode = out; a.y = y; a.residual = res; a.pdl = pdl;
+        if (T == 1 && out == GEMV_OUT_SWIGLU) { a.yq = e->hq; a.ycnt = e->hcnt; }   // down's Q8_0 input
         ++launches;
         // decode: records already in x (attention merge), or, for K <= 2560, RMSNorm
         // + quantization in the mat-vec's prologue (overlapping its first weight
@@ -188,7 +191,7 @@ static int engine_forward(alb_engine * e, int64_t T, bool pdl, int ncap_prefill 
         fa.out = e->att; fa.pdl = pdl;
         fa.xq = T == 1 ? e->xq : nullptr;   // decode: the merge writes the o_proj input records
         ALB_CUDA_TRY(launch_flash_attn(fa, st));
-        launches += S > 1 ? 3 : 2;
+        launches += S > 1 ? 4 : 2;   // QK-norm/RoPE, then scores + PV + merge, or the prefill attention
         const int o_in = T == 1 ? GEMV_IN_Q8 : GEMV_IN_F32;
         const void * o_x = T == 1 ? e->xq : static_cast<const void *>(e->att);
         if (e->tp == 1) {
@@ -198,12 +201,14 @@ static int engine_forward(alb_engine * e, int64_t T, bool pdl, int ncap_prefill 
             ALB_TRY(engine_gather_add_x(e, T, pdl));
         }
         ALB_CUDA_TRY(gemv(L.gu, 2 * (int64_t)e->F, e->E, GEMV_IN_F32_RMS, e->x, L.fn, GEMV_OUT_SWIGLU, e->h, nullptr));
+        const int d_in = T == 1 ? GEMV_IN_Q8 : GEMV_IN_F32;   // decode: records from the gate/up epilogue
+        const void * d_x = T == 1 ? static_cast<const void *>(e->hq) : static_cast<const void *>(e->h);
         if (e->tp == 1) {
-            ALB_CUDA_TRY(gemv(L.down, e->E, e->F, GEMV_IN_F32, e->h, nullptr, GEMV_OUT_PLAIN, e->x, e->x));
+            ALB_CUDA_TRY(gemv(L.down, e->E, e->F, d_in, d_x, nullptr, GEMV_OUT_PLAIN, e->x, e->x));
         } else {
-            ALB_CUDA_TRY(gemv(L.down, e->E, e->F, GEMV_IN_F32, e->h, nullptr, GEMV_OUT_PLAIN, e->part, nullptr));
+            ALB_CUDA_TRY(gemv(L.down, e->E, e->F, d_in, d_x, nullptr, GEMV_OUT_PLAIN, e->part, nullptr));
             ALB_TRY(engine_gather_add_x(e, T, pdl));
-            launches += 4;
+            launches += 2;   // the two k_gather_add (the NCCL all-gathers are NCCL's kernels)
         }
     }
     // final norm + lm_head on the last token (qwen3.cpp:235-238, 266-274)
@@ -222,7 +227,7 @@ static int engine_forward(alb_engine * e, int64_t T, bool pdl, int ncap_prefill 
         ALB_CUDA_TRY(launch_argmax(e->logits, e->V, e->v0, e->am_scratch, e->key, nullptr, pdl, st));
         ALB_TRY(nccl_allreduce(e->comm, e->key, e->key, 1, 1, 1, st));
         ALB_CUDA_TRY(launch_key_to_index(e->key, e->next_dev, false, st));
-        launches += 3;
+        launches += 2;   // argmax + key_to_index (the all-reduce is NCCL's)
     }
     e->launches_per_step = launches;
     return ALB_OK;
@@ -334,6 +339,9 @@ static int engine_init_acts(alb_engine * e) {
         uint8_t * q8 = nullptr;
         ALB_TRY(e->alloc(&q8, (size_t)(kmax / 32) * 34));
         e->xq = q8;
+        ALB_TRY(e->alloc(&e->hq, (size_t)(e->F / 32) * 34));
+        ALB_TRY(e->alloc(&e->hcnt, (size_t)(e->F / 32)));
+        ALB_CUDA_TRY(cudaMemsetAsync(e->hcnt, 0, (size_t)(e->F / 32) * sizeof(int), e->st));
     }
     if (U > 1) {
         ALB_TRY(e->alloc(&e->xn, U * e->E));
@@ -781,21 +789,28 @@ extern "C" int alb_engine_time_gemv(alb_engine * e, int32_t reps, float * us_per
     ALB_CUDA_TRY(cudaSetDevice(e->dev));
     std::vector<GemvArgs> list;
     double bytes = 0.0;
+    // the decode step's mat-vec launches with the step's input modes (outputs to
+    // scratch so the engine state is unchanged)
     auto add = [&](const uint8_t * W, const uint8_t * S, int64_t N, int64_t K, int in, const void * x, const float * nw,
                    int out, float * y, const float * res) {
         GemvArgs a;
         a.W = W; a.S = S ? S : W + q4_scale_offset(N, K); a.N = N; a.K = K;
         a.in_mode = in; a.x = x; a.norm_w = nw; a.eps = e->c.eps;
         a.out_mode = out; a.y = y; a.residual = res; a.pdl = true;
+        if (out == GEMV_OUT_SWIGLU) { a.yq = e->hq; a.ycnt = e->hcnt; }
         list.push_back(a);
-        bytes += (double)N * K * 18 / 32 + K * 4.0 + (out == GEMV_OUT_SWIGLU ? N / 2 : N) * 4.0;
+        const double in_bytes = in == GEMV_IN_Q8 ? K / 32 * 34.0 : in == GEMV_IN_F32 ? K * 4.0 : K * 8.0;
+        bytes += (double)N * K * 18 / 32 + in_bytes + (out == GEMV_OUT_SWIGLU ? N / 2 : N) * 4.0;
     };
+    const bool fused_rms = e->E <= 2560;   // as engine_forward
     for (int l = 0; l < e->c.n_layer; ++l) {
         alb_engine::Layer & L = e->layers[l];
-        add(L.qkv, nullptr, e->Nqkv, e->E, GEMV_IN_F32_RMS, e->x, L.an, GEMV_OUT_PLAIN, e->qkv, nullptr);
-        add(L.o, nullptr, e->E, e->Dq, GEMV_IN_F32, e->att, nullptr, GEMV_OUT_PLAIN, e->qkv, nullptr);
-        add(L.gu, nullptr, 2 * (int64_t)e->F, e->E, GEMV_IN_F32_RMS, e->x, L.fn, GEMV_OUT_SWIGLU, e->h, nullptr);
-        add(L.down, nullptr, e->E, e->F, GEMV_IN_F32, e->h, nullptr, GEMV_OUT_PLAIN, e->qkv, nullptr);
+        add(L.qkv, nullptr, e->Nqkv, e->E, fused_rms ? GEMV_IN_F32_RMS : GEMV_IN_Q8, fused_rms ? (const void *)e->x : e->xq,
+            L.an, GEMV_OUT_PLAIN, e->qkv, nullptr);
+        add(L.o, nullptr, e->E, e->Dq, GEMV_IN_Q8, e->xq, nullptr, GEMV_OUT_PLAIN, e->qkv, nullptr);
+        add(L.gu, nullptr, 2 * (int64_t)e->F, e->E, fused_rms ? GEMV_IN_F32_RMS : GEMV_IN_Q8,
+            fused_rms ? (const void *)e->x : e->xq, L.fn, GEMV_OUT_SWIGLU, e->h, nullptr);
+        add(L.down, nullptr, e->E, e->F, GEMV_IN_Q8, e->hq, nullptr, GEMV_OUT_PLAIN, e->qkv, nullptr);
     }
     add(e->lm_W, e->lm_S, e->V, e->E, GEMV_IN_F32_RMS, e->x, e->out_norm, GEMV_OUT_PLAIN, e->logits, nullptr);
     cudaGraph_t g = nullptr;

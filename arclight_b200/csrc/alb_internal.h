@@ -39,6 +39,10 @@ struct GemvArgs {
     int variant = 0;               // 0/1 = direct loads + L2 prefetch (default), 2 = bulk-copy pipeline
     int stage_budget = 0;          // bytes of shared-memory stages (0 = default)
     int * err = nullptr;           // device error word (filled by launch_gemv)
+    // SwiGLU only, optional: block_q8_0 records of y [N/2/32] written by the
+    // warp that completes each 32-value block; ycnt [N/2/32] zeroed once
+    uint8_t * yq = nullptr;
+    int * ycnt = nullptr;
 };
 
 struct FlashArgs {

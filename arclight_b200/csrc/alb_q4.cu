@@ -194,6 +194,33 @@ __device__ __forceinline__ void l2_prefetch(const void * p, size_t bytes) {
     }
 }
 
+// After lane 0 wrote the SwiGLU output y[item]: with a.yq set, the warp whose
+// value completes a 32-value block quantizes that block (quantize_row_q8_0 of
+// the fp32 values, the down projection's input) and re-arms its counter.
+// Writers publish y before their arrival (fence + atomic); the last one reads
+// the block from L2 after its own fence.  Called by the whole warp.
+__device__ __forceinline__ void gemv_swiglu_q8_tail(const GemvArgs & a, int64_t item, int lane) {
+    if (!a.yq) return;
+    const int64_t b = item >> 5;
+    int last = 0;
+    if (lane == 0) {
+        __threadfence();
+        last = atomicAdd(&a.ycnt[b], 1) == 31;
+    }
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (!last) return;
+    __threadfence();
+    const float v = __ldcg(a.y + b * 32 + lane);
+    int8_t q; uint16_t dh;
+    q8_block_lane(v, q, dh);
+    uint8_t * blk = a.yq + b * 34;
+    if (lane == 0) {
+        *reinterpret_cast<uint16_t *>(blk) = dh;
+        a.ycnt[b] = 0;
+    }
+    blk[2 + lane] = (uint8_t)q;
+}
+
 // Each CTA owns a contiguous range of row items; before waiting on the previous
 // kernel it asks the TMA unit to pull its whole weight range (nibbles and
 // scales, in PF-byte windows ahead of the compute) into L2, and each warp loads
@@ -286,6 +313,7 @@ k_gemv_direct(const GemvArgs a) {
                 }
             }
         }
+        if constexpr (OUT == GEMV_OUT_SWIGLU) gemv_swiglu_q8_tail(a, cur, lane);
     }
 }
 
@@ -421,6 +449,7 @@ k_gemv_tma(const GemvArgs a, const TmaPlan plan) {
                     }
                 }
             }
+            if constexpr (OUT == GEMV_OUT_SWIGLU) gemv_swiglu_q8_tail(a, item, lane);
         }
         __syncwarp();
         if (lane == 0) alb_mbar_arrive(&empty[st]);
@@ -492,6 +521,7 @@ cudaError_t launch_gemv(const GemvArgs & a_in, cudaStream_t s) {
     if (!a.err) return cudaErrorMemoryAllocation;
     if (a.K % 32 != 0 || a.K <= 0 || a.N <= 0 || a.K > 12288) return cudaErrorInvalidValue;
     if (a.out_mode == GEMV_OUT_SWIGLU && a.N % 2 != 0) return cudaErrorInvalidValue;
+    if (a.yq && (a.out_mode != GEMV_OUT_SWIGLU || !a.ycnt || !a.y || (a.N / 2) % 32 != 0)) return cudaErrorInvalidValue;
 #define ALB_GEMV_CASE(IN)                                                           \
     case IN:                                                                        \
         switch (a.out_mode) {                                                       \
