@@ -46,3 +46,14 @@ def test_invalid_arguments_are_rejected_without_a_gpu():
     assert L.alb_gemv_q4_0_q8_0(None, None, None, 16, 2560, None, None) == -1
     assert L.alb_quantize_q8_0(None, None, 33, 1, None) == -1
     assert b"invalid argument" in L.alb_last_error()
+    # fused quantizers: n must be a whole number of 32-value blocks
+    assert L.alb_rms_norm_q8(None, None, None, None, 1, 2560, 1e-6, None) == -1
+    assert L.alb_swiglu_q8(None, None, None, None, 9728, None) == -1
+    dummy = 16   # non-null host addresses: the size check fires before any device access
+    assert L.alb_rms_norm_q8(dummy, None, None, dummy, 1, 2561, 1e-6, None) == -1
+    assert L.alb_swiglu_q8(dummy, dummy, None, dummy, 100, None) == -1
+    # communicator: null id / out pointer, bad rank
+    assert L.alb_comm_create(None, 0, 1, 0, None) == -1
+    assert L.alb_allreduce_sum_f32(None, None, None, 1, None) == -1
+    assert L.alb_allgather_f32(None, None, None, 1, None) == -1
+    assert L.alb_comm_destroy(None) == 0
