@@ -1,6 +1,8 @@
 // alb_flash_attn_static: alb_flash_attn with its workspace in a fixed,
 // file-scope device array instead of a caller-provided buffer, so the call
 // allocates nothing (no cudaMalloc / cudaFree, no allocating library routine).
+// It serves callers that cannot allocate device memory, such as an operator
+// shim called from the reference's graph walk with only host scratch at hand.
 //
 // Limits and rules (also stated in include/alb_cuda.h):
 //   * the workspace alb_flash_attn_workspace_bytes(...) of the call must fit

@@ -137,7 +137,10 @@ ALB_API int alb_flash_attn(const float * q, const uint16_t * k_cache, const uint
 
 /* Size of the fixed device workspace of alb_flash_attn_static (one per device). */
 #define ALB_FLASH_ATTN_STATIC_BYTES (4u << 20)
-/* alb_flash_attn without a caller workspace and without allocating: the
+/* alb_flash_attn without a caller workspace and without allocating, for
+ * callers that cannot call cudaMalloc: an nnml operator shim runs inside the
+ * reference's graph walk with only params->work_data (host scratch) in hand
+ * and no device allocator of its own.  The
  * workspace is a file-scope device array of ALB_FLASH_ATTN_STATIC_BYTES per
  * device (calls whose alb_flash_attn_workspace_bytes exceeds it return
  * ALB_ERR_INVALID).  Calls on one device share that array and must not
