@@ -206,9 +206,11 @@ typedef void (*orc_range_fn)(void * ctx, int64_t begin, int64_t end);
 typedef struct { orc_range_fn fn; void * ctx; int64_t b, e; } orc_job;
 static void * orc_job_run(void * p) { orc_job * j = (orc_job *)p; j->fn(j->ctx, j->b, j->e); return NULL; }
 
-static void orc_parallel_for(int n_threads, int64_t n, orc_range_fn fn, void * ctx) {
-    if (n_threads <= 1 || n < 64) { fn(ctx, 0, n); return; }
+/* fn over [0, n) in n_threads contiguous ranges (one thread when n < min_n) */
+static void orc_parallel_for_min(int n_threads, int64_t n, int64_t min_n, orc_range_fn fn, void * ctx) {
+    if (n_threads <= 1 || n < min_n) { fn(ctx, 0, n); return; }
     if (n_threads > 64) n_threads = 64;
+    if (n_threads > n) n_threads = (int)n;
     pthread_t th[64];
     orc_job jobs[64];
     for (int t = 0; t < n_threads; ++t) {
@@ -218,6 +220,10 @@ static void orc_parallel_for(int n_threads, int64_t n, orc_range_fn fn, void * c
     for (int t = 1; t < n_threads; ++t) pthread_create(&th[t], NULL, orc_job_run, &jobs[t]);
     orc_job_run(&jobs[0]);
     for (int t = 1; t < n_threads; ++t) pthread_join(th[t], NULL);
+}
+
+static void orc_parallel_for(int n_threads, int64_t n, orc_range_fn fn, void * ctx) {
+    orc_parallel_for_min(n_threads, n, 64, fn, ctx);
 }
 
 /* ----------------------------------------------------------------- matvec */
@@ -471,28 +477,38 @@ static float vec_dot_f16_arm(int64_t n, const uint16_t * x, const uint16_t * y) 
  * L = sum_c p_c and O_d = sum_c p_c V_cd summed in double, out_d = O_d / L.
  * Softmax is shift invariant, so this is the same function as the
  * reference's online form; only roundings differ. */
-void orc_flash_attn(const float * q, const uint16_t * k, const uint16_t * v, const int32_t * kv_len,
-                    int64_t T, int64_t n_head, int64_t n_head_kv, int64_t D, float scale,
-                    int mode, float * out) {
-    const int64_t rk2 = n_head / n_head_kv;
-    const int64_t row = n_head_kv * D;
-    int64_t nmax = 1;
-    for (int64_t t = 0; t < T; ++t) nmax = kv_len[t] > nmax ? kv_len[t] : nmax;
+/* One (token, head) output of orc_flash_attn; the (token, head) pairs are
+ * independent, so threads split them without changing any result. */
+typedef struct {
+    const float * q; const uint16_t * k, * v; const int32_t * kv_len;
+    int64_t T, n_head, n_head_kv, D, nmax;
+    float scale; int mode; float * out;
+} fa_ctx;
+
+static void fa_range(void * pc, int64_t b, int64_t e) {
+    const fa_ctx * f = (const fa_ctx *)pc;
+    const int64_t D = f->D, n_head = f->n_head;
+    const int64_t rk2 = n_head / f->n_head_kv;
+    const int64_t row = f->n_head_kv * D;
+    const uint16_t * k = f->k, * v = f->v;
+    const float scale = f->scale;
     uint16_t * Qh = (uint16_t *)malloc(D * 2);
     uint16_t * VKQ16 = (uint16_t *)malloc(D * 2);
     float * VKQ32 = (float *)malloc(D * 4);
     float * Qf = (float *)malloc(D * 4);
-    float * sc = (float *)malloc(nmax * 4);
+    float * sc = (float *)malloc(f->nmax * 4);
     double * Od = (double *)malloc(D * sizeof(double));
-    for (int64_t t = 0; t < T; ++t) {
-        for (int64_t h = 0; h < n_head; ++h) {
+    for (int64_t idx = b; idx < e; ++idx) {
+        const int64_t t = idx / n_head, h = idx - t * n_head;
+        const int64_t n_kv = f->kv_len[t];
+        {
             const int64_t hk = h / rk2;
-            const float * pq = q + (t * n_head + h) * D;
-            float * po = out + (t * n_head + h) * D;
+            const float * pq = f->q + (t * n_head + h) * D;
+            float * po = f->out + (t * n_head + h) * D;
             for (int64_t d = 0; d < D; ++d) { Qh[d] = orc_fp32_to_fp16(pq[d]); Qf[d] = orc_fp16_to_fp32(Qh[d]); }
-            if (mode == 0) {
+            if (f->mode == 0) {
                 float M = -INFINITY;
-                for (int64_t c = 0; c < kv_len[t]; ++c) {
+                for (int64_t c = 0; c < n_kv; ++c) {
                     const uint16_t * kc = k + c * row + hk * D;
                     float a = 0.0f;
                     for (int64_t d = 0; d < D; ++d) a = fmaf(orc_fp16_to_fp32(kc[d]), Qf[d], a);
@@ -501,7 +517,7 @@ void orc_flash_attn(const float * q, const uint16_t * k, const uint16_t * v, con
                 }
                 double L = 0.0;
                 for (int64_t d = 0; d < D; ++d) Od[d] = 0.0;
-                for (int64_t c = 0; c < kv_len[t]; ++c) {
+                for (int64_t c = 0; c < n_kv; ++c) {
                     const float p = orc_neon_expf(sc[c] - M);
                     const uint16_t * vc = v + c * row + hk * D;
                     L += (double)p;
@@ -512,7 +528,7 @@ void orc_flash_attn(const float * q, const uint16_t * k, const uint16_t * v, con
             }
             float S = 0.0f, M = -INFINITY;
             memset(VKQ16, 0, D * 2);
-            for (int64_t c = 0; c < kv_len[t]; ++c) {
+            for (int64_t c = 0; c < n_kv; ++c) {
                 const uint16_t * kc = k + c * row + hk * D;
                 const uint16_t * vc = v + c * row + hk * D;
                 float s = vec_dot_f16_arm(D, kc, Qh);
@@ -538,6 +554,21 @@ void orc_flash_attn(const float * q, const uint16_t * k, const uint16_t * v, con
         }
     }
     free(Qh); free(VKQ16); free(VKQ32); free(Qf); free(sc); free(Od);
+}
+
+void orc_flash_attn_mt(const float * q, const uint16_t * k, const uint16_t * v, const int32_t * kv_len,
+                       int64_t T, int64_t n_head, int64_t n_head_kv, int64_t D, float scale,
+                       int mode, float * out, int n_threads) {
+    int64_t nmax = 1;
+    for (int64_t t = 0; t < T; ++t) nmax = kv_len[t] > nmax ? kv_len[t] : nmax;
+    fa_ctx f = { q, k, v, kv_len, T, n_head, n_head_kv, D, nmax, scale, mode, out };
+    orc_parallel_for_min(n_threads, T * n_head, 2, fa_range, &f);
+}
+
+void orc_flash_attn(const float * q, const uint16_t * k, const uint16_t * v, const int32_t * kv_len,
+                    int64_t T, int64_t n_head, int64_t n_head_kv, int64_t D, float scale,
+                    int mode, float * out) {
+    orc_flash_attn_mt(q, k, v, kv_len, T, n_head, n_head_kv, D, scale, mode, out, 1);
 }
 
 /* ------------------------------------------------------------ Qwen3 model */
@@ -642,16 +673,24 @@ void orc_model_reset(orc_model * m) {
     }
 }
 
-void orc_model_fill_kv(orc_model * m, int32_t n_pos, uint64_t seed) {
-    const int64_t Dkv = (int64_t)m->c.n_head_kv * m->c.head_dim;
-    if (n_pos > m->max_ctx) n_pos = m->max_ctx;
-    for (int l = 0; l < m->c.n_layer; ++l) {
-        const uint64_t sk = orc_tensor_seed(seed, l, 62), sv = orc_tensor_seed(seed, l, 63);
-        for (int64_t i = 0; i < (int64_t)n_pos * Dkv; ++i) {
-            m->layers[l].kc[i] = orc_fp32_to_fp16(orc_normal(m->table, sk, (uint64_t)i));
-            m->layers[l].vc[i] = orc_fp32_to_fp16(orc_normal(m->table, sv, (uint64_t)i));
+typedef struct { orc_model * m; int64_t n; uint64_t seed; } fill_ctx;
+
+static void fill_range(void * pc, int64_t b, int64_t e) {   /* layers [b, e) */
+    const fill_ctx * f = (const fill_ctx *)pc;
+    const int64_t Dkv = (int64_t)f->m->c.n_head_kv * f->m->c.head_dim;
+    for (int64_t l = b; l < e; ++l) {
+        const uint64_t sk = orc_tensor_seed(f->seed, (int)l, 62), sv = orc_tensor_seed(f->seed, (int)l, 63);
+        for (int64_t i = 0; i < f->n * Dkv; ++i) {
+            f->m->layers[l].kc[i] = orc_fp32_to_fp16(orc_normal(f->m->table, sk, (uint64_t)i));
+            f->m->layers[l].vc[i] = orc_fp32_to_fp16(orc_normal(f->m->table, sv, (uint64_t)i));
         }
     }
+}
+
+void orc_model_fill_kv(orc_model * m, int32_t n_pos, uint64_t seed) {
+    if (n_pos > m->max_ctx) n_pos = m->max_ctx;
+    fill_ctx f = { m, n_pos, seed };
+    orc_parallel_for_min(m->n_threads, m->c.n_layer, 2, fill_range, &f);
 }
 
 const orc_block_q4_0 * orc_model_q4_tensor(orc_model * m, int layer, int kind, int64_t * rows, int64_t * cols) {
@@ -757,7 +796,8 @@ int orc_model_forward(orc_model * m, const int32_t * tokens, int32_t T, int32_t 
                 L->vc[(int64_t)(pos0 + t) * Dkv + d] = orc_fp32_to_fp16(v[t * Dkv + d]);
             }
         }
-        orc_flash_attn(q, L->kc, L->vc, kv_len, Tcur, c->n_head, c->n_head_kv, HD, 1.0f / sqrtf((float)HD), fa_mode, att);
+        orc_flash_attn_mt(q, L->kc, L->vc, kv_len, Tcur, c->n_head, c->n_head_kv, HD, 1.0f / sqrtf((float)HD),
+                          fa_mode, att, m->n_threads);
         matmul_rows_cols_split(m, L->wo, att, o, Tcur, E, Dq, qb);
         if (l == c->n_layer - 1 && Tcur > 1) { /* keep the last row only (qwen3.cpp:235-238) */
             memmove(o, o + (Tcur - 1) * E, E * 4);

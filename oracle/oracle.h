@@ -100,6 +100,11 @@ void orc_gather_sum(const float * const * srcs, int n_srcs, float * dst, int64_t
 void orc_flash_attn(const float * q, const uint16_t * k, const uint16_t * v, const int32_t * kv_len,
                     int64_t T, int64_t n_head, int64_t n_head_kv, int64_t D, float scale,
                     int mode, float * out);
+/* the same over n_threads threads (the (token, head) outputs split among them;
+ * results identical to orc_flash_attn) */
+void orc_flash_attn_mt(const float * q, const uint16_t * k, const uint16_t * v, const int32_t * kv_len,
+                       int64_t T, int64_t n_head, int64_t n_head_kv, int64_t D, float scale,
+                       int mode, float * out, int n_threads);
 
 /* ---- Qwen3 model (qwen3.cpp:174-275), synthetic seeded weights ---- */
 typedef struct {
