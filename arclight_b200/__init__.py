@@ -59,12 +59,13 @@ def _declare(L: C.CDLL) -> None:
         "alb_device_check": (ci, [ci]),
         "alb_device_error": (ci, [ci]),
         "alb_q4_0_gpu_bytes": (sz, [i64, i64]),
-        "alb_q4_0_scale_offset": (sz, [i64, i64]),
+        "alb_q4_0_row_bytes": (sz, [i64]),
         "alb_repack_q4_0": (ci, [vp, vp, i64, i64, vp]),
         "alb_unpack_q4_0": (ci, [vp, vp, i64, i64, vp]),
         "alb_quantize_q8_0": (ci, [vp, vp, i64, i64, vp]),
         "alb_gemv_q4_0_q8_0": (ci, [vp, vp, vp, i64, i64, vp, vp]),
         "alb_gemv_q4_0_q8_0_block_dots": (ci, [vp, vp, vp, i64, i64, vp]),
+        "alb_mul_mat_q4_0_q8_0": (ci, [vp, vp, vp, i64, i64, vp]),
         "alb_rms_norm": (ci, [vp, vp, vp, i64, i64, f32, vp]),
         "alb_swiglu": (ci, [vp, vp, vp, i64, vp]),
         "alb_rms_norm_q8": (ci, [vp, vp, vp, vp, i64, i64, f32, vp]),
@@ -98,7 +99,6 @@ def _declare(L: C.CDLL) -> None:
         "alb_engine_norm_weights": (ci, [vp, i32, i32, vp, i64]),
         "alb_engine_fill_kv": (ci, [vp, i32, C.c_uint64]),
         "alb_engine_time_gemv": (ci, [vp, i32, vp, vp]),
-        "alb_engine_decode_trace": (ci, [vp, i32, i32, vp, i32]),
     }
     for name, (res, args) in sigs.items():
         if hasattr(L, name):

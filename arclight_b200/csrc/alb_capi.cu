@@ -36,9 +36,7 @@ extern "C" int alb_swiglu_q8(const float * g, const float * u, float * y, void *
 extern "C" int alb_get_rows_q4_0(const void * W, int64_t n_rows, int64_t K, const int32_t * ids, int64_t n_ids,
                                  float * out, void * stream) {
     ALB_CHECK_ARG(W && ids && out && n_rows > 0 && K > 0 && K % 32 == 0 && n_ids > 0 && n_ids < (1 << 30));
-    const uint8_t * Wn = (const uint8_t *)W;
-    ALB_CUDA_TRY(launch_embed(Wn, Wn + q4_scale_offset(n_rows, K), n_rows, K, ids, (int)n_ids, out, true,
-                              (cudaStream_t)stream));
+    ALB_CUDA_TRY(launch_embed((const uint8_t *)W, n_rows, K, ids, (int)n_ids, out, nullptr, true, (cudaStream_t)stream));
     return ALB_OK;
 }
 

@@ -138,6 +138,17 @@ __device__ __forceinline__ bool alb_mbar_wait(uint64_t * bar, uint32_t parity, u
         if ((i & 15) == 0 && alb_globaltimer() - t0 > ns) return false;
     }
 }
+// Bounded wait that polls the phase with plain try_wait (no suspend-time hint),
+// checking %globaltimer every 256 polls: for the short hand-offs of a
+// streaming pipeline, where a waiter must resume the moment the phase flips.
+__device__ __forceinline__ bool alb_mbar_wait_spin(uint64_t * bar, uint32_t parity, uint64_t ns = 2000000000ull) {
+    if (alb_mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = alb_globaltimer();
+    for (uint32_t i = 1;; ++i) {
+        if (alb_mbar_try_wait(bar, parity)) return true;
+        if ((i & 255) == 0 && alb_globaltimer() - t0 > ns) return false;
+    }
+}
 // Bounded wait for a thread with nothing else to do (a producer ahead of its
 // consumers): polls with exponential __nanosleep backoff (32 ns .. 512 ns), so
 // the waiting warp takes almost no issue slots from the warps that compute.

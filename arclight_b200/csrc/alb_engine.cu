@@ -22,7 +22,6 @@
 
 #include "alb_common.cuh"
 #include "alb_internal.h"
-#include "alb_mk.h"
 #include "alb_nccl.h"
 
 namespace alb {
@@ -77,7 +76,7 @@ struct alb_engine {
     };
     std::vector<Layer> layers;
     uint8_t * tok = nullptr, * out_w = nullptr;
-    const uint8_t * lm_W = nullptr, * lm_S = nullptr;
+    const uint8_t * lm_W = nullptr;                 // lm head rows of this rank (a view of the token table when tied)
     float * out_norm = nullptr, * table = nullptr, * rope = nullptr;
     float * x = nullptr, * qkv = nullptr, * q = nullptr, * att = nullptr, * h = nullptr, * logits = nullptr;
     float * part = nullptr, * part_all = nullptr;   // TP: this rank's O / down partial, all ranks' partials
@@ -100,10 +99,6 @@ struct alb_engine {
     size_t bytes = 0;
     int32_t * pinned = nullptr;     // host staging for the e2e path
     int launches_per_step = 0;
-    // persistent decode-step kernel (tp == 1): parameters and scratch
-    bool use_mk = false;
-    MkParams mk{};
-    MkLayer * mk_layers = nullptr;
 
     template <typename T> int alloc(T ** p, size_t n) {
         void * v = nullptr;
@@ -136,33 +131,20 @@ static int engine_forward(alb_engine * e, int64_t T, bool pdl, int ncap_prefill 
     const alb_qwen3_config & c = e->c;
     cudaStream_t st = e->st;
     int launches = 0;
-    ALB_CUDA_TRY(launch_embed(e->tok, e->tok + q4_scale_offset(c.n_vocab, e->E), c.n_vocab, e->E, e->tok_dev,
-                              (int)T, e->x, pdl, st));
+    ALB_CUDA_TRY(launch_embed(e->tok, c.n_vocab, e->E, e->tok_dev, (int)T, e->x, e->key, pdl, st));
     ++launches;
     auto gemv = [&](const uint8_t * W, int64_t N, int64_t K, int in, const void * x, const float * nw, int out,
                     float * y, const float * res) -> cudaError_t {
         GemvArgs a;
-        a.W = W; a.S = W + q4_scale_offset(N, K); a.N = N; a.K = K;
+        a.W = W; a.N = N; a.K = K;
         a.in_mode = in; a.x = x; a.norm_w = nw; a.eps = c.eps;
         a.out_mode = out; a.y = y; a.residual = res; a.pdl = pdl;
         if (T == 1 && out == GEMV_OUT_SWIGLU) { a.yq = e->hq; a.ycnt = e->hcnt; }   // down's Q8_0 input
         ++launches;
-        // decode: records already in x (attention merge), or, for K <= 2560, RMSNorm
-        // + quantization in the mat-vec's prologue (overlapping its first weight
-        // loads; measured the cheaper of the two there, not at K = 4096)
-        if (T == 1 && (in == GEMV_IN_Q8 || (in == GEMV_IN_F32_RMS && K <= 2560))) return launch_gemv(a, st);
-        if (T == 1) {
-            // otherwise the input is quantized once (RMSNorm fused) and the CTAs of
-            // the mat-vec stage its block_q8_0 records
-            const cudaError_t qe = in == GEMV_IN_F32_RMS
-                ? launch_rms_norm_q8(static_cast<const float *>(x), nw, nullptr, e->xq, 1, K, c.eps, pdl, st)
-                : launch_quantize_q8_0(static_cast<const float *>(x), e->xq, K, pdl, st);
-            if (qe != cudaSuccess) return qe;
-            ++launches;
-            a.in_mode = GEMV_IN_Q8;
-            a.x = e->xq;
-            return launch_gemv(a, st);
-        }
+        // decode: records already in x (attention merge, gate/up epilogue), or
+        // RMSNorm + quantization in the mat-vec's prologue, which overlaps the
+        // weight stages the producer warp has in flight
+        if (T == 1) return launch_gemv(a, st);
         // prefill: RMSNorm rows (when asked), then the tensor-core mat-mul
         const float * xin = static_cast<const float *>(x);
         if (in == GEMV_IN_F32_RMS) {
@@ -211,23 +193,27 @@ static int engine_forward(alb_engine * e, int64_t T, bool pdl, int ncap_prefill 
             launches += 2;   // the two k_gather_add (the NCCL all-gathers are NCCL's kernels)
         }
     }
-    // final norm + lm_head on the last token (qwen3.cpp:235-238, 266-274)
+    // final norm + lm_head on the last token (qwen3.cpp:235-238, 266-274) through
+    // the generic mul_mat's vec_dot chains (the output matrix is not repacked,
+    // model.cpp:342-353), with the greedy argmax (sampler.cpp:34-36) fused: every
+    // CTA max-reduces its (logit, index) keys into e->key (cleared by the
+    // embedding kernel of this pass); on one GPU the last CTA writes the token
     {
         GemvArgs a;
-        a.W = e->lm_W; a.S = e->lm_S; a.N = e->V; a.K = e->E;
+        a.W = e->lm_W; a.N = e->V; a.K = e->E;
         a.in_mode = GEMV_IN_F32_RMS; a.x = e->x + (size_t)(T - 1) * e->E; a.norm_w = e->out_norm; a.eps = c.eps;
-        a.out_mode = GEMV_OUT_PLAIN; a.y = e->logits; a.pdl = pdl;
+        a.out_mode = GEMV_OUT_LOGITS; a.y = e->logits; a.pdl = pdl;
+        a.key = e->key; a.idx_base = e->v0;
+        a.ticket = reinterpret_cast<int *>(e->am_scratch);
+        a.next = e->tp == 1 ? e->next_dev : nullptr;
         ALB_CUDA_TRY(launch_gemv(a, st));
         ++launches;
     }
-    if (e->tp == 1) {
-        ALB_CUDA_TRY(launch_argmax(e->logits, e->V, 0, e->am_scratch, e->key, e->next_dev, pdl, st));
-        ++launches;
-    } else {
-        ALB_CUDA_TRY(launch_argmax(e->logits, e->V, e->v0, e->am_scratch, e->key, nullptr, pdl, st));
+    if (e->tp > 1) {
+        // the shards' keys: all-reduce MAX, then the index (first maximum overall)
         ALB_TRY(nccl_allreduce(e->comm, e->key, e->key, 1, 1, 1, st));
         ALB_CUDA_TRY(launch_key_to_index(e->key, e->next_dev, false, st));
-        launches += 2;   // argmax + key_to_index (the all-reduce is NCCL's)
+        launches += 1;   // key_to_index (the all-reduce is NCCL's)
     }
     e->launches_per_step = launches;
     return ALB_OK;
@@ -235,18 +221,6 @@ static int engine_forward(alb_engine * e, int64_t T, bool pdl, int ncap_prefill 
 
 static int engine_build_graph(alb_engine * e) {
     if (e->gexec) return ALB_OK;
-    if (e->use_mk) {
-        ALB_CUDA_TRY(cudaStreamBeginCapture(e->st, cudaStreamCaptureModeThreadLocal));
-        const cudaError_t le = launch_decode_step(e->mk, e->st);
-        cudaGraph_t g = nullptr;
-        const cudaError_t ce = cudaStreamEndCapture(e->st, &g);
-        if (le != cudaSuccess) { if (g) cudaGraphDestroy(g); alb_set_last_cuda_error(le, "decode step kernel"); return ALB_ERR_CUDA; }
-        ALB_CUDA_TRY(ce);
-        e->graph = g;
-        ALB_CUDA_TRY(cudaGraphInstantiate(&e->gexec, g, 0));
-        e->launches_per_step = 1;
-        return ALB_OK;
-    }
     ALB_CUDA_TRY(cudaStreamBeginCapture(e->st, cudaStreamCaptureModeThreadLocal));
     int rc = engine_forward(e, 1, true);
     if (rc == ALB_OK) {
@@ -278,13 +252,11 @@ static int engine_init_weights(alb_engine * e) {
     ALB_TRY(e->alloc(&e->tok, q4_gpu_bytes(c.n_vocab, E)));
     ALB_CUDA_TRY(gen_q4(e->tok, c.n_vocab, E, 0, 1, c.n_vocab, seed(-1, T_TOK_EMBD), 0, E, 0, e->table, st));
     if (c.tied) {
-        e->lm_W = e->tok + (size_t)e->v0 * (E / 2);
-        e->lm_S = e->tok + q4_scale_offset(c.n_vocab, E) + (size_t)e->v0 * q4_scale_pitch(E) * 2;
+        e->lm_W = e->tok + (size_t)e->v0 * q4_row_bytes(E);   // this rank's vocabulary rows
     } else {
         ALB_TRY(e->alloc(&e->out_w, q4_gpu_bytes(e->V, E)));
         ALB_CUDA_TRY(gen_q4(e->out_w, e->V, E, 0, 1, e->V, seed(-1, T_OUTPUT), e->v0, E, 0, e->table, st));
         e->lm_W = e->out_w;
-        e->lm_S = e->out_w + q4_scale_offset(e->V, E);
     }
     ALB_TRY(e->alloc(&e->out_norm, E));
     ALB_CUDA_TRY(gen_norm(e->out_norm, E, seed(-1, T_OUTPUT_NORM), e->table, st));
@@ -384,62 +356,6 @@ static int engine_init_acts(alb_engine * e) {
     return ALB_OK;
 }
 
-// Parameters and scratch of the persistent decode-step kernel.
-static int engine_init_mk(alb_engine * e) {
-    // opt-in (ALB_DECODE_MK=1): the one-graph multi-kernel step is the faster decode path
-    const char * env = getenv("ALB_DECODE_MK");
-    if (e->tp != 1 || !env || atoi(env) == 0) return ALB_OK;
-    const int ncta = alb_sm_count();
-    const int G = e->Hq / e->Hkv;
-    if (G > 4) return ALB_OK;
-    // attention: the cells of each kv head split over S CTAs, <= MK_ATT_MAX_CELLS each
-    // (ALB_MK_SPLITS lowers S for tuning)
-    int S = ncta / e->Hkv;
-    if (const char * sv = getenv("ALB_MK_SPLITS")) { const int v = atoi(sv); if (v >= 1 && v < S) S = v; }
-    if (S < 1 || (e->max_ctx + S - 1) / S > MK_ATT_MAX_CELLS) return ALB_OK;
-    if ((int64_t)(e->E / 32) * 48 > MK_STAGE_OFFSET) return ALB_OK;
-    int dev_sm_optin = 0;
-    cudaDeviceGetAttribute(&dev_sm_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, e->dev);
-    if ((size_t)dev_sm_optin < mk_smem_bytes()) return ALB_OK;
-    std::vector<MkLayer> hl(e->c.n_layer);
-    for (int l = 0; l < e->c.n_layer; ++l) {
-        alb_engine::Layer & L = e->layers[l];
-        MkLayer & m = hl[l];
-        m.qkv_W = L.qkv; m.qkv_S = L.qkv + q4_scale_offset(e->Nqkv, e->E);
-        m.o_W = L.o; m.o_S = L.o + q4_scale_offset(e->E, e->Dq);
-        m.gu_W = L.gu; m.gu_S = L.gu + q4_scale_offset(2 * (int64_t)e->F, e->E);
-        m.dn_W = L.down; m.dn_S = L.down + q4_scale_offset(e->E, e->F);
-        m.an = L.an; m.fn = L.fn; m.qn = L.qn; m.kn = L.kn; m.kc = L.kc; m.vc = L.vc;
-    }
-    ALB_TRY(e->alloc(&e->mk_layers, hl.size()));
-    ALB_CUDA_TRY(cudaMemcpy(e->mk_layers, hl.data(), hl.size() * sizeof(MkLayer), cudaMemcpyHostToDevice));
-    MkParams & p = e->mk;
-    p.n_layer = e->c.n_layer; p.E = e->E; p.Hq = e->Hq; p.Hkv = e->Hkv; p.F = e->F; p.V = e->V; p.Nqkv = e->Nqkv;
-    p.Dq = e->Dq; p.v0 = e->v0; p.rank = e->rank; p.eps = e->c.eps; p.scale = 1.0f / sqrtf((float)e->c.head_dim);
-    p.layers = e->mk_layers; p.lm_W = e->lm_W; p.lm_S = e->lm_S; p.out_norm = e->out_norm;
-    p.tok_W = e->tok; p.tok_S = e->tok + q4_scale_offset(e->c.n_vocab, e->E); p.rope = e->rope;
-    p.x = e->x; p.qkv = e->qkv; p.att = e->att; p.h = e->h; p.logits = e->logits;
-    p.tok = e->tok_dev; p.pos = e->pos_dev; p.next = e->next_dev; p.gen_out = e->gen_out; p.step = e->step_dev;
-    p.gen_cap = e->gen_cap; p.advance = 1; p.S = S;
-    const char * pf = getenv("ALB_MK_PF");
-    p.pf_stages = pf ? atoi(pf) : 8;
-    ALB_TRY(e->alloc(&p.smax, (size_t)e->Hkv * S * G));
-    ALB_TRY(e->alloc(&p.part, (size_t)e->Hkv * S * G * 129));
-    int * words = nullptr;
-    ALB_TRY(e->alloc(&words, 64 + 3 * e->Hkv));
-    ALB_CUDA_TRY(cudaMemset(words, 0, (64 + 3 * e->Hkv) * sizeof(int)));
-    p.bar_count = reinterpret_cast<unsigned *>(words);
-    p.bar_gen = reinterpret_cast<unsigned *>(words + 1);
-    p.am_ticket = words + 2;
-    p.tickets = words + 64;
-    p.grp = reinterpret_cast<unsigned *>(words + 64 + e->Hkv);
-    ALB_TRY(e->alloc(&p.cand, (size_t)ncta));
-    p.err = device_error_ptr();
-    p.ncta = ncta;
-    e->use_mk = true;
-    return ALB_OK;
-}
-
 static void engine_free(alb_engine * e) {
     if (!e) return;
     cudaSetDevice(e->dev);
@@ -524,7 +440,6 @@ extern "C" int alb_engine_create(const alb_qwen3_config * cfg, uint64_t seed, in
     if (rc == ALB_OK && tp_size > 1) rc = nccl_init(&e->comm, tp_rank, tp_size, nccl_id);
     if (rc == ALB_OK) rc = engine_init_weights(e);
     if (rc == ALB_OK) rc = engine_init_acts(e);
-    if (rc == ALB_OK) rc = engine_init_mk(e);
     if (rc != ALB_OK) { engine_free(e); return rc; }
     *out = e;
     return ALB_OK;
@@ -626,7 +541,7 @@ extern "C" int alb_engine_logits(alb_engine * e, float * host, int64_t n) {
 extern "C" int alb_engine_info(const alb_engine * e, int64_t * info, int32_t n) {
     ALB_CHECK_ARG(e && info && n >= 8);
     info[0] = e->V; info[1] = e->v0; info[2] = e->Hq; info[3] = e->Hkv; info[4] = e->F;
-    info[5] = e->launches_per_step; info[6] = (int64_t)e->bytes; info[7] = e->use_mk ? e->mk.S : e->fa_S_decode;
+    info[5] = e->launches_per_step; info[6] = (int64_t)e->bytes; info[7] = e->fa_S_decode;
     return ALB_OK;
 }
 
@@ -689,41 +604,6 @@ extern "C" int alb_engine_norm_weights(alb_engine * e, int32_t layer, int32_t ki
     ALB_CHECK_ARG(src && n == len);
     ALB_CUDA_TRY(cudaMemcpy(host, src, (size_t)n * 4, cudaMemcpyDeviceToHost));
     return ALB_OK;
-}
-
-// Measurement hook: one decode step of the persistent kernel with CTA 0
-// recording %globaltimer (ns) at each phase boundary into host[0..n).  Returns
-// the number of stamps written (ALB_ERR_UNSUPPORTED when the persistent kernel
-// is not in use).
-extern "C" int alb_engine_decode_trace(alb_engine * e, int32_t token, int32_t pos, int64_t * host, int32_t n) {
-    ALB_CHECK_ARG(e && host && n > 0 && token >= 0 && token < e->c.n_vocab && pos >= 0 && pos < e->max_ctx);
-    if (!e->use_mk) { alb_set_last_error_msg("persistent decode kernel not in use"); return ALB_ERR_UNSUPPORTED; }
-    ALB_CUDA_TRY(cudaSetDevice(e->dev));
-    int64_t * tr = nullptr;
-    constexpr int TN = 24576 + 36 * 8 * 160;   // covers every stamp index below (<= 160 CTAs)
-    ALB_CUDA_TRY(cudaMalloc(&tr, TN * sizeof(int64_t)));
-    cudaMemsetAsync(tr, 0, TN * sizeof(int64_t), e->st);
-    e->pinned[0] = token;
-    e->pinned[1] = pos;
-    cudaMemcpyAsync(e->tok_dev, &e->pinned[0], 4, cudaMemcpyHostToDevice, e->st);
-    cudaMemcpyAsync(e->pos_dev, &e->pinned[1], 4, cudaMemcpyHostToDevice, e->st);
-    MkParams p = e->mk;
-    p.trace = tr;
-    cudaError_t le = launch_decode_step(p, e->st);
-    std::vector<int64_t> h(TN);
-    if (le == cudaSuccess) le = cudaMemcpyAsync(h.data(), tr, TN * sizeof(int64_t), cudaMemcpyDeviceToHost, e->st);
-    if (le == cudaSuccess) le = cudaStreamSynchronize(e->st);
-    cudaFree(tr);
-    ALB_CUDA_TRY(le);
-    int m = 0;
-    while (m < 1024 && h[m] != 0) ++m;
-    // stamps [0, m) are phases; when n > 1024 the per-stage stamps of the
-    // mat-vec phases follow at [1024, 8192): (wait start, data ready, released),
-    // then per layer and CTA the attention (start, end) at [8192, 8192 + 36 * 2 * ncta),
-    // and per layer and CTA 8 attention sub-phase stamps at [24576, 24576 + 36 * 8 * ncta)
-    const int cp = n < TN ? n : TN;
-    memcpy(host, h.data(), (size_t)cp * sizeof(int64_t));
-    return m;
 }
 
 // Times the decode step's Q4_0 mat-vec launches alone (all layers + lm head, in
@@ -791,10 +671,10 @@ extern "C" int alb_engine_time_gemv(alb_engine * e, int32_t reps, float * us_per
     double bytes = 0.0;
     // the decode step's mat-vec launches with the step's input modes (outputs to
     // scratch so the engine state is unchanged)
-    auto add = [&](const uint8_t * W, const uint8_t * S, int64_t N, int64_t K, int in, const void * x, const float * nw,
+    auto add = [&](const uint8_t * W, int64_t N, int64_t K, int in, const void * x, const float * nw,
                    int out, float * y, const float * res) {
         GemvArgs a;
-        a.W = W; a.S = S ? S : W + q4_scale_offset(N, K); a.N = N; a.K = K;
+        a.W = W; a.N = N; a.K = K;
         a.in_mode = in; a.x = x; a.norm_w = nw; a.eps = e->c.eps;
         a.out_mode = out; a.y = y; a.residual = res; a.pdl = true;
         if (out == GEMV_OUT_SWIGLU) { a.yq = e->hq; a.ycnt = e->hcnt; }
@@ -802,17 +682,14 @@ extern "C" int alb_engine_time_gemv(alb_engine * e, int32_t reps, float * us_per
         const double in_bytes = in == GEMV_IN_Q8 ? K / 32 * 34.0 : in == GEMV_IN_F32 ? K * 4.0 : K * 8.0;
         bytes += (double)N * K * 18 / 32 + in_bytes + (out == GEMV_OUT_SWIGLU ? N / 2 : N) * 4.0;
     };
-    const bool fused_rms = e->E <= 2560;   // as engine_forward
     for (int l = 0; l < e->c.n_layer; ++l) {
         alb_engine::Layer & L = e->layers[l];
-        add(L.qkv, nullptr, e->Nqkv, e->E, fused_rms ? GEMV_IN_F32_RMS : GEMV_IN_Q8, fused_rms ? (const void *)e->x : e->xq,
-            L.an, GEMV_OUT_PLAIN, e->qkv, nullptr);
-        add(L.o, nullptr, e->E, e->Dq, GEMV_IN_Q8, e->xq, nullptr, GEMV_OUT_PLAIN, e->qkv, nullptr);
-        add(L.gu, nullptr, 2 * (int64_t)e->F, e->E, fused_rms ? GEMV_IN_F32_RMS : GEMV_IN_Q8,
-            fused_rms ? (const void *)e->x : e->xq, L.fn, GEMV_OUT_SWIGLU, e->h, nullptr);
-        add(L.down, nullptr, e->E, e->F, GEMV_IN_Q8, e->hq, nullptr, GEMV_OUT_PLAIN, e->qkv, nullptr);
+        add(L.qkv, e->Nqkv, e->E, GEMV_IN_F32_RMS, e->x, L.an, GEMV_OUT_PLAIN, e->qkv, nullptr);
+        add(L.o, e->E, e->Dq, GEMV_IN_Q8, e->xq, nullptr, GEMV_OUT_PLAIN, e->qkv, nullptr);
+        add(L.gu, 2 * (int64_t)e->F, e->E, GEMV_IN_F32_RMS, e->x, L.fn, GEMV_OUT_SWIGLU, e->h, nullptr);
+        add(L.down, e->E, e->F, GEMV_IN_Q8, e->hq, nullptr, GEMV_OUT_PLAIN, e->qkv, nullptr);
     }
-    add(e->lm_W, e->lm_S, e->V, e->E, GEMV_IN_F32_RMS, e->x, e->out_norm, GEMV_OUT_PLAIN, e->logits, nullptr);
+    add(e->lm_W, e->V, e->E, GEMV_IN_F32_RMS, e->x, e->out_norm, GEMV_OUT_PAIR, e->logits, nullptr);
     cudaGraph_t g = nullptr;
     cudaGraphExec_t ge = nullptr;
     ALB_CUDA_TRY(cudaStreamBeginCapture(e->st, cudaStreamCaptureModeThreadLocal));

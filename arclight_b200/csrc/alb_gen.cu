@@ -74,7 +74,7 @@ __device__ __forceinline__ float d_normal(const float * __restrict__ t, uint64_t
 
 // One thread per (row, block).  quantize_row_q4_0_ref: first max-abs element,
 // d = max / -8, id = 1/d, q = min(15, (int8)(x*id + 8.5)), d stored fp16.
-__global__ void k_gen_q4(uint8_t * __restrict__ Wn, uint16_t * __restrict__ Ws, int64_t K, int64_t sp,
+__global__ void k_gen_q4(uint8_t * __restrict__ W, int64_t K, int64_t sp,
                          int64_t dst_row0, int64_t dst_row_stride, int64_t n_rows, uint64_t seed,
                          int64_t src_row0, int64_t K_full, int64_t c0, const float * __restrict__ table, float stdv) {
     const int64_t nb = K / 32;
@@ -100,8 +100,9 @@ __global__ void k_gen_q4(uint8_t * __restrict__ Wn, uint16_t * __restrict__ Ws, 
         words[j >> 2] |= ((q0 | (q1 << 4)) & 0xFF) << (8 * (j & 3));
     }
     const int64_t drow = dst_row0 + r * dst_row_stride;
-    *reinterpret_cast<uint4 *>(Wn + drow * (K / 2) + 16 * b) = make_uint4(words[0], words[1], words[2], words[3]);
-    uint16_t * srow = Ws + drow * sp;
+    uint8_t * row = W + drow * q4_row_bytes(K);   // row-interleaved GPU layout
+    *reinterpret_cast<uint4 *>(row + 16 * b) = make_uint4(words[0], words[1], words[2], words[3]);
+    uint16_t * srow = reinterpret_cast<uint16_t *>(row + K / 2);
     srow[b] = alb_f2h(d);
     if (b == nb - 1)
         for (int64_t j = nb; j < sp; ++j) srow[j] = 0;
@@ -125,8 +126,8 @@ __global__ void k_gen_f16(uint16_t * __restrict__ dst, int64_t cells, int64_t ro
 cudaError_t gen_q4(uint8_t * W, int64_t N_total, int64_t K, int64_t dst_row0, int64_t dst_row_stride, int64_t n_rows,
                    uint64_t seed, int64_t src_row0, int64_t K_full, int64_t c0, const float * table, cudaStream_t st) {
     const int64_t n = n_rows * (K / 32);
-    uint16_t * S = reinterpret_cast<uint16_t *>(W + q4_scale_offset(N_total, K));
-    k_gen_q4<<<(unsigned)((n + 127) / 128), 128, 0, st>>>(W, S, K, q4_scale_pitch(K), dst_row0, dst_row_stride, n_rows,
+    (void)N_total;
+    k_gen_q4<<<(unsigned)((n + 127) / 128), 128, 0, st>>>(W, K, q4_scale_pitch(K), dst_row0, dst_row_stride, n_rows,
                                                          seed, src_row0, K_full, c0, table, 0.02f);
     return cudaGetLastError();
 }

@@ -15,16 +15,21 @@ enum GemvIn : int {
     GEMV_IN_F32_RMS = 2,  // fp32 [K]: RMSNorm (ops.cpp:680-724) * w, then quantized
 };
 
-// What a GEMV writes.
+// What a GEMV writes, and which of the reference's summation chains it runs.
+// PLAIN / SWIGLU / DOTS: nnml_gemv_q4_0_4x4_q8_0 (gemm.cpp:127-190), one fp32
+// fma chain per row over its blocks in order.  PAIR / LOGITS: the generic
+// mul_mat's nnml_vec_dot_q4_0_q8_0 (arm.cpp:633-692): eight lane chains
+// (block parity x 4 partial dots) then a fixed add tree.
 enum GemvOut : int {
     GEMV_OUT_PLAIN = 0,   // y[n] = acc (+ residual[n])
     GEMV_OUT_SWIGLU = 1,  // rows interleaved (gate n, up n): y[n] = silu(gate)*up (ops.cpp:1038-1092)
     GEMV_OUT_DOTS = 2,    // y[n] = acc and I[n][b] = int32 block dots (parity check)
+    GEMV_OUT_PAIR = 3,    // y[n] = vec_dot(W[n], x)
+    GEMV_OUT_LOGITS = 4,  // PAIR, plus the greedy argmax key (and, with `next`, the token)
 };
 
 struct GemvArgs {
-    const uint8_t * W = nullptr;   // nibble plane of the alb Q4_0 GPU layout (row 0 of this view)
-    const uint8_t * S = nullptr;   // fp16 scale plane (row 0 of this view)
+    const uint8_t * W = nullptr;   // row 0 of this view of the alb Q4_0 GPU layout (16-byte aligned)
     int64_t N = 0, K = 0;          // physical rows, columns
     int in_mode = GEMV_IN_Q8;
     const void * x = nullptr;      // block_q8_0 or fp32 per in_mode
@@ -35,14 +40,21 @@ struct GemvArgs {
     const float * residual = nullptr;
     int32_t * dots = nullptr;
     bool pdl = false;              // launch as a programmatic dependent
-    int ctas_per_sm = 0;           // 0 = default
-    int variant = 0;               // 0/1 = direct loads + L2 prefetch (default), 2 = bulk-copy pipeline
-    int stage_budget = 0;          // bytes of shared-memory stages (0 = default)
+    int ctas = 0;                  // grid size (0 = one CTA per SM)
+    int smem_budget = 0;           // bytes of dynamic shared memory (0 = default)
     int * err = nullptr;           // device error word (filled by launch_gemv)
     // SwiGLU only, optional: block_q8_0 records of y [N/2/32] written by the
     // warp that completes each 32-value block; ycnt [N/2/32] zeroed once
     uint8_t * yq = nullptr;
     int * ycnt = nullptr;
+    // LOGITS only: running argmax key (ordered value << 32 | ~index; zeroed
+    // before the launch), row index offset of this shard, and optionally the
+    // token output: the last CTA (ticket, zero before the first launch, re-armed)
+    // turns the key into the index
+    unsigned long long * key = nullptr;
+    int64_t idx_base = 0;
+    int * ticket = nullptr;
+    int32_t * next = nullptr;
 };
 
 struct FlashArgs {
@@ -61,6 +73,8 @@ struct FlashArgs {
     bool pdl = false;
 };
 size_t flash_attn_ws_bytes(int Hq, int Hkv, int T, int S, int ncap);
+// false when the call's kernels need no workspace (launch_flash_attn's path choice)
+bool flash_attn_uses_ws(int Hq, int Hkv, int T, int S, int ncap);
 cudaError_t launch_flash_attn(const FlashArgs & f, cudaStream_t st);
 
 struct QkvArgs {
@@ -77,8 +91,8 @@ struct QkvArgs {
     bool pdl = false;
 };
 cudaError_t launch_qk_norm_rope_kv(const QkvArgs & a, cudaStream_t st);
-cudaError_t launch_embed(const uint8_t * Wn, const uint8_t * Ws, int64_t vocab, int64_t E, const int32_t * tokens,
-                         int T, float * x, bool pdl, cudaStream_t st);
+cudaError_t launch_embed(const uint8_t * W, int64_t vocab, int64_t E, const int32_t * tokens, int T, float * x,
+                         unsigned long long * key_reset, bool pdl, cudaStream_t st);
 // argmax over x[0..n): scratch >= 64*8 + 16 bytes with its ticket word zero at first use
 cudaError_t launch_argmax(const float * x, int64_t n, int64_t idx_base, void * scratch,
                           unsigned long long * key_out, int32_t * idx_out, bool pdl, cudaStream_t st);
@@ -95,6 +109,13 @@ cudaError_t launch_swiglu_q8(const float * g, const float * u, float * y, void *
                              cudaStream_t st);
 cudaError_t launch_swiglu(const float * g, const float * u, float * y, int64_t n, bool pdl, cudaStream_t st);
 
+// Sets a kernel's dynamic shared-memory limit on the current device when
+// `bytes` exceeds what was set there before (thread safe, per device).
+cudaError_t ensure_dynamic_smem(const void * func, size_t bytes);
+template <typename F> inline cudaError_t ensure_smem(F * func, size_t bytes) {
+    return ensure_dynamic_smem(reinterpret_cast<const void *>(func), bytes);
+}
+
 // Device-side error word (bounded waits that expire set it; see alb_device_error).
 enum : int { ALB_DEVERR_NONE = 0, ALB_DEVERR_MBAR_TIMEOUT = 1, ALB_DEVERR_FLAG_TIMEOUT = 2, ALB_DEVERR_BAD_TOKEN = 3 };
 // Host: the current device's error word (allocated once per device, zeroed).
@@ -109,19 +130,19 @@ cudaError_t launch_prefill_gemm(const uint8_t * W, int64_t N, int64_t K, const f
                                 int64_t M, float * y, int64_t y_stride, const float * residual, bool swiglu, void * ws,
                                 int * err, bool pdl, cudaStream_t st);
 
-// alb Q4_0 GPU layout: nibble plane [N][K/2] bytes, then (256-aligned) the fp16
-// scale plane [N][q4_scale_pitch(K)] (row pitch padded to 16 bytes so that every
-// row range is a legal bulk-copy source).
+// alb Q4_0 GPU layout, row-interleaved: row n occupies q4_row_bytes(K) bytes at
+// n * q4_row_bytes(K): the K/2 nibble bytes (block b's 16 qs bytes at 16 b),
+// then the K/32 fp16 scales padded with zeros to q4_scale_pitch(K) entries (a
+// 16-byte multiple).  Any run of consecutive rows is one contiguous, 16-byte
+// aligned range: one bulk copy brings a whole stage of rows.
 __host__ __device__ inline int64_t q4_scale_pitch(int64_t K) {   // in fp16 elements
     return ((K / 32) + 7) & ~(int64_t)7;
 }
-__host__ __device__ inline size_t q4_scale_offset(int64_t N, int64_t K) {
-    const size_t nib = (size_t)N * (size_t)(K / 2);
-    return (nib + 255) & ~(size_t)255;
+__host__ __device__ inline int64_t q4_row_bytes(int64_t K) {
+    return K / 2 + q4_scale_pitch(K) * 2;
 }
 __host__ __device__ inline size_t q4_gpu_bytes(int64_t N, int64_t K) {
-    const size_t sc = (size_t)N * (size_t)q4_scale_pitch(K) * 2;
-    return (q4_scale_offset(N, K) + sc + 255) & ~(size_t)255;
+    return ((size_t)N * (size_t)q4_row_bytes(K) + 255) & ~(size_t)255;
 }
 
 }  // namespace alb

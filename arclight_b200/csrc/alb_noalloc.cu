@@ -6,8 +6,13 @@
 //
 // Limits and rules (also stated in include/alb_cuda.h):
 //   * the workspace alb_flash_attn_workspace_bytes(...) of the call must fit
-//     ALB_FLASH_ATTN_STATIC_BYTES (4 MiB); larger calls are rejected with
-//     ALB_ERR_INVALID before anything is launched;
+//     ALB_FLASH_ATTN_STATIC_BYTES (4 MiB) when the call's path uses one (the
+//     split kernels); larger calls are rejected with ALB_ERR_INVALID before
+//     anything is launched.  Prefill ubatches (one split) and single-split
+//     decode calls whose scores fit shared memory use no workspace and are
+//     never rejected for size;
+//   * the array's address is looked up once per device and kept: a
+//     cudaDeviceReset of that device afterwards is not supported;
 //   * there is one such array per device, shared by every call on that
 //     device: calls that overlap in time (other streams, other host threads)
 //     race on it and must not be issued;
@@ -60,7 +65,8 @@ extern "C" int alb_flash_attn_static(const float * q, const uint16_t * k_cache, 
     const int G = n_head / n_head_kv;
     ALB_CHECK_ARG(G == 1 || G == 2 || G == 4 || G == 8);
     ALB_CHECK_ARG(splits >= 1 && splits <= 65535 && (int64_t)pos0 + T < (int64_t)1 << 30);
-    const size_t need = flash_attn_ws_bytes(n_head, n_head_kv, (int)T, splits, (int)(pos0 + T));
+    const bool uses_ws = flash_attn_uses_ws(n_head, n_head_kv, (int)T, splits, (int)(pos0 + T));
+    const size_t need = uses_ws ? flash_attn_ws_bytes(n_head, n_head_kv, (int)T, splits, (int)(pos0 + T)) : 0;
     if (need > ALB_FLASH_ATTN_STATIC_BYTES) {
         alb_set_last_error_msg("alb_flash_attn_static: workspace exceeds ALB_FLASH_ATTN_STATIC_BYTES");
         return ALB_ERR_INVALID;

@@ -12,18 +12,21 @@ namespace alb {
 // ------------------------------------------------------------------ embedding
 // GET_ROWS on the Q4_0 token table (ops.cpp:12-52, dequantize_row_q4_0
 // types.cpp:337-350): x[t][j] = (q - 8) * d.  One thread per 32-value block.
-__global__ void k_embed_q4_0(const uint8_t * __restrict__ Wn, const uint16_t * __restrict__ Ws, int64_t sp,
-                             const int32_t * __restrict__ tokens, int T, int64_t E, int64_t vocab,
-                             float * __restrict__ x, int * err) {
+// The first kernel of a forward pass also clears the greedy-argmax key that
+// the lm head of this pass accumulates into (key may be null).
+__global__ void k_embed_q4_0(const uint8_t * __restrict__ W, const int32_t * __restrict__ tokens, int T, int64_t E,
+                             int64_t vocab, float * __restrict__ x, int * err, unsigned long long * key) {
     const int64_t nb = E / 32;
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (int64_t)T * nb) return;
     const int t = (int)(i / nb), b = (int)(i - (int64_t)t * nb);
     alb_pdl_wait();
+    if (key && i == 0) *key = 0ull;
     int32_t tok = tokens[t];
     if (tok < 0 || tok >= vocab) { atomicExch(err, 3); tok = 0; }
-    const uint4 v = *reinterpret_cast<const uint4 *>(Wn + (size_t)tok * (E / 2) + 16 * b);
-    const float d = alb_h2f(Ws[(size_t)tok * sp + b]);
+    const uint8_t * row = W + (size_t)tok * q4_row_bytes(E);   // row-interleaved GPU layout
+    const uint4 v = *reinterpret_cast<const uint4 *>(row + 16 * b);
+    const float d = alb_h2f(reinterpret_cast<const uint16_t *>(row + E / 2)[b]);
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
     float * o = x + (size_t)t * E + 32 * b;
 #pragma unroll
@@ -758,16 +761,20 @@ size_t flash_attn_ws_bytes(int Hq, int Hkv, int T, int S, int ncap) {
 // shared memory available for the fused kernel's score array
 static constexpr size_t FA_FUSED_SMEM = 160 * 1024;
 
+// Which kernels a call takes: the token-tiled prefill kernel (T > 1, one
+// split) and the fused one-CTA kernel (one split, scores fit shared memory)
+// use no workspace; every other call runs the split kernels on it.
+bool flash_attn_uses_ws(int Hq, int Hkv, int T, int S, int ncap) {
+    if (T > 1 && S == 1) return false;
+    if (S == 1 && (size_t)(Hq / Hkv) * ncap * 4 <= FA_FUSED_SMEM) return false;
+    return true;
+}
+
 template <int G>
 static cudaError_t launch_fa_core(const FlashArgs & f, cudaStream_t st) {
     if (f.T > 1 && f.S == 1) {   // prefill ubatch: token tiles share the staged cells
-        static bool pattr = false;
-        if (!pattr) {
-            cudaError_t e = cudaFuncSetAttribute(k_fa_prefill<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 (int)FP_SMEM);
-            if (e != cudaSuccess) return e;
-            pattr = true;
-        }
+        cudaError_t e = ensure_smem(k_fa_prefill<G>, FP_SMEM);
+        if (e != cudaSuccess) return e;
         constexpr int TQ = FP_R / G;
         const dim3 grid((unsigned)f.Hkv, (unsigned)((f.T + TQ - 1) / TQ));
         return alb_launch(k_fa_prefill<G>, grid, dim3(256), FP_SMEM, st, f.pdl, f.q, f.kc, f.vc, f.Hq, f.Hkv, f.T,
@@ -776,13 +783,9 @@ static cudaError_t launch_fa_core(const FlashArgs & f, cudaStream_t st) {
     const int n_max = f.ncap;   // cells attended by the last token at most
     if (f.S == 1 && (size_t)G * n_max * 4 <= FA_FUSED_SMEM) {
         const size_t smem = (size_t)G * n_max * 4;
-        static bool attr = false;   // the kernel's static shared memory counts against the 48 KiB default too
-        if (!attr) {
-            cudaError_t e = cudaFuncSetAttribute(k_fa_fused<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 (int)FA_FUSED_SMEM);
-            if (e != cudaSuccess) return e;
-            attr = true;
-        }
+        // the kernel's static shared memory counts against the 48 KiB default too
+        cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void *>(k_fa_fused<G>), FA_FUSED_SMEM);
+        if (e != cudaSuccess) return e;
         return alb_launch(k_fa_fused<G>, dim3((unsigned)f.Hkv, (unsigned)f.T), dim3(128), smem, st, f.pdl, f.q, f.kc,
                           f.vc, f.Hq, f.Hkv, f.T, f.pos0, f.pos_dev, f.scale, f.out);
     }
@@ -793,17 +796,11 @@ static cudaError_t launch_fa_core(const FlashArgs & f, cudaStream_t st) {
     float * smax = reinterpret_cast<float *>(ws + l.smax_off);
     float * scores = reinterpret_cast<float *>(ws + l.scores_off);
     double * part = reinterpret_cast<double *>(ws + l.part_off);
-    static bool split_attr = false;   // per instantiation; legal inside stream capture
-    if (!split_attr) {
-        cudaError_t e = cudaFuncSetAttribute(k_fa_scores<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)FA_SCORES_SMEM);
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(k_fa_pv<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fa_pv_smem<G>());
-        if (e != cudaSuccess) return e;
-        split_attr = true;
-    }
+    cudaError_t e = ensure_smem(k_fa_scores<G>, FA_SCORES_SMEM);
+    if (e == cudaSuccess) e = ensure_smem(k_fa_pv<G>, fa_pv_smem<G>());
+    if (e != cudaSuccess) return e;
     dim3 grid((unsigned)f.Hkv, (unsigned)f.T, (unsigned)f.S);
-    cudaError_t e = alb_launch(k_fa_scores<G>, grid, dim3(128), FA_SCORES_SMEM, st, f.pdl, f.q, f.kc, f.Hq, f.Hkv, f.T,
+    e = alb_launch(k_fa_scores<G>, grid, dim3(128), FA_SCORES_SMEM, st, f.pdl, f.q, f.kc, f.Hq, f.Hkv, f.T,
                                f.pos0, f.pos_dev, f.scale, f.S, f.ncap, scores, smax);
     if (e != cudaSuccess) return e;
     e = alb_launch(k_fa_pv<G>, grid, dim3(128), fa_pv_smem<G>(), st, f.pdl, f.vc, f.Hq, f.Hkv, f.T, f.pos0,
@@ -1003,12 +1000,11 @@ cudaError_t launch_swiglu_q8(const float * g, const float * u, float * y, void *
                       static_cast<uint8_t *>(yq), nb);
 }
 
-cudaError_t launch_embed(const uint8_t * Wn, const uint8_t * Ws, int64_t vocab, int64_t E, const int32_t * tokens,
-                         int T, float * x, bool pdl, cudaStream_t st) {
+cudaError_t launch_embed(const uint8_t * W, int64_t vocab, int64_t E, const int32_t * tokens, int T, float * x,
+                         unsigned long long * key_reset, bool pdl, cudaStream_t st) {
     const int64_t n = (int64_t)T * (E / 32);
-    return alb_launch(k_embed_q4_0, dim3((unsigned)((n + 127) / 128)), dim3(128), 0, st, pdl, Wn,
-                      reinterpret_cast<const uint16_t *>(Ws), q4_scale_pitch(E), tokens, T, E, vocab, x,
-                      device_error_ptr());
+    return alb_launch(k_embed_q4_0, dim3((unsigned)((n + 127) / 128)), dim3(128), 0, st, pdl, W, tokens, T, E, vocab,
+                      x, device_error_ptr(), key_reset);
 }
 
 cudaError_t launch_qk_norm_rope_kv(const QkvArgs & a, cudaStream_t st) {

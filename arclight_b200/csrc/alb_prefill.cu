@@ -1,14 +1,17 @@
 // Prefill Q4_0 x Q8_0 mat-mul on the sm_100a tensor cores (tcgen05.mma
 // kind::i8, accumulators in TMEM).
 //
-// Y[m][n] = sum_b I(m,n,b) * dx[m][b] * dw[n][b], I = sum over the 32 values of
-// block b of q8[m][k] * (q4[n][k] - 8) (gemm.cpp:495-974, the same arithmetic
-// as the mat-vec: int32 block dots, exact block terms summed in double, one
-// rounding to fp32).  Because the scales change every 32 values of K, every
-// block is one MMA (M = 128 tokens, N = 64 rows of W, K = 32) into a fresh
-// TMEM accumulator, and the epilogue warps read it back (tcgen05.ld) and add
-// its exact double terms while the tensor core computes the next block into
-// the other half of the TMEM allocation.
+// Y[m][n] = fp32 fma chain over the blocks b in order of
+// float(I(m,n,b)) * (dx[m][b] * dw[n][b]), I = sum over the 32 values of block
+// b of q8[m][k] * (q4[n][k] - 8): the arithmetic of the reference's
+// nnml_gemm_q4_0_4x4_q8_0 (gemm.cpp:495-974: scvtf #4 of 16 I, fmul of the two
+// scales, fmla into the row's accumulator, block after block), which is the
+// mat-vec's chain, so every output row is bit-identical to the mat-vec of that
+// row.  Because the scales change every 32 values of K, every block is one MMA
+// (M = 128 tokens, N = 64 rows of W, K = 32) into a fresh TMEM accumulator,
+// and the epilogue warps read it back (tcgen05.ld) and advance their fp32
+// chains while the tensor core computes the next block into the other half of
+// the TMEM allocation.
 //
 // Operands in shared memory, K-major without swizzle (core matrices of 8 rows
 // x 16 bytes; the two 16-byte halves of a block are the two K chunks):
@@ -33,9 +36,9 @@ struct PgShared {
     alignas(128) int8_t a[PG_STAGES][PG_M * 32];   // MMA operand A per stage (core-matrix layout)
     alignas(128) int8_t b[2][PG_N * 32];           // MMA operand B (unpacked) for blocks b & 1
     alignas(16) uint8_t nib[PG_STAGES][PG_N * 16]; // W nibbles as loaded
-    alignas(16) double dx[PG_STAGES][PG_M];        // activation block scales (fp16-rounded)
+    alignas(16) float dx[PG_STAGES][PG_M];         // activation block scales (fp16-rounded)
     alignas(16) uint32_t dww[PG_STAGES][PG_N];     // 4-byte words holding the weight block scale
-    alignas(16) double dwd[2][PG_N];               // weight block scale as the bits of (dw * 2^-1008)
+    alignas(16) float dwf[2][PG_N];                // weight block scale as fp32
     uint64_t mma_done[2];
     uint32_t tmem_base;
     int abort_flag;
@@ -61,11 +64,11 @@ __device__ __forceinline__ int pg_off(int r, int c) { return (r >> 3) * 256 + c 
 __device__ __forceinline__ void pg_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void pg_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// Activations of the GEMM: xq int8 [M][K] row-major, xd double [M][K/32]
+// Activations of the GEMM: xq int8 [M][K] row-major, xd float [M][K/32]
 // (fp16-rounded Q8_0 scale), from fp32 rows (one warp per 32-value block,
 // quantize_row_q8_0 semantics, arm.cpp:1819-1853).
 __global__ void k_pg_quant(const float * __restrict__ x, int64_t M, int64_t K, int8_t * __restrict__ xq,
-                           double * __restrict__ xd) {
+                           float * __restrict__ xd) {
     alb_pdl_wait();
     const int lane = threadIdx.x & 31;
     const int64_t nb = K / 32;
@@ -77,19 +80,19 @@ __global__ void k_pg_quant(const float * __restrict__ x, int64_t M, int64_t K, i
     uint16_t dh;
     q8_block_lane(v, q, dh);
     xq[m * K + b * 32 + lane] = q;
-    if (lane == 0) xd[m * nb + b] = (double)alb_h2f(dh);
+    if (lane == 0) xd[m * nb + b] = alb_h2f(dh);
 }
 
 // Same from block_q8_0 rows (the reference layout, nnml.h:695-700).
 __global__ void k_pg_from_q8(const uint8_t * __restrict__ src, int64_t M, int64_t K, int8_t * __restrict__ xq,
-                             double * __restrict__ xd) {
+                             float * __restrict__ xd) {
     alb_pdl_wait();
     const int64_t nb = K / 32;
     const int64_t blk = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (blk >= M * nb) return;
     const uint8_t * s = src + blk * 34;
     const uint16_t dh = (uint16_t)(s[0] | (s[1] << 8));
-    xd[blk] = (double)alb_h2f(dh);
+    xd[blk] = alb_h2f(dh);
     int8_t * d = xq + blk * 32;   // row-major [M][K]: block blk = m * nb + b lands at m*K + 32 b
     for (int j = 0; j < 32; ++j) d[j] = (int8_t)s[2 + j];
 }
@@ -104,12 +107,12 @@ __device__ __forceinline__ bool pg_wait(PgShared & sh, int buf, uint32_t parity,
 template <int OUT>   // 0: y = acc (+ residual), 1: SwiGLU of interleaved (gate, up) rows
 __global__ void __launch_bounds__(PG_THREADS, 2)
 k_prefill_gemm(const uint8_t * __restrict__ Wn, const uint8_t * __restrict__ Ws, int64_t N, int64_t K,
-               const int8_t * __restrict__ xq, const double * __restrict__ xd, int64_t M, float * __restrict__ y,
+               const int8_t * __restrict__ xq, const float * __restrict__ xd, int64_t M, float * __restrict__ y,
                int64_t y_stride, const float * __restrict__ residual, int * err) {
     __shared__ PgShared sh;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t n0 = (int64_t)blockIdx.x * PG_N, m0 = (int64_t)blockIdx.y * PG_M;
-    const int64_t nb = K / 32, rb = K / 2, sp = q4_scale_pitch(K);
+    const int64_t nb = K / 32, rb = q4_row_bytes(K);   // row-interleaved layout: nibbles at 0, scales at K/2
     if (tid == 0) {
         alb_mbar_init(&sh.mma_done[0], 1);
         alb_mbar_init(&sh.mma_done[1], 1);
@@ -130,9 +133,9 @@ k_prefill_gemm(const uint8_t * __restrict__ Wn, const uint8_t * __restrict__ Ws,
     // epilogue mapping: warp w reads TMEM lanes 32*(w%4).., columns 32*(w/4)..
     const int quarter = warp & 3, chalf = warp >> 2;
     const int row = quarter * 32 + lane;                 // token row within the tile
-    double acc[32];
+    float acc[32];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) acc[j] = 0.0;
+    for (int j = 0; j < 32; ++j) acc[j] = 0.0f;
     uint32_t issued = 0, waited = 0;                     // MMAs committed / completions consumed (per buffer parity)
 
     // cp.async of block kb's inputs into ring stage kb % PG_STAGES (zero-filled past M / N)
@@ -154,15 +157,15 @@ k_prefill_gemm(const uint8_t * __restrict__ Wn, const uint8_t * __restrict__ Ws,
             } else if (tid < 2 * PG_N) {
                 const int n = tid - PG_N;
                 const bool in = n0 + n < N;
-                const uint8_t * src = Ws + (in ? (((n0 + n) * sp + kb) * 2 & ~(int64_t)3) : 0);
+                const uint8_t * src = Ws + (in ? ((n0 + n) * rb + ((kb * 2) & ~(int64_t)3)) : 0);
                 asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;"
                              :: "r"(pg_smem(&sh.dww[st][n])), "l"(src), "r"(in ? 4 : 0) : "memory");
             } else {
                 const int r = tid - 2 * PG_N;
                 const bool in = m0 + r < M;
-                const double * src = xd + (in ? (m0 + r) * nb + kb : 0);
-                asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;"
-                             :: "r"(pg_smem(&sh.dx[st][r])), "l"(src), "r"(in ? 8 : 0) : "memory");
+                const float * src = xd + (in ? (m0 + r) * nb + kb : 0);
+                asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;"
+                             :: "r"(pg_smem(&sh.dx[st][r])), "l"(src), "r"(in ? 4 : 0) : "memory");
             }
         }
         asm volatile("cp.async.commit_group;" ::: "memory");   // one group per block (empty past the end)
@@ -183,10 +186,15 @@ k_prefill_gemm(const uint8_t * __restrict__ Wn, const uint8_t * __restrict__ Ws,
                        "=r"(c[29]), "=r"(c[30]), "=r"(c[31])
                      : "r"(taddr));
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        const double dxr = sh.dx[st][row] * 0x1p1008;   // finite: d <= 65504 < 2^16
-        const double * dw = sh.dwd[s] + chalf * 32;
+        const float dxr = sh.dx[st][row];
+        const float * dw = sh.dwf[s] + chalf * 32;
+        // float(I) exactly as 2^23 * 1.5 + I - 2^23 * 1.5 (|I| < 2^22): integer add +
+        // fp32 subtract instead of a conversion; dx * dw is exact (11 x 11 bits)
 #pragma unroll
-        for (int j = 0; j < 32; ++j) acc[j] = fma(alb_i2d((int)c[j]), dxr * dw[j], acc[j]);
+        for (int j = 0; j < 32; ++j) {
+            const float t = __fsub_rn(__int_as_float((int)c[j] + 0x4B400000), 12582912.0f);
+            acc[j] = __fmaf_rn(t, __fmul_rn(dxr, dw[j]), acc[j]);
+        }
         pg_fence_before();
     };
 
@@ -199,7 +207,7 @@ k_prefill_gemm(const uint8_t * __restrict__ Wn, const uint8_t * __restrict__ Ws,
         if (tid >= PG_N && tid < 2 * PG_N) {   // weight scales of block b, once per block
             const int n = tid - PG_N;
             const uint32_t wd = sh.dww[st][n];
-            sh.dwd[s][n] = alb_h2d_bits((((n0 + n) * sp + b) & 1) ? (wd >> 16) : (wd & 0xFFFFu));
+            sh.dwf[s][n] = alb_h2f((uint16_t)((b & 1) ? (wd >> 16) : (wd & 0xFFFFu)));
         }
         if (tid < PG_N) {   // B: 16 nibble bytes of row tid -> 2 chunks of int8 (q - 8)
             const uint4 w = *reinterpret_cast<const uint4 *>(sh.nib[st] + tid * 16);
@@ -263,7 +271,7 @@ k_prefill_gemm(const uint8_t * __restrict__ Wn, const uint8_t * __restrict__ Ws,
         for (int j = 0; j < 32; ++j) {
             const int64_t n = nbase + j;
             if (n < N) {
-                const float v = __double2float_rn(acc[j]);
+                const float v = acc[j];
                 y[m * y_stride + n] = residual ? __fadd_rn(v, residual[m * y_stride + n]) : v;
             }
         }
@@ -272,14 +280,14 @@ k_prefill_gemm(const uint8_t * __restrict__ Wn, const uint8_t * __restrict__ Ws,
         for (int j = 0; j < 16; ++j) {
             const int64_t n = nbase + 2 * j;
             if (n + 1 < N)
-                y[m * y_stride + n / 2] = alb_swiglu1(__double2float_rn(acc[2 * j]), __double2float_rn(acc[2 * j + 1]));
+                y[m * y_stride + n / 2] = alb_swiglu1(acc[2 * j], acc[2 * j + 1]);
         }
     }
 }
 
 size_t prefill_ws_bytes(int64_t M, int64_t K) {
     const size_t q = ((size_t)M * K + 255) & ~(size_t)255;
-    return q + (size_t)M * (K / 32) * 8;
+    return q + (size_t)M * (K / 32) * 4;
 }
 
 // x fp32 [M][K] (already normalized if needed) -> y: workspace prefill_ws_bytes(M, K)
@@ -287,7 +295,7 @@ cudaError_t launch_prefill_gemm(const uint8_t * W, int64_t N, int64_t K, const f
                                 int64_t M, float * y, int64_t y_stride, const float * residual, bool swiglu, void * ws,
                                 int * err, bool pdl, cudaStream_t st) {
     int8_t * xq = reinterpret_cast<int8_t *>(ws);
-    double * xd = reinterpret_cast<double *>(reinterpret_cast<uint8_t *>(ws) + (((size_t)M * K + 255) & ~(size_t)255));
+    float * xd = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(ws) + (((size_t)M * K + 255) & ~(size_t)255));
     const int64_t nblk = M * (K / 32);
     cudaError_t e;
     if (x) e = alb_launch(k_pg_quant, dim3((unsigned)((nblk + 7) / 8)), dim3(256), 0, st, pdl, x, M, K, xq, xd);
@@ -295,12 +303,12 @@ cudaError_t launch_prefill_gemm(const uint8_t * W, int64_t N, int64_t K, const f
                         reinterpret_cast<const uint8_t *>(xq_blocks), M, K, xq, xd);
     if (e != cudaSuccess) return e;
     const dim3 grid((unsigned)((N + PG_N - 1) / PG_N), (unsigned)((M + PG_M - 1) / PG_M));
-    const uint8_t * Ws = W + q4_scale_offset(N, K);
+    const uint8_t * Ws = W + K / 2;   // scales of row n at Ws + n * q4_row_bytes(K)
     if (swiglu)
         return alb_launch(k_prefill_gemm<1>, grid, dim3(PG_THREADS), 0, st, pdl, W, Ws, N, K, (const int8_t *)xq,
-                          (const double *)xd, M, y, y_stride, residual, err);
+                          (const float *)xd, M, y, y_stride, residual, err);
     return alb_launch(k_prefill_gemm<0>, grid, dim3(PG_THREADS), 0, st, pdl, W, Ws, N, K, (const int8_t *)xq,
-                      (const double *)xd, M, y, y_stride, residual, err);
+                      (const float *)xd, M, y, y_stride, residual, err);
 }
 
 }  // namespace alb

@@ -2,18 +2,19 @@
 // layout (sm_100a).
 //
 // Reference semantics: nnml_gemv_q4_0_4x4_q8_0 (nnml/src/ops/arm/gemm.cpp:127-190)
-// driven by forward_mul_mat (nnml/src/ops/arm/arm.cpp:1855-1925); activations
-// quantized by quantize_row_q8_0 (arm.cpp:1819-1853).
+// driven by forward_mul_mat (arm.cpp:1855-1925) for the projections, and
+// nnml_vec_dot_q4_0_q8_0 (arm.cpp:401-692) driven by forward_mul_mat_generic
+// (common.cpp:120-248) for the lm head; activations quantized by
+// quantize_row_q8_0 (arm.cpp:1819-1853).  The GPU computes the same fp32 fma
+// chains in the same block order, so every output is bit-identical to the
+// reference's NEON arithmetic (the int32 block dots are exact integers either
+// way; only the order of the fp32 accumulation matters).
 //
-// Design: the weight is HBM-bound streamed once.  The GPU layout splits each
-// row into a 16-byte-per-block nibble plane and an fp16 scale plane so a warp
-// reads 512 contiguous bytes per step with 16-byte non-allocating loads.  One
-// warp owns one row (or a gate/up row pair); lanes stride over the K/32 blocks;
-// a 32-value block dot is 8 dp4a on the raw nibbles minus 8 * sum(a), which is
-// the reference's int32 I(n,b) exactly.  The Q8_0 activation lives in shared
-// memory in a padded 48-byte record per block (conflict-free 128-bit reads).
-// Weight loads of a warp's first row are issued before griddepcontrol.wait so
-// they overlap the previous kernel's tail under programmatic dependent launch.
+// Design: the weights are HBM-bound and streamed once, by bulk copies into a
+// shared-memory ring issued before the kernel waits on its predecessor; the
+// block dots are computed in parallel from shared memory (8 dp4a per block on
+// the raw nibbles minus 8 * sum(a)), and the short fp32 chains run one lane per
+// row over the staged exact terms.
 #include <cstdio>
 #include <cstdlib>
 
@@ -24,9 +25,9 @@ namespace alb {
 
 
 // ---------------------------------------------------------------- repack
-// block_q4_0 [N][K/32] (18-byte blocks) <-> nibble plane + pitched scale plane.
+// block_q4_0 [N][K/32] (18-byte blocks) <-> the row-interleaved GPU layout.
 __global__ void k_repack_q4_0(uint8_t * __restrict__ dst, const uint8_t * __restrict__ src,
-                              int64_t n_blocks, int64_t nb, int64_t spitch, size_t scale_off) {
+                              int64_t n_blocks, int64_t nb, int64_t spitch, int64_t rowb) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n_blocks) return;
     const uint16_t * s = reinterpret_cast<const uint16_t *>(src + i * 18);  // 2-byte aligned
@@ -38,22 +39,22 @@ __global__ void k_repack_q4_0(uint8_t * __restrict__ dst, const uint8_t * __rest
     v.y = (uint32_t)q[2] | ((uint32_t)q[3] << 16);
     v.z = (uint32_t)q[4] | ((uint32_t)q[5] << 16);
     v.w = (uint32_t)q[6] | ((uint32_t)q[7] << 16);
-    reinterpret_cast<uint4 *>(dst)[i] = v;
     const int64_t row = i / nb, b = i - row * nb;
-    uint16_t * sc = reinterpret_cast<uint16_t *>(dst + scale_off) + row * spitch;
+    *reinterpret_cast<uint4 *>(dst + row * rowb + 16 * b) = v;
+    uint16_t * sc = reinterpret_cast<uint16_t *>(dst + row * rowb + nb * 16);
     sc[b] = s[0];
     if (b == nb - 1)
         for (int64_t j = nb; j < spitch; ++j) sc[j] = 0;   // defined padding
 }
 
 __global__ void k_unpack_q4_0(uint8_t * __restrict__ dst, const uint8_t * __restrict__ src,
-                              int64_t n_blocks, int64_t nb, int64_t spitch, size_t scale_off) {
+                              int64_t n_blocks, int64_t nb, int64_t rowb) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n_blocks) return;
-    const uint4 v = reinterpret_cast<const uint4 *>(src)[i];
-    uint16_t * d = reinterpret_cast<uint16_t *>(dst + i * 18);
     const int64_t row = i / nb, b = i - row * nb;
-    d[0] = reinterpret_cast<const uint16_t *>(src + scale_off)[row * spitch + b];
+    const uint4 v = *reinterpret_cast<const uint4 *>(src + row * rowb + 16 * b);
+    uint16_t * d = reinterpret_cast<uint16_t *>(dst + i * 18);
+    d[0] = reinterpret_cast<const uint16_t *>(src + row * rowb + nb * 16)[b];
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) { d[1 + 2 * j] = (uint16_t)(w[j] & 0xFFFF); d[2 + 2 * j] = (uint16_t)(w[j] >> 16); }
@@ -79,438 +80,591 @@ cudaError_t launch_quantize_q8_0(const float * x, void * xq, int64_t n, bool pdl
                       static_cast<uint8_t *>(xq), nb);
 }
 
-// CONSUMERS_ONLY: synchronise the GEMV_WARPS consumer warps with named barrier 1
-// (the producer warp of the bulk-copy kernel does not take part).
-template <int IN, bool CONSUMERS_ONLY>
-__device__ __forceinline__ void gemv_prologue_impl(const GemvArgs & a, int * xs, int nb, uint4 * stage) {
+// ---------------------------------------------------------------- mat-vec
+// Shared-memory plan of one k_mv launch (computed on the host per K and mode).
+//   [0, ns * stage_bytes)        weight stages: R consecutive rows of the GPU
+//                                layout [R][q4_row_bytes(K)] (one bulk copy each)
+//   cb_off                       chain buffers (ncb of cb_bytes); the prologue's
+//                                staging of the input vector aliases them
+//   xs_off                       Q8_0 activation records, one per block
+//   bar_off                      mbarriers full[ns] empty[ns] done[ncb] free[ncb]
+struct MvPlan {
+    int R;                  // rows per stage (<= 64; <= 16 for the pair chain)
+    int RC;                 // rows per chain warp (each chain warp takes a contiguous half)
+    int ns, ncb;            // weight stages, chain buffers
+    uint32_t stage_bytes;   // R * row bytes
+    uint32_t cbp;           // chain-buffer row pitch in bytes (an odd multiple of 16)
+    uint32_t cbs;           // pair chain: row pitch of the dx*dw array (an odd number of words)
+    uint32_t cb_bytes;      // one chain buffer
+    uint32_t cb_off, xs_off, bar_off;
+    uint32_t smem;
+};
+
+static constexpr int MV_CW = 12;                       // block-dot warps
+static constexpr int MV_RU = 2;                        // rows per dot iteration (independent work)
+static constexpr int MV_CH = 2;                        // chain warps (alternate stages)
+static constexpr int MV_PW = MV_CW + MV_CH;            // the producer warp's index
+static constexpr int MV_THREADS = (MV_CW + MV_CH + 1) * 32;
+static constexpr int MV_NT = (MV_CW + MV_CH) * 32;     // threads of the prologue barrier
+
+// Activation records of the mat-vec: q as 8 packed words, the block scale d
+// (fp16-rounded, as float), sum(q), and for the pair chain the four partial
+// sums s_l over elements {4l..4l+3} u {16+4l..16+4l+3} (one per vdotq lane).
+// Strides of 48 B / 80 B keep the 16-byte reads of 8 consecutive blocks in
+// distinct bank groups.
+template <bool PAIR> struct XRec { static constexpr int INTS = PAIR ? 20 : 12; };
+
+template <bool PAIR>
+__device__ __forceinline__ void mv_store_rec(int * xs, int b, int lane, int8_t q, uint16_t dh) {
+    const int qi = (int)(uint8_t)q;
+    const int b1 = __shfl_down_sync(0xffffffffu, qi, 1);
+    const int b2 = __shfl_down_sync(0xffffffffu, qi, 2);
+    const int b3 = __shfl_down_sync(0xffffffffu, qi, 3);
+    int g4 = (int)q;   // sum over the lane's group of 4 (valid at lanes 4k)
+    g4 += __shfl_down_sync(0xffffffffu, g4, 1);
+    g4 += __shfl_down_sync(0xffffffffu, g4, 2);
+    int s = (int)q;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const int hi16 = __shfl_down_sync(0xffffffffu, g4, 16);
+    int * rec = xs + b * XRec<PAIR>::INTS;
+    if ((lane & 3) == 0) rec[lane >> 2] = qi | (b1 << 8) | (b2 << 16) | (b3 << 24);
+    if (lane == 0) {
+        rec[8] = __float_as_int(alb_h2f(dh));
+        rec[9] = s;
+    }
+    if constexpr (PAIR) {
+        if ((lane & 3) == 0 && lane < 16) rec[10 + (lane >> 2)] = g4 + hi16;
+    }
+}
+
+// Prologue of the consumer warps: the CTA's Q8_0 records of the input vector.
+//   IN_Q8     block_q8_0 records from global memory (staged with 16-byte loads);
+//   IN_F32    fp32 x quantized here (quantize_row_q8_0, arm.cpp:1819-1853);
+//   IN_F32_RMS RMSNorm * w first (ops.cpp:680-724: double sum of the fp32
+//             squares, mean rounded to float, 1/sqrtf(mean + eps)).
+// `stage` is scratch of gemv_stage_bytes(K, IN); ends with the consumers'
+// named barrier (the producer warp does not take part).
+template <int IN, bool PAIR>
+__device__ __forceinline__ void mv_prologue(const GemvArgs & a, int * xs, int nb, uint4 * stage) {
+    constexpr int XR = XRec<PAIR>::INTS;
+    constexpr int NT = MV_NT;
+    constexpr int NW = NT / 32;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if constexpr (IN == GEMV_IN_Q8) {
-        // stage the block_q8_0 vector (16-byte loads when aligned; never past
-        // its nb*34 bytes), then unpack per block
         const int nbytes = nb * 34;
+        const uint8_t * src8 = static_cast<const uint8_t *>(a.x);
         if ((reinterpret_cast<uintptr_t>(a.x) & 15) == 0) {
             const int n16 = nbytes / 16;
             const uint4 * src = static_cast<const uint4 *>(a.x);
-            for (int i = tid; i < n16; i += GEMV_WARPS * 32) stage[i] = src[i];
-            for (int i = n16 * 16 + tid; i < nbytes; i += GEMV_WARPS * 32)
-                reinterpret_cast<uint8_t *>(stage)[i] = static_cast<const uint8_t *>(a.x)[i];
+            for (int i = tid; i < n16; i += NT) stage[i] = src[i];
+            for (int i = n16 * 16 + tid; i < nbytes; i += NT) reinterpret_cast<uint8_t *>(stage)[i] = src8[i];
         } else {
-            for (int i = tid; i < nbytes; i += GEMV_WARPS * 32)
-                reinterpret_cast<uint8_t *>(stage)[i] = static_cast<const uint8_t *>(a.x)[i];
+            for (int i = tid; i < nbytes; i += NT) reinterpret_cast<uint8_t *>(stage)[i] = src8[i];
         }
-        if constexpr (CONSUMERS_ONLY) asm volatile("bar.sync 1, %0;" :: "n"(GEMV_WARPS * 32) : "memory");
-        else __syncthreads();
+        asm volatile("bar.sync 1, %0;" :: "n"(NT) : "memory");
         const uint8_t * xq = reinterpret_cast<const uint8_t *>(stage);
-        for (int b = tid; b < nb; b += GEMV_WARPS * 32) {
+        for (int b = tid; b < nb; b += NT) {
             const uint16_t * s = reinterpret_cast<const uint16_t *>(xq + (size_t)b * 34);
-            int * rec = xs + b * XREC_INTS;
-            int sum = 0;
+            int * rec = xs + b * XR;
+            int sum = 0, part[8];
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
                 const uint32_t v = (uint32_t)s[1 + 2 * k] | ((uint32_t)s[2 + 2 * k] << 16);
                 rec[k] = (int)v;
-                sum += (int8_t)(v & 0xFF) + (int8_t)((v >> 8) & 0xFF) + (int8_t)((v >> 16) & 0xFF) + (int8_t)(v >> 24);
+                part[k] = (int8_t)(v & 0xFF) + (int8_t)((v >> 8) & 0xFF) + (int8_t)((v >> 16) & 0xFF) + (int8_t)(v >> 24);
+                sum += part[k];
             }
             rec[8] = __float_as_int(alb_h2f(s[0]));
             rec[9] = sum;
+            if constexpr (PAIR) {
+#pragma unroll
+                for (int l = 0; l < 4; ++l) rec[10 + l] = part[l] + part[4 + l];
+            }
         }
     } else {
-        // x (and the norm weights) staged in shared memory with 16-byte copies,
-        // then the sum of squares in a 256-thread strided order and the blocks
-        // quantized from shared memory (no dependent global loads per block)
         const float * x = static_cast<const float *>(a.x);
         float * xf = reinterpret_cast<float *>(stage);
-        float * wf = xf + a.K;   // RMS only
+        float * wf = xf + a.K;
         const int K = (int)a.K;
         const bool vec = (K & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
                          (IN != GEMV_IN_F32_RMS || (reinterpret_cast<uintptr_t>(a.norm_w) & 15) == 0);
         if (vec) {
             const float4 * x4 = reinterpret_cast<const float4 *>(x);
             const float4 * w4 = reinterpret_cast<const float4 *>(a.norm_w);
-            for (int i = tid; i < K / 4; i += GEMV_WARPS * 32) {
+            for (int i = tid; i < K / 4; i += NT) {
                 reinterpret_cast<float4 *>(xf)[i] = x4[i];
                 if constexpr (IN == GEMV_IN_F32_RMS) reinterpret_cast<float4 *>(wf)[i] = w4[i];
             }
         } else {
-            for (int i = tid; i < K; i += GEMV_WARPS * 32) {
+            for (int i = tid; i < K; i += NT) {
                 xf[i] = x[i];
                 if constexpr (IN == GEMV_IN_F32_RMS) wf[i] = a.norm_w[i];
             }
         }
-        if constexpr (CONSUMERS_ONLY) asm volatile("bar.sync 1, %0;" :: "n"(GEMV_WARPS * 32) : "memory");
-        else __syncthreads();
+        asm volatile("bar.sync 1, %0;" :: "n"(NT) : "memory");
         float scale = 1.0f;
         if constexpr (IN == GEMV_IN_F32_RMS) {
-            // sum of float squares accumulated in double (ops.cpp:703-710)
-            __shared__ double red[GEMV_WARPS];
+            // every fp32 square is exact in double and the sum of K of them is too,
+            // so this order gives the reference's sequential double sum
+            __shared__ double red[NW];
             double s = 0.0;
-            for (int i = tid; i < K; i += GEMV_WARPS * 32) { const float v = xf[i]; s += (double)__fmul_rn(v, v); }
+            for (int i = tid; i < K; i += NT) { const float v = xf[i]; s += (double)__fmul_rn(v, v); }
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
             if (lane == 0) red[warp] = s;
-            if constexpr (CONSUMERS_ONLY) asm volatile("bar.sync 1, %0;" :: "n"(GEMV_WARPS * 32) : "memory");
-            else __syncthreads();
+            asm volatile("bar.sync 1, %0;" :: "n"(NT) : "memory");
             double t = 0.0;
 #pragma unroll
-            for (int w = 0; w < GEMV_WARPS; ++w) t += red[w];
+            for (int w = 0; w < NW; ++w) t += red[w];
             const float mean = (float)(t / (double)a.K);
             scale = 1.0f / sqrtf(__fadd_rn(mean, a.eps));
         }
-        for (int b = warp; b < nb; b += GEMV_WARPS) {
+        for (int b = warp; b < nb; b += NW) {
             float v = xf[b * 32 + lane];
             if constexpr (IN == GEMV_IN_F32_RMS) v = __fmul_rn(__fmul_rn(v, scale), wf[b * 32 + lane]);
             int8_t q; uint16_t dh;
             q8_block_lane(v, q, dh);
-            store_xrec(xs, b, lane, q, dh);
+            mv_store_rec<PAIR>(xs, b, lane, q, dh);
         }
     }
+    asm volatile("bar.sync 1, %0;" :: "n"(NT) : "memory");
 }
 
-// Shared memory after the activation records: the raw block_q8_0 vector
-// (IN_Q8) or the fp32 input (and norm weights) of the prologue.
+// Shared memory of the prologue's staging: the raw block_q8_0 vector (IN_Q8)
+// or the fp32 input (and norm weights).
 __host__ __device__ inline size_t gemv_stage_bytes(int64_t K, int in_mode) {
     const size_t q8 = ((size_t)(K / 32) * 34 + 15) / 16 * 16;
     const size_t f32 = in_mode == GEMV_IN_F32 ? (size_t)K * 4 : in_mode == GEMV_IN_F32_RMS ? (size_t)K * 8 : 0;
     return q8 > f32 ? q8 : f32;
 }
 
-template <int IN>
-__device__ __forceinline__ void gemv_prologue(const GemvArgs & a, int * xs, int nb, uint4 * stage) {
-    gemv_prologue_impl<IN, false>(a, xs, nb, stage);
-}
-template <int IN>
-__device__ __forceinline__ void gemv_prologue_bar(const GemvArgs & a, int * xs, int nb, uint4 * stage) {
-    gemv_prologue_impl<IN, true>(a, xs, nb, stage);
-}
-
-// L2 prefetch of [p, p + bytes) in <= 64 KiB bulk requests (16-byte granules).
-__device__ __forceinline__ void l2_prefetch(const void * p, size_t bytes) {
-    const uint8_t * c = static_cast<const uint8_t *>(p);
-    const uintptr_t a0 = reinterpret_cast<uintptr_t>(c) & ~(uintptr_t)15;
-    const uintptr_t a1 = (reinterpret_cast<uintptr_t>(c) + bytes + 15) & ~(uintptr_t)15;
-    for (uintptr_t a = a0; a < a1; a += 65536) {
-        const uint32_t n = (uint32_t)((a1 - a) < 65536 ? (a1 - a) : 65536);
-        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" :: "l"(a), "r"(n) : "memory");
-    }
+// Greedy-argmax key: ordered fp32 bits above the inverted index, so the
+// largest key is the largest value and, among equal values, the first index
+// (std::max_element, sampler.cpp:34-36).  Same encoding as k_argmax.
+__device__ __forceinline__ unsigned long long mv_key(float v, int64_t idx) {
+    uint32_t u = __float_as_uint(v);
+    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((unsigned long long)u << 32) | (unsigned long long)(uint32_t)(0x7FFFFFFF - (int32_t)idx);
 }
 
-// After lane 0 wrote the SwiGLU output y[item]: with a.yq set, the warp whose
-// value completes a 32-value block quantizes that block (quantize_row_q8_0 of
-// the fp32 values, the down projection's input) and re-arms its counter.
-// Writers publish y before their arrival (fence + atomic); the last one reads
-// the block from L2 after its own fence.  Called by the whole warp.
-__device__ __forceinline__ void gemv_swiglu_q8_tail(const GemvArgs & a, int64_t item, int lane) {
-    if (!a.yq) return;
-    const int64_t b = item >> 5;
-    int last = 0;
-    if (lane == 0) {
+// SwiGLU outputs [i0, i1) written by this warp: per touched 32-value block,
+// count them on the block's arrival counter; the warp that completes a block
+// quantizes it (quantize_row_q8_0 of the fp32 values: the down projection's
+// input records) and re-arms the counter.  Whole warp; writers fenced before.
+__device__ __forceinline__ void mv_swiglu_q8(const GemvArgs & a, int64_t i0, int64_t i1, int lane) {
+    for (int64_t j = i0 >> 5; j <= (i1 - 1) >> 5; ++j) {
+        const int64_t lo = i0 > 32 * j ? i0 : 32 * j, hi = i1 < 32 * j + 32 ? i1 : 32 * j + 32;
+        const int cnt = (int)(hi - lo);
+        int last = 0;
+        if (lane == 0) last = atomicAdd(&a.ycnt[j], cnt) + cnt == 32;
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (!last) continue;
         __threadfence();
-        last = atomicAdd(&a.ycnt[b], 1) == 31;
-    }
-    last = __shfl_sync(0xffffffffu, last, 0);
-    if (!last) return;
-    __threadfence();
-    const float v = __ldcg(a.y + b * 32 + lane);
-    int8_t q; uint16_t dh;
-    q8_block_lane(v, q, dh);
-    uint8_t * blk = a.yq + b * 34;
-    if (lane == 0) {
-        *reinterpret_cast<uint16_t *>(blk) = dh;
-        a.ycnt[b] = 0;
-    }
-    blk[2 + lane] = (uint8_t)q;
-}
-
-// Each CTA owns a contiguous range of row items; before waiting on the previous
-// kernel it asks the TMA unit to pull its whole weight range (nibbles and
-// scales, in PF-byte windows ahead of the compute) into L2, and each warp loads
-// its first item into registers.  The compute loop then mostly hits L2.
-template <int ITERS, int RPW, int IN, int OUT>
-__global__ void __launch_bounds__(GEMV_WARPS * 32)
-k_gemv_direct(const GemvArgs a) {
-    extern __shared__ int4 smem_i4[];
-    int * xs = reinterpret_cast<int *>(smem_i4);
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int nb = (int)(a.K / 32);
-    const size_t row_bytes = (size_t)a.K / 2;
-    const uint8_t * Wn = a.W;
-    const uint16_t * Ws = reinterpret_cast<const uint16_t *>(a.S);
-    const int64_t sp = q4_scale_pitch(a.K);
-    const int64_t n_items = a.N / RPW;
-    const int64_t it0 = n_items * blockIdx.x / gridDim.x;
-    const int64_t it1 = n_items * (blockIdx.x + 1) / gridDim.x;
-    constexpr size_t PF = 96 * 1024;      // prefetch window per CTA (nibble bytes)
-    const size_t item_bytes = row_bytes * RPW;
-    int64_t pf_item = it0;                // first item not yet prefetched
-    auto prefetch_upto = [&](int64_t item_end) {
-        if (item_end > it1) item_end = it1;
-        if (item_end <= pf_item) return;
-        l2_prefetch(Wn + pf_item * item_bytes, (size_t)(item_end - pf_item) * item_bytes);
-        l2_prefetch(Ws + pf_item * RPW * sp, (size_t)(item_end - pf_item) * RPW * sp * 2);
-        pf_item = item_end;
-    };
-    const int64_t pf_items = (int64_t)(PF / item_bytes) + 1;
-    if (threadIdx.x == 0) prefetch_upto(it0 + pf_items);
-
-    uint4 w[RPW][ITERS];
-    uint16_t dw[RPW][ITERS];
-    auto load = [&](int64_t it) {
-#pragma unroll
-        for (int r = 0; r < RPW; ++r) {
-            const int64_t row = it * RPW + r;
-            const uint8_t * wr = Wn + row * row_bytes;
-            const uint16_t * sr = Ws + row * sp;
-#pragma unroll
-            for (int i = 0; i < ITERS; ++i) {
-                const int b = lane + 32 * i;
-                if (b < nb) { w[r][i] = alb_ld_stream(wr + 16 * b); dw[r][i] = __ldg(sr + b); }
-            }
+        const float v = __ldcg(a.y + j * 32 + lane);
+        int8_t q; uint16_t dh;
+        q8_block_lane(v, q, dh);
+        uint8_t * blk = a.yq + j * 34;
+        if (lane == 0) {
+            *reinterpret_cast<uint16_t *>(blk) = dh;
+            a.ycnt[j] = 0;
         }
-    };
-    int64_t item = it0 + warp;
-    if (item < it1) load(item);   // weights do not depend on the previous kernel
-
-    alb_pdl_wait();
-    gemv_prologue<IN>(a, xs, nb, reinterpret_cast<uint4 *>(xs + nb * XREC_INTS));
-    __syncthreads();
-    alb_pdl_trigger();
-
-    for (; item < it1; item += GEMV_WARPS) {
-        if (warp == 0 && lane == 0) prefetch_upto(item + pf_items);
-        double acc[RPW];
-#pragma unroll
-        for (int r = 0; r < RPW; ++r) acc[r] = 0.0;
-#pragma unroll
-        for (int i = 0; i < ITERS; ++i) {
-            const int b = lane + 32 * i;
-            if (b < nb) {
-                const int4 * rec = reinterpret_cast<const int4 *>(xs + b * XREC_INTS);
-                const int4 a_lo = rec[0], a_hi = rec[1];
-                const int2 ds = reinterpret_cast<const int2 *>(rec + 2)[0];
-                const float dx = __int_as_float(ds.x);
-#pragma unroll
-                for (int r = 0; r < RPW; ++r) {
-                    const int I = q4q8_dot(w[r][i], a_lo, a_hi, ds.y);
-                    if constexpr (OUT == GEMV_OUT_DOTS) a.dots[(item * RPW + r) * nb + b] = I;
-                    acc[r] = fma((double)I, (double)__fmul_rn(dx, alb_h2f(dw[r][i])), acc[r]);
-                }
-            }
-        }
-        const int64_t cur = item;
-        if (item + GEMV_WARPS < it1) load(item + GEMV_WARPS);  // next item's weights in flight
-#pragma unroll
-        for (int r = 0; r < RPW; ++r) acc[r] = alb_warp_sum_d(acc[r]);
-        if (lane == 0 && a.y) {
-            if constexpr (OUT == GEMV_OUT_SWIGLU) {
-                const float g = __double2float_rn(acc[0]), u = __double2float_rn(acc[1]);
-                a.y[cur] = alb_swiglu1(g, u);
-            } else {
-#pragma unroll
-                for (int r = 0; r < RPW; ++r) {
-                    const int64_t row = cur * RPW + r;
-                    const float yv = __double2float_rn(acc[r]);
-                    a.y[row] = a.residual ? __fadd_rn(yv, a.residual[row]) : yv;
-                }
-            }
-        }
-        if constexpr (OUT == GEMV_OUT_SWIGLU) gemv_swiglu_q8_tail(a, cur, lane);
+        blk[2 + lane] = (uint8_t)q;
     }
 }
 
-// ---------------------------------------------------------------- bulk-copy pipeline
-// One producer warp streams the CTA's contiguous row range through an NS-stage
-// shared-memory ring with cp.async.bulk (16-byte aligned 1-D copies, one for
-// the nibbles and one for the scales of GEMV_WARPS*RPW rows, completion counted
-// on the stage's mbarrier).  It never waits on the previous kernel: under PDL
-// the first NS stages are in flight while the previous grid drains.  The
-// GEMV_WARPS consumer warps wait (bounded) on the full barrier, each computes
-// its RPW rows of the stage from shared memory and releases the slot.
-struct TmaPlan {
-    int ns;            // stages
-    int rs;            // rows per stage
-    uint32_t nib_bytes, sc_bytes, stage_bytes, xs_bytes;
-    size_t smem;
-};
-
-__host__ __device__ inline TmaPlan tma_plan(int64_t K, int rpw, int max_stage_budget, int in_mode) {
-    TmaPlan p;
-    const int64_t nb = K / 32;
-    p.rs = GEMV_WARPS * rpw;
-    p.nib_bytes = (uint32_t)(p.rs * (K / 2));
-    p.sc_bytes = (uint32_t)(p.rs * q4_scale_pitch(K) * 2);
-    p.stage_bytes = p.nib_bytes + p.sc_bytes;
-    p.ns = (int)(max_stage_budget / p.stage_bytes);
-    if (p.ns < 2) p.ns = 2;
-    if (p.ns > 8) p.ns = 8;
-    p.xs_bytes = (uint32_t)(nb * XREC_INTS * 4 + gemv_stage_bytes(K, in_mode));
-    p.smem = (size_t)p.ns * p.stage_bytes + p.xs_bytes + 2 * 8 * p.ns;
-    return p;
-}
-
-template <int ITERS, int RPW, int IN, int OUT>
-__global__ void __launch_bounds__((GEMV_WARPS + 1) * 32)
-k_gemv_tma(const GemvArgs a, const TmaPlan plan) {
-    extern __shared__ int4 smem_i4[];
-    uint8_t * smem = reinterpret_cast<uint8_t *>(smem_i4);
-    uint8_t * stages = smem;
-    int * xs = reinterpret_cast<int *>(smem + (size_t)plan.ns * plan.stage_bytes);
-    uint64_t * full = reinterpret_cast<uint64_t *>(smem + (size_t)plan.ns * plan.stage_bytes + plan.xs_bytes);
-    uint64_t * empty = full + plan.ns;
-
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int nb = (int)(a.K / 32);
-    const int64_t sp = q4_scale_pitch(a.K);
-    const size_t row_bytes = (size_t)a.K / 2;
-    const int64_t n_items = a.N / RPW;
-    const int64_t it0 = n_items * blockIdx.x / gridDim.x;
-    const int64_t it1 = n_items * (blockIdx.x + 1) / gridDim.x;
-    const int n_groups = (int)((it1 - it0 + GEMV_WARPS - 1) / GEMV_WARPS);
-    const int NS = plan.ns;
-
-    if (threadIdx.x == GEMV_WARPS * 32) {
-        for (int i = 0; i < NS; ++i) { alb_mbar_init(&full[i], 1); alb_mbar_init(&empty[i], GEMV_WARPS); }
+// Batch-1 Q4_0 x Q8_0 mat-vec with the reference's summation order.
+//
+// Each CTA owns a contiguous range of rows.  Its producer warp streams them
+// through an ns-stage shared-memory ring, R whole rows per stage (nibbles and
+// scales, two bulk copies), and never waits on the previous kernel: under
+// programmatic dependent launch the first stages are in flight while the
+// previous grid drains.  For each stage the 8 consumer warps compute the int32
+// block dots I(n, b) of its R x K/32 blocks (lanes over consecutive blocks of
+// one row: conflict-free 16-byte reads) and store the terms
+// (float(I), f32(dx) * f32(dw)) -- both exact -- in a chain buffer; then one
+// warp (stages rotate over the warps) runs, one lane per row, the fp32 fma
+// chain over the blocks in order: acc = fma(float(I), dx*dw, acc)
+// (nnml_gemv_q4_0_4x4_q8_0, gemm.cpp:179-181; vcvtq_n_f32_s32(16 I, 4) is
+// float(I) exactly).  The pair variant follows nnml_vec_dot_q4_0_q8_0
+// (arm.cpp:633-692, the generic mul_mat of the lm head): four lanes per row,
+// lane l accumulating partial dot l of even blocks and of odd blocks in two
+// chains, then ((l0+l1)+(l2+l3)) of each, even plus odd.
+//
+// Every wait is bounded; on a timeout the kernel records an error code,
+// stops its loops and (producer) waits for its copies in flight before exit.
+template <int IN, int OUT>
+__global__ void __launch_bounds__(MV_THREADS, 2)
+k_mv(const GemvArgs a, const MvPlan p) {
+    constexpr bool PAIR = OUT == GEMV_OUT_PAIR || OUT == GEMV_OUT_LOGITS;
+    constexpr int XR = XRec<PAIR>::INTS;
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ int s_abort;
+    __shared__ unsigned long long s_best[MV_CH];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int nb = (int)(a.K >> 5);
+    const uint32_t rowb = (uint32_t)q4_row_bytes(a.K);   // bytes per weight row (nibbles, then scales)
+    const uint32_t scol = (uint32_t)(a.K >> 1);           // scales' offset in a row
+    constexpr int US = OUT == GEMV_OUT_SWIGLU ? 2 : 1;   // SwiGLU rows come in (gate, up) pairs
+    const int64_t units = a.N / US;
+    const int64_t n0 = units * blockIdx.x / gridDim.x * US, n1 = units * (blockIdx.x + 1) / gridDim.x * US;
+    const int R = p.R;
+    const int nst = (int)((n1 - n0 + R - 1) / R);
+    uint64_t * full = reinterpret_cast<uint64_t *>(smem + p.bar_off);
+    uint64_t * empty = full + p.ns;
+    uint64_t * done = empty + p.ns;
+    uint64_t * freeb = done + p.ncb;
+    int * xs = reinterpret_cast<int *>(smem + p.xs_off);
+    uint8_t * cbase = smem + p.cb_off;
+    if (tid == 0) {
+        for (int i = 0; i < p.ns; ++i) { alb_mbar_init(&full[i], 1); alb_mbar_init(&empty[i], MV_CW); }
+        for (int i = 0; i < p.ncb; ++i) { alb_mbar_init(&done[i], MV_CW); alb_mbar_init(&freeb[i], MV_CH); }
+        s_abort = 0;
         alb_mbar_fence_init();
     }
+    if (tid < MV_CH) s_best[tid] = 0ull;
     __syncthreads();
+    // the next kernel may launch now (and start its own weight stream); it waits
+    // for this grid's completion before it reads anything this grid writes
+    alb_pdl_trigger();
 
-    if (warp == GEMV_WARPS) {
+    if (warp == MV_PW) {
         // ------------------------------------------------ producer warp
         if (lane == 0) {
-            bool ok = true;
-            int issued = 0;
-            for (int g = 0; g < n_groups && ok; ++g) {
-                const int st = g % NS;
-                if (g >= NS && !alb_mbar_wait(&empty[st], (uint32_t)((g / NS - 1) & 1))) { ok = false; break; }
-                const int64_t ig = it0 + (int64_t)g * GEMV_WARPS;
-                const int64_t items = (it1 - ig) < GEMV_WARPS ? (it1 - ig) : GEMV_WARPS;
-                const int64_t r0 = ig * RPW, rows = items * RPW;
-                const uint32_t nbytes = (uint32_t)(rows * row_bytes), sbytes = (uint32_t)(rows * sp * 2);
-                uint8_t * dst = stages + (size_t)st * plan.stage_bytes;
-                alb_mbar_expect_tx(&full[st], nbytes + sbytes);
-                alb_bulk_g2s(dst, a.W + r0 * row_bytes, nbytes, &full[st]);
-                alb_bulk_g2s(dst + plan.nib_bytes, a.S + r0 * sp * 2, sbytes, &full[st]);
-                issued = g + 1;
+            int g = 0;
+            for (; g < nst; ++g) {
+                const int slot = g % p.ns;
+                if (g >= p.ns && !alb_mbar_wait(&empty[slot], (uint32_t)((g / p.ns - 1) & 1))) {
+                    atomicExch(a.err, ALB_DEVERR_MBAR_TIMEOUT);
+                    s_abort = 1;
+                    break;
+                }
+                const int64_t r0 = n0 + (int64_t)g * R;
+                const uint32_t bytes = (uint32_t)((n1 - r0) < R ? (n1 - r0) : R) * rowb;
+                alb_mbar_expect_tx(&full[slot], bytes);
+                alb_bulk_g2s(smem + (size_t)slot * p.stage_bytes, a.W + r0 * rowb, bytes, &full[slot]);
             }
-            if (!ok) atomicExch(a.err, ALB_DEVERR_MBAR_TIMEOUT);
-            // never leave with copies in flight: the last stages' phases must complete
-            for (int g = issued - NS < 0 ? 0 : issued - NS; g < issued; ++g)
-                alb_mbar_wait(&full[g % NS], (uint32_t)((g / NS) & 1));
+            // never exit with copies in flight
+            for (int j = g - p.ns < 0 ? 0 : g - p.ns; j < g; ++j)
+                alb_mbar_wait(&full[j % p.ns], (uint32_t)((j / p.ns) & 1));
         }
         return;
     }
 
-    // ---------------------------------------------------- consumer warps
+    // ------------------------------------- dot and chain warps: the input records
     alb_pdl_wait();
-    gemv_prologue_bar<IN>(a, xs, nb, reinterpret_cast<uint4 *>(xs + nb * XREC_INTS));
-    asm volatile("bar.sync 1, %0;" :: "n"(GEMV_WARPS * 32) : "memory");
-    alb_pdl_trigger();
+    mv_prologue<IN, PAIR>(a, xs, nb, reinterpret_cast<uint4 *>(cbase));
 
-    for (int g = 0; g < n_groups; ++g) {
-        const int st = g % NS;
-        if (!alb_mbar_wait(&full[st], (uint32_t)((g / NS) & 1))) {
+    if (warp < MV_CW) {
+        // ---------------------------------------------------- block-dot warps
+        // This warp's lanes own blocks b = 32 * group + lane for the whole launch
+        // (their Q8_0 records stay in registers); each stage, the m warps of the
+        // group take its rows j, j + m, ..., MV_RU rows per iteration.
+        // dot warp w: block group w % nbg, row phase w / nbg among the
+        // ceil((MV_CW - group) / nbg) warps of that group (every group gets one:
+        // nb <= 32 * MV_CW)
+        const int nbg = (nb + 31) >> 5;
+        const int bg = warp % nbg, jr = warp / nbg, m = (MV_CW - bg + nbg - 1) / nbg;
+        const int b = bg * 32 + lane;
+        const bool valid = b < nb;
+        int4 lo = make_int4(0, 0, 0, 0), hi = lo;
+        int asum = 0, sg0 = 0, sg1 = 0, sg2 = 0, sg3 = 0;
+        float dxv = 0.0f;
+        if (valid) {
+            const int * rec = xs + b * XR;
+            lo = *reinterpret_cast<const int4 *>(rec);
+            hi = *reinterpret_cast<const int4 *>(rec + 4);
+            dxv = __int_as_float(rec[8]);
+            if constexpr (!PAIR) {
+                asum = rec[9];
+            } else {
+                const int4 ds = *reinterpret_cast<const int4 *>(rec + 8);    // d, sum, s0, s1
+                const int2 s23 = *reinterpret_cast<const int2 *>(rec + 12);  // s2, s3
+                sg0 = ds.z; sg1 = ds.w; sg2 = s23.x; sg3 = s23.y;
+            }
+        }
+        for (int g = 0; g < nst; ++g) {
+            const int slot = g % p.ns, cbi = g % p.ncb;
+            if (*reinterpret_cast<volatile int *>(&s_abort)) break;
+            bool ok = alb_mbar_wait(&full[slot], (uint32_t)((g / p.ns) & 1));
+            if (ok && g >= p.ncb) ok = alb_mbar_wait(&freeb[cbi], (uint32_t)((g / p.ncb - 1) & 1));
+            if (!ok) {
+                if (lane == 0) atomicExch(a.err, ALB_DEVERR_MBAR_TIMEOUT);
+                s_abort = 1;
+                break;
+            }
+            const int64_t r0 = n0 + (int64_t)g * R;
+            const int rg = (int)((n1 - r0) < R ? (n1 - r0) : R);
+            const uint8_t * stg = smem + (size_t)slot * p.stage_bytes;
+            uint8_t * cb = cbase + (size_t)cbi * p.cb_bytes;
+            if (valid) {
+                for (int r = jr; r < rg; r += MV_RU * m) {
+                    const int nr = r + m < rg ? 2 : 1;
+                    uint4 w[MV_RU];
+                    uint32_t dwb[MV_RU];
+#pragma unroll
+                    for (int k = 0; k < MV_RU; ++k) {
+                        if (k < nr) {
+                            const uint8_t * row = stg + (size_t)(r + k * m) * rowb;
+                            w[k] = *reinterpret_cast<const uint4 *>(row + 16 * b);
+                            dwb[k] = reinterpret_cast<const uint16_t *>(row + scol)[b];
+                        }
+                    }
+#pragma unroll
+                    for (int k = 0; k < MV_RU; ++k) {
+                        if (k < nr) {
+                            const int rk = r + k * m;
+                            const float s = __fmul_rn(dxv, alb_h2f_bits(dwb[k]));   // exact: 11 x 11 bits
+                            if constexpr (!PAIR) {
+                                const int I = q4q8_dot_fast(w[k], lo, hi, asum);
+                                *reinterpret_cast<float2 *>(cb + (size_t)rk * p.cbp + 8 * b) =
+                                    make_float2(alb_i2f_small(I), s);
+                                if constexpr (OUT == GEMV_OUT_DOTS) a.dots[(r0 + rk) * nb + b] = I;
+                            } else {
+                                const uint32_t wv[4] = {w[k].x, w[k].y, w[k].z, w[k].w};
+                                const int lov[4] = {lo.x, lo.y, lo.z, lo.w}, hiv[4] = {hi.x, hi.y, hi.z, hi.w};
+                                const int sg[4] = {sg0, sg1, sg2, sg3};
+                                int pl[4];
+#pragma unroll
+                                for (int l = 0; l < 4; ++l) {
+                                    int lo_s = 0, hi_s = 0;
+                                    asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(lo_s) : "r"(wv[l] & 0x0F0F0F0Fu), "r"(lov[l]));
+                                    asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(hi_s) : "r"(wv[l] & 0xF0F0F0F0u), "r"(hiv[l]));
+                                    pl[l] = lo_s + (hi_s >> 4) - 8 * sg[l];   // hi_s = 16 * sum(hi * a): exact shift
+                                }
+                                float * T = reinterpret_cast<float *>(cb + (size_t)rk * p.cbp) + 4 * b;
+                                float * S = reinterpret_cast<float *>(cb + (size_t)R * p.cbp + (size_t)rk * p.cbs) + b;
+                                if ((nb & 1) && b == nb - 1) {
+                                    // scalar tail of an odd block count (arm.cpp:675-691): sumi, dw, dx
+                                    *reinterpret_cast<float4 *>(T) = make_float4(
+                                        alb_i2f_small(pl[0] + pl[1] + pl[2] + pl[3]), alb_h2f_bits(dwb[k]), 0.0f, 0.0f);
+                                    *S = dxv;
+                                } else {
+                                    *reinterpret_cast<float4 *>(T) = make_float4(alb_i2f_small(pl[0]), alb_i2f_small(pl[1]),
+                                                                                 alb_i2f_small(pl[2]), alb_i2f_small(pl[3]));
+                                    *S = s;
+                                }
+                            }
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) { alb_mbar_arrive(&empty[slot]); alb_mbar_arrive(&done[cbi]); }
+        }
+        return;
+    }
+
+    // ---------------------------------------------------------- chain warps
+    // Both chain warps take every stage, chain warp cw the rows [cw * RC, cw * RC + RC).
+    const int cw = warp - MV_CW;
+    const int rb0 = cw * p.RC;
+    unsigned long long best = 0ull;   // LOGITS: this lane's best key
+    for (int g = 0; g < nst; ++g) {
+        const int cbi = g % p.ncb;
+        if (*reinterpret_cast<volatile int *>(&s_abort)) break;
+        if (!alb_mbar_wait(&done[cbi], (uint32_t)((g / p.ncb) & 1))) {
             if (lane == 0) atomicExch(a.err, ALB_DEVERR_MBAR_TIMEOUT);
+            s_abort = 1;
             break;
         }
-        const int64_t item = it0 + (int64_t)g * GEMV_WARPS + warp;
-        if (item < it1) {
-            const uint8_t * nib = stages + (size_t)st * plan.stage_bytes + (size_t)warp * RPW * row_bytes;
-            const uint16_t * sc = reinterpret_cast<const uint16_t *>(stages + (size_t)st * plan.stage_bytes + plan.nib_bytes) + (size_t)warp * RPW * sp;
-            double acc[RPW];
-#pragma unroll
-            for (int r = 0; r < RPW; ++r) acc[r] = 0.0;
-#pragma unroll
-            for (int i = 0; i < ITERS; ++i) {
-                const int b = lane + 32 * i;
+        const int64_t r0 = n0 + (int64_t)g * R;
+        const int rg = (int)((n1 - r0) < R ? (n1 - r0) : R);
+        const uint8_t * cb = cbase + (size_t)cbi * p.cb_bytes;
+        if constexpr (!PAIR) {
+            // acc = fma(float(I), f32(dx) * f32(dw), acc), blocks in order
+            const int r = rb0 + lane;
+            const bool mine = lane < p.RC && r < rg;
+            float acc = 0.0f;
+            if (mine) {
+                const float4 * e = reinterpret_cast<const float4 *>(cb + (size_t)r * p.cbp);
+                int b = 0;
+#pragma unroll 8
+                for (; b + 1 < nb; b += 2) {
+                    const float4 v = e[b >> 1];
+                    acc = __fmaf_rn(v.x, v.y, acc);
+                    acc = __fmaf_rn(v.z, v.w, acc);
+                }
                 if (b < nb) {
-                    const int4 * rec = reinterpret_cast<const int4 *>(xs + b * XREC_INTS);
-                    const int4 a_lo = rec[0], a_hi = rec[1];
-                    const int2 ds = reinterpret_cast<const int2 *>(rec + 2)[0];
-                    const float dx = __int_as_float(ds.x);
-#pragma unroll
-                    for (int r = 0; r < RPW; ++r) {
-                        const uint4 w = *reinterpret_cast<const uint4 *>(nib + r * row_bytes + 16 * b);
-                        const int I = q4q8_dot(w, a_lo, a_hi, ds.y);
-                        acc[r] = fma((double)I, (double)__fmul_rn(dx, alb_h2f(sc[r * sp + b])), acc[r]);
+                    const float2 v = reinterpret_cast<const float2 *>(e)[b];
+                    acc = __fmaf_rn(v.x, v.y, acc);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) alb_mbar_arrive(&freeb[cbi]);   // the terms are in registers now
+            if constexpr (OUT == GEMV_OUT_SWIGLU) {
+                // RC is even, so gate row r (even) and up row r + 1 share the warp
+                const float up = __shfl_down_sync(0xffffffffu, acc, 1);
+                if (mine && !(r & 1)) a.y[(r0 + r) >> 1] = alb_swiglu1(acc, up);
+                if (a.yq) {
+                    __threadfence();
+                    __syncwarp();
+                    const int ra = rb0 < rg ? rb0 : rg, rz = (rb0 + p.RC) < rg ? (rb0 + p.RC) : rg;
+                    if (rz > ra) mv_swiglu_q8(a, (r0 + ra) >> 1, (r0 + rz) >> 1, lane);
+                }
+            } else {
+                if (mine && a.y) {
+                    const int64_t n = r0 + r;
+                    a.y[n] = a.residual ? __fadd_rn(acc, a.residual[n]) : acc;
+                }
+            }
+        } else {
+            const int rr = rb0 + (lane >> 2), l = lane & 3;
+            const bool mine = (lane >> 2) < p.RC && rr < rg;
+            float sv0 = 0.0f, sv1 = 0.0f;
+            float tail = 0.0f;
+            if (mine) {
+                const float * T = reinterpret_cast<const float *>(cb + (size_t)rr * p.cbp) + l;
+                const float * S = reinterpret_cast<const float *>(cb + (size_t)R * p.cbp + (size_t)rr * p.cbs);
+                int b = 0;
+#pragma unroll 8
+                for (; b + 1 < nb; b += 2) {
+                    sv0 = __fmaf_rn(T[4 * b], S[b], sv0);
+                    sv1 = __fmaf_rn(T[4 * b + 4], S[b + 1], sv1);
+                }
+                if (b < nb) {   // odd block count: ((sumi * dw) * dx), added after the vector sum
+                    const float * Tt = T - l + 4 * b;
+                    tail = __fmul_rn(__fmul_rn(Tt[0], Tt[1]), S[b]);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) alb_mbar_arrive(&freeb[cbi]);
+            // vaddvq_f32 = (l0 + l1) + (l2 + l3), then sumv0 + sumv1 (arm.cpp:671)
+            float a0 = __fadd_rn(sv0, __shfl_xor_sync(0xffffffffu, sv0, 1));
+            a0 = __fadd_rn(a0, __shfl_xor_sync(0xffffffffu, a0, 2));
+            float a1 = __fadd_rn(sv1, __shfl_xor_sync(0xffffffffu, sv1, 1));
+            a1 = __fadd_rn(a1, __shfl_xor_sync(0xffffffffu, a1, 2));
+            float sum = __fadd_rn(a0, a1);
+            if (nb & 1) sum = __fadd_rn(sum, tail);
+            if (mine && l == 0) {
+                const int64_t n = r0 + rr;
+                if (a.y) a.y[n] = sum;
+                if constexpr (OUT == GEMV_OUT_LOGITS) {
+                    if (sum == sum) {
+                        const unsigned long long k = mv_key(sum, a.idx_base + n);
+                        best = k > best ? k : best;
                     }
                 }
             }
+        }
+    }
+    if constexpr (OUT == GEMV_OUT_LOGITS) {
 #pragma unroll
-            for (int r = 0; r < RPW; ++r) acc[r] = alb_warp_sum_d(acc[r]);
-            if (lane == 0) {
-                if constexpr (OUT == GEMV_OUT_SWIGLU) {
-                    const float gt = __double2float_rn(acc[0]), u = __double2float_rn(acc[1]);
-                    a.y[item] = alb_swiglu1(gt, u);
-                } else {
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+            best = other > best ? other : best;
+        }
+        if (lane == 0) s_best[cw] = best;
+        asm volatile("bar.sync 2, %0;" :: "n"(MV_CH * 32) : "memory");
+        if (cw == 0 && lane == 0) {
+            unsigned long long m = 0ull;
 #pragma unroll
-                    for (int r = 0; r < RPW; ++r) {
-                        const int64_t row = item * RPW + r;
-                        const float yv = __double2float_rn(acc[r]);
-                    a.y[row] = a.residual ? __fadd_rn(yv, a.residual[row]) : yv;
-                    }
+            for (int w = 0; w < MV_CH; ++w) m = s_best[w] > m ? s_best[w] : m;
+            if (m) atomicMax(a.key, m);
+            if (a.next) {
+                __threadfence();
+                if (atomicAdd(a.ticket, 1) == (int)gridDim.x - 1) {
+                    __threadfence();
+                    const unsigned long long k = atomicOr(a.key, 0ull);
+                    if (k == 0ull) atomicExch(a.err, ALB_DEVERR_BAD_TOKEN);
+                    *a.next = k ? 0x7FFFFFFF - (int32_t)(k & 0xFFFFFFFFull) : 0;
+                    *a.ticket = 0;
                 }
             }
-            if constexpr (OUT == GEMV_OUT_SWIGLU) gemv_swiglu_q8_tail(a, item, lane);
         }
-        __syncwarp();
-        if (lane == 0) alb_mbar_arrive(&empty[st]);
     }
 }
 
-template <int ITERS, int RPW, int IN, int OUT>
-static cudaError_t launch_gemv_t(const GemvArgs & a, cudaStream_t stream) {
-    const int nb = (int)(a.K / 32);
-    const int64_t items = a.N / RPW;
-    const bool direct = (OUT == GEMV_OUT_DOTS) || a.variant != 2;
-    if (direct) {
-        auto kern = k_gemv_direct<ITERS, RPW, IN, OUT>;
-        const size_t smem = (size_t)nb * XREC_INTS * 4 + gemv_stage_bytes(a.K, IN);
-        static size_t attr_smem = 0;   // per instantiation
-        if (smem > 48 * 1024 && smem > attr_smem) {
-            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            if (e != cudaSuccess) return e;
-            attr_smem = smem;
-        }
-        const int per_sm = a.ctas_per_sm > 0 ? a.ctas_per_sm : 3;
-        int64_t grid = (int64_t)alb_sm_count() * per_sm;
-        if (grid * GEMV_WARPS > items) grid = (items + GEMV_WARPS - 1) / GEMV_WARPS;
-        if (grid < 1) grid = 1;
-        return alb_launch(kern, dim3((unsigned)grid), dim3(GEMV_WARPS * 32), smem, stream, a.pdl, a);
-    }
-    auto kern = k_gemv_tma<ITERS, RPW, IN, OUT>;
-    const TmaPlan plan = tma_plan(a.K, RPW, a.stage_budget > 0 ? a.stage_budget : 88 * 1024, IN);
-    static size_t attr_smem = 0;
-    if (plan.smem > attr_smem) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan.smem);
-        if (e != cudaSuccess) return e;
-        attr_smem = plan.smem;
-    }
-    const int per_sm = a.ctas_per_sm > 0 ? a.ctas_per_sm : 1;
-    int64_t grid = (int64_t)alb_sm_count() * per_sm;
-    if (grid * GEMV_WARPS > items) grid = (items + GEMV_WARPS - 1) / GEMV_WARPS;
-    if (grid < 1) grid = 1;
-    return alb_launch(kern, dim3((unsigned)grid), dim3((GEMV_WARPS + 1) * 32), plan.smem, stream, a.pdl, a, plan);
+// odd multiple of 16 >= x (distinct 16-byte bank groups for rows read together)
+static inline uint32_t mv_odd16(uint32_t x) {
+    uint32_t r = (x + 15) & ~15u;
+    if (((r >> 4) & 1) == 0) r += 16;
+    return r;
 }
 
-template <int ITERS, int IN, int OUT>
-static cudaError_t dispatch_rpw(const GemvArgs & a, cudaStream_t s) {
-    constexpr int RPW = (OUT == GEMV_OUT_SWIGLU) ? 2 : (ITERS <= 5 ? 2 : 1);
-    if (a.N % RPW != 0) return launch_gemv_t<ITERS, 1, IN, OUT == GEMV_OUT_SWIGLU ? GEMV_OUT_PLAIN : OUT>(a, s);
-    return launch_gemv_t<ITERS, RPW, IN, OUT>(a, s);
+// Shared-memory plan: stages of about `stage_target` bytes of whole rows (one
+// bulk copy each: large copies stream at full HBM rate, small ones are limited
+// by the per-copy cost), two chain buffers, and as many stages (2..6) as fit the
+// budget, so that a CTA of the next kernel can be resident beside this one and
+// start its own weight stream.
+static MvPlan mv_plan(int64_t K, bool pair, int in_mode, int budget, int stage_target) {
+    const int64_t nb = K / 32;
+    const int64_t row_bytes = q4_row_bytes(K);
+    const int rmax = pair ? 16 : 64;
+    int R = (int)(stage_target / row_bytes);
+    if (R > rmax) R = rmax;
+    if (R < 2) R = 2;
+    R &= ~1;
+    MvPlan p{};
+    for (;;) {
+        p.R = R;
+        p.RC = pair ? (R + 1) / 2 : (((R + 1) / 2) + 1) & ~1;   // even: SwiGLU pairs stay in one warp
+        if (p.RC > (pair ? 8 : 32)) p.RC = pair ? 8 : 32;
+        p.ns = 2;
+        p.ncb = 2;
+        p.stage_bytes = (uint32_t)(R * row_bytes);
+        // chain entries per (row, block): (float(I), dx * dw), or for the pair
+        // chain the four float partial dots [R][nb][4] and dx * dw [R][nb]
+        p.cbp = mv_odd16((uint32_t)(nb * (pair ? 16 : 8)));
+        if (pair) {
+            uint32_t words = (uint32_t)nb;
+            if ((words & 1) == 0) words += 1;
+            p.cbs = words * 4;
+            p.cb_bytes = ((uint32_t)R * p.cbp + (uint32_t)R * p.cbs + 15) & ~15u;
+        } else {
+            p.cbs = 0;
+            p.cb_bytes = (uint32_t)R * p.cbp;
+        }
+        uint32_t region = (uint32_t)p.ncb * p.cb_bytes;
+        const uint32_t stg = (uint32_t)gemv_stage_bytes(K, in_mode);
+        if (stg > region) region = stg;
+        const uint32_t xsb = (uint32_t)(nb * (pair ? XRec<true>::INTS : XRec<false>::INTS) * 4);
+        const uint32_t fixed = ((region + 127) & ~127u) + ((xsb + 127) & ~127u) + 8 * 2 * (6 + p.ncb);
+        while (p.ns < 6 && (int)(fixed + (uint32_t)(p.ns + 1) * p.stage_bytes) <= budget) ++p.ns;
+        p.cb_off = (uint32_t)p.ns * p.stage_bytes;
+        p.xs_off = p.cb_off + ((region + 127) & ~127u);
+        p.bar_off = p.xs_off + ((xsb + 127) & ~127u);
+        p.smem = p.bar_off + 8 * 2 * (p.ns + p.ncb);
+        if ((int)p.smem <= budget || R <= 2) break;
+        R = (R - 2) & ~1;
+        if (R < 2) R = 2;
+    }
+    return p;
+}
+
+// Tuning knobs (read once per process): ALB_MV_SMEM_KB (shared-memory budget
+// of a CTA, default 110), ALB_MV_STAGE_KB (target stage size, default 32),
+// ALB_MV_CPS (CTAs per SM, default 1).
+static int mv_knob(const char * name, int dflt) {
+    const char * v = getenv(name);
+    return v && atoi(v) > 0 ? atoi(v) : dflt;
 }
 
 template <int IN, int OUT>
-static cudaError_t dispatch_iters(const GemvArgs & a, cudaStream_t s) {
-    const int it = (int)((a.K / 32 + 31) / 32);
-    switch (it) {
-        case 1: return dispatch_rpw<1, IN, OUT>(a, s);
-        case 2: return dispatch_rpw<2, IN, OUT>(a, s);
-        case 3: return dispatch_rpw<3, IN, OUT>(a, s);
-        case 4: return dispatch_rpw<4, IN, OUT>(a, s);
-        case 5: return dispatch_rpw<5, IN, OUT>(a, s);
-        case 6: return dispatch_rpw<6, IN, OUT>(a, s);
-        case 7: case 8: return dispatch_rpw<8, IN, OUT>(a, s);
-        case 9: case 10: return dispatch_rpw<10, IN, OUT>(a, s);
-        case 11: case 12: return dispatch_rpw<12, IN, OUT>(a, s);
+static cudaError_t launch_mv_t(const GemvArgs & a, cudaStream_t stream) {
+    constexpr bool PAIR = OUT == GEMV_OUT_PAIR || OUT == GEMV_OUT_LOGITS;
+    static const int budget_kb = mv_knob("ALB_MV_SMEM_KB", 110);
+    static const int stage_kb = mv_knob("ALB_MV_STAGE_KB", 32);
+    const MvPlan p = mv_plan(a.K, PAIR, IN, a.smem_budget > 0 ? a.smem_budget : budget_kb * 1024, stage_kb * 1024);
+    auto kern = k_mv<IN, OUT>;
+    cudaError_t e = ensure_smem(kern, p.smem);
+    if (e != cudaSuccess) return e;
+    const int64_t units = OUT == GEMV_OUT_SWIGLU ? a.N / 2 : a.N;
+    static const int cps = mv_knob("ALB_MV_CPS", 1);
+    int64_t grid = a.ctas > 0 ? a.ctas : (int64_t)alb_sm_count() * cps;
+    if (grid > units) grid = units;
+    if (grid < 1) grid = 1;
+    return alb_launch(kern, dim3((unsigned)grid), dim3(MV_THREADS), p.smem, stream, a.pdl, a, p);
+}
+
+template <int IN>
+static cudaError_t dispatch_out(const GemvArgs & a, cudaStream_t s) {
+    switch (a.out_mode) {
+        case GEMV_OUT_PLAIN: return launch_mv_t<IN, GEMV_OUT_PLAIN>(a, s);
+        case GEMV_OUT_SWIGLU: return launch_mv_t<IN, GEMV_OUT_SWIGLU>(a, s);
+        case GEMV_OUT_DOTS: return launch_mv_t<IN, GEMV_OUT_DOTS>(a, s);
+        case GEMV_OUT_PAIR: return launch_mv_t<IN, GEMV_OUT_PAIR>(a, s);
+        case GEMV_OUT_LOGITS: return launch_mv_t<IN, GEMV_OUT_LOGITS>(a, s);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -519,24 +673,22 @@ cudaError_t launch_gemv(const GemvArgs & a_in, cudaStream_t s) {
     GemvArgs a = a_in;
     if (!a.err) a.err = device_error_ptr();
     if (!a.err) return cudaErrorMemoryAllocation;
-    if (a.K % 32 != 0 || a.K <= 0 || a.N <= 0 || a.K > 12288) return cudaErrorInvalidValue;
+    // K <= 12288: at most 12 block groups of 32, one per dot warp at least
+    if (a.K % 32 != 0 || a.K <= 0 || a.N <= 0 || a.K > 32 * 32 * MV_CW || a.N >= ((int64_t)1 << 30))
+        return cudaErrorInvalidValue;
+    // bulk copies: 16-byte aligned sources (row strides K/2 and pitch*2 are multiples of 16)
+    if (reinterpret_cast<uintptr_t>(a.W) & 15) return cudaErrorInvalidValue;   // bulk-copy source alignment
     if (a.out_mode == GEMV_OUT_SWIGLU && a.N % 2 != 0) return cudaErrorInvalidValue;
-    if (a.yq && (a.out_mode != GEMV_OUT_SWIGLU || !a.ycnt || !a.y || (a.N / 2) % 32 != 0)) return cudaErrorInvalidValue;
-#define ALB_GEMV_CASE(IN)                                                           \
-    case IN:                                                                        \
-        switch (a.out_mode) {                                                       \
-            case GEMV_OUT_PLAIN: return dispatch_iters<IN, GEMV_OUT_PLAIN>(a, s);   \
-            case GEMV_OUT_SWIGLU: return dispatch_iters<IN, GEMV_OUT_SWIGLU>(a, s); \
-            case GEMV_OUT_DOTS: return dispatch_iters<IN, GEMV_OUT_DOTS>(a, s);     \
-            default: return cudaErrorInvalidValue;                                  \
-        }
+    if (a.out_mode == GEMV_OUT_SWIGLU && !a.y) return cudaErrorInvalidValue;
+    if (a.yq && (a.out_mode != GEMV_OUT_SWIGLU || !a.ycnt || (a.N / 2) % 32 != 0)) return cudaErrorInvalidValue;
+    if (a.out_mode == GEMV_OUT_LOGITS && (!a.key || (a.next && !a.ticket))) return cudaErrorInvalidValue;
+    if (a.out_mode == GEMV_OUT_DOTS && !a.dots) return cudaErrorInvalidValue;
     switch (a.in_mode) {
-        ALB_GEMV_CASE(GEMV_IN_Q8)
-        ALB_GEMV_CASE(GEMV_IN_F32)
-        ALB_GEMV_CASE(GEMV_IN_F32_RMS)
+        case GEMV_IN_Q8: return dispatch_out<GEMV_IN_Q8>(a, s);
+        case GEMV_IN_F32: return dispatch_out<GEMV_IN_F32>(a, s);
+        case GEMV_IN_F32_RMS: return dispatch_out<GEMV_IN_F32_RMS>(a, s);
         default: return cudaErrorInvalidValue;
     }
-#undef ALB_GEMV_CASE
 }
 
 }  // namespace alb
@@ -544,36 +696,14 @@ cudaError_t launch_gemv(const GemvArgs & a_in, cudaStream_t s) {
 // ================================================================ C ABI
 using namespace alb;
 
-// Tuning knobs for the standalone C-ABI mat-vec (read once per process):
-//   ALB_GEMV_VARIANT=1|2 (direct loads + L2 prefetch | bulk-copy pipeline),
-//   ALB_GEMV_CTAS=<CTAs per SM>, ALB_GEMV_STAGE_KB=<shared-memory stage budget>,
-//   ALB_GEMV_PDL=0|1 (programmatic dependent launch, default 1).
-static void apply_gemv_knobs(GemvArgs & a) {
-    static int variant = -1, ctas = 0, stage_kb = 0, pdl = 1;
-    if (variant < 0) {
-        const char * p = getenv("ALB_GEMV_PDL");
-        pdl = p ? atoi(p) : 1;
-        const char * v = getenv("ALB_GEMV_VARIANT");
-        const char * c = getenv("ALB_GEMV_CTAS");
-        const char * k = getenv("ALB_GEMV_STAGE_KB");
-        variant = v ? atoi(v) : 1;
-        ctas = c ? atoi(c) : 0;
-        stage_kb = k ? atoi(k) : 0;
-    }
-    a.variant = variant;
-    a.ctas_per_sm = ctas;
-    a.stage_budget = stage_kb * 1024;
-    a.pdl = pdl != 0;
-}
-
 extern "C" size_t alb_q4_0_gpu_bytes(int64_t N, int64_t K) { return q4_gpu_bytes(N, K); }
-extern "C" size_t alb_q4_0_scale_offset(int64_t N, int64_t K) { return q4_scale_offset(N, K); }
+extern "C" size_t alb_q4_0_row_bytes(int64_t K) { return (K > 0 && K % 32 == 0) ? (size_t)q4_row_bytes(K) : 0; }
 
 extern "C" int alb_repack_q4_0(void * dst, const void * src, int64_t N, int64_t K, void * stream) {
     ALB_CHECK_ARG(dst && src && N > 0 && K > 0 && K % 32 == 0);
     const int64_t nbk = N * (K / 32);
     k_repack_q4_0<<<(unsigned)((nbk + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
-        (uint8_t *)dst, (const uint8_t *)src, nbk, K / 32, q4_scale_pitch(K), q4_scale_offset(N, K));
+        (uint8_t *)dst, (const uint8_t *)src, nbk, K / 32, q4_scale_pitch(K), q4_row_bytes(K));
     ALB_CUDA_TRY(cudaGetLastError());
     return ALB_OK;
 }
@@ -582,7 +712,7 @@ extern "C" int alb_unpack_q4_0(void * dst, const void * src, int64_t N, int64_t 
     ALB_CHECK_ARG(dst && src && N > 0 && K > 0 && K % 32 == 0);
     const int64_t nbk = N * (K / 32);
     k_unpack_q4_0<<<(unsigned)((nbk + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
-        (uint8_t *)dst, (const uint8_t *)src, nbk, K / 32, q4_scale_pitch(K), q4_scale_offset(N, K));
+        (uint8_t *)dst, (const uint8_t *)src, nbk, K / 32, q4_row_bytes(K));
     ALB_CUDA_TRY(cudaGetLastError());
     return ALB_OK;
 }
@@ -599,11 +729,21 @@ extern "C" int alb_gemv_q4_0_q8_0(const void * W, const void * xq, float * y, in
                                   const float * residual, void * stream) {
     ALB_CHECK_ARG(W && xq && y && N > 0 && K > 0 && K % 32 == 0 && K <= 12288);
     GemvArgs a;
-    a.W = (const uint8_t *)W; a.S = (const uint8_t *)W + q4_scale_offset(N, K); a.N = N; a.K = K;
+    a.W = (const uint8_t *)W; a.N = N; a.K = K;
     a.in_mode = GEMV_IN_Q8; a.x = xq;
     a.out_mode = GEMV_OUT_PLAIN; a.y = y; a.residual = residual;
     a.pdl = true;
-    apply_gemv_knobs(a);
+    ALB_CUDA_TRY(launch_gemv(a, (cudaStream_t)stream));
+    return ALB_OK;
+}
+
+extern "C" int alb_mul_mat_q4_0_q8_0(const void * W, const void * xq, float * y, int64_t N, int64_t K, void * stream) {
+    ALB_CHECK_ARG(W && xq && y && N > 0 && K > 0 && K % 32 == 0 && K <= 12288);
+    GemvArgs a;
+    a.W = (const uint8_t *)W; a.N = N; a.K = K;
+    a.in_mode = GEMV_IN_Q8; a.x = xq;
+    a.out_mode = GEMV_OUT_PAIR; a.y = y;
+    a.pdl = true;
     ALB_CUDA_TRY(launch_gemv(a, (cudaStream_t)stream));
     return ALB_OK;
 }
@@ -612,7 +752,7 @@ extern "C" int alb_gemv_q4_0_q8_0_block_dots(const void * W, const void * xq, in
                                              void * stream) {
     ALB_CHECK_ARG(W && xq && I && N > 0 && K > 0 && K % 32 == 0 && K <= 12288);
     GemvArgs a;
-    a.W = (const uint8_t *)W; a.S = (const uint8_t *)W + q4_scale_offset(N, K); a.N = N; a.K = K;
+    a.W = (const uint8_t *)W; a.N = N; a.K = K;
     a.in_mode = GEMV_IN_Q8; a.x = xq;
     a.out_mode = GEMV_OUT_DOTS; a.dots = I; a.y = nullptr;
     ALB_CUDA_TRY(launch_gemv(a, (cudaStream_t)stream));

@@ -51,6 +51,18 @@ __device__ __forceinline__ int q4q8_dot_fast(uint4 w, const int4 a_lo, const int
     asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(t) : "r"(w.w & 0xF0F0F0F0u), "r"(a_hi.w));
     return s + (t >> 4) - 8 * asum;   // t is 16 * (sum of hi * a): exact division
 }
+// Exact conversions on the integer / fp32 pipes (no conversion instruction: the
+// conversion unit is a fraction of the ALU rate and saturates in the mat-vec).
+// int32 with |i| < 2^22 -> float: bits(1.5 * 2^23 + i) - 1.5 * 2^23.
+__device__ __forceinline__ float alb_i2f_small(int i) {
+    return __fsub_rn(__int_as_float(i + 0x4B400000), 12582912.0f);
+}
+// fp16 bits -> float for every finite half: exponent and mantissa placed in a
+// float (value * 2^-112, a float denormal for a half subnormal), times 2^112.
+__device__ __forceinline__ float alb_h2f_bits(uint32_t h) {
+    return __fmul_rn(__int_as_float((int)(((h & 0x7FFFu) << 13) | ((h & 0x8000u) << 16))), 0x1p112f);
+}
+
 // fp16 bits -> the bits of (value * 2^-1008) as a double (see alb_h2d), without
 // the final scaling; pairs with an operand pre-scaled by 2^1008.
 __device__ __forceinline__ double alb_h2d_bits(uint32_t h) {

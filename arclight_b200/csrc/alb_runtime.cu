@@ -1,7 +1,10 @@
 // Runtime helpers of libalb_cuda.so: status strings, device checks.
 #include <cstdio>
 #include <cstring>
+#include <atomic>
+#include <map>
 #include <mutex>
+#include <utility>
 
 #include "alb_common.cuh"
 #include "alb_internal.h"
@@ -14,19 +17,38 @@ void alb_set_last_cuda_error(cudaError_t e, const char * what) {
 void alb_set_last_error_msg(const char * msg) { snprintf(g_last_error, sizeof(g_last_error), "%s", msg); }
 
 int alb_sm_count() {
-    static int count[64] = {0};
+    static std::atomic<int> count[64];
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) dev = 0;
-    if (count[dev] == 0) {
-        int c = 0;
+    int c = count[dev].load(std::memory_order_relaxed);
+    if (c == 0) {
         cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev);
-        count[dev] = c > 0 ? c : 148;
+        if (c <= 0) c = 148;
+        count[dev].store(c, std::memory_order_relaxed);
     }
-    return count[dev];
+    return c;
 }
 
 namespace alb {
+// cudaFuncAttributeMaxDynamicSharedMemorySize is a per-device property of a
+// kernel: remember, per (device, kernel), the largest value set so far, under a
+// lock (several host threads may drive several devices in one process).
+cudaError_t ensure_dynamic_smem(const void * func, size_t bytes) {
+    if (bytes <= 48 * 1024) return cudaSuccess;
+    static std::mutex mu;
+    static std::map<std::pair<int, const void *>, size_t> done;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lk(mu);
+    size_t & cur = done[std::make_pair(dev, func)];
+    if (cur >= bytes) return cudaSuccess;
+    e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e == cudaSuccess) cur = bytes;
+    return e;
+}
+
 int * device_error_ptr() {
     static int * ptrs[64] = {nullptr};
     static std::mutex mu;

@@ -12,11 +12,12 @@
  * ArcLight tree).  Layouts:
  *   block_q4_0  : {fp16 d; uint8 qs[16]}  18 B per 32 values (nnml.h:646-651)
  *   block_q8_0  : {fp16 d; int8  qs[32]}  34 B per 32 values (nnml.h:695-700)
- *   alb Q4_0 GPU layout (what alb_repack_q4_0 writes; replaces block_q4_0x4):
- *       nibble plane  [N][K/2] bytes, block b of row n at n*K/2 + 16*b, the 16
- *                     bytes of block_q4_0.qs unchanged;
- *       scale plane   [N][pitch] fp16 at byte offset alb_q4_0_scale_offset(N, K),
- *                     pitch = K/32 rounded up to a multiple of 8 (16-byte rows).
+ *   alb Q4_0 GPU layout (what alb_repack_q4_0 writes; replaces block_q4_0x4),
+ *       row-interleaved: row n occupies alb_q4_0_row_bytes(K) bytes at
+ *       n * alb_q4_0_row_bytes(K): the 16 qs bytes of each of its K/32 blocks
+ *       (block b at 16*b, block_q4_0.qs unchanged), then the K/32 fp16 scales
+ *       padded with zeros to a multiple of 8 entries (16 bytes).  A run of
+ *       consecutive rows is one contiguous 16-byte aligned range.
  *   activations fp32 row-major; KV cache fp16 [cells][n_head_kv][head_dim].
  */
 #ifndef ALB_CUDA_H
@@ -57,9 +58,10 @@ ALB_API int          alb_device_check(int dev);
 ALB_API int          alb_device_error(int clear);
 
 /* ---------------------------------------------------------------- formats */
-/* Bytes of the alb Q4_0 GPU layout of an [N x K] weight (K % 32 == 0). */
+/* Bytes of the alb Q4_0 GPU layout of an [N x K] weight (K % 32 == 0), and of
+ * one of its rows (0 for an invalid K). */
 ALB_API size_t alb_q4_0_gpu_bytes(int64_t N, int64_t K);
-ALB_API size_t alb_q4_0_scale_offset(int64_t N, int64_t K);
+ALB_API size_t alb_q4_0_row_bytes(int64_t K);
 /* format_repack / repack<block_q4_0,4,4> (types.cpp:199-240): block_q4_0 rows
  * [N][K/32] (device) -> alb GPU layout (device). */
 ALB_API int alb_repack_q4_0(void * dst, const void * src_blocks, int64_t N, int64_t K, void * stream);
@@ -73,17 +75,27 @@ ALB_API int alb_quantize_q8_0(const float * x, void * xq, int64_t K, int64_t row
 
 /* ------------------------------------------------------------------- GEMV */
 /* nnml_gemv_q4_0_4x4_q8_0 (gemm.cpp:127-190) driven by forward_mul_mat
- * (arm.cpp:1855-1925), ne11 = 1: y[n] = sum_b I(n,b) * f32(dw) * f32(dx)
- * (+ residual[n] when non-null: the ADD of qwen3.cpp:239/270 fused).
- * W in the alb GPU layout, xq block_q8_0 [K/32]. */
+ * (arm.cpp:1855-1925), ne11 = 1: per row, acc = fma(float(I(n,b)),
+ * f32(dx_b) * f32(dw_b), acc) over the blocks b in order from 0 (the NEON
+ * chain, gemm.cpp:179-181), then y[n] = acc (+ residual[n] when non-null: the
+ * ADD of qwen3.cpp:239/270 fused).  Bit-identical to the reference's
+ * arithmetic.  W in the alb GPU layout (16-byte aligned), xq block_q8_0 [K/32];
+ * K <= 12288. */
 ALB_API int alb_gemv_q4_0_q8_0(const void * W, const void * xq, float * y, int64_t N, int64_t K,
                        const float * residual, void * stream);
+/* forward_mul_mat_generic (common.cpp:120-248) with nnml_vec_dot_q4_0_q8_0
+ * (arm.cpp:633-692), the path of the un-repacked lm head / token table: per
+ * row, four partial block dots accumulated in two fp32 fma chains per lane
+ * (even and odd blocks), summed as ((l0+l1)+(l2+l3)) per chain, then even +
+ * odd, then the scalar tail of an odd block count.  y [N]. */
+ALB_API int alb_mul_mat_q4_0_q8_0(const void * W, const void * xq, float * y, int64_t N, int64_t K, void * stream);
 /* ------------------------------------------------------------------- GEMM */
 /* nnml_gemm_q4_0_4x4_q8_0 (gemm.cpp:495-974) driven by forward_mul_mat
- * (arm.cpp:1855-1925), ne11 = M > 1 (prefill): y[m][n] = sum_b I(m,n,b) * f32(dw) *
- * f32(dx) (+ residual[m][n] when non-null), exact block terms summed in double;
- * on tcgen05 int8 tensor cores.  W in the alb GPU layout [N][K], xq block_q8_0
- * [M][K/32], y / residual [M][N].  workspace: alb_gemm_workspace_bytes(M, K). */
+ * (arm.cpp:1855-1925), ne11 = M > 1 (prefill): every output the same fp32 fma
+ * chain over the blocks as alb_gemv_q4_0_q8_0 (the reference's gemm and gemv
+ * share it), + residual[m][n] when non-null; block dots on tcgen05 int8
+ * tensor cores.  W in the alb GPU layout [N][K], xq block_q8_0 [M][K/32],
+ * y / residual [M][N].  workspace: alb_gemm_workspace_bytes(M, K). */
 ALB_API size_t alb_gemm_workspace_bytes(int64_t M, int64_t K);
 ALB_API int alb_gemm_q4_0_q8_0(const void * W, const void * xq, float * y, int64_t M, int64_t N, int64_t K,
                                const float * residual, void * workspace, void * stream);
@@ -146,7 +158,10 @@ ALB_API int alb_flash_attn(const float * q, const uint16_t * k_cache, const uint
  * ALB_ERR_INVALID).  Calls on one device share that array and must not
  * overlap in time.  The first call on a device looks the array up and clears
  * it (cudaGetSymbolAddress, cudaMemsetAsync on `stream`); make it outside any
- * stream capture.  Same results as alb_flash_attn.  No counterpart in the
+ * stream capture.  The looked-up address is kept for the life of the process:
+ * a cudaDeviceReset of that device is not supported afterwards.  Calls whose
+ * path needs no workspace (single split, fused or token-tiled kernels) are
+ * never rejected for size.  Same results as alb_flash_attn.  No counterpart in the
  * reference (its ops take scratch from params->work_data, thread.h:166-167). */
 ALB_API int alb_flash_attn_static(const float * q, const uint16_t * k_cache, const uint16_t * v_cache, int64_t T,
                                   int32_t n_head, int32_t n_head_kv, int32_t pos0, float scale, int32_t splits,
@@ -214,9 +229,6 @@ ALB_API void * alb_engine_stream(alb_engine * e);
 ALB_API int alb_engine_weight_blocks(alb_engine * e, int32_t layer, int32_t kind, void * host, int64_t * rows,
                                      int64_t * cols);
 ALB_API int alb_engine_norm_weights(alb_engine * e, int32_t layer, int32_t kind, float * host, int64_t n);
-/* Measurement hook: one decode step with the persistent kernel's CTA 0
- * stamping %globaltimer (ns) at each phase boundary; returns the stamp count. */
-ALB_API int alb_engine_decode_trace(alb_engine * e, int32_t token, int32_t pos, int64_t * host, int32_t n);
 /* Measurement hook: mean duration and algorithmic bytes per launch of the
  * decode step's Q4_0 mat-vecs replayed alone from a CUDA graph. */
 ALB_API int alb_engine_time_gemv(alb_engine * e, int32_t reps, float * us_per_launch, double * bytes_per_launch);

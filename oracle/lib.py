@@ -77,6 +77,7 @@ def lib() -> C.CDLL:
             "orc_model_set_exact": (None, [vp, C.c_int]),
             "orc_model_set_tp": (None, [vp, C.c_int]),
             "orc_gemv_q4_0_q8_0_exact_tp": (None, [vp, vp, vp, C.c_int64, C.c_int64, C.c_int, C.c_int]),
+            "orc_gemv_q4_0_q8_0_tp": (None, [vp, vp, vp, C.c_int64, C.c_int64, C.c_int, C.c_int]),
             "orc_vec_dot_q4_0_q8_0": (f32, [vp, vp, i64]),
             "orc_mul_mat_generic": (None, [vp, vp, vp, i64, i64, C.c_int]),
             "orc_rms_norm": (None, [vp, vp, vp, i64, i64, f32]),
@@ -173,6 +174,17 @@ def gemv_exact(w: np.ndarray, xq: np.ndarray, threads: int = 8) -> np.ndarray:
     return y
 
 
+def gemv_tp(w: np.ndarray, xq: np.ndarray, tp: int, threads: int = 8) -> np.ndarray:
+    """The reference's TP mat-vec of a column-split matrix: node chains over K/tp
+    slices, partials added in node order."""
+    w = np.ascontiguousarray(w)
+    xq = np.ascontiguousarray(xq)
+    n, nb = w.shape
+    y = np.empty(n, np.float32)
+    lib().orc_gemv_q4_0_q8_0_tp(_ptr(w), _ptr(xq), _ptr(y), n, nb * 32, tp, threads)
+    return y
+
+
 def mul_mat_generic(w: np.ndarray, xq: np.ndarray, threads: int = 8) -> np.ndarray:
     w = np.ascontiguousarray(w)
     xq = np.ascontiguousarray(xq)
@@ -208,7 +220,9 @@ def swiglu(g: np.ndarray, u: np.ndarray) -> np.ndarray:
 
 
 def flash_attn(q, k, v, kv_len, scale, mode=0):
-    """q [T][H][D] f32, k/v [cells][Hkv][D] fp16 bits (uint16), kv_len [T] int32."""
+    """q [T][H][D] f32, k/v [cells][Hkv][D] fp16 bits (uint16), kv_len [T] int32.
+    mode 0: fp32 scores / double sums (the CUDA semantics); 1: the reference's
+    fp16-accumulating NEON loop; 2: fp64 attention (the yardstick)."""
     q = np.ascontiguousarray(q, np.float32)
     k = np.ascontiguousarray(k, np.uint16)
     v = np.ascontiguousarray(v, np.uint16)
@@ -270,12 +284,12 @@ class Model:
         lib().orc_model_fill_kv(self.h, int(n_pos), int(seed))
 
     def set_exact(self, exact: bool):
-        """True (default): exactly rounded mat-vecs; False: the reference's NEON fp32 chains."""
+        """False (default): the reference's NEON fp32 chains; True: exactly rounded mat-vecs."""
         lib().orc_model_set_exact(self.h, 1 if exact else 0)
 
     def set_tp(self, tp: int):
         """tp > 1: O and down projections as tp node partials added in node order
-        (the reference's tensor-parallel GATHER), exact mat-vecs."""
+        (the reference's tensor-parallel GATHER)."""
         lib().orc_model_set_tp(self.h, int(tp))
 
 

@@ -307,6 +307,36 @@ void orc_gemv_q4_0_q8_0_exact_tp(const orc_block_q4_0 * W, const orc_block_q8_0 
     orc_parallel_for(n_threads, N, gemv_tp_range, &c);
 }
 
+/* Tensor-parallel form of the NEON chain (the reference's own TP arithmetic):
+ * node j runs nnml_gemv_q4_0_4x4_q8_0 (gemm.cpp:127-190) over its column slice
+ * of K/tp (model.cpp:21-54 slices O / down by input columns in 32-aligned
+ * units), a fresh fp32 fma chain from 0; GATHER then adds the node partials in
+ * node order in fp32 (ops.cpp:1465-1511, nnml_vec_add_f32 arm.cpp:2435-2451). */
+static void gemv_tp_chain_range(void * p, int64_t n0, int64_t n1) {
+    const gemv_tp_ctx * c = (const gemv_tp_ctx *)p;
+    const int64_t nbs = c->nb / c->tp;
+    for (int64_t n = n0; n < n1; ++n) {
+        const orc_block_q4_0 * w = c->W + n * c->nb;
+        float acc = 0.0f;
+        for (int j = 0; j < c->tp; ++j) {
+            float part = 0.0f;
+            for (int64_t b = j * nbs; b < (j + 1) * nbs; ++b) {
+                const int32_t I = block_dot_q4_0_q8_0(&w[b], &c->xq[b]);
+                const float s = orc_fp16_to_fp32(c->xq[b].d) * orc_fp16_to_fp32(w[b].d);
+                part = fmaf((float)I, s, part);
+            }
+            acc = j == 0 ? part : acc + part;
+        }
+        c->y[n] = acc;
+    }
+}
+
+void orc_gemv_q4_0_q8_0_tp(const orc_block_q4_0 * W, const orc_block_q8_0 * xq, float * y,
+                           int64_t N, int64_t K, int tp, int n_threads) {
+    gemv_tp_ctx c = { W, xq, y, K / ORC_QK, tp > 0 ? tp : 1 };
+    orc_parallel_for(n_threads, N, gemv_tp_chain_range, &c);
+}
+
 /* nnml_vec_dot_q4_0_q8_0 NEON path (arm.cpp:633-692): blocks in pairs, two
  * float32x4 accumulators; lane i of vdotq_s32 sums elements 4i..4i+3 of the
  * low half and of the high half; vmlaq_n_f32 is contracted to fmla under
@@ -497,7 +527,7 @@ static void fa_range(void * pc, int64_t b, int64_t e) {
     float * VKQ32 = (float *)malloc(D * 4);
     float * Qf = (float *)malloc(D * 4);
     float * sc = (float *)malloc(f->nmax * 4);
-    double * Od = (double *)malloc(D * sizeof(double));
+    double * Od = (double *)malloc((D + (f->mode == 2 ? f->nmax : 0)) * sizeof(double));
     for (int64_t idx = b; idx < e; ++idx) {
         const int64_t t = idx / n_head, h = idx - t * n_head;
         const int64_t n_kv = f->kv_len[t];
@@ -506,6 +536,30 @@ static void fa_range(void * pc, int64_t b, int64_t e) {
             const float * pq = f->q + (t * n_head + h) * D;
             float * po = f->out + (t * n_head + h) * D;
             for (int64_t d = 0; d < D; ++d) { Qh[d] = orc_fp32_to_fp16(pq[d]); Qf[d] = orc_fp16_to_fp32(Qh[d]); }
+            if (f->mode == 2) {
+                /* fp64 reference attention on the same inputs (fp16-rounded q, fp16
+                 * K/V): scores, exp and sums in double, one rounding at the end;
+                 * the yardstick for the errors of modes 0 and 1 */
+                double M = -INFINITY;
+                double * sd = Od + D;   /* scratch of n_kv doubles after Od */
+                for (int64_t c = 0; c < n_kv; ++c) {
+                    const uint16_t * kc = k + c * row + hk * D;
+                    double a = 0.0;
+                    for (int64_t d = 0; d < D; ++d) a += (double)orc_fp16_to_fp32(kc[d]) * (double)Qf[d];
+                    sd[c] = a * (double)scale;
+                    M = sd[c] > M ? sd[c] : M;
+                }
+                double L = 0.0;
+                for (int64_t d = 0; d < D; ++d) Od[d] = 0.0;
+                for (int64_t c = 0; c < n_kv; ++c) {
+                    const double p = exp(sd[c] - M);
+                    const uint16_t * vc = v + c * row + hk * D;
+                    L += p;
+                    for (int64_t d = 0; d < D; ++d) Od[d] += p * (double)orc_fp16_to_fp32(vc[d]);
+                }
+                for (int64_t d = 0; d < D; ++d) po[d] = L > 0.0 ? (float)(Od[d] / L) : 0.0f;
+                continue;
+            }
             if (f->mode == 0) {
                 float M = -INFINITY;
                 for (int64_t c = 0; c < n_kv; ++c) {
@@ -586,7 +640,7 @@ struct orc_model {
     orc_layer * layers;
     float * table;
     uint64_t seed;
-    int exact;   /* 1: exactly rounded mat-vecs (default); 0: NEON fp32 chains */
+    int exact;   /* 0: the reference's NEON fp32 chains (default); 1: exactly rounded mat-vecs */
     int tp;      /* > 1: O / down as tp column-slice partials added in node order */
 };
 
@@ -621,7 +675,7 @@ orc_model * orc_model_create(const orc_qwen3_config * cfg, uint64_t seed, int32_
     m->max_ctx = max_ctx;
     m->n_threads = n_threads > 0 ? n_threads : 1;
     m->seed = seed;
-    m->exact = 1;
+    m->exact = 0;
     m->tp = 1;
     m->table = (float *)malloc(65537 * sizeof(float));
     orc_normal_table(m->table);
@@ -743,13 +797,16 @@ static void matmul_rows(orc_model * m, const orc_block_q4_0 * W, const float * x
 void orc_model_set_exact(orc_model * m, int exact) { m->exact = exact; }
 void orc_model_set_tp(orc_model * m, int tp) { m->tp = tp > 0 ? tp : 1; }
 
-/* O / down projections: tp > 1 forms the node partials (exact mode only). */
+/* O / down projections: tp > 1 forms the node partials over the column slices
+ * and adds them in node order (the chain of each slice in the default mode,
+ * exactly rounded slice sums in exact mode). */
 static void matmul_rows_cols_split(orc_model * m, const orc_block_q4_0 * W, const float * x, float * y,
                                    int64_t T, int64_t N, int64_t K, orc_block_q8_0 * qbuf) {
-    if (m->tp <= 1 || !m->exact) { matmul_rows(m, W, x, y, T, N, K, qbuf); return; }
+    if (m->tp <= 1) { matmul_rows(m, W, x, y, T, N, K, qbuf); return; }
     for (int64_t t = 0; t < T; ++t) {
         orc_quantize_row_q8_0(x + t * K, qbuf, K);
-        orc_gemv_q4_0_q8_0_exact_tp(W, qbuf, y + t * N, N, K, m->tp, m->n_threads);
+        if (m->exact) orc_gemv_q4_0_q8_0_exact_tp(W, qbuf, y + t * N, N, K, m->tp, m->n_threads);
+        else orc_gemv_q4_0_q8_0_tp(W, qbuf, y + t * N, N, K, m->tp, m->n_threads);
     }
 }
 

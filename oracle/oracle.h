@@ -69,6 +69,11 @@ void orc_gemv_q4_0_q8_0_exact(const orc_block_q4_0 * W, const orc_block_q8_0 * x
  * order in fp32 (GATHER, ops.cpp:1465-1511). */
 void orc_gemv_q4_0_q8_0_exact_tp(const orc_block_q4_0 * W, const orc_block_q8_0 * xq, float * y,
                                  int64_t N, int64_t K, int tp, int n_threads);
+/* Tensor-parallel NEON chain (the reference's TP arithmetic for O / down): node
+ * j's partial is the fp32 chain over its K/tp column slice, partials added in
+ * node order in fp32 (GATHER, ops.cpp:1465-1511). */
+void orc_gemv_q4_0_q8_0_tp(const orc_block_q4_0 * W, const orc_block_q8_0 * xq, float * y,
+                           int64_t N, int64_t K, int tp, int n_threads);
 /* nnml_vec_dot_q4_0_q8_0 NEON path (arm.cpp:633-692): generic mul_mat (lm_head). */
 float orc_vec_dot_q4_0_q8_0(const orc_block_q4_0 * x, const orc_block_q8_0 * y, int64_t k);
 void  orc_mul_mat_generic(const orc_block_q4_0 * W, const orc_block_q8_0 * xq, float * y,
@@ -96,7 +101,9 @@ void orc_gather_sum(const float * const * srcs, int n_srcs, float * dst, int64_t
  * out  : [T][n_head][D] fp32
  * mode 0: fp32 scores, global-max softmax with nnml_v_expf, double sums (the
  *         split-independent semantics of the CUDA kernels);
- * mode 1: ARM-faithful fp16 VKQ/KQ accumulation with online softmax. */
+ * mode 1: ARM-faithful fp16 VKQ/KQ accumulation with online softmax;
+ * mode 2: the same function in fp64 (scores, exp, sums), rounded once: the
+ *         yardstick that modes 0 and 1 are measured against. */
 void orc_flash_attn(const float * q, const uint16_t * k, const uint16_t * v, const int32_t * kv_len,
                     int64_t T, int64_t n_head, int64_t n_head_kv, int64_t D, float scale,
                     int mode, float * out);
@@ -135,12 +142,12 @@ void orc_model_reset(orc_model * m);
  * layer set to fp16(N(0,1)) from the seeded generator, element (cell, e) of
  * layer l drawn at index cell * Dkv + e under orc_tensor_seed(seed, l, 62 | 63). */
 void orc_model_fill_kv(orc_model * m, int32_t n_pos, uint64_t seed);
-/* exact != 0 (default): mat-vecs use orc_gemv_q4_0_q8_0_exact (also for the lm
- * head); 0: the reference's NEON fp32 chains (gemv for projections,
- * nnml_vec_dot_q4_0_q8_0 lanes for the lm head). */
+/* exact == 0 (default): the reference's NEON fp32 chains (gemv for the
+ * projections, nnml_vec_dot_q4_0_q8_0 lanes for the lm head); != 0: every
+ * mat-vec exactly rounded (orc_gemv_q4_0_q8_0_exact, for error studies). */
 void orc_model_set_exact(orc_model * m, int exact);
 /* tp > 1: the O and down projections as tp node partials added in node order,
- * then the residual (qwen3.cpp:232-241,262-270 with is_tp); exact mode only. */
+ * then the residual (qwen3.cpp:232-241,262-270 with is_tp). */
 void orc_model_set_tp(orc_model * m, int tp);
 /* greedy argmax (sampler.cpp:34-36: std::max_element => first maximum) */
 int32_t orc_argmax(const float * x, int64_t n);

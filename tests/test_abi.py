@@ -31,19 +31,27 @@ def test_only_c_abi_symbols_are_exported():
 
 def test_q4_gpu_layout_sizes():
     L = A.lib()
-    # nibble plane N*K/2 (256-aligned) + scale plane N*K/16
-    assert L.alb_q4_0_scale_offset(9728, 2560) == 9728 * 1280
-    assert L.alb_q4_0_gpu_bytes(9728, 2560) == 9728 * 1280 + 9728 * 160
-    assert L.alb_q4_0_scale_offset(3, 32) == 256
-    # every plane start is 16-byte aligned for the vector loads
-    for n, k in [(1, 32), (7, 96), (151936, 2560), (1216, 2560)]:
-        assert L.alb_q4_0_scale_offset(n, k) % 256 == 0
+    # row-interleaved: K/2 nibble bytes + K/32 fp16 scales padded to 8 entries, per row
+    assert L.alb_q4_0_row_bytes(2560) == 1280 + 160
+    assert L.alb_q4_0_row_bytes(9728) == 4864 + 608
+    assert L.alb_q4_0_row_bytes(32) == 16 + 16
+    assert L.alb_q4_0_row_bytes(96) == 48 + 16
+    assert L.alb_q4_0_row_bytes(33) == 0
+    assert L.alb_q4_0_gpu_bytes(9728, 2560) == 9728 * 1440
+    assert L.alb_q4_0_gpu_bytes(3, 32) == 256            # rounded up to 256 bytes
+    # every row starts 16-byte aligned (one bulk copy per run of rows)
+    for k in (32, 96, 1216, 2560, 4096, 9728, 12288):
+        assert L.alb_q4_0_row_bytes(k) % 16 == 0
 
 
 def test_invalid_arguments_are_rejected_without_a_gpu():
     L = A.lib()
     # null pointers / bad K are caught on the host before any CUDA call
     assert L.alb_gemv_q4_0_q8_0(None, None, None, 16, 2560, None, None) == -1
+    assert L.alb_mul_mat_q4_0_q8_0(None, None, None, 16, 2560, None) == -1
+    dummy16 = 16
+    assert L.alb_mul_mat_q4_0_q8_0(dummy16, dummy16, dummy16, 16, 2561, None) == -1   # K % 32
+    assert L.alb_gemv_q4_0_q8_0(dummy16, dummy16, dummy16, 16, 12320, None, None) == -1   # K beyond 12288
     assert L.alb_quantize_q8_0(None, None, 33, 1, None) == -1
     assert b"invalid argument" in L.alb_last_error()
     # fused quantizers: n must be a whole number of 32-value blocks

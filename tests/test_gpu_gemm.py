@@ -1,9 +1,12 @@
-"""GPU parity of the prefill Q4_0 x Q8_0 mat-mul (tcgen05 kind::i8, exact block
-terms in double) against the oracle's exactly rounded mat-vec, row by row.
+"""GPU parity of the prefill Q4_0 x Q8_0 mat-mul (tcgen05 kind::i8 block dots,
+fp32 chains in the epilogue) against the oracle, row by row.
 
 Bar (north_star): per-op fp32 outputs within 1e-3 relative of the reference's
-NEON chain; here every output row is also bit-identical to the oracle's exact
-mat-vec of that row (the same block terms, summed in double, rounded once).
+NEON chain.  The reference's gemm (gemm.cpp:495-974) accumulates each output
+with the same fp32 fma chain over the blocks as its gemv, so every GPU output
+row is asserted bit-identical to the oracle's NEON-chain mat-vec of that row,
+including the config-4 prefill shapes (M = 2048 tokens, N = 6144 / 19456,
+K = 2560; rows sampled across every M tile).
 """
 import numpy as np
 import pytest
@@ -39,8 +42,11 @@ def upload_weight(wq):
     (1, 64, 32),         # minimal
     (300, 64, 9728),     # down_proj K
     (128, 1216, 2560),   # TP=8 gate/up shard width
+    (2048, 6144, 2560),  # config 4: fused QKV of the 4B over a 2048-token prompt
+    (2048, 19456, 2560), # config 4: gate/up
+    (2048, 2560, 9728),  # config 4: down
 ])
-def test_gemm_rows_match_exact_gemv(M, N, K):
+def test_gemm_rows_match_chain_gemv(M, N, K):
     rng = np.random.default_rng(M * 7 + N + K)
     wq = O.quantize_q4_0((rng.standard_normal((N, K)) * 0.02).astype(np.float32))
     x = rng.standard_normal((M, K)).astype(np.float32)
@@ -55,9 +61,11 @@ def test_gemm_rows_match_exact_gemv(M, N, K):
     torch.cuda.synchronize()
     assert A.lib().alb_device_error(0) == 0
     got = y.cpu().numpy()
-    for m in range(M):
-        ref_exact = O.gemv_exact(wq, xq[m])
-        np.testing.assert_array_equal(got[m], ref_exact, err_msg=f"row {m}")
+    assert np.all(np.isfinite(got)), "unwritten outputs"
+    rows = range(M) if M <= 300 else sorted(set(list(range(0, M, 61)) + [1, 127, 128, 1023, M - 1]))
+    for m in rows:
+        ref, _ = O.gemv(wq, xq[m])
+        np.testing.assert_array_equal(got[m], ref, err_msg=f"row {m}")
     ref_neon, _ = O.gemv(wq, xq[M - 1])
     assert_rel(got[M - 1], ref_neon, what=f"gemm {M}x{N}x{K} vs NEON chain")
 
@@ -77,5 +85,5 @@ def test_gemm_residual():
     torch.cuda.synchronize()
     got = y.cpu().numpy()
     for m in (0, 64, M - 1):
-        exp = (O.gemv_exact(wq, xq[m]) + res[m]).astype(np.float32)
+        exp = (O.gemv(wq, xq[m])[0] + res[m]).astype(np.float32)
         np.testing.assert_array_equal(got[m], exp)

