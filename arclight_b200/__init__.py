@@ -93,6 +93,7 @@ def _declare(L: C.CDLL) -> None:
         "alb_engine_decode": (ci, [vp, i32, i32, vp]),
         "alb_engine_decode_loop": (ci, [vp, i32, i32, i32, vp, i32]),
         "alb_engine_logits": (ci, [vp, vp, i64]),
+        "alb_engine_hidden": (ci, [vp, vp, i64]),
         "alb_engine_info": (ci, [vp, vp, i32]),
         "alb_engine_stream": (vp, [vp]),
         "alb_engine_weight_blocks": (ci, [vp, i32, i32, vp, vp, vp]),

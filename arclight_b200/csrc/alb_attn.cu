@@ -1,0 +1,456 @@
+// Split-K flash attention over the fp16 KV cache (decode and multi-token split
+// calls), sm_100a.
+//
+// Reference: nnml_compute_forward_flash_attn_ext_f16 (nnml/src/ops/arm/arm.cpp:
+// 2196-2433), one sequence, causal: token t (position p0 + t) attends cells
+// [0, p0 + t + 1); GQA broadcast of G = Hq/Hkv query heads per KV head.
+//
+// Semantics (the oracle's attention mode 0; independent of the split count):
+// Q rounded to fp16 (arm.cpp:2307); score s_c = sequential fp32 fma chain over
+// d of K.Q, times scale; M = max_c s_c; p_c = v_expf(s_c - M) (the reference's
+// NEON exp, arm.cpp:1757-1787); L and every O_d are double sums in a canonical
+// order: cells in order within chunks of AT_CHUNK cells, chunk sums added in
+// chunk order; out = O / L.  Every p * v is exact in double, so only the
+// additions round, and they are the same additions on any GPU split.  Softmax
+// is shift invariant: this is the reference's function with fp32/fp64
+// arithmetic in place of its fp16 accumulators (within 1e-5 of an fp64
+// attention, while the reference's own fp16 rounding is 1e-3 .. 5e-2 from it).
+//
+// Two launches:
+//   k_att_scores  CTA (kv head h, token t, split s): scores of the split's
+//                 cells and its per-head maxima; for a decode step it first
+//                 applies the per-head QK-RMSNorm and NEOX RoPE to the raw
+//                 projection (qwen3.cpp:215-224, ops.cpp:830-938) and stores
+//                 the new K/V cell (set_rows, ops.cpp:135-181);
+//   k_att_pv      same grid: the global maxima, p, and per chunk the ordered
+//                 sums (one thread per dimension, cells in order); the last
+//                 CTA of (h, t) to finish adds the chunk partials in chunk
+//                 order, writes the output and, for a decode step, the
+//                 block_q8_0 records of the output (the O projection's input).
+#include <cfloat>
+#include <cmath>
+
+#include "alb_common.cuh"
+#include "alb_internal.h"
+#include "alb_q4_dev.cuh"
+
+namespace alb {
+
+static constexpr int AT_CHUNK = 128;                    // canonical summation chunk (cells)
+static constexpr int AT_ST = 64;                        // cells per staging step (AT_CHUNK / 2)
+static constexpr int AT_NST = 3;                        // K ring depth of k_att_scores
+static constexpr int AT_KPITCH = 272;                   // padded K row in shared memory
+static constexpr size_t AT_SCORES_SMEM = (size_t)AT_NST * AT_ST * AT_KPITCH;   // 52,224 B
+
+__device__ __forceinline__ void at_cp16(void * dst, const void * src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(alb_smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void at_cp4(void * dst, const void * src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" :: "r"(alb_smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void at_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N> __device__ __forceinline__ void at_wait() { asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory"); }
+
+// Chunks of n cells, and the contiguous chunk range [j0, j1) of split s of Su.
+__device__ __forceinline__ int at_nchunks(int n) { return (n + AT_CHUNK - 1) / AT_CHUNK; }
+__device__ __forceinline__ int at_splits_used(int n, int S) {
+    const int nc = at_nchunks(n);
+    return nc < S ? nc : S;
+}
+__device__ __forceinline__ void at_split(int nc, int Su, int s, int & j0, int & j1) {
+    j0 = (int)((int64_t)nc * s / Su);
+    j1 = (int)((int64_t)nc * (s + 1) / Su);
+}
+
+struct AttParams {
+    const float * q = nullptr;        // [T][Hq][128] fp32 (when qkv is null)
+    const float * qkv = nullptr;      // decode, fused: [Hq + 2 Hkv][128] raw projection of the token
+    const float * qn = nullptr, * kn = nullptr;   // QK-norm weights [128]
+    float eps = 1e-6f;
+    const float2 * rope = nullptr;    // [max_pos][64] (cos, sin)
+    const uint16_t * kc = nullptr;    // [cells][Hkv][128] fp16
+    const uint16_t * vc = nullptr;
+    uint16_t * kcw = nullptr, * vcw = nullptr;   // fused: where the new K/V cell goes (same caches)
+    int Hq = 0, Hkv = 0, T = 1, S = 1, ncap = 0;
+    int32_t pos0 = 0;
+    const int32_t * pos_dev = nullptr;
+    float scale = 0.0f;
+    int * tickets = nullptr;          // [Hkv * T]
+    float * smax = nullptr;           // [Hkv][T][S][G]
+    float * scores = nullptr;         // [Hkv][T][G][ncap]
+    double * part = nullptr;          // [Hkv][T][nchunks(ncap)][G][129]
+    float * out = nullptr;            // [T][Hq][128]
+    uint8_t * xq = nullptr;           // optional block_q8_0 records of out [T][Hq * 4]
+};
+
+struct AtLayout { size_t tickets_off, smax_off, scores_off, part_off, bytes; };
+static AtLayout at_layout(int Hq, int Hkv, int T, int S, int ncap) {
+    const int G = Hq / Hkv;
+    AtLayout l;
+    l.tickets_off = 0;
+    l.smax_off = ((size_t)Hkv * T * 4 + 255) & ~(size_t)255;
+    l.scores_off = (l.smax_off + (size_t)Hkv * T * S * G * 4 + 255) & ~(size_t)255;
+    l.part_off = (l.scores_off + (size_t)Hkv * T * G * ncap * 4 + 255) & ~(size_t)255;
+    const size_t nch = (size_t)((ncap + AT_CHUNK - 1) / AT_CHUNK);
+    l.bytes = l.part_off + (size_t)Hkv * T * nch * G * 129 * 8;
+    return l;
+}
+
+// Per-head RMSNorm over 128 values (sequential double sum of the fp32 squares,
+// ops.cpp:703-710) * w, then NEOX RoPE at position pos; v[] is the thread's
+// element (thread d of 128), the result is rounded to fp16 when `to_half`.
+// sq is 128 floats of shared scratch; all 128 threads call it.
+__device__ __forceinline__ float at_norm_rope(float v, const float * __restrict__ w, float eps, float2 cs, float * sq,
+                                              float * res, double * mean_out) {
+    const int d = threadIdx.x;
+    sq[d] = __fmul_rn(v, v);
+    __syncthreads();
+    if (d == 0) {
+        double s = 0.0;
+        for (int i = 0; i < 128; ++i) s += (double)sq[i];
+        *mean_out = s;
+    }
+    __syncthreads();
+    const float mean = (float)(*mean_out / 128.0);
+    const float scale = 1.0f / sqrtf(__fadd_rn(mean, eps));
+    res[d] = __fmul_rn(__fmul_rn(v, scale), w[d]);
+    __syncthreads();
+    float o;
+    if (d < 64) o = __fsub_rn(__fmul_rn(res[d], cs.x), __fmul_rn(res[d + 64], cs.y));
+    else        o = __fadd_rn(__fmul_rn(res[d - 64], cs.y), __fmul_rn(res[d], cs.x));
+    __syncthreads();   // res and sq are reused by the next call
+    return o;
+}
+
+// --------------------------------------------------------------- scores
+template <int G, bool FUSED>
+__global__ void __launch_bounds__(128)
+k_att_scores(const AttParams a) {
+    extern __shared__ __align__(16) uint8_t at_ring[];   // AT_NST x AT_ST x AT_KPITCH
+    __shared__ __align__(16) float qs[G][128];
+    __shared__ __align__(16) float knew[128];
+    __shared__ float sq[128], res[128];
+    __shared__ double mean_s;
+    __shared__ float red[4][G];
+    const int h = blockIdx.x, t = blockIdx.y, s = blockIdx.z, tid = threadIdx.x;
+    // positions come from memory written before this graph replay started
+    const int p0 = a.pos_dev ? a.pos_dev[0] : a.pos0;
+    const int n = p0 + t + 1;
+    const int Su = at_splits_used(n, a.S);
+    if (s == 0 && tid == 0) a.tickets[h * a.T + t] = 0;   // re-armed for k_att_pv of this call
+    if (s >= Su) return;
+    int j0, j1;
+    at_split(at_nchunks(n), Su, s, j0, j1);
+    const int c0 = j0 * AT_CHUNK, c1 = min(n, j1 * AT_CHUNK);
+    const int64_t row = (int64_t)a.Hkv * 128;
+    const uint16_t * kb = a.kc + (size_t)h * 128;
+    const int nst = (c1 - c0 + AT_ST - 1) / AT_ST;
+    auto issue = [&](int i) {
+        if (i < nst) {
+            const int cb = c0 + i * AT_ST, rows = min(AT_ST, c1 - cb);
+            uint8_t * dst = at_ring + (i % AT_NST) * AT_ST * AT_KPITCH;
+            for (int p = tid; p < rows * 16; p += 128) {
+                const int r = p >> 4, j = p & 15;
+                at_cp16(dst + r * AT_KPITCH + j * 16, kb + (size_t)(cb + r) * row + j * 8);
+            }
+        }
+        at_commit();   // one group per stage, empty past the end
+    };
+    // A decode step's cached cells were written by earlier steps: stream them
+    // before waiting.  Other calls may follow the kernel that stored the cells.
+    if constexpr (FUSED) {
+#pragma unroll
+        for (int i = 0; i < AT_NST - 1; ++i) issue(i);
+    }
+    alb_pdl_wait();
+    if constexpr (!FUSED) {
+#pragma unroll
+        for (int i = 0; i < AT_NST - 1; ++i) issue(i);
+    }
+    if constexpr (FUSED) {
+        // QK-norm + RoPE of this KV head's G query heads (and of its new K cell
+        // when this split holds it), from the raw projection of the token
+        const float2 cs = a.rope[(size_t)(n - 1) * 64 + (tid & 63)];
+        for (int g = 0; g < G; ++g) {
+            const float v = a.qkv[(size_t)(h * G + g) * 128 + tid];
+            const float o = at_norm_rope(v, a.qn, a.eps, cs, sq, res, &mean_s);
+            qs[g][tid] = __half2float(__float2half_rn(o));   // Q -> fp16 (arm.cpp:2307)
+        }
+        if (c1 == n) {   // the new cell n - 1 is this split's last
+            const float kv = a.qkv[(size_t)(a.Hq + h) * 128 + tid];
+            const float ko = at_norm_rope(kv, a.kn, a.eps, cs, sq, res, &mean_s);
+            const uint16_t kh = alb_f2h(ko);
+            knew[tid] = __half2float(__ushort_as_half(kh));
+            a.kcw[(size_t)(n - 1) * row + (size_t)h * 128 + tid] = kh;
+            a.vcw[(size_t)(n - 1) * row + (size_t)h * 128 + tid] =
+                alb_f2h(a.qkv[(size_t)(a.Hq + a.Hkv + h) * 128 + tid]);
+        }
+    } else {
+        for (int i = tid; i < G * 128; i += 128) {
+            const int g = i / 128, d = i - g * 128;
+            qs[g][d] = __half2float(__float2half_rn(a.q[((size_t)t * a.Hq + h * G + g) * 128 + d]));
+        }
+    }
+    constexpr int GH = G >= 2 ? 2 : 1, GPT = G / GH;
+    const int cl = tid & (AT_ST - 1), gh = tid / AT_ST;   // cell of the stage, head half
+    float mx[GPT];
+#pragma unroll
+    for (int k = 0; k < GPT; ++k) mx[k] = -INFINITY;
+    float * sc = a.scores + ((size_t)h * a.T + t) * G * a.ncap;
+    for (int i = 0; i < nst; ++i) {
+        at_wait<AT_NST - 2>();
+        __syncthreads();   // stage i visible to all; stage i-1 consumed by all; q / knew visible
+        issue(i + AT_NST - 1);
+        const int c = c0 + i * AT_ST + cl;
+        if (gh < GH && c < c1) {
+            const uint8_t * kr = at_ring + (i % AT_NST) * AT_ST * AT_KPITCH + cl * AT_KPITCH;
+            uint4 krow[16];
+            if (FUSED && c == n - 1) {   // the new cell: its fp16 K from this kernel, not the cache
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    uint32_t wd[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        wd[e] = (uint32_t)alb_f2h(knew[8 * j + 2 * e]) | ((uint32_t)alb_f2h(knew[8 * j + 2 * e + 1]) << 16);
+                    krow[j] = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) krow[j] = *reinterpret_cast<const uint4 *>(kr + j * 16);
+            }
+            float acc[GPT];
+#pragma unroll
+            for (int k = 0; k < GPT; ++k) acc[k] = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {   // dims 8j .. 8j+7, in order (the reference's sequential chain)
+                const uint32_t wd[4] = {krow[j].x, krow[j].y, krow[j].z, krow[j].w};
+                float kf[8];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&wd[e]));
+                    kf[2 * e] = f.x;
+                    kf[2 * e + 1] = f.y;
+                }
+#pragma unroll
+                for (int k = 0; k < GPT; ++k) {
+                    const float * qg = qs[gh * GPT + k];
+                    const float4 qa = *reinterpret_cast<const float4 *>(qg + 8 * j);
+                    const float4 qb = *reinterpret_cast<const float4 *>(qg + 8 * j + 4);
+                    acc[k] = __fmaf_rn(kf[0], qa.x, acc[k]);
+                    acc[k] = __fmaf_rn(kf[1], qa.y, acc[k]);
+                    acc[k] = __fmaf_rn(kf[2], qa.z, acc[k]);
+                    acc[k] = __fmaf_rn(kf[3], qa.w, acc[k]);
+                    acc[k] = __fmaf_rn(kf[4], qb.x, acc[k]);
+                    acc[k] = __fmaf_rn(kf[5], qb.y, acc[k]);
+                    acc[k] = __fmaf_rn(kf[6], qb.z, acc[k]);
+                    acc[k] = __fmaf_rn(kf[7], qb.w, acc[k]);
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < GPT; ++k) {
+                const float v = __fmul_rn(acc[k], a.scale);
+                sc[(size_t)(gh * GPT + k) * a.ncap + c] = v;
+                mx[k] = fmaxf(mx[k], v);
+            }
+        }
+    }
+    at_wait<0>();
+    const int lane = tid & 31, warp = tid >> 5;
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const float m = alb_warp_max(g / GPT == gh ? mx[g % GPT] : -INFINITY);
+        if (lane == 0) red[warp][g] = m;
+    }
+    __syncthreads();
+    if (tid < G) {
+        const int g = tid;
+        a.smax[(((size_t)h * a.T + t) * a.S + s) * G + g] = fmaxf(fmaxf(red[0][g], red[1][g]), fmaxf(red[2][g], red[3][g]));
+    }
+    alb_pdl_trigger();
+}
+
+// --------------------------------------------------------------- P.V + merge
+template <int G>
+__host__ __device__ constexpr size_t at_pv_stage() { return (size_t)AT_ST * 256 + (size_t)G * AT_ST * 4; }
+template <int G>
+__host__ __device__ constexpr size_t at_pv_smem() { return 2 * at_pv_stage<G>() + (size_t)G * AT_ST * 8; }
+
+template <int G>
+__global__ void __launch_bounds__(128)
+k_att_pv(const AttParams a) {
+    extern __shared__ __align__(16) uint8_t at_sm[];   // 2 x (V rows [AT_ST][256 B] + scores [G][AT_ST]), p [G][AT_ST]
+    double * pd = reinterpret_cast<double *>(at_sm + 2 * at_pv_stage<G>());
+    __shared__ float Ms[G];
+    __shared__ double Ls[G];
+    __shared__ int last_s;
+    const int h = blockIdx.x, t = blockIdx.y, s = blockIdx.z, tid = threadIdx.x;
+    const int p0 = a.pos_dev ? a.pos_dev[0] : a.pos0;
+    const int n = p0 + t + 1;
+    const int Su = at_splits_used(n, a.S);
+    if (s >= Su) return;
+    const int nch = at_nchunks(n);
+    int j0, j1;
+    at_split(nch, Su, s, j0, j1);
+    const int64_t row = (int64_t)a.Hkv * 128;
+    const uint16_t * vb = a.vc + (size_t)h * 128;
+    const float * sc = a.scores + ((size_t)h * a.T + t) * G * a.ncap;
+    const size_t nchmax = (size_t)((a.ncap + AT_CHUNK - 1) / AT_CHUNK);
+    double * part = a.part + ((size_t)h * a.T + t) * nchmax * G * 129;
+    alb_pdl_wait();   // the scores (and the new V cell) come from k_att_scores
+    if (tid < G) {
+        float m = -INFINITY;
+        for (int k = 0; k < Su; ++k) m = fmaxf(m, a.smax[(((size_t)h * a.T + t) * a.S + k) * G + tid]);
+        Ms[tid] = m;
+    }
+    // staging steps: AT_ST cells each, two per chunk, double-buffered
+    const int cbeg = j0 * AT_CHUNK, cend = min(n, j1 * AT_CHUNK);
+    const int nsteps = (cend - cbeg + AT_ST - 1) / AT_ST;
+    auto issue = [&](int i) {
+        if (i < nsteps) {
+            const int cb = cbeg + i * AT_ST, rows = min(AT_ST, cend - cb);
+            uint8_t * dst = at_sm + (i & 1) * at_pv_stage<G>();
+            for (int p = tid; p < rows * 16; p += 128) {
+                const int r = p >> 4, j = p & 15;
+                at_cp16(dst + r * 256 + j * 16, vb + (size_t)(cb + r) * row + j * 8);
+            }
+            if (tid < rows) {
+                float * sdst = reinterpret_cast<float *>(dst + AT_ST * 256);
+#pragma unroll
+                for (int g = 0; g < G; ++g) at_cp4(sdst + g * AT_ST + tid, sc + (size_t)g * a.ncap + cb + tid);
+            }
+        }
+        at_commit();
+    };
+    issue(0);
+    double O[G];
+    double Lc = 0.0;   // thread g < G: the chunk's sum of p for query head g
+#pragma unroll
+    for (int g = 0; g < G; ++g) O[g] = 0.0;
+    for (int i = 0; i < nsteps; ++i) {
+        issue(i + 1);
+        at_wait<1>();
+        __syncthreads();   // step i visible; Ms visible; pd free
+        const uint8_t * stg = at_sm + (i & 1) * at_pv_stage<G>();
+        const int cb = cbeg + i * AT_ST, rows = min(AT_ST, cend - cb);
+        if (tid < AT_ST) {
+            const float * ss = reinterpret_cast<const float *>(stg + AT_ST * 256);
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                double v = 0.0;
+                if (tid < rows) v = (double)alb_ref_expf(__fsub_rn(ss[g * AT_ST + tid], Ms[g])) * 0x1p1008;
+                pd[g * AT_ST + tid] = v;   // p * 2^1008, exact
+            }
+        }
+        __syncthreads();
+        if (tid < G) {   // the chunk's sum of p, cells in order
+            for (int c = 0; c < rows; ++c) Lc += pd[tid * AT_ST + c] * 0x1p-1008;
+        }
+        // O_g,d: cells in order; V bits enter as (v * 2^-1008) and p as (p * 2^1008),
+        // so fma(p', v', O) adds the exact product p * v
+        const uint16_t * vs = reinterpret_cast<const uint16_t *>(stg) + tid;
+        for (int c = 0; c < rows; ++c) {
+            const double vd = alb_h2d_bits(vs[c * 128]);
+#pragma unroll
+            for (int g = 0; g < G; ++g) O[g] = fma(pd[g * AT_ST + c], vd, O[g]);
+        }
+        // chunk complete (every second step, or the split's last): its partial
+        const int j = (cb - j0 * AT_CHUNK) / AT_CHUNK + j0;
+        if ((i & 1) == 1 || i == nsteps - 1) {
+            double * pj = part + (size_t)j * G * 129;
+#pragma unroll
+            for (int g = 0; g < G; ++g) { pj[g * 129 + tid] = O[g]; O[g] = 0.0; }
+            if (tid < G) { pj[tid * 129 + 128] = Lc; Lc = 0.0; }
+        }
+        __syncthreads();   // pd and buffer i & 1 consumed
+    }
+    at_wait<0>();
+    // the last CTA of (h, t) adds every chunk's partial in chunk order
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) last_s = atomicAdd(&a.tickets[h * a.T + t], 1) == Su - 1;
+    __syncthreads();
+    if (!last_s) { alb_pdl_trigger(); return; }
+    __threadfence();
+    if (tid < G) {
+        double L = 0.0;
+        for (int j = 0; j < nch; ++j) L += __ldcg(part + (size_t)j * G * 129 + tid * 129 + 128);
+        Ls[tid] = L;
+    }
+    __syncthreads();
+    const int lane = tid & 31, warp = tid >> 5;
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        double Od = 0.0;
+        for (int j = 0; j < nch; ++j) Od += __ldcg(part + (size_t)j * G * 129 + g * 129 + tid);
+        const float v = Ls[g] > 0.0 ? __double2float_rn(Od / Ls[g]) : 0.0f;
+        const int hq = h * G + g;
+        a.out[((size_t)t * a.Hq + hq) * 128 + tid] = v;
+        if (a.xq) {   // quantize_row_q8_0 of the output: warp w owns block (hq, w)
+            int8_t q; uint16_t dh;
+            q8_block_lane(v, q, dh);
+            uint8_t * blk = a.xq + (((size_t)t * a.Hq + hq) * 4 + warp) * 34;
+            if (lane == 0) *reinterpret_cast<uint16_t *>(blk) = dh;
+            blk[2 + lane] = (uint8_t)q;
+        }
+    }
+    if (tid == 0) a.tickets[h * a.T + t] = 0;
+    alb_pdl_trigger();
+}
+
+template <int G, bool FUSED>
+static cudaError_t launch_att_t(const AttParams & p, bool pdl, cudaStream_t st) {
+    cudaError_t e = ensure_smem(k_att_scores<G, FUSED>, AT_SCORES_SMEM);
+    if (e == cudaSuccess) e = ensure_smem(k_att_pv<G>, at_pv_smem<G>());
+    if (e != cudaSuccess) return e;
+    const dim3 grid((unsigned)p.Hkv, (unsigned)p.T, (unsigned)p.S);
+    e = alb_launch(k_att_scores<G, FUSED>, grid, dim3(128), AT_SCORES_SMEM, st, pdl, p);
+    if (e != cudaSuccess) return e;
+    return alb_launch(k_att_pv<G>, grid, dim3(128), at_pv_smem<G>(), st, pdl, p);
+}
+
+template <bool FUSED>
+static cudaError_t launch_att(const AttParams & p, bool pdl, cudaStream_t st) {
+    if (p.Hkv <= 0 || p.Hq % p.Hkv != 0 || p.S < 1 || p.S > 65535 || p.T < 1 || p.T > 65535 || p.ncap <= 0)
+        return cudaErrorInvalidValue;
+    switch (p.Hq / p.Hkv) {
+        case 1: return launch_att_t<1, FUSED>(p, pdl, st);
+        case 2: return launch_att_t<2, FUSED>(p, pdl, st);
+        case 4: return launch_att_t<4, FUSED>(p, pdl, st);
+        case 8: return launch_att_t<8, FUSED>(p, pdl, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+static AttParams att_params(const FlashArgs & f) {
+    AttParams p;
+    const AtLayout l = at_layout(f.Hq, f.Hkv, f.T, f.S, f.ncap);
+    uint8_t * ws = reinterpret_cast<uint8_t *>(f.ws);
+    p.tickets = reinterpret_cast<int *>(ws + l.tickets_off);
+    p.smax = reinterpret_cast<float *>(ws + l.smax_off);
+    p.scores = reinterpret_cast<float *>(ws + l.scores_off);
+    p.part = reinterpret_cast<double *>(ws + l.part_off);
+    p.q = f.q; p.kc = f.kc; p.vc = f.vc; p.Hq = f.Hq; p.Hkv = f.Hkv; p.T = f.T; p.S = f.S; p.ncap = f.ncap;
+    p.pos0 = f.pos0; p.pos_dev = f.pos_dev; p.scale = f.scale; p.out = f.out;
+    p.xq = static_cast<uint8_t *>(f.xq);
+    return p;
+}
+
+size_t split_attn_ws_bytes(int Hq, int Hkv, int T, int S, int ncap) {
+    return at_layout(Hq, Hkv, T, S, ncap).bytes;
+}
+
+cudaError_t launch_split_attn(const FlashArgs & f, cudaStream_t st) {
+    if (!f.ws) return cudaErrorInvalidValue;
+    return launch_att<false>(att_params(f), f.pdl, st);
+}
+
+cudaError_t launch_attn_decode(const FlashArgs & f, const QkvArgs & qa, cudaStream_t st) {
+    if (!f.ws || f.T != 1 || !qa.qkv || !qa.rope || !qa.q_norm || !qa.k_norm) return cudaErrorInvalidValue;
+    AttParams p = att_params(f);
+    p.q = nullptr;
+    p.qkv = qa.qkv; p.qn = qa.q_norm; p.kn = qa.k_norm; p.eps = qa.eps; p.rope = qa.rope;
+    p.kcw = qa.kc; p.vcw = qa.vc;
+    return launch_att<true>(p, f.pdl, st);
+}
+
+}  // namespace alb

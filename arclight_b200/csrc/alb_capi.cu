@@ -101,6 +101,7 @@ extern "C" int alb_flash_attn(const float * q, const uint16_t * k_cache, const u
     f.ncap = (int)(pos0 + T);
     f.q = q; f.kc = k_cache; f.vc = v_cache; f.Hq = n_head; f.Hkv = n_head_kv; f.T = (int)T;
     f.pos0 = pos0; f.scale = scale; f.S = splits; f.ws = (float *)workspace; f.out = out; f.pdl = true;
+    ALB_CHECK_ARG(workspace || !flash_attn_uses_ws(n_head, n_head_kv, (int)T, splits, f.ncap));
     ALB_CUDA_TRY(launch_flash_attn(f, (cudaStream_t)stream));
     return ALB_OK;
 }

@@ -169,6 +169,25 @@ __device__ __forceinline__ void alb_bulk_g2s(void * dst_smem, const void * src, 
                  :: "r"(alb_smem_addr(dst_smem)), "l"(src), "r"(bytes), "r"(alb_smem_addr(bar)) : "memory");
 }
 
+// ---------------------------------------------------------------- RMSNorm mean
+// rms_norm_f32 (ops.cpp:703-710) sums the n fp32 squares in double in index
+// order, then rounds sum / n to float.  A parallel sum of the same terms differs
+// from that sequential sum by at most 2 (n - 1) u |sum| (u = 2^-53, recursive
+// summation bound on each), so when both ends of [par - d, par + d] with
+// d = 8 n u par give the same float mean, the sequential sum gives it too; only
+// otherwise (probability ~ 16 n u / 2^-24 per norm) must the caller take the
+// sequential sum itself.
+__device__ __forceinline__ bool alb_rms_mean_certain(double par, int n) {
+    const double d = par * (double)n * 0x1p-50;
+    return (float)((par - d) / (double)n) == (float)((par + d) / (double)n);
+}
+// The sequential sum of the squares of x[0..n) (one thread).
+__device__ __forceinline__ double alb_rms_seq_sum(const float * x, int n) {
+    double s = 0.0;
+    for (int i = 0; i < n; ++i) s += (double)__fmul_rn(x[i], x[i]);
+    return s;
+}
+
 // ---------------------------------------------------------------- reference expf / silu
 // nnml_v_expf (arm.cpp:1757-1787) per lane, so SwiGLU matches the reference's
 // NEON path bit for bit: exp(x) = 2^n (1 + p(b)), n from the 1.5*2^23 shift,

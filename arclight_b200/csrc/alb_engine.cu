@@ -165,15 +165,21 @@ static int engine_forward(alb_engine * e, int64_t T, bool pdl, int ncap_prefill 
         qa.qkv = e->qkv; qa.qkv_stride = e->Nqkv; qa.Hq = e->Hq; qa.Hkv = e->Hkv; qa.T = (int)T;
         qa.q_norm = L.qn; qa.k_norm = L.kn; qa.eps = c.eps; qa.rope = reinterpret_cast<const float2 *>(e->rope);
         qa.pos_dev = e->pos_dev; qa.q_out = e->q; qa.kc = L.kc; qa.vc = L.vc; qa.pdl = pdl;
-        ALB_CUDA_TRY(launch_qk_norm_rope_kv(qa, st));
         FlashArgs fa;
         fa.q = e->q; fa.kc = L.kc; fa.vc = L.vc; fa.Hq = e->Hq; fa.Hkv = e->Hkv; fa.T = (int)T;
         fa.pos_dev = e->pos_dev; fa.scale = 1.0f / sqrtf((float)c.head_dim); fa.S = S; fa.ws = e->fa_ws;
         fa.ncap = T == 1 ? e->max_ctx : ncap_prefill;
         fa.out = e->att; fa.pdl = pdl;
-        fa.xq = T == 1 ? e->xq : nullptr;   // decode: the merge writes the o_proj input records
-        ALB_CUDA_TRY(launch_flash_attn(fa, st));
-        launches += S > 1 ? 4 : 2;   // QK-norm/RoPE, then scores + PV + merge, or the prefill attention
+        if (T == 1) {
+            // decode: QK-norm + RoPE + K/V store inside the split score kernel; the
+            // last CTA of each KV head writes the O projection's Q8_0 input records
+            fa.xq = e->xq;
+            ALB_CUDA_TRY(launch_attn_decode(fa, qa, st));
+        } else {
+            ALB_CUDA_TRY(launch_qk_norm_rope_kv(qa, st));
+            ALB_CUDA_TRY(launch_flash_attn(fa, st));
+        }
+        launches += 2;   // scores + P.V, or QK-norm/RoPE + the prefill attention
         const int o_in = T == 1 ? GEMV_IN_Q8 : GEMV_IN_F32;
         const void * o_x = T == 1 ? e->xq : static_cast<const void *>(e->att);
         if (e->tp == 1) {
@@ -342,9 +348,7 @@ static int engine_init_acts(alb_engine * e) {
     int S = (4 * alb_sm_count() + e->Hkv - 1) / e->Hkv;
     if (S > 1024) S = 1024;
     e->fa_S_decode = S;
-    e->fa_ws_bytes = flash_attn_ws_bytes(e->Hq, e->Hkv, 1, S, e->max_ctx);
-    const size_t pre = flash_attn_ws_bytes(e->Hq, e->Hkv, e->max_ub, 1, e->max_ctx);   // prefill beyond fused smem
-    if (pre > e->fa_ws_bytes) e->fa_ws_bytes = pre;
+    e->fa_ws_bytes = flash_attn_ws_bytes(e->Hq, e->Hkv, 1, S, e->max_ctx);   // prefill ubatches need none
     uint8_t * ws = nullptr;
     ALB_TRY(e->alloc(&ws, e->fa_ws_bytes));
     e->fa_ws = reinterpret_cast<float *>(ws);
@@ -534,6 +538,15 @@ extern "C" int alb_engine_logits(alb_engine * e, float * host, int64_t n) {
     ALB_CHECK_ARG(e && host && n == e->V);
     ALB_CUDA_TRY(cudaSetDevice(e->dev));
     ALB_CUDA_TRY(cudaMemcpyAsync(host, e->logits, (size_t)n * 4, cudaMemcpyDeviceToHost, e->st));
+    ALB_CUDA_TRY(cudaStreamSynchronize(e->st));
+    return ALB_OK;
+}
+
+// The residual stream of the last forward pass (rows of its ubatch), for checks.
+extern "C" int alb_engine_hidden(alb_engine * e, float * host, int64_t rows) {
+    ALB_CHECK_ARG(e && host && rows > 0 && rows <= e->max_ub);
+    ALB_CUDA_TRY(cudaSetDevice(e->dev));
+    ALB_CUDA_TRY(cudaMemcpyAsync(host, e->x, (size_t)rows * e->E * 4, cudaMemcpyDeviceToHost, e->st));
     ALB_CUDA_TRY(cudaStreamSynchronize(e->st));
     return ALB_OK;
 }

@@ -73,6 +73,8 @@ struct FlashArgs {
     bool pdl = false;
 };
 size_t flash_attn_ws_bytes(int Hq, int Hkv, int T, int S, int ncap);
+size_t split_attn_ws_bytes(int Hq, int Hkv, int T, int S, int ncap);
+cudaError_t launch_split_attn(const FlashArgs & f, cudaStream_t st);
 // false when the call's kernels need no workspace (launch_flash_attn's path choice)
 bool flash_attn_uses_ws(int Hq, int Hkv, int T, int S, int ncap);
 cudaError_t launch_flash_attn(const FlashArgs & f, cudaStream_t st);
@@ -91,6 +93,10 @@ struct QkvArgs {
     bool pdl = false;
 };
 cudaError_t launch_qk_norm_rope_kv(const QkvArgs & a, cudaStream_t st);
+// Decode step attention with QK-norm + RoPE + the K/V store fused (T = 1):
+// f describes the attention (workspace, splits, output and its Q8_0 records),
+// qa the raw QKV projection, norm weights, RoPE table and the caches to store into.
+cudaError_t launch_attn_decode(const FlashArgs & f, const QkvArgs & qa, cudaStream_t st);
 cudaError_t launch_embed(const uint8_t * W, int64_t vocab, int64_t E, const int32_t * tokens, int T, float * x,
                          unsigned long long * key_reset, bool pdl, cudaStream_t st);
 // argmax over x[0..n): scratch >= 64*8 + 16 bytes with its ticket word zero at first use

@@ -8,9 +8,8 @@
 //   * the workspace alb_flash_attn_workspace_bytes(...) of the call must fit
 //     ALB_FLASH_ATTN_STATIC_BYTES (4 MiB) when the call's path uses one (the
 //     split kernels); larger calls are rejected with ALB_ERR_INVALID before
-//     anything is launched.  Prefill ubatches (one split) and single-split
-//     decode calls whose scores fit shared memory use no workspace and are
-//     never rejected for size;
+//     anything is launched.  Prefill ubatches (T > 1, one split) use no
+//     workspace and are never rejected for size;
 //   * the array's address is looked up once per device and kept: a
 //     cudaDeviceReset of that device afterwards is not supported;
 //   * there is one such array per device, shared by every call on that

@@ -171,8 +171,11 @@ k_prefill_gemm(const uint8_t * __restrict__ Wn, const uint8_t * __restrict__ Ws,
         asm volatile("cp.async.commit_group;" ::: "memory");   // one group per block (empty past the end)
     };
 
-    auto epilogue = [&](int64_t kb) {
-        const int s = (int)(kb & 1), st = (int)(kb % PG_STAGES);
+    // dxr: this thread's token-row scale of block kb, read from the ring when the
+    // block landed (the ring stage is refilled by other warps while this one may
+    // still be in its epilogue, so the scale is carried in a register)
+    auto epilogue = [&](int64_t kb, float dxr) {
+        const int s = (int)(kb & 1);
         pg_fence_after();
         uint32_t c[32];
         const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(s * PG_N + chalf * 32);
@@ -186,7 +189,6 @@ k_prefill_gemm(const uint8_t * __restrict__ Wn, const uint8_t * __restrict__ Ws,
                        "=r"(c[29]), "=r"(c[30]), "=r"(c[31])
                      : "r"(taddr));
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        const float dxr = sh.dx[st][row];
         const float * dw = sh.dwf[s] + chalf * 32;
         // float(I) exactly as 2^23 * 1.5 + I - 2^23 * 1.5 (|I| < 2^22): integer add +
         // fp32 subtract instead of a conversion; dx * dw is exact (11 x 11 bits)
@@ -200,10 +202,13 @@ k_prefill_gemm(const uint8_t * __restrict__ Wn, const uint8_t * __restrict__ Ws,
 
     for (int64_t kb = 0; kb < PG_STAGES - 1; ++kb) prefetch(kb);
     bool ok = true;
+    float dx_prev = 0.0f, dx_cur = 0.0f;   // this row's activation scales of blocks b-1 and b
     for (int64_t b = 0; b < nb && ok; ++b) {
         const int s = (int)(b & 1), st = (int)(b % PG_STAGES);
         asm volatile("cp.async.wait_group %0;" :: "n"(PG_STAGES - 2) : "memory");   // block b has landed
         __syncthreads();
+        dx_prev = dx_cur;
+        dx_cur = sh.dx[st][row];   // stage st is refilled only after the next iteration's epilogue
         if (tid >= PG_N && tid < 2 * PG_N) {   // weight scales of block b, once per block
             const int n = tid - PG_N;
             const uint32_t wd = sh.dww[st][n];
@@ -236,7 +241,7 @@ k_prefill_gemm(const uint8_t * __restrict__ Wn, const uint8_t * __restrict__ Ws,
         ++issued;
         if (b > 0) {   // block b-1 (other TMEM buffer) while the tensor core works on block b
             ok = pg_wait(sh, s ^ 1, (uint32_t)(((b - 1) >> 1) & 1), err);
-            if (ok) { epilogue(b - 1); ++waited; }
+            if (ok) { epilogue(b - 1, dx_prev); ++waited; }
         }
         // block b-1 is consumed (MMA done, scales read): its ring stage takes block b + PG_STAGES - 1
         prefetch(b + PG_STAGES - 1);
@@ -246,7 +251,7 @@ k_prefill_gemm(const uint8_t * __restrict__ Wn, const uint8_t * __restrict__ Ws,
     if (ok) {
         const int64_t b = nb - 1;
         ok = pg_wait(sh, (int)(b & 1), (uint32_t)((b >> 1) & 1), err);
-        if (ok) { epilogue(b); ++waited; }
+        if (ok) { epilogue(b, dx_cur); ++waited; }
     }
     asm volatile("cp.async.wait_all;" ::: "memory");   // no copy in flight past this point
     if (!ok) {

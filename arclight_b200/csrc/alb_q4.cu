@@ -205,9 +205,10 @@ __device__ __forceinline__ void mv_prologue(const GemvArgs & a, int * xs, int nb
         asm volatile("bar.sync 1, %0;" :: "n"(NT) : "memory");
         float scale = 1.0f;
         if constexpr (IN == GEMV_IN_F32_RMS) {
-            // every fp32 square is exact in double and the sum of K of them is too,
-            // so this order gives the reference's sequential double sum
+            // a parallel double sum of the fp32 squares; the reference's
+            // sequential sum (ops.cpp:703-710) only where the float mean could differ
             __shared__ double red[NW];
+            __shared__ double seq_sum;
             double s = 0.0;
             for (int i = tid; i < K; i += NT) { const float v = xf[i]; s += (double)__fmul_rn(v, v); }
 #pragma unroll
@@ -217,6 +218,11 @@ __device__ __forceinline__ void mv_prologue(const GemvArgs & a, int * xs, int nb
             double t = 0.0;
 #pragma unroll
             for (int w = 0; w < NW; ++w) t += red[w];
+            if (!alb_rms_mean_certain(t, K)) {   // uniform across the CTA
+                if (tid == 0) seq_sum = alb_rms_seq_sum(xf, K);
+                asm volatile("bar.sync 1, %0;" :: "n"(NT) : "memory");
+                t = seq_sum;
+            }
             const float mean = (float)(t / (double)a.K);
             scale = 1.0f / sqrtf(__fadd_rn(mean, a.eps));
         }

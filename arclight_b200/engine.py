@@ -90,6 +90,12 @@ class Engine:
         check(lib().alb_engine_logits(self.h, out.ctypes.data_as(C.c_void_p), out.size), "alb_engine_logits")
         return out
 
+    def hidden(self, rows: int) -> np.ndarray:
+        """Residual stream of the last forward pass, rows [0, rows) of its ubatch."""
+        out = np.empty((rows, self.cfg["n_embd"]), np.float32)
+        check(lib().alb_engine_hidden(self.h, out.ctypes.data_as(C.c_void_p), rows), "alb_engine_hidden")
+        return out
+
     def stream(self) -> int:
         return lib().alb_engine_stream(self.h) or 0
 

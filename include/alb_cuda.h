@@ -136,11 +136,13 @@ ALB_API int alb_qk_norm_rope_kv(const float * qkv, int64_t T, int32_t n_head, in
  * causal: token t (position pos0+t) attends cells [0, pos0+t] of the fp16
  * caches [cells][Hkv][128]; GQA ratio n_head/n_head_kv in {1,2,4,8}.  Scores
  * are fp32 (Q rounded to fp16 as the reference), the softmax uses the global
- * max and the reference's NEON exp, sums are double: the result does not depend
- * on `splits` (the cells are split over that many CTAs and merged in-kernel).
+ * max and the reference's NEON exp, and the sums of p and p*v are double in a
+ * canonical order (cells in order within 128-cell chunks, chunk sums in chunk
+ * order): the result does not depend on `splits` (the cells are split over that
+ * many CTAs per KV head and token, whole chunks each, and merged in-kernel).
  * Workspace: alb_flash_attn_workspace_bytes(.., n_cells = pos0 + T) (no
- * state kept between calls); may be NULL when splits == 1 and
- * 4 * (n_head/n_head_kv) * (pos0+T) <= 160 KiB.  q/out [T][Hq][128]. */
+ * state kept between calls); may be NULL when T > 1 and splits == 1 (the
+ * token-tiled prefill kernel).  q/out [T][Hq][128]. */
 ALB_API size_t alb_flash_attn_workspace_bytes(int32_t n_head, int32_t n_head_kv, int64_t T, int32_t splits,
                                              int32_t n_cells);
 ALB_API int alb_flash_attn(const float * q, const uint16_t * k_cache, const uint16_t * v_cache, int64_t T,
@@ -160,7 +162,7 @@ ALB_API int alb_flash_attn(const float * q, const uint16_t * k_cache, const uint
  * it (cudaGetSymbolAddress, cudaMemsetAsync on `stream`); make it outside any
  * stream capture.  The looked-up address is kept for the life of the process:
  * a cudaDeviceReset of that device is not supported afterwards.  Calls whose
- * path needs no workspace (single split, fused or token-tiled kernels) are
+ * path needs no workspace (T > 1 with one split: the token-tiled kernel) are
  * never rejected for size.  Same results as alb_flash_attn.  No counterpart in the
  * reference (its ops take scratch from params->work_data, thread.h:166-167). */
 ALB_API int alb_flash_attn_static(const float * q, const uint16_t * k_cache, const uint16_t * v_cache, int64_t T,
@@ -219,6 +221,9 @@ ALB_API int alb_engine_decode_loop(alb_engine * e, int32_t token, int32_t pos, i
                                    int32_t sync);
 /* Last logits of this rank's vocabulary shard [n_vocab / tp_size]. */
 ALB_API int alb_engine_logits(alb_engine * e, float * host, int64_t n);
+/* The residual stream (the hidden state before the output norm) of the last
+ * forward pass, rows [0, rows) of its ubatch, [rows][n_embd] (host). */
+ALB_API int alb_engine_hidden(alb_engine * e, float * host, int64_t rows);
 /* info[0..7] = local vocab, vocab offset, local q heads, local kv heads, local
  * ffn, kernel launches per decode step, device bytes, decode attention splits */
 ALB_API int alb_engine_info(const alb_engine * e, int64_t * info, int32_t n);

@@ -527,7 +527,7 @@ static void fa_range(void * pc, int64_t b, int64_t e) {
     float * VKQ32 = (float *)malloc(D * 4);
     float * Qf = (float *)malloc(D * 4);
     float * sc = (float *)malloc(f->nmax * 4);
-    double * Od = (double *)malloc((D + (f->mode == 2 ? f->nmax : 0)) * sizeof(double));
+    double * Od = (double *)malloc((2 * D + (f->mode == 2 ? f->nmax : 0)) * sizeof(double));
     for (int64_t idx = b; idx < e; ++idx) {
         const int64_t t = idx / n_head, h = idx - t * n_head;
         const int64_t n_kv = f->kv_len[t];
@@ -541,7 +541,7 @@ static void fa_range(void * pc, int64_t b, int64_t e) {
                  * K/V): scores, exp and sums in double, one rounding at the end;
                  * the yardstick for the errors of modes 0 and 1 */
                 double M = -INFINITY;
-                double * sd = Od + D;   /* scratch of n_kv doubles after Od */
+                double * sd = Od + 2 * D;   /* scratch of n_kv doubles after Od and Oc */
                 for (int64_t c = 0; c < n_kv; ++c) {
                     const uint16_t * kc = k + c * row + hk * D;
                     double a = 0.0;
@@ -569,13 +569,24 @@ static void fa_range(void * pc, int64_t b, int64_t e) {
                     sc[c] = a * scale;
                     M = sc[c] > M ? sc[c] : M;
                 }
+                /* chunked canonical order: cells in order within each ORC_FA_CHUNK-cell
+                 * chunk from 0, chunk sums added in chunk order from 0 (every p * v is
+                 * exact in double; only the additions round) */
                 double L = 0.0;
+                double * Oc = Od + D;
                 for (int64_t d = 0; d < D; ++d) Od[d] = 0.0;
-                for (int64_t c = 0; c < n_kv; ++c) {
-                    const float p = orc_neon_expf(sc[c] - M);
-                    const uint16_t * vc = v + c * row + hk * D;
-                    L += (double)p;
-                    for (int64_t d = 0; d < D; ++d) Od[d] += (double)p * (double)orc_fp16_to_fp32(vc[d]);
+                for (int64_t c0 = 0; c0 < n_kv; c0 += ORC_FA_CHUNK) {
+                    const int64_t c1 = c0 + ORC_FA_CHUNK < n_kv ? c0 + ORC_FA_CHUNK : n_kv;
+                    double Lc = 0.0;
+                    for (int64_t d = 0; d < D; ++d) Oc[d] = 0.0;
+                    for (int64_t c = c0; c < c1; ++c) {
+                        const float p = orc_neon_expf(sc[c] - M);
+                        const uint16_t * vc = v + c * row + hk * D;
+                        Lc += (double)p;
+                        for (int64_t d = 0; d < D; ++d) Oc[d] += (double)p * (double)orc_fp16_to_fp32(vc[d]);
+                    }
+                    L += Lc;
+                    for (int64_t d = 0; d < D; ++d) Od[d] += Oc[d];
                 }
                 for (int64_t d = 0; d < D; ++d) po[d] = L > 0.0 ? (float)(Od[d] / L) : 0.0f;
                 continue;

@@ -99,11 +99,14 @@ void orc_gather_sum(const float * const * srcs, int n_srcs, float * dst, int64_t
  * kv_len[t]: token t attends cells [0, kv_len[t]) (the causal mask of
  *        cgraph.cpp:1224-1261 for one sequence filled in order)
  * out  : [T][n_head][D] fp32
- * mode 0: fp32 scores, global-max softmax with nnml_v_expf, double sums (the
- *         split-independent semantics of the CUDA kernels);
+ * mode 0: fp32 scores, global-max softmax with nnml_v_expf, double sums in a
+ *         canonical order: cells in order within chunks of ORC_FA_CHUNK cells,
+ *         chunk sums added in chunk order (the semantics of the CUDA kernels,
+ *         independent of how they split the cells);
  * mode 1: ARM-faithful fp16 VKQ/KQ accumulation with online softmax;
  * mode 2: the same function in fp64 (scores, exp, sums), rounded once: the
  *         yardstick that modes 0 and 1 are measured against. */
+#define ORC_FA_CHUNK 128
 void orc_flash_attn(const float * q, const uint16_t * k, const uint16_t * v, const int32_t * kv_len,
                     int64_t T, int64_t n_head, int64_t n_head_kv, int64_t D, float scale,
                     int mode, float * out);
