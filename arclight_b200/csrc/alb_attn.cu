@@ -96,30 +96,61 @@ static AtLayout at_layout(int Hq, int Hkv, int T, int S, int ncap) {
     return l;
 }
 
-// Per-head RMSNorm over 128 values (sequential double sum of the fp32 squares,
-// ops.cpp:703-710) * w, then NEOX RoPE at position pos; v[] is the thread's
-// element (thread d of 128), the result is rounded to fp16 when `to_half`.
-// sq is 128 floats of shared scratch; all 128 threads call it.
-__device__ __forceinline__ float at_norm_rope(float v, const float * __restrict__ w, float eps, float2 cs, float * sq,
-                                              float * res, double * mean_out) {
-    const int d = threadIdx.x;
-    sq[d] = __fmul_rn(v, v);
+// Per-head RMSNorm over 128 values * w, then NEOX RoPE at the position of cs,
+// for NH heads at once (qwen3.cpp:215-224, ops.cpp:680-724, 830-938).  Thread d
+// of 128 holds element d of head k in v[k] (heads k >= nh are idle).  Each
+// head's mean is the reference's sequential double sum of the fp32 squares
+// divided by 128: a parallel double sum stands in for it where the rounded
+// float mean is certainly the same, one thread re-sums it sequentially where
+// not.  Heads k < nq use wq, the others wk.  Returns the roped values in v.
+template <int NH>
+__device__ __forceinline__ void at_norm_rope_heads(float (&v)[NH], int nh, int nq, const float * __restrict__ wq,
+                                                   const float * __restrict__ wk, float eps, float2 cs,
+                                                   float (*hb)[128], double (*hred)[NH], double * hseq) {
+    const int d = threadIdx.x, lane = d & 31, warp = d >> 5;
+    double part[NH];
+#pragma unroll
+    for (int k = 0; k < NH; ++k) {
+        part[k] = (double)__fmul_rn(v[k], v[k]);
+        hb[k][d] = v[k];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int k = 0; k < NH; ++k) part[k] += __shfl_xor_sync(0xffffffffu, part[k], o);
+    if (lane == 0)
+#pragma unroll
+        for (int k = 0; k < NH; ++k) hred[warp][k] = part[k];
     __syncthreads();
-    if (d == 0) {
-        double s = 0.0;
-        for (int i = 0; i < 128; ++i) s += (double)sq[i];
-        *mean_out = s;
+    double tot[NH];
+    bool sure[NH];
+#pragma unroll
+    for (int k = 0; k < NH; ++k) {
+        tot[k] = ((hred[0][k] + hred[1][k]) + hred[2][k]) + hred[3][k];
+        sure[k] = k >= nh || alb_rms_mean_certain(tot[k], 128);
+    }
+    if (d < nh && d < NH) {   // rare: the sequential sum of a head whose certificate failed
+        bool mine_sure = true;
+#pragma unroll
+        for (int k = 0; k < NH; ++k) if (k == d) mine_sure = sure[k];
+        if (!mine_sure) hseq[d] = alb_rms_seq_sum(hb[d], 128);
+    }
+    __syncthreads();   // hseq ready; hb is rewritten below
+#pragma unroll
+    for (int k = 0; k < NH; ++k) {
+        if (k >= nh) continue;
+        const double sum = sure[k] ? tot[k] : hseq[k];
+        const float mean = (float)(sum / 128.0);
+        const float scale = 1.0f / sqrtf(__fadd_rn(mean, eps));
+        hb[k][d] = __fmul_rn(__fmul_rn(v[k], scale), (k < nq ? wq : wk)[d]);
     }
     __syncthreads();
-    const float mean = (float)(*mean_out / 128.0);
-    const float scale = 1.0f / sqrtf(__fadd_rn(mean, eps));
-    res[d] = __fmul_rn(__fmul_rn(v, scale), w[d]);
-    __syncthreads();
-    float o;
-    if (d < 64) o = __fsub_rn(__fmul_rn(res[d], cs.x), __fmul_rn(res[d + 64], cs.y));
-    else        o = __fadd_rn(__fmul_rn(res[d - 64], cs.y), __fmul_rn(res[d], cs.x));
-    __syncthreads();   // res and sq are reused by the next call
-    return o;
+#pragma unroll
+    for (int k = 0; k < NH; ++k) {
+        if (k >= nh) continue;
+        if (d < 64) v[k] = __fsub_rn(__fmul_rn(hb[k][d], cs.x), __fmul_rn(hb[k][d + 64], cs.y));
+        else        v[k] = __fadd_rn(__fmul_rn(hb[k][d - 64], cs.y), __fmul_rn(hb[k][d], cs.x));
+    }
 }
 
 // --------------------------------------------------------------- scores
@@ -129,8 +160,9 @@ k_att_scores(const AttParams a) {
     extern __shared__ __align__(16) uint8_t at_ring[];   // AT_NST x AT_ST x AT_KPITCH
     __shared__ __align__(16) float qs[G][128];
     __shared__ __align__(16) float knew[128];
-    __shared__ float sq[128], res[128];
-    __shared__ double mean_s;
+    __shared__ float hb[FUSED ? G + 1 : 1][128];
+    __shared__ double hred[4][G + 1];
+    __shared__ double hseq[G + 1];
     __shared__ float red[4][G];
     const int h = blockIdx.x, t = blockIdx.y, s = blockIdx.z, tid = threadIdx.x;
     // positions come from memory written before this graph replay started
@@ -168,18 +200,20 @@ k_att_scores(const AttParams a) {
         for (int i = 0; i < AT_NST - 1; ++i) issue(i);
     }
     if constexpr (FUSED) {
-        // QK-norm + RoPE of this KV head's G query heads (and of its new K cell
-        // when this split holds it), from the raw projection of the token
+        // QK-norm + RoPE of this KV head's G query heads and, when this split
+        // holds the new cell n - 1 (its last), of the new K, all heads at once,
+        // from the raw projection of the token
         const float2 cs = a.rope[(size_t)(n - 1) * 64 + (tid & 63)];
-        for (int g = 0; g < G; ++g) {
-            const float v = a.qkv[(size_t)(h * G + g) * 128 + tid];
-            const float o = at_norm_rope(v, a.qn, a.eps, cs, sq, res, &mean_s);
-            qs[g][tid] = __half2float(__float2half_rn(o));   // Q -> fp16 (arm.cpp:2307)
-        }
-        if (c1 == n) {   // the new cell n - 1 is this split's last
-            const float kv = a.qkv[(size_t)(a.Hq + h) * 128 + tid];
-            const float ko = at_norm_rope(kv, a.kn, a.eps, cs, sq, res, &mean_s);
-            const uint16_t kh = alb_f2h(ko);
+        const bool with_k = c1 == n;
+        float v[G + 1];
+#pragma unroll
+        for (int g = 0; g < G; ++g) v[g] = a.qkv[(size_t)(h * G + g) * 128 + tid];
+        v[G] = with_k ? a.qkv[(size_t)(a.Hq + h) * 128 + tid] : 0.0f;
+        at_norm_rope_heads<G + 1>(v, with_k ? G + 1 : G, G, a.qn, a.kn, a.eps, cs, hb, hred, hseq);
+#pragma unroll
+        for (int g = 0; g < G; ++g) qs[g][tid] = __half2float(__float2half_rn(v[g]));   // Q -> fp16 (arm.cpp:2307)
+        if (with_k) {
+            const uint16_t kh = alb_f2h(v[G]);
             knew[tid] = __half2float(__ushort_as_half(kh));
             a.kcw[(size_t)(n - 1) * row + (size_t)h * 128 + tid] = kh;
             a.vcw[(size_t)(n - 1) * row + (size_t)h * 128 + tid] =
@@ -275,15 +309,34 @@ __host__ __device__ constexpr size_t at_pv_stage() { return (size_t)AT_ST * 256 
 template <int G>
 __host__ __device__ constexpr size_t at_pv_smem() { return 2 * at_pv_stage<G>() + (size_t)G * AT_ST * 8; }
 
+static constexpr int AT_PV_THREADS = 160;   // warps 0-3: one thread per dimension; warp 4: the sums of p
+
+// Ordered double sum of n values at p[0], p[stride], ... (n >= 0), loads issued
+// eight at a time ahead of the additions.
+__device__ __forceinline__ double at_ordered_sum(const double * __restrict__ p, size_t stride, int n) {
+    double acc = 0.0;
+    for (int j0 = 0; j0 < n; j0 += 8) {
+        double t[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) t[k] = j0 + k < n ? __ldcg(p + (size_t)(j0 + k) * stride) : 0.0;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+            if (j0 + k < n) acc += t[k];
+    }
+    return acc;
+}
+
 template <int G>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(AT_PV_THREADS)
 k_att_pv(const AttParams a) {
     extern __shared__ __align__(16) uint8_t at_sm[];   // 2 x (V rows [AT_ST][256 B] + scores [G][AT_ST]), p [G][AT_ST]
     double * pd = reinterpret_cast<double *>(at_sm + 2 * at_pv_stage<G>());
     __shared__ float Ms[G];
+    __shared__ float redm[4][G];
     __shared__ double Ls[G];
     __shared__ int last_s;
     const int h = blockIdx.x, t = blockIdx.y, s = blockIdx.z, tid = threadIdx.x;
+    const int lane = tid & 31, warp = tid >> 5;
     const int p0 = a.pos_dev ? a.pos_dev[0] : a.pos0;
     const int n = p0 + t + 1;
     const int Su = at_splits_used(n, a.S);
@@ -296,38 +349,57 @@ k_att_pv(const AttParams a) {
     const float * sc = a.scores + ((size_t)h * a.T + t) * G * a.ncap;
     const size_t nchmax = (size_t)((a.ncap + AT_CHUNK - 1) / AT_CHUNK);
     double * part = a.part + ((size_t)h * a.T + t) * nchmax * G * 129;
-    alb_pdl_wait();   // the scores (and the new V cell) come from k_att_scores
-    if (tid < G) {
-        float m = -INFINITY;
-        for (int k = 0; k < Su; ++k) m = fmaxf(m, a.smax[(((size_t)h * a.T + t) * a.S + k) * G + tid]);
-        Ms[tid] = m;
-    }
     // staging steps: AT_ST cells each, two per chunk, double-buffered
     const int cbeg = j0 * AT_CHUNK, cend = min(n, j1 * AT_CHUNK);
     const int nsteps = (cend - cbeg + AT_ST - 1) / AT_ST;
-    auto issue = [&](int i) {
-        if (i < nsteps) {
-            const int cb = cbeg + i * AT_ST, rows = min(AT_ST, cend - cb);
-            uint8_t * dst = at_sm + (i & 1) * at_pv_stage<G>();
-            for (int p = tid; p < rows * 16; p += 128) {
-                const int r = p >> 4, j = p & 15;
-                at_cp16(dst + r * 256 + j * 16, vb + (size_t)(cb + r) * row + j * 8);
-            }
-            if (tid < rows) {
-                float * sdst = reinterpret_cast<float *>(dst + AT_ST * 256);
-#pragma unroll
-                for (int g = 0; g < G; ++g) at_cp4(sdst + g * AT_ST + tid, sc + (size_t)g * a.ncap + cb + tid);
-            }
+    // V rows of step i with cells in [lo, hi) and / or its scores
+    auto issue_v = [&](int i, int lo, int hi) {
+        const int cb = cbeg + i * AT_ST, rows = min(AT_ST, cend - cb);
+        uint8_t * dst = at_sm + (i & 1) * at_pv_stage<G>();
+        for (int p = tid; p < rows * 16; p += AT_PV_THREADS) {
+            const int r = p >> 4, j = p & 15;
+            if (cb + r >= lo && cb + r < hi) at_cp16(dst + r * 256 + j * 16, vb + (size_t)(cb + r) * row + j * 8);
         }
-        at_commit();
     };
-    issue(0);
+    auto issue_s = [&](int i) {
+        const int cb = cbeg + i * AT_ST, rows = min(AT_ST, cend - cb);
+        float * sdst = reinterpret_cast<float *>(at_sm + (i & 1) * at_pv_stage<G>() + AT_ST * 256);
+        for (int p = tid; p < rows * G; p += AT_PV_THREADS) {
+            const int g = p / rows, c = p - g * rows;
+            at_cp4(sdst + g * AT_ST + c, sc + (size_t)g * a.ncap + cb + c);
+        }
+    };
+    // The cached cells' V (all but the new cell n - 1, which the score kernel of
+    // a decode step stores) before waiting on the score kernel.
+    const int n_old = a.qkv ? n - 1 : 0;   // fused decode call: cells < n - 1 are stable
+    if (nsteps > 0) issue_v(0, 0, n_old);
+    at_commit();
+    alb_pdl_wait();   // the scores, maxima (and the new V cell) come from k_att_scores
+    if (nsteps > 0) {
+        issue_v(0, n_old, n);
+        issue_s(0);
+    }
+    at_commit();
+    {   // global maxima over the splits' maxima (max is exact: any order)
+        float m = -INFINITY;
+        if (tid < 128) {
+            const int g = tid % G;
+            const float * sm = a.smax + ((size_t)h * a.T + t) * a.S * G + g;
+            for (int k = tid / G; k < Su; k += 128 / G) m = fmaxf(m, sm[(size_t)k * G]);
+        }
+#pragma unroll
+        for (int o = G; o < 32; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (tid < 128 && lane < G) redm[warp][lane] = m;
+    }
+    __syncthreads();
+    if (tid < G) Ms[tid] = fmaxf(fmaxf(redm[0][tid], redm[1][tid]), fmaxf(redm[2][tid], redm[3][tid]));
     double O[G];
-    double Lc = 0.0;   // thread g < G: the chunk's sum of p for query head g
+    double Lc = 0.0;   // warp 4, lane g < G: the chunk's sum of p for query head g
 #pragma unroll
     for (int g = 0; g < G; ++g) O[g] = 0.0;
     for (int i = 0; i < nsteps; ++i) {
-        issue(i + 1);
+        if (i + 1 < nsteps) { issue_v(i + 1, 0, n); issue_s(i + 1); }
+        at_commit();
         at_wait<1>();
         __syncthreads();   // step i visible; Ms visible; pd free
         const uint8_t * stg = at_sm + (i & 1) * at_pv_stage<G>();
@@ -342,24 +414,30 @@ k_att_pv(const AttParams a) {
             }
         }
         __syncthreads();
-        if (tid < G) {   // the chunk's sum of p, cells in order
-            for (int c = 0; c < rows; ++c) Lc += pd[tid * AT_ST + c] * 0x1p-1008;
-        }
-        // O_g,d: cells in order; V bits enter as (v * 2^-1008) and p as (p * 2^1008),
-        // so fma(p', v', O) adds the exact product p * v
-        const uint16_t * vs = reinterpret_cast<const uint16_t *>(stg) + tid;
-        for (int c = 0; c < rows; ++c) {
-            const double vd = alb_h2d_bits(vs[c * 128]);
+        if (warp == 4) {
+            if (lane < G)   // the chunk's sum of p, cells in order
+                for (int c = 0; c < rows; ++c) Lc += pd[lane * AT_ST + c] * 0x1p-1008;
+        } else {
+            // O_g,d: cells in order; V bits enter as (v * 2^-1008) and p as
+            // (p * 2^1008), so fma(p', v', O) adds the exact product p * v
+            const uint16_t * vs = reinterpret_cast<const uint16_t *>(stg) + tid;
+            for (int c = 0; c < rows; ++c) {
+                const double vd = alb_h2d_bits(vs[c * 128]);
 #pragma unroll
-            for (int g = 0; g < G; ++g) O[g] = fma(pd[g * AT_ST + c], vd, O[g]);
+                for (int g = 0; g < G; ++g) O[g] = fma(pd[g * AT_ST + c], vd, O[g]);
+            }
         }
         // chunk complete (every second step, or the split's last): its partial
         const int j = (cb - j0 * AT_CHUNK) / AT_CHUNK + j0;
         if ((i & 1) == 1 || i == nsteps - 1) {
             double * pj = part + (size_t)j * G * 129;
+            if (warp < 4) {
 #pragma unroll
-            for (int g = 0; g < G; ++g) { pj[g * 129 + tid] = O[g]; O[g] = 0.0; }
-            if (tid < G) { pj[tid * 129 + 128] = Lc; Lc = 0.0; }
+                for (int g = 0; g < G; ++g) { pj[g * 129 + tid] = O[g]; O[g] = 0.0; }
+            } else if (lane < G) {
+                pj[lane * 129 + 128] = Lc;
+                Lc = 0.0;
+            }
         }
         __syncthreads();   // pd and buffer i & 1 consumed
     }
@@ -371,26 +449,39 @@ k_att_pv(const AttParams a) {
     __syncthreads();
     if (!last_s) { alb_pdl_trigger(); return; }
     __threadfence();
-    if (tid < G) {
-        double L = 0.0;
-        for (int j = 0; j < nch; ++j) L += __ldcg(part + (size_t)j * G * 129 + tid * 129 + 128);
-        Ls[tid] = L;
+    double Od[G];
+    if (warp == 4) {
+        if (lane < G) Ls[lane] = at_ordered_sum(part + lane * 129 + 128, (size_t)G * 129, nch);
+    } else {
+#pragma unroll
+        for (int g = 0; g < G; ++g) Od[g] = at_ordered_sum(part + g * 129 + tid, (size_t)G * 129, nch);
     }
     __syncthreads();
-    const int lane = tid & 31, warp = tid >> 5;
+    if (warp < 4) {
+        float v[G];
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-        double Od = 0.0;
-        for (int j = 0; j < nch; ++j) Od += __ldcg(part + (size_t)j * G * 129 + g * 129 + tid);
-        const float v = Ls[g] > 0.0 ? __double2float_rn(Od / Ls[g]) : 0.0f;
-        const int hq = h * G + g;
-        a.out[((size_t)t * a.Hq + hq) * 128 + tid] = v;
-        if (a.xq) {   // quantize_row_q8_0 of the output: warp w owns block (hq, w)
-            int8_t q; uint16_t dh;
-            q8_block_lane(v, q, dh);
-            uint8_t * blk = a.xq + (((size_t)t * a.Hq + hq) * 4 + warp) * 34;
-            if (lane == 0) *reinterpret_cast<uint16_t *>(blk) = dh;
-            blk[2 + lane] = (uint8_t)q;
+        for (int g = 0; g < G; ++g) {
+            v[g] = Ls[g] > 0.0 ? __double2float_rn(Od[g] / Ls[g]) : 0.0f;
+            a.out[((size_t)t * a.Hq + h * G + g) * 128 + tid] = v[g];
+        }
+        if (a.xq) {
+            // quantize_row_q8_0 of the output (arm.cpp:1834-1851): warp w owns
+            // block w of every head; the G reductions run interleaved
+            float amax[G];
+#pragma unroll
+            for (int g = 0; g < G; ++g) amax[g] = fabsf(v[g]);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+                for (int g = 0; g < G; ++g) amax[g] = fmaxf(amax[g], __shfl_xor_sync(0xffffffffu, amax[g], o));
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                const float d = amax[g] / 127.0f;
+                const float id = d != 0.0f ? 1.0f / d : 0.0f;
+                uint8_t * blk = a.xq + (((size_t)t * a.Hq + h * G + g) * 4 + warp) * 34;
+                if (lane == 0) *reinterpret_cast<uint16_t *>(blk) = alb_f2h(d);
+                blk[2 + lane] = (uint8_t)(int8_t)__float2int_rn(__fmul_rn(v[g], id));
+            }
         }
     }
     if (tid == 0) a.tickets[h * a.T + t] = 0;
@@ -405,7 +496,7 @@ static cudaError_t launch_att_t(const AttParams & p, bool pdl, cudaStream_t st) 
     const dim3 grid((unsigned)p.Hkv, (unsigned)p.T, (unsigned)p.S);
     e = alb_launch(k_att_scores<G, FUSED>, grid, dim3(128), AT_SCORES_SMEM, st, pdl, p);
     if (e != cudaSuccess) return e;
-    return alb_launch(k_att_pv<G>, grid, dim3(128), at_pv_smem<G>(), st, pdl, p);
+    return alb_launch(k_att_pv<G>, grid, dim3(AT_PV_THREADS), at_pv_smem<G>(), st, pdl, p);
 }
 
 template <bool FUSED>

@@ -82,8 +82,6 @@ struct alb_engine {
     float * part = nullptr, * part_all = nullptr;   // TP: this rank's O / down partial, all ranks' partials
     float * xn = nullptr;                           // prefill: RMS-normalized rows
     void * xq = nullptr;                            // decode: block_q8_0 input of the next mat-vec
-    uint8_t * hq = nullptr;                         // decode: block_q8_0 of the SwiGLU output (down's input)
-    int * hcnt = nullptr;                           // its per-block arrival counters (self re-arming)
     void * pg_ws = nullptr;                         // prefill: quantized activations of the mat-mul
     int32_t * tok_dev = nullptr, * pos_dev = nullptr, * next_dev = nullptr, * step_dev = nullptr, * gen_out = nullptr;
     int32_t gen_cap = 0;
@@ -139,7 +137,6 @@ static int engine_forward(alb_engine * e, int64_t T, bool pdl, int ncap_prefill 
         a.W = W; a.N = N; a.K = K;
         a.in_mode = in; a.x = x; a.norm_w = nw; a.eps = c.eps;
         a.out_mode = out; a.y = y; a.residual = res; a.pdl = pdl;
-        if (T == 1 && out == GEMV_OUT_SWIGLU) { a.yq = e->hq; a.ycnt = e->hcnt; }   // down's Q8_0 input
         ++launches;
         // decode: records already in x (attention merge, gate/up epilogue), or
         // RMSNorm + quantization in the mat-vec's prologue, which overlaps the
@@ -189,12 +186,12 @@ static int engine_forward(alb_engine * e, int64_t T, bool pdl, int ncap_prefill 
             ALB_TRY(engine_gather_add_x(e, T, pdl));
         }
         ALB_CUDA_TRY(gemv(L.gu, 2 * (int64_t)e->F, e->E, GEMV_IN_F32_RMS, e->x, L.fn, GEMV_OUT_SWIGLU, e->h, nullptr));
-        const int d_in = T == 1 ? GEMV_IN_Q8 : GEMV_IN_F32;   // decode: records from the gate/up epilogue
-        const void * d_x = T == 1 ? static_cast<const void *>(e->hq) : static_cast<const void *>(e->h);
+        // down: the SwiGLU output quantized in the mat-vec's prologue (decode)
+        // or by the mat-mul's quantizer (prefill)
         if (e->tp == 1) {
-            ALB_CUDA_TRY(gemv(L.down, e->E, e->F, d_in, d_x, nullptr, GEMV_OUT_PLAIN, e->x, e->x));
+            ALB_CUDA_TRY(gemv(L.down, e->E, e->F, GEMV_IN_F32, e->h, nullptr, GEMV_OUT_PLAIN, e->x, e->x));
         } else {
-            ALB_CUDA_TRY(gemv(L.down, e->E, e->F, d_in, d_x, nullptr, GEMV_OUT_PLAIN, e->part, nullptr));
+            ALB_CUDA_TRY(gemv(L.down, e->E, e->F, GEMV_IN_F32, e->h, nullptr, GEMV_OUT_PLAIN, e->part, nullptr));
             ALB_TRY(engine_gather_add_x(e, T, pdl));
             launches += 2;   // the two k_gather_add (the NCCL all-gathers are NCCL's kernels)
         }
@@ -268,19 +265,27 @@ static int engine_init_weights(alb_engine * e) {
     ALB_CUDA_TRY(gen_norm(e->out_norm, E, seed(-1, T_OUTPUT_NORM), e->table, st));
     e->layers.resize(c.n_layer);
     const int64_t cells = e->max_ctx;
+    // one buffer for every layer's mat-vec weights, in the decode step's order
+    // (QKV, O, gate/up, down of each layer: one sequential stream per token)
+    auto a256 = [](size_t b) { return (b + 255) & ~(size_t)255; };
+    const size_t b_qkv = a256(q4_gpu_bytes(e->Nqkv, E)), b_o = a256(q4_gpu_bytes(E, e->Dq));
+    const size_t b_gu = a256(q4_gpu_bytes(2 * (int64_t)e->F, E)), b_down = a256(q4_gpu_bytes(E, e->F));
+    const size_t b_layer = b_qkv + b_o + b_gu + b_down;
+    uint8_t * arena = nullptr;
+    ALB_TRY(e->alloc(&arena, b_layer * (size_t)c.n_layer));
     for (int l = 0; l < c.n_layer; ++l) {
         alb_engine::Layer & L = e->layers[l];
-        ALB_TRY(e->alloc(&L.qkv, q4_gpu_bytes(e->Nqkv, E)));
+        L.qkv = arena + (size_t)l * b_layer;
+        L.o = L.qkv + b_qkv;
+        L.gu = L.o + b_o;
+        L.down = L.gu + b_gu;
         ALB_CUDA_TRY(gen_q4(L.qkv, e->Nqkv, E, 0, 1, e->Dq, seed(l, T_WQ), (int64_t)e->rank * e->Dq, E, 0, e->table, st));
         ALB_CUDA_TRY(gen_q4(L.qkv, e->Nqkv, E, e->Dq, 1, e->Dkv, seed(l, T_WK), (int64_t)e->rank * e->Dkv, E, 0, e->table, st));
         ALB_CUDA_TRY(gen_q4(L.qkv, e->Nqkv, E, e->Dq + e->Dkv, 1, e->Dkv, seed(l, T_WV), (int64_t)e->rank * e->Dkv, E, 0,
                             e->table, st));
-        ALB_TRY(e->alloc(&L.o, q4_gpu_bytes(E, e->Dq)));
         ALB_CUDA_TRY(gen_q4(L.o, E, e->Dq, 0, 1, E, seed(l, T_WO), 0, Dq_full, (int64_t)e->rank * e->Dq, e->table, st));
-        ALB_TRY(e->alloc(&L.gu, q4_gpu_bytes(2 * (int64_t)e->F, E)));
         ALB_CUDA_TRY(gen_q4(L.gu, 2 * (int64_t)e->F, E, 0, 2, e->F, seed(l, T_GATE), (int64_t)e->rank * e->F, E, 0, e->table, st));
         ALB_CUDA_TRY(gen_q4(L.gu, 2 * (int64_t)e->F, E, 1, 2, e->F, seed(l, T_UP), (int64_t)e->rank * e->F, E, 0, e->table, st));
-        ALB_TRY(e->alloc(&L.down, q4_gpu_bytes(E, e->F)));
         ALB_CUDA_TRY(gen_q4(L.down, E, e->F, 0, 1, E, seed(l, T_DOWN), 0, c.n_ff, (int64_t)e->rank * e->F, e->table, st));
         ALB_TRY(e->alloc(&L.an, E));
         ALB_TRY(e->alloc(&L.fn, E));
@@ -317,9 +322,6 @@ static int engine_init_acts(alb_engine * e) {
         uint8_t * q8 = nullptr;
         ALB_TRY(e->alloc(&q8, (size_t)(kmax / 32) * 34));
         e->xq = q8;
-        ALB_TRY(e->alloc(&e->hq, (size_t)(e->F / 32) * 34));
-        ALB_TRY(e->alloc(&e->hcnt, (size_t)(e->F / 32)));
-        ALB_CUDA_TRY(cudaMemsetAsync(e->hcnt, 0, (size_t)(e->F / 32) * sizeof(int), e->st));
     }
     if (U > 1) {
         ALB_TRY(e->alloc(&e->xn, U * e->E));
@@ -690,7 +692,6 @@ extern "C" int alb_engine_time_gemv(alb_engine * e, int32_t reps, float * us_per
         a.W = W; a.N = N; a.K = K;
         a.in_mode = in; a.x = x; a.norm_w = nw; a.eps = e->c.eps;
         a.out_mode = out; a.y = y; a.residual = res; a.pdl = true;
-        if (out == GEMV_OUT_SWIGLU) { a.yq = e->hq; a.ycnt = e->hcnt; }
         list.push_back(a);
         const double in_bytes = in == GEMV_IN_Q8 ? K / 32 * 34.0 : in == GEMV_IN_F32 ? K * 4.0 : K * 8.0;
         bytes += (double)N * K * 18 / 32 + in_bytes + (out == GEMV_OUT_SWIGLU ? N / 2 : N) * 4.0;
@@ -700,7 +701,7 @@ extern "C" int alb_engine_time_gemv(alb_engine * e, int32_t reps, float * us_per
         add(L.qkv, e->Nqkv, e->E, GEMV_IN_F32_RMS, e->x, L.an, GEMV_OUT_PLAIN, e->qkv, nullptr);
         add(L.o, e->E, e->Dq, GEMV_IN_Q8, e->xq, nullptr, GEMV_OUT_PLAIN, e->qkv, nullptr);
         add(L.gu, 2 * (int64_t)e->F, e->E, GEMV_IN_F32_RMS, e->x, L.fn, GEMV_OUT_SWIGLU, e->h, nullptr);
-        add(L.down, e->E, e->F, GEMV_IN_Q8, e->hq, nullptr, GEMV_OUT_PLAIN, e->qkv, nullptr);
+        add(L.down, e->E, e->F, GEMV_IN_F32, e->h, nullptr, GEMV_OUT_PLAIN, e->qkv, nullptr);
     }
     add(e->lm_W, e->V, e->E, GEMV_IN_F32_RMS, e->x, e->out_norm, GEMV_OUT_PAIR, e->logits, nullptr);
     cudaGraph_t g = nullptr;

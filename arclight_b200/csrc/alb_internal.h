@@ -43,10 +43,6 @@ struct GemvArgs {
     int ctas = 0;                  // grid size (0 = one CTA per SM)
     int smem_budget = 0;           // bytes of dynamic shared memory (0 = default)
     int * err = nullptr;           // device error word (filled by launch_gemv)
-    // SwiGLU only, optional: block_q8_0 records of y [N/2/32] written by the
-    // warp that completes each 32-value block; ycnt [N/2/32] zeroed once
-    uint8_t * yq = nullptr;
-    int * ycnt = nullptr;
     // LOGITS only: running argmax key (ordered value << 32 | ~index; zeroed
     // before the launch), row index offset of this shard, and optionally the
     // token output: the last CTA (ticket, zero before the first launch, re-armed)

@@ -114,27 +114,38 @@ static constexpr int MV_NT = (MV_CW + MV_CH) * 32;     // threads of the prologu
 // distinct bank groups.
 template <bool PAIR> struct XRec { static constexpr int INTS = PAIR ? 20 : 12; };
 
+// quantize_row_q8_0 of one 32-value block by four consecutive threads (the
+// block's group of 4 lanes), thread t holding elements 8t..8t+7: amax over the
+// block, d = amax / 127, id = 1 / d (0 when d = 0), q = RNE(x * id), d stored
+// as fp16 (arm.cpp:1834-1851); writes the mat-vec record (words, d, sum, and
+// for the pair chain the four partial sums over {4l..4l+3} u {16+4l..16+4l+3}).
 template <bool PAIR>
-__device__ __forceinline__ void mv_store_rec(int * xs, int b, int lane, int8_t q, uint16_t dh) {
-    const int qi = (int)(uint8_t)q;
-    const int b1 = __shfl_down_sync(0xffffffffu, qi, 1);
-    const int b2 = __shfl_down_sync(0xffffffffu, qi, 2);
-    const int b3 = __shfl_down_sync(0xffffffffu, qi, 3);
-    int g4 = (int)q;   // sum over the lane's group of 4 (valid at lanes 4k)
-    g4 += __shfl_down_sync(0xffffffffu, g4, 1);
-    g4 += __shfl_down_sync(0xffffffffu, g4, 2);
-    int s = (int)q;
+__device__ __forceinline__ void mv_quant_rec(int * rec, const float (&v)[8], int t, bool on) {
+    float amax = 0.0f;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    const int hi16 = __shfl_down_sync(0xffffffffu, g4, 16);
-    int * rec = xs + b * XRec<PAIR>::INTS;
-    if ((lane & 3) == 0) rec[lane >> 2] = qi | (b1 << 8) | (b2 << 16) | (b3 << 24);
-    if (lane == 0) {
-        rec[8] = __float_as_int(alb_h2f(dh));
+    for (int k = 0; k < 8; ++k) amax = fmaxf(amax, fabsf(v[k]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    const float d = amax / 127.0f;
+    const float id = d != 0.0f ? 1.0f / d : 0.0f;
+    int q[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) q[k] = __float2int_rn(__fmul_rn(v[k], id));
+    const int w0 = (q[0] & 0xFF) | ((q[1] & 0xFF) << 8) | ((q[2] & 0xFF) << 16) | ((q[3] & 0xFF) << 24);
+    const int w1 = (q[4] & 0xFF) | ((q[5] & 0xFF) << 8) | ((q[6] & 0xFF) << 16) | ((q[7] & 0xFF) << 24);
+    const int s0 = q[0] + q[1] + q[2] + q[3], s1 = q[4] + q[5] + q[6] + q[7];
+    if (on) *reinterpret_cast<int2 *>(rec + 2 * t) = make_int2(w0, w1);
+    int s = s0 + s1;
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    if (on && t == 0) {
+        rec[8] = __float_as_int(alb_h2f(alb_f2h(d)));
         rec[9] = s;
     }
     if constexpr (PAIR) {
-        if ((lane & 3) == 0 && lane < 16) rec[10 + (lane >> 2)] = g4 + hi16;
+        // word w of the block is thread w/2's; partial l = word l + word 4 + l
+        const int o0 = __shfl_xor_sync(0xffffffffu, s0, 2), o1 = __shfl_xor_sync(0xffffffffu, s1, 2);
+        if (on && t < 2) *reinterpret_cast<int2 *>(rec + 10 + 2 * t) = make_int2(s0 + o0, s1 + o1);
     }
 }
 
@@ -226,12 +237,25 @@ __device__ __forceinline__ void mv_prologue(const GemvArgs & a, int * xs, int nb
             const float mean = (float)(t / (double)a.K);
             scale = 1.0f / sqrtf(__fadd_rn(mean, a.eps));
         }
-        for (int b = warp; b < nb; b += NW) {
-            float v = xf[b * 32 + lane];
-            if constexpr (IN == GEMV_IN_F32_RMS) v = __fmul_rn(__fmul_rn(v, scale), wf[b * 32 + lane]);
-            int8_t q; uint16_t dh;
-            q8_block_lane(v, q, dh);
-            mv_store_rec<PAIR>(xs, b, lane, q, dh);
+        // quantize_row_q8_0: four threads per block, eight values each (whole
+        // warps iterate: the block's four lanes exchange their maxima and sums)
+        for (int i0 = warp * 32; i0 < nb * 4; i0 += NT) {
+            const int i = i0 + lane, b = i >> 2, t = i & 3;
+            const bool on = i < nb * 4;
+            float v[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+            if (on) {
+                const float4 * x4 = reinterpret_cast<const float4 *>(xf + b * 32 + 8 * t);
+                const float4 u0 = x4[0], u1 = x4[1];
+                v[0] = u0.x; v[1] = u0.y; v[2] = u0.z; v[3] = u0.w; v[4] = u1.x; v[5] = u1.y; v[6] = u1.z; v[7] = u1.w;
+                if constexpr (IN == GEMV_IN_F32_RMS) {
+                    const float4 * w4 = reinterpret_cast<const float4 *>(wf + b * 32 + 8 * t);
+                    const float4 z0 = w4[0], z1 = w4[1];
+                    const float wv[8] = {z0.x, z0.y, z0.z, z0.w, z1.x, z1.y, z1.z, z1.w};
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) v[k] = __fmul_rn(__fmul_rn(v[k], scale), wv[k]);
+                }
+            }
+            mv_quant_rec<PAIR>(xs + b * XR, v, t, on);
         }
     }
     asm volatile("bar.sync 1, %0;" :: "n"(NT) : "memory");
@@ -252,31 +276,6 @@ __device__ __forceinline__ unsigned long long mv_key(float v, int64_t idx) {
     uint32_t u = __float_as_uint(v);
     u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
     return ((unsigned long long)u << 32) | (unsigned long long)(uint32_t)(0x7FFFFFFF - (int32_t)idx);
-}
-
-// SwiGLU outputs [i0, i1) written by this warp: per touched 32-value block,
-// count them on the block's arrival counter; the warp that completes a block
-// quantizes it (quantize_row_q8_0 of the fp32 values: the down projection's
-// input records) and re-arms the counter.  Whole warp; writers fenced before.
-__device__ __forceinline__ void mv_swiglu_q8(const GemvArgs & a, int64_t i0, int64_t i1, int lane) {
-    for (int64_t j = i0 >> 5; j <= (i1 - 1) >> 5; ++j) {
-        const int64_t lo = i0 > 32 * j ? i0 : 32 * j, hi = i1 < 32 * j + 32 ? i1 : 32 * j + 32;
-        const int cnt = (int)(hi - lo);
-        int last = 0;
-        if (lane == 0) last = atomicAdd(&a.ycnt[j], cnt) + cnt == 32;
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (!last) continue;
-        __threadfence();
-        const float v = __ldcg(a.y + j * 32 + lane);
-        int8_t q; uint16_t dh;
-        q8_block_lane(v, q, dh);
-        uint8_t * blk = a.yq + j * 34;
-        if (lane == 0) {
-            *reinterpret_cast<uint16_t *>(blk) = dh;
-            a.ycnt[j] = 0;
-        }
-        blk[2 + lane] = (uint8_t)q;
-    }
 }
 
 // Batch-1 Q4_0 x Q8_0 mat-vec with the reference's summation order.
@@ -502,12 +501,6 @@ k_mv(const GemvArgs a, const MvPlan p) {
                 // RC is even, so gate row r (even) and up row r + 1 share the warp
                 const float up = __shfl_down_sync(0xffffffffu, acc, 1);
                 if (mine && !(r & 1)) a.y[(r0 + r) >> 1] = alb_swiglu1(acc, up);
-                if (a.yq) {
-                    __threadfence();
-                    __syncwarp();
-                    const int ra = rb0 < rg ? rb0 : rg, rz = (rb0 + p.RC) < rg ? (rb0 + p.RC) : rg;
-                    if (rz > ra) mv_swiglu_q8(a, (r0 + ra) >> 1, (r0 + rz) >> 1, lane);
-                }
             } else {
                 if (mine && a.y) {
                     const int64_t n = r0 + r;
@@ -686,7 +679,6 @@ cudaError_t launch_gemv(const GemvArgs & a_in, cudaStream_t s) {
     if (reinterpret_cast<uintptr_t>(a.W) & 15) return cudaErrorInvalidValue;   // bulk-copy source alignment
     if (a.out_mode == GEMV_OUT_SWIGLU && a.N % 2 != 0) return cudaErrorInvalidValue;
     if (a.out_mode == GEMV_OUT_SWIGLU && !a.y) return cudaErrorInvalidValue;
-    if (a.yq && (a.out_mode != GEMV_OUT_SWIGLU || !a.ycnt || (a.N / 2) % 32 != 0)) return cudaErrorInvalidValue;
     if (a.out_mode == GEMV_OUT_LOGITS && (!a.key || (a.next && !a.ticket))) return cudaErrorInvalidValue;
     if (a.out_mode == GEMV_OUT_DOTS && !a.dots) return cudaErrorInvalidValue;
     switch (a.in_mode) {

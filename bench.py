@@ -42,6 +42,27 @@ def load_peaks():
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
 
 
+def host_cpu():
+    """Model name, logical CPUs and NUMA nodes of the host (for cpu_baseline)."""
+    model = None
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    try:
+        numa = len([d for d in os.listdir("/sys/devices/system/node") if d.startswith("node") and d[4:].isdigit()])
+    except OSError:
+        numa = None
+    return {"model": model, "logical_cpus": os.cpu_count(), "numa_nodes": numa}
+
+
+DTYPE_DECODE = ("q4_0 weights x q8_0 activations: int32 block dots in the reference's fp32 chains; "
+                "attention fp32 scores, fp64 softmax sums; fp16 KV")
+
+
 # ----------------------------------------------------------------- clocks
 class ClockSampler:
     """Samples nvidia-smi SM clocks and throttle reasons during the timed region."""
@@ -94,6 +115,9 @@ class ClockSampler:
 # ----------------------------------------------------------------- GEMV (config 1)
 GEMV_N, GEMV_K = 9728, 2560
 GEMV_BYTES = GEMV_N * (GEMV_K // 32) * 18 + (GEMV_K // 32) * 34 + GEMV_N * 4  # 14 049 952
+# DRAM bytes (read + write) of one config-1 launch from an ncu capture; None until captured
+GEMV_TRAFFIC = None
+GEMV_TRAFFIC_SRC = "ncu dram__bytes_read.sum + dram__bytes_write.sum of one k_mv launch (config 1)"
 
 
 def cpu_gemv_baseline(seconds: float = 12.0):
@@ -109,25 +133,13 @@ def cpu_gemv_baseline(seconds: float = 12.0):
         O.gemv(wq, xq, threads)
         n += 1
     dt = (time.perf_counter() - t0) / n
-    return {"value": GEMV_BYTES / dt / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+    return {"value": GEMV_BYTES / dt / 1e9, "unit": "GB/s", "cores": threads, "kind": "port", "cpu": host_cpu(),
             "sample": f"{n} mat-vecs of config 1 ({GEMV_N}x{GEMV_K}) in {seconds:.0f} s"}
 
 
-def run_gemv(args, rank, world):
+def gemv_graph(L, A, Ws, xqs, y, n_copies):
+    """One CUDA graph = one pass over the weight copies (n_copies launches, PDL edges)."""
     import torch
-    import arclight_b200 as A
-    from arclight_b200 import bench_util as BU
-
-    L = A.lib()
-    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
-    torch.cuda.set_device(dev)
-    A.check(L.alb_device_check(dev.index), "device check")
-    s = torch.cuda.current_stream()
-    n_copies = 24
-    Ws, xqs = BU.make_gemv_weights(n_copies, GEMV_N, GEMV_K, seed=1234)
-    y = torch.empty(GEMV_N, dtype=torch.float32, device=dev)
-
-    # one CUDA graph = one pass over the 24 weight copies (24 launches, PDL edges)
     g = torch.cuda.CUDAGraph()
     cap = torch.cuda.Stream()
     with torch.cuda.stream(cap):
@@ -139,6 +151,56 @@ def run_gemv(args, rank, world):
             for i in range(n_copies):
                 A.check(L.alb_gemv_q4_0_q8_0(Ws[i].data_ptr(), xqs.data_ptr(), y.data_ptr(), GEMV_N, GEMV_K,
                                              None, cap.cuda_stream))
+    return g
+
+
+def gemv_config1_record(reps: int = 40):
+    """Config 1 (one Q4_0 x Q8_0 mat-vec, W 9728 x 2560) timed on this GPU: 24
+    rotating weight copies (336 MB > L2) replayed from one CUDA graph; mean
+    CUDA-event time per launch and algorithmic GB/s."""
+    import torch
+    import arclight_b200 as A
+    from arclight_b200 import bench_util as BU
+    L = A.lib()
+    n_copies = 24
+    Ws, xqs = BU.make_gemv_weights(n_copies, GEMV_N, GEMV_K, seed=1234)
+    y = torch.empty(GEMV_N, dtype=torch.float32, device="cuda")
+    g = gemv_graph(L, A, Ws, xqs, y, n_copies)
+    s = torch.cuda.current_stream()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(reps):
+        g.replay()
+    e1.record(s)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * n_copies)
+    peaks = load_peaks()
+    gbs = GEMV_BYTES / (us * 1e-6) / 1e9
+    del Ws, g
+    torch.cuda.empty_cache()
+    return {"workload": "config1_gemv", "kernel": "k_mv (Q4_0 x Q8_0 mat-vec, W 9728x2560)", "us_per_launch": us,
+            "algorithmic_bytes_per_launch": GEMV_BYTES, "achieved_gbs": gbs, "peak_gbs": peaks["hbm_gbs"],
+            "frac": gbs / peaks["hbm_gbs"], "launches": reps * n_copies,
+            "l2": "24 rotating weight copies (336 MB > 126 MB L2)"}
+
+
+def run_gemv(args, rank, world):
+    import torch
+    import arclight_b200 as A
+    from arclight_b200 import bench_util as BU
+    L = A.lib()
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    A.check(L.alb_device_check(dev.index), "device check")
+    s = torch.cuda.current_stream()
+    n_copies = 24
+    Ws, xqs = BU.make_gemv_weights(n_copies, GEMV_N, GEMV_K, seed=1234)
+    y = torch.empty(GEMV_N, dtype=torch.float32, device=dev)
+
+    g = gemv_graph(L, A, Ws, xqs, y, n_copies)
     reps = max(1, args.steps // n_copies)
     steps = reps * n_copies
     with ClockSampler(dev.index) as clk:
@@ -191,12 +253,14 @@ def run_gemv(args, rank, world):
         "metric": "Q4_0xQ8_0 GEMV HBM GB/s (config 1, W 9728x2560)",
         "value": achieved * world, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "q4_0 x q8_0 -> int32 dots, fp32 accumulate", "data": "synthetic",
+        "vs_baseline": None, "dtype": "q4_0 x q8_0 -> int32 block dots, the reference's fp32 block chain",
+        "data": "synthetic",
         "config": {"workload": "config1_gemv", "N": GEMV_N, "K": GEMV_K, "weight_copies": n_copies,
                    "l2": "inputs larger than L2: 24 rotating weight copies (336 MB)"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": achieved / peaks["hbm_gbs"], "traffic": None,
-                     "peak_src": peaks["src"], "algorithmic_bytes_per_launch": GEMV_BYTES},
+                     "frac": achieved / peaks["hbm_gbs"], "traffic": GEMV_TRAFFIC, "traffic_src": GEMV_TRAFFIC_SRC,
+                     "peak_src": peaks["src"], "kernel": "k_mv", "algorithmic_bytes_per_launch": GEMV_BYTES,
+                     "avg_launch_us": launch_us},
         "e2e": {"value": GEMV_BYTES / (e2e_ms * 1e-3) / 1e9 * world, "unit": "GB/s",
                 "h2d_bytes_per_step": GEMV_K * 4, "d2h_bytes_per_step": GEMV_N * 4},
         "gpu_launches": args.steps,
@@ -219,25 +283,31 @@ def decode_bytes_per_token(cfg, pos_mean):
     return L * per_layer + lm + norms + kv
 
 
-def cpu_decode_baseline(cfg, seconds=20.0):
+DECODE_PROMPT = 512
+
+
+def cpu_decode_baseline(cfg, seconds=20.0, pos0=DECODE_PROMPT):
     """The oracle (reference semantics, all host threads) decoding the same model
-    from an empty cache: a bounded sample of tokens."""
+    at the GPU bench's positions: its KV cache holds pos0 cells (seeded N(0,1)
+    fp16, standing in for the prompt's K/V: the same work per token) and a
+    bounded sample of greedy steps runs from position pos0."""
     from oracle import lib as O
     threads = os.cpu_count() or 1
     t0 = time.perf_counter()
-    m = O.Model(cfg, 1234, 64, threads)
+    m = O.Model(cfg, 1234, pos0 + 64, threads)
+    m.fill_kv(pos0, 99)
     build_s = time.perf_counter() - t0
     n, tok, t0 = 0, 1, time.perf_counter()
     while n < 3 or (time.perf_counter() - t0 < seconds and n < 60):
-        lg, _ = m.forward([tok], n, 0)
+        lg, _ = m.forward([tok], pos0 + n, 0)
         tok = O.argmax(lg)
         n += 1
     dt = (time.perf_counter() - t0) / n
     m.close()
-    return {"value": 1.0 / dt, "unit": "tok/s", "cores": threads, "kind": "port",
-            "sample": f"{n} greedy decode steps of the same model at positions 0..{n - 1} "
-                      f"(oracle/oracle.c, {threads} threads; weights generated in {build_s:.0f} s); "
-                      f"decode is weight-bound, the 4B KV traffic at the bench positions is 4% of the bytes"}
+    return {"value": 1.0 / dt, "unit": "tok/s", "cores": threads, "kind": "port", "cpu": host_cpu(),
+            "sample": f"{n} greedy decode steps of the same model at positions {pos0}..{pos0 + n - 1} over a "
+                      f"cache pre-filled to {pos0} cells (oracle/oracle.c, {threads} threads; weights and cache "
+                      f"generated in {build_s:.0f} s)"}
 
 
 def cpu_long_baseline(cfg, ctx, seconds=20.0):
@@ -257,7 +327,7 @@ def cpu_long_baseline(cfg, ctx, seconds=20.0):
         n += 1
     dt = (time.perf_counter() - t0) / n
     m.close()
-    return {"value": 1.0 / dt, "unit": "tok/s", "cores": threads, "kind": "port",
+    return {"value": 1.0 / dt, "unit": "tok/s", "cores": threads, "kind": "port", "cpu": host_cpu(),
             "sample": f"{n} greedy decode step(s) of the same 8B model at positions {ctx}..{ctx + n - 1} over a "
                       f"cache pre-filled to {ctx} cells (oracle/oracle.c, {threads} threads; model and cache "
                       f"generated in {setup_s:.0f} s)"}
@@ -274,9 +344,15 @@ def cpu_prefill_baseline(cfg, n_tokens=48):
     m.forward(prompt, 0)
     dt = time.perf_counter() - t0
     m.close()
-    return {"value": n_tokens / dt, "unit": "tok/s", "cores": threads, "kind": "port",
+    return {"value": n_tokens / dt, "unit": "tok/s", "cores": threads, "kind": "port", "cpu": host_cpu(),
             "sample": f"one {n_tokens}-token prompt prefilled from an empty cache (oracle/oracle.c, {threads} threads; "
                       f"its mat-muls run row by row, as the reference's gemv path)"}
+
+
+# DRAM bytes (read + write) per mat-vec launch of the decode step, mean over the
+# step's launches, from an ncu capture; None until captured
+DECODE_MV_TRAFFIC = None
+DECODE_MV_TRAFFIC_SRC = "ncu dram__bytes_read.sum + dram__bytes_write.sum, mean over one decode step's k_mv launches"
 
 
 def run_decode(args, rank, world):
@@ -297,7 +373,7 @@ def run_decode(args, rank, world):
         obj = [nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(obj, src=0)
         nid = obj[0]
-    n_prompt, n_gen = 512, args.steps
+    n_prompt, n_gen = DECODE_PROMPT, args.steps
     max_ctx = n_prompt + max(n_gen, args.warmup) + 16
     e = Engine(cfg, 1234, max_ctx, 256, rank, world, nid, local)
     prompt = np.random.default_rng(1234).integers(0, cfg["n_vocab"], n_prompt).astype(np.int32)
@@ -336,23 +412,18 @@ def run_decode(args, rank, world):
     pos_mean = n_prompt + (n_gen - 1) / 2.0
     bpt = decode_bytes_per_token(cfg, pos_mean)
     step_gbs = bpt * tok_s / 1e9
-    if info["launches_per_step"] == 1:
-        # the persistent step kernel is the only launch of a step: its CUDA-event
-        # duration is ms_per_step (the graph replays one kernel per token)
-        roofline = {"bound": "hbm", "achieved": step_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                    "frac": step_gbs / peaks["hbm_gbs"], "traffic": None, "peak_src": peaks["src"],
-                    "kernel": "k_decode_step (persistent decode step: every mat-vec, attention, norms, lm head)",
-                    "algorithmic_bytes_per_launch": bpt, "avg_launch_us": ms * 1000.0}
-    else:
-        roofline = {"bound": "hbm", "achieved": gemv["gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                    "frac": gemv["gbs"] / peaks["hbm_gbs"], "traffic": None, "peak_src": peaks["src"],
-                    "kernel": "q4_0 x q8_0 mat-vec (all decode-step launches)",
-                    "algorithmic_bytes_per_launch": gemv["bytes_per_launch"], "avg_launch_us": gemv["us_per_launch"]}
+    # dominant kernel: the Q4_0 mat-vec (k_mv), every launch of the step (QKV,
+    # O, gate/up, down of each layer, lm head) with the step's input modes
+    roofline = {"bound": "hbm", "achieved": gemv["gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": gemv["gbs"] / peaks["hbm_gbs"], "traffic": DECODE_MV_TRAFFIC,
+                "traffic_src": DECODE_MV_TRAFFIC_SRC, "peak_src": peaks["src"],
+                "kernel": "k_mv: q4_0 x q8_0 mat-vec (all decode-step launches, replayed from a CUDA graph)",
+                "algorithmic_bytes_per_launch": gemv["bytes_per_launch"], "avg_launch_us": gemv["us_per_launch"]}
     out = {
         "metric": "Qwen3-4B Q4_0 decode tok/s bs=1",
         "value": tok_s, "unit": "tok/s", "n_gpus": world, "steps": n_gen, "warmup": max(args.warmup, 3),
         "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": "q4_0 weights x q8_0 activations (int32 block dots), fp32/fp64 accumulate, fp16 KV",
+        "dtype": DTYPE_DECODE,
         "data": "synthetic: seeded random-init Qwen3-4B-shaped weights (device-generated), uniform random prompt",
         "config": {"workload": "config3_decode_qwen3_4b", "prompt": n_prompt, "decode_steps": n_gen,
                    "parallelism": f"tp{world}", "global_batch": 1,
@@ -370,6 +441,8 @@ def run_decode(args, rank, world):
         "clocks": clk.summary(),
     }
     e.close()
+    if world == 1:
+        out["config1_gemv"] = gemv_config1_record()
     return out
 
 
@@ -380,9 +453,8 @@ LONG_CTX = 32768
 # ----------------------------------------------------------------- attention alone (config 5 shape)
 ATT_HQ, ATT_HKV, ATT_CELLS, ATT_COPIES = 32, 8, 32768, 4
 ATT_BYTES = 2 * ATT_CELLS * ATT_HKV * 128 * 2 + 2 * ATT_HQ * 128 * 4   # K + V + q + out per call
-# DRAM bytes per call from one ncu capture of the three kernels (scores 68.21 MB,
-# PV 72.78 MB, merge 2.46 MB; caches flushed between kernels by ncu)
-ATT_TRAFFIC = 143.45e6
+# DRAM bytes (read + write) per call from an ncu capture of its two kernels; None until captured
+ATT_TRAFFIC = None
 
 
 def cpu_attn_baseline(seconds: float = 10.0):
@@ -398,7 +470,7 @@ def cpu_attn_baseline(seconds: float = 10.0):
         O.flash_attn(q, k, v, kv_len, 1.0 / np.sqrt(128.0), 0)
         n += 1
     dt = (time.perf_counter() - t0) / n
-    return {"value": ATT_BYTES / dt / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
+    return {"value": ATT_BYTES / dt / 1e9, "unit": "GB/s", "cores": 1, "kind": "port", "cpu": host_cpu(),
             "sample": f"{n} attention calls ({ATT_HQ}/{ATT_HKV} heads over {ATT_CELLS} cells) in {seconds:.0f} s"}
 
 
@@ -483,17 +555,18 @@ def run_attn(args, rank, world):
         "metric": "split-K flash decode GB/s (config 5 attention: 32/8 heads, 32768 fp16 cells)",
         "value": achieved * world, "unit": "GB/s", "n_gpus": world, "steps": steps, "warmup": max(args.warmup, 3),
         "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "fp16 KV, fp32 scores (sequential fma), fp64 softmax sums", "data": "synthetic: N(0,1) q/K/V",
+        "dtype": "fp16 KV, fp32 scores (sequential fma), fp64 softmax sums in chunk order",
+        "data": "synthetic: N(0,1) q/K/V",
         "config": {"workload": "config5_attention", "n_head": ATT_HQ, "n_head_kv": ATT_HKV, "cells": ATT_CELLS,
                    "splits": S, "kv_copies": ATT_COPIES, "l2": "inputs larger than L2: 4 rotating caches (512 MB)"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / peaks["hbm_gbs"], "traffic": ATT_TRAFFIC, "peak_src": peaks["src"],
-                     "traffic_src": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the three kernels of one call",
-                     "kernel": "k_fa_scores + k_fa_pv + k_fa_merge (one call)",
+                     "traffic_src": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the two kernels of one call",
+                     "kernel": "k_att_scores + k_att_pv (one call)",
                      "algorithmic_bytes_per_launch": ATT_BYTES},
         "e2e": {"value": ATT_BYTES / (e2e_ms * 1e-3) / 1e9 * world, "unit": "GB/s",
                 "h2d_bytes_per_step": ATT_HQ * 128 * 4, "d2h_bytes_per_step": ATT_HQ * 128 * 4},
-        "gpu_launches": 3 * steps,
+        "gpu_launches": 2 * steps,
         "clocks": clk.summary(),
     }
 
@@ -555,7 +628,7 @@ def run_long(args, rank, world):
         "metric": "Qwen3-8B Q4_0 decode tok/s bs=1 at 32768-token context",
         "value": 1000.0 / ms, "unit": "tok/s", "n_gpus": world, "steps": n_gen, "warmup": max(args.warmup, 3),
         "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": "q4_0 weights x q8_0 activations (int32 block dots), fp32/fp64 accumulate, fp16 KV",
+        "dtype": DTYPE_DECODE,
         "data": "synthetic: seeded random-init Qwen3-8B-shaped weights; KV cache filled with seeded N(0,1) fp16",
         "config": {"workload": "config5_long_qwen3_8b", "context": LONG_CTX, "decode_steps": n_gen,
                    "parallelism": f"tp{world}", "global_batch": 1,
@@ -633,7 +706,7 @@ def run_prefill(args, rank, world):
         "metric": "Qwen3-4B Q4_0 prefill tok/s (2048-token prompt, 1/TTFT)",
         "value": T * 1000.0 / ms, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms, "ttft_ms": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": "q4_0 x q8_0 int8 tensor cores (tcgen05 kind::i8), exact fp64 block sums, fp16 KV",
+        "dtype": "q4_0 x q8_0 int8 tensor cores (tcgen05 kind::i8), the reference's fp32 block chain, fp16 KV",
         "data": "synthetic: seeded random-init Qwen3-4B-shaped weights, uniform random prompt",
         "config": {"workload": "config4_prefill_qwen3_4b", "prompt": T, "parallelism": f"tp{world}",
                    "global_batch": 1, "l2": "inputs larger than L2 (2.26 GB of weights per prefill)",
