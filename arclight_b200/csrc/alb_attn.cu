@@ -81,6 +81,7 @@ struct AttParams {
     double * part = nullptr;          // [Hkv][T][nchunks(ncap)][G][129]
     float * out = nullptr;            // [T][Hq][128]
     uint8_t * xq = nullptr;           // optional block_q8_0 records of out [T][Hq * 4]
+    int * err = nullptr;              // device error word (bounded waits of the cluster kernel)
 };
 
 struct AtLayout { size_t tickets_off, smax_off, scores_off, part_off, bytes; };
@@ -103,7 +104,13 @@ static AtLayout at_layout(int Hq, int Hkv, int T, int S, int ncap) {
 // divided by 128: a parallel double sum stands in for it where the rounded
 // float mean is certainly the same, one thread re-sums it sequentially where
 // not.  Heads k < nq use wq, the others wk.  Returns the roped values in v.
-template <int NH>
+// SUB: called by threads 0..127 of a larger CTA (named barrier 1 of 128
+// threads instead of __syncthreads).
+__device__ __forceinline__ void at_sync128(bool sub) {
+    if (sub) asm volatile("bar.sync 1, 128;" ::: "memory");
+    else __syncthreads();
+}
+template <int NH, bool SUB = false>
 __device__ __forceinline__ void at_norm_rope_heads(float (&v)[NH], int nh, int nq, const float * __restrict__ wq,
                                                    const float * __restrict__ wk, float eps, float2 cs,
                                                    float (*hb)[128], double (*hred)[NH], double * hseq) {
@@ -121,7 +128,7 @@ __device__ __forceinline__ void at_norm_rope_heads(float (&v)[NH], int nh, int n
     if (lane == 0)
 #pragma unroll
         for (int k = 0; k < NH; ++k) hred[warp][k] = part[k];
-    __syncthreads();
+    at_sync128(SUB);
     double tot[NH];
     bool sure[NH];
 #pragma unroll
@@ -135,7 +142,7 @@ __device__ __forceinline__ void at_norm_rope_heads(float (&v)[NH], int nh, int n
         for (int k = 0; k < NH; ++k) if (k == d) mine_sure = sure[k];
         if (!mine_sure) hseq[d] = alb_rms_seq_sum(hb[d], 128);
     }
-    __syncthreads();   // hseq ready; hb is rewritten below
+    at_sync128(SUB);   // hseq ready; hb is rewritten below
 #pragma unroll
     for (int k = 0; k < NH; ++k) {
         if (k >= nh) continue;
@@ -144,7 +151,7 @@ __device__ __forceinline__ void at_norm_rope_heads(float (&v)[NH], int nh, int n
         const float scale = 1.0f / sqrtf(__fadd_rn(mean, eps));
         hb[k][d] = __fmul_rn(__fmul_rn(v[k], scale), (k < nq ? wq : wk)[d]);
     }
-    __syncthreads();
+    at_sync128(SUB);
 #pragma unroll
     for (int k = 0; k < NH; ++k) {
         if (k >= nh) continue;
@@ -488,6 +495,323 @@ k_att_pv(const AttParams a) {
     alb_pdl_trigger();
 }
 
+// ------------------------------------------- decode: one cluster per KV head
+// The decode step's attention of one token in ONE launch: a thread-block
+// cluster of CL_CS CTAs per KV head, CTA r taking the contiguous chunks
+// [nch r / CL_CS, nch (r + 1) / CL_CS) of the n = pos + 1 cells.  Same
+// arithmetic and summation order as k_att_scores + k_att_pv (so the same
+// results bit for bit):
+//   1. QK-norm + RoPE of the G query heads (and, in the CTA holding cell
+//      n - 1, of the new K, stored with the new V into the caches);
+//   2. scores of the CTA's cells into shared memory, per-head maxima;
+//   3. cluster barrier; the global maxima read from every CTA's shared memory
+//      (DSMEM), so no workspace round trip and no second launch;
+//   4. p, and per 128-cell chunk the ordered double sums of p and p * v, to
+//      the workspace;
+//   5. cluster barrier; each CTA merges whole 32-dimension output blocks
+//      (chunk partials in chunk order), writes them and their Q8_0 records.
+// K and V stages of cached cells are streamed before the dependency wait.
+// Every wait on a stage is bounded (error word set, results then invalid);
+// every CTA takes both cluster barriers.  Cells per CTA <= CL_MAXC.
+static constexpr int CL_CS = 8;                          // CTAs per cluster (portable size)
+static constexpr int CL_ST = 64;                         // cells per stage
+static constexpr int CL_KR = 2, CL_VR = 2;               // K / V ring stages
+static constexpr int CL_MAXC = 1024;                     // cells per CTA (scores kept in shared memory)
+static constexpr int CL_THREADS = 288;                   // warps 0-7: scores / P.V; warp 8: the sums of p
+
+template <int G>
+__host__ __device__ constexpr size_t cl_smem() {
+    return (size_t)CL_KR * CL_ST * AT_KPITCH + (size_t)CL_VR * CL_ST * 256 + (size_t)G * CL_MAXC * 4 +
+           (size_t)G * CL_ST * 8 + 8 * (CL_KR + CL_VR);
+}
+
+__device__ __forceinline__ void cl_cp_arrive(uint64_t * bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" :: "r"(alb_smem_addr(bar)) : "memory");
+}
+__device__ __forceinline__ void cl_barrier() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float cl_ld_remote(const float * local, int rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(alb_smem_addr(local)), "r"(rank));
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+    return v;
+}
+
+template <int G>
+__global__ void __launch_bounds__(CL_THREADS, 1)
+k_att_decode_cl(const AttParams a) {
+    constexpr int GPT = G >= 4 ? G / 4 : 1;            // heads per thread in the score phase
+    constexpr int GQ = G >= 4 ? 4 : G;                 // head groups of 64 threads there
+    constexpr int HPT = G >= 2 ? G / 2 : 1;            // heads per thread in the P.V phase
+    extern __shared__ __align__(16) uint8_t cl_sm[];
+    uint8_t * kring = cl_sm;                                                     // [CL_KR][CL_ST][AT_KPITCH]
+    uint8_t * vring = kring + (size_t)CL_KR * CL_ST * AT_KPITCH;                 // [CL_VR][CL_ST][256]
+    float * sc = reinterpret_cast<float *>(vring + (size_t)CL_VR * CL_ST * 256); // [G][CL_MAXC]
+    double * pd = reinterpret_cast<double *>(sc + (size_t)G * CL_MAXC);          // [G][CL_ST]
+    uint64_t * kfull = reinterpret_cast<uint64_t *>(pd + (size_t)G * CL_ST);
+    uint64_t * vfull = kfull + CL_KR;
+    __shared__ __align__(16) float qs[G][128];
+    __shared__ __align__(16) float knew[128];
+    __shared__ __align__(16) uint16_t vnew[128];
+    __shared__ float hb[G + 1][128];
+    __shared__ double hred[4][G + 1];
+    __shared__ double hseq[G + 1];
+    __shared__ float cmax[G];
+    __shared__ float redm[8][GPT];
+    __shared__ float Ms[G];
+    __shared__ int s_bad;
+    const int r = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int p0 = a.pos_dev ? a.pos_dev[0] : a.pos0;    // written before this graph replay started
+    const int n = p0 + 1;
+    const int nch = at_nchunks(n);
+    const int j0 = (int)((int64_t)nch * r / CL_CS), j1 = (int)((int64_t)nch * (r + 1) / CL_CS);
+    const int c0 = j0 * AT_CHUNK, c1 = min(n, j1 * AT_CHUNK);
+    const int ncell = c1 > c0 ? c1 - c0 : 0;
+    const bool fits = ncell <= CL_MAXC;
+    const int nst = fits ? (ncell + CL_ST - 1) / CL_ST : 0;
+    const bool holder = ncell > 0 && c1 == n;            // this CTA holds the new cell n - 1
+    const int64_t row = (int64_t)a.Hkv * 128;
+    const uint16_t * kb = a.kc + (size_t)h * 128;
+    const uint16_t * vb = a.vc + (size_t)h * 128;
+    if (tid == 0) {
+        for (int i = 0; i < CL_KR; ++i) alb_mbar_init(&kfull[i], CL_THREADS);
+        for (int i = 0; i < CL_VR; ++i) alb_mbar_init(&vfull[i], CL_THREADS);
+        s_bad = fits ? 0 : 1;
+        alb_mbar_fence_init();
+    }
+    __syncthreads();
+    // stage i of K (V): the cached rows by cp.async, completion counted on the
+    // stage's mbarrier (one noinc arrival per thread); the new cell's row is
+    // never copied (K: knew is used; V: vnew is written into the ring)
+    auto issue = [&](bool is_v, int i, bool vnew_ready) {
+        if (i >= nst) return;
+        const int cb = c0 + i * CL_ST, rows = min(CL_ST, c1 - cb);
+        uint8_t * dst = is_v ? vring + (size_t)(i % CL_VR) * CL_ST * 256
+                             : kring + (size_t)(i % CL_KR) * CL_ST * AT_KPITCH;
+        const int pitch = is_v ? 256 : AT_KPITCH;
+        const uint16_t * src = is_v ? vb : kb;
+        for (int p = tid; p < rows * 16; p += CL_THREADS) {
+            const int rr = p >> 4, j = p & 15;
+            if (cb + rr < n - 1) at_cp16(dst + rr * pitch + j * 16, src + (size_t)(cb + rr) * row + j * 8);
+            else if (is_v && vnew_ready)
+                *reinterpret_cast<uint4 *>(dst + rr * pitch + j * 16) = reinterpret_cast<const uint4 *>(vnew)[j];
+        }
+        cl_cp_arrive(is_v ? &vfull[i % CL_VR] : &kfull[i % CL_KR]);
+    };
+    for (int i = 0; i < CL_KR; ++i) issue(false, i, false);
+    for (int i = 0; i < CL_VR; ++i) issue(true, i, false);
+    // the norm weights and the RoPE row do not depend on the previous kernel
+    const float2 cs = a.rope[(size_t)(n - 1) * 64 + (tid & 63)];
+    alb_pdl_wait();
+
+    // 1. QK-norm + RoPE (threads 0..127)
+    if (tid < 128) {
+        float v[G + 1];
+#pragma unroll
+        for (int g = 0; g < G; ++g) v[g] = a.qkv[(size_t)(h * G + g) * 128 + tid];
+        v[G] = holder ? a.qkv[(size_t)(a.Hq + h) * 128 + tid] : 0.0f;
+        const float vraw = holder ? a.qkv[(size_t)(a.Hq + a.Hkv + h) * 128 + tid] : 0.0f;
+        at_norm_rope_heads<G + 1, true>(v, holder ? G + 1 : G, G, a.qn, a.kn, a.eps, cs, hb, hred, hseq);
+#pragma unroll
+        for (int g = 0; g < G; ++g) qs[g][tid] = __half2float(__float2half_rn(v[g]));   // Q -> fp16 (arm.cpp:2307)
+        if (holder) {
+            const uint16_t kh = alb_f2h(v[G]), vh = alb_f2h(vraw);
+            knew[tid] = __half2float(__ushort_as_half(kh));
+            vnew[tid] = vh;
+            a.kcw[(size_t)(n - 1) * row + (size_t)h * 128 + tid] = kh;
+            a.vcw[(size_t)(n - 1) * row + (size_t)h * 128 + tid] = vh;
+        }
+    }
+    __syncthreads();   // qs, knew, vnew visible
+    if (holder) {      // the new cell's V row, when its stage was issued above
+        const int i = (n - 1 - c0) / CL_ST;
+        if (i < CL_VR && tid < 16) {
+            uint8_t * dst = vring + (size_t)(i % CL_VR) * CL_ST * 256 + (size_t)(n - 1 - c0 - i * CL_ST) * 256;
+            reinterpret_cast<uint4 *>(dst)[tid] = reinterpret_cast<const uint4 *>(vnew)[tid];
+        }
+    }
+
+    // 2. scores of the CTA's cells (thread: cell tid % 64 of the stage, heads
+    //    GPT * (tid / 64) ..), the sequential fp32 chain over d
+    const int cl = tid & (CL_ST - 1), gq = tid >> 6;
+    const bool sthr = tid < 64 * GQ;
+    float mx[GPT];
+#pragma unroll
+    for (int k = 0; k < GPT; ++k) mx[k] = -INFINITY;
+    for (int i = 0; i < nst; ++i) {
+        if (!alb_mbar_wait(&kfull[i % CL_KR], (uint32_t)((i / CL_KR) & 1))) {
+            if (tid == 0) atomicExch(a.err, ALB_DEVERR_MBAR_TIMEOUT);
+            s_bad = 1;
+        }
+        const int c = c0 + i * CL_ST + cl;
+        if (sthr && c < c1) {
+            const uint8_t * kr = kring + (size_t)(i % CL_KR) * CL_ST * AT_KPITCH + cl * AT_KPITCH;
+            float acc[GPT];
+#pragma unroll
+            for (int k = 0; k < GPT; ++k) acc[k] = 0.0f;
+#pragma unroll 4
+            for (int j = 0; j < 16; ++j) {   // dims 8j .. 8j+7, in order (the reference's sequential chain)
+                float kf[8];
+                if (c == n - 1) {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) kf[e] = knew[8 * j + e];
+                } else {
+                    const uint4 kv = *reinterpret_cast<const uint4 *>(kr + j * 16);
+                    const uint32_t wd[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&wd[e]));
+                        kf[2 * e] = f.x;
+                        kf[2 * e + 1] = f.y;
+                    }
+                }
+#pragma unroll
+                for (int k = 0; k < GPT; ++k) {
+                    const float * qg = qs[gq * GPT + k];
+                    const float4 qa = *reinterpret_cast<const float4 *>(qg + 8 * j);
+                    const float4 qb = *reinterpret_cast<const float4 *>(qg + 8 * j + 4);
+                    acc[k] = __fmaf_rn(kf[0], qa.x, acc[k]);
+                    acc[k] = __fmaf_rn(kf[1], qa.y, acc[k]);
+                    acc[k] = __fmaf_rn(kf[2], qa.z, acc[k]);
+                    acc[k] = __fmaf_rn(kf[3], qa.w, acc[k]);
+                    acc[k] = __fmaf_rn(kf[4], qb.x, acc[k]);
+                    acc[k] = __fmaf_rn(kf[5], qb.y, acc[k]);
+                    acc[k] = __fmaf_rn(kf[6], qb.z, acc[k]);
+                    acc[k] = __fmaf_rn(kf[7], qb.w, acc[k]);
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < GPT; ++k) {
+                const float v = __fmul_rn(acc[k], a.scale);
+                sc[(size_t)(gq * GPT + k) * CL_MAXC + (c - c0)] = v;
+                mx[k] = fmaxf(mx[k], v);
+            }
+        }
+        __syncthreads();   // K stage consumed by every thread
+        issue(false, i + CL_KR, true);
+    }
+    // per-head maxima of this CTA: the 64 cells of a head group are warps 2gq, 2gq+1
+#pragma unroll
+    for (int k = 0; k < GPT; ++k) {
+        const float m = alb_warp_max(mx[k]);
+        if (lane == 0 && warp < 8) redm[warp][k] = m;
+    }
+    __syncthreads();
+    if (tid < G) {
+        const int q = tid / GPT, k = tid % GPT;
+        cmax[tid] = fmaxf(redm[2 * q][k], redm[2 * q + 1][k]);
+    }
+
+    // 3. the global maxima: every CTA's cmax through distributed shared memory
+    cl_barrier();
+    if (tid < G) {
+        float m = -INFINITY;
+#pragma unroll
+        for (int k = 0; k < CL_CS; ++k) m = fmaxf(m, cl_ld_remote(&cmax[tid], k));
+        Ms[tid] = m;
+    }
+    __syncthreads();
+
+    // 4. p, and per chunk the ordered double sums (warps 0-7: O for dimension
+    //    tid % 128 of heads (tid / 128) + 2k; warp 8: the sums of p)
+    const int d = tid & 127, gh = (tid >> 7) & 1;
+    double O[HPT];
+    double Lc = 0.0;
+#pragma unroll
+    for (int k = 0; k < HPT; ++k) O[k] = 0.0;
+    const size_t nchmax = (size_t)((a.ncap + AT_CHUNK - 1) / AT_CHUNK);
+    double * part = a.part + (size_t)h * nchmax * G * 129;
+    for (int i = 0; i < nst; ++i) {
+        if (!alb_mbar_wait(&vfull[i % CL_VR], (uint32_t)((i / CL_VR) & 1))) {
+            if (tid == 0) atomicExch(a.err, ALB_DEVERR_MBAR_TIMEOUT);
+            s_bad = 1;
+        }
+        const int cb = c0 + i * CL_ST, rows = min(CL_ST, c1 - cb);
+        if (tid < 64 * GQ) {
+#pragma unroll
+            for (int k = 0; k < GPT; ++k) {
+                const int g = gq * GPT + k;
+                double v = 0.0;
+                if (cl < rows) v = (double)alb_ref_expf(__fsub_rn(sc[(size_t)g * CL_MAXC + (cb - c0) + cl], Ms[g])) * 0x1p1008;
+                pd[g * CL_ST + cl] = v;   // p * 2^1008, exact
+            }
+        }
+        __syncthreads();
+        if (warp == 8) {
+            if (lane < G)   // the chunk's sum of p, cells in order
+                for (int c = 0; c < rows; ++c) Lc += pd[lane * CL_ST + c] * 0x1p-1008;
+        } else if (G >= 2 || gh == 0) {
+            // V bits enter as (v * 2^-1008) and p as (p * 2^1008): fma adds the exact p * v
+            const uint16_t * vs = reinterpret_cast<const uint16_t *>(vring + (size_t)(i % CL_VR) * CL_ST * 256) + d;
+            for (int c = 0; c < rows; ++c) {
+                const double vd = alb_h2d_bits(vs[c * 128]);
+#pragma unroll
+                for (int k = 0; k < HPT; ++k) O[k] = fma(pd[(gh + 2 * k) * CL_ST + c], vd, O[k]);
+            }
+        }
+        const int j = j0 + (cb - c0) / AT_CHUNK;
+        if ((i & 1) == 1 || i == nst - 1) {   // a chunk ends (two stages per chunk, or the CTA's last)
+            double * pj = part + (size_t)j * G * 129;
+            if (warp == 8) {
+                if (lane < G) { pj[lane * 129 + 128] = Lc; Lc = 0.0; }
+            } else if (G >= 2 || gh == 0) {
+#pragma unroll
+                for (int k = 0; k < HPT; ++k) { pj[(gh + 2 * k) * 129 + d] = O[k]; O[k] = 0.0; }
+            }
+        }
+        __syncthreads();   // V stage and pd consumed
+        issue(true, i + CL_VR, true);
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");   // no copy in flight past this point
+
+    // 5. merge: this CTA's output blocks (head g, dims 32w .. 32w+31), block
+    //    b = r, r + CL_CS, ... of the G * 4, one warp each
+    __threadfence();
+    cl_barrier();
+    for (int b = r + CL_CS * warp; b < G * 4 && warp < 8; b += CL_CS * 8) {
+        const int g = b >> 2, w = b & 3, dd = 32 * w + lane;
+        const double L = at_ordered_sum(part + g * 129 + 128, (size_t)G * 129, nch);
+        const double Od = at_ordered_sum(part + g * 129 + dd, (size_t)G * 129, nch);
+        const float v = L > 0.0 ? __double2float_rn(Od / L) : 0.0f;
+        const int hq = h * G + g;
+        a.out[(size_t)hq * 128 + dd] = v;
+        if (a.xq) {   // quantize_row_q8_0 of the block (arm.cpp:1834-1851)
+            int8_t q;
+            uint16_t dh;
+            q8_block_lane(v, q, dh);
+            uint8_t * blk = a.xq + ((size_t)hq * 4 + w) * 34;
+            if (lane == 0) *reinterpret_cast<uint16_t *>(blk) = dh;
+            blk[2 + lane] = (uint8_t)q;
+        }
+    }
+    if (s_bad && tid == 0 && !fits) atomicExch(a.err, ALB_DEVERR_MBAR_TIMEOUT);
+    alb_pdl_trigger();
+}
+
+template <int G>
+static cudaError_t launch_att_cl_t(const AttParams & p, bool pdl, cudaStream_t st) {
+    cudaError_t e = ensure_smem(k_att_decode_cl<G>, cl_smem<G>());
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(CL_CS, (unsigned)p.Hkv, 1);
+    cfg.blockDim = dim3(CL_THREADS);
+    cfg.dynamicSmemBytes = cl_smem<G>();
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = CL_CS;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, k_att_decode_cl<G>, p);
+}
+
 template <int G, bool FUSED>
 static cudaError_t launch_att_t(const AttParams & p, bool pdl, cudaStream_t st) {
     cudaError_t e = ensure_smem(k_att_scores<G, FUSED>, AT_SCORES_SMEM);
@@ -523,8 +847,12 @@ static AttParams att_params(const FlashArgs & f) {
     p.q = f.q; p.kc = f.kc; p.vc = f.vc; p.Hq = f.Hq; p.Hkv = f.Hkv; p.T = f.T; p.S = f.S; p.ncap = f.ncap;
     p.pos0 = f.pos0; p.pos_dev = f.pos_dev; p.scale = f.scale; p.out = f.out;
     p.xq = static_cast<uint8_t *>(f.xq);
+    p.err = device_error_ptr();
     return p;
 }
+
+// Cells one decode-step cluster launch serves (the split kernels serve more).
+int attn_decode_cluster_max_cells() { return CL_CS * CL_MAXC; }
 
 size_t split_attn_ws_bytes(int Hq, int Hkv, int T, int S, int ncap) {
     return at_layout(Hq, Hkv, T, S, ncap).bytes;
@@ -535,13 +863,22 @@ cudaError_t launch_split_attn(const FlashArgs & f, cudaStream_t st) {
     return launch_att<false>(att_params(f), f.pdl, st);
 }
 
-cudaError_t launch_attn_decode(const FlashArgs & f, const QkvArgs & qa, cudaStream_t st) {
+cudaError_t launch_attn_decode(const FlashArgs & f, const QkvArgs & qa, bool cluster, cudaStream_t st) {
     if (!f.ws || f.T != 1 || !qa.qkv || !qa.rope || !qa.q_norm || !qa.k_norm) return cudaErrorInvalidValue;
     AttParams p = att_params(f);
     p.q = nullptr;
     p.qkv = qa.qkv; p.qn = qa.q_norm; p.kn = qa.k_norm; p.eps = qa.eps; p.rope = qa.rope;
     p.kcw = qa.kc; p.vcw = qa.vc;
-    return launch_att<true>(p, f.pdl, st);
+    if (!p.err) return cudaErrorMemoryAllocation;
+    if (!cluster) return launch_att<true>(p, f.pdl, st);
+    if (p.Hkv <= 0 || p.Hq % p.Hkv != 0 || p.Hkv > 65535 || p.ncap > CL_CS * CL_MAXC) return cudaErrorInvalidValue;
+    switch (p.Hq / p.Hkv) {
+        case 1: return launch_att_cl_t<1>(p, f.pdl, st);
+        case 2: return launch_att_cl_t<2>(p, f.pdl, st);
+        case 4: return launch_att_cl_t<4>(p, f.pdl, st);
+        case 8: return launch_att_cl_t<8>(p, f.pdl, st);
+        default: return cudaErrorInvalidValue;
+    }
 }
 
 }  // namespace alb

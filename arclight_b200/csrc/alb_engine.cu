@@ -89,6 +89,7 @@ struct alb_engine {
     void * am_scratch = nullptr;
     float * fa_ws = nullptr;
     int fa_S_decode = 1;
+    bool fa_cluster = false;    // decode attention: one cluster launch per layer (max_ctx small enough)
     size_t fa_ws_bytes = 0;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t gexec = nullptr;
@@ -171,12 +172,13 @@ static int engine_forward(alb_engine * e, int64_t T, bool pdl, int ncap_prefill 
             // decode: QK-norm + RoPE + K/V store inside the split score kernel; the
             // last CTA of each KV head writes the O projection's Q8_0 input records
             fa.xq = e->xq;
-            ALB_CUDA_TRY(launch_attn_decode(fa, qa, st));
+            ALB_CUDA_TRY(launch_attn_decode(fa, qa, e->fa_cluster, st));
+            launches += e->fa_cluster ? 1 : 2;   // the cluster kernel, or scores + P.V
         } else {
             ALB_CUDA_TRY(launch_qk_norm_rope_kv(qa, st));
             ALB_CUDA_TRY(launch_flash_attn(fa, st));
+            launches += 2;   // QK-norm/RoPE + the prefill attention
         }
-        launches += 2;   // scores + P.V, or QK-norm/RoPE + the prefill attention
         const int o_in = T == 1 ? GEMV_IN_Q8 : GEMV_IN_F32;
         const void * o_x = T == 1 ? e->xq : static_cast<const void *>(e->att);
         if (e->tp == 1) {
@@ -350,6 +352,7 @@ static int engine_init_acts(alb_engine * e) {
     int S = (4 * alb_sm_count() + e->Hkv - 1) / e->Hkv;
     if (S > 1024) S = 1024;
     e->fa_S_decode = S;
+    e->fa_cluster = e->max_ctx <= attn_decode_cluster_max_cells();
     e->fa_ws_bytes = flash_attn_ws_bytes(e->Hq, e->Hkv, 1, S, e->max_ctx);   // prefill ubatches need none
     uint8_t * ws = nullptr;
     ALB_TRY(e->alloc(&ws, e->fa_ws_bytes));

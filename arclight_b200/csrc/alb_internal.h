@@ -92,7 +92,11 @@ cudaError_t launch_qk_norm_rope_kv(const QkvArgs & a, cudaStream_t st);
 // Decode step attention with QK-norm + RoPE + the K/V store fused (T = 1):
 // f describes the attention (workspace, splits, output and its Q8_0 records),
 // qa the raw QKV projection, norm weights, RoPE table and the caches to store into.
-cudaError_t launch_attn_decode(const FlashArgs & f, const QkvArgs & qa, cudaStream_t st);
+// Decode-step attention of one token from the raw QKV projection (QK-norm,
+// RoPE and the new K/V cell included): one cluster launch when `cluster`
+// (f.ncap <= attn_decode_cluster_max_cells()), else the two split kernels.
+cudaError_t launch_attn_decode(const FlashArgs & f, const QkvArgs & qa, bool cluster, cudaStream_t st);
+int attn_decode_cluster_max_cells();
 cudaError_t launch_embed(const uint8_t * W, int64_t vocab, int64_t E, const int32_t * tokens, int T, float * x,
                          unsigned long long * key_reset, bool pdl, cudaStream_t st);
 // argmax over x[0..n): scratch >= 64*8 + 16 bytes with its ticket word zero at first use

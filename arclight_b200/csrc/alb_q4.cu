@@ -149,11 +149,32 @@ __device__ __forceinline__ void mv_quant_rec(int * rec, const float (&v)[8], int
     }
 }
 
+// dst[0..n) = src[0..n) (16-byte words), by the consumer warps: every load of
+// a thread is issued before its stores (one round trip for up to 8 words a
+// thread).
+__device__ __forceinline__ void mv_stage16(uint4 * dst, const uint4 * __restrict__ src, int n) {
+    constexpr int U = 8;
+    for (int i0 = 0; i0 < n; i0 += U * MV_NT) {
+        uint4 v[U];
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const int i = i0 + threadIdx.x + k * MV_NT;
+            if (i < n) v[k] = src[i];
+        }
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const int i = i0 + threadIdx.x + k * MV_NT;
+            if (i < n) dst[i] = v[k];
+        }
+    }
+}
+
 // Prologue of the consumer warps: the CTA's Q8_0 records of the input vector.
 //   IN_Q8     block_q8_0 records from global memory (staged with 16-byte loads);
 //   IN_F32    fp32 x quantized here (quantize_row_q8_0, arm.cpp:1819-1853);
 //   IN_F32_RMS RMSNorm * w first (ops.cpp:680-724: double sum of the fp32
-//             squares, mean rounded to float, 1/sqrtf(mean + eps)).
+//             squares, mean rounded to float, 1/sqrtf(mean + eps)); w is
+//             already staged at stage + K floats.
 // `stage` is scratch of gemv_stage_bytes(K, IN); ends with the consumers'
 // named barrier (the producer warp does not take part).
 template <int IN, bool PAIR>
@@ -168,7 +189,7 @@ __device__ __forceinline__ void mv_prologue(const GemvArgs & a, int * xs, int nb
         if ((reinterpret_cast<uintptr_t>(a.x) & 15) == 0) {
             const int n16 = nbytes / 16;
             const uint4 * src = static_cast<const uint4 *>(a.x);
-            for (int i = tid; i < n16; i += NT) stage[i] = src[i];
+            mv_stage16(stage, src, n16);
             for (int i = n16 * 16 + tid; i < nbytes; i += NT) reinterpret_cast<uint8_t *>(stage)[i] = src8[i];
         } else {
             for (int i = tid; i < nbytes; i += NT) reinterpret_cast<uint8_t *>(stage)[i] = src8[i];
@@ -196,22 +217,12 @@ __device__ __forceinline__ void mv_prologue(const GemvArgs & a, int * xs, int nb
     } else {
         const float * x = static_cast<const float *>(a.x);
         float * xf = reinterpret_cast<float *>(stage);
-        float * wf = xf + a.K;
+        float * wf = xf + a.K;   // the norm weights: staged before the dependency wait
         const int K = (int)a.K;
-        const bool vec = (K & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
-                         (IN != GEMV_IN_F32_RMS || (reinterpret_cast<uintptr_t>(a.norm_w) & 15) == 0);
-        if (vec) {
-            const float4 * x4 = reinterpret_cast<const float4 *>(x);
-            const float4 * w4 = reinterpret_cast<const float4 *>(a.norm_w);
-            for (int i = tid; i < K / 4; i += NT) {
-                reinterpret_cast<float4 *>(xf)[i] = x4[i];
-                if constexpr (IN == GEMV_IN_F32_RMS) reinterpret_cast<float4 *>(wf)[i] = w4[i];
-            }
+        if ((reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+            mv_stage16(stage, reinterpret_cast<const uint4 *>(x), K / 4);
         } else {
-            for (int i = tid; i < K; i += NT) {
-                xf[i] = x[i];
-                if constexpr (IN == GEMV_IN_F32_RMS) wf[i] = a.norm_w[i];
-            }
+            for (int i = tid; i < K; i += NT) xf[i] = x[i];
         }
         asm volatile("bar.sync 1, %0;" :: "n"(NT) : "memory");
         float scale = 1.0f;
@@ -357,6 +368,15 @@ k_mv(const GemvArgs a, const MvPlan p) {
     }
 
     // ------------------------------------- dot and chain warps: the input records
+    if constexpr (IN == GEMV_IN_F32_RMS) {
+        // the norm weights do not depend on the previous kernel (the prologue's
+        // first barrier orders these stores before their use)
+        float * wf = reinterpret_cast<float *>(cbase) + a.K;
+        if ((reinterpret_cast<uintptr_t>(a.norm_w) & 15) == 0)
+            mv_stage16(reinterpret_cast<uint4 *>(wf), reinterpret_cast<const uint4 *>(a.norm_w), (int)(a.K / 4));
+        else
+            for (int i = tid; i < (int)a.K; i += MV_NT) wf[i] = a.norm_w[i];
+    }
     alb_pdl_wait();
     mv_prologue<IN, PAIR>(a, xs, nb, reinterpret_cast<uint4 *>(cbase));
 
