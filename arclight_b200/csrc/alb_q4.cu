@@ -90,8 +90,8 @@ cudaError_t launch_quantize_q8_0(const float * x, void * xq, int64_t n, bool pdl
 //   bar_off                      mbarriers full[ns] empty[ns] done[ncb] free[ncb]
 struct MvPlan {
     int R;                  // rows per stage (<= 64; <= 16 for the pair chain)
-    int RC;                 // rows per chain warp (each chain warp takes a contiguous half)
-    int ns, ncb;            // weight stages, chain buffers
+    int RC;                 // rows per chain-warp pass (32, or 8 for the pair chain)
+    int ns, ncb;            // weight stages, chain buffers (ncb == MV_CH: one per chain warp)
     uint32_t stage_bytes;   // R * row bytes
     uint32_t cbp;           // chain-buffer row pitch in bytes (an odd multiple of 16)
     uint32_t cbs;           // pair chain: row pitch of the dx*dw array (an odd number of words)
@@ -100,9 +100,9 @@ struct MvPlan {
     uint32_t smem;
 };
 
-static constexpr int MV_CW = 12;                       // block-dot warps
+static constexpr int MV_CW = 24;                       // block-dot warps
 static constexpr int MV_RU = 2;                        // rows per dot iteration (independent work)
-static constexpr int MV_CH = 2;                        // chain warps (alternate stages)
+static constexpr int MV_CH = 4;                        // chain warps: stage g goes to chain warp g % MV_CH
 static constexpr int MV_PW = MV_CW + MV_CH;            // the producer warp's index
 static constexpr int MV_THREADS = (MV_CW + MV_CH + 1) * 32;
 static constexpr int MV_NT = (MV_CW + MV_CH) * 32;     // threads of the prologue barrier
@@ -291,16 +291,17 @@ __device__ __forceinline__ unsigned long long mv_key(float v, int64_t idx) {
 
 // Batch-1 Q4_0 x Q8_0 mat-vec with the reference's summation order.
 //
-// Each CTA owns a contiguous range of rows.  Its producer warp streams them
-// through an ns-stage shared-memory ring, R whole rows per stage (nibbles and
-// scales, two bulk copies), and never waits on the previous kernel: under
-// programmatic dependent launch the first stages are in flight while the
-// previous grid drains.  For each stage the 8 consumer warps compute the int32
-// block dots I(n, b) of its R x K/32 blocks (lanes over consecutive blocks of
-// one row: conflict-free 16-byte reads) and store the terms
-// (float(I), f32(dx) * f32(dw)) -- both exact -- in a chain buffer; then one
-// warp (stages rotate over the warps) runs, one lane per row, the fp32 fma
-// chain over the blocks in order: acc = fma(float(I), dx*dw, acc)
+// One CTA per SM owns a contiguous range of rows.  Its producer warp streams
+// them through an ns-stage shared-memory ring, R whole rows per stage (nibbles
+// and scales of the row-interleaved layout: one bulk copy), and never waits on
+// the previous kernel: under programmatic dependent launch the first stages
+// are in flight while the previous grid drains.  For each stage the MV_CW dot
+// warps compute the int32 block dots I(n, b) of its R x K/32 blocks (lanes over
+// consecutive blocks of one row: conflict-free 16-byte reads) and store the
+// terms (float(I), f32(dx) * f32(dw)) -- both exact -- in the stage's chain
+// buffer; then chain warp g % MV_CH (stages rotate over the chain warps, so
+// the chains of several stages run at once) runs, one lane per row, the fp32
+// fma chain over the blocks in order: acc = fma(float(I), dx*dw, acc)
 // (nnml_gemv_q4_0_4x4_q8_0, gemm.cpp:179-181; vcvtq_n_f32_s32(16 I, 4) is
 // float(I) exactly).  The pair variant follows nnml_vec_dot_q4_0_q8_0
 // (arm.cpp:633-692, the generic mul_mat of the lm head): four lanes per row,
@@ -310,7 +311,7 @@ __device__ __forceinline__ unsigned long long mv_key(float v, int64_t idx) {
 // Every wait is bounded; on a timeout the kernel records an error code,
 // stops its loops and (producer) waits for its copies in flight before exit.
 template <int IN, int OUT>
-__global__ void __launch_bounds__(MV_THREADS, 2)
+__global__ void __launch_bounds__(MV_THREADS, 1)
 k_mv(const GemvArgs a, const MvPlan p) {
     constexpr bool PAIR = OUT == GEMV_OUT_PAIR || OUT == GEMV_OUT_LOGITS;
     constexpr int XR = XRec<PAIR>::INTS;
@@ -334,7 +335,7 @@ k_mv(const GemvArgs a, const MvPlan p) {
     uint8_t * cbase = smem + p.cb_off;
     if (tid == 0) {
         for (int i = 0; i < p.ns; ++i) { alb_mbar_init(&full[i], 1); alb_mbar_init(&empty[i], MV_CW); }
-        for (int i = 0; i < p.ncb; ++i) { alb_mbar_init(&done[i], MV_CW); alb_mbar_init(&freeb[i], MV_CH); }
+        for (int i = 0; i < p.ncb; ++i) { alb_mbar_init(&done[i], MV_CW); alb_mbar_init(&freeb[i], 1); }
         s_abort = 0;
         alb_mbar_fence_init();
     }
@@ -481,11 +482,11 @@ k_mv(const GemvArgs a, const MvPlan p) {
     }
 
     // ---------------------------------------------------------- chain warps
-    // Both chain warps take every stage, chain warp cw the rows [cw * RC, cw * RC + RC).
+    // Chain warp cw takes the stages g = cw, cw + MV_CH, ... (chain buffer cw),
+    // all their rows, in passes of RC rows (one lane per row; four for the pair chain).
     const int cw = warp - MV_CW;
-    const int rb0 = cw * p.RC;
     unsigned long long best = 0ull;   // LOGITS: this lane's best key
-    for (int g = 0; g < nst; ++g) {
+    for (int g = cw; g < nst; g += MV_CH) {
         const int cbi = g % p.ncb;
         if (*reinterpret_cast<volatile int *>(&s_abort)) break;
         if (!alb_mbar_wait(&done[cbi], (uint32_t)((g / p.ncb) & 1))) {
@@ -497,71 +498,90 @@ k_mv(const GemvArgs a, const MvPlan p) {
         const int rg = (int)((n1 - r0) < R ? (n1 - r0) : R);
         const uint8_t * cb = cbase + (size_t)cbi * p.cb_bytes;
         if constexpr (!PAIR) {
-            // acc = fma(float(I), f32(dx) * f32(dw), acc), blocks in order
-            const int r = rb0 + lane;
-            const bool mine = lane < p.RC && r < rg;
-            float acc = 0.0f;
-            if (mine) {
-                const float4 * e = reinterpret_cast<const float4 *>(cb + (size_t)r * p.cbp);
-                int b = 0;
+            float accs[2];   // R <= 64: at most two passes of 32 rows
+#pragma unroll
+            for (int ps = 0; ps < 2; ++ps) {
+                // acc = fma(float(I), f32(dx) * f32(dw), acc), blocks in order
+                const int r = ps * 32 + lane;
+                float acc = 0.0f;
+                if (r < rg) {
+                    const float4 * e = reinterpret_cast<const float4 *>(cb + (size_t)r * p.cbp);
+                    int b = 0;
 #pragma unroll 8
-                for (; b + 1 < nb; b += 2) {
-                    const float4 v = e[b >> 1];
-                    acc = __fmaf_rn(v.x, v.y, acc);
-                    acc = __fmaf_rn(v.z, v.w, acc);
+                    for (; b + 1 < nb; b += 2) {
+                        const float4 v = e[b >> 1];
+                        acc = __fmaf_rn(v.x, v.y, acc);
+                        acc = __fmaf_rn(v.z, v.w, acc);
+                    }
+                    if (b < nb) {
+                        const float2 v = reinterpret_cast<const float2 *>(e)[b];
+                        acc = __fmaf_rn(v.x, v.y, acc);
+                    }
                 }
-                if (b < nb) {
-                    const float2 v = reinterpret_cast<const float2 *>(e)[b];
-                    acc = __fmaf_rn(v.x, v.y, acc);
-                }
+                accs[ps] = acc;
             }
             __syncwarp();
             if (lane == 0) alb_mbar_arrive(&freeb[cbi]);   // the terms are in registers now
-            if constexpr (OUT == GEMV_OUT_SWIGLU) {
-                // RC is even, so gate row r (even) and up row r + 1 share the warp
-                const float up = __shfl_down_sync(0xffffffffu, acc, 1);
-                if (mine && !(r & 1)) a.y[(r0 + r) >> 1] = alb_swiglu1(acc, up);
-            } else {
-                if (mine && a.y) {
-                    const int64_t n = r0 + r;
-                    a.y[n] = a.residual ? __fadd_rn(acc, a.residual[n]) : acc;
+#pragma unroll
+            for (int ps = 0; ps < 2; ++ps) {
+                const int r = ps * 32 + lane;
+                const float acc = accs[ps];
+                if constexpr (OUT == GEMV_OUT_SWIGLU) {
+                    // passes hold 32 rows: gate row r (even) and up row r + 1 share the warp
+                    const float up = __shfl_down_sync(0xffffffffu, acc, 1);
+                    if (r < rg && !(r & 1)) a.y[(r0 + r) >> 1] = alb_swiglu1(acc, up);
+                } else {
+                    if (r < rg && a.y) {
+                        const int64_t n = r0 + r;
+                        a.y[n] = a.residual ? __fadd_rn(acc, a.residual[n]) : acc;
+                    }
                 }
             }
         } else {
-            const int rr = rb0 + (lane >> 2), l = lane & 3;
-            const bool mine = (lane >> 2) < p.RC && rr < rg;
-            float sv0 = 0.0f, sv1 = 0.0f;
-            float tail = 0.0f;
-            if (mine) {
-                const float * T = reinterpret_cast<const float *>(cb + (size_t)rr * p.cbp) + l;
-                const float * S = reinterpret_cast<const float *>(cb + (size_t)R * p.cbp + (size_t)rr * p.cbs);
-                int b = 0;
+            float sums[2];   // R <= 16: at most two passes of 8 rows
+#pragma unroll
+            for (int ps = 0; ps < 2; ++ps) {
+                const int rr = ps * 8 + (lane >> 2), l = lane & 3;
+                const bool mine = rr < rg;
+                float sv0 = 0.0f, sv1 = 0.0f;
+                float tail = 0.0f;
+                if (mine) {
+                    const float * T = reinterpret_cast<const float *>(cb + (size_t)rr * p.cbp) + l;
+                    const float * S = reinterpret_cast<const float *>(cb + (size_t)R * p.cbp + (size_t)rr * p.cbs);
+                    int b = 0;
 #pragma unroll 8
-                for (; b + 1 < nb; b += 2) {
-                    sv0 = __fmaf_rn(T[4 * b], S[b], sv0);
-                    sv1 = __fmaf_rn(T[4 * b + 4], S[b + 1], sv1);
+                    for (; b + 1 < nb; b += 2) {
+                        sv0 = __fmaf_rn(T[4 * b], S[b], sv0);
+                        sv1 = __fmaf_rn(T[4 * b + 4], S[b + 1], sv1);
+                    }
+                    if (b < nb) {   // odd block count: ((sumi * dw) * dx), added after the vector sum
+                        const float * Tt = T - l + 4 * b;
+                        tail = __fmul_rn(__fmul_rn(Tt[0], Tt[1]), S[b]);
+                    }
                 }
-                if (b < nb) {   // odd block count: ((sumi * dw) * dx), added after the vector sum
-                    const float * Tt = T - l + 4 * b;
-                    tail = __fmul_rn(__fmul_rn(Tt[0], Tt[1]), S[b]);
-                }
+                // vaddvq_f32 = (l0 + l1) + (l2 + l3), then sumv0 + sumv1 (arm.cpp:671)
+                float a0 = __fadd_rn(sv0, __shfl_xor_sync(0xffffffffu, sv0, 1));
+                a0 = __fadd_rn(a0, __shfl_xor_sync(0xffffffffu, a0, 2));
+                float a1 = __fadd_rn(sv1, __shfl_xor_sync(0xffffffffu, sv1, 1));
+                a1 = __fadd_rn(a1, __shfl_xor_sync(0xffffffffu, a1, 2));
+                float sum = __fadd_rn(a0, a1);
+                if (nb & 1) sum = __fadd_rn(sum, tail);
+                sums[ps] = sum;
             }
             __syncwarp();
             if (lane == 0) alb_mbar_arrive(&freeb[cbi]);
-            // vaddvq_f32 = (l0 + l1) + (l2 + l3), then sumv0 + sumv1 (arm.cpp:671)
-            float a0 = __fadd_rn(sv0, __shfl_xor_sync(0xffffffffu, sv0, 1));
-            a0 = __fadd_rn(a0, __shfl_xor_sync(0xffffffffu, a0, 2));
-            float a1 = __fadd_rn(sv1, __shfl_xor_sync(0xffffffffu, sv1, 1));
-            a1 = __fadd_rn(a1, __shfl_xor_sync(0xffffffffu, a1, 2));
-            float sum = __fadd_rn(a0, a1);
-            if (nb & 1) sum = __fadd_rn(sum, tail);
-            if (mine && l == 0) {
-                const int64_t n = r0 + rr;
-                if (a.y) a.y[n] = sum;
-                if constexpr (OUT == GEMV_OUT_LOGITS) {
-                    if (sum == sum) {
-                        const unsigned long long k = mv_key(sum, a.idx_base + n);
-                        best = k > best ? k : best;
+#pragma unroll
+            for (int ps = 0; ps < 2; ++ps) {
+                const int rr = ps * 8 + (lane >> 2), l = lane & 3;
+                if (rr < rg && l == 0) {
+                    const int64_t n = r0 + rr;
+                    const float sum = sums[ps];
+                    if (a.y) a.y[n] = sum;
+                    if constexpr (OUT == GEMV_OUT_LOGITS) {
+                        if (sum == sum) {
+                            const unsigned long long k = mv_key(sum, a.idx_base + n);
+                            best = k > best ? k : best;
+                        }
                     }
                 }
             }
@@ -603,13 +623,13 @@ static inline uint32_t mv_odd16(uint32_t x) {
 
 // Shared-memory plan: stages of about `stage_target` bytes of whole rows (one
 // bulk copy each: large copies stream at full HBM rate, small ones are limited
-// by the per-copy cost), two chain buffers, and as many stages (2..6) as fit the
-// budget, so that a CTA of the next kernel can be resident beside this one and
-// start its own weight stream.
+// by the per-copy cost), one chain buffer per chain warp, and as many stages
+// (2..8) as fit the budget (one CTA per SM: the ring, not a second resident
+// kernel, keeps HBM busy).
 static MvPlan mv_plan(int64_t K, bool pair, int in_mode, int budget, int stage_target) {
     const int64_t nb = K / 32;
     const int64_t row_bytes = q4_row_bytes(K);
-    const int rmax = pair ? 16 : 64;
+    const int rmax = pair ? 16 : 64;   // two chain passes of 8 (pair) or 32 rows
     int R = (int)(stage_target / row_bytes);
     if (R > rmax) R = rmax;
     if (R < 2) R = 2;
@@ -617,10 +637,9 @@ static MvPlan mv_plan(int64_t K, bool pair, int in_mode, int budget, int stage_t
     MvPlan p{};
     for (;;) {
         p.R = R;
-        p.RC = pair ? (R + 1) / 2 : (((R + 1) / 2) + 1) & ~1;   // even: SwiGLU pairs stay in one warp
-        if (p.RC > (pair ? 8 : 32)) p.RC = pair ? 8 : 32;
+        p.RC = pair ? 8 : 32;
         p.ns = 2;
-        p.ncb = 2;
+        p.ncb = MV_CH;
         p.stage_bytes = (uint32_t)(R * row_bytes);
         // chain entries per (row, block): (float(I), dx * dw), or for the pair
         // chain the four float partial dots [R][nb][4] and dx * dw [R][nb]
@@ -639,7 +658,7 @@ static MvPlan mv_plan(int64_t K, bool pair, int in_mode, int budget, int stage_t
         if (stg > region) region = stg;
         const uint32_t xsb = (uint32_t)(nb * (pair ? XRec<true>::INTS : XRec<false>::INTS) * 4);
         const uint32_t fixed = ((region + 127) & ~127u) + ((xsb + 127) & ~127u) + 8 * 2 * (6 + p.ncb);
-        while (p.ns < 6 && (int)(fixed + (uint32_t)(p.ns + 1) * p.stage_bytes) <= budget) ++p.ns;
+        while (p.ns < 8 && (int)(fixed + (uint32_t)(p.ns + 1) * p.stage_bytes) <= budget) ++p.ns;
         p.cb_off = (uint32_t)p.ns * p.stage_bytes;
         p.xs_off = p.cb_off + ((region + 127) & ~127u);
         p.bar_off = p.xs_off + ((xsb + 127) & ~127u);
@@ -652,7 +671,7 @@ static MvPlan mv_plan(int64_t K, bool pair, int in_mode, int budget, int stage_t
 }
 
 // Tuning knobs (read once per process): ALB_MV_SMEM_KB (shared-memory budget
-// of a CTA, default 110), ALB_MV_STAGE_KB (target stage size, default 32),
+// of a CTA, default 160), ALB_MV_STAGE_KB (target stage size, default 32),
 // ALB_MV_CPS (CTAs per SM, default 1).
 static int mv_knob(const char * name, int dflt) {
     const char * v = getenv(name);
@@ -662,7 +681,7 @@ static int mv_knob(const char * name, int dflt) {
 template <int IN, int OUT>
 static cudaError_t launch_mv_t(const GemvArgs & a, cudaStream_t stream) {
     constexpr bool PAIR = OUT == GEMV_OUT_PAIR || OUT == GEMV_OUT_LOGITS;
-    static const int budget_kb = mv_knob("ALB_MV_SMEM_KB", 110);
+    static const int budget_kb = mv_knob("ALB_MV_SMEM_KB", 160);
     static const int stage_kb = mv_knob("ALB_MV_STAGE_KB", 32);
     const MvPlan p = mv_plan(a.K, PAIR, IN, a.smem_budget > 0 ? a.smem_budget : budget_kb * 1024, stage_kb * 1024);
     auto kern = k_mv<IN, OUT>;
@@ -692,8 +711,8 @@ cudaError_t launch_gemv(const GemvArgs & a_in, cudaStream_t s) {
     GemvArgs a = a_in;
     if (!a.err) a.err = device_error_ptr();
     if (!a.err) return cudaErrorMemoryAllocation;
-    // K <= 12288: at most 12 block groups of 32, one per dot warp at least
-    if (a.K % 32 != 0 || a.K <= 0 || a.N <= 0 || a.K > 32 * 32 * MV_CW || a.N >= ((int64_t)1 << 30))
+    // K <= 12288 (the C ABI's limit; the dot warps would take up to 32 * 32 * MV_CW)
+    if (a.K % 32 != 0 || a.K <= 0 || a.N <= 0 || a.K > 12288 || a.N >= ((int64_t)1 << 30))
         return cudaErrorInvalidValue;
     // bulk copies: 16-byte aligned sources (row strides K/2 and pitch*2 are multiples of 16)
     if (reinterpret_cast<uintptr_t>(a.W) & 15) return cudaErrorInvalidValue;   // bulk-copy source alignment
