@@ -39,8 +39,9 @@ namespace alb {
 static constexpr int AT_CHUNK = 128;                    // canonical summation chunk (cells)
 static constexpr int AT_ST = 64;                        // cells per staging step (AT_CHUNK / 2)
 static constexpr int AT_NST = 3;                        // K ring depth of k_att_scores
+static constexpr int AT_SST = 128;                      // cells per K stage of k_att_scores (one per thread)
 static constexpr int AT_KPITCH = 272;                   // padded K row in shared memory
-static constexpr size_t AT_SCORES_SMEM = (size_t)AT_NST * AT_ST * AT_KPITCH;   // 52,224 B
+static constexpr size_t AT_SCORES_SMEM = (size_t)AT_NST * AT_SST * AT_KPITCH;   // 104,448 B
 
 __device__ __forceinline__ void at_cp16(void * dst, const void * src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(alb_smem_addr(dst)), "l"(src) : "memory");
@@ -51,15 +52,30 @@ __device__ __forceinline__ void at_cp4(void * dst, const void * src) {
 __device__ __forceinline__ void at_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N> __device__ __forceinline__ void at_wait() { asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory"); }
 
-// Chunks of n cells, and the contiguous chunk range [j0, j1) of split s of Su.
-__device__ __forceinline__ int at_nchunks(int n) { return (n + AT_CHUNK - 1) / AT_CHUNK; }
-__device__ __forceinline__ int at_splits_used(int n, int S) {
-    const int nc = at_nchunks(n);
-    return nc < S ? nc : S;
+// Chunks of n cells; superchunks of scn = ceil(chunks / AT_SUPER) consecutive
+// chunks (one chunk each up to AT_SUPER chunks), at most AT_SUPER of them.
+// The canonical sums add cells in order within a chunk, chunk sums in order
+// within a superchunk and superchunk sums in order; a split holds whole
+// superchunks, so its partials do not depend on the split count.
+static constexpr int AT_SUPER = 64;
+__host__ __device__ __forceinline__ int at_nchunks(int n) { return (n + AT_CHUNK - 1) / AT_CHUNK; }
+__host__ __device__ __forceinline__ int at_scn(int nch) { return nch > AT_SUPER ? (nch + AT_SUPER - 1) / AT_SUPER : 1; }
+__host__ __device__ __forceinline__ int at_nsuper(int nch) { const int k = at_scn(nch); return (nch + k - 1) / k; }
+// Superchunk slots of one token's partials when it attends at most ncap cells:
+// the most superchunks any n <= ncap has (64 chunks make 64 superchunks, 65 make 33).
+__host__ __device__ __forceinline__ int at_nsuper_max(int ncap) {
+    const int nch = at_nchunks(ncap);
+    return nch < AT_SUPER ? nch : AT_SUPER;
 }
-__device__ __forceinline__ void at_split(int nc, int Su, int s, int & j0, int & j1) {
-    j0 = (int)((int64_t)nc * s / Su);
-    j1 = (int)((int64_t)nc * (s + 1) / Su);
+__device__ __forceinline__ int at_splits_used(int n, int S) {
+    const int ns = at_nsuper(at_nchunks(n));
+    return ns < S ? ns : S;
+}
+// The chunk range [j0, j1) of split s of Su: superchunks [ns s / Su, ns (s + 1) / Su).
+__device__ __forceinline__ void at_split(int nch, int Su, int s, int & j0, int & j1) {
+    const int ns = at_nsuper(nch), k = at_scn(nch);
+    j0 = (int)((int64_t)ns * s / Su) * k;
+    j1 = min(nch, (int)((int64_t)ns * (s + 1) / Su) * k);
 }
 
 struct AttParams {
@@ -78,7 +94,7 @@ struct AttParams {
     int * tickets = nullptr;          // [Hkv * T]
     float * smax = nullptr;           // [Hkv][T][S][G]
     float * scores = nullptr;         // [Hkv][T][G][ncap]
-    double * part = nullptr;          // [Hkv][T][nchunks(ncap)][G][129]
+    double * part = nullptr;          // [Hkv][T][at_nsuper_max(ncap)][G][129]
     float * out = nullptr;            // [T][Hq][128]
     uint8_t * xq = nullptr;           // optional block_q8_0 records of out [T][Hq * 4]
     int * err = nullptr;              // device error word (bounded waits of the cluster kernel)
@@ -92,8 +108,8 @@ static AtLayout at_layout(int Hq, int Hkv, int T, int S, int ncap) {
     l.smax_off = ((size_t)Hkv * T * 4 + 255) & ~(size_t)255;
     l.scores_off = (l.smax_off + (size_t)Hkv * T * S * G * 4 + 255) & ~(size_t)255;
     l.part_off = (l.scores_off + (size_t)Hkv * T * G * ncap * 4 + 255) & ~(size_t)255;
-    const size_t nch = (size_t)((ncap + AT_CHUNK - 1) / AT_CHUNK);
-    l.bytes = l.part_off + (size_t)Hkv * T * nch * G * 129 * 8;
+    const size_t nsp = (size_t)at_nsuper_max(ncap);
+    l.bytes = l.part_off + (size_t)Hkv * T * nsp * G * 129 * 8;
     return l;
 }
 
@@ -164,7 +180,7 @@ __device__ __forceinline__ void at_norm_rope_heads(float (&v)[NH], int nh, int n
 template <int G, bool FUSED>
 __global__ void __launch_bounds__(128)
 k_att_scores(const AttParams a) {
-    extern __shared__ __align__(16) uint8_t at_ring[];   // AT_NST x AT_ST x AT_KPITCH
+    extern __shared__ __align__(16) uint8_t at_ring[];   // AT_NST x AT_SST x AT_KPITCH
     __shared__ __align__(16) float qs[G][128];
     __shared__ __align__(16) float knew[128];
     __shared__ float hb[FUSED ? G + 1 : 1][128];
@@ -183,11 +199,11 @@ k_att_scores(const AttParams a) {
     const int c0 = j0 * AT_CHUNK, c1 = min(n, j1 * AT_CHUNK);
     const int64_t row = (int64_t)a.Hkv * 128;
     const uint16_t * kb = a.kc + (size_t)h * 128;
-    const int nst = (c1 - c0 + AT_ST - 1) / AT_ST;
+    const int nst = (c1 - c0 + AT_SST - 1) / AT_SST;
     auto issue = [&](int i) {
         if (i < nst) {
-            const int cb = c0 + i * AT_ST, rows = min(AT_ST, c1 - cb);
-            uint8_t * dst = at_ring + (i % AT_NST) * AT_ST * AT_KPITCH;
+            const int cb = c0 + i * AT_SST, rows = min(AT_SST, c1 - cb);
+            uint8_t * dst = at_ring + (i % AT_NST) * AT_SST * AT_KPITCH;
             for (int p = tid; p < rows * 16; p += 128) {
                 const int r = p >> 4, j = p & 15;
                 at_cp16(dst + r * AT_KPITCH + j * 16, kb + (size_t)(cb + r) * row + j * 8);
@@ -232,66 +248,58 @@ k_att_scores(const AttParams a) {
             qs[g][d] = __half2float(__float2half_rn(a.q[((size_t)t * a.Hq + h * G + g) * 128 + d]));
         }
     }
-    constexpr int GH = G >= 2 ? 2 : 1, GPT = G / GH;
-    const int cl = tid & (AT_ST - 1), gh = tid / AT_ST;   // cell of the stage, head half
-    float mx[GPT];
+    // thread tid: cell tid of each stage, all G heads (each K element is
+    // converted once and feeds G independent chains)
+    float mx[G];
 #pragma unroll
-    for (int k = 0; k < GPT; ++k) mx[k] = -INFINITY;
+    for (int g = 0; g < G; ++g) mx[g] = -INFINITY;
     float * sc = a.scores + ((size_t)h * a.T + t) * G * a.ncap;
     for (int i = 0; i < nst; ++i) {
         at_wait<AT_NST - 2>();
         __syncthreads();   // stage i visible to all; stage i-1 consumed by all; q / knew visible
         issue(i + AT_NST - 1);
-        const int c = c0 + i * AT_ST + cl;
-        if (gh < GH && c < c1) {
-            const uint8_t * kr = at_ring + (i % AT_NST) * AT_ST * AT_KPITCH + cl * AT_KPITCH;
-            uint4 krow[16];
-            if (FUSED && c == n - 1) {   // the new cell: its fp16 K from this kernel, not the cache
+        const int c = c0 + i * AT_SST + tid;
+        if (c < c1) {
+            const uint8_t * kr = at_ring + (i % AT_NST) * AT_SST * AT_KPITCH + tid * AT_KPITCH;
+            const bool knew_row = FUSED && c == n - 1;   // the new cell: its fp16 K from this kernel
+            float acc[G];
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    uint32_t wd[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e)
-                        wd[e] = (uint32_t)alb_f2h(knew[8 * j + 2 * e]) | ((uint32_t)alb_f2h(knew[8 * j + 2 * e + 1]) << 16);
-                    krow[j] = make_uint4(wd[0], wd[1], wd[2], wd[3]);
-                }
-            } else {
-#pragma unroll
-                for (int j = 0; j < 16; ++j) krow[j] = *reinterpret_cast<const uint4 *>(kr + j * 16);
-            }
-            float acc[GPT];
-#pragma unroll
-            for (int k = 0; k < GPT; ++k) acc[k] = 0.0f;
-#pragma unroll
+            for (int g = 0; g < G; ++g) acc[g] = 0.0f;
+#pragma unroll 4
             for (int j = 0; j < 16; ++j) {   // dims 8j .. 8j+7, in order (the reference's sequential chain)
-                const uint32_t wd[4] = {krow[j].x, krow[j].y, krow[j].z, krow[j].w};
                 float kf[8];
+                if (knew_row) {
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&wd[e]));
-                    kf[2 * e] = f.x;
-                    kf[2 * e + 1] = f.y;
+                    for (int e = 0; e < 8; ++e) kf[e] = knew[8 * j + e];
+                } else {
+                    const uint4 kv = *reinterpret_cast<const uint4 *>(kr + j * 16);
+                    const uint32_t wd[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&wd[e]));
+                        kf[2 * e] = f.x;
+                        kf[2 * e + 1] = f.y;
+                    }
                 }
 #pragma unroll
-                for (int k = 0; k < GPT; ++k) {
-                    const float * qg = qs[gh * GPT + k];
-                    const float4 qa = *reinterpret_cast<const float4 *>(qg + 8 * j);
-                    const float4 qb = *reinterpret_cast<const float4 *>(qg + 8 * j + 4);
-                    acc[k] = __fmaf_rn(kf[0], qa.x, acc[k]);
-                    acc[k] = __fmaf_rn(kf[1], qa.y, acc[k]);
-                    acc[k] = __fmaf_rn(kf[2], qa.z, acc[k]);
-                    acc[k] = __fmaf_rn(kf[3], qa.w, acc[k]);
-                    acc[k] = __fmaf_rn(kf[4], qb.x, acc[k]);
-                    acc[k] = __fmaf_rn(kf[5], qb.y, acc[k]);
-                    acc[k] = __fmaf_rn(kf[6], qb.z, acc[k]);
-                    acc[k] = __fmaf_rn(kf[7], qb.w, acc[k]);
+                for (int g = 0; g < G; ++g) {
+                    const float4 qa = *reinterpret_cast<const float4 *>(&qs[g][8 * j]);
+                    const float4 qb = *reinterpret_cast<const float4 *>(&qs[g][8 * j + 4]);
+                    acc[g] = __fmaf_rn(kf[0], qa.x, acc[g]);
+                    acc[g] = __fmaf_rn(kf[1], qa.y, acc[g]);
+                    acc[g] = __fmaf_rn(kf[2], qa.z, acc[g]);
+                    acc[g] = __fmaf_rn(kf[3], qa.w, acc[g]);
+                    acc[g] = __fmaf_rn(kf[4], qb.x, acc[g]);
+                    acc[g] = __fmaf_rn(kf[5], qb.y, acc[g]);
+                    acc[g] = __fmaf_rn(kf[6], qb.z, acc[g]);
+                    acc[g] = __fmaf_rn(kf[7], qb.w, acc[g]);
                 }
             }
 #pragma unroll
-            for (int k = 0; k < GPT; ++k) {
-                const float v = __fmul_rn(acc[k], a.scale);
-                sc[(size_t)(gh * GPT + k) * a.ncap + c] = v;
-                mx[k] = fmaxf(mx[k], v);
+            for (int g = 0; g < G; ++g) {
+                const float v = __fmul_rn(acc[g], a.scale);
+                sc[(size_t)g * a.ncap + c] = v;
+                mx[g] = fmaxf(mx[g], v);
             }
         }
     }
@@ -299,7 +307,7 @@ k_att_scores(const AttParams a) {
     const int lane = tid & 31, warp = tid >> 5;
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-        const float m = alb_warp_max(g / GPT == gh ? mx[g % GPT] : -INFINITY);
+        const float m = alb_warp_max(mx[g]);
         if (lane == 0) red[warp][g] = m;
     }
     __syncthreads();
@@ -316,6 +324,21 @@ __host__ __device__ constexpr size_t at_pv_stage() { return (size_t)AT_ST * 256 
 template <int G>
 __host__ __device__ constexpr size_t at_pv_smem() { return 2 * at_pv_stage<G>() + (size_t)G * AT_ST * 8; }
 
+// Lc + p[0] + p[1] + ... + p[n-1] in order (p[c] = pd[c * stride] * 2^-1008,
+// exact), the loads issued eight cells ahead of the dependent additions.
+__device__ __forceinline__ double at_psum(double Lc, const double * pd, int stride, int n) {
+    int c = 0;
+    for (; c + 8 <= n; c += 8) {
+        double t[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) t[u] = pd[(c + u) * stride] * 0x1p-1008;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) Lc += t[u];
+    }
+    for (; c < n; ++c) Lc += pd[c * stride] * 0x1p-1008;
+    return Lc;
+}
+
 static constexpr int AT_PV_THREADS = 160;   // warps 0-3: one thread per dimension; warp 4: the sums of p
 
 // Ordered double sum of n values at p[0], p[stride], ... (n >= 0), loads issued
@@ -331,6 +354,27 @@ __device__ __forceinline__ double at_ordered_sum(const double * __restrict__ p, 
             if (j0 + k < n) acc += t[k];
     }
     return acc;
+}
+
+// out[g] = ordered double sum over k < n of p[k * G * 129 + g * 129] for every
+// head g at once, loads issued eight partials (all heads) ahead.
+template <int G>
+__device__ __forceinline__ void at_ordered_sums(double (&out)[G], const double * __restrict__ p, int n) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) out[g] = 0.0;
+    for (int k0 = 0; k0 < n; k0 += 8) {
+        double t[8][G];
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+#pragma unroll
+            for (int g = 0; g < G; ++g)
+                t[k][g] = k0 + k < n ? __ldcg(p + (size_t)(k0 + k) * G * 129 + g * 129) : 0.0;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+            if (k0 + k < n)
+#pragma unroll
+                for (int g = 0; g < G; ++g) out[g] += t[k][g];
+    }
 }
 
 template <int G>
@@ -354,8 +398,13 @@ k_att_pv(const AttParams a) {
     const int64_t row = (int64_t)a.Hkv * 128;
     const uint16_t * vb = a.vc + (size_t)h * 128;
     const float * sc = a.scores + ((size_t)h * a.T + t) * G * a.ncap;
-    const size_t nchmax = (size_t)((a.ncap + AT_CHUNK - 1) / AT_CHUNK);
-    double * part = a.part + ((size_t)h * a.T + t) * nchmax * G * 129;
+    const size_t nspmax = (size_t)at_nsuper_max(a.ncap);
+    double * part = a.part + ((size_t)h * a.T + t) * nspmax * G * 129;
+    const int scn = at_scn(nch), nsp = at_nsuper(nch);
+    double Osp[G];   // this superchunk's running sums (chunk sums in order)
+    double Lsp = 0.0;
+#pragma unroll
+    for (int g = 0; g < G; ++g) Osp[g] = 0.0;
     // staging steps: AT_ST cells each, two per chunk, double-buffered
     const int cbeg = j0 * AT_CHUNK, cend = min(n, j1 * AT_CHUNK);
     const int nsteps = (cend - cbeg + AT_ST - 1) / AT_ST;
@@ -417,33 +466,54 @@ k_att_pv(const AttParams a) {
             for (int g = 0; g < G; ++g) {
                 double v = 0.0;
                 if (tid < rows) v = (double)alb_ref_expf(__fsub_rn(ss[g * AT_ST + tid], Ms[g])) * 0x1p1008;
-                pd[g * AT_ST + tid] = v;   // p * 2^1008, exact
+                pd[tid * G + g] = v;   // p * 2^1008, exact; [cell][head]
             }
         }
         __syncthreads();
         if (warp == 4) {
-            if (lane < G)   // the chunk's sum of p, cells in order
-                for (int c = 0; c < rows; ++c) Lc += pd[lane * AT_ST + c] * 0x1p-1008;
+            if (lane < G) Lc = at_psum(Lc, pd + lane, G, rows);   // the chunk's sum of p, cells in order
         } else {
             // O_g,d: cells in order; V bits enter as (v * 2^-1008) and p as
-            // (p * 2^1008), so fma(p', v', O) adds the exact product p * v
+            // (p * 2^1008), so fma(p', v', O) adds the exact product p * v.
+            // Four cells per step with their loads issued first.
             const uint16_t * vs = reinterpret_cast<const uint16_t *>(stg) + tid;
-            for (int c = 0; c < rows; ++c) {
+            int c = 0;
+            for (; c + 4 <= rows; c += 4) {
+                double vd[4], pp[4][G];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    vd[u] = alb_h2d_bits(vs[(c + u) * 128]);
+#pragma unroll
+                    for (int g = 0; g < G; ++g) pp[u][g] = pd[(c + u) * G + g];
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+#pragma unroll
+                    for (int g = 0; g < G; ++g) O[g] = fma(pp[u][g], vd[u], O[g]);
+            }
+            for (; c < rows; ++c) {
                 const double vd = alb_h2d_bits(vs[c * 128]);
 #pragma unroll
-                for (int g = 0; g < G; ++g) O[g] = fma(pd[g * AT_ST + c], vd, O[g]);
+                for (int g = 0; g < G; ++g) O[g] = fma(pd[c * G + g], vd, O[g]);
             }
         }
-        // chunk complete (every second step, or the split's last): its partial
+        // a chunk ends (every second step, or the split's last): its sums join
+        // the superchunk's; a superchunk ends: its partial is written
         const int j = (cb - j0 * AT_CHUNK) / AT_CHUNK + j0;
         if ((i & 1) == 1 || i == nsteps - 1) {
-            double * pj = part + (size_t)j * G * 129;
+            const bool send = (j + 1) % scn == 0 || j == nch - 1;
+            double * pj = part + (size_t)(j / scn) * G * 129;
             if (warp < 4) {
 #pragma unroll
-                for (int g = 0; g < G; ++g) { pj[g * 129 + tid] = O[g]; O[g] = 0.0; }
+                for (int g = 0; g < G; ++g) {
+                    Osp[g] += O[g];
+                    O[g] = 0.0;
+                    if (send) { pj[g * 129 + tid] = Osp[g]; Osp[g] = 0.0; }
+                }
             } else if (lane < G) {
-                pj[lane * 129 + 128] = Lc;
+                Lsp += Lc;
                 Lc = 0.0;
+                if (send) { pj[lane * 129 + 128] = Lsp; Lsp = 0.0; }
             }
         }
         __syncthreads();   // pd and buffer i & 1 consumed
@@ -458,10 +528,9 @@ k_att_pv(const AttParams a) {
     __threadfence();
     double Od[G];
     if (warp == 4) {
-        if (lane < G) Ls[lane] = at_ordered_sum(part + lane * 129 + 128, (size_t)G * 129, nch);
+        if (lane < G) Ls[lane] = at_ordered_sum(part + lane * 129 + 128, (size_t)G * 129, nsp);
     } else {
-#pragma unroll
-        for (int g = 0; g < G; ++g) Od[g] = at_ordered_sum(part + g * 129 + tid, (size_t)G * 129, nch);
+        at_ordered_sums<G>(Od, part + tid, nsp);
     }
     __syncthreads();
     if (warp < 4) {
@@ -518,6 +587,8 @@ static constexpr int CL_ST = 64;                         // cells per stage
 static constexpr int CL_KR = 2, CL_VR = 2;               // K / V ring stages
 static constexpr int CL_MAXC = 1024;                     // cells per CTA (scores kept in shared memory)
 static constexpr int CL_THREADS = 288;                   // warps 0-7: scores / P.V; warp 8: the sums of p
+
+static_assert(CL_CS * CL_MAXC <= AT_SUPER * AT_CHUNK, "cluster path: one chunk per superchunk");
 
 template <int G>
 __host__ __device__ constexpr size_t cl_smem() {
@@ -722,8 +793,9 @@ k_att_decode_cl(const AttParams a) {
     double Lc = 0.0;
 #pragma unroll
     for (int k = 0; k < HPT; ++k) O[k] = 0.0;
-    const size_t nchmax = (size_t)((a.ncap + AT_CHUNK - 1) / AT_CHUNK);
-    double * part = a.part + (size_t)h * nchmax * G * 129;
+    // ncap <= CL_CS * CL_MAXC = AT_SUPER chunks: one chunk per superchunk
+    const size_t nspmax = (size_t)at_nsuper_max(a.ncap);
+    double * part = a.part + (size_t)h * nspmax * G * 129;
     for (int i = 0; i < nst; ++i) {
         if (!alb_mbar_wait(&vfull[i % CL_VR], (uint32_t)((i / CL_VR) & 1))) {
             if (tid == 0) atomicExch(a.err, ALB_DEVERR_MBAR_TIMEOUT);
@@ -741,8 +813,7 @@ k_att_decode_cl(const AttParams a) {
         }
         __syncthreads();
         if (warp == 8) {
-            if (lane < G)   // the chunk's sum of p, cells in order
-                for (int c = 0; c < rows; ++c) Lc += pd[lane * CL_ST + c] * 0x1p-1008;
+            if (lane < G) Lc = at_psum(Lc, pd + lane * CL_ST, 1, rows);   // the chunk's sum of p, cells in order
         } else if (G >= 2 || gh == 0) {
             // V bits enter as (v * 2^-1008) and p as (p * 2^1008): fma adds the exact p * v
             const uint16_t * vs = reinterpret_cast<const uint16_t *>(vring + (size_t)(i % CL_VR) * CL_ST * 256) + d;

@@ -231,12 +231,24 @@ k_fa_prefill(const float * __restrict__ q, const uint16_t * __restrict__ kc, con
     if (tid < FP_R) Mrow[tid] = fmaxf(red_m[0][tid], red_m[1][tid]);
     // ---- pass 2: p, L and O (chunk partials: O in registers, L by row threads)
     const int r4 = (tid >> 4) * 4, d8 = (tid & 15) * 8;   // P.V tile of this thread
-    double O[4][8];
-    double Lc = 0.0, Lt = 0.0;                            // thread r < FP_R: row r's chunk and total sums
+    double O[4][8], Osp[4][8];                            // chunk sums, superchunk sums
+    double Lc = 0.0, Lsp = 0.0, Lt = 0.0;                 // thread r < FP_R: row r's chunk, superchunk, total
+    // per row: its chunks (of its own causal cells) and chunks per superchunk
+    // (the canonical order: chunk sums in order within superchunks of
+    // ceil(chunks / 64) chunks, superchunk sums in order)
+    int nch_u[4], scn_u[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        const int nr = p0 + t0 + (r4 + u) / G + 1;
+        nch_u[u] = (nr + 127) / 128;
+        scn_u[u] = nch_u[u] > 64 ? (nch_u[u] + 63) / 64 : 1;
+    }
+    const int nch_l = (p0 + t0 + (tid & (FP_R - 1)) / G + 1 + 127) / 128;
+    const int scn_l = nch_l > 64 ? (nch_l + 63) / 64 : 1;
 #pragma unroll
     for (int u = 0; u < 4; ++u)
 #pragma unroll
-        for (int e = 0; e < 8; ++e) { O[u][e] = 0.0; Otot[(r4 + u) * 128 + d8 + e] = 0.0; }
+        for (int e = 0; e < 8; ++e) { O[u][e] = 0.0; Osp[u][e] = 0.0; Otot[(r4 + u) * 128 + d8 + e] = 0.0; }
     issue(0, true);
     for (int i = 0; i < nst; ++i) {
         issue(i + 1, true);
@@ -277,12 +289,23 @@ k_fa_prefill(const float * __restrict__ q, const uint16_t * __restrict__ kc, con
                 for (int e = 0; e < 8; ++e) O[u][e] = fma(p, vd[e], O[u][e]);
             }
         }
-        if ((i & 1) == 1 || i == nst - 1) {   // a 128-cell chunk ends: add its partials in chunk order
+        if ((i & 1) == 1 || i == nst - 1) {   // a 128-cell chunk ends: its sums join the superchunk's
+            const int j = i >> 1;
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
+            for (int u = 0; u < 4; ++u) {
+                const bool send = (j + 1) % scn_u[u] == 0 || j == nch_u[u] - 1;
 #pragma unroll
-                for (int e = 0; e < 8; ++e) { Otot[(r4 + u) * 128 + d8 + e] += O[u][e]; O[u][e] = 0.0; }
-            if (tid < FP_R) { Lt += Lc; Lc = 0.0; }
+                for (int e = 0; e < 8; ++e) {
+                    Osp[u][e] += O[u][e];
+                    O[u][e] = 0.0;
+                    if (send) { Otot[(r4 + u) * 128 + d8 + e] += Osp[u][e]; Osp[u][e] = 0.0; }
+                }
+            }
+            if (tid < FP_R) {
+                Lsp += Lc;
+                Lc = 0.0;
+                if ((j + 1) % scn_l == 0 || j == nch_l - 1) { Lt += Lsp; Lsp = 0.0; }
+            }
         }
         __syncthreads();   // pd and buffer i & 1 consumed
     }

@@ -527,7 +527,7 @@ static void fa_range(void * pc, int64_t b, int64_t e) {
     float * VKQ32 = (float *)malloc(D * 4);
     float * Qf = (float *)malloc(D * 4);
     float * sc = (float *)malloc(f->nmax * 4);
-    double * Od = (double *)malloc((2 * D + (f->mode == 2 ? f->nmax : 0)) * sizeof(double));
+    double * Od = (double *)malloc((3 * D + (f->mode == 2 ? f->nmax : 0)) * sizeof(double));
     for (int64_t idx = b; idx < e; ++idx) {
         const int64_t t = idx / n_head, h = idx - t * n_head;
         const int64_t n_kv = f->kv_len[t];
@@ -541,7 +541,7 @@ static void fa_range(void * pc, int64_t b, int64_t e) {
                  * K/V): scores, exp and sums in double, one rounding at the end;
                  * the yardstick for the errors of modes 0 and 1 */
                 double M = -INFINITY;
-                double * sd = Od + 2 * D;   /* scratch of n_kv doubles after Od and Oc */
+                double * sd = Od + 3 * D;   /* scratch of n_kv doubles after Od, Oc and Os */
                 for (int64_t c = 0; c < n_kv; ++c) {
                     const uint16_t * kc = k + c * row + hk * D;
                     double a = 0.0;
@@ -570,12 +570,17 @@ static void fa_range(void * pc, int64_t b, int64_t e) {
                     M = sc[c] > M ? sc[c] : M;
                 }
                 /* chunked canonical order: cells in order within each ORC_FA_CHUNK-cell
-                 * chunk from 0, chunk sums added in chunk order from 0 (every p * v is
+                 * chunk from 0; chunk sums added in chunk order from 0 within each
+                 * superchunk of scn consecutive chunks (scn = 1 up to ORC_FA_SUPER
+                 * chunks); superchunk sums added in order from 0 (every p * v is
                  * exact in double; only the additions round) */
-                double L = 0.0;
-                double * Oc = Od + D;
-                for (int64_t d = 0; d < D; ++d) Od[d] = 0.0;
-                for (int64_t c0 = 0; c0 < n_kv; c0 += ORC_FA_CHUNK) {
+                const int64_t nch = (n_kv + ORC_FA_CHUNK - 1) / ORC_FA_CHUNK;
+                const int64_t scn = nch > ORC_FA_SUPER ? (nch + ORC_FA_SUPER - 1) / ORC_FA_SUPER : 1;
+                double L = 0.0, Ls = 0.0;
+                double * Oc = Od + D, * Os = Od + 2 * D;
+                for (int64_t d = 0; d < D; ++d) { Od[d] = 0.0; Os[d] = 0.0; }
+                for (int64_t j = 0; j < nch; ++j) {
+                    const int64_t c0 = j * ORC_FA_CHUNK;
                     const int64_t c1 = c0 + ORC_FA_CHUNK < n_kv ? c0 + ORC_FA_CHUNK : n_kv;
                     double Lc = 0.0;
                     for (int64_t d = 0; d < D; ++d) Oc[d] = 0.0;
@@ -585,8 +590,13 @@ static void fa_range(void * pc, int64_t b, int64_t e) {
                         Lc += (double)p;
                         for (int64_t d = 0; d < D; ++d) Oc[d] += (double)p * (double)orc_fp16_to_fp32(vc[d]);
                     }
-                    L += Lc;
-                    for (int64_t d = 0; d < D; ++d) Od[d] += Oc[d];
+                    Ls += Lc;
+                    for (int64_t d = 0; d < D; ++d) Os[d] += Oc[d];
+                    if ((j + 1) % scn == 0 || j == nch - 1) {   /* a superchunk ends */
+                        L += Ls;
+                        Ls = 0.0;
+                        for (int64_t d = 0; d < D; ++d) { Od[d] += Os[d]; Os[d] = 0.0; }
+                    }
                 }
                 for (int64_t d = 0; d < D; ++d) po[d] = L > 0.0 ? (float)(Od[d] / L) : 0.0f;
                 continue;

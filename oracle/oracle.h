@@ -107,6 +107,9 @@ void orc_gather_sum(const float * const * srcs, int n_srcs, float * dst, int64_t
  * mode 2: the same function in fp64 (scores, exp, sums), rounded once: the
  *         yardstick that modes 0 and 1 are measured against. */
 #define ORC_FA_CHUNK 128
+/* at most this many superchunks: a superchunk is ceil(chunks / ORC_FA_SUPER)
+ * consecutive chunks (one chunk up to 64 chunks = 8192 cells) */
+#define ORC_FA_SUPER 64
 void orc_flash_attn(const float * q, const uint16_t * k, const uint16_t * v, const int32_t * kv_len,
                     int64_t T, int64_t n_head, int64_t n_head_kv, int64_t D, float scale,
                     int mode, float * out);

@@ -152,6 +152,11 @@ def test_qk_norm_rope_kv(Hq, Hkv, T, pos0):
     (16, 8, 100, 37, 1),     # G = 2 tiles of 32 tokens after a cached prefix
     (8, 8, 70, 10, 1),       # G = 1 tiles of 64 tokens
     (64, 8, 20, 3, 1),       # G = 8 tiles of 8 tokens
+    # past 64 chunks (8192 cells) chunk sums are grouped in superchunks
+    (32, 8, 1, 20000, 74),   # 157 chunks: superchunks of 3, splits hold whole superchunks
+    (8, 2, 1, 32767, 296),   # 32768 cells: superchunks of 4
+    (8, 2, 40, 8170, 1),     # prefill tile whose rows straddle 64 chunks (superchunks of 1 and 2)
+    (8, 2, 3, 8190, 8),      # split call, tokens on both sides of 8192 cells
 ])
 def test_flash_attn(Hq, Hkv, T, pos0, S):
     rng = np.random.default_rng(Hq + T + pos0)
