@@ -319,10 +319,11 @@ k_att_scores(const AttParams a) {
 }
 
 // --------------------------------------------------------------- P.V + merge
+static constexpr int AT_PVR = 2;   // V / score stages in k_att_pv's ring (AT_PVR - 1 ahead; deeper rings measured slower)
 template <int G>
 __host__ __device__ constexpr size_t at_pv_stage() { return (size_t)AT_ST * 256 + (size_t)G * AT_ST * 4; }
 template <int G>
-__host__ __device__ constexpr size_t at_pv_smem() { return 2 * at_pv_stage<G>() + (size_t)G * AT_ST * 8; }
+__host__ __device__ constexpr size_t at_pv_smem() { return AT_PVR * at_pv_stage<G>() + (size_t)G * AT_ST * 8; }
 
 // Lc + p[0] + p[1] + ... + p[n-1] in order (p[c] = pd[c * stride] * 2^-1008,
 // exact), the loads issued eight cells ahead of the dependent additions.
@@ -381,7 +382,7 @@ template <int G>
 __global__ void __launch_bounds__(AT_PV_THREADS)
 k_att_pv(const AttParams a) {
     extern __shared__ __align__(16) uint8_t at_sm[];   // 2 x (V rows [AT_ST][256 B] + scores [G][AT_ST]), p [G][AT_ST]
-    double * pd = reinterpret_cast<double *>(at_sm + 2 * at_pv_stage<G>());
+    double * pd = reinterpret_cast<double *>(at_sm + AT_PVR * at_pv_stage<G>());
     __shared__ float Ms[G];
     __shared__ float redm[4][G];
     __shared__ double Ls[G];
@@ -401,17 +402,19 @@ k_att_pv(const AttParams a) {
     const size_t nspmax = (size_t)at_nsuper_max(a.ncap);
     double * part = a.part + ((size_t)h * a.T + t) * nspmax * G * 129;
     const int scn = at_scn(nch), nsp = at_nsuper(nch);
-    double Osp[G];   // this superchunk's running sums (chunk sums in order)
+    double Osp[2][G];   // this superchunk's running sums (chunk sums in order)
     double Lsp = 0.0;
 #pragma unroll
-    for (int g = 0; g < G; ++g) Osp[g] = 0.0;
+    for (int e = 0; e < 2; ++e)
+#pragma unroll
+        for (int g = 0; g < G; ++g) Osp[e][g] = 0.0;
     // staging steps: AT_ST cells each, two per chunk, double-buffered
     const int cbeg = j0 * AT_CHUNK, cend = min(n, j1 * AT_CHUNK);
     const int nsteps = (cend - cbeg + AT_ST - 1) / AT_ST;
     // V rows of step i with cells in [lo, hi) and / or its scores
     auto issue_v = [&](int i, int lo, int hi) {
         const int cb = cbeg + i * AT_ST, rows = min(AT_ST, cend - cb);
-        uint8_t * dst = at_sm + (i & 1) * at_pv_stage<G>();
+        uint8_t * dst = at_sm + (i % AT_PVR) * at_pv_stage<G>();
         for (int p = tid; p < rows * 16; p += AT_PV_THREADS) {
             const int r = p >> 4, j = p & 15;
             if (cb + r >= lo && cb + r < hi) at_cp16(dst + r * 256 + j * 16, vb + (size_t)(cb + r) * row + j * 8);
@@ -419,7 +422,7 @@ k_att_pv(const AttParams a) {
     };
     auto issue_s = [&](int i) {
         const int cb = cbeg + i * AT_ST, rows = min(AT_ST, cend - cb);
-        float * sdst = reinterpret_cast<float *>(at_sm + (i & 1) * at_pv_stage<G>() + AT_ST * 256);
+        float * sdst = reinterpret_cast<float *>(at_sm + (i % AT_PVR) * at_pv_stage<G>() + AT_ST * 256);
         for (int p = tid; p < rows * G; p += AT_PV_THREADS) {
             const int g = p / rows, c = p - g * rows;
             at_cp4(sdst + g * AT_ST + c, sc + (size_t)g * a.ncap + cb + c);
@@ -428,14 +431,20 @@ k_att_pv(const AttParams a) {
     // The cached cells' V (all but the new cell n - 1, which the score kernel of
     // a decode step stores) before waiting on the score kernel.
     const int n_old = a.qkv ? n - 1 : 0;   // fused decode call: cells < n - 1 are stable
-    if (nsteps > 0) issue_v(0, 0, n_old);
-    at_commit();
-    alb_pdl_wait();   // the scores, maxima (and the new V cell) come from k_att_scores
-    if (nsteps > 0) {
-        issue_v(0, n_old, n);
-        issue_s(0);
+#pragma unroll
+    for (int k = 0; k < AT_PVR - 1; ++k) {
+        if (k < nsteps) issue_v(k, 0, n_old);
+        at_commit();
     }
-    at_commit();
+    alb_pdl_wait();   // the scores, maxima (and the new V cell) come from k_att_scores
+#pragma unroll
+    for (int k = 0; k < AT_PVR - 1; ++k) {
+        if (k < nsteps) {
+            issue_v(k, n_old, n);
+            issue_s(k);
+        }
+        at_commit();
+    }
     {   // global maxima over the splits' maxima (max is exact: any order)
         float m = -INFINITY;
         if (tid < 128) {
@@ -449,16 +458,23 @@ k_att_pv(const AttParams a) {
     }
     __syncthreads();
     if (tid < G) Ms[tid] = fmaxf(fmaxf(redm[0][tid], redm[1][tid]), fmaxf(redm[2][tid], redm[3][tid]));
-    double O[G];
+    // O: threads t < 64 hold dimensions 2t, 2t + 1 of every head (one 32-bit V
+    // load and one conversion per value serve G double fmas)
+    double O[2][G];
     double Lc = 0.0;   // warp 4, lane g < G: the chunk's sum of p for query head g
 #pragma unroll
-    for (int g = 0; g < G; ++g) O[g] = 0.0;
+    for (int e = 0; e < 2; ++e)
+#pragma unroll
+        for (int g = 0; g < G; ++g) O[e][g] = 0.0;
     for (int i = 0; i < nsteps; ++i) {
-        if (i + 1 < nsteps) { issue_v(i + 1, 0, n); issue_s(i + 1); }
+        if (i + AT_PVR - 1 < nsteps) { issue_v(i + AT_PVR - 1, 0, n); issue_s(i + AT_PVR - 1); }
         at_commit();
-        at_wait<1>();
+        // commit groups: V of stages 0..R-2 (before the wait), then V + scores of
+        // stages 0..R-2, then one per loop stage: stage i is complete when at
+        // most R - 1 groups are pending
+        at_wait<AT_PVR - 1>();
         __syncthreads();   // step i visible; Ms visible; pd free
-        const uint8_t * stg = at_sm + (i & 1) * at_pv_stage<G>();
+        const uint8_t * stg = at_sm + (i % AT_PVR) * at_pv_stage<G>();
         const int cb = cbeg + i * AT_ST, rows = min(AT_ST, cend - cb);
         if (tid < AT_ST) {
             const float * ss = reinterpret_cast<const float *>(stg + AT_ST * 256);
@@ -472,29 +488,38 @@ k_att_pv(const AttParams a) {
         __syncthreads();
         if (warp == 4) {
             if (lane < G) Lc = at_psum(Lc, pd + lane, G, rows);   // the chunk's sum of p, cells in order
-        } else {
+        } else if (tid < 64) {
             // O_g,d: cells in order; V bits enter as (v * 2^-1008) and p as
             // (p * 2^1008), so fma(p', v', O) adds the exact product p * v.
-            // Four cells per step with their loads issued first.
-            const uint16_t * vs = reinterpret_cast<const uint16_t *>(stg) + tid;
+            // Two cells per step with their loads issued first.
+            const uint32_t * vs = reinterpret_cast<const uint32_t *>(stg) + tid;   // dims 2 tid, 2 tid + 1
             int c = 0;
-            for (; c + 4 <= rows; c += 4) {
-                double vd[4], pp[4][G];
+            for (; c + 2 <= rows; c += 2) {
+                double vd[2][2], pp[2][G];
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    vd[u] = alb_h2d_bits(vs[(c + u) * 128]);
+                for (int u = 0; u < 2; ++u) {
+                    const uint32_t w = vs[(c + u) * 64];
+                    vd[u][0] = alb_h2d_bits(w & 0xFFFFu);
+                    vd[u][1] = alb_h2d_bits(w >> 16);
 #pragma unroll
                     for (int g = 0; g < G; ++g) pp[u][g] = pd[(c + u) * G + g];
                 }
 #pragma unroll
-                for (int u = 0; u < 4; ++u)
+                for (int u = 0; u < 2; ++u)
 #pragma unroll
-                    for (int g = 0; g < G; ++g) O[g] = fma(pp[u][g], vd[u], O[g]);
+                    for (int e = 0; e < 2; ++e)
+#pragma unroll
+                        for (int g = 0; g < G; ++g) O[e][g] = fma(pp[u][g], vd[u][e], O[e][g]);
             }
             for (; c < rows; ++c) {
-                const double vd = alb_h2d_bits(vs[c * 128]);
+                const uint32_t w = vs[c * 64];
+                const double v0 = alb_h2d_bits(w & 0xFFFFu), v1 = alb_h2d_bits(w >> 16);
 #pragma unroll
-                for (int g = 0; g < G; ++g) O[g] = fma(pd[c * G + g], vd, O[g]);
+                for (int g = 0; g < G; ++g) {
+                    const double pg = pd[c * G + g];
+                    O[0][g] = fma(pg, v0, O[0][g]);
+                    O[1][g] = fma(pg, v1, O[1][g]);
+                }
             }
         }
         // a chunk ends (every second step, or the split's last): its sums join
@@ -503,14 +528,16 @@ k_att_pv(const AttParams a) {
         if ((i & 1) == 1 || i == nsteps - 1) {
             const bool send = (j + 1) % scn == 0 || j == nch - 1;
             double * pj = part + (size_t)(j / scn) * G * 129;
-            if (warp < 4) {
+            if (tid < 64) {
 #pragma unroll
-                for (int g = 0; g < G; ++g) {
-                    Osp[g] += O[g];
-                    O[g] = 0.0;
-                    if (send) { pj[g * 129 + tid] = Osp[g]; Osp[g] = 0.0; }
-                }
-            } else if (lane < G) {
+                for (int e = 0; e < 2; ++e)
+#pragma unroll
+                    for (int g = 0; g < G; ++g) {
+                        Osp[e][g] += O[e][g];
+                        O[e][g] = 0.0;
+                        if (send) { pj[g * 129 + 2 * tid + e] = Osp[e][g]; Osp[e][g] = 0.0; }
+                    }
+            } else if (warp == 4 && lane < G) {
                 Lsp += Lc;
                 Lc = 0.0;
                 if (send) { pj[lane * 129 + 128] = Lsp; Lsp = 0.0; }
