@@ -350,9 +350,21 @@ def cpu_prefill_baseline(cfg, n_tokens=48):
 
 
 # DRAM bytes (read + write) per mat-vec launch of the decode step, mean over the
-# step's launches, from an ncu capture; None until captured
-DECODE_MV_TRAFFIC = None
-DECODE_MV_TRAFFIC_SRC = "ncu dram__bytes_read.sum + dram__bytes_write.sum, mean over one decode step's k_mv launches"
+# step's 145 launches: each launch's ncu figure (profiles/k_mv_qwen3_4b_decode.md,
+# a 4-layer model of the same shapes; every layer reads the same bytes)
+DECODE_MV_TRAFFIC = 15.67e6
+DECODE_MV_TRAFFIC_SRC = ("ncu dram__bytes_read.sum + dram__bytes_write.sum per k_mv launch (4-layer case), "
+                         "mean over the 145 launches of the 36-layer step")
+
+
+def profile_cfg(cfg, args):
+    """The workload's model, or (--n-layer) the same shapes with fewer layers:
+    the same kernels on a few hundred MB, for ncu captures."""
+    return dict(cfg, n_layer=args.n_layer) if args.n_layer > 0 else cfg
+
+
+def profile_tag(args):
+    return f"_profile_case_{args.n_layer}_layers" if args.n_layer > 0 else ""
 
 
 def run_decode(args, rank, world):
@@ -362,7 +374,7 @@ def run_decode(args, rank, world):
     from arclight_b200.configs import QWEN3_4B
     from arclight_b200.engine import Engine, nccl_unique_id
 
-    cfg = QWEN3_4B
+    cfg = profile_cfg(QWEN3_4B, args)
     L = A.lib()
     local = int(os.environ.get("LOCAL_RANK", 0))
     torch.cuda.set_device(local)
@@ -425,7 +437,7 @@ def run_decode(args, rank, world):
         "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": DTYPE_DECODE,
         "data": "synthetic: seeded random-init Qwen3-4B-shaped weights (device-generated), uniform random prompt",
-        "config": {"workload": "config3_decode_qwen3_4b", "prompt": n_prompt, "decode_steps": n_gen,
+        "config": {"workload": "config3_decode_qwen3_4b" + profile_tag(args), "prompt": n_prompt, "decode_steps": n_gen,
                    "parallelism": f"tp{world}", "global_batch": 1,
                    "l2": "inputs larger than L2 (2.26 GB of weights per token)",
                    "launches_per_token": info["launches_per_step"], "attn_splits": info["attn_splits"]},
@@ -453,8 +465,9 @@ LONG_CTX = 32768
 # ----------------------------------------------------------------- attention alone (config 5 shape)
 ATT_HQ, ATT_HKV, ATT_CELLS, ATT_COPIES = 32, 8, 32768, 4
 ATT_BYTES = 2 * ATT_CELLS * ATT_HKV * 128 * 2 + 2 * ATT_HQ * 128 * 4   # K + V + q + out per call
-# DRAM bytes (read + write) per call from an ncu capture of its two kernels; None until captured
-ATT_TRAFFIC = None
+# DRAM bytes (read + write) per call: ncu figures of its two kernels
+# (profiles/k_att_split_config5_attention.md: scores 67.95 MB, P.V 72.40 MB)
+ATT_TRAFFIC = 140.35e6
 
 
 def cpu_attn_baseline(seconds: float = 10.0):
@@ -660,7 +673,7 @@ def run_prefill(args, rank, world):
     from arclight_b200.engine import Engine, nccl_unique_id
     import ctypes as C
 
-    cfg = QWEN3_4B
+    cfg = profile_cfg(QWEN3_4B, args)
     L = A.lib()
     local = int(os.environ.get("LOCAL_RANK", 0))
     torch.cuda.set_device(local)
@@ -708,7 +721,7 @@ def run_prefill(args, rank, world):
         "ms_per_step": ms, "ttft_ms": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "q4_0 x q8_0 int8 tensor cores (tcgen05 kind::i8), the reference's fp32 block chain, fp16 KV",
         "data": "synthetic: seeded random-init Qwen3-4B-shaped weights, uniform random prompt",
-        "config": {"workload": "config4_prefill_qwen3_4b", "prompt": T, "parallelism": f"tp{world}",
+        "config": {"workload": "config4_prefill_qwen3_4b" + profile_tag(args), "prompt": T, "parallelism": f"tp{world}",
                    "global_batch": 1, "l2": "inputs larger than L2 (2.26 GB of weights per prefill)",
                    "launches_per_prefill": info["launches_per_step"]},
         "roofline": {"bound": "tensor", "achieved": tops, "peak": INT8_PEAK_TOPS, "unit": "TOP/s",
@@ -732,6 +745,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="decode", choices=["decode", "gemv", "prefill", "long", "attn"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--n-layer", type=int, default=0,
+                    help="decode/prefill with this many layers: a small case for ncu captures, not a bench value")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.steps is None:
