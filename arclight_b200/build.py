@@ -16,6 +16,10 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 OBJ = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libalb_cuda.so")
+APPS = os.path.join(PKG, "apps")
+SHIM = os.path.join(PKG, "libalb_nnml_ops.so")      # nnml-shaped operator shim over the C ABI
+AL_BENCH = os.path.join(PKG, "al_bench")            # C++ driver of the engine (al-gen's flow)
+CXX = os.environ.get("CXX", shutil.which("g++") or "g++")
 NVCC = os.environ.get("NVCC", shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -52,20 +56,49 @@ def build(verbose: bool = False) -> str:
     srcs = sources()
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 4)) as ex:
         objs = list(ex.map(lambda s: compile_one(s, hdr_t), srcs))
-    if os.path.exists(LIB) and os.path.getmtime(LIB) > max(os.path.getmtime(o) for o in objs):
-        return LIB
-    cmd = [NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-lcuda", "-ldl", "-lpthread"]
-    r = subprocess.run(cmd, capture_output=True, text=True)
-    if r.returncode != 0:
-        raise RuntimeError("link failed:\n" + r.stderr)
-    if verbose:
-        print("built", LIB)
+    if not (os.path.exists(LIB) and os.path.getmtime(LIB) > max(os.path.getmtime(o) for o in objs)):
+        cmd = [NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-lcuda", "-ldl", "-lpthread"]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError("link failed:\n" + r.stderr)
+        if verbose:
+            print("built", LIB)
+    build_apps(verbose)
     return LIB
+
+
+def _stale(out: str, deps) -> bool:
+    return not os.path.exists(out) or os.path.getmtime(out) < max(os.path.getmtime(d) for d in deps)
+
+
+def build_apps(verbose: bool = False) -> None:
+    """Host C++ on top of the C ABI: the nnml operator shim (a shared library)
+    and the al_bench driver, both linked against the in-tree libalb_cuda.so."""
+    inc = ["-I" + os.path.join(ROOT, "include"), "-I" + APPS]
+    link = ["-L" + PKG, "-lalb_cuda", "-Wl,-rpath,$ORIGIN"]
+    hdr = os.path.join(ROOT, "include", "alb_cuda.h")
+    shim_src = [os.path.join(APPS, "nnml_gpu_ops.cpp"), os.path.join(APPS, "nnml_gpu_ops.h")]
+    if _stale(SHIM, shim_src + [hdr, LIB]):
+        cmd = [CXX, "-O2", "-std=c++17", "-fPIC", "-shared", "-fvisibility=hidden", *inc, shim_src[0], "-o", SHIM, *link]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError("nnml shim build failed:\n" + r.stderr)
+        if verbose:
+            print("built", SHIM)
+    bench_src = os.path.join(APPS, "al_bench.cpp")
+    if _stale(AL_BENCH, [bench_src, hdr, LIB]):
+        cmd = [CXX, "-O2", "-std=c++17", "-pthread", *inc, bench_src, "-o", AL_BENCH, *link]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError("al_bench build failed:\n" + r.stderr)
+        if verbose:
+            print("built", AL_BENCH)
 
 
 if __name__ == "__main__":
     if "--clean" in sys.argv:
         shutil.rmtree(OBJ, ignore_errors=True)
-        if os.path.exists(LIB):
-            os.remove(LIB)
+        for f in (LIB, SHIM, AL_BENCH):
+            if os.path.exists(f):
+                os.remove(f)
     build(verbose=True)

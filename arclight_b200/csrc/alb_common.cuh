@@ -163,6 +163,22 @@ __device__ __forceinline__ bool alb_mbar_wait_backoff(uint64_t * bar, uint32_t p
         if (alb_globaltimer() - t0 > ns) return false;
     }
 }
+// Bounded wait that naps between polls (__nanosleep, doubling from 32 ns up to
+// max_nap ns): a waiting warp issues a handful of instructions per nap instead
+// of polling back to back, leaving the issue slots to the warps that work.
+// Gives up after `ns` nanoseconds of %globaltimer (default 2 s).
+__device__ __forceinline__ bool alb_mbar_wait_nap(uint64_t * bar, uint32_t parity, uint32_t max_nap,
+                                                  uint64_t ns = 2000000000ull) {
+    if (alb_mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = alb_globaltimer();
+    uint32_t nap = 32;
+    for (;;) {
+        __nanosleep(nap);
+        if (alb_mbar_try_wait(bar, parity)) return true;
+        if (nap < max_nap) nap <<= 1;
+        if (alb_globaltimer() - t0 > ns) return false;
+    }
+}
 // 1-D bulk copy global -> shared, completion counted on `bar` (16-byte aligned, size % 16 == 0).
 __device__ __forceinline__ void alb_bulk_g2s(void * dst_smem, const void * src, uint32_t bytes, uint64_t * bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"

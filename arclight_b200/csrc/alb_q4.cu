@@ -351,7 +351,7 @@ k_mv(const GemvArgs a, const MvPlan p) {
             int g = 0;
             for (; g < nst; ++g) {
                 const int slot = g % p.ns;
-                if (g >= p.ns && !alb_mbar_wait(&empty[slot], (uint32_t)((g / p.ns - 1) & 1))) {
+                if (g >= p.ns && !alb_mbar_wait_nap(&empty[slot], (uint32_t)((g / p.ns - 1) & 1), 256)) {
                     atomicExch(a.err, ALB_DEVERR_MBAR_TIMEOUT);
                     s_abort = 1;
                     break;
@@ -412,8 +412,8 @@ k_mv(const GemvArgs a, const MvPlan p) {
         for (int g = 0; g < nst; ++g) {
             const int slot = g % p.ns, cbi = g % p.ncb;
             if (*reinterpret_cast<volatile int *>(&s_abort)) break;
-            bool ok = alb_mbar_wait(&full[slot], (uint32_t)((g / p.ns) & 1));
-            if (ok && g >= p.ncb) ok = alb_mbar_wait(&freeb[cbi], (uint32_t)((g / p.ncb - 1) & 1));
+            bool ok = alb_mbar_wait_nap(&full[slot], (uint32_t)((g / p.ns) & 1), 128);
+            if (ok && g >= p.ncb) ok = alb_mbar_wait_nap(&freeb[cbi], (uint32_t)((g / p.ncb - 1) & 1), 128);
             if (!ok) {
                 if (lane == 0) atomicExch(a.err, ALB_DEVERR_MBAR_TIMEOUT);
                 s_abort = 1;
@@ -489,7 +489,7 @@ k_mv(const GemvArgs a, const MvPlan p) {
     for (int g = cw; g < nst; g += MV_CH) {
         const int cbi = g % p.ncb;
         if (*reinterpret_cast<volatile int *>(&s_abort)) break;
-        if (!alb_mbar_wait(&done[cbi], (uint32_t)((g / p.ncb) & 1))) {
+        if (!alb_mbar_wait_nap(&done[cbi], (uint32_t)((g / p.ncb) & 1), 256)) {
             if (lane == 0) atomicExch(a.err, ALB_DEVERR_MBAR_TIMEOUT);
             s_abort = 1;
             break;
