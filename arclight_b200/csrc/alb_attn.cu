@@ -8,13 +8,15 @@
 // Semantics (the oracle's attention mode 0; independent of the split count):
 // Q rounded to fp16 (arm.cpp:2307); score s_c = sequential fp32 fma chain over
 // d of K.Q, times scale; M = max_c s_c; p_c = v_expf(s_c - M) (the reference's
-// NEON exp, arm.cpp:1757-1787); L and every O_d are double sums in a canonical
-// order: cells in order within chunks of AT_CHUNK cells, chunk sums added in
-// chunk order; out = O / L.  Every p * v is exact in double, so only the
-// additions round, and they are the same additions on any GPU split.  Softmax
-// is shift invariant: this is the reference's function with fp32/fp64
-// arithmetic in place of its fp16 accumulators (within 1e-5 of an fp64
-// attention, while the reference's own fp16 rounding is 1e-3 .. 5e-2 from it).
+// NEON exp, arm.cpp:1757-1787); L and every O_d in a canonical order: within
+// each chunk of AT_CHUNK cells, cells in order in fp32 (L_c = L_c + p,
+// O_c = fmaf(p, v, O_c)); the chunk sums widened to double and added in chunk
+// order (in superchunks past AT_SUPER chunks); out = O / L.  These are the same
+// operations on any GPU split.  Softmax is shift invariant: this is the
+// reference's function with fp32/fp64 arithmetic in place of its fp16
+// accumulators (within 1e-6 of an fp64 attention, while the reference's own
+// fp16 rounding is 1e-3 .. 5e-2 from it).  fp32 chains inside a chunk keep the
+// P.V on the fp32 pipe: B200 issues fp64 fmas at about a quarter of that rate.
 //
 // Two launches:
 //   k_att_scores  CTA (kv head h, token t, split s): scores of the split's
@@ -325,18 +327,19 @@ __host__ __device__ constexpr size_t at_pv_stage() { return (size_t)AT_ST * 256 
 template <int G>
 __host__ __device__ constexpr size_t at_pv_smem() { return AT_PVR * at_pv_stage<G>() + (size_t)G * AT_ST * 8; }
 
-// Lc + p[0] + p[1] + ... + p[n-1] in order (p[c] = pd[c * stride] * 2^-1008,
-// exact), the loads issued eight cells ahead of the dependent additions.
-__device__ __forceinline__ double at_psum(double Lc, const double * pd, int stride, int n) {
+// Lc + p[0] + p[stride] + ... + p[(n-1) stride] in order, in fp32 (a chunk's
+// sum of p in the canonical order), the loads issued eight cells ahead of the
+// dependent additions.
+__device__ __forceinline__ float at_psum(float Lc, const float * p, int stride, int n) {
     int c = 0;
     for (; c + 8 <= n; c += 8) {
-        double t[8];
+        float t[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) t[u] = pd[(c + u) * stride] * 0x1p-1008;
+        for (int u = 0; u < 8; ++u) t[u] = p[(c + u) * stride];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) Lc += t[u];
+        for (int u = 0; u < 8; ++u) Lc = __fadd_rn(Lc, t[u]);
     }
-    for (; c < n; ++c) Lc += pd[c * stride] * 0x1p-1008;
+    for (; c < n; ++c) Lc = __fadd_rn(Lc, p[c * stride]);
     return Lc;
 }
 
@@ -382,7 +385,7 @@ template <int G>
 __global__ void __launch_bounds__(AT_PV_THREADS)
 k_att_pv(const AttParams a) {
     extern __shared__ __align__(16) uint8_t at_sm[];   // 2 x (V rows [AT_ST][256 B] + scores [G][AT_ST]), p [G][AT_ST]
-    double * pd = reinterpret_cast<double *>(at_sm + AT_PVR * at_pv_stage<G>());
+    float * pf = reinterpret_cast<float *>(at_sm + AT_PVR * at_pv_stage<G>());   // p of the step, [cell][head]
     __shared__ float Ms[G];
     __shared__ float redm[4][G];
     __shared__ double Ls[G];
@@ -460,12 +463,12 @@ k_att_pv(const AttParams a) {
     if (tid < G) Ms[tid] = fmaxf(fmaxf(redm[0][tid], redm[1][tid]), fmaxf(redm[2][tid], redm[3][tid]));
     // O: threads t < 64 hold dimensions 2t, 2t + 1 of every head (one 32-bit V
     // load and one conversion per value serve G double fmas)
-    double O[2][G];
-    double Lc = 0.0;   // warp 4, lane g < G: the chunk's sum of p for query head g
+    float O[2][G];
+    float Lc = 0.0f;   // warp 4, lane g < G: the chunk's sum of p for query head g
 #pragma unroll
     for (int e = 0; e < 2; ++e)
 #pragma unroll
-        for (int g = 0; g < G; ++g) O[e][g] = 0.0;
+        for (int g = 0; g < G; ++g) O[e][g] = 0.0f;
     for (int i = 0; i < nsteps; ++i) {
         if (i + AT_PVR - 1 < nsteps) { issue_v(i + AT_PVR - 1, 0, n); issue_s(i + AT_PVR - 1); }
         at_commit();
@@ -473,52 +476,52 @@ k_att_pv(const AttParams a) {
         // stages 0..R-2, then one per loop stage: stage i is complete when at
         // most R - 1 groups are pending
         at_wait<AT_PVR - 1>();
-        __syncthreads();   // step i visible; Ms visible; pd free
+        __syncthreads();   // step i visible; Ms visible; pf free
         const uint8_t * stg = at_sm + (i % AT_PVR) * at_pv_stage<G>();
         const int cb = cbeg + i * AT_ST, rows = min(AT_ST, cend - cb);
         if (tid < AT_ST) {
             const float * ss = reinterpret_cast<const float *>(stg + AT_ST * 256);
 #pragma unroll
             for (int g = 0; g < G; ++g) {
-                double v = 0.0;
-                if (tid < rows) v = (double)alb_ref_expf(__fsub_rn(ss[g * AT_ST + tid], Ms[g])) * 0x1p1008;
-                pd[tid * G + g] = v;   // p * 2^1008, exact; [cell][head]
+                float v = 0.0f;
+                if (tid < rows) v = alb_ref_expf(__fsub_rn(ss[g * AT_ST + tid], Ms[g]));
+                pf[tid * G + g] = v;
             }
         }
         __syncthreads();
         if (warp == 4) {
-            if (lane < G) Lc = at_psum(Lc, pd + lane, G, rows);   // the chunk's sum of p, cells in order
+            if (lane < G) Lc = at_psum(Lc, pf + lane, G, rows);   // the chunk's sum of p, cells in order
         } else if (tid < 64) {
-            // O_g,d: cells in order; V bits enter as (v * 2^-1008) and p as
-            // (p * 2^1008), so fma(p', v', O) adds the exact product p * v.
-            // Two cells per step with their loads issued first.
+            // O_g,d = fmaf(p, v, O_g,d), cells in order (fp32, the canonical
+            // within-chunk order).  Four cells per step with their loads issued first.
             const uint32_t * vs = reinterpret_cast<const uint32_t *>(stg) + tid;   // dims 2 tid, 2 tid + 1
             int c = 0;
-            for (; c + 2 <= rows; c += 2) {
-                double vd[2][2], pp[2][G];
+            for (; c + 4 <= rows; c += 4) {
+                float2 vf[4];
+                float pp[4][G];
 #pragma unroll
-                for (int u = 0; u < 2; ++u) {
+                for (int u = 0; u < 4; ++u) {
                     const uint32_t w = vs[(c + u) * 64];
-                    vd[u][0] = alb_h2d_bits(w & 0xFFFFu);
-                    vd[u][1] = alb_h2d_bits(w >> 16);
+                    vf[u] = __half22float2(*reinterpret_cast<const __half2 *>(&w));
 #pragma unroll
-                    for (int g = 0; g < G; ++g) pp[u][g] = pd[(c + u) * G + g];
+                    for (int g = 0; g < G; ++g) pp[u][g] = pf[(c + u) * G + g];
                 }
 #pragma unroll
-                for (int u = 0; u < 2; ++u)
+                for (int u = 0; u < 4; ++u)
 #pragma unroll
-                    for (int e = 0; e < 2; ++e)
-#pragma unroll
-                        for (int g = 0; g < G; ++g) O[e][g] = fma(pp[u][g], vd[u][e], O[e][g]);
+                    for (int g = 0; g < G; ++g) {
+                        O[0][g] = __fmaf_rn(pp[u][g], vf[u].x, O[0][g]);
+                        O[1][g] = __fmaf_rn(pp[u][g], vf[u].y, O[1][g]);
+                    }
             }
             for (; c < rows; ++c) {
                 const uint32_t w = vs[c * 64];
-                const double v0 = alb_h2d_bits(w & 0xFFFFu), v1 = alb_h2d_bits(w >> 16);
+                const float2 v = __half22float2(*reinterpret_cast<const __half2 *>(&w));
 #pragma unroll
                 for (int g = 0; g < G; ++g) {
-                    const double pg = pd[c * G + g];
-                    O[0][g] = fma(pg, v0, O[0][g]);
-                    O[1][g] = fma(pg, v1, O[1][g]);
+                    const float pg = pf[c * G + g];
+                    O[0][g] = __fmaf_rn(pg, v.x, O[0][g]);
+                    O[1][g] = __fmaf_rn(pg, v.y, O[1][g]);
                 }
             }
         }
@@ -533,17 +536,17 @@ k_att_pv(const AttParams a) {
                 for (int e = 0; e < 2; ++e)
 #pragma unroll
                     for (int g = 0; g < G; ++g) {
-                        Osp[e][g] += O[e][g];
-                        O[e][g] = 0.0;
+                        Osp[e][g] += (double)O[e][g];
+                        O[e][g] = 0.0f;
                         if (send) { pj[g * 129 + 2 * tid + e] = Osp[e][g]; Osp[e][g] = 0.0; }
                     }
             } else if (warp == 4 && lane < G) {
-                Lsp += Lc;
-                Lc = 0.0;
+                Lsp += (double)Lc;
+                Lc = 0.0f;
                 if (send) { pj[lane * 129 + 128] = Lsp; Lsp = 0.0; }
             }
         }
-        __syncthreads();   // pd and buffer i & 1 consumed
+        __syncthreads();   // pf and buffer i & 1 consumed
     }
     at_wait<0>();
     // the last CTA of (h, t) adds every chunk's partial in chunk order
@@ -602,10 +605,12 @@ k_att_pv(const AttParams a) {
 //   2. scores of the CTA's cells into shared memory, per-head maxima;
 //   3. cluster barrier; the global maxima read from every CTA's shared memory
 //      (DSMEM), so no workspace round trip and no second launch;
-//   4. p, and per 128-cell chunk the ordered double sums of p and p * v, to
-//      the workspace;
+//   4. p, and per 128-cell chunk the ordered fp32 sums of p and p * v, kept in
+//      shared memory (the K ring's region);
 //   5. cluster barrier; each CTA merges whole 32-dimension output blocks
-//      (chunk partials in chunk order), writes them and their Q8_0 records.
+//      (chunk partials, read through DSMEM, added in double in chunk order),
+//      writes them and their Q8_0 records; a last cluster barrier keeps every
+//      CTA's partials alive until all reads are done.
 // K and V stages of cached cells are streamed before the dependency wait.
 // Every wait on a stage is bounded (error word set, results then invalid);
 // every CTA takes both cluster barriers.  Cells per CTA <= CL_MAXC.
@@ -617,9 +622,16 @@ static constexpr int CL_THREADS = 288;                   // warps 0-7: scores / 
 
 static_assert(CL_CS * CL_MAXC <= AT_SUPER * AT_CHUNK, "cluster path: one chunk per superchunk");
 
+// The K ring's region holds the CTA's chunk partials (O and L of each head,
+// [chunk][G][129] doubles) once the scores are done.
+template <int G>
+__host__ __device__ constexpr size_t cl_kregion() {
+    return (size_t)CL_KR * CL_ST * AT_KPITCH > (size_t)(CL_MAXC / AT_CHUNK) * G * 129 * 8
+               ? (size_t)CL_KR * CL_ST * AT_KPITCH : (size_t)(CL_MAXC / AT_CHUNK) * G * 129 * 8;
+}
 template <int G>
 __host__ __device__ constexpr size_t cl_smem() {
-    return (size_t)CL_KR * CL_ST * AT_KPITCH + (size_t)CL_VR * CL_ST * 256 + (size_t)G * CL_MAXC * 4 +
+    return cl_kregion<G>() + (size_t)CL_VR * CL_ST * 256 + (size_t)G * CL_MAXC * 4 +
            (size_t)G * CL_ST * 8 + 8 * (CL_KR + CL_VR);
 }
 
@@ -629,6 +641,16 @@ __device__ __forceinline__ void cl_cp_arrive(uint64_t * bar) {
 __device__ __forceinline__ void cl_barrier() {
     asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
     asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cl_map(const void * local, int rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(alb_smem_addr(local)), "r"(rank));
+    return remote;
+}
+__device__ __forceinline__ double cl_ld_f64(uint32_t addr) {
+    double v;
+    asm volatile("ld.shared::cluster.f64 %0, [%1];" : "=d"(v) : "r"(addr) : "memory");
+    return v;
 }
 __device__ __forceinline__ float cl_ld_remote(const float * local, int rank) {
     uint32_t remote;
@@ -646,10 +668,11 @@ k_att_decode_cl(const AttParams a) {
     constexpr int HPT = G >= 2 ? G / 2 : 1;            // heads per thread in the P.V phase
     extern __shared__ __align__(16) uint8_t cl_sm[];
     uint8_t * kring = cl_sm;                                                     // [CL_KR][CL_ST][AT_KPITCH]
-    uint8_t * vring = kring + (size_t)CL_KR * CL_ST * AT_KPITCH;                 // [CL_VR][CL_ST][256]
+    uint8_t * vring = kring + cl_kregion<G>();                                   // [CL_VR][CL_ST][256]
+    double * cpart = reinterpret_cast<double *>(kring);   // after the scores: [chunk - j0][G][129]
     float * sc = reinterpret_cast<float *>(vring + (size_t)CL_VR * CL_ST * 256); // [G][CL_MAXC]
-    double * pd = reinterpret_cast<double *>(sc + (size_t)G * CL_MAXC);          // [G][CL_ST]
-    uint64_t * kfull = reinterpret_cast<uint64_t *>(pd + (size_t)G * CL_ST);
+    float * pf = reinterpret_cast<float *>(sc + (size_t)G * CL_MAXC);            // [G][CL_ST] p of the stage
+    uint64_t * kfull = reinterpret_cast<uint64_t *>(pf + (size_t)2 * G * CL_ST);
     uint64_t * vfull = kfull + CL_KR;
     __shared__ __align__(16) float qs[G][128];
     __shared__ __align__(16) float knew[128];
@@ -681,6 +704,9 @@ k_att_decode_cl(const AttParams a) {
         alb_mbar_fence_init();
     }
     __syncthreads();
+    // the O projection may launch now and stream its weights on the SMs' free
+    // halves; it waits for this grid's completion before reading the output
+    alb_pdl_trigger();
     // stage i of K (V): the cached rows by cp.async, completion counted on the
     // stage's mbarrier (one noinc arrival per thread); the new cell's row is
     // never copied (K: knew is used; V: vnew is written into the ring)
@@ -813,16 +839,13 @@ k_att_decode_cl(const AttParams a) {
     }
     __syncthreads();
 
-    // 4. p, and per chunk the ordered double sums (warps 0-7: O for dimension
+    // 4. p, and per chunk the ordered fp32 sums (warps 0-7: O for dimension
     //    tid % 128 of heads (tid / 128) + 2k; warp 8: the sums of p)
     const int d = tid & 127, gh = (tid >> 7) & 1;
-    double O[HPT];
-    double Lc = 0.0;
+    float O[HPT];
+    float Lc = 0.0f;
 #pragma unroll
-    for (int k = 0; k < HPT; ++k) O[k] = 0.0;
-    // ncap <= CL_CS * CL_MAXC = AT_SUPER chunks: one chunk per superchunk
-    const size_t nspmax = (size_t)at_nsuper_max(a.ncap);
-    double * part = a.part + (size_t)h * nspmax * G * 129;
+    for (int k = 0; k < HPT; ++k) O[k] = 0.0f;
     for (int i = 0; i < nst; ++i) {
         if (!alb_mbar_wait(&vfull[i % CL_VR], (uint32_t)((i / CL_VR) & 1))) {
             if (tid == 0) atomicExch(a.err, ALB_DEVERR_MBAR_TIMEOUT);
@@ -833,46 +856,81 @@ k_att_decode_cl(const AttParams a) {
 #pragma unroll
             for (int k = 0; k < GPT; ++k) {
                 const int g = gq * GPT + k;
-                double v = 0.0;
-                if (cl < rows) v = (double)alb_ref_expf(__fsub_rn(sc[(size_t)g * CL_MAXC + (cb - c0) + cl], Ms[g])) * 0x1p1008;
-                pd[g * CL_ST + cl] = v;   // p * 2^1008, exact
+                float v = 0.0f;
+                if (cl < rows) v = alb_ref_expf(__fsub_rn(sc[(size_t)g * CL_MAXC + (cb - c0) + cl], Ms[g]));
+                pf[g * CL_ST + cl] = v;
             }
         }
         __syncthreads();
         if (warp == 8) {
-            if (lane < G) Lc = at_psum(Lc, pd + lane * CL_ST, 1, rows);   // the chunk's sum of p, cells in order
+            if (lane < G) Lc = at_psum(Lc, pf + lane * CL_ST, 1, rows);   // the chunk's sum of p, cells in order
         } else if (G >= 2 || gh == 0) {
-            // V bits enter as (v * 2^-1008) and p as (p * 2^1008): fma adds the exact p * v
-            const uint16_t * vs = reinterpret_cast<const uint16_t *>(vring + (size_t)(i % CL_VR) * CL_ST * 256) + d;
-            for (int c = 0; c < rows; ++c) {
-                const double vd = alb_h2d_bits(vs[c * 128]);
+            // O = fmaf(p, v, O), cells in order (fp32, the canonical within-chunk
+            // order); four cells per step with their loads issued first
+            const __half * vs = reinterpret_cast<const __half *>(vring + (size_t)(i % CL_VR) * CL_ST * 256) + d;
+            int c = 0;
+            for (; c + 4 <= rows; c += 4) {
+                float vf[4], pp[4][HPT];
 #pragma unroll
-                for (int k = 0; k < HPT; ++k) O[k] = fma(pd[(gh + 2 * k) * CL_ST + c], vd, O[k]);
+                for (int u = 0; u < 4; ++u) {
+                    vf[u] = __half2float(vs[(c + u) * 128]);
+#pragma unroll
+                    for (int k = 0; k < HPT; ++k) pp[u][k] = pf[(gh + 2 * k) * CL_ST + c + u];
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+#pragma unroll
+                    for (int k = 0; k < HPT; ++k) O[k] = __fmaf_rn(pp[u][k], vf[u], O[k]);
+            }
+            for (; c < rows; ++c) {
+                const float v = __half2float(vs[c * 128]);
+#pragma unroll
+                for (int k = 0; k < HPT; ++k) O[k] = __fmaf_rn(pf[(gh + 2 * k) * CL_ST + c], v, O[k]);
             }
         }
         const int j = j0 + (cb - c0) / AT_CHUNK;
         if ((i & 1) == 1 || i == nst - 1) {   // a chunk ends (two stages per chunk, or the CTA's last)
-            double * pj = part + (size_t)j * G * 129;
+            double * pj = cpart + (size_t)(j - j0) * G * 129;
             if (warp == 8) {
-                if (lane < G) { pj[lane * 129 + 128] = Lc; Lc = 0.0; }
+                if (lane < G) { pj[lane * 129 + 128] = (double)Lc; Lc = 0.0f; }
             } else if (G >= 2 || gh == 0) {
 #pragma unroll
-                for (int k = 0; k < HPT; ++k) { pj[(gh + 2 * k) * 129 + d] = O[k]; O[k] = 0.0; }
+                for (int k = 0; k < HPT; ++k) { pj[(gh + 2 * k) * 129 + d] = (double)O[k]; O[k] = 0.0f; }
             }
         }
-        __syncthreads();   // V stage and pd consumed
+        __syncthreads();   // V stage and pf consumed
         issue(true, i + CL_VR, true);
     }
     asm volatile("cp.async.wait_all;" ::: "memory");   // no copy in flight past this point
 
     // 5. merge: this CTA's output blocks (head g, dims 32w .. 32w+31), block
-    //    b = r, r + CL_CS, ... of the G * 4, one warp each
-    __threadfence();
-    cl_barrier();
+    //    b = r, r + CL_CS, ... of the G * 4, one warp each.  Chunk j's partials
+    //    are in the shared memory of the CTA that owns it (rank o with
+    //    j0(o) <= j < j1(o)), read through distributed shared memory and added
+    //    in chunk order (at_ordered_sum's order: 0.0 + P_0 + P_1 + ...).
+    cl_barrier();   // every CTA's partials written (release / acquire at cluster scope)
     for (int b = r + CL_CS * warp; b < G * 4 && warp < 8; b += CL_CS * 8) {
         const int g = b >> 2, w = b & 3, dd = 32 * w + lane;
-        const double L = at_ordered_sum(part + g * 129 + 128, (size_t)G * 129, nch);
-        const double Od = at_ordered_sum(part + g * 129 + dd, (size_t)G * 129, nch);
+        double L = 0.0, Od = 0.0;
+        int own = 0;
+        for (int jb = 0; jb < nch; jb += 8) {
+            double tl[8], to[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const int j = jb + k;
+                tl[k] = 0.0; to[k] = 0.0;
+                if (j < nch) {
+                    while (j >= (int)((int64_t)nch * (own + 1) / CL_CS)) ++own;
+                    const int lj = j - (int)((int64_t)nch * own / CL_CS);
+                    const uint32_t base = cl_map(cpart + ((size_t)lj * G + g) * 129, own);
+                    tl[k] = cl_ld_f64(base + 128 * 8);
+                    to[k] = cl_ld_f64(base + (uint32_t)dd * 8);
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+                if (jb + k < nch) { L += tl[k]; Od += to[k]; }
+        }
         const float v = L > 0.0 ? __double2float_rn(Od / L) : 0.0f;
         const int hq = h * G + g;
         a.out[(size_t)hq * 128 + dd] = v;
@@ -886,7 +944,7 @@ k_att_decode_cl(const AttParams a) {
         }
     }
     if (s_bad && tid == 0 && !fits) atomicExch(a.err, ALB_DEVERR_MBAR_TIMEOUT);
-    alb_pdl_trigger();
+    cl_barrier();   // no CTA leaves while another may still read its partials
 }
 
 template <int G>

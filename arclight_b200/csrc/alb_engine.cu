@@ -208,6 +208,7 @@ static int engine_forward(alb_engine * e, int64_t T, bool pdl, int ncap_prefill 
         a.W = e->lm_W; a.N = e->V; a.K = e->E;
         a.in_mode = GEMV_IN_F32_RMS; a.x = e->x + (size_t)(T - 1) * e->E; a.norm_w = e->out_norm; a.eps = c.eps;
         a.out_mode = GEMV_OUT_LOGITS; a.y = e->logits; a.pdl = pdl;
+        a.ctas = 2 * alb_sm_count();   // the step's last mat-vec: both halves of every SM
         a.key = e->key; a.idx_base = e->v0;
         a.ticket = reinterpret_cast<int *>(e->am_scratch);
         a.next = e->tp == 1 ? e->next_dev : nullptr;

@@ -100,9 +100,9 @@ k_qk_norm_rope_kv(const float * __restrict__ qkv, int64_t qkv_stride, int Hq, in
 // ------------------------------------------------------------ flash attention
 // Prefill attention (T > 1 tokens, one split).  Semantics of the split-K
 // kernels (alb_attn.cu, the oracle's mode 0): fp16-rounded Q, fp32 score
-// chains, global-max softmax with the reference's NEON exp, double sums of
-// p and p * v in the canonical order -- cells in order within 128-cell chunks,
-// chunk sums added in chunk order.
+// chains, global-max softmax with the reference's NEON exp, sums of p and p * v
+// in the canonical order -- cells in order in fp32 within 128-cell chunks, the
+// chunk sums added in double in chunk order.
 __device__ __forceinline__ void fa_cp16(void * dst, const void * src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(alb_smem_addr(dst)), "l"(src) : "memory");
 }
@@ -116,9 +116,9 @@ __device__ __forceinline__ void fa_wait_all() { asm volatile("cp.async.wait_all;
 // decode kernels: every score is the sequential fp32 fma chain over d of the
 // fp16-rounded q (16 chains per thread: one cell, 16 rows); pass 1 takes the
 // row maxima over each row's causal cells, pass 2 recomputes the same scores,
-// forms p = v_expf(s - M) (L in double) and accumulates O += p * v in double as
-// a register tile of 4 rows x 8 dims per thread, cell by cell in order (p kept
-// as p * 2^1008 so the V bits enter the fma with no conversion instruction).
+// forms p = v_expf(s - M) and accumulates the chunk's L (row threads) and
+// O = fmaf(p, v, O) in fp32 as a register tile of 4 rows x 8 dims per thread,
+// cell by cell in order; chunk sums join double superchunk and total sums.
 static constexpr int FP_R = 64;                 // rows per CTA
 static constexpr int FP_CH = 64;                // cells per stage (two stages per 128-cell chunk)
 static constexpr int FP_KPITCH = 272;           // padded K row in shared memory
@@ -165,8 +165,8 @@ k_fa_prefill(const float * __restrict__ q, const uint16_t * __restrict__ kc, con
     float * qT = reinterpret_cast<float *>(fp_sm);                            // [128][FP_R]
     uint8_t * kst = fp_sm + (size_t)128 * FP_R * 4;                           // 2 x [FP_CH][FP_KPITCH]
     uint8_t * vst = kst + 2 * FP_CH * FP_KPITCH;                              // 2 x [FP_CH][256]
-    double * pd = reinterpret_cast<double *>(vst + 2 * FP_CH * 256);          // [FP_R][FP_CH]
-    double * Otot = pd + FP_R * FP_CH;                                        // [FP_R][128]
+    float * pf = reinterpret_cast<float *>(vst + 2 * FP_CH * 256);            // [FP_R][FP_CH] p of the stage
+    double * Otot = reinterpret_cast<double *>(pf + 2 * FP_R * FP_CH);         // [FP_R][128]
     __shared__ float Mrow[FP_R];
     __shared__ float red_m[2][FP_R];
     const int h = blockIdx.x, t0 = blockIdx.y * TQ, tid = threadIdx.x;
@@ -231,8 +231,10 @@ k_fa_prefill(const float * __restrict__ q, const uint16_t * __restrict__ kc, con
     if (tid < FP_R) Mrow[tid] = fmaxf(red_m[0][tid], red_m[1][tid]);
     // ---- pass 2: p, L and O (chunk partials: O in registers, L by row threads)
     const int r4 = (tid >> 4) * 4, d8 = (tid & 15) * 8;   // P.V tile of this thread
-    double O[4][8], Osp[4][8];                            // chunk sums, superchunk sums
-    double Lc = 0.0, Lsp = 0.0, Lt = 0.0;                 // thread r < FP_R: row r's chunk, superchunk, total
+    float O[4][8];                                        // chunk sums (fp32, cells in order)
+    double Osp[4][8];                                     // superchunk sums
+    float Lc = 0.0f;                                      // thread r < FP_R: row r's chunk sum of p,
+    double Lsp = 0.0, Lt = 0.0;                           // its superchunk and total sums
     // per row: its chunks (of its own causal cells) and chunks per superchunk
     // (the canonical order: chunk sums in order within superchunks of
     // ceil(chunks / 64) chunks, superchunk sums in order)
@@ -248,45 +250,43 @@ k_fa_prefill(const float * __restrict__ q, const uint16_t * __restrict__ kc, con
 #pragma unroll
     for (int u = 0; u < 4; ++u)
 #pragma unroll
-        for (int e = 0; e < 8; ++e) { O[u][e] = 0.0; Osp[u][e] = 0.0; Otot[(r4 + u) * 128 + d8 + e] = 0.0; }
+        for (int e = 0; e < 8; ++e) { O[u][e] = 0.0f; Osp[u][e] = 0.0; Otot[(r4 + u) * 128 + d8 + e] = 0.0; }
     issue(0, true);
     for (int i = 0; i < nst; ++i) {
         issue(i + 1, true);
         asm volatile("cp.async.wait_group 1;" ::: "memory");
-        __syncthreads();   // stage i visible; Mrow visible; pd free
+        __syncthreads();   // stage i visible; Mrow visible; pf free
         const int c = i * FP_CH + cl;
         float a[16];
         if (c < n) fp_scores16(kst + (i & 1) * FP_CH * FP_KPITCH + cl * FP_KPITCH, qT, rg, a);
 #pragma unroll
         for (int k = 0; k < 16; ++k) {
             const int r = 16 * rg + k, tt = r / G;
-            double v = 0.0;
-            if (c < n && tt < tn && c <= p0 + t0 + tt) {
-                const float p = alb_ref_expf(__fsub_rn(__fmul_rn(a[k], scale), Mrow[r]));
-                v = (double)p * 0x1p1008;
-            }
-            pd[r * FP_CH + cl] = v;
+            float v = 0.0f;
+            if (c < n && tt < tn && c <= p0 + t0 + tt) v = alb_ref_expf(__fsub_rn(__fmul_rn(a[k], scale), Mrow[r]));
+            pf[r * FP_CH + cl] = v;
         }
         __syncthreads();
-        if (tid < FP_R) {   // row tid's sum of p over the stage's cells, in order
-            for (int cc = 0; cc < FP_CH; ++cc) Lc += pd[tid * FP_CH + cc] * 0x1p-1008;
+        if (tid < FP_R) {   // row tid's sum of p over the stage's cells, in order (masked cells add 0)
+            for (int cc = 0; cc < FP_CH; ++cc) Lc = __fadd_rn(Lc, pf[tid * FP_CH + cc]);
         }
         const int rows = min(FP_CH, n - i * FP_CH);
         const uint8_t * vs = vst + (i & 1) * FP_CH * 256 + d8 * 2;
         for (int cc = 0; cc < rows; ++cc) {
             const uint4 vv = *reinterpret_cast<const uint4 *>(vs + cc * 256);
             const uint32_t wd[4] = {vv.x, vv.y, vv.z, vv.w};
-            double vd[8];
+            float vf[8];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                vd[2 * e] = alb_h2d_bits(wd[e] & 0xFFFFu);
-                vd[2 * e + 1] = alb_h2d_bits(wd[e] >> 16);
+                const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&wd[e]));
+                vf[2 * e] = f.x;
+                vf[2 * e + 1] = f.y;
             }
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
-                const double p = pd[(r4 + u) * FP_CH + cc];
+                const float p = pf[(r4 + u) * FP_CH + cc];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) O[u][e] = fma(p, vd[e], O[u][e]);
+                for (int e = 0; e < 8; ++e) O[u][e] = __fmaf_rn(p, vf[e], O[u][e]);   // fp32, cells in order
             }
         }
         if ((i & 1) == 1 || i == nst - 1) {   // a 128-cell chunk ends: its sums join the superchunk's
@@ -296,18 +296,18 @@ k_fa_prefill(const float * __restrict__ q, const uint16_t * __restrict__ kc, con
                 const bool send = (j + 1) % scn_u[u] == 0 || j == nch_u[u] - 1;
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
-                    Osp[u][e] += O[u][e];
-                    O[u][e] = 0.0;
+                    Osp[u][e] += (double)O[u][e];
+                    O[u][e] = 0.0f;
                     if (send) { Otot[(r4 + u) * 128 + d8 + e] += Osp[u][e]; Osp[u][e] = 0.0; }
                 }
             }
             if (tid < FP_R) {
-                Lsp += Lc;
-                Lc = 0.0;
+                Lsp += (double)Lc;
+                Lc = 0.0f;
                 if ((j + 1) % scn_l == 0 || j == nch_l - 1) { Lt += Lsp; Lsp = 0.0; }
             }
         }
-        __syncthreads();   // pd and buffer i & 1 consumed
+        __syncthreads();   // pf and buffer i & 1 consumed
     }
     fa_wait_all();
     __shared__ double Lrow[FP_R];

@@ -100,9 +100,9 @@ struct MvPlan {
     uint32_t smem;
 };
 
-static constexpr int MV_CW = 24;                       // block-dot warps
-static constexpr int MV_RU = 2;                        // rows per dot iteration (independent work)
-static constexpr int MV_CH = 4;                        // chain warps: stage g goes to chain warp g % MV_CH
+static constexpr int MV_CW = 12;                       // block-dot warps
+static constexpr int MV_RU = 3;                        // rows per dot iteration (independent work)
+static constexpr int MV_CH = 2;                        // chain warps: stage g goes to chain warp g % MV_CH
 static constexpr int MV_PW = MV_CW + MV_CH;            // the producer warp's index
 static constexpr int MV_THREADS = (MV_CW + MV_CH + 1) * 32;
 static constexpr int MV_NT = (MV_CW + MV_CH) * 32;     // threads of the prologue barrier
@@ -291,11 +291,14 @@ __device__ __forceinline__ unsigned long long mv_key(float v, int64_t idx) {
 
 // Batch-1 Q4_0 x Q8_0 mat-vec with the reference's summation order.
 //
-// One CTA per SM owns a contiguous range of rows.  Its producer warp streams
-// them through an ns-stage shared-memory ring, R whole rows per stage (nibbles
-// and scales of the row-interleaved layout: one bulk copy), and never waits on
-// the previous kernel: under programmatic dependent launch the first stages
-// are in flight while the previous grid drains.  For each stage the MV_CW dot
+// Each CTA owns a contiguous range of rows (one CTA per SM).  A CTA takes at
+// most half of an SM (480 threads, <= 64 registers, ~108 KB of shared memory),
+// so under programmatic dependent launch the NEXT kernel's CTA is resident on
+// the same SM while this one computes: its producer warp, which never waits on
+// the previous kernel, streams the next matrix into its own ring meanwhile.
+// The producer streams the rows through an ns-stage shared-memory ring, R
+// whole rows per stage (nibbles and scales of the row-interleaved layout: one
+// bulk copy).  For each stage the MV_CW dot
 // warps compute the int32 block dots I(n, b) of its R x K/32 blocks (lanes over
 // consecutive blocks of one row: conflict-free 16-byte reads) and store the
 // terms (float(I), f32(dx) * f32(dw)) -- both exact -- in the stage's chain
@@ -311,7 +314,7 @@ __device__ __forceinline__ unsigned long long mv_key(float v, int64_t idx) {
 // Every wait is bounded; on a timeout the kernel records an error code,
 // stops its loops and (producer) waits for its copies in flight before exit.
 template <int IN, int OUT>
-__global__ void __launch_bounds__(MV_THREADS, 1)
+__global__ void __launch_bounds__(MV_THREADS, 2)
 k_mv(const GemvArgs a, const MvPlan p) {
     constexpr bool PAIR = OUT == GEMV_OUT_PAIR || OUT == GEMV_OUT_LOGITS;
     constexpr int XR = XRec<PAIR>::INTS;
@@ -348,10 +351,9 @@ k_mv(const GemvArgs a, const MvPlan p) {
     if (warp == MV_PW) {
         // ------------------------------------------------ producer warp
         if (lane == 0) {
-            int g = 0;
+            int g = 0, slot = 0, round = 0;
             for (; g < nst; ++g) {
-                const int slot = g % p.ns;
-                if (g >= p.ns && !alb_mbar_wait_nap(&empty[slot], (uint32_t)((g / p.ns - 1) & 1), 256)) {
+                if (round > 0 && !alb_mbar_wait(&empty[slot], (uint32_t)((round - 1) & 1))) {
                     atomicExch(a.err, ALB_DEVERR_MBAR_TIMEOUT);
                     s_abort = 1;
                     break;
@@ -360,6 +362,7 @@ k_mv(const GemvArgs a, const MvPlan p) {
                 const uint32_t bytes = (uint32_t)((n1 - r0) < R ? (n1 - r0) : R) * rowb;
                 alb_mbar_expect_tx(&full[slot], bytes);
                 alb_bulk_g2s(smem + (size_t)slot * p.stage_bytes, a.W + r0 * rowb, bytes, &full[slot]);
+                if (++slot == p.ns) { slot = 0; ++round; }
             }
             // never exit with copies in flight
             for (int j = g - p.ns < 0 ? 0 : g - p.ns; j < g; ++j)
@@ -409,43 +412,46 @@ k_mv(const GemvArgs a, const MvPlan p) {
                 sg0 = ds.z; sg1 = ds.w; sg2 = s23.x; sg3 = s23.y;
             }
         }
+        // fp16 bits of dx for the exact mixed-precision product dx * dw
+        const unsigned short dxh = __half_as_ushort(__float2half_rn(dxv));
+        const uint32_t wofs = 16u * (uint32_t)b, sofs = scol + 2u * (uint32_t)b;
+        const int n_rows = (int)(n1 - n0);
+        int slot = 0, cbi = 0, ring_round = 0, chain_round = 0;
         for (int g = 0; g < nst; ++g) {
-            const int slot = g % p.ns, cbi = g % p.ncb;
             if (*reinterpret_cast<volatile int *>(&s_abort)) break;
-            bool ok = alb_mbar_wait_nap(&full[slot], (uint32_t)((g / p.ns) & 1), 128);
-            if (ok && g >= p.ncb) ok = alb_mbar_wait_nap(&freeb[cbi], (uint32_t)((g / p.ncb - 1) & 1), 128);
+            bool ok = alb_mbar_wait(&full[slot], (uint32_t)(ring_round & 1));
+            if (ok && chain_round > 0) ok = alb_mbar_wait(&freeb[cbi], (uint32_t)((chain_round - 1) & 1));
             if (!ok) {
                 if (lane == 0) atomicExch(a.err, ALB_DEVERR_MBAR_TIMEOUT);
                 s_abort = 1;
                 break;
             }
-            const int64_t r0 = n0 + (int64_t)g * R;
-            const int rg = (int)((n1 - r0) < R ? (n1 - r0) : R);
-            const uint8_t * stg = smem + (size_t)slot * p.stage_bytes;
-            uint8_t * cb = cbase + (size_t)cbi * p.cb_bytes;
+            const int rb = g * R;
+            const int rg = n_rows - rb < R ? n_rows - rb : R;
+            const uint8_t * stg = smem + (uint32_t)slot * p.stage_bytes;
+            uint8_t * cb = cbase + (uint32_t)cbi * p.cb_bytes;
             if (valid) {
                 for (int r = jr; r < rg; r += MV_RU * m) {
-                    const int nr = r + m < rg ? 2 : 1;
                     uint4 w[MV_RU];
-                    uint32_t dwb[MV_RU];
+                    unsigned short dwb[MV_RU];
 #pragma unroll
                     for (int k = 0; k < MV_RU; ++k) {
-                        if (k < nr) {
-                            const uint8_t * row = stg + (size_t)(r + k * m) * rowb;
-                            w[k] = *reinterpret_cast<const uint4 *>(row + 16 * b);
-                            dwb[k] = reinterpret_cast<const uint16_t *>(row + scol)[b];
+                        if (r + k * m < rg) {
+                            const uint8_t * row = stg + (uint32_t)(r + k * m) * rowb;
+                            w[k] = *reinterpret_cast<const uint4 *>(row + wofs);
+                            dwb[k] = *reinterpret_cast<const unsigned short *>(row + sofs);
                         }
                     }
 #pragma unroll
                     for (int k = 0; k < MV_RU; ++k) {
-                        if (k < nr) {
-                            const int rk = r + k * m;
-                            const float s = __fmul_rn(dxv, alb_h2f_bits(dwb[k]));   // exact: 11 x 11 bits
+                        const int rk = r + k * m;
+                        if (rk < rg) {
+                            const float s = alb_mul_f16_exact(dxh, dwb[k]);   // f32(dx) * f32(dw), exact
                             if constexpr (!PAIR) {
                                 const int I = q4q8_dot_fast(w[k], lo, hi, asum);
-                                *reinterpret_cast<float2 *>(cb + (size_t)rk * p.cbp + 8 * b) =
+                                *reinterpret_cast<float2 *>(cb + (uint32_t)rk * p.cbp + 8u * (uint32_t)b) =
                                     make_float2(alb_i2f_small(I), s);
-                                if constexpr (OUT == GEMV_OUT_DOTS) a.dots[(r0 + rk) * nb + b] = I;
+                                if constexpr (OUT == GEMV_OUT_DOTS) a.dots[(n0 + rb + rk) * nb + b] = I;
                             } else {
                                 const uint32_t wv[4] = {w[k].x, w[k].y, w[k].z, w[k].w};
                                 const int lov[4] = {lo.x, lo.y, lo.z, lo.w}, hiv[4] = {hi.x, hi.y, hi.z, hi.w};
@@ -458,8 +464,8 @@ k_mv(const GemvArgs a, const MvPlan p) {
                                     asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(hi_s) : "r"(wv[l] & 0xF0F0F0F0u), "r"(hiv[l]));
                                     pl[l] = lo_s + (hi_s >> 4) - 8 * sg[l];   // hi_s = 16 * sum(hi * a): exact shift
                                 }
-                                float * T = reinterpret_cast<float *>(cb + (size_t)rk * p.cbp) + 4 * b;
-                                float * S = reinterpret_cast<float *>(cb + (size_t)R * p.cbp + (size_t)rk * p.cbs) + b;
+                                float * T = reinterpret_cast<float *>(cb + (uint32_t)rk * p.cbp) + 4 * b;
+                                float * S = reinterpret_cast<float *>(cb + (uint32_t)R * p.cbp + (uint32_t)rk * p.cbs) + b;
                                 if ((nb & 1) && b == nb - 1) {
                                     // scalar tail of an odd block count (arm.cpp:675-691): sumi, dw, dx
                                     *reinterpret_cast<float4 *>(T) = make_float4(
@@ -477,6 +483,8 @@ k_mv(const GemvArgs a, const MvPlan p) {
             }
             __syncwarp();
             if (lane == 0) { alb_mbar_arrive(&empty[slot]); alb_mbar_arrive(&done[cbi]); }
+            if (++slot == p.ns) { slot = 0; ++ring_round; }
+            if (++cbi == MV_CH) { cbi = 0; ++chain_round; }
         }
         return;
     }
@@ -487,9 +495,9 @@ k_mv(const GemvArgs a, const MvPlan p) {
     const int cw = warp - MV_CW;
     unsigned long long best = 0ull;   // LOGITS: this lane's best key
     for (int g = cw; g < nst; g += MV_CH) {
-        const int cbi = g % p.ncb;
+        const int cbi = cw;   // g % MV_CH
         if (*reinterpret_cast<volatile int *>(&s_abort)) break;
-        if (!alb_mbar_wait_nap(&done[cbi], (uint32_t)((g / p.ncb) & 1), 256)) {
+        if (!alb_mbar_wait(&done[cbi], (uint32_t)((g / MV_CH) & 1))) {
             if (lane == 0) atomicExch(a.err, ALB_DEVERR_MBAR_TIMEOUT);
             s_abort = 1;
             break;
@@ -624,8 +632,8 @@ static inline uint32_t mv_odd16(uint32_t x) {
 // Shared-memory plan: stages of about `stage_target` bytes of whole rows (one
 // bulk copy each: large copies stream at full HBM rate, small ones are limited
 // by the per-copy cost), one chain buffer per chain warp, and as many stages
-// (2..8) as fit the budget (one CTA per SM: the ring, not a second resident
-// kernel, keeps HBM busy).
+// (2..8) as fit the budget (about half an SM's shared memory, so that the next
+// launch's CTA fits beside this one and prefetches its own weights).
 static MvPlan mv_plan(int64_t K, bool pair, int in_mode, int budget, int stage_target) {
     const int64_t nb = K / 32;
     const int64_t row_bytes = q4_row_bytes(K);
@@ -671,8 +679,9 @@ static MvPlan mv_plan(int64_t K, bool pair, int in_mode, int budget, int stage_t
 }
 
 // Tuning knobs (read once per process): ALB_MV_SMEM_KB (shared-memory budget
-// of a CTA, default 160), ALB_MV_STAGE_KB (target stage size, default 32),
-// ALB_MV_CPS (CTAs per SM, default 1).
+// of a CTA, default 108: two CTAs per SM), ALB_MV_STAGE_KB (target stage size,
+// default 32), ALB_MV_CPS (CTAs per SM of a launch, default 1: the other half
+// of each SM is for the next launch).
 static int mv_knob(const char * name, int dflt) {
     const char * v = getenv(name);
     return v && atoi(v) > 0 ? atoi(v) : dflt;
@@ -681,7 +690,7 @@ static int mv_knob(const char * name, int dflt) {
 template <int IN, int OUT>
 static cudaError_t launch_mv_t(const GemvArgs & a, cudaStream_t stream) {
     constexpr bool PAIR = OUT == GEMV_OUT_PAIR || OUT == GEMV_OUT_LOGITS;
-    static const int budget_kb = mv_knob("ALB_MV_SMEM_KB", 160);
+    static const int budget_kb = mv_knob("ALB_MV_SMEM_KB", 108);
     static const int stage_kb = mv_knob("ALB_MV_STAGE_KB", 32);
     const MvPlan p = mv_plan(a.K, PAIR, IN, a.smem_budget > 0 ? a.smem_budget : budget_kb * 1024, stage_kb * 1024);
     auto kern = k_mv<IN, OUT>;

@@ -63,6 +63,15 @@ __device__ __forceinline__ float alb_h2f_bits(uint32_t h) {
     return __fmul_rn(__int_as_float((int)(((h & 0x7FFFu) << 13) | ((h & 0x8000u) << 16))), 0x1p112f);
 }
 
+// f32(a) * f32(b) of two fp16 bit patterns, exactly (11 x 11 significand bits
+// fit a float, subnormals included): one mixed-precision fma (sm_100) whose -0
+// addend leaves the product, and its sign of zero, unchanged.
+__device__ __forceinline__ float alb_mul_f16_exact(unsigned short a, unsigned short b) {
+    float r;
+    asm("fma.rn.f32.f16 %0, %1, %2, %3;" : "=f"(r) : "h"(a), "h"(b), "f"(-0.0f));
+    return r;
+}
+
 // fp16 bits -> the bits of (value * 2^-1008) as a double (see alb_h2d), without
 // the final scaling; pairs with an operand pre-scaled by 2^1008.
 __device__ __forceinline__ double alb_h2d_bits(uint32_t h) {

@@ -60,7 +60,7 @@ def host_cpu():
 
 
 DTYPE_DECODE = ("q4_0 weights x q8_0 activations: int32 block dots in the reference's fp32 chains; "
-                "attention fp32 scores, fp64 softmax sums; fp16 KV")
+                "attention fp32 scores and chunk sums, fp64 chunk merge; fp16 KV")
 
 
 # ----------------------------------------------------------------- clocks
@@ -568,7 +568,7 @@ def run_attn(args, rank, world):
         "metric": "split-K flash decode GB/s (config 5 attention: 32/8 heads, 32768 fp16 cells)",
         "value": achieved * world, "unit": "GB/s", "n_gpus": world, "steps": steps, "warmup": max(args.warmup, 3),
         "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "fp16 KV, fp32 scores (sequential fma), fp64 softmax sums in chunk order",
+        "dtype": "fp16 KV, fp32 scores (sequential fma), fp32 softmax sums within 128-cell chunks, fp64 across chunks",
         "data": "synthetic: N(0,1) q/K/V",
         "config": {"workload": "config5_attention", "n_head": ATT_HQ, "n_head_kv": ATT_HKV, "cells": ATT_CELLS,
                    "splits": S, "kv_copies": ATT_COPIES, "l2": "inputs larger than L2: 4 rotating caches (512 MB)"},

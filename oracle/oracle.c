@@ -569,29 +569,30 @@ static void fa_range(void * pc, int64_t b, int64_t e) {
                     sc[c] = a * scale;
                     M = sc[c] > M ? sc[c] : M;
                 }
-                /* chunked canonical order: cells in order within each ORC_FA_CHUNK-cell
-                 * chunk from 0; chunk sums added in chunk order from 0 within each
-                 * superchunk of scn consecutive chunks (scn = 1 up to ORC_FA_SUPER
-                 * chunks); superchunk sums added in order from 0 (every p * v is
-                 * exact in double; only the additions round) */
+                /* chunked canonical order: within each ORC_FA_CHUNK-cell chunk, cells
+                 * in order from 0 in fp32 (L_c = L_c + p, O_c = fmaf(p, v, O_c)); the
+                 * chunk sums, widened to double, added in chunk order from 0 within
+                 * each superchunk of scn consecutive chunks (scn = 1 up to
+                 * ORC_FA_SUPER chunks); superchunk sums added in order from 0 */
                 const int64_t nch = (n_kv + ORC_FA_CHUNK - 1) / ORC_FA_CHUNK;
                 const int64_t scn = nch > ORC_FA_SUPER ? (nch + ORC_FA_SUPER - 1) / ORC_FA_SUPER : 1;
                 double L = 0.0, Ls = 0.0;
-                double * Oc = Od + D, * Os = Od + 2 * D;
+                double * Os = Od + 2 * D;
                 for (int64_t d = 0; d < D; ++d) { Od[d] = 0.0; Os[d] = 0.0; }
                 for (int64_t j = 0; j < nch; ++j) {
                     const int64_t c0 = j * ORC_FA_CHUNK;
                     const int64_t c1 = c0 + ORC_FA_CHUNK < n_kv ? c0 + ORC_FA_CHUNK : n_kv;
-                    double Lc = 0.0;
-                    for (int64_t d = 0; d < D; ++d) Oc[d] = 0.0;
+                    float Lc = 0.0f;
+                    float * Ocf = VKQ32;
+                    for (int64_t d = 0; d < D; ++d) Ocf[d] = 0.0f;
                     for (int64_t c = c0; c < c1; ++c) {
                         const float p = orc_neon_expf(sc[c] - M);
                         const uint16_t * vc = v + c * row + hk * D;
-                        Lc += (double)p;
-                        for (int64_t d = 0; d < D; ++d) Oc[d] += (double)p * (double)orc_fp16_to_fp32(vc[d]);
+                        Lc = Lc + p;
+                        for (int64_t d = 0; d < D; ++d) Ocf[d] = fmaf(p, orc_fp16_to_fp32(vc[d]), Ocf[d]);
                     }
-                    Ls += Lc;
-                    for (int64_t d = 0; d < D; ++d) Os[d] += Oc[d];
+                    Ls += (double)Lc;
+                    for (int64_t d = 0; d < D; ++d) Os[d] += (double)Ocf[d];
                     if ((j + 1) % scn == 0 || j == nch - 1) {   /* a superchunk ends */
                         L += Ls;
                         Ls = 0.0;
