@@ -674,8 +674,8 @@ k_att_decode_cl(const AttParams a) {
     float * pf = reinterpret_cast<float *>(sc + (size_t)G * CL_MAXC);            // [G][CL_ST] p of the stage
     uint64_t * kfull = reinterpret_cast<uint64_t *>(pf + (size_t)2 * G * CL_ST);
     uint64_t * vfull = kfull + CL_KR;
-    __shared__ __align__(16) float qs[G][128];
-    __shared__ __align__(16) float knew[128];
+    __shared__ __align__(16) unsigned short qh[G][128];   // fp16 bits of the rounded Q
+    __shared__ __align__(16) unsigned short knewh[128];
     __shared__ __align__(16) uint16_t vnew[128];
     __shared__ float hb[G + 1][128];
     __shared__ double hred[4][G + 1];
@@ -740,16 +740,16 @@ k_att_decode_cl(const AttParams a) {
         const float vraw = holder ? a.qkv[(size_t)(a.Hq + a.Hkv + h) * 128 + tid] : 0.0f;
         at_norm_rope_heads<G + 1, true>(v, holder ? G + 1 : G, G, a.qn, a.kn, a.eps, cs, hb, hred, hseq);
 #pragma unroll
-        for (int g = 0; g < G; ++g) qs[g][tid] = __half2float(__float2half_rn(v[g]));   // Q -> fp16 (arm.cpp:2307)
+        for (int g = 0; g < G; ++g) qh[g][tid] = __half_as_ushort(__float2half_rn(v[g]));   // Q -> fp16 (arm.cpp:2307)
         if (holder) {
             const uint16_t kh = alb_f2h(v[G]), vh = alb_f2h(vraw);
-            knew[tid] = __half2float(__ushort_as_half(kh));
+            knewh[tid] = kh;
             vnew[tid] = vh;
             a.kcw[(size_t)(n - 1) * row + (size_t)h * 128 + tid] = kh;
             a.vcw[(size_t)(n - 1) * row + (size_t)h * 128 + tid] = vh;
         }
     }
-    __syncthreads();   // qs, knew, vnew visible
+    __syncthreads();   // qh, knewh, vnew visible
     if (holder) {      // the new cell's V row, when its stage was issued above
         const int i = (n - 1 - c0) / CL_ST;
         if (i < CL_VR && tid < 16) {
@@ -778,33 +778,20 @@ k_att_decode_cl(const AttParams a) {
             for (int k = 0; k < GPT; ++k) acc[k] = 0.0f;
 #pragma unroll 4
             for (int j = 0; j < 16; ++j) {   // dims 8j .. 8j+7, in order (the reference's sequential chain)
-                float kf[8];
-                if (c == n - 1) {
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) kf[e] = knew[8 * j + e];
-                } else {
-                    const uint4 kv = *reinterpret_cast<const uint4 *>(kr + j * 16);
-                    const uint32_t wd[4] = {kv.x, kv.y, kv.z, kv.w};
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&wd[e]));
-                        kf[2 * e] = f.x;
-                        kf[2 * e + 1] = f.y;
-                    }
-                }
+                // acc = fma(f32(k_d), f32(q_d), acc) as one mixed-precision fma on the
+                // fp16 bits (the product of two halves is exact in fp32)
+                const uint4 kv = c == n - 1 ? *reinterpret_cast<const uint4 *>(knewh + 8 * j)
+                                            : *reinterpret_cast<const uint4 *>(kr + j * 16);
+                const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w};
 #pragma unroll
                 for (int k = 0; k < GPT; ++k) {
-                    const float * qg = qs[gq * GPT + k];
-                    const float4 qa = *reinterpret_cast<const float4 *>(qg + 8 * j);
-                    const float4 qb = *reinterpret_cast<const float4 *>(qg + 8 * j + 4);
-                    acc[k] = __fmaf_rn(kf[0], qa.x, acc[k]);
-                    acc[k] = __fmaf_rn(kf[1], qa.y, acc[k]);
-                    acc[k] = __fmaf_rn(kf[2], qa.z, acc[k]);
-                    acc[k] = __fmaf_rn(kf[3], qa.w, acc[k]);
-                    acc[k] = __fmaf_rn(kf[4], qb.x, acc[k]);
-                    acc[k] = __fmaf_rn(kf[5], qb.y, acc[k]);
-                    acc[k] = __fmaf_rn(kf[6], qb.z, acc[k]);
-                    acc[k] = __fmaf_rn(kf[7], qb.w, acc[k]);
+                    const uint4 qv = *reinterpret_cast<const uint4 *>(&qh[gq * GPT + k][8 * j]);
+                    const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        acc[k] = alb_fma_f16_f32((unsigned short)(kw[e] & 0xFFFFu), (unsigned short)(qw[e] & 0xFFFFu), acc[k]);
+                        acc[k] = alb_fma_f16_f32((unsigned short)(kw[e] >> 16), (unsigned short)(qw[e] >> 16), acc[k]);
+                    }
                 }
             }
 #pragma unroll

@@ -197,6 +197,24 @@ __device__ __forceinline__ bool alb_rms_mean_certain(double par, int n) {
     const double d = par * (double)n * 0x1p-50;
     return (float)((par - d) / (double)n) == (float)((par + d) / (double)n);
 }
+// The same certificate without a division: inv_n is 1/n rounded to double,
+// and the bounds are widened by par * 2^-48, which covers the rounding of
+// inv_n, of par -/+ d and of the products.  When the float images of
+// (par - d) * inv_n and (par + d) * inv_n agree, the reference's float mean
+// (its sequential sum divided by n, rounded to double, then to float) is that
+// value, returned in `mean`; otherwise the caller takes the sequential sum.
+__device__ __forceinline__ bool alb_rms_mean_cert(double par, int n, double inv_n, float & mean) {
+    const double d = par * (double)n * 0x1p-50 + par * 0x1p-48;
+    const float lo = (float)((par - d) * inv_n), hi = (float)((par + d) * inv_n);
+    mean = lo;
+    return lo == hi;
+}
+// Pairwise sum of v[0..N) (a fixed tree: depth log2 N instead of a chain of N).
+template <int N>
+__device__ __forceinline__ double alb_tree_sum(const double * v) {
+    if constexpr (N == 1) return v[0];
+    else return alb_tree_sum<N / 2>(v) + alb_tree_sum<N - N / 2>(v + N / 2);
+}
 // The sequential sum of the squares of x[0..n) (one thread).
 __device__ __forceinline__ double alb_rms_seq_sum(const float * x, int n) {
     double s = 0.0;

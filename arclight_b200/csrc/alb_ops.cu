@@ -436,6 +436,7 @@ k_rms_norm(const float * __restrict__ x, const float * __restrict__ w, float * _
     const float * xr = x + (size_t)blockIdx.x * n;
     float * yr = y + (size_t)blockIdx.x * n;
     __shared__ double red[8];
+    const double inv_n = 1.0 / (double)n;
     alb_pdl_wait();
     double s = 0.0;
     for (int64_t i = threadIdx.x; i < n; i += 256) { const float v = xr[i]; s += (double)__fmul_rn(v, v); }
@@ -443,16 +444,14 @@ k_rms_norm(const float * __restrict__ x, const float * __restrict__ w, float * _
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
     __syncthreads();
-    double t = 0.0;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) t += red[i];
-    if (!alb_rms_mean_certain(t, (int)n)) {   // the reference's sequential sum (uniform branch)
+    const double t = alb_tree_sum<8>(red);
+    float mean;
+    if (!alb_rms_mean_cert(t, (int)n, inv_n, mean)) {   // the reference's sequential sum (uniform branch)
         __syncthreads();
         if (threadIdx.x == 0) red[0] = alb_rms_seq_sum(xr, (int)n);
         __syncthreads();
-        t = red[0];
+        mean = (float)(red[0] / (double)n);
     }
-    const float mean = (float)(t / (double)n);
     const float scale = 1.0f / sqrtf(__fadd_rn(mean, eps));
     for (int64_t i = threadIdx.x; i < n; i += 256) {
         const float v = __fmul_rn(xr[i], scale);
@@ -478,6 +477,7 @@ k_rms_norm_q8(const float * __restrict__ x, const float * __restrict__ w, float 
               uint8_t * __restrict__ yq, int64_t n, float eps) {
     const float * xr = x + (size_t)blockIdx.x * n;
     __shared__ double red[8];
+    const double inv_n = 1.0 / (double)n;
     alb_pdl_wait();
     double s = 0.0;
     for (int64_t i = threadIdx.x; i < n; i += 256) { const float v = xr[i]; s += (double)__fmul_rn(v, v); }
@@ -485,16 +485,14 @@ k_rms_norm_q8(const float * __restrict__ x, const float * __restrict__ w, float 
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
     __syncthreads();
-    double t = 0.0;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) t += red[i];
-    if (!alb_rms_mean_certain(t, (int)n)) {   // the reference's sequential sum (uniform branch)
+    const double t = alb_tree_sum<8>(red);
+    float mean;
+    if (!alb_rms_mean_cert(t, (int)n, inv_n, mean)) {   // the reference's sequential sum (uniform branch)
         __syncthreads();
         if (threadIdx.x == 0) red[0] = alb_rms_seq_sum(xr, (int)n);
         __syncthreads();
-        t = red[0];
+        mean = (float)(red[0] / (double)n);
     }
-    const float mean = (float)(t / (double)n);
     const float scale = 1.0f / sqrtf(__fadd_rn(mean, eps));
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int64_t nb = n / 32;

@@ -10,8 +10,8 @@
 // row.  Because the scales change every 32 values of K, every block is one MMA
 // (M = 128 tokens, N = 64 rows of W, K = 32) into a fresh TMEM accumulator,
 // and the epilogue warps read it back (tcgen05.ld) and advance their fp32
-// chains while the tensor core computes the next block into the other half of
-// the TMEM allocation.
+// chains while the tensor core computes the next blocks into the other
+// buffers of the TMEM allocation.
 //
 // Operands in shared memory, K-major without swizzle (core matrices of 8 rows
 // x 16 bytes; the two 16-byte halves of a block are the two K chunks):
@@ -27,19 +27,25 @@ namespace alb {
 
 static constexpr int PG_M = 128;          // tokens per tile (TMEM lanes)
 static constexpr int PG_N = 64;           // weight rows per tile (TMEM columns per buffer)
-static constexpr int PG_THREADS = 256;    // 8 warps: all load, thread 0 issues, all read back
-static constexpr uint32_t PG_TMEM_COLS = 2 * PG_N;
-
-static constexpr int PG_STAGES = 4;       // cp.async ring depth (blocks of K in flight)
+static constexpr int PG_D = 5;            // operand ring stages (blocks of K in flight)
+static constexpr int PG_LAG = 2;          // blocks the loader keeps in flight before publishing one
+static constexpr int PG_NB = 4;           // TMEM accumulator buffers (blocks the MMA may run ahead)
+static constexpr int PG_EW = 8;           // epilogue warps
+static constexpr int PG_THREADS = (2 + PG_EW) * 32;   // warp 0 loads, warp 1 unpacks + issues, 2.. epilogue
+static constexpr uint32_t PG_TMEM_COLS = PG_NB * PG_N;
 
 struct PgShared {
-    alignas(128) int8_t a[PG_STAGES][PG_M * 32];   // MMA operand A per stage (core-matrix layout)
-    alignas(128) int8_t b[2][PG_N * 32];           // MMA operand B (unpacked) for blocks b & 1
-    alignas(16) uint8_t nib[PG_STAGES][PG_N * 16]; // W nibbles as loaded
-    alignas(16) float dx[PG_STAGES][PG_M];         // activation block scales (fp16-rounded)
-    alignas(16) uint32_t dww[PG_STAGES][PG_N];     // 4-byte words holding the weight block scale
-    alignas(16) float dwf[2][PG_N];                // weight block scale as fp32
-    uint64_t mma_done[2];
+    alignas(128) int8_t a[PG_D][PG_M * 32];   // MMA operand A per stage (core-matrix layout)
+    alignas(128) int8_t b[PG_D][PG_N * 32];   // MMA operand B (nibbles unpacked to int8 q - 8) per stage
+    alignas(16) uint8_t nib[PG_D][PG_N * 16]; // W nibbles as loaded
+    alignas(16) float dx[PG_D][PG_M];         // activation block scales (fp16-rounded)
+    alignas(16) uint32_t dww[PG_D][PG_N];     // 4-byte words holding the weight block scale
+    alignas(16) float dwf[PG_D][PG_N];        // weight block scale as fp32
+    uint64_t full[PG_D];                      // stage loaded and fenced for the tensor core (loader lane 0)
+    uint64_t empty[PG_D];                     // stage consumed (its MMA + the epilogue warps' scale reads)
+    uint64_t tfull[PG_NB];                    // accumulator ready (MMA commit + the issuer's dwf release)
+    uint64_t tempty[PG_NB];                   // accumulator read back (epilogue warps)
+    uint64_t drain;                           // every MMA of the CTA complete
     uint32_t tmem_base;
     int abort_flag;
 };
@@ -97,13 +103,32 @@ __global__ void k_pg_from_q8(const uint8_t * __restrict__ src, int64_t M, int64_
     for (int j = 0; j < 32; ++j) d[j] = (int8_t)s[2 + j];
 }
 
-__device__ __forceinline__ bool pg_wait(PgShared & sh, int buf, uint32_t parity, int * err) {
-    if (alb_mbar_wait(&sh.mma_done[buf], parity)) return true;
-    if ((threadIdx.x & 31) == 0) atomicExch(err, ALB_DEVERR_MBAR_TIMEOUT);
+// Bounded wait on one of the kernel's mbarriers; a timeout records an error
+// code and raises the CTA's abort flag (every role then leaves its loop).
+__device__ __forceinline__ bool pg_wait(PgShared & sh, uint64_t * bar, uint32_t parity, int * err) {
+    if (alb_mbar_wait(bar, parity)) return true;
+    atomicExch(err, ALB_DEVERR_MBAR_TIMEOUT);
     sh.abort_flag = 1;
     return false;
 }
+__device__ __forceinline__ bool pg_aborted(PgShared & sh) { return *reinterpret_cast<volatile int *>(&sh.abort_flag) != 0; }
 
+// Warp-specialised pipeline, one CTA per (64 weight rows, 128 tokens), two CTAs
+// per SM:
+//   warp 0      loads block b's operands into ring stage b % PG_D (cp.async)
+//               once empty[stage] says the stage's previous block is consumed;
+//               PG_LAG blocks later its lanes wait for those copies, fence them
+//               for the async proxy (the tensor core reads A) and lane 0
+//               publishes the stage on full[stage];
+//   warp 1      unpacks the nibbles into the B operand, converts the weight
+//               scales, and (lane 0) issues the block's MMA into TMEM buffer
+//               b % PG_NB once tempty[buffer] says its previous block was read
+//               back; the MMA's commit arrives on tfull[buffer] and empty[stage];
+//   warps 2..9  read each block's accumulator back (tcgen05.ld: warp w reads
+//               TMEM lanes 32 (w % 4) .., columns 32 ((w - 2) / 4) ..), release
+//               the buffer and the stage, and advance their 32 fp32 chains.
+// No CTA-wide barrier per block: the tensor core runs up to PG_NB blocks ahead
+// of the epilogue and the loads PG_D blocks ahead of the tensor core.
 template <int OUT>   // 0: y = acc (+ residual), 1: SwiGLU of interleaved (gate, up) rows
 __global__ void __launch_bounds__(PG_THREADS, 2)
 k_prefill_gemm(const uint8_t * __restrict__ Wn, const uint8_t * __restrict__ Ws, int64_t N, int64_t K,
@@ -114,12 +139,13 @@ k_prefill_gemm(const uint8_t * __restrict__ Wn, const uint8_t * __restrict__ Ws,
     const int64_t n0 = (int64_t)blockIdx.x * PG_N, m0 = (int64_t)blockIdx.y * PG_M;
     const int64_t nb = K / 32, rb = q4_row_bytes(K);   // row-interleaved layout: nibbles at 0, scales at K/2
     if (tid == 0) {
-        alb_mbar_init(&sh.mma_done[0], 1);
-        alb_mbar_init(&sh.mma_done[1], 1);
+        for (int i = 0; i < PG_D; ++i) { alb_mbar_init(&sh.full[i], 1); alb_mbar_init(&sh.empty[i], 1 + PG_EW); }
+        for (int i = 0; i < PG_NB; ++i) { alb_mbar_init(&sh.tfull[i], 2); alb_mbar_init(&sh.tempty[i], PG_EW); }
+        alb_mbar_init(&sh.drain, 1);
         sh.abort_flag = 0;
         alb_mbar_fence_init();
     }
-    if (warp == 0) {
+    if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
                      :: "r"(pg_smem(&sh.tmem_base)), "r"(PG_TMEM_COLS) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -130,144 +156,150 @@ k_prefill_gemm(const uint8_t * __restrict__ Wn, const uint8_t * __restrict__ Ws,
     const uint32_t tmem = sh.tmem_base;
     alb_pdl_wait();
 
-    // epilogue mapping: warp w reads TMEM lanes 32*(w%4).., columns 32*(w/4)..
-    const int quarter = warp & 3, chalf = warp >> 2;
-    const int row = quarter * 32 + lane;                 // token row within the tile
+    const int quarter = warp & 3, chalf = (warp - 2) >> 2;   // epilogue warps
+    const int row = quarter * 32 + lane;                     // token row within the tile
     float acc[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) acc[j] = 0.0f;
-    uint32_t issued = 0, waited = 0;                     // MMAs committed / completions consumed (per buffer parity)
 
-    // cp.async of block kb's inputs into ring stage kb % PG_STAGES (zero-filled past M / N)
-    auto prefetch = [&](int64_t kb) {
-        const int st = (int)(kb % PG_STAGES);
-        if (kb < nb) {
-            {   // A: thread t -> row t/2, chunk t%2 (16 B)
-                const int r = tid >> 1, c = tid & 1;
+    if (warp == 0) {
+        // ------------------------------------------------------------ loads
+        int64_t published = 0;   // blocks published on full[]
+        for (int64_t b = 0; b < nb; ++b) {
+            const int st = (int)(b % PG_D);
+            if (b >= PG_D && !pg_wait(sh, &sh.empty[st], (uint32_t)((b / PG_D - 1) & 1), err)) break;
+            if (pg_aborted(sh)) break;
+            for (int i = lane; i < PG_M * 2; i += 32) {   // A: row i/2, 16-byte chunk i%2
+                const int r = i >> 1, c = i & 1;
                 const bool in = m0 + r < M;
-                const int8_t * src = xq + (in ? (m0 + r) * K + kb * 32 + c * 16 : 0);
+                const int8_t * src = xq + (in ? (m0 + r) * K + b * 32 + c * 16 : 0);
                 asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;"
                              :: "r"(pg_smem(sh.a[st] + pg_off(r, c))), "l"(src), "r"(in ? 16 : 0) : "memory");
             }
-            if (tid < PG_N) {
-                const bool in = n0 + tid < N;
-                const uint8_t * src = Wn + (in ? (n0 + tid) * rb + kb * 16 : 0);
-                asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;"
-                             :: "r"(pg_smem(sh.nib[st] + tid * 16)), "l"(src), "r"(in ? 16 : 0) : "memory");
-            } else if (tid < 2 * PG_N) {
-                const int n = tid - PG_N;
+#pragma unroll
+            for (int k = 0; k < PG_N / 32; ++k) {        // nibbles and the scale word of rows lane, lane + 32
+                const int n = lane + 32 * k;
                 const bool in = n0 + n < N;
-                const uint8_t * src = Ws + (in ? ((n0 + n) * rb + ((kb * 2) & ~(int64_t)3)) : 0);
+                const uint8_t * srcn = Wn + (in ? (n0 + n) * rb + b * 16 : 0);
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;"
+                             :: "r"(pg_smem(sh.nib[st] + n * 16)), "l"(srcn), "r"(in ? 16 : 0) : "memory");
+                const uint8_t * srcs = Ws + (in ? ((n0 + n) * rb + ((b * 2) & ~(int64_t)3)) : 0);
                 asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;"
-                             :: "r"(pg_smem(&sh.dww[st][n])), "l"(src), "r"(in ? 4 : 0) : "memory");
-            } else {
-                const int r = tid - 2 * PG_N;
+                             :: "r"(pg_smem(&sh.dww[st][n])), "l"(srcs), "r"(in ? 4 : 0) : "memory");
+            }
+#pragma unroll
+            for (int k = 0; k < PG_M / 32; ++k) {        // activation scales of rows lane + 32 k
+                const int r = lane + 32 * k;
                 const bool in = m0 + r < M;
-                const float * src = xd + (in ? (m0 + r) * nb + kb : 0);
+                const float * src = xd + (in ? (m0 + r) * nb + b : 0);
                 asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;"
                              :: "r"(pg_smem(&sh.dx[st][r])), "l"(src), "r"(in ? 4 : 0) : "memory");
             }
+            asm volatile("cp.async.commit_group;" ::: "memory");
+            if (b >= PG_LAG) {   // block b - PG_LAG has landed: fence it for the tensor core, publish it
+                asm volatile("cp.async.wait_group %0;" :: "n"(PG_LAG) : "memory");
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) alb_mbar_arrive(&sh.full[(int)((b - PG_LAG) % PG_D)]);
+            }
+            published = b - PG_LAG + 1;
         }
-        asm volatile("cp.async.commit_group;" ::: "memory");   // one group per block (empty past the end)
-    };
-
-    // dxr: this thread's token-row scale of block kb, read from the ring when the
-    // block landed (the ring stage is refilled by other warps while this one may
-    // still be in its epilogue, so the scale is carried in a register)
-    auto epilogue = [&](int64_t kb, float dxr) {
-        const int s = (int)(kb & 1);
-        pg_fence_after();
-        uint32_t c[32];
-        const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(s * PG_N + chalf * 32);
-        asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-                     "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-                     "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-                     : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3]), "=r"(c[4]), "=r"(c[5]), "=r"(c[6]), "=r"(c[7]),
-                       "=r"(c[8]), "=r"(c[9]), "=r"(c[10]), "=r"(c[11]), "=r"(c[12]), "=r"(c[13]), "=r"(c[14]),
-                       "=r"(c[15]), "=r"(c[16]), "=r"(c[17]), "=r"(c[18]), "=r"(c[19]), "=r"(c[20]), "=r"(c[21]),
-                       "=r"(c[22]), "=r"(c[23]), "=r"(c[24]), "=r"(c[25]), "=r"(c[26]), "=r"(c[27]), "=r"(c[28]),
-                       "=r"(c[29]), "=r"(c[30]), "=r"(c[31])
-                     : "r"(taddr));
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        const float * dw = sh.dwf[s] + chalf * 32;
-        // float(I) exactly as 2^23 * 1.5 + I - 2^23 * 1.5 (|I| < 2^22): integer add +
-        // fp32 subtract instead of a conversion; dx * dw is exact (11 x 11 bits)
+        asm volatile("cp.async.wait_all;" ::: "memory");   // no copy in flight past this point
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (!pg_aborted(sh) && lane == 0)
+            for (int64_t j = published < 0 ? 0 : published; j < nb; ++j) alb_mbar_arrive(&sh.full[(int)(j % PG_D)]);
+    } else if (warp == 1) {
+        // ------------------------------------------- unpack + MMA issue
+        for (int64_t b = 0; b < nb; ++b) {
+            const int st = (int)(b % PG_D), tb = (int)(b % PG_NB);
+            if (pg_aborted(sh)) break;
+            if (!pg_wait(sh, &sh.full[st], (uint32_t)((b / PG_D) & 1), err)) break;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-            const float t = __fsub_rn(__int_as_float((int)c[j] + 0x4B400000), 12582912.0f);
-            acc[j] = __fmaf_rn(t, __fmul_rn(dxr, dw[j]), acc[j]);
+            for (int k = 0; k < PG_N / 32; ++k) {        // rows lane, lane + 32: 16 nibble bytes -> 2 chunks of int8 (q - 8)
+                const int n = lane + 32 * k;
+                const uint4 w = *reinterpret_cast<const uint4 *>(sh.nib[st] + n * 16);
+                const uint4 lo = make_uint4(__vsub4(w.x & 0x0F0F0F0Fu, 0x08080808u), __vsub4(w.y & 0x0F0F0F0Fu, 0x08080808u),
+                                            __vsub4(w.z & 0x0F0F0F0Fu, 0x08080808u), __vsub4(w.w & 0x0F0F0F0Fu, 0x08080808u));
+                const uint4 hi = make_uint4(__vsub4((w.x >> 4) & 0x0F0F0F0Fu, 0x08080808u),
+                                            __vsub4((w.y >> 4) & 0x0F0F0F0Fu, 0x08080808u),
+                                            __vsub4((w.z >> 4) & 0x0F0F0F0Fu, 0x08080808u),
+                                            __vsub4((w.w >> 4) & 0x0F0F0F0Fu, 0x08080808u));
+                *reinterpret_cast<uint4 *>(sh.b[st] + pg_off(n, 0)) = lo;
+                *reinterpret_cast<uint4 *>(sh.b[st] + pg_off(n, 1)) = hi;
+                const uint32_t wd = sh.dww[st][n];
+                sh.dwf[st][n] = alb_h2f((uint16_t)((b & 1) ? (wd >> 16) : (wd & 0xFFFFu)));
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic stores -> tensor core
+            __syncwarp();
+            if (b >= PG_NB && !pg_wait(sh, &sh.tempty[tb], (uint32_t)((b / PG_NB - 1) & 1), err)) break;
+            if (lane == 0) {
+                pg_fence_after();
+                const uint64_t da = pg_desc(sh.a[st]), db = pg_desc(sh.b[st]);
+                const uint32_t zero = 0;
+                asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                             "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}"
+                             :: "r"(tmem + (uint32_t)(tb * PG_N)), "l"(da), "l"(db), "r"(PG_IDESC), "r"(zero), "r"(zero)
+                             : "memory");
+                asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                             :: "r"(pg_smem(&sh.tfull[tb])) : "memory");
+                asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                             :: "r"(pg_smem(&sh.empty[st])) : "memory");
+                alb_mbar_arrive(&sh.tfull[tb]);   // release: this block's dwf (and the loads this warp observed)
+            }
+            __syncwarp();
         }
-        pg_fence_before();
-    };
-
-    for (int64_t kb = 0; kb < PG_STAGES - 1; ++kb) prefetch(kb);
-    bool ok = true;
-    float dx_prev = 0.0f, dx_cur = 0.0f;   // this row's activation scales of blocks b-1 and b
-    for (int64_t b = 0; b < nb && ok; ++b) {
-        const int s = (int)(b & 1), st = (int)(b % PG_STAGES);
-        asm volatile("cp.async.wait_group %0;" :: "n"(PG_STAGES - 2) : "memory");   // block b has landed
-        __syncthreads();
-        dx_prev = dx_cur;
-        dx_cur = sh.dx[st][row];   // stage st is refilled only after the next iteration's epilogue
-        if (tid >= PG_N && tid < 2 * PG_N) {   // weight scales of block b, once per block
-            const int n = tid - PG_N;
-            const uint32_t wd = sh.dww[st][n];
-            sh.dwf[s][n] = alb_h2f((uint16_t)((b & 1) ? (wd >> 16) : (wd & 0xFFFFu)));
-        }
-        if (tid < PG_N) {   // B: 16 nibble bytes of row tid -> 2 chunks of int8 (q - 8)
-            const uint4 w = *reinterpret_cast<const uint4 *>(sh.nib[st] + tid * 16);
-            const uint4 lo = make_uint4(__vsub4(w.x & 0x0F0F0F0Fu, 0x08080808u), __vsub4(w.y & 0x0F0F0F0Fu, 0x08080808u),
-                                        __vsub4(w.z & 0x0F0F0F0Fu, 0x08080808u), __vsub4(w.w & 0x0F0F0F0Fu, 0x08080808u));
-            const uint4 hi = make_uint4(__vsub4((w.x >> 4) & 0x0F0F0F0Fu, 0x08080808u),
-                                        __vsub4((w.y >> 4) & 0x0F0F0F0Fu, 0x08080808u),
-                                        __vsub4((w.z >> 4) & 0x0F0F0F0Fu, 0x08080808u),
-                                        __vsub4((w.w >> 4) & 0x0F0F0F0Fu, 0x08080808u));
-            *reinterpret_cast<uint4 *>(sh.b[s] + pg_off(tid, 0)) = lo;
-            *reinterpret_cast<uint4 *>(sh.b[s] + pg_off(tid, 1)) = hi;
-        }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic / cp.async stores -> tensor core
-        __syncthreads();
-        if (tid == 0) {
-            pg_fence_after();
-            const uint64_t da = pg_desc(sh.a[st]), db = pg_desc(sh.b[s]);
-            const uint32_t zero = 0;
-            asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-                         "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}"
-                         :: "r"(tmem + (uint32_t)(s * PG_N)), "l"(da), "l"(db), "r"(PG_IDESC), "r"(zero), "r"(zero)
-                         : "memory");
+        if (lane == 0) {   // every MMA issued by this thread complete (the TMEM is freed below)
             asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
-                         :: "r"(pg_smem(&sh.mma_done[s])) : "memory");
+                         :: "r"(pg_smem(&sh.drain)) : "memory");
+            pg_wait(sh, &sh.drain, 0u, err);
         }
-        ++issued;
-        if (b > 0) {   // block b-1 (other TMEM buffer) while the tensor core works on block b
-            ok = pg_wait(sh, s ^ 1, (uint32_t)(((b - 1) >> 1) & 1), err);
-            if (ok) { epilogue(b - 1, dx_prev); ++waited; }
-        }
-        // block b-1 is consumed (MMA done, scales read): its ring stage takes block b + PG_STAGES - 1
-        prefetch(b + PG_STAGES - 1);
-        __syncthreads();
-        if (sh.abort_flag) ok = false;
-    }
-    if (ok) {
-        const int64_t b = nb - 1;
-        ok = pg_wait(sh, (int)(b & 1), (uint32_t)((b >> 1) & 1), err);
-        if (ok) { epilogue(b, dx_cur); ++waited; }
-    }
-    asm volatile("cp.async.wait_all;" ::: "memory");   // no copy in flight past this point
-    if (!ok) {
-        // every committed MMA must have completed before the TMEM is freed
-        for (uint32_t q = waited; q < issued; ++q) {
-            const int64_t b = q;
-            alb_mbar_wait(&sh.mma_done[b & 1], (uint32_t)((b >> 1) & 1));
+        __syncwarp();
+    } else {
+        // --------------------------------------------------- epilogue warps
+        for (int64_t b = 0; b < nb; ++b) {
+            const int st = (int)(b % PG_D), tb = (int)(b % PG_NB);
+            if (pg_aborted(sh)) break;
+            if (!pg_wait(sh, &sh.tfull[tb], (uint32_t)((b / PG_NB) & 1), err)) break;
+            pg_fence_after();
+            uint32_t c[32];
+            const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(tb * PG_N + chalf * 32);
+            asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+                         "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                         "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                         : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3]), "=r"(c[4]), "=r"(c[5]), "=r"(c[6]), "=r"(c[7]),
+                           "=r"(c[8]), "=r"(c[9]), "=r"(c[10]), "=r"(c[11]), "=r"(c[12]), "=r"(c[13]), "=r"(c[14]),
+                           "=r"(c[15]), "=r"(c[16]), "=r"(c[17]), "=r"(c[18]), "=r"(c[19]), "=r"(c[20]), "=r"(c[21]),
+                           "=r"(c[22]), "=r"(c[23]), "=r"(c[24]), "=r"(c[25]), "=r"(c[26]), "=r"(c[27]), "=r"(c[28]),
+                           "=r"(c[29]), "=r"(c[30]), "=r"(c[31])
+                         : "r"(taddr));
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            const float dxr = sh.dx[st][row];
+            float dw[32];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float4 v = *reinterpret_cast<const float4 *>(&sh.dwf[st][chalf * 32 + 4 * j]);
+                dw[4 * j] = v.x; dw[4 * j + 1] = v.y; dw[4 * j + 2] = v.z; dw[4 * j + 3] = v.w;
+            }
+            pg_fence_before();
+            __syncwarp();
+            if (lane == 0) { alb_mbar_arrive(&sh.tempty[tb]); alb_mbar_arrive(&sh.empty[st]); }
+            // float(I) exactly as 2^23 * 1.5 + I - 2^23 * 1.5 (|I| < 2^22): integer add +
+            // fp32 subtract instead of a conversion; dx * dw is exact (11 x 11 bits)
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const float t = __fsub_rn(__int_as_float((int)c[j] + 0x4B400000), 12582912.0f);
+                acc[j] = __fmaf_rn(t, __fmul_rn(dxr, dw[j]), acc[j]);
+            }
         }
     }
     pg_fence_before();
     __syncthreads();
-    if (warp == 0) {
+    if (warp == 1) {
         pg_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(PG_TMEM_COLS) : "memory");
     }
-    if (!ok) return;
+    if (warp < 2 || pg_aborted(sh)) return;
     const int64_t m = m0 + row;
     if (m >= M) return;
     const int64_t nbase = n0 + chalf * 32;

@@ -216,6 +216,7 @@ __device__ __forceinline__ void mv_prologue(const GemvArgs & a, int * xs, int nb
         }
     } else {
         const float * x = static_cast<const float *>(a.x);
+        const double inv_k = 1.0 / (double)a.K;   // independent of the loads below
         float * xf = reinterpret_cast<float *>(stage);
         float * wf = xf + a.K;   // the norm weights: staged before the dependency wait
         const int K = (int)a.K;
@@ -237,15 +238,13 @@ __device__ __forceinline__ void mv_prologue(const GemvArgs & a, int * xs, int nb
             for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
             if (lane == 0) red[warp] = s;
             asm volatile("bar.sync 1, %0;" :: "n"(NT) : "memory");
-            double t = 0.0;
-#pragma unroll
-            for (int w = 0; w < NW; ++w) t += red[w];
-            if (!alb_rms_mean_certain(t, K)) {   // uniform across the CTA
+            const double t = alb_tree_sum<NW>(red);
+            float mean;
+            if (!alb_rms_mean_cert(t, K, inv_k, mean)) {   // uniform across the CTA
                 if (tid == 0) seq_sum = alb_rms_seq_sum(xf, K);
                 asm volatile("bar.sync 1, %0;" :: "n"(NT) : "memory");
-                t = seq_sum;
+                mean = (float)(seq_sum / (double)a.K);
             }
-            const float mean = (float)(t / (double)a.K);
             scale = 1.0f / sqrtf(__fadd_rn(mean, a.eps));
         }
         // quantize_row_q8_0: four threads per block, eight values each (whole

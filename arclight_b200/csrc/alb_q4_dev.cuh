@@ -72,6 +72,15 @@ __device__ __forceinline__ float alb_mul_f16_exact(unsigned short a, unsigned sh
     return r;
 }
 
+// fma(f32(a), f32(b), c) with one rounding, a and b given as fp16 bits: the
+// mixed-precision fma of sm_100 (the fp16 product is exact in fp32, so this is
+// the fp32 fma of the converted values, without the conversions).
+__device__ __forceinline__ float alb_fma_f16_f32(unsigned short a, unsigned short b, float c) {
+    float r;
+    asm("fma.rn.f32.f16 %0, %1, %2, %3;" : "=f"(r) : "h"(a), "h"(b), "f"(c));
+    return r;
+}
+
 // fp16 bits -> the bits of (value * 2^-1008) as a double (see alb_h2d), without
 // the final scaling; pairs with an operand pre-scaled by 2^1008.
 __device__ __forceinline__ double alb_h2d_bits(uint32_t h) {
