@@ -30,22 +30,25 @@ static constexpr int PG_N = 64;           // weight rows per tile (TMEM columns 
 static constexpr int PG_D = 5;            // operand ring stages (blocks of K in flight)
 static constexpr int PG_LAG = 2;          // blocks the loader keeps in flight before publishing one
 static constexpr int PG_NB = 4;           // TMEM accumulator buffers (blocks the MMA may run ahead)
-static constexpr int PG_EW = 8;           // epilogue warps
-static constexpr int PG_THREADS = (2 + PG_EW) * 32;   // warp 0 loads, warp 1 unpacks + issues, 2.. epilogue
+static constexpr int PG_NI = PG_NB;       // unpack + MMA-issue warps (issuer i: blocks i, i + PG_NI, .., TMEM buffer i)
+static constexpr int PG_EW = 4 * (PG_N / 32);   // epilogue warps: 4 TMEM lane quarters x 32-column groups
+static constexpr int PG_E0 = 1 + PG_NI;   // first epilogue warp
+static constexpr int PG_THREADS = (1 + PG_NI + PG_EW) * 32;   // warp 0 loads, 1..PG_NI issue, then the epilogue
 static constexpr uint32_t PG_TMEM_COLS = PG_NB * PG_N;
+static constexpr int PG_CTAS = 512 / PG_TMEM_COLS;   // CTAs per SM (the SM's 512 TMEM columns)
 
 struct PgShared {
     alignas(128) int8_t a[PG_D][PG_M * 32];   // MMA operand A per stage (core-matrix layout)
     alignas(128) int8_t b[PG_D][PG_N * 32];   // MMA operand B (nibbles unpacked to int8 q - 8) per stage
     alignas(16) uint8_t nib[PG_D][PG_N * 16]; // W nibbles as loaded
     alignas(16) float dx[PG_D][PG_M];         // activation block scales (fp16-rounded)
-    alignas(16) uint32_t dww[PG_D][PG_N];     // 4-byte words holding the weight block scale
+    alignas(16) uint16_t dws[2][PG_N][8];     // weight scales of blocks 8j .. 8j+7 (slot j % 2), one 16-byte load per row
     alignas(16) float dwf[PG_D][PG_N];        // weight block scale as fp32
     uint64_t full[PG_D];                      // stage loaded and fenced for the tensor core (loader lane 0)
     uint64_t empty[PG_D];                     // stage consumed (its MMA + the epilogue warps' scale reads)
     uint64_t tfull[PG_NB];                    // accumulator ready (MMA commit + the issuer's dwf release)
     uint64_t tempty[PG_NB];                   // accumulator read back (epilogue warps)
-    uint64_t drain;                           // every MMA of the CTA complete
+    uint64_t drain;                           // every MMA of the CTA complete (one commit per issuer)
     uint32_t tmem_base;
     int abort_flag;
 };
@@ -70,9 +73,13 @@ __device__ __forceinline__ int pg_off(int r, int c) { return (r >> 3) * 256 + c 
 __device__ __forceinline__ void pg_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void pg_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// Activations of the GEMM: xq int8 [M][K] row-major, xd float [M][K/32]
-// (fp16-rounded Q8_0 scale), from fp32 rows (one warp per 32-value block,
-// quantize_row_q8_0 semantics, arm.cpp:1819-1853).
+// Activations of the GEMM: xq int8 [M][K] row-major, xd float [K/32][Mp]
+// (block-major, Mp = M rounded up to 4: one block's scales of 128 tokens are
+// one contiguous 512-byte run) holding the fp16-rounded Q8_0 scales, from fp32
+// rows (one warp per 32-value block, quantize_row_q8_0 semantics,
+// arm.cpp:1819-1853).
+__host__ __device__ inline int64_t pg_mpad(int64_t M) { return (M + 3) & ~(int64_t)3; }
+
 __global__ void k_pg_quant(const float * __restrict__ x, int64_t M, int64_t K, int8_t * __restrict__ xq,
                            float * __restrict__ xd) {
     alb_pdl_wait();
@@ -86,7 +93,7 @@ __global__ void k_pg_quant(const float * __restrict__ x, int64_t M, int64_t K, i
     uint16_t dh;
     q8_block_lane(v, q, dh);
     xq[m * K + b * 32 + lane] = q;
-    if (lane == 0) xd[m * nb + b] = alb_h2f(dh);
+    if (lane == 0) xd[b * pg_mpad(M) + m] = alb_h2f(dh);
 }
 
 // Same from block_q8_0 rows (the reference layout, nnml.h:695-700).
@@ -98,7 +105,7 @@ __global__ void k_pg_from_q8(const uint8_t * __restrict__ src, int64_t M, int64_
     if (blk >= M * nb) return;
     const uint8_t * s = src + blk * 34;
     const uint16_t dh = (uint16_t)(s[0] | (s[1] << 8));
-    xd[blk] = alb_h2f(dh);
+    xd[(blk % nb) * pg_mpad(M) + blk / nb] = alb_h2f(dh);
     int8_t * d = xq + blk * 32;   // row-major [M][K]: block blk = m * nb + b lands at m*K + 32 b
     for (int j = 0; j < 32; ++j) d[j] = (int8_t)s[2 + j];
 }
@@ -120,28 +127,33 @@ __device__ __forceinline__ bool pg_aborted(PgShared & sh) { return *reinterpret_
 //               PG_LAG blocks later its lanes wait for those copies, fence them
 //               for the async proxy (the tensor core reads A) and lane 0
 //               publishes the stage on full[stage];
-//   warp 1      unpacks the nibbles into the B operand, converts the weight
-//               scales, and (lane 0) issues the block's MMA into TMEM buffer
-//               b % PG_NB once tempty[buffer] says its previous block was read
-//               back; the MMA's commit arrives on tfull[buffer] and empty[stage];
-//   warps 2..9  read each block's accumulator back (tcgen05.ld: warp w reads
-//               TMEM lanes 32 (w % 4) .., columns 32 ((w - 2) / 4) ..), release
-//               the buffer and the stage, and advance their 32 fp32 chains.
+//   warps 1..4  (issuer i: blocks i, i + 4, ..; TMEM buffer i) unpack the
+//               nibbles into the B operand, convert the weight scales, and
+//               (lane 0) issue the block's MMA once tempty[i] says the buffer's
+//               previous block was read back; the MMA's commit arrives on
+//               tfull[i] and empty[stage].  One issuer's serial path (waits,
+//               unpack, proxy fence, issue) is ~1.2 us per block: four of them
+//               keep the tensor core and the epilogue fed;
+//   warps 5..12 read each block's accumulator back (tcgen05.ld: warp w reads
+//               TMEM lanes 32 (w % 4) .., columns 32 ((w - 5) / 4) ..), release
+//               the buffer, advance their 32 fp32 chains, release the stage.
 // No CTA-wide barrier per block: the tensor core runs up to PG_NB blocks ahead
 // of the epilogue and the loads PG_D blocks ahead of the tensor core.
 template <int OUT>   // 0: y = acc (+ residual), 1: SwiGLU of interleaved (gate, up) rows
-__global__ void __launch_bounds__(PG_THREADS, 2)
+__global__ void __launch_bounds__(PG_THREADS, PG_CTAS)
 k_prefill_gemm(const uint8_t * __restrict__ Wn, const uint8_t * __restrict__ Ws, int64_t N, int64_t K,
                const int8_t * __restrict__ xq, const float * __restrict__ xd, int64_t M, float * __restrict__ y,
                int64_t y_stride, const float * __restrict__ residual, int * err) {
-    __shared__ PgShared sh;
+    extern __shared__ __align__(128) uint8_t pg_dyn[];
+    PgShared & sh = *reinterpret_cast<PgShared *>(pg_dyn);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t n0 = (int64_t)blockIdx.x * PG_N, m0 = (int64_t)blockIdx.y * PG_M;
     const int64_t nb = K / 32, rb = q4_row_bytes(K);   // row-interleaved layout: nibbles at 0, scales at K/2
+    const int64_t Mp = pg_mpad(M);                       // row stride of the block-major activation scales
     if (tid == 0) {
         for (int i = 0; i < PG_D; ++i) { alb_mbar_init(&sh.full[i], 1); alb_mbar_init(&sh.empty[i], 1 + PG_EW); }
         for (int i = 0; i < PG_NB; ++i) { alb_mbar_init(&sh.tfull[i], 2); alb_mbar_init(&sh.tempty[i], PG_EW); }
-        alb_mbar_init(&sh.drain, 1);
+        alb_mbar_init(&sh.drain, PG_NI);
         sh.abort_flag = 0;
         alb_mbar_fence_init();
     }
@@ -156,7 +168,7 @@ k_prefill_gemm(const uint8_t * __restrict__ Wn, const uint8_t * __restrict__ Ws,
     const uint32_t tmem = sh.tmem_base;
     alb_pdl_wait();
 
-    const int quarter = warp & 3, chalf = (warp - 2) >> 2;   // epilogue warps
+    const int quarter = warp & 3, chalf = (warp - PG_E0) >> 2;   // epilogue warps: lane quarter, 32-column group
     const int row = quarter * 32 + lane;                     // token row within the tile
     float acc[32];
 #pragma unroll
@@ -177,23 +189,26 @@ k_prefill_gemm(const uint8_t * __restrict__ Wn, const uint8_t * __restrict__ Ws,
                              :: "r"(pg_smem(sh.a[st] + pg_off(r, c))), "l"(src), "r"(in ? 16 : 0) : "memory");
             }
 #pragma unroll
-            for (int k = 0; k < PG_N / 32; ++k) {        // nibbles and the scale word of rows lane, lane + 32
+            for (int k = 0; k < PG_N / 32; ++k) {        // nibbles of rows lane, lane + 32 (and every 8 blocks their scales)
                 const int n = lane + 32 * k;
                 const bool in = n0 + n < N;
                 const uint8_t * srcn = Wn + (in ? (n0 + n) * rb + b * 16 : 0);
                 asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;"
                              :: "r"(pg_smem(sh.nib[st] + n * 16)), "l"(srcn), "r"(in ? 16 : 0) : "memory");
-                const uint8_t * srcs = Ws + (in ? ((n0 + n) * rb + ((b * 2) & ~(int64_t)3)) : 0);
-                asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;"
-                             :: "r"(pg_smem(&sh.dww[st][n])), "l"(srcs), "r"(in ? 4 : 0) : "memory");
+                if ((b & 7) == 0) {   // scales of blocks b .. b+7 (16 bytes, zero past the row's last block)
+                    const int64_t nbytes = (nb - b) * 2 < 16 ? (nb - b) * 2 : 16;
+                    const uint8_t * srcs = Ws + (in ? (n0 + n) * rb + b * 2 : 0);
+                    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;"
+                                 :: "r"(pg_smem(sh.dws[(b >> 3) & 1][n])), "l"(srcs), "r"(in ? (int)nbytes : 0) : "memory");
+                }
             }
-#pragma unroll
-            for (int k = 0; k < PG_M / 32; ++k) {        // activation scales of rows lane + 32 k
-                const int r = lane + 32 * k;
-                const bool in = m0 + r < M;
-                const float * src = xd + (in ? (m0 + r) * nb + b : 0);
-                asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;"
-                             :: "r"(pg_smem(&sh.dx[st][r])), "l"(src), "r"(in ? 4 : 0) : "memory");
+            {   // activation scales of the 128 rows: one contiguous run of the block-major xd
+                const int r = 4 * lane;
+                const int64_t left = M - (m0 + r);
+                const int bytes = left >= 4 ? 16 : left > 0 ? (int)left * 4 : 0;
+                const float * src = xd + (bytes ? b * Mp + m0 + r : 0);
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;"
+                             :: "r"(pg_smem(&sh.dx[st][r])), "l"(src), "r"(bytes) : "memory");
             }
             asm volatile("cp.async.commit_group;" ::: "memory");
             if (b >= PG_LAG) {   // block b - PG_LAG has landed: fence it for the tensor core, publish it
@@ -209,10 +224,11 @@ k_prefill_gemm(const uint8_t * __restrict__ Wn, const uint8_t * __restrict__ Ws,
         __syncwarp();
         if (!pg_aborted(sh) && lane == 0)
             for (int64_t j = published < 0 ? 0 : published; j < nb; ++j) alb_mbar_arrive(&sh.full[(int)(j % PG_D)]);
-    } else if (warp == 1) {
+    } else if (warp < PG_E0) {
         // ------------------------------------------- unpack + MMA issue
-        for (int64_t b = 0; b < nb; ++b) {
-            const int st = (int)(b % PG_D), tb = (int)(b % PG_NB);
+        const int tb = warp - 1;   // this issuer's TMEM buffer; its blocks are tb, tb + PG_NI, ..
+        for (int64_t b = tb; b < nb; b += PG_NI) {
+            const int st = (int)(b % PG_D);
             if (pg_aborted(sh)) break;
             if (!pg_wait(sh, &sh.full[st], (uint32_t)((b / PG_D) & 1), err)) break;
 #pragma unroll
@@ -227,8 +243,7 @@ k_prefill_gemm(const uint8_t * __restrict__ Wn, const uint8_t * __restrict__ Ws,
                                             __vsub4((w.w >> 4) & 0x0F0F0F0Fu, 0x08080808u));
                 *reinterpret_cast<uint4 *>(sh.b[st] + pg_off(n, 0)) = lo;
                 *reinterpret_cast<uint4 *>(sh.b[st] + pg_off(n, 1)) = hi;
-                const uint32_t wd = sh.dww[st][n];
-                sh.dwf[st][n] = alb_h2f((uint16_t)((b & 1) ? (wd >> 16) : (wd & 0xFFFFu)));
+                sh.dwf[st][n] = alb_h2f(sh.dws[(b >> 3) & 1][n][b & 7]);
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic stores -> tensor core
             __syncwarp();
@@ -262,35 +277,42 @@ k_prefill_gemm(const uint8_t * __restrict__ Wn, const uint8_t * __restrict__ Ws,
             if (pg_aborted(sh)) break;
             if (!pg_wait(sh, &sh.tfull[tb], (uint32_t)((b / PG_NB) & 1), err)) break;
             pg_fence_after();
-            uint32_t c[32];
             const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(tb * PG_N + chalf * 32);
-            asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-                         "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-                         "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-                         : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3]), "=r"(c[4]), "=r"(c[5]), "=r"(c[6]), "=r"(c[7]),
-                           "=r"(c[8]), "=r"(c[9]), "=r"(c[10]), "=r"(c[11]), "=r"(c[12]), "=r"(c[13]), "=r"(c[14]),
-                           "=r"(c[15]), "=r"(c[16]), "=r"(c[17]), "=r"(c[18]), "=r"(c[19]), "=r"(c[20]), "=r"(c[21]),
-                           "=r"(c[22]), "=r"(c[23]), "=r"(c[24]), "=r"(c[25]), "=r"(c[26]), "=r"(c[27]), "=r"(c[28]),
-                           "=r"(c[29]), "=r"(c[30]), "=r"(c[31])
-                         : "r"(taddr));
-            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
             const float dxr = sh.dx[st][row];
-            float dw[32];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const float4 v = *reinterpret_cast<const float4 *>(&sh.dwf[st][chalf * 32 + 4 * j]);
-                dw[4 * j] = v.x; dw[4 * j + 1] = v.y; dw[4 * j + 2] = v.z; dw[4 * j + 3] = v.w;
-            }
-            pg_fence_before();
-            __syncwarp();
-            if (lane == 0) { alb_mbar_arrive(&sh.tempty[tb]); alb_mbar_arrive(&sh.empty[st]); }
+            const float * dwp = &sh.dwf[st][chalf * 32];
+            // two halves of 16 columns (16 accumulator words live at a time); the
+            // buffer is released once the second half is in registers.
             // float(I) exactly as 2^23 * 1.5 + I - 2^23 * 1.5 (|I| < 2^22): integer add +
             // fp32 subtract instead of a conversion; dx * dw is exact (11 x 11 bits)
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const float t = __fsub_rn(__int_as_float((int)c[j] + 0x4B400000), 12582912.0f);
-                acc[j] = __fmaf_rn(t, __fmul_rn(dxr, dw[j]), acc[j]);
+            for (int hf = 0; hf < 2; ++hf) {
+                uint32_t c[16];
+                asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+                             "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+                             : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3]), "=r"(c[4]), "=r"(c[5]), "=r"(c[6]),
+                               "=r"(c[7]), "=r"(c[8]), "=r"(c[9]), "=r"(c[10]), "=r"(c[11]), "=r"(c[12]), "=r"(c[13]),
+                               "=r"(c[14]), "=r"(c[15])
+                             : "r"(taddr + (uint32_t)(16 * hf)));
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                if (hf == 1) {
+                    pg_fence_before();
+                    __syncwarp();
+                    if (lane == 0) alb_mbar_arrive(&sh.tempty[tb]);   // the accumulator is in registers
+                }
+#pragma unroll
+                for (int j4 = 0; j4 < 4; ++j4) {
+                    const float4 w4 = *reinterpret_cast<const float4 *>(dwp + 16 * hf + 4 * j4);
+                    const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int j = 16 * hf + 4 * j4 + u;
+                        const float t = __fsub_rn(__int_as_float((int)c[4 * j4 + u] + 0x4B400000), 12582912.0f);
+                        acc[j] = __fmaf_rn(t, __fmul_rn(dxr, wv[u]), acc[j]);
+                    }
+                }
             }
+            __syncwarp();
+            if (lane == 0) alb_mbar_arrive(&sh.empty[st]);   // the stage's scales are read
         }
     }
     pg_fence_before();
@@ -299,7 +321,7 @@ k_prefill_gemm(const uint8_t * __restrict__ Wn, const uint8_t * __restrict__ Ws,
         pg_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(PG_TMEM_COLS) : "memory");
     }
-    if (warp < 2 || pg_aborted(sh)) return;
+    if (warp < PG_E0 || pg_aborted(sh)) return;
     const int64_t m = m0 + row;
     if (m >= M) return;
     const int64_t nbase = n0 + chalf * 32;
@@ -324,7 +346,7 @@ k_prefill_gemm(const uint8_t * __restrict__ Wn, const uint8_t * __restrict__ Ws,
 
 size_t prefill_ws_bytes(int64_t M, int64_t K) {
     const size_t q = ((size_t)M * K + 255) & ~(size_t)255;
-    return q + (size_t)M * (K / 32) * 4;
+    return q + (size_t)pg_mpad(M) * (K / 32) * 4;
 }
 
 // x fp32 [M][K] (already normalized if needed) -> y: workspace prefill_ws_bytes(M, K)
@@ -332,7 +354,7 @@ cudaError_t launch_prefill_gemm(const uint8_t * W, int64_t N, int64_t K, const f
                                 int64_t M, float * y, int64_t y_stride, const float * residual, bool swiglu, void * ws,
                                 int * err, bool pdl, cudaStream_t st) {
     int8_t * xq = reinterpret_cast<int8_t *>(ws);
-    float * xd = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(ws) + (((size_t)M * K + 255) & ~(size_t)255));
+    float * xd = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(ws) + (((size_t)M * K + 255) & ~(size_t)255));   // [K/32][pg_mpad(M)]
     const int64_t nblk = M * (K / 32);
     cudaError_t e;
     if (x) e = alb_launch(k_pg_quant, dim3((unsigned)((nblk + 7) / 8)), dim3(256), 0, st, pdl, x, M, K, xq, xd);
@@ -341,10 +363,16 @@ cudaError_t launch_prefill_gemm(const uint8_t * W, int64_t N, int64_t K, const f
     if (e != cudaSuccess) return e;
     const dim3 grid((unsigned)((N + PG_N - 1) / PG_N), (unsigned)((M + PG_M - 1) / PG_M));
     const uint8_t * Ws = W + K / 2;   // scales of row n at Ws + n * q4_row_bytes(K)
-    if (swiglu)
-        return alb_launch(k_prefill_gemm<1>, grid, dim3(PG_THREADS), 0, st, pdl, W, Ws, N, K, (const int8_t *)xq,
+    const size_t smem = sizeof(PgShared);
+    if (swiglu) {
+        e = ensure_smem(k_prefill_gemm<1>, smem);
+        if (e != cudaSuccess) return e;
+        return alb_launch(k_prefill_gemm<1>, grid, dim3(PG_THREADS), smem, st, pdl, W, Ws, N, K, (const int8_t *)xq,
                           (const float *)xd, M, y, y_stride, residual, err);
-    return alb_launch(k_prefill_gemm<0>, grid, dim3(PG_THREADS), 0, st, pdl, W, Ws, N, K, (const int8_t *)xq,
+    }
+    e = ensure_smem(k_prefill_gemm<0>, smem);
+    if (e != cudaSuccess) return e;
+    return alb_launch(k_prefill_gemm<0>, grid, dim3(PG_THREADS), smem, st, pdl, W, Ws, N, K, (const int8_t *)xq,
                       (const float *)xd, M, y, y_stride, residual, err);
 }
 
