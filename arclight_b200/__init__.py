@@ -98,6 +98,8 @@ def _declare(L: C.CDLL) -> None:
         "alb_engine_stream": (vp, [vp]),
         "alb_engine_weight_blocks": (ci, [vp, i32, i32, vp, vp, vp]),
         "alb_engine_norm_weights": (ci, [vp, i32, i32, vp, i64]),
+        "alb_engine_set_weight_blocks": (ci, [vp, i32, i32, vp, i64, i64]),
+        "alb_engine_set_norm_weights": (ci, [vp, i32, i32, vp, i64]),
         "alb_engine_fill_kv": (ci, [vp, i32, C.c_uint64]),
         "alb_engine_time_gemv": (ci, [vp, i32, vp, vp]),
     }

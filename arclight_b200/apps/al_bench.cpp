@@ -3,17 +3,20 @@
 //
 // The counterpart of the reference's al-gen flow (apps/al-gen.cpp:13-141:
 // load the model, build the KV cache and graph, ctx.infer(prompt, max_gen),
-// ctx.print_perf()) over the C ABI of libalb_cuda.so.  There is no GGUF file
-// or tokenizer here: the model is the seeded synthetic Qwen3 of the named
-// shape (the engine generates it on the device) and the prompt is seeded
+// ctx.print_perf()) over the C ABI of libalb_cuda.so.  The model is either a
+// Qwen3 Q4_0 GGUF file (--gguf: configuration from its qwen3.* keys, tensors
+// uploaded through alb_engine_set_weight_blocks / _set_norm_weights, each rank
+// keeping its shard) or the seeded synthetic Qwen3 of a named shape (the engine
+// generates it on the device).  There is no tokenizer: the prompt is seeded
 // uniform token ids.  Tensor parallelism (--numa tp --nodes N in the
 // reference, model.cpp:21-54) runs one thread per GPU rank, all ranks joining
 // one NCCL clique.
 //
-//   al_bench [--model 0.6b|4b|8b|tiny|tiny_gqa] [--prompt N] [--max_gen M]
-//            [--max_length L] [--ubatch U] [--seed S] [--nodes N] [--loop]
-//            [--print_tokens]
+//   al_bench [--model 0.6b|4b|8b|tiny|tiny_gqa | --gguf FILE] [--prompt N]
+//            [--max_gen M] [--max_length L] [--ubatch U] [--seed S] [--nodes N]
+//            [--loop] [--print_tokens]
 #include <chrono>
+#include <memory>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -23,11 +26,13 @@
 #include <vector>
 
 #include "alb_cuda.h"
+#include "gguf_reader.h"
 
 namespace {
 
 struct Args {
     std::string model = "4b";
+    std::string gguf_path;
     int prompt = 512, max_gen = 128, max_length = 0, ubatch = 256, nodes = 1;
     unsigned long long seed = 1234;
     bool loop = false, print_tokens = false;
@@ -52,6 +57,7 @@ bool parse(int argc, char ** argv, Args & a) {
             return argv[++i];
         };
         if (k == "--model") a.model = val("--model");
+        else if (k == "--gguf") a.gguf_path = val("--gguf");
         else if (k == "--prompt") a.prompt = std::atoi(val("--prompt"));
         else if (k == "--max_gen") a.max_gen = std::atoi(val("--max_gen"));
         else if (k == "--max_length") a.max_length = std::atoi(val("--max_length"));
@@ -66,6 +72,55 @@ bool parse(int argc, char ** argv, Args & a) {
     return a.prompt > 0 && a.max_gen >= 0 && a.nodes >= 1 && a.max_length >= a.prompt + a.max_gen;
 }
 
+// Qwen3 configuration from a GGUF file's keys (models/qwen3.cpp:7-16).
+bool config_from_gguf(const gguf::File & f, alb_qwen3_config & c) {
+    const std::string & arch = f.str("general.architecture");
+    if (!arch.empty() && arch != "qwen3") throw std::runtime_error("architecture " + arch + " is not qwen3");
+    c.n_layer = (int32_t)f.num("qwen3.block_count");
+    c.n_embd = (int32_t)f.num("qwen3.embedding_length");
+    c.n_head = (int32_t)f.num("qwen3.attention.head_count");
+    c.n_head_kv = (int32_t)f.num("qwen3.attention.head_count_kv");
+    c.head_dim = (int32_t)f.num_or("qwen3.attention.key_length", c.n_embd / c.n_head);
+    c.n_ff = (int32_t)f.num("qwen3.feed_forward_length");
+    c.n_vocab = (int32_t)f.tensor("token_embd.weight").ne.at(1);
+    c.tied = f.has_tensor("output.weight") ? 0 : 1;
+    c.eps = (float)f.num_or("qwen3.attention.layer_norm_rms_epsilon", 1e-6);
+    c.freq_base = (float)f.num_or("qwen3.rope.freq_base", 1e6);
+    return true;
+}
+
+// Every tensor of the file into engine e (tensor names: models/qwen3.cpp:32-45;
+// kinds: the C ABI's).
+int upload_gguf(alb_engine * e, const gguf::File & f, const alb_qwen3_config & c) {
+    struct Item { std::string name; int layer, kind; bool norm; };
+    std::vector<Item> plan = {{"token_embd.weight", -1, 0, false}, {"output_norm.weight", -1, 2, true}};
+    if (!c.tied) plan.push_back({"output.weight", -1, 1, false});
+    const std::pair<const char *, int> per_layer[] = {
+        {"attn_norm.weight", 3}, {"attn_q.weight", 4}, {"attn_k.weight", 5}, {"attn_v.weight", 6},
+        {"attn_output.weight", 7}, {"attn_q_norm.weight", 8}, {"attn_k_norm.weight", 9}, {"ffn_norm.weight", 10},
+        {"ffn_gate.weight", 11}, {"ffn_up.weight", 12}, {"ffn_down.weight", 13}};
+    for (int l = 0; l < c.n_layer; ++l)
+        for (const auto & [suffix, kind] : per_layer)
+            plan.push_back({"blk." + std::to_string(l) + "." + suffix, l, kind, kind == 3 || kind == 8 || kind == 9 || kind == 10});
+    for (const Item & it : plan) {
+        const gguf::Tensor & t = f.tensor(it.name);
+        int rc;
+        if (it.norm) {
+            int64_t n = 1;
+            for (uint64_t x : t.ne) n *= (int64_t)x;
+            std::vector<float> w((size_t)n);
+            if (t.type == gguf::GGML_F32) std::memcpy(w.data(), f.data(t), (size_t)n * 4);
+            else throw std::runtime_error(it.name + ": norm weights must be F32");
+            rc = alb_engine_set_norm_weights(e, it.layer, it.kind, w.data(), n);
+        } else {
+            if (t.type != gguf::GGML_Q4_0 || t.ne.size() != 2) throw std::runtime_error(it.name + ": not a Q4_0 matrix");
+            rc = alb_engine_set_weight_blocks(e, it.layer, it.kind, f.data(t), (int64_t)t.ne[1], (int64_t)t.ne[0]);
+        }
+        if (rc != ALB_OK) return rc;
+    }
+    return ALB_OK;
+}
+
 struct RankResult {
     int rc = ALB_OK;
     std::string what;
@@ -73,8 +128,8 @@ struct RankResult {
     std::vector<int32_t> tokens;
 };
 
-void run_rank(const Args & a, const alb_qwen3_config & cfg, const std::vector<int32_t> & prompt, const void * nccl_id,
-              int rank, RankResult & out) {
+void run_rank(const Args & a, const alb_qwen3_config & cfg, const gguf::File * model, const std::vector<int32_t> & prompt,
+              const void * nccl_id, int rank, RankResult & out) {
     alb_engine * e = nullptr;
     auto fail = [&](int rc, const char * what) {
         out.rc = rc;
@@ -82,6 +137,17 @@ void run_rank(const Args & a, const alb_qwen3_config & cfg, const std::vector<in
     };
     int rc = alb_engine_create(&cfg, a.seed, a.max_length, a.ubatch, rank, a.nodes, nccl_id, rank, &e);
     if (rc != ALB_OK) { fail(rc, "alb_engine_create"); return; }
+    if (model) {
+        try {
+            rc = upload_gguf(e, *model, cfg);
+        } catch (const std::exception & x) {
+            out.rc = ALB_ERR_INVALID;
+            out.what = std::string("gguf: ") + x.what();
+            alb_engine_destroy(e);
+            return;
+        }
+        if (rc != ALB_OK) { fail(rc, "alb_engine_set_weight_blocks"); alb_engine_destroy(e); return; }
+    }
     int32_t tok = 0;
     const auto t0 = std::chrono::steady_clock::now();
     rc = alb_engine_prefill(e, prompt.data(), (int32_t)prompt.size(), 0, &tok);
@@ -112,8 +178,21 @@ void run_rank(const Args & a, const alb_qwen3_config & cfg, const std::vector<in
 int main(int argc, char ** argv) {
     Args a;
     alb_qwen3_config cfg;
-    if (!parse(argc, argv, a) || !config_of(a.model, cfg)) {
-        std::fprintf(stderr, "usage: al_bench [--model 0.6b|4b|8b|tiny|tiny_gqa] [--prompt N] [--max_gen M] "
+    std::unique_ptr<gguf::File> model;
+    bool ok = parse(argc, argv, a);
+    if (ok && !a.gguf_path.empty()) {
+        try {
+            model = std::make_unique<gguf::File>(a.gguf_path);
+            config_from_gguf(*model, cfg);
+        } catch (const std::exception & x) {
+            std::fprintf(stderr, "al_bench: %s: %s\n", a.gguf_path.c_str(), x.what());
+            return 1;
+        }
+    } else if (ok) {
+        ok = config_of(a.model, cfg);
+    }
+    if (!ok) {
+        std::fprintf(stderr, "usage: al_bench [--model 0.6b|4b|8b|tiny|tiny_gqa | --gguf FILE] [--prompt N] [--max_gen M] "
                              "[--max_length L] [--ubatch U] [--seed S] [--nodes N] [--loop] [--print_tokens]\n");
         return 2;
     }
@@ -134,7 +213,7 @@ int main(int argc, char ** argv) {
     std::vector<RankResult> res((size_t)a.nodes);
     std::vector<std::thread> threads;
     for (int r = 0; r < a.nodes; ++r)
-        threads.emplace_back(run_rank, std::cref(a), std::cref(cfg), std::cref(prompt),
+        threads.emplace_back(run_rank, std::cref(a), std::cref(cfg), model.get(), std::cref(prompt),
                              a.nodes > 1 ? (const void *)nccl_id : nullptr, r, std::ref(res[(size_t)r]));
     for (auto & t : threads) t.join();
     for (int r = 0; r < a.nodes; ++r) {

@@ -577,6 +577,7 @@ extern "C" int alb_engine_weight_blocks(alb_engine * e, int32_t layer, int32_t k
     int64_t N = 0, K = 0, r0 = 0, nr = 0, stride = 1;
     if (layer < 0) {
         if (kind == T_TOK_EMBD) { W = e->tok; N = e->c.n_vocab; K = e->E; nr = N; }
+        else if (kind == T_OUTPUT && !e->c.tied) { W = e->out_w; N = e->V; K = e->E; nr = N; }
         else return ALB_ERR_INVALID;
     } else {
         alb_engine::Layer & L = e->layers[layer];
@@ -622,6 +623,90 @@ extern "C" int alb_engine_norm_weights(alb_engine * e, int32_t layer, int32_t ki
     }
     ALB_CHECK_ARG(src && n == len);
     ALB_CUDA_TRY(cudaMemcpy(host, src, (size_t)n * 4, cudaMemcpyDeviceToHost));
+    return ALB_OK;
+}
+
+// External weights (a model loaded from GGUF, model.cpp:355-474).  `host` holds
+// the FULL tensor of (layer, kind) -- every rank's part -- in the reference
+// block_q4_0 layout, [rows][cols / 32] blocks of 18 bytes; this rank keeps its
+// shard the way slice_tensor (model.cpp:40-110) splits tensor-parallel weights:
+// Q, K, V, gate, up and the untied lm head by rows, O and down by columns, the
+// token table whole.  The shard is repacked on the device into the GPU layout
+// in place of the generated weights (the captured step graph reads the same
+// buffers, so nothing else changes).
+extern "C" int alb_engine_set_weight_blocks(alb_engine * e, int32_t layer, int32_t kind, const void * host,
+                                            int64_t rows, int64_t cols) {
+    ALB_CHECK_ARG(e && host && rows > 0 && cols > 0 && cols % 32 == 0 && layer >= -1 && layer < e->c.n_layer);
+    ALB_CUDA_TRY(cudaSetDevice(e->dev));
+    uint8_t * W = nullptr;
+    int64_t K = 0, r0 = 0, nr = 0, stride = 1;            // GPU buffer: columns, first row, shard rows, row step
+    int64_t full_rows = 0, full_cols = 0, src_r0 = 0, src_c0 = 0;
+    const int64_t tp = e->tp, rk = e->rank;
+    if (layer < 0) {
+        if (kind == T_TOK_EMBD) {
+            W = e->tok; K = e->E; nr = e->c.n_vocab; full_rows = nr; full_cols = K;
+        } else if (kind == T_OUTPUT && !e->c.tied) {
+            W = e->out_w; K = e->E; nr = e->V; full_rows = (int64_t)e->V * tp; full_cols = K; src_r0 = e->v0;
+        } else {
+            return ALB_ERR_INVALID;
+        }
+    } else {
+        alb_engine::Layer & L = e->layers[layer];
+        switch (kind) {
+            case T_WQ: W = L.qkv; K = e->E; r0 = 0; nr = e->Dq; break;
+            case T_WK: W = L.qkv; K = e->E; r0 = e->Dq; nr = e->Dkv; break;
+            case T_WV: W = L.qkv; K = e->E; r0 = e->Dq + e->Dkv; nr = e->Dkv; break;
+            case T_GATE: W = L.gu; K = e->E; r0 = 0; nr = e->F; stride = 2; break;
+            case T_UP: W = L.gu; K = e->E; r0 = 1; nr = e->F; stride = 2; break;
+            case T_WO: W = L.o; K = e->Dq; nr = e->E; break;
+            case T_DOWN: W = L.down; K = e->F; nr = e->E; break;
+            default: return ALB_ERR_INVALID;
+        }
+        if (kind == T_WO || kind == T_DOWN) {   // column shards
+            full_rows = nr; full_cols = K * tp; src_c0 = rk * K;
+        } else {                                  // row shards
+            full_rows = nr * tp; full_cols = K; src_r0 = rk * nr;
+        }
+    }
+    ALB_CHECK_ARG(rows == full_rows && cols == full_cols);
+    const size_t blk = 18, srb = (size_t)(full_cols / 32) * blk, drb = (size_t)(K / 32) * blk;
+    std::vector<uint8_t> shard((size_t)nr * drb);
+    for (int64_t i = 0; i < nr; ++i)
+        memcpy(shard.data() + (size_t)i * drb, static_cast<const uint8_t *>(host) + (size_t)(src_r0 + i) * srb +
+                                                    (size_t)(src_c0 / 32) * blk, drb);
+    uint8_t * raw = nullptr, * gpu = nullptr;
+    const size_t rowb = q4_row_bytes(K);
+    int rc = ALB_OK;
+    if (cudaMalloc(&raw, shard.size()) != cudaSuccess || cudaMalloc(&gpu, (size_t)nr * rowb) != cudaSuccess) rc = ALB_ERR_CUDA;
+    if (rc == ALB_OK && cudaMemcpyAsync(raw, shard.data(), shard.size(), cudaMemcpyHostToDevice, e->st) != cudaSuccess)
+        rc = ALB_ERR_CUDA;
+    if (rc == ALB_OK) rc = alb_repack_q4_0(gpu, raw, nr, K, e->st);
+    if (rc == ALB_OK && cudaMemcpy2DAsync(W + (size_t)r0 * rowb, (size_t)stride * rowb, gpu, rowb, rowb, (size_t)nr,
+                                          cudaMemcpyDeviceToDevice, e->st) != cudaSuccess)
+        rc = ALB_ERR_CUDA;
+    if (rc == ALB_OK && cudaStreamSynchronize(e->st) != cudaSuccess) rc = ALB_ERR_CUDA;
+    if (raw) cudaFree(raw);
+    if (gpu) cudaFree(gpu);
+    if (rc == ALB_ERR_CUDA) alb_set_last_error_msg(cudaGetErrorString(cudaGetLastError()));
+    return rc;
+}
+
+// fp32 norm weights of (layer, kind) (every rank holds them whole).
+extern "C" int alb_engine_set_norm_weights(alb_engine * e, int32_t layer, int32_t kind, const float * host, int64_t n) {
+    ALB_CHECK_ARG(e && host && layer >= -1 && layer < e->c.n_layer);
+    float * dst = nullptr;
+    int64_t len = 0;
+    if (layer < 0 && kind == T_OUTPUT_NORM) { dst = e->out_norm; len = e->E; }
+    else if (layer >= 0) {
+        alb_engine::Layer & L = e->layers[layer];
+        if (kind == T_ATTN_NORM) { dst = L.an; len = e->E; }
+        if (kind == T_FFN_NORM) { dst = L.fn; len = e->E; }
+        if (kind == T_Q_NORM) { dst = L.qn; len = 128; }
+        if (kind == T_K_NORM) { dst = L.kn; len = 128; }
+    }
+    ALB_CHECK_ARG(dst && n == len);
+    ALB_CUDA_TRY(cudaSetDevice(e->dev));
+    ALB_CUDA_TRY(cudaMemcpy(dst, host, (size_t)n * 4, cudaMemcpyHostToDevice));
     return ALB_OK;
 }
 

@@ -230,10 +230,21 @@ ALB_API int alb_engine_info(const alb_engine * e, int64_t * info, int32_t n);
 ALB_API void * alb_engine_stream(alb_engine * e);
 /* This rank's shard of weight (layer, kind) in block_q4_0 rows (host), kinds as
  * oracle.h (4 WQ, 5 WK, 6 WV, 7 WO, 11 GATE, 12 UP, 13 DOWN; layer -1 kind 0 =
- * token table).  host = NULL only reports the shard shape. */
+ * token table, kind 1 = untied lm head).  host = NULL only reports the shard shape. */
 ALB_API int alb_engine_weight_blocks(alb_engine * e, int32_t layer, int32_t kind, void * host, int64_t * rows,
                                      int64_t * cols);
 ALB_API int alb_engine_norm_weights(alb_engine * e, int32_t layer, int32_t kind, float * host, int64_t n);
+/* External weights (the reference's model load, model.cpp:355-474 with
+ * slice_tensor, model.cpp:40-110): host = the FULL tensor of (layer, kind) in
+ * block_q4_0 rows (all ranks' rows / columns: rows x cols values); the engine
+ * keeps its tensor-parallel shard (Q, K, V, gate, up, untied lm head by rows;
+ * O, down by columns; the token table whole) and repacks it on the device.
+ * Kinds as alb_engine_weight_blocks, plus layer -1 kind 1 = untied lm head. */
+ALB_API int alb_engine_set_weight_blocks(alb_engine * e, int32_t layer, int32_t kind, const void * host, int64_t rows,
+                                         int64_t cols);
+/* fp32 norm weights of (layer, kind): 3 attn, 10 ffn (n_embd), 8 q, 9 k (head_dim);
+ * layer -1 kind 2 = output norm. */
+ALB_API int alb_engine_set_norm_weights(alb_engine * e, int32_t layer, int32_t kind, const float * host, int64_t n);
 /* Measurement hook: mean duration and algorithmic bytes per launch of the
  * decode step's Q4_0 mat-vecs replayed alone from a CUDA graph. */
 ALB_API int alb_engine_time_gemv(alb_engine * e, int32_t reps, float * us_per_launch, double * bytes_per_launch);

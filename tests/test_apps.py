@@ -59,6 +59,16 @@ def test_al_bench_arguments():
     assert r.returncode == 2
 
 
+def test_al_bench_rejects_bad_gguf(tmp_path):
+    # the file is read before any device is touched
+    r = subprocess.run([B.AL_BENCH, "--gguf", str(tmp_path / "missing.gguf")], capture_output=True, text=True)
+    assert r.returncode == 1 and "cannot open" in r.stderr
+    bad = tmp_path / "bad.gguf"
+    bad.write_bytes(b"NOPE" + bytes(64))
+    r = subprocess.run([B.AL_BENCH, "--gguf", str(bad)], capture_output=True, text=True)
+    assert r.returncode == 1 and "not a GGUF file" in r.stderr
+
+
 def test_al_bench_reports_missing_device():
     if A.lib().alb_device_check(0) == 0:
         pytest.skip("a B200 is present (the GPU tests run the driver)")

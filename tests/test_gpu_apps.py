@@ -73,6 +73,22 @@ def test_al_bench_matches_oracle(name, cfg):
     assert toks_loop == toks
 
 
+def test_al_bench_loads_gguf(tmp_path):
+    # a GGUF file of the engine's seeded tiny_gqa weights: al_bench --gguf
+    # generates the same greedy tokens as al_bench on the generated weights
+    from arclight_b200 import gguf as G
+    from arclight_b200.engine import Engine
+    seed = 11
+    e = Engine(TINY_GQA, seed, 64, 16)
+    path = str(tmp_path / "tiny_gqa.gguf")
+    G.engine_to_gguf(e, path)
+    e.close()
+    args = ["--prompt", "24", "--max_gen", "6", "--seed", str(seed), "--ubatch", "16", "--print_tokens"]
+    p_gen, t_gen = run_bench(["--model", "tiny_gqa", *args])
+    p_file, t_file = run_bench(["--gguf", path, *args])
+    assert p_file == p_gen and t_file == t_gen
+
+
 def view(t, shape, esize):
     v = Tensor()
     for i in range(4):
