@@ -70,6 +70,19 @@ static constexpr uint32_t PG_IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint
 // byte offset of (row r, 16-byte chunk c) in a K-major core-matrix tile
 __device__ __forceinline__ int pg_off(int r, int c) { return (r >> 3) * 256 + c * 128 + (r & 7) * 16; }
 
+// 16 TMEM columns of this warp's 32 lanes <- v (two 8-column tcgen05.st: a
+// store takes a run of consecutive registers, so narrow ones keep the
+// epilogue within its register budget; the caller waits with wait::st).
+__device__ __forceinline__ void pg_tmem_fill16(uint32_t taddr, uint32_t v) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};" :: "r"(taddr), "r"(v) : "memory");
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};" :: "r"(taddr + 8u), "r"(v) : "memory");
+}
+// float(I) from the accumulator: every buffer is pre-set to bits(1.5 * 2^23)
+// before its MMA accumulates the int32 block dot onto it, so the accumulator
+// holds bits(1.5 * 2^23) + I and one fp32 subtract gives float(I) exactly
+// (|I| < 2^22).
+static constexpr uint32_t PG_BIAS = 0x4B400000u;
+
 __device__ __forceinline__ void pg_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void pg_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -134,9 +147,11 @@ __device__ __forceinline__ bool pg_aborted(PgShared & sh) { return *reinterpret_
 //               tfull[i] and empty[stage].  One issuer's serial path (waits,
 //               unpack, proxy fence, issue) is ~1.2 us per block: four of them
 //               keep the tensor core and the epilogue fed;
-//   warps 5..12 read each block's accumulator back (tcgen05.ld: warp w reads
-//               TMEM lanes 32 (w % 4) .., columns 32 ((w - 5) / 4) ..), release
-//               the buffer, advance their 32 fp32 chains, release the stage.
+//   warps 5..12 pre-set every buffer to the float-conversion bias, read each
+//               block's accumulator back (tcgen05.ld: warp w reads TMEM lanes
+//               32 (w % 4) .., columns 32 ((w - 5) / 4) ..), set the bias again,
+//               release the buffer, advance their 32 fp32 chains, release the
+//               stage.
 // No CTA-wide barrier per block: the tensor core runs up to PG_NB blocks ahead
 // of the epilogue and the loads PG_D blocks ahead of the tensor core.
 template <int OUT>   // 0: y = acc (+ residual), 1: SwiGLU of interleaved (gate, up) rows
@@ -247,14 +262,14 @@ k_prefill_gemm(const uint8_t * __restrict__ Wn, const uint8_t * __restrict__ Ws,
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic stores -> tensor core
             __syncwarp();
-            if (b >= PG_NB && !pg_wait(sh, &sh.tempty[tb], (uint32_t)((b / PG_NB - 1) & 1), err)) break;
+            if (!pg_wait(sh, &sh.tempty[tb], (uint32_t)((b / PG_NB) & 1), err)) break;   // phase 0: the first bias fill
             if (lane == 0) {
                 pg_fence_after();
                 const uint64_t da = pg_desc(sh.a[st]), db = pg_desc(sh.b[st]);
-                const uint32_t zero = 0;
+                const uint32_t accumulate = 1, zero = 0;   // D = bias + A.B
                 asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
                              "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}"
-                             :: "r"(tmem + (uint32_t)(tb * PG_N)), "l"(da), "l"(db), "r"(PG_IDESC), "r"(zero), "r"(zero)
+                             :: "r"(tmem + (uint32_t)(tb * PG_N)), "l"(da), "l"(db), "r"(PG_IDESC), "r"(accumulate), "r"(zero)
                              : "memory");
                 asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
                              :: "r"(pg_smem(&sh.tfull[tb])) : "memory");
@@ -272,6 +287,18 @@ k_prefill_gemm(const uint8_t * __restrict__ Wn, const uint8_t * __restrict__ Ws,
         __syncwarp();
     } else {
         // --------------------------------------------------- epilogue warps
+        {   // every buffer's columns of this warp <- the bias; tempty phase 0
+            const uint32_t t0 = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(chalf * 32);
+            for (int k = 0; k < PG_NB; ++k) {
+                pg_tmem_fill16(t0 + (uint32_t)(k * PG_N), PG_BIAS);
+                pg_tmem_fill16(t0 + (uint32_t)(k * PG_N + 16), PG_BIAS);
+            }
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            pg_fence_before();
+            __syncwarp();
+            if (lane == 0)
+                for (int k = 0; k < PG_NB; ++k) alb_mbar_arrive(&sh.tempty[k]);
+        }
         for (int64_t b = 0; b < nb; ++b) {
             const int st = (int)(b % PG_D), tb = (int)(b % PG_NB);
             if (pg_aborted(sh)) break;
@@ -280,10 +307,9 @@ k_prefill_gemm(const uint8_t * __restrict__ Wn, const uint8_t * __restrict__ Ws,
             const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(tb * PG_N + chalf * 32);
             const float dxr = sh.dx[st][row];
             const float * dwp = &sh.dwf[st][chalf * 32];
-            // two halves of 16 columns (16 accumulator words live at a time); the
-            // buffer is released once the second half is in registers.
-            // float(I) exactly as 2^23 * 1.5 + I - 2^23 * 1.5 (|I| < 2^22): integer add +
-            // fp32 subtract instead of a conversion; dx * dw is exact (11 x 11 bits)
+            // two halves of 16 columns (16 accumulator words live at a time).  The
+            // accumulator holds bits(1.5 * 2^23) + I: one fp32 subtract gives
+            // float(I); dx * dw is exact (11 x 11 bits)
 #pragma unroll
             for (int hf = 0; hf < 2; ++hf) {
                 uint32_t c[16];
@@ -294,11 +320,6 @@ k_prefill_gemm(const uint8_t * __restrict__ Wn, const uint8_t * __restrict__ Ws,
                                "=r"(c[14]), "=r"(c[15])
                              : "r"(taddr + (uint32_t)(16 * hf)));
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                if (hf == 1) {
-                    pg_fence_before();
-                    __syncwarp();
-                    if (lane == 0) alb_mbar_arrive(&sh.tempty[tb]);   // the accumulator is in registers
-                }
 #pragma unroll
                 for (int j4 = 0; j4 < 4; ++j4) {
                     const float4 w4 = *reinterpret_cast<const float4 *>(dwp + 16 * hf + 4 * j4);
@@ -306,13 +327,19 @@ k_prefill_gemm(const uint8_t * __restrict__ Wn, const uint8_t * __restrict__ Ws,
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
                         const int j = 16 * hf + 4 * j4 + u;
-                        const float t = __fsub_rn(__int_as_float((int)c[4 * j4 + u] + 0x4B400000), 12582912.0f);
+                        const float t = __fsub_rn(__uint_as_float(c[4 * j4 + u]), 12582912.0f);
                         acc[j] = __fmaf_rn(t, __fmul_rn(dxr, wv[u]), acc[j]);
                     }
                 }
             }
+            // the accumulator was read: set the bias again, release the buffer
+            // (after the chain steps, when the 16 words of a fill are free registers)
+            pg_tmem_fill16(taddr, PG_BIAS);
+            pg_tmem_fill16(taddr + 16u, PG_BIAS);
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            pg_fence_before();
             __syncwarp();
-            if (lane == 0) alb_mbar_arrive(&sh.empty[st]);   // the stage's scales are read
+            if (lane == 0) { alb_mbar_arrive(&sh.tempty[tb]); alb_mbar_arrive(&sh.empty[st]); }   // buffer and scales
         }
     }
     pg_fence_before();
