@@ -83,6 +83,7 @@ struct alb_engine {
     float * xn = nullptr;                           // prefill: RMS-normalized rows
     void * xq = nullptr;                            // decode: block_q8_0 input of the next mat-vec
     void * pg_ws = nullptr;                         // prefill: quantized activations of the mat-mul
+    float * fa_sws = nullptr;                       // prefill: the attention's score workspace
     int32_t * tok_dev = nullptr, * pos_dev = nullptr, * next_dev = nullptr, * step_dev = nullptr, * gen_out = nullptr;
     int32_t gen_cap = 0;
     unsigned long long * key = nullptr;
@@ -176,6 +177,7 @@ static int engine_forward(alb_engine * e, int64_t T, bool pdl, int ncap_prefill 
             launches += e->fa_cluster ? 1 : 2;   // the cluster kernel, or scores + P.V
         } else {
             ALB_CUDA_TRY(launch_qk_norm_rope_kv(qa, st));
+            fa.sws = e->fa_sws;   // sized for max_ubatch tokens over max_ctx cells (ncap <= max_ctx)
             ALB_CUDA_TRY(launch_flash_attn(fa, st));
             launches += 2;   // QK-norm/RoPE + the prefill attention
         }
@@ -333,6 +335,10 @@ static int engine_init_acts(alb_engine * e) {
         uint8_t * w = nullptr;
         ALB_TRY(e->alloc(&w, prefill_ws_bytes(U, kmax)));
         e->pg_ws = w;
+        // prefill attention scores, written by pass 1 and read by pass 2
+        uint8_t * sw = nullptr;
+        ALB_TRY(e->alloc(&sw, fa_prefill_scores_bytes(e->Hq, e->Hkv, (int)U, e->max_ctx)));
+        e->fa_sws = reinterpret_cast<float *>(sw);
     }
     if (e->tp > 1) {
         ALB_TRY(e->alloc(&e->part, U * e->E));

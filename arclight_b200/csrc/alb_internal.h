@@ -66,8 +66,11 @@ struct FlashArgs {
     float * ws = nullptr;               // flash_attn_ws_bytes()
     float * out = nullptr;              // [T][Hq][128] fp32
     void * xq = nullptr;                // optional: block_q8_0 records of out, [T][Hq*4]
+    float * sws = nullptr;              // optional, prefill: score workspace (fa_prefill_scores_bytes)
     bool pdl = false;
 };
+// Bytes of the prefill attention's score workspace for T tokens over ncap cells.
+size_t fa_prefill_scores_bytes(int Hq, int Hkv, int T, int ncap);
 size_t flash_attn_ws_bytes(int Hq, int Hkv, int T, int S, int ncap);
 size_t split_attn_ws_bytes(int Hq, int Hkv, int T, int S, int ncap);
 cudaError_t launch_split_attn(const FlashArgs & f, cudaStream_t st);

@@ -156,10 +156,15 @@ __device__ __forceinline__ void fp_scores16(const uint8_t * __restrict__ kr, con
     }
 }
 
-template <int G>
+// STORE: pass 1 also writes every scaled score of the tile (64 rows x n cells)
+// to the workspace `sws` (row stride `sstride`), and pass 2 reads them back --
+// each thread re-reads exactly the values it wrote -- instead of recomputing
+// the 128-long chains (bit-identical scores, no K stages in pass 2).
+template <int G, bool STORE>
 __global__ void __launch_bounds__(256, 1)
 k_fa_prefill(const float * __restrict__ q, const uint16_t * __restrict__ kc, const uint16_t * __restrict__ vc, int Hq,
-             int Hkv, int T, int32_t pos0, const int32_t * __restrict__ pos_dev, float scale, float * __restrict__ out) {
+             int Hkv, int T, int32_t pos0, const int32_t * __restrict__ pos_dev, float scale, float * __restrict__ out,
+             float * __restrict__ sws, int64_t sstride) {
     constexpr int TQ = FP_R / G;
     extern __shared__ __align__(16) uint8_t fp_sm[];
     float * qT = reinterpret_cast<float *>(fp_sm);                            // [128][FP_R]
@@ -185,7 +190,9 @@ k_fa_prefill(const float * __restrict__ q, const uint16_t * __restrict__ kc, con
     }
     const int64_t row = (int64_t)Hkv * 128;
     const int nst = (n + FP_CH - 1) / FP_CH;
-    auto issue = [&](int i, bool with_v) {
+    // this tile's scores in the workspace: [FP_R rows][sstride cells]
+    float * sreg = STORE ? sws + ((size_t)blockIdx.x * gridDim.y + blockIdx.y) * FP_R * (size_t)sstride : nullptr;
+    auto issue = [&](int i, bool with_k, bool with_v) {
         if (i < nst) {
             const int cb = i * FP_CH, rows = min(FP_CH, n - cb);
             uint8_t * kd = kst + (i & 1) * FP_CH * FP_KPITCH;
@@ -193,7 +200,7 @@ k_fa_prefill(const float * __restrict__ q, const uint16_t * __restrict__ kc, con
             for (int p = tid; p < rows * 16; p += 256) {
                 const int r = p >> 4, j = p & 15;
                 const size_t src = (size_t)(cb + r) * row + (size_t)h * 128 + j * 8;
-                fa_cp16(kd + r * FP_KPITCH + j * 16, kc + src);
+                if (with_k) fa_cp16(kd + r * FP_KPITCH + j * 16, kc + src);
                 if (with_v) fa_cp16(vd + r * 256 + j * 16, vc + src);
             }
         }
@@ -204,9 +211,9 @@ k_fa_prefill(const float * __restrict__ q, const uint16_t * __restrict__ kc, con
     float mx[16];
 #pragma unroll
     for (int k = 0; k < 16; ++k) mx[k] = -INFINITY;
-    issue(0, false);
+    issue(0, true, false);
     for (int i = 0; i < nst; ++i) {
-        issue(i + 1, false);
+        issue(i + 1, true, false);
         asm volatile("cp.async.wait_group 1;" ::: "memory");
         __syncthreads();   // stage i (and q^T) visible
         const int c = i * FP_CH + cl;
@@ -216,7 +223,9 @@ k_fa_prefill(const float * __restrict__ q, const uint16_t * __restrict__ kc, con
 #pragma unroll
             for (int k = 0; k < 16; ++k) {
                 const int tt = (16 * rg + k) / G;
-                if (tt < tn && c <= p0 + t0 + tt) mx[k] = fmaxf(mx[k], __fmul_rn(a[k], scale));
+                const float v = __fmul_rn(a[k], scale);
+                if (STORE) sreg[(size_t)(16 * rg + k) * sstride + c] = v;
+                if (tt < tn && c <= p0 + t0 + tt) mx[k] = fmaxf(mx[k], v);
             }
         }
         __syncthreads();   // buffer i & 1 consumed before stage i + 2 refills it
@@ -251,19 +260,27 @@ k_fa_prefill(const float * __restrict__ q, const uint16_t * __restrict__ kc, con
     for (int u = 0; u < 4; ++u)
 #pragma unroll
         for (int e = 0; e < 8; ++e) { O[u][e] = 0.0f; Osp[u][e] = 0.0; Otot[(r4 + u) * 128 + d8 + e] = 0.0; }
-    issue(0, true);
+    issue(0, !STORE, true);
     for (int i = 0; i < nst; ++i) {
-        issue(i + 1, true);
+        issue(i + 1, !STORE, true);
+        const int c = i * FP_CH + cl;
+        float a[16];   // scaled scores (STORE: read back; issued before the stage wait)
+        if (STORE && c < n) {
+#pragma unroll
+            for (int k = 0; k < 16; ++k) a[k] = sreg[(size_t)(16 * rg + k) * sstride + c];
+        }
         asm volatile("cp.async.wait_group 1;" ::: "memory");
         __syncthreads();   // stage i visible; Mrow visible; pf free
-        const int c = i * FP_CH + cl;
-        float a[16];
-        if (c < n) fp_scores16(kst + (i & 1) * FP_CH * FP_KPITCH + cl * FP_KPITCH, qT, rg, a);
+        if (!STORE && c < n) {
+            fp_scores16(kst + (i & 1) * FP_CH * FP_KPITCH + cl * FP_KPITCH, qT, rg, a);
+#pragma unroll
+            for (int k = 0; k < 16; ++k) a[k] = __fmul_rn(a[k], scale);
+        }
 #pragma unroll
         for (int k = 0; k < 16; ++k) {
             const int r = 16 * rg + k, tt = r / G;
             float v = 0.0f;
-            if (c < n && tt < tn && c <= p0 + t0 + tt) v = alb_ref_expf(__fsub_rn(__fmul_rn(a[k], scale), Mrow[r]));
+            if (c < n && tt < tn && c <= p0 + t0 + tt) v = alb_ref_expf(__fsub_rn(a[k], Mrow[r]));
             pf[r * FP_CH + cl] = v;
         }
         __syncthreads();
@@ -336,14 +353,27 @@ bool flash_attn_uses_ws(int Hq, int Hkv, int T, int S, int ncap) {
     return !(T > 1 && S == 1);
 }
 
-template <int G>
-static cudaError_t launch_fa_prefill(const FlashArgs & f, cudaStream_t st) {
-    cudaError_t e = ensure_smem(k_fa_prefill<G>, FP_SMEM);
+// Score workspace of the stored-score prefill path: FP_R rows x sstride cells
+// per CTA (KV head x token tile), sstride = ncap rounded up to 4.
+size_t fa_prefill_scores_bytes(int Hq, int Hkv, int T, int ncap) {
+    if (Hkv <= 0 || Hq % Hkv != 0 || T <= 1) return 0;
+    const int TQ = FP_R / (Hq / Hkv);
+    return (size_t)Hkv * ((T + TQ - 1) / TQ) * FP_R * (size_t)((ncap + 3) & ~3) * 4;
+}
+
+template <int G, bool STORE>
+static cudaError_t launch_fa_prefill_t(const FlashArgs & f, cudaStream_t st) {
+    cudaError_t e = ensure_smem(k_fa_prefill<G, STORE>, FP_SMEM);
     if (e != cudaSuccess) return e;
     constexpr int TQ = FP_R / G;
     const dim3 grid((unsigned)f.Hkv, (unsigned)((f.T + TQ - 1) / TQ));
-    e = alb_launch(k_fa_prefill<G>, grid, dim3(256), FP_SMEM, st, f.pdl, f.q, f.kc, f.vc, f.Hq, f.Hkv, f.T, f.pos0,
-                   f.pos_dev, f.scale, f.out);
+    return alb_launch(k_fa_prefill<G, STORE>, grid, dim3(256), FP_SMEM, st, f.pdl, f.q, f.kc, f.vc, f.Hq, f.Hkv, f.T,
+                      f.pos0, f.pos_dev, f.scale, f.out, f.sws, (int64_t)((f.ncap + 3) & ~3));
+}
+
+template <int G>
+static cudaError_t launch_fa_prefill(const FlashArgs & f, cudaStream_t st) {
+    cudaError_t e = f.sws ? launch_fa_prefill_t<G, true>(f, st) : launch_fa_prefill_t<G, false>(f, st);
     if (e != cudaSuccess || !f.xq) return e;
     return launch_quantize_q8_0(f.out, f.xq, (int64_t)f.T * f.Hq * 128, f.pdl, st);
 }
