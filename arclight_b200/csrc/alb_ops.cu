@@ -126,30 +126,34 @@ static constexpr size_t FP_SMEM = (size_t)128 * FP_R * 4 + 2 * FP_CH * FP_KPITCH
                                   (size_t)FP_R * FP_CH * 8 + (size_t)FP_R * 128 * 8;
                                   // q^T, K x2, V x2, p, O totals: 198,656 B
 
-// the 16 score chains of one cell (K row in shared memory) against rows
-// 16*rg .. 16*rg+15 of q^T [128][FP_R]
-__device__ __forceinline__ void fp_scores16(const uint8_t * __restrict__ kr, const float * __restrict__ qT, int rg,
-                                            float (&a)[16]) {
+// The 16 score chains of two cells (K rows kr0, kr1 in shared memory) against
+// rows 8*rg .. 8*rg+7 of q^T [128][FP_R]: a[8u + k] = cell u, row 8*rg + k, each
+// the sequential fp32 fma chain over d.  Every broadcast q load feeds two
+// cells' fmas (half the shared-memory loads per fma of one cell x 16 rows).
+__device__ __forceinline__ void fp_scores2x8(const uint8_t * __restrict__ kr0, const uint8_t * __restrict__ kr1,
+                                             const float * __restrict__ qT, int rg, float (&a)[16]) {
 #pragma unroll
     for (int k = 0; k < 16; ++k) a[k] = 0.0f;
 #pragma unroll 2
     for (int j = 0; j < 16; ++j) {
-        const uint4 kv = *reinterpret_cast<const uint4 *>(kr + j * 16);
-        const uint32_t wd[4] = {kv.x, kv.y, kv.z, kv.w};
+        const uint4 kv0 = *reinterpret_cast<const uint4 *>(kr0 + j * 16);
+        const uint4 kv1 = *reinterpret_cast<const uint4 *>(kr1 + j * 16);
+        const uint32_t w0[4] = {kv0.x, kv0.y, kv0.z, kv0.w}, w1[4] = {kv1.x, kv1.y, kv1.z, kv1.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-            const float2 kf = __half22float2(*reinterpret_cast<const __half2 *>(&wd[e]));
+            const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&w0[e]));
+            const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&w1[e]));
 #pragma unroll
             for (int hlf = 0; hlf < 2; ++hlf) {
-                const float kd = hlf ? kf.y : kf.x;
-                const float * qd = qT + (8 * j + 2 * e + hlf) * FP_R + 16 * rg;
+                const float k0 = hlf ? f0.y : f0.x, k1 = hlf ? f1.y : f1.x;
+                const float * qd = qT + (8 * j + 2 * e + hlf) * FP_R + 8 * rg;
+                const float4 qa = *reinterpret_cast<const float4 *>(qd);
+                const float4 qb = *reinterpret_cast<const float4 *>(qd + 4);
+                const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
 #pragma unroll
-                for (int k4 = 0; k4 < 4; ++k4) {
-                    const float4 q4 = *reinterpret_cast<const float4 *>(qd + 4 * k4);
-                    a[4 * k4 + 0] = __fmaf_rn(kd, q4.x, a[4 * k4 + 0]);
-                    a[4 * k4 + 1] = __fmaf_rn(kd, q4.y, a[4 * k4 + 1]);
-                    a[4 * k4 + 2] = __fmaf_rn(kd, q4.z, a[4 * k4 + 2]);
-                    a[4 * k4 + 3] = __fmaf_rn(kd, q4.w, a[4 * k4 + 3]);
+                for (int k = 0; k < 8; ++k) {
+                    a[k] = __fmaf_rn(k0, qv[k], a[k]);
+                    a[8 + k] = __fmaf_rn(k1, qv[k], a[8 + k]);
                 }
             }
         }
@@ -173,7 +177,6 @@ k_fa_prefill(const float * __restrict__ q, const uint16_t * __restrict__ kc, con
     float * pf = reinterpret_cast<float *>(vst + 2 * FP_CH * 256);            // [FP_R][FP_CH] p of the stage
     double * Otot = reinterpret_cast<double *>(pf + 2 * FP_R * FP_CH);         // [FP_R][128]
     __shared__ float Mrow[FP_R];
-    __shared__ float red_m[2][FP_R];
     const int h = blockIdx.x, t0 = blockIdx.y * TQ, tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5;
     alb_pdl_wait();
@@ -206,38 +209,44 @@ k_fa_prefill(const float * __restrict__ q, const uint16_t * __restrict__ kc, con
         }
         fa_commit();
     };
-    const int cl = tid & (FP_CH - 1), rg = tid >> 6;   // score phase: cell of the stage, rows 16*rg ..
+    // score phase: cells pr and pr + 32 of the stage, rows 8*rg .. 8*rg+7 (warp = row group)
+    const int pr = tid & 31, rg = tid >> 5;
     // ---- pass 1: row maxima over the causal cells
-    float mx[16];
+    float mx[8];
 #pragma unroll
-    for (int k = 0; k < 16; ++k) mx[k] = -INFINITY;
+    for (int k = 0; k < 8; ++k) mx[k] = -INFINITY;
     issue(0, true, false);
     for (int i = 0; i < nst; ++i) {
         issue(i + 1, true, false);
         asm volatile("cp.async.wait_group 1;" ::: "memory");
         __syncthreads();   // stage i (and q^T) visible
-        const int c = i * FP_CH + cl;
-        if (c < n) {
+        const int cA = i * FP_CH + pr;
+        if (cA < n) {   // (cell cA + 32 may lie past n: its chains are computed and dropped)
             float a[16];
-            fp_scores16(kst + (i & 1) * FP_CH * FP_KPITCH + cl * FP_KPITCH, qT, rg, a);
+            const uint8_t * ks = kst + (i & 1) * FP_CH * FP_KPITCH;
+            fp_scores2x8(ks + pr * FP_KPITCH, ks + (pr + 32) * FP_KPITCH, qT, rg, a);
 #pragma unroll
-            for (int k = 0; k < 16; ++k) {
-                const int tt = (16 * rg + k) / G;
-                const float v = __fmul_rn(a[k], scale);
-                if (STORE) sreg[(size_t)(16 * rg + k) * sstride + c] = v;
-                if (tt < tn && c <= p0 + t0 + tt) mx[k] = fmaxf(mx[k], v);
+            for (int u = 0; u < 2; ++u) {
+                const int c = cA + 32 * u;
+                if (c < n) {
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        const int r = 8 * rg + k, tt = r / G;
+                        const float v = __fmul_rn(a[8 * u + k], scale);
+                        if (STORE) sreg[(size_t)r * sstride + c] = v;
+                        if (tt < tn && c <= p0 + t0 + tt) mx[k] = fmaxf(mx[k], v);
+                    }
+                }
             }
         }
         __syncthreads();   // buffer i & 1 consumed before stage i + 2 refills it
     }
     fa_wait_all();
 #pragma unroll
-    for (int k = 0; k < 16; ++k) {
+    for (int k = 0; k < 8; ++k) {   // warp rg holds every cell of rows 8*rg ..
         const float m = alb_warp_max(mx[k]);
-        if (lane == 0) red_m[warp & 1][16 * rg + k] = m;
+        if (lane == 0) Mrow[8 * rg + k] = m;
     }
-    __syncthreads();
-    if (tid < FP_R) Mrow[tid] = fmaxf(red_m[0][tid], red_m[1][tid]);
     // ---- pass 2: p, L and O (chunk partials: O in registers, L by row threads)
     const int r4 = (tid >> 4) * 4, d8 = (tid & 15) * 8;   // P.V tile of this thread
     float O[4][8];                                        // chunk sums (fp32, cells in order)
@@ -263,25 +272,35 @@ k_fa_prefill(const float * __restrict__ q, const uint16_t * __restrict__ kc, con
     issue(0, !STORE, true);
     for (int i = 0; i < nst; ++i) {
         issue(i + 1, !STORE, true);
-        const int c = i * FP_CH + cl;
-        float a[16];   // scaled scores (STORE: read back; issued before the stage wait)
-        if (STORE && c < n) {
+        const int cA = i * FP_CH + pr;
+        float a[16];   // scaled scores of cells cA, cA + 32 (STORE: read back, issued before the stage wait)
 #pragma unroll
-            for (int k = 0; k < 16; ++k) a[k] = sreg[(size_t)(16 * rg + k) * sstride + c];
+        for (int k = 0; k < 16; ++k) a[k] = 0.0f;
+        if (STORE) {
+#pragma unroll
+            for (int u = 0; u < 2; ++u)
+                if (cA + 32 * u < n)
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) a[8 * u + k] = sreg[(size_t)(8 * rg + k) * sstride + cA + 32 * u];
         }
         asm volatile("cp.async.wait_group 1;" ::: "memory");
         __syncthreads();   // stage i visible; Mrow visible; pf free
-        if (!STORE && c < n) {
-            fp_scores16(kst + (i & 1) * FP_CH * FP_KPITCH + cl * FP_KPITCH, qT, rg, a);
+        if (!STORE && cA < n) {
+            const uint8_t * ks = kst + (i & 1) * FP_CH * FP_KPITCH;
+            fp_scores2x8(ks + pr * FP_KPITCH, ks + (pr + 32) * FP_KPITCH, qT, rg, a);
 #pragma unroll
             for (int k = 0; k < 16; ++k) a[k] = __fmul_rn(a[k], scale);
         }
 #pragma unroll
-        for (int k = 0; k < 16; ++k) {
-            const int r = 16 * rg + k, tt = r / G;
-            float v = 0.0f;
-            if (c < n && tt < tn && c <= p0 + t0 + tt) v = alb_ref_expf(__fsub_rn(a[k], Mrow[r]));
-            pf[r * FP_CH + cl] = v;
+        for (int u = 0; u < 2; ++u) {
+            const int c = cA + 32 * u;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const int r = 8 * rg + k, tt = r / G;
+                float v = 0.0f;
+                if (c < n && tt < tn && c <= p0 + t0 + tt) v = alb_ref_expf(__fsub_rn(a[8 * u + k], Mrow[r]));
+                pf[r * FP_CH + pr + 32 * u] = v;
+            }
         }
         __syncthreads();
         if (tid < FP_R) {   // row tid's sum of p over the stage's cells, in order (masked cells add 0)
