@@ -122,6 +122,8 @@ __device__ __forceinline__ void fa_wait_all() { asm volatile("cp.async.wait_all;
 static constexpr int FP_R = 64;                 // rows per CTA
 static constexpr int FP_CH = 64;                // cells per stage (two stages per 128-cell chunk)
 static constexpr int FP_KPITCH = 272;           // padded K row in shared memory
+static constexpr int FP_PP = FP_CH + 4;         // padded row of p (floats): the row scans and the P.V
+                                                // tile's rows r, r + 4 fall in distinct banks
 static constexpr size_t FP_SMEM = (size_t)128 * FP_R * 4 + 2 * FP_CH * FP_KPITCH + 2 * FP_CH * 256 +
                                   (size_t)FP_R * FP_CH * 8 + (size_t)FP_R * 128 * 8;
                                   // q^T, K x2, V x2, p, O totals: 198,656 B
@@ -174,7 +176,7 @@ k_fa_prefill(const float * __restrict__ q, const uint16_t * __restrict__ kc, con
     float * qT = reinterpret_cast<float *>(fp_sm);                            // [128][FP_R]
     uint8_t * kst = fp_sm + (size_t)128 * FP_R * 4;                           // 2 x [FP_CH][FP_KPITCH]
     uint8_t * vst = kst + 2 * FP_CH * FP_KPITCH;                              // 2 x [FP_CH][256]
-    float * pf = reinterpret_cast<float *>(vst + 2 * FP_CH * 256);            // [FP_R][FP_CH] p of the stage
+    float * pf = reinterpret_cast<float *>(vst + 2 * FP_CH * 256);            // [FP_R][FP_PP] p of the stage
     double * Otot = reinterpret_cast<double *>(pf + 2 * FP_R * FP_CH);         // [FP_R][128]
     __shared__ float Mrow[FP_R];
     const int h = blockIdx.x, t0 = blockIdx.y * TQ, tid = threadIdx.x;
@@ -299,16 +301,25 @@ k_fa_prefill(const float * __restrict__ q, const uint16_t * __restrict__ kc, con
                 const int r = 8 * rg + k, tt = r / G;
                 float v = 0.0f;
                 if (c < n && tt < tn && c <= p0 + t0 + tt) v = alb_ref_expf(__fsub_rn(a[8 * u + k], Mrow[r]));
-                pf[r * FP_CH + pr + 32 * u] = v;
+                pf[r * FP_PP + pr + 32 * u] = v;
             }
         }
         __syncthreads();
         if (tid < FP_R) {   // row tid's sum of p over the stage's cells, in order (masked cells add 0)
-            for (int cc = 0; cc < FP_CH; ++cc) Lc = __fadd_rn(Lc, pf[tid * FP_CH + cc]);
+            const float * prow = pf + tid * FP_PP;
+#pragma unroll 4
+            for (int cc = 0; cc < FP_CH; cc += 4) {
+                const float4 p4 = *reinterpret_cast<const float4 *>(prow + cc);
+                Lc = __fadd_rn(Lc, p4.x);
+                Lc = __fadd_rn(Lc, p4.y);
+                Lc = __fadd_rn(Lc, p4.z);
+                Lc = __fadd_rn(Lc, p4.w);
+            }
         }
         const int rows = min(FP_CH, n - i * FP_CH);
         const uint8_t * vs = vst + (i & 1) * FP_CH * 256 + d8 * 2;
-        for (int cc = 0; cc < rows; ++cc) {
+        // one cell of V (8 dims) into O's 4 rows, p from the given values
+        auto pv_cell = [&](int cc, const float (&p)[4]) {
             const uint4 vv = *reinterpret_cast<const uint4 *>(vs + cc * 256);
             const uint32_t wd[4] = {vv.x, vv.y, vv.z, vv.w};
             float vf[8];
@@ -319,11 +330,25 @@ k_fa_prefill(const float * __restrict__ q, const uint16_t * __restrict__ kc, con
                 vf[2 * e + 1] = f.y;
             }
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const float p = pf[(r4 + u) * FP_CH + cc];
+            for (int u = 0; u < 4; ++u)
 #pragma unroll
-                for (int e = 0; e < 8; ++e) O[u][e] = __fmaf_rn(p, vf[e], O[u][e]);   // fp32, cells in order
-            }
+                for (int e = 0; e < 8; ++e) O[u][e] = __fmaf_rn(p[u], vf[e], O[u][e]);   // fp32, cells in order
+        };
+        int cc = 0;
+        for (; cc + 4 <= rows; cc += 4) {   // p of 4 cells per row in one 16-byte load
+            float4 p4[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) p4[u] = *reinterpret_cast<const float4 *>(pf + (r4 + u) * FP_PP + cc);
+            { const float p[4] = {p4[0].x, p4[1].x, p4[2].x, p4[3].x}; pv_cell(cc, p); }
+            { const float p[4] = {p4[0].y, p4[1].y, p4[2].y, p4[3].y}; pv_cell(cc + 1, p); }
+            { const float p[4] = {p4[0].z, p4[1].z, p4[2].z, p4[3].z}; pv_cell(cc + 2, p); }
+            { const float p[4] = {p4[0].w, p4[1].w, p4[2].w, p4[3].w}; pv_cell(cc + 3, p); }
+        }
+        for (; cc < rows; ++cc) {   // the ragged tail of the last stage
+            float p[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) p[u] = pf[(r4 + u) * FP_PP + cc];
+            pv_cell(cc, p);
         }
         if ((i & 1) == 1 || i == nst - 1) {   // a 128-cell chunk ends: its sums join the superchunk's
             const int j = i >> 1;
