@@ -18,6 +18,7 @@ HEADER = os.path.join(ROOT, "include", "alb_cuda.h")
 
 ALB_OK = 0
 ALB_ERR_INVALID = -1
+ALB_ERR_NO_SLOT = -7
 ALB_FLASH_ATTN_STATIC_BYTES = 4 << 20   # include/alb_cuda.h
 _lib = None
 
@@ -26,11 +27,15 @@ class AlbError(RuntimeError):
     pass
 
 
-def header_symbols(path: str = HEADER) -> list[str]:
-    """Every function the C ABI header declares."""
-    src = open(path).read()
-    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
-    return sorted(set(re.findall(r"\b(alb_[a-z0-9_]+)\s*\(", src)))
+def header_symbols(path: str | None = None) -> list[str]:
+    """Every function the C ABI headers declare (include/*.h, or one header)."""
+    inc = os.path.join(ROOT, "include")
+    paths = [path] if path else sorted(os.path.join(inc, f) for f in os.listdir(inc) if f.endswith(".h"))
+    names = set()
+    for p in paths:
+        src = re.sub(r"/\*.*?\*/", "", open(p).read(), flags=re.S)
+        names.update(re.findall(r"\b(alb_[a-z0-9_]+)\s*\(", src))
+    return sorted(names)
 
 
 def lib() -> C.CDLL:
@@ -102,6 +107,18 @@ def _declare(L: C.CDLL) -> None:
         "alb_engine_set_norm_weights": (ci, [vp, i32, i32, vp, i64]),
         "alb_engine_fill_kv": (ci, [vp, i32, C.c_uint64]),
         "alb_engine_time_gemv": (ci, [vp, i32, vp, vp]),
+        "alb_kv_create": (ci, [C.c_uint32, C.c_uint32, i32, C.c_uint32, vp]),
+        "alb_kv_destroy": (ci, [vp]),
+        "alb_kv_clear": (ci, [vp]),
+        "alb_kv_find_slot": (ci, [vp, vp, vp, i32, i32, vp]),
+        "alb_kv_prepare": (ci, [vp, vp, i32, vp, vp, vp]),
+        "alb_kv_apply": (ci, [vp, vp, vp, i32, vp, vp]),
+        "alb_kv_seq_rm": (ci, [vp, i32, i32, i32]),
+        "alb_kv_seq_add": (ci, [vp, i32, i32, i32, i32]),
+        "alb_kv_seq_pos_range": (ci, [vp, i32, vp, vp]),
+        "alb_kv_mask": (ci, [vp, vp, vp, i32, i32, C.c_uint32, vp]),
+        "alb_kv_cell": (ci, [vp, C.c_uint32, C.c_uint32, vp, vp, vp]),
+        "alb_kv_info": (ci, [vp, C.c_uint32, vp, i32]),
     }
     for name, (res, args) in sigs.items():
         if hasattr(L, name):

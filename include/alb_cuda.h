@@ -44,6 +44,7 @@ enum {
     ALB_ERR_TIMEOUT = -4,     /* a bounded device/host wait expired */
     ALB_ERR_UNSUPPORTED = -5, /* no sm_100a device / feature not built */
     ALB_ERR_OOM = -6,
+    ALB_ERR_NO_SLOT = -7,     /* KV cache: too few free cells for the ubatch */
 };
 
 /* ---------------------------------------------------------------- runtime */
