@@ -40,6 +40,17 @@ extern "C" int alb_get_rows_q4_0(const void * W, int64_t n_rows, int64_t K, cons
     return ALB_OK;
 }
 
+// SET_ROWS of fp32 rows into an fp16 row array at device indices (the KV store
+// of cpy_k / cpy_v with the KV-cache manager's cell indices).
+extern "C" int alb_set_rows_f16(const float * src, int64_t n_rows, int64_t row_len, const int64_t * idx, uint16_t * dst,
+                                int64_t dst_rows, void * stream) {
+    ALB_CHECK_ARG(src && idx && dst && n_rows > 0 && row_len > 0 && row_len % 8 == 0 && dst_rows > 0);
+    ALB_CHECK_ARG(n_rows <= ((int64_t)1 << 40) / row_len && dst_rows <= ((int64_t)1 << 40) / row_len);
+    ALB_CHECK_ARG(((uintptr_t)src & 15) == 0 && ((uintptr_t)dst & 15) == 0);
+    ALB_CUDA_TRY(alb::launch_set_rows_f16(src, n_rows, row_len, idx, dst, dst_rows, (cudaStream_t)stream));
+    return ALB_OK;
+}
+
 namespace alb {
 // nnml_rope_cache_init (ops.cpp:759-771) with ext_factor 0, freq_scale 1,
 // mscale 1: theta_0 = p, theta_{i+1} = theta_i * theta_scale (fp32 products),

@@ -117,6 +117,8 @@ cudaError_t launch_quantize_q8_0(const float * x, void * xq, int64_t n, bool pdl
 cudaError_t launch_swiglu_q8(const float * g, const float * u, float * y, void * yq, int64_t n, bool pdl,
                              cudaStream_t st);
 cudaError_t launch_swiglu(const float * g, const float * u, float * y, int64_t n, bool pdl, cudaStream_t st);
+cudaError_t launch_set_rows_f16(const float * src, int64_t n_rows, int64_t row_len, const int64_t * idx, uint16_t * dst,
+                                int64_t dst_rows, cudaStream_t st);
 
 // Sets a kernel's dynamic shared-memory limit on the current device when
 // `bytes` exceeds what was set there before (thread safe, per device).
@@ -126,7 +128,8 @@ template <typename F> inline cudaError_t ensure_smem(F * func, size_t bytes) {
 }
 
 // Device-side error word (bounded waits that expire set it; see alb_device_error).
-enum : int { ALB_DEVERR_NONE = 0, ALB_DEVERR_MBAR_TIMEOUT = 1, ALB_DEVERR_FLAG_TIMEOUT = 2, ALB_DEVERR_BAD_TOKEN = 3 };
+enum : int { ALB_DEVERR_NONE = 0, ALB_DEVERR_MBAR_TIMEOUT = 1, ALB_DEVERR_FLAG_TIMEOUT = 2, ALB_DEVERR_BAD_TOKEN = 3,
+             ALB_DEVERR_BAD_INDEX = 4 };
 // Host: the current device's error word (allocated once per device, zeroed).
 int * device_error_ptr();
 

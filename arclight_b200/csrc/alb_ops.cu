@@ -14,6 +14,32 @@ namespace alb {
 // types.cpp:337-350): x[t][j] = (q - 8) * d.  One thread per 32-value block.
 // The first kernel of a forward pass also clears the greedy-argmax key that
 // the lm head of this pass accumulates into (key may be null).
+// SET_ROWS to fp16 (ops.cpp:135-181, as cpy_k / cpy_v use it with the KV cache's
+// cell indices, cgraph.cpp:1114-1180): dst[idx[r]] = fp16(src[r]) with RNE
+// (common.cpp:19-24).  One thread per 8 values (one 16-byte store); a row whose
+// index lies outside [0, dst_rows) is skipped and sets the device error word.
+__global__ void k_set_rows_f16(const float * __restrict__ src, int64_t n_rows, int64_t row_len,
+                               const int64_t * __restrict__ idx, uint16_t * __restrict__ dst, int64_t dst_rows,
+                               int * err) {
+    const int64_t per_row = row_len / 8;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n_rows * per_row) return;
+    const int64_t r = i / per_row, c = (i - r * per_row) * 8;
+    const int64_t d = idx[r];
+    if (d < 0 || d >= dst_rows) {
+        if (c == 0) atomicExch(err, ALB_DEVERR_BAD_INDEX);
+        return;
+    }
+    const float4 a = *reinterpret_cast<const float4 *>(src + r * row_len + c);
+    const float4 b = *reinterpret_cast<const float4 *>(src + r * row_len + c + 4);
+    uint4 o;
+    o.x = (uint32_t)alb_f2h(a.x) | ((uint32_t)alb_f2h(a.y) << 16);
+    o.y = (uint32_t)alb_f2h(a.z) | ((uint32_t)alb_f2h(a.w) << 16);
+    o.z = (uint32_t)alb_f2h(b.x) | ((uint32_t)alb_f2h(b.y) << 16);
+    o.w = (uint32_t)alb_f2h(b.z) | ((uint32_t)alb_f2h(b.w) << 16);
+    *reinterpret_cast<uint4 *>(dst + d * row_len + c) = o;
+}
+
 __global__ void k_embed_q4_0(const uint8_t * __restrict__ W, const int32_t * __restrict__ tokens, int T, int64_t E,
                              int64_t vocab, float * __restrict__ x, int * err, unsigned long long * key) {
     const int64_t nb = E / 32;
@@ -384,6 +410,15 @@ k_fa_prefill(const float * __restrict__ q, const uint16_t * __restrict__ kc, con
         for (int e = 0; e < 8; ++e) o[e] = Ls > 0.0 ? __double2float_rn(Otot[r * 128 + d8 + e] / Ls) : 0.0f;
     }
     alb_pdl_trigger();
+}
+
+cudaError_t launch_set_rows_f16(const float * src, int64_t n_rows, int64_t row_len, const int64_t * idx, uint16_t * dst,
+                                int64_t dst_rows, cudaStream_t st) {
+    int * err = device_error_ptr();
+    if (!err) return cudaErrorMemoryAllocation;
+    const int64_t n = n_rows * (row_len / 8);
+    k_set_rows_f16<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(src, n_rows, row_len, idx, dst, dst_rows, err);
+    return cudaGetLastError();
 }
 
 size_t flash_attn_ws_bytes(int Hq, int Hkv, int T, int S, int ncap) {

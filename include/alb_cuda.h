@@ -54,7 +54,8 @@ ALB_API const char * alb_last_error(void);
 ALB_API int          alb_device_check(int dev);
 /* Device-side error word of the current device: 0, or the code of a bounded
  * in-kernel wait that expired (1 = mbarrier, 2 = cross-CTA / cross-rank flag),
- * or 3 = a decode step produced no valid next token (token 0 was fed back).
+ * or 3 = a decode step produced no valid next token (token 0 was fed back), or
+ * 4 = alb_set_rows_f16 met a row index outside its destination (row skipped).
  * Kernels never trap; they record the error and return.  clear != 0 resets it. */
 ALB_API int          alb_device_error(int clear);
 
@@ -121,6 +122,14 @@ ALB_API int alb_swiglu_q8(const float * g, const float * u, float * y, void * yq
 /* GET_ROWS of a Q4_0 table in the alb GPU layout (ops.cpp:12-52): out [n_ids][K]. */
 ALB_API int alb_get_rows_q4_0(const void * W, int64_t n_rows, int64_t K, const int32_t * ids, int64_t n_ids,
                               float * out, void * stream);
+/* SET_ROWS into fp16 (ops.cpp:135-181; cpy_k / cpy_v, cgraph.cpp:1114-1180):
+ * dst[idx[r]][:] = fp16(src[r][:]) (round to nearest even) for r < n_rows; idx
+ * (device, int64) are row indices of dst [dst_rows][row_len], e.g. the cell
+ * indices of alb_kv_prepare.  row_len % 8 == 0, src and dst 16-byte aligned.  A
+ * row whose index is outside [0, dst_rows) is skipped and alb_device_error()
+ * reports 4. */
+ALB_API int alb_set_rows_f16(const float * src, int64_t n_rows, int64_t row_len, const int64_t * idx, uint16_t * dst,
+                             int64_t dst_rows, void * stream);
 /* RoPE cos/sin table of nnml_rope_cache_init (ops.cpp:759-771; NEOX, ext_factor 0,
  * freq_scale 1): host-computed, copied to table_dev [max_pos][head_dim/2] (cos, sin). */
 ALB_API int alb_rope_table(float * table_dev, int32_t max_pos, int32_t head_dim, float freq_base);

@@ -65,3 +65,12 @@ def test_invalid_arguments_are_rejected_without_a_gpu():
     assert L.alb_allreduce_sum_f32(None, None, None, 1, None) == -1
     assert L.alb_allgather_f32(None, None, None, 1, None) == -1
     assert L.alb_comm_destroy(None) == 0
+
+
+def test_set_rows_rejects_bad_shapes_before_any_device_call():
+    L = A.lib()
+    p = C.c_void_p(4096)   # never dereferenced: the argument checks return first
+    assert L.alb_set_rows_f16(p, 2, 1020, p, p, 8, None) == A.ALB_ERR_INVALID    # row_len % 8
+    assert L.alb_set_rows_f16(p, 0, 1024, p, p, 8, None) == A.ALB_ERR_INVALID    # no rows
+    assert L.alb_set_rows_f16(None, 2, 1024, p, p, 8, None) == A.ALB_ERR_INVALID
+    assert L.alb_set_rows_f16(C.c_void_p(4100), 2, 1024, p, p, 8, None) == A.ALB_ERR_INVALID   # unaligned src

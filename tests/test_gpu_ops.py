@@ -207,3 +207,37 @@ def test_argmax_first_max(n):
         A.check(L.alb_argmax(X.data_ptr(), n, scratch.data_ptr(), idx.data_ptr(), st()))
         torch.cuda.synchronize()
         assert int(idx.item()) == O.argmax(x)
+
+
+def test_set_rows_f16_at_kv_cache_cells():
+    """SET_ROWS of K rows into an fp16 cache at the cells the KV-cache manager
+    hands out (two sequences interleaved in one stream): every stored value is
+    the oracle's RNE fp16 of the input, bit for bit, and no other row changes.
+    An index past the cache is skipped and reported by the device error word."""
+    from arclight_b200.kvcache import KVCache
+    rng = np.random.default_rng(7)
+    kv = KVCache(256, 2, True, 32)
+    pos = np.array([0, 0, 1, 1, 2, 3, 2], np.int32)
+    seq = np.array([0, 1, 0, 1, 0, 0, 1], np.int32)
+    (cells,) = kv.prepare([(pos, seq)])
+    kv.apply(pos, seq, cells)
+    row = 1024                                    # n_head_kv * head_dim of Qwen3-4B
+    src = (rng.standard_normal((len(pos), row)) * np.float32(3)).astype(np.float32)
+    src[0, :4] = [65504.0, 65520.0, 1e-8, -2.9802322e-08]   # overflow to inf, subnormal, round to -0
+    cache = np.full((256, row), 0x7E00, np.uint16)           # NaN bits: untouched rows stay so
+    S, I, D = cu(src), cu(cells.astype(np.int64)), cu(cache.view(np.int16))
+    L.alb_device_error(1)
+    A.check(L.alb_set_rows_f16(S.data_ptr(), len(pos), row, I.data_ptr(), D.data_ptr(), 256, st()))
+    torch.cuda.synchronize()
+    got = D.cpu().numpy().view(np.uint16)
+    want = cache.copy()
+    want[cells] = O.fp32_to_fp16(src)
+    np.testing.assert_array_equal(got, want)
+    assert L.alb_device_error(0) == 0
+    bad = cu(np.array([3, 256, 5], np.int64))   # 256 is past the 256-row cache
+    A.check(L.alb_set_rows_f16(S.data_ptr(), 3, row, bad.data_ptr(), D.data_ptr(), 256, st()))
+    torch.cuda.synchronize()
+    assert L.alb_device_error(1) == 4
+    got = D.cpu().numpy().view(np.uint16)
+    want[3], want[5] = O.fp32_to_fp16(src[0]), O.fp32_to_fp16(src[2])
+    np.testing.assert_array_equal(got, want)
