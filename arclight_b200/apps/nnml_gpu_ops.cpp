@@ -57,6 +57,19 @@ extern "C" int nnml_gpu_forward_get_rows(const nnml_gpu_state * params, nnml_gpu
                              ids->ne[0], static_cast<float *>(dst->data), params->stream);
 }
 
+extern "C" int nnml_gpu_forward_set_rows(const nnml_gpu_state * params, nnml_gpu_tensor * dst) {
+    if (!params || !dst) return ALB_ERR_INVALID;
+    if (not_mine(params)) return ALB_OK;
+    const nnml_gpu_tensor * rows = dst->src[0], * idx = dst->src[1];
+    if (!rows || !idx || !idx->data || !dense_f32(rows) || !dst->data) return ALB_ERR_INVALID;
+    // dst: dense fp16 rows of the same length as src0's
+    if (dst->ne[0] != rows->ne[0] || dst->nb[0] != 2 || dst->nb[1] != (size_t)dst->ne[0] * 2) return ALB_ERR_INVALID;
+    if (idx->ne[0] != rows->ne[1] || idx->nb[0] != 8) return ALB_ERR_INVALID;
+    return alb_set_rows_f16(static_cast<const float *>(rows->data), rows->ne[1], rows->ne[0],
+                            static_cast<const int64_t *>(idx->data), static_cast<uint16_t *>(dst->data), dst->ne[1],
+                            params->stream);
+}
+
 extern "C" int nnml_gpu_forward_swiglu(const nnml_gpu_state * params, nnml_gpu_tensor * dst) {
     if (!params || !dst) return ALB_ERR_INVALID;
     if (not_mine(params)) return ALB_OK;

@@ -48,6 +48,11 @@ ALB_API int nnml_gpu_forward_rms_norm_mul(const nnml_gpu_state * params, nnml_gp
 /* GET_ROWS of a Q4_0 table (ops.cpp:12-52): dst [n_ids][K] fp32, src0 table
  * (alb GPU layout [n_rows][K]), src1 int32 ids [n_ids]. */
 ALB_API int nnml_gpu_forward_get_rows(const nnml_gpu_state * params, nnml_gpu_tensor * dst);
+/* SET_ROWS into an fp16 array (ops.cpp:135-181, the KV store of cpy_k / cpy_v,
+ * cgraph.cpp:1114-1180): dst fp16 [rows][row_len] (the cache view) gets row
+ * src1[r] := fp16(src0 row r) for the fp32 rows src0 [n][row_len] and the int64
+ * indices src1 [n] (device; e.g. alb_kv_prepare's cells). */
+ALB_API int nnml_gpu_forward_set_rows(const nnml_gpu_state * params, nnml_gpu_tensor * dst);
 /* GLU/SWIGLU, split form (ops.cpp:1038-1092): dst [n] = silu(src0) * src1. */
 ALB_API int nnml_gpu_forward_swiglu(const nnml_gpu_state * params, nnml_gpu_tensor * dst);
 /* FLASH_ATTN_EXT (arm.cpp:2196-2433), one sequence, causal: dst and src0 (q)

@@ -12,6 +12,7 @@ import arclight_b200 as A
 from arclight_b200 import build as B
 
 SHIM_OPS = ["nnml_gpu_forward_mul_mat", "nnml_gpu_forward_rms_norm_mul", "nnml_gpu_forward_get_rows",
+            "nnml_gpu_forward_set_rows",
             "nnml_gpu_forward_swiglu", "nnml_gpu_forward_flash_attn_ext", "nnml_gpu_sample_greedy"]
 
 

@@ -189,6 +189,18 @@ def test_shim_get_rows():
     assert torch.equal(out, ref)
 
 
+def test_shim_set_rows():
+    rng = np.random.default_rng(8)
+    rows = torch.from_numpy(rng.standard_normal((5, 1024)).astype(np.float32)).cuda()
+    idx = torch.tensor([9, 0, 3, 63, 7], dtype=torch.int64, device="cuda")
+    cache = torch.zeros((64, 1024), dtype=torch.int16, device="cuda")
+    assert call("nnml_gpu_forward_set_rows", view(cache, [1024, 64], 2), [view(rows, [1024, 5], 4), view(idx, [5], 8)]) == 0
+    torch.cuda.synchronize()
+    want = np.zeros((64, 1024), np.uint16)
+    want[idx.cpu().numpy()] = O.fp32_to_fp16(rows.cpu().numpy())
+    np.testing.assert_array_equal(cache.cpu().numpy().view(np.uint16), want)
+
+
 @pytest.mark.parametrize("T,pos0,splits", [(1, 700, 74), (24, 0, 1)])
 def test_shim_flash_attn(T, pos0, splits):
     Hq, Hkv = 32, 8
