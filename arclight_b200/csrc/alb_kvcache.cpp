@@ -272,17 +272,22 @@ void seq_rm(alb_kv_cache * kv, int32_t sid, int32_t p0, int32_t p1) {
 
 // llm_kv_cache::apply_ubatch (cgraph.cpp:1420-1468)
 int apply_ubatch(alb_kv_cache * kv, const Slot & sl, const Ubatch & u) {
+    const size_t sz = sl.size();
+    // the reference asserts this; here it is checked before any cell changes
+    for (size_t s = 0; s < sl.strm.size(); ++s)
+        for (uint32_t idx : sl.idxs[s]) {
+            const Cells & c = kv->cells[sl.strm[s]];
+            if (!c.empty(idx) && __builtin_popcountll(c.seqs[idx]) != 1)
+                return fail(ALB_ERR_INVALID, "kv: overwritten cell is not held by exactly one sequence");
+        }
     int32_t max_rm[MAX_SEQ];   // highest position overwritten per sequence
     for (auto & m : max_rm) m = -1;
-    const size_t sz = sl.size();
     for (size_t s = 0; s < sl.strm.size(); ++s) {
         Cells & c = kv->cells[sl.strm[s]];
         for (size_t k = 0; k < sz; ++k) {
             const size_t i = s * sz + k;
             const uint32_t idx = sl.idxs[s][k];
             if (!c.empty(idx)) {
-                if (__builtin_popcountll(c.seqs[idx]) != 1)
-                    return fail(ALB_ERR_INVALID, "kv: overwritten cell is not held by exactly one sequence");
                 const int prev = __builtin_ctzll(c.seqs[idx]);
                 if (c.pos[idx] > max_rm[prev]) max_rm[prev] = c.pos[idx];
                 c.rm(idx);

@@ -174,6 +174,8 @@ def record(cfg, seed: int, n_ops: int, backend) -> list[dict]:
     n_seq_max = cfg[1]
     ops = []
     full = False
+    used = set()   # flat cells some apply has written
+    kv_size = cfg[0]
     for _ in range(n_ops):
         nxt = [max(backend.pos_range(s)[1] + 1, 0) for s in range(n_seq_max)]
         r = rng.random()
@@ -200,10 +202,26 @@ def record(cfg, seed: int, n_ops: int, backend) -> list[dict]:
             if out is None:
                 continue
             for (p, s, ns), idxs in zip(ubs, out):
+                used.update(idxs)
                 n_kv = backend.apply(p, s, idxs)
                 dig = mask_digest(backend.mask(p, s, ns, n_kv))
                 ops.append({"op": "apply", "pos": p, "seq": s, "idxs": idxs, "n_kv": n_kv,
                             "n_stream_ub": ns, "mask": list(dig)})
+        elif r < 0.56 and used:
+            # a ubatch of one sequence written over cells used before (apply
+            # without prepare): the overwritten sequences lose those positions
+            # and every earlier one (apply_ubatch's purge)
+            s = int(rng.integers(0, n_seq_max))
+            pool = sorted(c for c in used if cfg[2] or c // kv_size == s)
+            n = min(len(pool), int(rng.integers(1, 5)))
+            if n == 0:
+                continue
+            idxs = sorted(int(c) for c in rng.choice(pool, size=n, replace=False))
+            p = list(range(nxt[s], nxt[s] + n))
+            n_kv = backend.apply(p, [s] * n, idxs)
+            dig = mask_digest(backend.mask(p, [s] * n, 1, n_kv))
+            ops.append({"op": "apply", "pos": p, "seq": [s] * n, "idxs": idxs, "n_kv": n_kv,
+                        "n_stream_ub": 1, "mask": list(dig)})
         elif r < 0.65:
             s = int(rng.integers(-1, n_seq_max)) if rng.random() < 0.2 else int(rng.integers(0, n_seq_max))
             hi = max(nxt) + 2

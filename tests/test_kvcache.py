@@ -146,3 +146,16 @@ def test_invalid_arguments_are_errors():
         kv.apply([0, 1], [0, 0], [3, 3])               # a cell given twice
     with pytest.raises(A.AlbError):
         kv.seq_rm(7, 0, -1)
+
+
+def test_overwrite_purges_the_sequence_up_to_the_lost_position():
+    """apply_ubatch (cgraph.cpp:1420-1468): writing over cell 3 (position 3 of
+    sequence 0) drops position 3 and every earlier position of sequence 0."""
+    kv = KVCache(64, 1, True, 32)
+    p = np.arange(10, dtype=np.int32)
+    (idx,) = kv.prepare([(p, np.zeros(10, np.int32))])
+    kv.apply(p, np.zeros(10, np.int32), idx)
+    kv.apply([10], [0], [3])
+    assert (kv.seq_pos_min(0), kv.seq_pos_max(0)) == (4, 10)
+    assert [kv.cell(0, i)[0] for i in range(11)] == [-1, -1, -1, 10, 4, 5, 6, 7, 8, 9, -1]
+    assert kv.info()["used"] == 7 and kv.info()["head"] == 4
