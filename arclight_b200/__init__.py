@@ -81,6 +81,8 @@ def _declare(L: C.CDLL) -> None:
         "alb_allgather_f32": (ci, [vp, vp, vp, i64, vp]),
         "alb_get_rows_q4_0": (ci, [vp, i64, i64, vp, i64, vp, vp]),
         "alb_set_rows_f16": (ci, [vp, i64, i64, vp, vp, i64, vp]),
+        "alb_get_rows_f16": (ci, [vp, i64, i64, vp, i64, vp, vp]),
+        "alb_kv_visible_cells": (ci, [vp, i32, i32, C.c_uint32, vp, vp]),
         "alb_rope_table": (ci, [vp, i32, i32, f32]),
         "alb_qk_norm_rope_kv": (ci, [vp, i64, i32, i32, vp, vp, f32, vp, i32, vp, vp, vp, vp]),
         "alb_flash_attn_workspace_bytes": (sz, [i32, i32, i64, i32, i32]),

@@ -51,6 +51,17 @@ extern "C" int alb_set_rows_f16(const float * src, int64_t n_rows, int64_t row_l
     return ALB_OK;
 }
 
+// GET_ROWS of fp16 rows at device indices (e.g. the KV cells one sequence sees,
+// gathered for attention).
+extern "C" int alb_get_rows_f16(const uint16_t * src, int64_t src_rows, int64_t row_len, const int64_t * idx,
+                                int64_t n_rows, uint16_t * dst, void * stream) {
+    ALB_CHECK_ARG(src && idx && dst && n_rows > 0 && src_rows > 0 && row_len > 0 && row_len % 8 == 0);
+    ALB_CHECK_ARG(n_rows <= ((int64_t)1 << 40) / row_len && src_rows <= ((int64_t)1 << 40) / row_len);
+    ALB_CHECK_ARG(((uintptr_t)src & 15) == 0 && ((uintptr_t)dst & 15) == 0);
+    ALB_CUDA_TRY(alb::launch_get_rows_f16(src, src_rows, row_len, idx, n_rows, dst, (cudaStream_t)stream));
+    return ALB_OK;
+}
+
 namespace alb {
 // nnml_rope_cache_init (ops.cpp:759-771) with ext_factor 0, freq_scale 1,
 // mscale 1: theta_0 = p, theta_{i+1} = theta_i * theta_scale (fp32 products),

@@ -119,6 +119,8 @@ cudaError_t launch_swiglu_q8(const float * g, const float * u, float * y, void *
 cudaError_t launch_swiglu(const float * g, const float * u, float * y, int64_t n, bool pdl, cudaStream_t st);
 cudaError_t launch_set_rows_f16(const float * src, int64_t n_rows, int64_t row_len, const int64_t * idx, uint16_t * dst,
                                 int64_t dst_rows, cudaStream_t st);
+cudaError_t launch_get_rows_f16(const uint16_t * src, int64_t src_rows, int64_t row_len, const int64_t * idx,
+                                int64_t n_rows, uint16_t * dst, cudaStream_t st);
 
 // Sets a kernel's dynamic shared-memory limit on the current device when
 // `bytes` exceeds what was set there before (thread safe, per device).

@@ -513,6 +513,20 @@ int alb_kv_mask(const alb_kv_cache * kv, const int32_t * pos, const int32_t * se
     return ALB_OK;
 }
 
+int alb_kv_visible_cells(const alb_kv_cache * kv, int32_t seq_id, int32_t pos, uint32_t n_kv, int64_t * cells_out,
+                         int32_t * n_out) {
+    if (!kv || !cells_out || !n_out || seq_id < 0 || seq_id >= (int32_t)kv->seq_to_stream.size() || n_kv == 0 ||
+        n_kv > kv->size)
+        return fail(ALB_ERR_INVALID, "kv: bad visible-cells arguments");
+    const uint32_t st = kv->seq_to_stream[seq_id];
+    const Cells & c = kv->cells[st];
+    int32_t n = 0;
+    for (uint32_t j = 0; j < n_kv; ++j)
+        if (!c.empty(j) && c.has(j, seq_id) && c.pos[j] <= pos) cells_out[n++] = (int64_t)st * kv->size + j;
+    *n_out = n;
+    return ALB_OK;
+}
+
 int alb_kv_cell(const alb_kv_cache * kv, uint32_t stream, uint32_t cell, int32_t * pos, uint64_t * seqs,
                 int32_t * shift) {
     if (!kv || stream >= kv->n_stream || cell >= kv->size) return fail(ALB_ERR_INVALID, "kv: bad cell");

@@ -40,6 +40,26 @@ __global__ void k_set_rows_f16(const float * __restrict__ src, int64_t n_rows, i
     *reinterpret_cast<uint4 *>(dst + d * row_len + c) = o;
 }
 
+// GET_ROWS of fp16 rows (ops.cpp:12-131 for an F16 table): dst[r] = src[idx[r]],
+// one thread per 8 values; a row whose index lies outside [0, src_rows) is
+// written as zeros and sets the device error word.
+__global__ void k_get_rows_f16(const uint16_t * __restrict__ src, int64_t src_rows, int64_t row_len,
+                               const int64_t * __restrict__ idx, int64_t n_rows, uint16_t * __restrict__ dst,
+                               int * err) {
+    const int64_t per_row = row_len / 8;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n_rows * per_row) return;
+    const int64_t r = i / per_row, c = (i - r * per_row) * 8;
+    const int64_t s = idx[r];
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (s >= 0 && s < src_rows) {
+        v = *reinterpret_cast<const uint4 *>(src + s * row_len + c);
+    } else if (c == 0) {
+        atomicExch(err, ALB_DEVERR_BAD_INDEX);
+    }
+    *reinterpret_cast<uint4 *>(dst + r * row_len + c) = v;
+}
+
 __global__ void k_embed_q4_0(const uint8_t * __restrict__ W, const int32_t * __restrict__ tokens, int T, int64_t E,
                              int64_t vocab, float * __restrict__ x, int * err, unsigned long long * key) {
     const int64_t nb = E / 32;
@@ -418,6 +438,15 @@ cudaError_t launch_set_rows_f16(const float * src, int64_t n_rows, int64_t row_l
     if (!err) return cudaErrorMemoryAllocation;
     const int64_t n = n_rows * (row_len / 8);
     k_set_rows_f16<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(src, n_rows, row_len, idx, dst, dst_rows, err);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_get_rows_f16(const uint16_t * src, int64_t src_rows, int64_t row_len, const int64_t * idx,
+                                int64_t n_rows, uint16_t * dst, cudaStream_t st) {
+    int * err = device_error_ptr();
+    if (!err) return cudaErrorMemoryAllocation;
+    const int64_t n = n_rows * (row_len / 8);
+    k_get_rows_f16<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(src, src_rows, row_len, idx, n_rows, dst, err);
     return cudaGetLastError();
 }
 

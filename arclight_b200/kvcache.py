@@ -117,6 +117,16 @@ class KVCache:
                                   out.ctypes.data), "alb_kv_mask")
         return out
 
+    def visible_cells(self, seq_id: int, pos: int, n_kv: int | None = None) -> np.ndarray:
+        """Flat indices of the cells (seq_id, pos) may see among the first n_kv,
+        ascending: one mask row as a list (the rows to gather for attention)."""
+        n_kv = self.n_kv if n_kv is None else n_kv
+        out = np.zeros(max(n_kv, 1), dtype=np.int64)
+        n = C.c_int32()
+        check(self._L.alb_kv_visible_cells(self._h, seq_id, pos, n_kv, out.ctypes.data, C.byref(n)),
+              "alb_kv_visible_cells")
+        return out[:n.value].copy()
+
     def cell(self, stream: int, idx: int) -> tuple[int, int, int]:
         """(position or -1, sequence bit set, accumulated shift) of one cell."""
         p, q, sh = C.c_int32(), C.c_uint64(), C.c_int32()

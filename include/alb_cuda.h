@@ -55,7 +55,7 @@ ALB_API int          alb_device_check(int dev);
 /* Device-side error word of the current device: 0, or the code of a bounded
  * in-kernel wait that expired (1 = mbarrier, 2 = cross-CTA / cross-rank flag),
  * or 3 = a decode step produced no valid next token (token 0 was fed back), or
- * 4 = alb_set_rows_f16 met a row index outside its destination (row skipped).
+ * 4 = alb_set_rows_f16 / alb_get_rows_f16 met a row index out of range.
  * Kernels never trap; they record the error and return.  clear != 0 resets it. */
 ALB_API int          alb_device_error(int clear);
 
@@ -130,6 +130,14 @@ ALB_API int alb_get_rows_q4_0(const void * W, int64_t n_rows, int64_t K, const i
  * reports 4. */
 ALB_API int alb_set_rows_f16(const float * src, int64_t n_rows, int64_t row_len, const int64_t * idx, uint16_t * dst,
                              int64_t dst_rows, void * stream);
+/* GET_ROWS of fp16 rows (ops.cpp:12-131 for an F16 source): dst[r][:] =
+ * src[idx[r]][:] for r < n_rows, idx (device, int64) row indices of src
+ * [src_rows][row_len].  With alb_kv_visible_cells it gathers the K/V cells one
+ * sequence sees, in cell order, for alb_flash_attn (several sequences in one
+ * cache).  row_len % 8 == 0, src and dst 16-byte aligned; an index outside
+ * [0, src_rows) gives a zero row and alb_device_error() reports 4. */
+ALB_API int alb_get_rows_f16(const uint16_t * src, int64_t src_rows, int64_t row_len, const int64_t * idx,
+                             int64_t n_rows, uint16_t * dst, void * stream);
 /* RoPE cos/sin table of nnml_rope_cache_init (ops.cpp:759-771; NEOX, ext_factor 0,
  * freq_scale 1): host-computed, copied to table_dev [max_pos][head_dim/2] (cos, sin). */
 ALB_API int alb_rope_table(float * table_dev, int32_t max_pos, int32_t head_dim, float freq_base);

@@ -77,6 +77,12 @@ ALB_API int alb_kv_seq_pos_range(const alb_kv_cache * kv, int32_t seq_id, int32_
  * elsewhere and on the padding rows. */
 ALB_API int alb_kv_mask(const alb_kv_cache * kv, const int32_t * pos, const int32_t * seq_id, int32_t n_tokens,
                         int32_t n_stream_ub, uint32_t n_kv, float * mask);
+/* One row of that mask as a list: the flat indices (stream * kv_size + cell,
+ * ascending) of the cells j < n_kv that query (seq_id, pos) may see, into
+ * cells_out (room for n_kv); *n_out = their count.  Gathering those K/V rows
+ * (alb_get_rows_f16) gives the contiguous cache alb_flash_attn takes. */
+ALB_API int alb_kv_visible_cells(const alb_kv_cache * kv, int32_t seq_id, int32_t pos, uint32_t n_kv,
+                                 int64_t * cells_out, int32_t * n_out);
 /* Inspection: cell `cell` of stream `stream`: its position (-1 empty), the
  * bit set of its sequences and its accumulated shift. */
 ALB_API int alb_kv_cell(const alb_kv_cache * kv, uint32_t stream, uint32_t cell, int32_t * pos, uint64_t * seqs,

@@ -241,3 +241,43 @@ def test_set_rows_f16_at_kv_cache_cells():
     got = D.cpu().numpy().view(np.uint16)
     want[3], want[5] = O.fp32_to_fp16(src[0]), O.fp32_to_fp16(src[2])
     np.testing.assert_array_equal(got, want)
+
+
+@pytest.mark.parametrize("seq_id,pos,splits", [(0, 59, 4), (1, 30, 1)])
+def test_attention_of_one_sequence_in_a_shared_cache(seq_id, pos, splits):
+    """Two sequences interleaved in one fp16 cache (cells alternate): the cells
+    one query sees (alb_kv_visible_cells, its mask row) gathered in cell order
+    by alb_get_rows_f16 are that sequence's K/V bit for bit, and alb_flash_attn
+    over them equals the oracle's attention over that sequence alone."""
+    from arclight_b200.kvcache import KVCache
+    Hq, Hkv, cells = 32, 8, 256
+    kv = KVCache(cells, 2, True, 32)
+    seq = (np.arange(120) % 2).astype(np.int32)
+    tpos = (np.arange(120) // 2).astype(np.int32)
+    (slot,) = kv.prepare([(tpos, seq)])
+    n_kv = kv.apply(tpos, seq, slot)
+    vis = kv.visible_cells(seq_id, pos, n_kv)
+    assert vis.tolist() == list(range(seq_id, 2 * pos + seq_id + 1, 2))
+    rng = np.random.default_rng(seq_id + pos)
+    k = O.fp32_to_fp16(rng.standard_normal((cells, Hkv, 128)).astype(np.float32))
+    v = O.fp32_to_fp16(rng.standard_normal((cells, Hkv, 128)).astype(np.float32))
+    q = (rng.standard_normal((1, Hq, 128)) * 0.5).astype(np.float32)
+    n = len(vis)
+    Kd, Vd, Qd, I = cu(k.view(np.int16)), cu(v.view(np.int16)), cu(q), cu(vis)
+    Kg = torch.empty((n, Hkv, 128), dtype=torch.int16, device="cuda")
+    Vg = torch.empty_like(Kg)
+    L.alb_device_error(1)
+    A.check(L.alb_get_rows_f16(Kd.data_ptr(), cells, Hkv * 128, I.data_ptr(), n, Kg.data_ptr(), st()))
+    A.check(L.alb_get_rows_f16(Vd.data_ptr(), cells, Hkv * 128, I.data_ptr(), n, Vg.data_ptr(), st()))
+    scale = 1.0 / math.sqrt(128.0)
+    ws = torch.zeros(max(1, L.alb_flash_attn_workspace_bytes(Hq, Hkv, 1, splits, n)), dtype=torch.uint8, device="cuda")
+    out = torch.empty((1, Hq, 128), dtype=torch.float32, device="cuda")
+    A.check(L.alb_flash_attn(Qd.data_ptr(), Kg.data_ptr(), Vg.data_ptr(), 1, Hq, Hkv, n - 1, scale, splits,
+                             ws.data_ptr(), out.data_ptr(), st()))
+    torch.cuda.synchronize()
+    assert L.alb_device_error(0) == 0
+    np.testing.assert_array_equal(Kg.cpu().numpy().view(np.uint16), k[vis])
+    np.testing.assert_array_equal(Vg.cpu().numpy().view(np.uint16), v[vis])
+    kv_len = np.array([n], np.int32)
+    np.testing.assert_array_equal(out.cpu().numpy(), O.flash_attn(q, k[vis], v[vis], kv_len, scale, mode=0))
+    assert max_rel_err(out.cpu().numpy(), O.flash_attn(q, k[vis], v[vis], kv_len, scale, mode=2)) < 1e-5

@@ -159,3 +159,16 @@ def test_overwrite_purges_the_sequence_up_to_the_lost_position():
     assert (kv.seq_pos_min(0), kv.seq_pos_max(0)) == (4, 10)
     assert [kv.cell(0, i)[0] for i in range(11)] == [-1, -1, -1, 10, 4, 5, 6, 7, 8, 9, -1]
     assert kv.info()["used"] == 7 and kv.info()["head"] == 4
+
+
+@pytest.mark.parametrize("cfg", CONFIGS)
+def test_visible_cells_are_the_mask_rows(cfg):
+    b = ProductBackend(cfg)
+    record(cfg, 5, 80, b)
+    kv = b.kv
+    for s in range(cfg[1]):
+        st = 0 if cfg[2] else s
+        for p in (0, 7, 40, 500):
+            row = kv.set_inputs_attn_mask([p], [s], 1, kv.kv_size)[0, 0]
+            want = st * kv.kv_size + np.nonzero(row == 0)[0]
+            assert np.array_equal(kv.visible_cells(s, p, kv.kv_size), want)
