@@ -23,6 +23,7 @@
 #include "alb_common.cuh"
 #include "alb_internal.h"
 #include "alb_nccl.h"
+#include "alb_wait.h"
 
 namespace alb {
 void normal_table_host(std::vector<float> & t);
@@ -69,6 +70,8 @@ struct alb_engine {
     int dev = 0;
     cudaStream_t st = nullptr;
     void * comm = nullptr;
+    bool comm_failed = false;        // the communicator was aborted: no further steps
+    double comm_timeout_ms = 0.0;    // bounded wait for steps with collectives
     struct Layer {
         uint8_t * qkv = nullptr, * o = nullptr, * gu = nullptr, * down = nullptr;
         float * an = nullptr, * fn = nullptr, * qn = nullptr, * kn = nullptr;
@@ -454,6 +457,8 @@ extern "C" int alb_engine_create(const alb_qwen3_config * cfg, uint64_t seed, in
     int rc = ALB_OK;
     if (cudaStreamCreateWithFlags(&e->st, cudaStreamNonBlocking) != cudaSuccess) rc = ALB_ERR_CUDA;
     if (rc == ALB_OK && tp_size > 1) rc = nccl_init(&e->comm, tp_rank, tp_size, nccl_id);
+    if (const char * v = getenv("ALB_NCCL_TIMEOUT_MS")) e->comm_timeout_ms = atof(v);
+    if (e->comm_timeout_ms <= 0.0) e->comm_timeout_ms = 120000.0;
     if (rc == ALB_OK) rc = engine_init_weights(e);
     if (rc == ALB_OK) rc = engine_init_acts(e);
     if (rc != ALB_OK) { engine_free(e); return rc; }
@@ -479,11 +484,56 @@ extern "C" int alb_engine_reset(alb_engine * e) {
     return ALB_OK;
 }
 
+// Wait for the engine's stream.  A tensor-parallel engine waits boundedly: a
+// peer that stops answering within ALB_NCCL_TIMEOUT_MS (default 120 s), or an
+// asynchronous NCCL error, aborts the communicator so the collective kernels
+// spinning on that peer return; the engine then refuses further steps.
+static int engine_sync(alb_engine * e) {
+    if (!e->comm) {
+        ALB_CUDA_TRY(cudaStreamSynchronize(e->st));
+        return ALB_OK;
+    }
+    cudaError_t serr = cudaSuccess;
+    auto query = [&]() {
+        const cudaError_t q = cudaStreamQuery(e->st);
+        if (q == cudaSuccess) return 0;
+        if (q == cudaErrorNotReady) return 1;
+        serr = q;
+        return -1;
+    };
+    const WaitResult w = bounded_wait(query, [&]() { return nccl_async_error(e->comm) != ALB_OK ? 1 : 0; },
+                                      e->comm_timeout_ms);
+    (void)cudaGetLastError();   // the polls' not-ready answers
+    if (w == WaitResult::kDone) return ALB_OK;
+    if (w == WaitResult::kStreamError) {
+        alb_set_last_cuda_error(serr, "engine stream");
+        return ALB_ERR_CUDA;
+    }
+    nccl_destroy(e->comm, true);   // ncclCommAbort: the collectives in flight return
+    e->comm = nullptr;
+    e->comm_failed = true;
+    bounded_wait(query, []() { return 0; }, e->comm_timeout_ms);
+    (void)cudaGetLastError();
+    alb_set_last_error_msg(w == WaitResult::kTimeout
+                               ? "tensor-parallel peer did not answer within ALB_NCCL_TIMEOUT_MS: communicator aborted"
+                               : "NCCL reported an error: communicator aborted");
+    return w == WaitResult::kTimeout ? ALB_ERR_TIMEOUT : ALB_ERR_NCCL;
+}
+
+static int engine_usable(const alb_engine * e) {
+    if (e->comm_failed) {
+        alb_set_last_error_msg("the engine's communicator was aborted; destroy the engine");
+        return ALB_ERR_NCCL;
+    }
+    return ALB_OK;
+}
+
 // decoding_context::decode / process_ubatch (context.cpp:74-205) for a prompt
 // chunk: tokens at positions [pos0, pos0 + n), split into ubatches of max_ubatch.
 extern "C" int alb_engine_prefill(alb_engine * e, const int32_t * tokens, int32_t n, int32_t pos0,
                                   int32_t * next_token) {
     ALB_CHECK_ARG(e && tokens && n > 0 && pos0 >= 0 && (int64_t)pos0 + n <= e->max_ctx);
+    ALB_TRY(engine_usable(e));
     for (int32_t i = 0; i < n; ++i) ALB_CHECK_ARG(tokens[i] >= 0 && tokens[i] < e->c.n_vocab);
     ALB_CUDA_TRY(cudaSetDevice(e->dev));
     for (int32_t off = 0; off < n; off += e->max_ub) {
@@ -491,12 +541,11 @@ extern "C" int alb_engine_prefill(alb_engine * e, const int32_t * tokens, int32_
         const int32_t p = pos0 + off;
         ALB_CUDA_TRY(cudaMemcpyAsync(e->tok_dev, tokens + off, (size_t)T * 4, cudaMemcpyHostToDevice, e->st));
         ALB_CUDA_TRY(cudaMemcpyAsync(e->pos_dev, &p, 4, cudaMemcpyHostToDevice, e->st));
-        ALB_CUDA_TRY(cudaStreamSynchronize(e->st));   // pageable sources: keep them alive
+        ALB_TRY(engine_sync(e));   // pageable sources: keep them alive
         ALB_TRY(engine_forward(e, T, false, p + T));
     }
     ALB_CUDA_TRY(cudaMemcpyAsync(e->pinned, e->next_dev, 4, cudaMemcpyDeviceToHost, e->st));
-    ALB_CUDA_TRY(cudaStreamSynchronize(e->st));
-    ALB_TRY(nccl_async_error(e->comm));
+    ALB_TRY(engine_sync(e));
     if (next_token) *next_token = e->pinned[0];
     return ALB_OK;
 }
@@ -505,6 +554,7 @@ extern "C" int alb_engine_prefill(alb_engine * e, const int32_t * tokens, int32_
 // buffers in and out: 8 bytes H2D (token, pos), 4 bytes D2H (next token).
 extern "C" int alb_engine_decode(alb_engine * e, int32_t token, int32_t pos, int32_t * next_token) {
     ALB_CHECK_ARG(e && token >= 0 && token < e->c.n_vocab && pos >= 0 && pos < e->max_ctx);
+    ALB_TRY(engine_usable(e));
     ALB_CUDA_TRY(cudaSetDevice(e->dev));
     ALB_TRY(engine_build_graph(e));
     e->pinned[0] = token;
@@ -513,8 +563,7 @@ extern "C" int alb_engine_decode(alb_engine * e, int32_t token, int32_t pos, int
     ALB_CUDA_TRY(cudaMemcpyAsync(e->pos_dev, &e->pinned[1], 4, cudaMemcpyHostToDevice, e->st));
     ALB_CUDA_TRY(cudaGraphLaunch(e->gexec, e->st));
     ALB_CUDA_TRY(cudaMemcpyAsync(&e->pinned[2], e->next_dev, 4, cudaMemcpyDeviceToHost, e->st));
-    ALB_CUDA_TRY(cudaStreamSynchronize(e->st));
-    ALB_TRY(nccl_async_error(e->comm));
+    ALB_TRY(engine_sync(e));
     if (next_token) *next_token = e->pinned[2];
     return ALB_OK;
 }
@@ -527,6 +576,7 @@ extern "C" int alb_engine_decode_loop(alb_engine * e, int32_t token, int32_t pos
                                       int32_t * tokens_out, int32_t sync) {
     ALB_CHECK_ARG(e && token >= 0 && token < e->c.n_vocab && pos >= 0 && n_steps > 0 && n_steps <= e->gen_cap);
     ALB_CHECK_ARG((int64_t)pos + n_steps <= e->max_ctx);
+    ALB_TRY(engine_usable(e));
     ALB_CUDA_TRY(cudaSetDevice(e->dev));
     ALB_TRY(engine_build_graph(e));
     e->pinned[0] = token;
@@ -539,10 +589,7 @@ extern "C" int alb_engine_decode_loop(alb_engine * e, int32_t token, int32_t pos
     if (tokens_out) {
         ALB_CUDA_TRY(cudaMemcpyAsync(tokens_out, e->gen_out, (size_t)n_steps * 4, cudaMemcpyDeviceToHost, e->st));
     }
-    if (sync || tokens_out) {
-        ALB_CUDA_TRY(cudaStreamSynchronize(e->st));
-        ALB_TRY(nccl_async_error(e->comm));
-    }
+    if (sync || tokens_out) ALB_TRY(engine_sync(e));
     return ALB_OK;
 }
 
