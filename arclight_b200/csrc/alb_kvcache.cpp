@@ -11,6 +11,7 @@
 // after a truncation by seq_rm(seq, p, -1) that is then refilled from p, cell c
 // holds position c: the engine's device cache is addressed by position for that
 // reason, and the KV-cache tests check this property.
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <limits>
@@ -433,7 +434,6 @@ int alb_kv_apply(alb_kv_cache * kv, const int32_t * pos, const int32_t * seq_id,
     Slot sl;
     sl.strm.assign(n_seqs, 0);
     sl.idxs.assign(n_seqs, {});
-    std::vector<uint8_t> seen((size_t)kv->n_stream * kv->size, 0);
     for (uint32_t s = 0; s < n_seqs; ++s) {
         for (uint32_t k = 0; k < sz; ++k) {
             const int64_t f = idxs[s * sz + k];
@@ -441,10 +441,13 @@ int alb_kv_apply(alb_kv_cache * kv, const int32_t * pos, const int32_t * seq_id,
             const uint32_t st = (uint32_t)(f / kv->size);
             if (k == 0) sl.strm[s] = st;
             if (st != sl.strm[s]) return fail(ALB_ERR_INVALID, "kv: one sequence's cells span streams");
-            if (seen[f]++) return fail(ALB_ERR_INVALID, "kv: a cell given twice");
             sl.idxs[s].push_back((uint32_t)(f % kv->size));
         }
     }
+    std::vector<int64_t> sorted(idxs, idxs + n_tokens);   // no cell twice
+    std::sort(sorted.begin(), sorted.end());
+    if (std::adjacent_find(sorted.begin(), sorted.end()) != sorted.end())
+        return fail(ALB_ERR_INVALID, "kv: a cell given twice");
     r = apply_ubatch(kv, sl, u);
     if (r != ALB_OK) return r;
     kv->n_kv = get_n_kv(kv, sl);
