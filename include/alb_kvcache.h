@@ -18,6 +18,11 @@
  *
  * Cell indices handed out and taken back are flat: stream * kv_size + cell, the
  * reference's K/V row indices (set_inputs_attn_kidx, cgraph.cpp:1182-1194).
+ *
+ * Host memory only, no CUDA call.  A cache object has one owner: calls on one
+ * object must not overlap; calls on distinct objects are independent.  Errors
+ * leave the cells unchanged and return ALB_ERR_INVALID (message in
+ * alb_last_error()), where the reference asserts.
  */
 #ifndef ALB_KVCACHE_H
 #define ALB_KVCACHE_H
