@@ -74,3 +74,41 @@ def test_set_rows_rejects_bad_shapes_before_any_device_call():
     assert L.alb_set_rows_f16(p, 0, 1024, p, p, 8, None) == A.ALB_ERR_INVALID    # no rows
     assert L.alb_set_rows_f16(None, 2, 1024, p, p, 8, None) == A.ALB_ERR_INVALID
     assert L.alb_set_rows_f16(C.c_void_p(4100), 2, 1024, p, p, 8, None) == A.ALB_ERR_INVALID   # unaligned src
+
+
+def test_headers_are_plain_c_and_the_kv_manager_links(tmp_path):
+    """include/*.h compile as C11 (what a cgo / JNI / ctypes binding sees), and a
+    C program linked against libalb_cuda.so drives the KV-cache manager (host
+    only, no device call): one sequence's cells are its positions."""
+    import os
+    import shutil
+    cc = shutil.which("gcc")
+    if not cc:
+        pytest.skip("no gcc")
+    src = tmp_path / "abi.c"
+    src.write_text(r'''
+#include <stdio.h>
+#include "alb_cuda.h"
+#include "alb_kvcache.h"
+int main(void) {
+    alb_kv_cache * kv = NULL;
+    if (alb_kv_create(64, 1, 1, 32, &kv) != ALB_OK) return 1;
+    int32_t pos[5] = {0, 1, 2, 3, 4}, seq[5] = {0, 0, 0, 0, 0}, sizes[1] = {5};
+    int64_t cells[5];
+    uint32_t n_kv = 0;
+    if (alb_kv_prepare(kv, sizes, 1, pos, seq, cells) != ALB_OK) return 2;
+    if (alb_kv_apply(kv, pos, seq, 5, cells, &n_kv) != ALB_OK || n_kv != 32) return 3;
+    for (int i = 0; i < 5; ++i) if (cells[i] != i) return 4;
+    if (alb_kv_create(100, 1, 1, 32, &kv) != ALB_ERR_INVALID) return 5;
+    printf("ok %s\n", alb_last_error());
+    return alb_kv_destroy(kv);
+}
+''')
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    exe = tmp_path / "abi"
+    subprocess.run([cc, "-std=c11", "-Wall", "-Werror", "-I" + os.path.join(root, "include"), str(src), "-o", str(exe),
+                    "-L" + os.path.dirname(A.LIB_PATH), "-lalb_cuda", "-Wl,-rpath," + os.path.dirname(A.LIB_PATH)],
+                   check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert out.returncode == 0, (out.returncode, out.stdout, out.stderr)
+    assert out.stdout.startswith("ok kv: bad cache shape")
