@@ -85,6 +85,7 @@ def _declare(L: C.CDLL) -> None:
         "alb_kv_visible_cells": (ci, [vp, i32, i32, C.c_uint32, vp, vp]),
         "alb_rope_table": (ci, [vp, i32, i32, f32]),
         "alb_qk_norm_rope_kv": (ci, [vp, i64, i32, i32, vp, vp, f32, vp, i32, vp, vp, vp, vp]),
+        "alb_qk_norm_rope_kv_cells": (ci, [vp, i64, i32, i32, vp, vp, f32, vp, i32, vp, vp, i64, vp, vp, vp, vp]),
         "alb_flash_attn_workspace_bytes": (sz, [i32, i32, i64, i32, i32]),
         "alb_flash_attn": (ci, [vp, vp, vp, i64, i32, i32, i32, f32, i32, vp, vp, vp]),
         "alb_gemm_workspace_bytes": (C.c_size_t, [i64, i64]),

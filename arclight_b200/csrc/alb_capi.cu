@@ -105,6 +105,26 @@ extern "C" int alb_qk_norm_rope_kv(const float * qkv, int64_t T, int32_t n_head,
     return ALB_OK;
 }
 
+// The same with per-token positions and cells (device arrays), for a ubatch
+// placed by the KV-cache manager (several sequences, cells != positions).
+extern "C" int alb_qk_norm_rope_kv_cells(const float * qkv, int64_t T, int32_t n_head, int32_t n_head_kv,
+                                         const float * q_norm, const float * k_norm, float eps,
+                                         const float * rope_table, int32_t max_pos, const int32_t * positions,
+                                         const int64_t * cells, int64_t n_cells, float * q_out, uint16_t * k_cache,
+                                         uint16_t * v_cache, void * stream) {
+    ALB_CHECK_ARG(qkv && q_norm && k_norm && rope_table && q_out && k_cache && v_cache && positions && cells);
+    ALB_CHECK_ARG(T > 0 && T < 65536 && n_head > 0 && n_head_kv > 0 && max_pos > 0 && n_cells > 0);
+    QkvArgs a;
+    a.qkv = qkv; a.qkv_stride = (int64_t)(n_head + 2 * n_head_kv) * 128;
+    a.Hq = n_head; a.Hkv = n_head_kv; a.T = (int)T;
+    a.q_norm = q_norm; a.k_norm = k_norm; a.eps = eps;
+    a.rope = reinterpret_cast<const float2 *>(rope_table);
+    a.q_out = q_out; a.kc = k_cache; a.vc = v_cache; a.pdl = true;
+    a.pos_tok = positions; a.cell_tok = cells; a.n_cells = n_cells; a.max_pos = max_pos;
+    ALB_CUDA_TRY(launch_qk_norm_rope_kv(a, (cudaStream_t)stream));
+    return ALB_OK;
+}
+
 extern "C" size_t alb_flash_attn_workspace_bytes(int32_t n_head, int32_t n_head_kv, int64_t T, int32_t splits,
                                                  int32_t n_cells) {
     if (n_head <= 0 || n_head_kv <= 0 || T <= 0 || splits <= 0 || n_cells <= 0) return 0;

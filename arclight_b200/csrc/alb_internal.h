@@ -90,6 +90,11 @@ struct QkvArgs {
     float * q_out = nullptr;            // [T][Hq][128]
     uint16_t * kc = nullptr, * vc = nullptr;  // cache base of this layer [cells][Hkv][128]
     bool pdl = false;
+    // optional, device, per token: positions and cells (else pos0 + t for both)
+    const int32_t * pos_tok = nullptr;
+    const int64_t * cell_tok = nullptr;
+    int64_t n_cells = 0;                // cache rows (bound of cell_tok)
+    int32_t max_pos = 0;                // RoPE table rows (bound of pos_tok)
 };
 cudaError_t launch_qk_norm_rope_kv(const QkvArgs & a, cudaStream_t st);
 // Decode step attention with QK-norm + RoPE + the K/V store fused (T = 1):

@@ -91,24 +91,35 @@ __global__ void k_embed_q4_0(const uint8_t * __restrict__ W, const int32_t * __r
 // ops.cpp:680-724) then NEOX RoPE at pos0+t (ops.cpp:830-938) using the host
 // cos/sin table (nnml_rope_cache_init, ops.cpp:759-771); K heads likewise with
 // k_norm and are stored fp32->fp16 (RNE) into the K cache row pos0+t
-// (set_rows, ops.cpp:135-181); V heads are stored as is.
+// (set_rows, ops.cpp:135-181); V heads are stored as is.  With pos_tok /
+// cell_tok (device, per token) token t takes position pos_tok[t] and stores
+// into cell cell_tok[t] instead (a ubatch of several sequences placed by the
+// KV-cache manager); a position outside the RoPE table or a cell outside the
+// cache skips the token and sets the device error word.
 // Block = 128 threads (one per dimension), grid = (Hq + 2*Hkv, T).
 __global__ void __launch_bounds__(128)
 k_qk_norm_rope_kv(const float * __restrict__ qkv, int64_t qkv_stride, int Hq, int Hkv,
                   const float * __restrict__ qn_w, const float * __restrict__ kn_w, float eps,
                   const float2 * __restrict__ rope, int32_t pos0, const int32_t * __restrict__ pos_dev,
                   float * __restrict__ q_out, uint16_t * __restrict__ kc, uint16_t * __restrict__ vc,
-                  int64_t kv_row) {
+                  int64_t kv_row, const int32_t * __restrict__ pos_tok, const int64_t * __restrict__ cell_tok,
+                  int64_t n_cells, int32_t max_pos, int * err) {
     const int head = blockIdx.x, t = blockIdx.y, d = threadIdx.x;
     const int lane = d & 31, warp = d >> 5;
     alb_pdl_wait();
-    const int32_t pos = (pos_dev ? pos_dev[0] : pos0) + t;
+    const int32_t pos = pos_tok ? pos_tok[t] : (pos_dev ? pos_dev[0] : pos0) + t;
+    const int64_t cell = cell_tok ? cell_tok[t] : (int64_t)pos;
+    if ((pos_tok || cell_tok) && (pos < 0 || pos >= max_pos || cell < 0 || cell >= n_cells)) {
+        if (d == 0) atomicExch(err, ALB_DEVERR_BAD_INDEX);   // the whole block leaves: no store, no read
+        alb_pdl_trigger();
+        return;
+    }
     const float * src = qkv + (size_t)t * qkv_stride;
     __shared__ float buf[128];
     __shared__ double red[4];
     if (head >= Hq + Hkv) {   // V head: plain fp16 store
         const int hv = head - Hq - Hkv;
-        vc[(size_t)pos * kv_row + hv * 128 + d] = alb_f2h(src[(Hq + Hkv) * 128 + hv * 128 + d]);
+        vc[(size_t)cell * kv_row + hv * 128 + d] = alb_f2h(src[(Hq + Hkv) * 128 + hv * 128 + d]);
         alb_pdl_trigger();
         return;
     }
@@ -139,7 +150,7 @@ k_qk_norm_rope_kv(const float * __restrict__ qkv, int64_t qkv_stride, int Hq, in
     if (d < 64) outv = __fsub_rn(__fmul_rn(buf[d], cs.x), __fmul_rn(buf[d + 64], cs.y));
     else        outv = __fadd_rn(__fmul_rn(buf[d - 64], cs.y), __fmul_rn(buf[d], cs.x));
     if (is_q) q_out[((size_t)t * Hq + hh) * 128 + d] = outv;
-    else      kc[(size_t)pos * kv_row + hh * 128 + d] = alb_f2h(outv);
+    else      kc[(size_t)cell * kv_row + hh * 128 + d] = alb_f2h(outv);
     alb_pdl_trigger();
 }
 
@@ -690,9 +701,14 @@ cudaError_t launch_embed(const uint8_t * W, int64_t vocab, int64_t E, const int3
 
 cudaError_t launch_qk_norm_rope_kv(const QkvArgs & a, cudaStream_t st) {
     dim3 grid((unsigned)(a.Hq + 2 * a.Hkv), (unsigned)a.T);
+    int * err = nullptr;
+    if (a.pos_tok || a.cell_tok) {
+        err = device_error_ptr();
+        if (!err) return cudaErrorMemoryAllocation;
+    }
     return alb_launch(k_qk_norm_rope_kv, grid, dim3(128), 0, st, a.pdl, a.qkv, a.qkv_stride, a.Hq, a.Hkv,
                       a.q_norm, a.k_norm, a.eps, a.rope, a.pos0, a.pos_dev, a.q_out, a.kc, a.vc,
-                      (int64_t)a.Hkv * 128);
+                      (int64_t)a.Hkv * 128, a.pos_tok, a.cell_tok, a.n_cells, a.max_pos, err);
 }
 
 cudaError_t launch_rms_norm(const float * x, const float * w, float * y, int64_t rows, int64_t n, float eps, bool pdl,

@@ -55,7 +55,8 @@ ALB_API int          alb_device_check(int dev);
 /* Device-side error word of the current device: 0, or the code of a bounded
  * in-kernel wait that expired (1 = mbarrier, 2 = cross-CTA / cross-rank flag),
  * or 3 = a decode step produced no valid next token (token 0 was fed back), or
- * 4 = alb_set_rows_f16 / alb_get_rows_f16 met a row index out of range.
+ * 4 = alb_set_rows_f16 / alb_get_rows_f16 / alb_qk_norm_rope_kv_cells met a row
+ * index out of range.
  * Kernels never trap; they record the error and return.  clear != 0 resets it. */
 ALB_API int          alb_device_error(int clear);
 
@@ -148,6 +149,17 @@ ALB_API int alb_rope_table(float * table_dev, int32_t max_pos, int32_t head_dim,
 ALB_API int alb_qk_norm_rope_kv(const float * qkv, int64_t T, int32_t n_head, int32_t n_head_kv,
                                 const float * q_norm, const float * k_norm, float eps, const float * rope_table,
                                 int32_t pos0, float * q_out, uint16_t * k_cache, uint16_t * v_cache, void * stream);
+
+/* alb_qk_norm_rope_kv for a ubatch placed by the KV-cache manager: token t takes
+ * position positions[t] (device int32; < max_pos, the RoPE table's rows) and
+ * stores its K/V rows into cell cells[t] (device int64, e.g. alb_kv_prepare's
+ * flat indices; < n_cells, the cache's rows).  A token outside those bounds is
+ * skipped and alb_device_error() reports 4. */
+ALB_API int alb_qk_norm_rope_kv_cells(const float * qkv, int64_t T, int32_t n_head, int32_t n_head_kv,
+                                      const float * q_norm, const float * k_norm, float eps, const float * rope_table,
+                                      int32_t max_pos, const int32_t * positions, const int64_t * cells,
+                                      int64_t n_cells, float * q_out, uint16_t * k_cache, uint16_t * v_cache,
+                                      void * stream);
 
 /* ------------------------------------------------------------- attention */
 /* nnml_compute_forward_flash_attn_ext_f16 (arm.cpp:2196-2433), one sequence,

@@ -139,6 +139,57 @@ def test_qk_norm_rope_kv(Hq, Hkv, T, pos0):
         np.testing.assert_array_equal(VC.cpu().numpy()[pos0 + t].view(np.uint16), O.fp32_to_fp16(v[t]))
 
 
+def test_qk_norm_rope_kv_at_manager_cells():
+    """A ubatch of sequence 1 placed by the KV-cache manager after sequence 0's
+    cells 3..5 were freed: token t is rotated at its own position and its K/V
+    rows land in the cell the manager chose (bit for bit vs the oracle); other
+    rows stay untouched; a cell past the cache is skipped and reported."""
+    from arclight_b200.kvcache import KVCache
+    Hq, Hkv, ncell = 16, 8, 64
+    kv = KVCache(ncell, 2, True, 32)
+    p0 = np.arange(10, dtype=np.int32)
+    (c0,) = kv.prepare([(p0, np.zeros(10, np.int32))])
+    kv.apply(p0, np.zeros(10, np.int32), c0)
+    kv.seq_rm(0, 3, 6)
+    pos = np.arange(5, dtype=np.int32)
+    (cells,) = kv.prepare([(pos, np.ones(5, np.int32))])
+    assert cells.tolist() == [3, 4, 5, 10, 11]
+    T = len(pos)
+    rng = np.random.default_rng(11)
+    qkv = (rng.standard_normal((T, (Hq + 2 * Hkv) * 128)) * 2).astype(np.float32)
+    qn = (1 + 0.01 * rng.standard_normal(128)).astype(np.float32)
+    kn = (1 + 0.01 * rng.standard_normal(128)).astype(np.float32)
+    rt = rope_table(ncell)
+    Q = torch.empty((T, Hq, 128), dtype=torch.float32, device="cuda")
+    KC = torch.full((ncell, Hkv, 128), 0x7E00, dtype=torch.int16, device="cuda")
+    VC = torch.full((ncell, Hkv, 128), 0x7E00, dtype=torch.int16, device="cuda")
+    QKV, QN, KN, P, CI = cu(qkv), cu(qn), cu(kn), cu(pos), cu(cells.astype(np.int64))
+    L.alb_device_error(1)
+    A.check(L.alb_qk_norm_rope_kv_cells(QKV.data_ptr(), T, Hq, Hkv, QN.data_ptr(), KN.data_ptr(), 1e-6,
+                                        rt.data_ptr(), ncell, P.data_ptr(), CI.data_ptr(), ncell, Q.data_ptr(),
+                                        KC.data_ptr(), VC.data_ptr(), st()))
+    torch.cuda.synchronize()
+    assert L.alb_device_error(0) == 0
+    q = qkv[:, :Hq * 128].reshape(T, Hq, 128)
+    k = qkv[:, Hq * 128:(Hq + Hkv) * 128].reshape(T, Hkv, 128)
+    v = qkv[:, (Hq + Hkv) * 128:].reshape(T, Hkv, 128)
+    kc, vc = KC.cpu().numpy().view(np.uint16), VC.cpu().numpy().view(np.uint16)
+    for t in range(T):
+        np.testing.assert_array_equal(Q.cpu().numpy()[t], O.rope_neox(O.rms_norm(q[t], qn), int(pos[t])))
+        kr = O.rope_neox(O.rms_norm(k[t], kn), int(pos[t]))
+        np.testing.assert_array_equal(kc[cells[t]], O.fp32_to_fp16(kr))
+        np.testing.assert_array_equal(vc[cells[t]], O.fp32_to_fp16(v[t]))
+    untouched = np.setdiff1d(np.arange(ncell), cells)
+    assert np.all(kc[untouched] == 0x7E00) and np.all(vc[untouched] == 0x7E00)
+    bad = cu(np.array([7, 64, 8, 9, 12], np.int64))   # 64 is past the 64-row cache
+    A.check(L.alb_qk_norm_rope_kv_cells(QKV.data_ptr(), T, Hq, Hkv, QN.data_ptr(), KN.data_ptr(), 1e-6,
+                                        rt.data_ptr(), ncell, P.data_ptr(), bad.data_ptr(), ncell, Q.data_ptr(),
+                                        KC.data_ptr(), VC.data_ptr(), st()))
+    torch.cuda.synchronize()
+    assert L.alb_device_error(1) == 4
+    assert np.all(KC.cpu().numpy().view(np.uint16)[7] == O.fp32_to_fp16(O.rope_neox(O.rms_norm(k[0], kn), 0)))
+
+
 @pytest.mark.parametrize("Hq,Hkv,T,pos0,S", [
     (32, 8, 1, 639, 74),     # 4B decode at the config-3 mean position
     (32, 8, 1, 0, 74),       # first token: one cell, most splits empty
