@@ -332,3 +332,29 @@ def test_attention_of_one_sequence_in_a_shared_cache(seq_id, pos, splits):
     kv_len = np.array([n], np.int32)
     np.testing.assert_array_equal(out.cpu().numpy(), O.flash_attn(q, k[vis], v[vis], kv_len, scale, mode=0))
     assert max_rel_err(out.cpu().numpy(), O.flash_attn(q, k[vis], v[vis], kv_len, scale, mode=2)) < 1e-5
+
+
+def test_split_attention_on_two_devices_in_one_process():
+    """Kernels that need more than 48 KB of dynamic shared memory get that
+    attribute per device: the split attention runs on device 0, then on device
+    1, in one process, both bit-identical to the oracle.  (One GPU: skipped.)"""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    Hq, Hkv, T, pos0, S = 32, 8, 1, 2047, 74
+    rng = np.random.default_rng(21)
+    cells = pos0 + T
+    k = O.fp32_to_fp16(rng.standard_normal((cells, Hkv, 128)).astype(np.float32))
+    v = O.fp32_to_fp16(rng.standard_normal((cells, Hkv, 128)).astype(np.float32))
+    q = (rng.standard_normal((T, Hq, 128)) * 0.5).astype(np.float32)
+    scale = 1.0 / math.sqrt(128.0)
+    ref = O.flash_attn(q, k, v, np.array([cells], np.int32), scale, mode=0)
+    for dev in (0, 1):
+        with torch.cuda.device(dev):
+            ws = torch.zeros(L.alb_flash_attn_workspace_bytes(Hq, Hkv, T, S, cells), dtype=torch.uint8, device="cuda")
+            out = torch.empty((T, Hq, 128), dtype=torch.float32, device="cuda")
+            Kd, Vd, Qd = cu(k.view(np.int16)), cu(v.view(np.int16)), cu(q)
+            A.check(L.alb_flash_attn(Qd.data_ptr(), Kd.data_ptr(), Vd.data_ptr(), T, Hq, Hkv, pos0, scale, S,
+                                     ws.data_ptr(), out.data_ptr(), torch.cuda.current_stream().cuda_stream),
+                    f"split attention on device {dev}")
+            torch.cuda.synchronize()
+            np.testing.assert_array_equal(out.cpu().numpy(), ref)
